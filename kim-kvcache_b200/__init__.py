@@ -1,0 +1,228 @@
+"""Python bindings (ctypes) for the kim-kvcache B200 library.
+
+The product is the shared library lib/libkk_b200.so: the C++ host token-loop
+runtime and the sm_100a CUDA kernels behind the C ABI declared in
+include/kk_runtime.h and include/kk_kernels.h. This module only loads that
+library and describes its C signatures; it contains no compute of its own.
+It raises ImportError-style errors when the library is missing instead of
+falling back to anything else.
+
+The directory name is not a valid Python identifier, so callers load it by
+path, e.g. ``kk = load_package()`` from the repository root helper below.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import importlib.util
+import os
+import sys
+from pathlib import Path
+
+PKG_DIR = Path(__file__).resolve().parent
+LIB_PATH = PKG_DIR / "lib" / "libkk_b200.so"
+
+
+class KkEntry(C.Structure):
+    _fields_ = [("logical_token_begin", C.c_uint32), ("valid_tokens", C.c_uint16),
+                ("kind", C.c_uint8), ("reserved", C.c_uint8), ("slot", C.c_uint32),
+                ("generation", C.c_uint32)]
+
+
+class KkHandle(C.Structure):
+    _fields_ = [("kind", C.c_uint8), ("reserved", C.c_uint8 * 3), ("slot", C.c_uint32),
+                ("generation", C.c_uint32)]
+
+
+class KkPageMeta(C.Structure):
+    _fields_ = [("state", C.c_uint8), ("reserved", C.c_uint8), ("valid_tokens", C.c_uint16),
+                ("ref_count", C.c_uint32), ("promotion_pins", C.c_uint32),
+                ("inflight_readers", C.c_uint32), ("mutable_owner", C.c_uint64)]
+
+
+class KkPoolSnapshot(C.Structure):
+    _fields_ = [("total_slots", C.c_uint32), ("free_slots", C.c_uint32),
+                ("allocated_slots", C.c_uint32), ("reserved", C.c_uint32),
+                ("successful_allocations", C.c_uint64), ("successful_releases", C.c_uint64),
+                ("failed_allocations", C.c_uint64), ("rejected_releases", C.c_uint64)]
+
+
+class KkMgrSnapshot(C.Structure):
+    _fields_ = [("request_count", C.c_uint64), ("promotion_count", C.c_uint64),
+                ("page_lease_count", C.c_uint64), ("token_reservation_count", C.c_uint64),
+                ("micro_pool", KkPoolSnapshot), ("extent_pool", KkPoolSnapshot)]
+
+
+class KkTableOut(C.Structure):
+    _fields_ = [("entries", C.POINTER(KkEntry)), ("capacity", C.c_uint32),
+                ("count", C.c_uint32), ("version", C.c_uint64)]
+
+
+def _struct_tuple(s: C.Structure) -> tuple:
+    out = []
+    for name, _ in s._fields_:
+        if name == "reserved":
+            continue
+        v = getattr(s, name)
+        out.append(_struct_tuple(v) if isinstance(v, C.Structure) else v)
+    return tuple(out)
+
+
+_P = C.c_void_p
+_U32, _U64, _I = C.c_uint32, C.c_uint64, C.c_int
+MANAGER_SIGNATURES = {
+    "mgr_create": (_P, [_U32, _U32]),
+    "mgr_destroy": (None, [_P]),
+    "mgr_create_request": (_I, [_P, _U64]),
+    "mgr_append": (_I, [_P, _U64, _U32]),
+    "mgr_reserve_token": (_I, [_P, _U64, _U32, C.POINTER(_U64), C.POINTER(KkTableOut),
+                               C.POINTER(KkTableOut)]),
+    "mgr_commit_reservation": (_I, [_P, _U64]),
+    "mgr_rollback_reservation": (_I, [_P, _U64]),
+    "mgr_seal_tail": (_I, [_P, _U64]),
+    "mgr_fork": (_I, [_P, _U64, _U64]),
+    "mgr_release": (_I, [_P, _U64]),
+    "mgr_prepare_promotion": (_I, [_P, _U64, _U32, C.POINTER(_U64), C.POINTER(KkHandle),
+                                   C.POINTER(KkHandle)]),
+    "mgr_commit_promotion": (_I, [_P, _U64]),
+    "mgr_rollback_promotion": (_I, [_P, _U64]),
+    "mgr_acquire_request_lease": (_I, [_P, _U64, C.POINTER(_U64), C.POINTER(_U32)]),
+    "mgr_acquire_promotion_lease": (_I, [_P, _U64, C.POINTER(_U64), C.POINTER(_U32)]),
+    "mgr_acquire_reservation_lease": (_I, [_P, _U64, C.POINTER(_U64), C.POINTER(_U32)]),
+    "mgr_release_lease": (_I, [_P, _U64]),
+    "mgr_block_table": (_I, [_P, _U64, C.POINTER(KkTableOut)]),
+    "mgr_page_metadata": (_I, [_P, KkHandle, C.POINTER(KkPageMeta)]),
+    "mgr_snapshot": (None, [_P, C.POINTER(KkMgrSnapshot)]),
+    "mgr_check_invariants": (_I, [_P]),
+    "float_to_half": (C.c_uint16, [C.c_float]),
+    "half_to_float": (C.c_float, [C.c_uint16]),
+}
+
+
+def bind(lib: C.CDLL, prefix: str, signatures: dict) -> dict:
+    """Attaches argtypes/restype to every `prefix + name` symbol; returns name->fn."""
+    fns = {}
+    for name, (res, args) in signatures.items():
+        fn = getattr(lib, prefix + name)
+        fn.restype = res
+        fn.argtypes = args
+        fns[name] = fn
+    return fns
+
+
+_LIB = None
+
+
+def load_library() -> C.CDLL:
+    """Loads lib/libkk_b200.so (built by build.py). Raises OSError if absent."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise OSError(f"{LIB_PATH} is missing: run `python kim-kvcache_b200/build.py`")
+        _LIB = C.CDLL(str(LIB_PATH))
+    return _LIB
+
+
+class Manager:
+    """KvCacheManager through a C ABI (`prefix` kkrt_ = this library, kref_ =
+    the reference oracle twin with identical signatures)."""
+
+    MAX_ENTRIES = 4096
+
+    def __init__(self, lib: C.CDLL, prefix: str, micro: int, extent: int):
+        self.f = bind(lib, prefix, MANAGER_SIGNATURES)
+        self.h = self.f["mgr_create"](micro, extent)
+        if not self.h:
+            raise ValueError("invalid capacities")
+        self._buf = [(KkEntry * self.MAX_ENTRIES)() for _ in range(2)]
+
+    def close(self):
+        if self.h:
+            self.f["mgr_destroy"](self.h)
+            self.h = None
+
+    __del__ = close
+
+    def _table(self, i=0):
+        return KkTableOut(C.cast(self._buf[i], C.POINTER(KkEntry)), self.MAX_ENTRIES, 0, 0)
+
+    @staticmethod
+    def _entries(t: KkTableOut, buf) -> tuple:
+        return (t.version, tuple(_struct_tuple(buf[i]) for i in range(t.count)))
+
+    def create(self, rid):
+        return self.f["mgr_create_request"](self.h, rid)
+
+    def append(self, rid, n):
+        return self.f["mgr_append"](self.h, rid, n)
+
+    def reserve(self, rid, expected):
+        r = C.c_uint64(0)
+        b, v = self._table(0), self._table(1)
+        err = self.f["mgr_reserve_token"](self.h, rid, expected, C.byref(r), C.byref(b), C.byref(v))
+        return err, r.value, self._entries(b, self._buf[0]), self._entries(v, self._buf[1])
+
+    def commit(self, res_id):
+        return self.f["mgr_commit_reservation"](self.h, res_id)
+
+    def rollback(self, res_id):
+        return self.f["mgr_rollback_reservation"](self.h, res_id)
+
+    def seal(self, rid):
+        return self.f["mgr_seal_tail"](self.h, rid)
+
+    def fork(self, src, child):
+        return self.f["mgr_fork"](self.h, src, child)
+
+    def release(self, rid):
+        return self.f["mgr_release"](self.h, rid)
+
+    def prepare_promotion(self, rid, begin):
+        pid = C.c_uint64(0)
+        src = (KkHandle * 8)()
+        tgt = KkHandle()
+        err = self.f["mgr_prepare_promotion"](self.h, rid, begin, C.byref(pid), src, C.byref(tgt))
+        return err, pid.value, tuple(_struct_tuple(s) for s in src), _struct_tuple(tgt)
+
+    def commit_promotion(self, pid):
+        return self.f["mgr_commit_promotion"](self.h, pid)
+
+    def rollback_promotion(self, pid):
+        return self.f["mgr_rollback_promotion"](self.h, pid)
+
+    def _lease(self, name, key):
+        lid, n = C.c_uint64(0), C.c_uint32(0)
+        err = self.f[name](self.h, key, C.byref(lid), C.byref(n))
+        return err, lid.value, n.value
+
+    def lease_request(self, rid):
+        return self._lease("mgr_acquire_request_lease", rid)
+
+    def lease_promotion(self, pid):
+        return self._lease("mgr_acquire_promotion_lease", pid)
+
+    def lease_reservation(self, res_id):
+        return self._lease("mgr_acquire_reservation_lease", res_id)
+
+    def release_lease(self, lid):
+        return self.f["mgr_release_lease"](self.h, lid)
+
+    def table(self, rid):
+        t = self._table(0)
+        if not self.f["mgr_block_table"](self.h, rid, C.byref(t)):
+            return None
+        return self._entries(t, self._buf[0])
+
+    def page_meta(self, kind, slot, generation):
+        m = KkPageMeta()
+        h = KkHandle(kind, (C.c_uint8 * 3)(), slot, generation)
+        if not self.f["mgr_page_metadata"](self.h, h, C.byref(m)):
+            return None
+        return _struct_tuple(m)
+
+    def snapshot(self):
+        s = KkMgrSnapshot()
+        self.f["mgr_snapshot"](self.h, C.byref(s))
+        return _struct_tuple(s)
+
+    def invariants(self):
+        return bool(self.f["mgr_check_invariants"](self.h))

@@ -1,0 +1,100 @@
+"""Builds libkk_b200.so in-tree: the host token-loop runtime (C++17), the
+sm_100a CUDA kernels and their C ABI, in one shared library.
+
+Usage: python kim-kvcache_b200/build.py [--force] [-j N]
+
+Objects go to kim-kvcache_b200/_build/, the library to
+kim-kvcache_b200/lib/libkk_b200.so (both git-ignored; the .so travels to the
+GPU box with the working tree). Recompiles a source when it or any header
+under csrc/ or include/ is newer than its object.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+OBJ = PKG / "_build"
+LIB = PKG / "lib" / "libkk_b200.so"
+
+NVCC = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+CUDA_HOME = Path(NVCC).resolve().parent.parent
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{CUDA_HOME / 'include'}"]
+CXXFLAGS = COMMON + ["-fPIC", "-fvisibility=hidden", "-Wall", "-Wextra", "-ffp-contract=off"]
+NVCCFLAGS = COMMON + ARCH + ["-lineinfo", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+                            "--expt-relaxed-constexpr", "-Xptxas", "-warn-spills"]
+
+
+def sources() -> list[Path]:
+    out = []
+    for sub in ("host", "capi", "cuda"):
+        d = CSRC / sub
+        if d.exists():
+            out += sorted(d.glob("*.cpp")) + sorted(d.glob("*.cu"))
+    return out
+
+
+def newest_header() -> float:
+    stamps = [p.stat().st_mtime for d in (CSRC, ROOT / "include")
+              for p in d.rglob("*") if p.suffix in (".h", ".cuh", ".inc")]
+    return max(stamps, default=0.0)
+
+
+def compile_one(src: Path, force: bool, hdr_time: float, extra: list[str]) -> tuple[Path, str]:
+    obj = OBJ / (src.relative_to(CSRC).as_posix().replace("/", "__") + ".o")
+    if (not force and obj.exists() and obj.stat().st_mtime >= src.stat().st_mtime
+            and obj.stat().st_mtime >= hdr_time):
+        return obj, ""
+    if src.suffix == ".cu":
+        cmd = [NVCC, *NVCCFLAGS, *extra, "-c", str(src), "-o", str(obj)]
+    else:
+        cmd = ["g++", *CXXFLAGS, "-c", str(src), "-o", str(obj)]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"compile failed: {src}\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return obj, (res.stdout + res.stderr).strip()
+
+
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
+          ptxas_info: bool = False) -> Path:
+    OBJ.mkdir(parents=True, exist_ok=True)
+    LIB.parent.mkdir(parents=True, exist_ok=True)
+    hdr_time = newest_header()
+    extra = ["-Xptxas", "-v"] if ptxas_info else []
+    srcs = sources()
+    jobs = jobs or min(8, os.cpu_count() or 4)
+    with cf.ThreadPoolExecutor(jobs) as pool:
+        results = list(pool.map(lambda s: compile_one(s, force, hdr_time, extra), srcs))
+    objs = [r[0] for r in results]
+    for (obj, log) in results:
+        if log and (verbose or ptxas_info):
+            print(f"[{obj.name}]\n{log}")
+    lib_time = LIB.stat().st_mtime if LIB.exists() else 0.0
+    if force or not LIB.exists() or any(o.stat().st_mtime > lib_time for o in objs):
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda", "-lpthread"]
+        res = subprocess.run(cmd, capture_output=True, text=True)
+        if res.returncode != 0:
+            raise RuntimeError(f"link failed\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return LIB
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=None)
+    ap.add_argument("-v", action="store_true")
+    ap.add_argument("--ptxas-info", action="store_true")
+    a = ap.parse_args()
+    try:
+        print(build(a.force, a.j, a.v, a.ptxas_info))
+    except RuntimeError as e:
+        print(e, file=sys.stderr)
+        sys.exit(1)

@@ -1,0 +1,205 @@
+// TEST INFRASTRUCTURE ONLY — never linked into, loaded by, or called from the
+// product library.
+//
+// C shim over the reference implementation itself: compiled together with
+// the reference's own CPU sources (read in place from the reference tree by
+// oracle/Makefile) into oracle/_ref/libkimkv_ref.so. Exposes kref_* twins of
+// the kkrt_* entry points in include/kk_runtime.h so the parity tests can run
+// identical operation streams on the reference and on the product runtime.
+#include "../include/kk_runtime.h"
+
+#include "kim-kv/model/weight_manifest.h"
+#include "kim-kv/reference/kv_reference.h"
+#include "kim-kv/runtime/kv_cache_manager.h"
+
+#include <cstring>
+#include <vector>
+
+using namespace kimkvcache;
+
+namespace {
+
+KvCacheManager* M(void* p) { return static_cast<KvCacheManager*>(p); }
+
+void tableOut(BlockTable const& t, kk_table_out* out)
+{
+    if (out == nullptr) {
+        return;
+    }
+    out->count = static_cast<uint32_t>(t.entries().size());
+    out->version = t.version();
+    for (std::size_t i = 0; i < t.entries().size() && i < out->capacity; ++i) {
+        MappingEntry const& m = t.entries()[i];
+        out->entries[i] = kk_entry{m.logical_token_begin, m.valid_tokens,
+            static_cast<uint8_t>(m.kind), 0, m.handle.slot, m.handle.generation};
+    }
+}
+
+kk_handle handleOut(PageHandle h)
+{
+    kk_handle out{};
+    out.kind = static_cast<uint8_t>(h.kind);
+    out.slot = h.slot;
+    out.generation = h.generation;
+    return out;
+}
+
+int leaseOut(PageLeaseAcquireResult const& r, uint64_t* lease, uint32_t* n)
+{
+    if (lease != nullptr) *lease = r.lease_id;
+    if (n != nullptr) *n = static_cast<uint32_t>(r.handles.size());
+    return static_cast<int>(r.error);
+}
+
+void poolOut(PagePoolSnapshot const& s, kk_pool_snapshot* o)
+{
+    o->total_slots = s.total_slots;
+    o->free_slots = s.free_slots;
+    o->allocated_slots = s.allocated_slots;
+    o->reserved = 0;
+    o->successful_allocations = s.successful_allocations;
+    o->successful_releases = s.successful_releases;
+    o->failed_allocations = s.failed_allocations;
+    o->rejected_releases = s.rejected_releases;
+}
+
+} // namespace
+
+extern "C" {
+
+KK_API void* kref_mgr_create(uint32_t micro, uint32_t extent)
+{
+    try {
+        return new KvCacheManager(micro, extent);
+    } catch (...) {
+        return nullptr;
+    }
+}
+KK_API void kref_mgr_destroy(void* p) { delete M(p); }
+KK_API int kref_mgr_create_request(void* p, uint64_t id) { return int(M(p)->createRequest(id)); }
+KK_API int kref_mgr_append(void* p, uint64_t id, uint32_t n) { return int(M(p)->append(id, n)); }
+KK_API int kref_mgr_reserve_token(void* p, uint64_t id, uint32_t expected, uint64_t* rid,
+    kk_table_out* before, kk_table_out* reserved)
+{
+    TokenReservationResult const r = M(p)->reserveToken(id, expected);
+    if (rid != nullptr) *rid = r.reservation_id;
+    tableOut(r.before, before);
+    tableOut(r.reserved, reserved);
+    return static_cast<int>(r.error);
+}
+KK_API int kref_mgr_commit_reservation(void* p, uint64_t id)
+{
+    return int(M(p)->commitTokenReservation(id));
+}
+KK_API int kref_mgr_rollback_reservation(void* p, uint64_t id)
+{
+    return int(M(p)->rollbackTokenReservation(id));
+}
+KK_API int kref_mgr_seal_tail(void* p, uint64_t id) { return int(M(p)->sealTail(id)); }
+KK_API int kref_mgr_fork(void* p, uint64_t s, uint64_t c) { return int(M(p)->forkRequest(s, c)); }
+KK_API int kref_mgr_release(void* p, uint64_t id) { return int(M(p)->releaseRequest(id)); }
+KK_API int kref_mgr_prepare_promotion(void* p, uint64_t id, uint32_t begin, uint64_t* pid,
+    kk_handle* sources, kk_handle* target)
+{
+    PromotionPrepareResult const r = M(p)->preparePromotion(id, begin);
+    if (pid != nullptr) *pid = r.promotion_id;
+    for (std::size_t k = 0; sources != nullptr && k < kPromotionSourcePageCount; ++k) {
+        sources[k] = handleOut(r.source_handles[k]);
+    }
+    if (target != nullptr) *target = handleOut(r.target_handle);
+    return static_cast<int>(r.error);
+}
+KK_API int kref_mgr_commit_promotion(void* p, uint64_t id) { return int(M(p)->commitPromotion(id)); }
+KK_API int kref_mgr_rollback_promotion(void* p, uint64_t id)
+{
+    return int(M(p)->rollbackPromotion(id));
+}
+KK_API int kref_mgr_acquire_request_lease(void* p, uint64_t id, uint64_t* l, uint32_t* n)
+{
+    return leaseOut(M(p)->acquireRequestReadLease(id), l, n);
+}
+KK_API int kref_mgr_acquire_promotion_lease(void* p, uint64_t id, uint64_t* l, uint32_t* n)
+{
+    return leaseOut(M(p)->acquirePromotionIoLease(id), l, n);
+}
+KK_API int kref_mgr_acquire_reservation_lease(void* p, uint64_t id, uint64_t* l, uint32_t* n)
+{
+    return leaseOut(M(p)->acquireTokenReservationLease(id), l, n);
+}
+KK_API int kref_mgr_release_lease(void* p, uint64_t id) { return int(M(p)->releasePageLease(id)); }
+KK_API int kref_mgr_block_table(void* p, uint64_t id, kk_table_out* out)
+{
+    std::optional<BlockTable> const t = M(p)->blockTable(id);
+    if (!t) return 0;
+    tableOut(*t, out);
+    return 1;
+}
+KK_API int kref_mgr_page_metadata(void* p, kk_handle h, kk_page_meta* out)
+{
+    std::optional<PageMetadataSnapshot> const m =
+        M(p)->pageMetadata(PageHandle{static_cast<PageKind>(h.kind), h.slot, h.generation});
+    if (!m) return 0;
+    out->state = static_cast<uint8_t>(m->state);
+    out->reserved = 0;
+    out->valid_tokens = m->valid_tokens;
+    out->ref_count = m->ref_count;
+    out->promotion_pins = m->promotion_pins;
+    out->inflight_readers = m->inflight_readers;
+    out->mutable_owner = m->mutable_owner;
+    return 1;
+}
+KK_API void kref_mgr_snapshot(void* p, kk_mgr_snapshot* out)
+{
+    KvCacheManagerSnapshot const s = M(p)->snapshot();
+    out->request_count = s.request_count;
+    out->promotion_count = s.promotion_count;
+    out->page_lease_count = s.page_lease_count;
+    out->token_reservation_count = s.token_reservation_count;
+    poolOut(s.micro_pool, &out->micro_pool);
+    poolOut(s.extent_pool, &out->extent_pool);
+}
+KK_API int kref_mgr_check_invariants(void* p) { return M(p)->checkInvariants() ? 1 : 0; }
+
+KK_API uint16_t kref_float_to_half(float v) { return floatToKvScalar(v); }
+KK_API float kref_half_to_float(uint16_t v) { return kvScalarToFloat(v); }
+
+// referenceAttention (src/reference/kv_reference.cpp:136-234) on a contiguous
+// [layer][K/V][token][head][dim] FP16 buffer with an FP32 query [layer][head][dim].
+// Returns 1 on success.
+KK_API int kref_reference_attention(uint32_t layers, uint32_t heads, uint32_t dim,
+    uint16_t const* kv, uint32_t token_count, float const* query, float* output)
+{
+    KvLayout const layout{layers, heads, dim};
+    std::size_t elements = 0;
+    if (!layout.elementsForTokens(token_count, elements)) return 0;
+    std::vector<KvScalar> contiguous(kv, kv + elements);
+    std::size_t const q_elems = static_cast<std::size_t>(layers) * heads * dim;
+    std::vector<float> q(query, query + q_elems);
+    std::vector<float> out;
+    if (!referenceAttention(layout, contiguous, token_count, q, out)) return 0;
+    std::memcpy(output, out.data(), out.size() * sizeof(float));
+    return 1;
+}
+
+// loadWeightManifest + validateWeightDataFile (src/model/weight_manifest.cpp:461-684).
+// Returns the WeightManifestError of the first failing step (0 = both ok).
+KK_API int kref_manifest_check(char const* manifest_path, char const* data_path)
+{
+    WeightManifestLoadResult const loaded = loadWeightManifest(manifest_path);
+    if (!loaded.ok()) return static_cast<int>(loaded.status.error);
+    if (data_path == nullptr) return 0;
+    return static_cast<int>(validateWeightDataFile(loaded.manifest, data_path).error);
+}
+
+// computeWeightDataSha256 (src/model/weight_manifest.cpp:648-684); hex digest
+// into out (65 bytes).
+KK_API int kref_sha256_range(char const* data_path, uint64_t offset, uint64_t bytes, char* out)
+{
+    std::string digest;
+    WeightManifestStatus const s = computeWeightDataSha256(data_path, offset, bytes, digest);
+    if (!s.ok()) return static_cast<int>(s.error);
+    std::memcpy(out, digest.c_str(), digest.size() + 1);
+    return 0;
+}
+
+} // extern "C"
