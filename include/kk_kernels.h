@@ -1,0 +1,205 @@
+/*
+ * kim-kvcache B200 — C ABI of the sm_100a token-loop kernels.
+ *
+ * These entry points replace the reference's internal CUDA launch layer and
+ * its cuBLAS calls:
+ *   src/cuda/kv/kernels.cuh:31-143          cuda_detail::launch* (KV pages, attention)
+ *   src/cuda/model/kernels.cuh:11-117       cuda_model_detail::launch* (norm, RoPE, ...)
+ *   src/cuda/model/runner_support.cpp:196-274  cublasGemmEx wrappers (dense projections)
+ *
+ * Conventions: plain pointers to device memory, sizes in elements unless
+ * named *_bytes, `stream` is a cudaStream_t (NULL = legacy default stream).
+ * Every function returns 0 on a successful launch, KK_EINVAL for rejected
+ * arguments (nothing is launched), or a CUDA runtime error code.
+ * FP16 tensors are passed as uint16_t bit patterns.
+ *
+ * KV page layout (same as the reference, include/kim-kv/core/kv_layout.h:73-90):
+ * a page holds every layer of its tokens as [layer][K/V][token][kv_head][dim];
+ * micro pages hold 8 tokens, extent pages 64; pools are arrays of pages.
+ */
+#ifndef KK_KERNELS_H
+#define KK_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KK_KAPI __attribute__((visibility("default")))
+#else
+#define KK_KAPI
+#endif
+
+#define KK_EINVAL 1000
+
+typedef struct kk_kv_pools {
+    void* micro;               /* micro_capacity pages of layers*2*8*kv_heads*head_dim fp16 */
+    void* extent;              /* extent_capacity pages of layers*2*64*kv_heads*head_dim fp16 */
+    uint32_t micro_capacity;
+    uint32_t extent_capacity;
+    uint32_t layers;
+    uint32_t kv_heads;
+    uint32_t head_dim;
+    uint32_t reserved;
+} kk_kv_pools;
+
+/* One block-table entry as the kernels read it (reference DeviceBlockDescriptor,
+ * include/kim-kv/engine/engine_kv.h:100-117, without the generation). */
+typedef struct kk_page_desc {
+    uint32_t slot;
+    uint32_t logical_token_begin;
+    uint16_t valid_tokens;
+    uint8_t kind;              /* 0 micro, 1 extent */
+    uint8_t reserved0;
+    uint32_t reserved1;
+} kk_page_desc;
+
+/* Destination of one lane's new token (reference CudaEngineTransaction::writeLayer
+ * slot mapping, src/cuda/engine/transaction.cpp:158-194). */
+typedef struct kk_kv_slot {
+    uint32_t slot;
+    uint16_t page_token;
+    uint8_t kind;
+    uint8_t active;            /* 0: lane skipped */
+} kk_kv_slot;
+
+/* Partial-tail copy-on-write: first `tokens` tokens of src -> dst. */
+typedef struct kk_kv_copy {
+    uint32_t src_slot;
+    uint32_t dst_slot;
+    uint16_t tokens;
+    uint8_t src_kind;
+    uint8_t dst_kind;
+} kk_kv_copy;
+
+/* One lane of a ragged decode-attention batch (reference DevicePagedDecodeBatchItem,
+ * include/kim-kv/engine/engine_kv.h:172-181). */
+typedef struct kk_attn_lane {
+    uint32_t desc_offset;      /* first entry of this lane in the descriptor array */
+    uint32_t desc_count;
+    uint32_t token_count;      /* attended tokens, current token included */
+    uint32_t item_offset;      /* filled by kk_attention_plan */
+    uint32_t item_count;       /* filled by kk_attention_plan */
+    uint32_t query_row;        /* row of query / output used by this lane */
+    uint32_t reserved[2];
+} kk_attn_lane;
+
+/* A split-KV work item: a run of one lane's descriptors. */
+typedef struct kk_attn_item {
+    uint32_t lane;
+    uint32_t desc_begin;
+    uint32_t desc_end;
+    uint32_t reserved;
+} kk_attn_item;
+
+/* ---- K1: fused GQA paged decode attention ------------------------------------
+ * Replaces launchPagedDecodeAttention / launchPagedDecodeAttentionBatch
+ * (src/cuda/attention/paged_decode_kernels.cu:533-617): QK^T, online softmax and
+ * PV in one pass that walks micro and extent entries directly, all lanes and
+ * KV heads of a layer in one launch, split over the context with a combine.
+ * head_dim must be 64; kv_heads in {1,2,4,8}; q_heads/kv_heads <= 16.
+ * query/output rows: [q_heads][head_dim] fp16 at row stride *_stride elements. */
+KK_KAPI uint32_t kk_attention_plan(const kk_page_desc* host_descs, kk_attn_lane* host_lanes,
+    uint32_t num_lanes, uint32_t target_tokens, kk_attn_item* host_items, uint32_t max_items);
+KK_KAPI uint64_t kk_attention_workspace_bytes(uint32_t num_lanes, uint32_t num_items,
+    uint32_t q_heads, uint32_t head_dim);
+/* Zero-fills the per-lane completion counters of a fresh workspace (once). */
+KK_KAPI int kk_attention_workspace_init(void* workspace, uint32_t num_lanes, void* stream);
+KK_KAPI int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer,
+    uint32_t q_heads, const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, const uint16_t* query, uint32_t query_stride,
+    uint16_t* output, uint32_t output_stride, float scale, void* workspace,
+    uint64_t workspace_bytes, void* stream);
+
+/* ---- K2: batched KV append / copy-on-write -----------------------------------
+ * kk_kv_write replaces launchWriteLayerToken (paged_decode_kernels.cu:65-99) and
+ * launchAppendTokens (src/cuda/kv/page_kernels.cu:77-127) for one token per
+ * lane: writes K and V of layers [layer_begin, +layer_count) for every active
+ * lane. key/value element (lane, layer, head, dim) lives at
+ * lane*lane_stride + layer*layer_stride + head*head_dim + dim.
+ * kk_kv_copy_tokens replaces launchCopyLayerTokens / launchCopyPageTokens
+ * (paged_decode_kernels.cu:29-63, page_kernels.cu:46-75). */
+KK_KAPI int kk_kv_write(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t layer_count,
+    const kk_kv_slot* slots, uint32_t num_lanes, const uint16_t* key, const uint16_t* value,
+    uint64_t lane_stride, uint64_t layer_stride, void* stream);
+KK_KAPI int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin,
+    uint32_t layer_count, const kk_kv_copy* copies, uint32_t num_copies, void* stream);
+
+/* ---- K3: norms, RoPE, SiLU gate, residual -------------------------------------
+ * Replace launchRmsNorm(Batch), launchRope(Batch), launchSwiGlu, launchResidualAdd,
+ * launchEmbedding(Batch) (src/cuda/model/kernels.cu:16-218). */
+KK_KAPI int kk_rmsnorm(const uint16_t* x, const uint16_t* weight, uint16_t* y, uint32_t rows,
+    uint32_t cols, float eps, void* stream);
+KK_KAPI int kk_embed_rmsnorm(const uint16_t* embed, const uint32_t* tokens,
+    const uint16_t* weight, uint16_t* hidden, uint16_t* y, uint32_t rows, uint32_t cols,
+    float eps, void* stream);
+KK_KAPI int kk_rope(uint16_t* q, uint32_t q_stride, uint16_t* k, uint32_t k_stride,
+    const uint32_t* positions, uint32_t rows, uint32_t q_heads, uint32_t kv_heads,
+    uint32_t head_dim, float theta, void* stream);
+KK_KAPI int kk_silu_mul(const uint16_t* gate, const uint16_t* up, uint16_t* out, uint32_t rows,
+    uint32_t cols, void* stream);
+KK_KAPI int kk_residual_add(uint16_t* hidden, const uint16_t* update, uint64_t count,
+    void* stream);
+
+/* ---- K4/K5: tcgen05 weight-streaming GEMM with fused epilogues ---------------
+ * Y[n][m] = sum_k W[m][k] * X[n][k] for m < M, n < N (N <= 64): FP16 operands,
+ * FP32 accumulation in tensor memory, split-K across a thread-block cluster with
+ * a distributed-shared-memory reduction, then one of the epilogues below.
+ * Replaces cublasGemmEx in gemmBatch / logitsGemmBatch
+ * (src/cuda/model/runner_support.cpp:196-274) plus the elementwise kernel that
+ * follows each projection. K % 8 == 0. */
+enum kk_epilogue {
+    KK_EPI_STORE_F16 = 0,    /* out[n*out_stride+m] = half(acc) */
+    KK_EPI_STORE_F32 = 1,    /* out[n*out_stride+m] = acc */
+    KK_EPI_RESIDUAL = 2,     /* out[...] = hadd(out[...], half(acc)) */
+    KK_EPI_SILU_PAIRS = 3,   /* rows 2i / 2i+1 = gate_i / up_i: out[n*out_stride+i] =
+                                half(silu(half(g)) * half(u)) */
+    KK_EPI_QKV_ROPE = 4,     /* rows [0,q_rows): q, RoPE'd into out; next kv_rows: k,
+                                RoPE'd into the KV page slot; next kv_rows: v into the page */
+    KK_EPI_ARGMAX = 5,       /* fp32 logits (optional) + greedy argmax per column */
+};
+
+typedef struct kk_gemm_desc {
+    const uint16_t* weight;    /* [M][K] fp16 row-major */
+    uint32_t M;
+    uint32_t K;
+    const uint16_t* x;         /* [x_rows][x_stride] fp16 */
+    uint32_t N;
+    uint32_t x_stride;
+    uint32_t x_rows;           /* allocated rows of x (>= N) */
+    uint32_t epilogue;
+    void* out;
+    uint32_t out_stride;
+    uint32_t split_k;          /* 0 = choose automatically */
+    /* KK_EPI_QKV_ROPE */
+    const uint32_t* positions; /* [N] */
+    const kk_kv_slot* slots;   /* [N] */
+    kk_kv_pools pools;
+    uint32_t layer;
+    uint32_t q_rows;
+    uint32_t kv_rows;
+    uint32_t head_dim;
+    float rope_theta;
+    /* KK_EPI_ARGMAX */
+    uint32_t* tokens;          /* [N] greedy ids */
+    void* argmax_workspace;    /* kk_argmax_workspace_bytes(M, N) bytes, zeroed once */
+} kk_gemm_desc;
+
+KK_KAPI uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N);
+KK_KAPI int kk_gemm(const kk_gemm_desc* desc, void* stream);
+
+/* Reads and clears the device-side status words of all kernel modules
+ * (synchronises the stream). 0 = no kernel recorded an error. */
+KK_KAPI int kk_device_status(void* stream);
+
+/* Programmatic dependent launch for subsequent launches on this thread (0/1). */
+KK_KAPI void kk_set_pdl(int enabled);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KK_KERNELS_H */

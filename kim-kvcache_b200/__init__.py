@@ -226,3 +226,85 @@ class Manager:
 
     def invariants(self):
         return bool(self.f["mgr_check_invariants"](self.h))
+
+
+# ---- kernel C ABI (include/kk_kernels.h) ------------------------------------
+
+KK_EINVAL = 1000
+EPI_STORE_F16, EPI_STORE_F32, EPI_RESIDUAL, EPI_SILU_PAIRS, EPI_QKV_ROPE, EPI_ARGMAX = range(6)
+
+
+class KvPools(C.Structure):
+    _fields_ = [("micro", C.c_void_p), ("extent", C.c_void_p), ("micro_capacity", C.c_uint32),
+                ("extent_capacity", C.c_uint32), ("layers", C.c_uint32), ("kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("reserved", C.c_uint32)]
+
+
+class PageDesc(C.Structure):
+    _fields_ = [("slot", C.c_uint32), ("logical_token_begin", C.c_uint32),
+                ("valid_tokens", C.c_uint16), ("kind", C.c_uint8), ("reserved0", C.c_uint8),
+                ("reserved1", C.c_uint32)]
+
+
+class KvSlot(C.Structure):
+    _fields_ = [("slot", C.c_uint32), ("page_token", C.c_uint16), ("kind", C.c_uint8),
+                ("active", C.c_uint8)]
+
+
+class KvCopy(C.Structure):
+    _fields_ = [("src_slot", C.c_uint32), ("dst_slot", C.c_uint32), ("tokens", C.c_uint16),
+                ("src_kind", C.c_uint8), ("dst_kind", C.c_uint8)]
+
+
+class AttnLane(C.Structure):
+    _fields_ = [("desc_offset", C.c_uint32), ("desc_count", C.c_uint32),
+                ("token_count", C.c_uint32), ("item_offset", C.c_uint32),
+                ("item_count", C.c_uint32), ("query_row", C.c_uint32),
+                ("reserved", C.c_uint32 * 2)]
+
+
+class AttnItem(C.Structure):
+    _fields_ = [("lane", C.c_uint32), ("desc_begin", C.c_uint32), ("desc_end", C.c_uint32),
+                ("reserved", C.c_uint32)]
+
+
+class GemmDesc(C.Structure):
+    _fields_ = [("weight", C.c_void_p), ("M", C.c_uint32), ("K", C.c_uint32), ("x", C.c_void_p),
+                ("N", C.c_uint32), ("x_stride", C.c_uint32), ("x_rows", C.c_uint32),
+                ("epilogue", C.c_uint32), ("out", C.c_void_p), ("out_stride", C.c_uint32),
+                ("split_k", C.c_uint32), ("positions", C.c_void_p), ("slots", C.c_void_p),
+                ("pools", KvPools), ("layer", C.c_uint32), ("q_rows", C.c_uint32),
+                ("kv_rows", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
+                ("tokens", C.c_void_p), ("argmax_workspace", C.c_void_p)]
+
+
+_VP = C.c_void_p
+KERNEL_SIGNATURES = {
+    "attention_plan": (_U32, [C.POINTER(PageDesc), C.POINTER(AttnLane), _U32, _U32,
+                              C.POINTER(AttnItem), _U32]),
+    "attention_workspace_bytes": (_U64, [_U32, _U32, _U32, _U32]),
+    "attention_workspace_init": (_I, [_VP, _U32, _VP]),
+    "paged_decode_attention": (_I, [C.POINTER(KvPools), _U32, _U32, _VP, _VP, _U32, _VP, _U32,
+                                    _VP, _U32, _VP, _U32, C.c_float, _VP, _U64, _VP]),
+    "kv_write": (_I, [C.POINTER(KvPools), _U32, _U32, _VP, _U32, _VP, _VP, _U64, _U64, _VP]),
+    "kv_copy_tokens": (_I, [C.POINTER(KvPools), _U32, _U32, _VP, _U32, _VP]),
+    "rmsnorm": (_I, [_VP, _VP, _VP, _U32, _U32, C.c_float, _VP]),
+    "embed_rmsnorm": (_I, [_VP, _VP, _VP, _VP, _VP, _U32, _U32, C.c_float, _VP]),
+    "rope": (_I, [_VP, _U32, _VP, _U32, _VP, _U32, _U32, _U32, _U32, C.c_float, _VP]),
+    "silu_mul": (_I, [_VP, _VP, _VP, _U32, _U32, _VP]),
+    "residual_add": (_I, [_VP, _VP, _U64, _VP]),
+    "argmax_workspace_bytes": (_U64, [_U32, _U32]),
+    "gemm": (_I, [C.POINTER(GemmDesc), _VP]),
+    "device_status": (_I, [_VP]),
+    "set_pdl": (None, [_I]),
+}
+
+_KERNELS = None
+
+
+def kernels() -> dict:
+    """name -> ctypes function for every kk_* kernel entry point."""
+    global _KERNELS
+    if _KERNELS is None:
+        _KERNELS = bind(load_library(), "kk_", KERNEL_SIGNATURES)
+    return _KERNELS

@@ -79,7 +79,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
             print(f"[{obj.name}]\n{log}")
     lib_time = LIB.stat().st_mtime if LIB.exists() else 0.0
     if force or not LIB.exists() or any(o.stat().st_mtime > lib_time for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcuda", "-lpthread"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")

@@ -1,0 +1,542 @@
+// K4/K5 — weight-streaming tensor-core GEMM for sm_100a (tcgen05 + TMEM + TMA).
+//
+// Y[n][m] = sum_k W[m][k] X[n][k]: W is a decoder weight ([out][in] FP16,
+// streamed from HBM exactly once per step), X holds the batch's activations
+// (N <= 64 rows). This replaces the reference's cublasGemmEx projections
+// (src/cuda/model/runner_support.cpp:196-274) and the elementwise kernels that
+// follow them (RoPE, KV write, SwiGLU, residual add, argmax; src/cuda/model/
+// kernels.cu, src/cuda/attention/paged_decode_kernels.cu:65-99).
+//
+// Structure of one CTA (128 threads):
+//  * warp 0 / lane 0 issues TMA loads of 128x64 W tiles and BNx64 X tiles
+//    (128-byte swizzle) into an NS-stage mbarrier ring; W tiles for the first
+//    stages are requested before griddepcontrol.wait, so under programmatic
+//    dependent launch the weight stream starts while the previous kernel is
+//    still finishing;
+//  * warp 1 / lane 0 issues tcgen05.mma (M=128, N=BN, K=16, FP16 in, FP32
+//    accumulate in TMEM) and releases stages with tcgen05.commit;
+//  * all 4 warps drain TMEM with tcgen05.ld.
+// The K dimension is split across the CTAs of a thread-block cluster (up to 8);
+// each CTA parks its FP32 partial tile in shared memory and, after a cluster
+// barrier, reduces a disjoint subset of the batch columns over all CTAs'
+// partials through distributed shared memory (fixed order: deterministic),
+// then runs the fused epilogue for those columns.
+// No TMA multicast is used anywhere.
+#include "../../../include/kk_kernels.h"
+#include "launch.cuh"
+
+#include <cfloat>
+#include <mutex>
+
+namespace kk {
+
+__device__ unsigned int g_gemm_status;
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
+constexpr int kThreads = 128;
+constexpr int kStages = 4;
+constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
+
+struct EpiArgs {
+    std::uint32_t kind;
+    void* out;
+    std::uint32_t out_stride;
+    // KK_EPI_QKV_ROPE
+    std::uint32_t const* positions;
+    kk_kv_slot const* slots;
+    __half* micro;
+    __half* extent;
+    std::uint64_t micro_page;
+    std::uint64_t extent_page;
+    std::uint32_t micro_slots;
+    std::uint32_t extent_slots;
+    std::uint32_t kv_row;        // kv_heads * head_dim
+    std::uint32_t layer;
+    std::uint32_t q_rows;
+    std::uint32_t kv_rows;
+    float theta;
+    // KK_EPI_ARGMAX
+    std::uint32_t* tokens;
+    float* part_val;
+    std::uint32_t* part_idx;
+    std::uint32_t* counter;
+    std::uint32_t num_m_tiles;
+};
+
+struct GemmArgs {
+    std::uint32_t M;
+    std::uint32_t K;
+    std::uint32_t N;
+    std::uint32_t split;
+    std::uint32_t kb_total;
+    EpiArgs epi;
+};
+
+__device__ __forceinline__ bool better(float v, std::uint32_t i, float bv, std::uint32_t bi)
+{
+    return v > bv || (v == bv && i < bi);
+}
+
+template <int BN>
+constexpr std::uint32_t tmemCols()
+{
+    return BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
+}
+
+template <int BN>
+constexpr std::size_t smemBytes()
+{
+    return 1024 /* alignment slack */ + kStages * (kTileWBytes + BN * 128) + 1024 /* barriers + scratch */;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
+    GemmArgs args)
+{
+    extern __shared__ std::uint8_t smem_raw[];
+    std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    std::uint8_t* smem = smem_raw + pad;
+    std::uint8_t* w_stage = smem;
+    std::uint8_t* x_stage = smem + kStages * kTileWBytes;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(x_stage + kStages * BN * 128);
+    std::uint64_t* empty = full + kStages;
+    std::uint64_t* accum = empty + kStages;
+    std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(accum + 1);
+    float* xchg = reinterpret_cast<float*>(tmem_slot + 4);          // [128]
+    float* amax_v = xchg + kBM;                                      // [4]
+    std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4);  // [4]
+    int* flag = reinterpret_cast<int*>(amax_i + 4);
+
+    std::uint32_t const tid = threadIdx.x;
+    std::uint32_t const warp = tid / 32;
+    std::uint32_t const lane = tid % 32;
+    std::uint32_t const S = args.split;
+    std::uint32_t const rank = S > 1 ? cluster_rank() : 0;
+    std::uint32_t const m_tile = blockIdx.y;
+    std::uint32_t const kb_begin = rank * args.kb_total / S;
+    std::uint32_t const nk = (rank + 1) * args.kb_total / S - kb_begin;
+    constexpr std::uint32_t kStageBytes = kTileWBytes + BN * 128;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(accum, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_w);
+        prefetch_tensormap(&tm_x);
+    }
+    if (warp == 2) {
+        tmem_alloc(tmem_slot, tmemCols<BN>());
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    std::uint32_t const tmem = *tmem_slot;
+
+    if (warp == 0 && lane == 0) {
+        // Producer. Weights never depend on the previous kernel: request them
+        // before waiting for it; activations only after.
+        std::uint32_t const pre = nk < kStages ? nk : kStages;
+        std::uint64_t const policy = l2_policy_evict_first();
+        for (std::uint32_t i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(&full[i], kStageBytes);
+            tma_load_2d_hint(w_stage + i * kTileWBytes, &tm_w, &full[i],
+                static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
+        }
+        pdl_wait();
+        for (std::uint32_t i = 0; i < pre; ++i) {
+            tma_load_2d(x_stage + i * BN * 128, &tm_x, &full[i],
+                static_cast<int>((kb_begin + i) * kBK), 0);
+        }
+        for (std::uint32_t i = pre; i < nk; ++i) {
+            std::uint32_t const s = i % kStages;
+            if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, &g_gemm_status)) {
+                break;
+            }
+            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            tma_load_2d_hint(w_stage + s * kTileWBytes, &tm_w, &full[s],
+                static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
+            tma_load_2d(x_stage + s * BN * 128, &tm_x, &full[s],
+                static_cast<int>((kb_begin + i) * kBK), 0);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer.
+        std::uint32_t const idesc = umma_idesc_f16_f32(kBM, BN);
+        for (std::uint32_t i = 0; i < nk; ++i) {
+            std::uint32_t const s = i % kStages;
+            if (!mbar_wait(&full[s], (i / kStages) & 1u, &g_gemm_status)) {
+                break;
+            }
+            tc_fence_after();
+            std::uint64_t const a = umma_desc_k_sw128(w_stage + s * kTileWBytes);
+            std::uint64_t const b = umma_desc_k_sw128(x_stage + s * BN * 128);
+#pragma unroll
+            for (std::uint32_t k = 0; k < kBK / 16; ++k) {
+                // +32 bytes along K inside the 128-byte swizzle row: +2 in addr>>4 units.
+                tc_mma_f16(tmem, a + 2 * k, b + 2 * k, idesc, (i | k) != 0 ? 1u : 0u);
+            }
+            tc_commit(&empty[s]);
+        }
+        tc_commit(accum);
+    }
+    pdl_wait();
+    bool const have_acc = mbar_wait(accum, 0, &g_gemm_status);
+    tc_fence_after();
+    pdl_launch_dependents();
+
+    // TMEM -> this CTA's FP32 partial tile, column-major [BN][128] (aliases the
+    // W stages: every MMA that read them has completed).
+    float* part = reinterpret_cast<float*>(smem);
+    std::uint32_t const row = tid;
+#pragma unroll
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + ((warp * 32u) << 16) + static_cast<std::uint32_t>(c0), v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            part[(c0 + j) * kBM + row] = have_acc && nk != 0 ? v[j] : 0.f;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (S > 1) {
+        cluster_sync();
+    }
+
+    std::uint32_t const n0 = rank * args.N / S;
+    std::uint32_t const n1 = (rank + 1) * args.N / S;
+    std::uint32_t const m = m_tile * kBM + row;
+    EpiArgs const& e = args.epi;
+    std::uint32_t remote[8];
+    for (std::uint32_t r = 0; r < S && r < 8; ++r) {
+        remote[r] = S > 1 ? cluster_map(part, r) : smem_u32(part);
+    }
+    for (std::uint32_t n = n0; n < n1; ++n) {
+        float acc = 0.f;
+        if (S > 1) {
+            for (std::uint32_t r = 0; r < S; ++r) {
+                acc += ld_cluster_f32(remote[r] + (n * kBM + row) * 4u);
+            }
+        } else {
+            acc = part[n * kBM + row];
+        }
+        switch (e.kind) {
+        case KK_EPI_STORE_F16:
+            if (m < args.M) {
+                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + m] = __float2half_rn(acc);
+            }
+            break;
+        case KK_EPI_STORE_F32:
+            if (m < args.M) {
+                static_cast<float*>(e.out)[std::uint64_t(n) * e.out_stride + m] = acc;
+            }
+            break;
+        case KK_EPI_RESIDUAL:
+            if (m < args.M) {
+                __half* h = static_cast<__half*>(e.out) + std::uint64_t(n) * e.out_stride + m;
+                *h = __hadd(*h, __float2half_rn(acc));
+            }
+            break;
+        case KK_EPI_SILU_PAIRS: {
+            float const mine = __half2float(__float2half_rn(acc));
+            float const other = __shfl_xor_sync(0xffffffffu, mine, 1);
+            if ((m & 1u) == 0 && m < args.M) {
+                float const g = mine;
+                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + m / 2] =
+                    __float2half_rn(g / (1.0f + expf(-g)) * other);
+            }
+            break;
+        }
+        case KK_EPI_QKV_ROPE: {
+            float const mine = __half2float(__float2half_rn(acc));
+            xchg[row] = mine;
+            __syncthreads();
+            float const other = xchg[row ^ 32u];
+            __syncthreads();
+            std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
+            if (m >= args.M || m >= kv_end) {
+                break;
+            }
+            bool const is_v = m >= e.q_rows + e.kv_rows;
+            std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
+            float out = mine;
+            if (!is_v) {
+                std::uint32_t const d = idx & 63u;
+                float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+                float const angle = static_cast<float>(e.positions[n]) * inv_freq;
+                float const c = cosf(angle);
+                float const s = sinf(angle);
+                out = d < 32u ? mine * c - other * s : mine * c + other * s;
+            }
+            __half const hv = __float2half_rn(out);
+            if (m < e.q_rows) {
+                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + idx] = hv;
+            } else {
+                kk_kv_slot const sl = e.slots[n];
+                bool const micro = sl.kind == 0;
+                std::uint32_t const cap = micro ? 8u : 64u;
+                if (sl.active && sl.page_token < cap
+                    && (micro ? sl.slot < e.micro_slots : sl.slot < e.extent_slots)) {
+                    __half* page = micro ? e.micro + std::uint64_t(sl.slot) * e.micro_page
+                                         : e.extent + std::uint64_t(sl.slot) * e.extent_page;
+                    std::uint64_t const off = ((std::uint64_t(e.layer) * 2u + (is_v ? 1u : 0u)) * cap
+                        + sl.page_token) * e.kv_row + idx;
+                    page[off] = hv;
+                } else if (sl.active) {
+                    atomicCAS(&g_gemm_status, kErrNone, kErrBadDescriptor);
+                }
+            }
+            break;
+        }
+        case KK_EPI_ARGMAX: {
+            bool const valid = m < args.M;
+            if (valid && e.out != nullptr) {
+                static_cast<float*>(e.out)[std::uint64_t(n) * e.out_stride + m] = acc;
+            }
+            float bv = valid ? acc : -INFINITY;
+            std::uint32_t bi = valid ? m : 0xffffffffu;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                float const ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                std::uint32_t const oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (better(ov, oi, bv, bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) {
+                amax_v[warp] = bv;
+                amax_i[warp] = bi;
+            }
+            __syncthreads();
+            if (tid == 0) {
+                for (int w = 1; w < 4; ++w) {
+                    if (better(amax_v[w], amax_i[w], bv, bi)) {
+                        bv = amax_v[w];
+                        bi = amax_i[w];
+                    }
+                }
+                e.part_val[std::uint64_t(m_tile) * args.N + n] = bv;
+                e.part_idx[std::uint64_t(m_tile) * args.N + n] = bi;
+            }
+            __syncthreads();
+            break;
+        }
+        default:
+            break;
+        }
+    }
+
+    if (e.kind == KK_EPI_ARGMAX) {
+        // The last CTA of the launch folds the per-tile winners of every column.
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            std::uint32_t const done = atomicAdd(e.counter, 1u);
+            *flag = done + 1 == e.num_m_tiles * S;
+        }
+        __syncthreads();
+        if (*flag) {
+            __threadfence();
+            for (std::uint32_t n = tid; n < args.N; n += kThreads) {
+                float bv = -FLT_MAX;     // same starting point as the reference reduction
+                std::uint32_t bi = 0;
+                for (std::uint32_t t = 0; t < e.num_m_tiles; ++t) {
+                    float const v = __ldcg(e.part_val + std::uint64_t(t) * args.N + n);
+                    std::uint32_t const i = __ldcg(e.part_idx + std::uint64_t(t) * args.N + n);
+                    if (better(v, i, bv, bi)) {
+                        bv = v;
+                        bi = i;
+                    }
+                }
+                e.tokens[n] = bi;
+            }
+            if (tid == 0) {
+                *e.counter = 0;
+            }
+        }
+    }
+
+    if (S > 1) {
+        cluster_sync();  // keep this CTA's partial alive until every peer has read it
+    }
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem, tmemCols<BN>());
+    }
+}
+
+// ---- host side ------------------------------------------------------------------
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+    cuuint64_t const*, cuuint64_t const*, cuuint32_t const*, cuuint32_t const*,
+    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encodeFn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q)
+                == cudaSuccess && q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    return fn;
+}
+
+// 2D FP16 tensor [rows][cols] (row stride in elements), box 64 x box_rows, 128B swizzle.
+bool makeMap(CUtensorMap* map, void const* base, std::uint64_t cols, std::uint64_t rows,
+    std::uint64_t stride_elems, std::uint32_t box_rows)
+{
+    EncodeTiledFn const fn = encodeFn();
+    if (fn == nullptr) {
+        return false;
+    }
+    cuuint64_t const dims[2] = {cols, rows};
+    cuuint64_t const strides[1] = {stride_elems * 2};
+    cuuint32_t const box[2] = {static_cast<cuuint32_t>(kBK), box_rows};
+    cuuint32_t const elem_strides[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+               elem_strides, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
+        == CUDA_SUCCESS;
+}
+
+int g_sms = 0;
+
+template <int BN>
+int launchGemm(kk_gemm_desc const& d, GemmArgs args, cudaStream_t stream)
+{
+    static bool configured = false;
+    std::size_t const smem = smemBytes<BN>();
+    if (!configured) {
+        cudaError_t const e = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        if (e != cudaSuccess) {
+            return static_cast<int>(e);
+        }
+        configured = true;
+    }
+    CUtensorMap tm_w{}, tm_x{};
+    if (!makeMap(&tm_w, d.weight, d.K, d.M, d.K, kBM)
+        || !makeMap(&tm_x, d.x, d.K, d.x_rows, d.x_stride, BN)) {
+        return KK_EINVAL;
+    }
+    if (g_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_sms <= 0) {
+            g_sms = 148;
+        }
+    }
+    std::uint32_t const tiles = (d.M + kBM - 1) / kBM;
+    std::uint32_t split = d.split_k;
+    if (split == 0) {
+        // Aim for roughly two CTAs per SM across the launch.
+        std::uint32_t const target = 2u * static_cast<std::uint32_t>(g_sms);
+        split = target / tiles;
+    }
+    std::uint32_t const max_split = args.kb_total < 8u ? args.kb_total : 8u;
+    split = split < 1u ? 1u : (split > max_split ? max_split : split);
+    args.split = split;
+    args.epi.num_m_tiles = tiles;
+    return static_cast<int>(launch(gemm_tc_kernel<BN>, dim3(split, tiles), dim3(kThreads), smem,
+        stream, split, tm_w, tm_x, args));
+}
+
+} // namespace
+} // namespace kk
+
+extern "C" {
+
+uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N)
+{
+    std::uint64_t const tiles = (M + 127u) / 128u;
+    return 256u + tiles * N * 8u;
+}
+
+int kk_gemm(const kk_gemm_desc* d, void* stream)
+{
+    using namespace kk;
+    if (d == nullptr || d->weight == nullptr || d->x == nullptr || d->M == 0 || d->K == 0
+        || d->K % 8 != 0 || d->N == 0 || d->N > 64 || d->x_rows < d->N || d->x_stride < d->K
+        || d->x_stride % 8 != 0 || d->epilogue > KK_EPI_ARGMAX
+        || (reinterpret_cast<std::uintptr_t>(d->weight) & 15u) != 0
+        || (reinterpret_cast<std::uintptr_t>(d->x) & 15u) != 0) {
+        return KK_EINVAL;
+    }
+    GemmArgs args{};
+    args.M = d->M;
+    args.K = d->K;
+    args.N = d->N;
+    args.kb_total = (d->K + kBK - 1) / kBK;
+    EpiArgs& e = args.epi;
+    e.kind = d->epilogue;
+    e.out = d->out;
+    e.out_stride = d->out_stride;
+    if (d->epilogue != KK_EPI_ARGMAX && d->out == nullptr) {
+        return KK_EINVAL;
+    }
+    if (d->epilogue == KK_EPI_SILU_PAIRS && d->M % 2 != 0) {
+        return KK_EINVAL;
+    }
+    if (d->epilogue == KK_EPI_QKV_ROPE) {
+        kk_kv_pools const& p = d->pools;
+        if (d->head_dim != 64 || p.head_dim != 64 || d->positions == nullptr
+            || d->slots == nullptr || d->q_rows % 64 != 0 || d->kv_rows % 64 != 0
+            || d->kv_rows != p.kv_heads * p.head_dim || d->layer >= p.layers
+            || d->M != d->q_rows + 2 * d->kv_rows || !(d->rope_theta > 0.f)) {
+            return KK_EINVAL;
+        }
+        e.positions = d->positions;
+        e.slots = d->slots;
+        e.micro = static_cast<__half*>(p.micro);
+        e.extent = static_cast<__half*>(p.extent);
+        e.kv_row = p.kv_heads * p.head_dim;
+        e.micro_page = std::uint64_t(p.layers) * 2u * 8u * e.kv_row;
+        e.extent_page = std::uint64_t(p.layers) * 2u * 64u * e.kv_row;
+        e.micro_slots = p.micro == nullptr ? 0 : p.micro_capacity;
+        e.extent_slots = p.extent == nullptr ? 0 : p.extent_capacity;
+        e.layer = d->layer;
+        e.q_rows = d->q_rows;
+        e.kv_rows = d->kv_rows;
+        e.theta = d->rope_theta;
+    }
+    if (d->epilogue == KK_EPI_ARGMAX) {
+        if (d->tokens == nullptr || d->argmax_workspace == nullptr) {
+            return KK_EINVAL;
+        }
+        std::uint64_t const tiles = (d->M + 127u) / 128u;
+        char* ws = static_cast<char*>(d->argmax_workspace);
+        e.counter = reinterpret_cast<std::uint32_t*>(ws);
+        e.part_val = reinterpret_cast<float*>(ws + 256);
+        e.part_idx = reinterpret_cast<std::uint32_t*>(ws + 256 + tiles * d->N * 4u);
+        e.tokens = d->tokens;
+    }
+    cudaStream_t const s = static_cast<cudaStream_t>(stream);
+    if (d->N <= 16) {
+        return launchGemm<16>(*d, args, s);
+    }
+    if (d->N <= 32) {
+        return launchGemm<32>(*d, args, s);
+    }
+    return launchGemm<64>(*d, args, s);
+}
+
+} // extern "C"
+
+namespace kk {
+int gemmStatus(cudaStream_t stream) { return readStatus(&g_gemm_status, stream); }
+} // namespace kk

@@ -1,0 +1,162 @@
+// K2 — batched KV append and copy-on-write over the page pools.
+//
+// kk_kv_write: one launch writes the new token's K and V of a range of layers
+// for every lane (the reference issues one tiny launch per lane per layer,
+// src/cuda/engine/transaction.cpp:195-204). One warp moves one (lane, layer,
+// K|V) row of kv_heads*head_dim FP16 values with 16-byte accesses.
+// kk_kv_copy_tokens: partial-tail copy-on-write of the first `tokens` tokens
+// of a page into a fresh page, for a range of layers (reference
+// copyLayerTokensKernel / copyPageTokensKernel, paged_decode_kernels.cu:29-63,
+// page_kernels.cu:46-75). Both are bandwidth-bound byte movers.
+#include "../../../include/kk_kernels.h"
+#include "launch.cuh"
+
+namespace kk {
+
+__device__ unsigned int g_pages_status;
+
+namespace {
+
+struct PoolView {
+    __half* micro;
+    __half* extent;
+    std::uint64_t micro_page;
+    std::uint64_t extent_page;
+    std::uint32_t micro_slots;
+    std::uint32_t extent_slots;
+    std::uint32_t row;         // kv_heads * head_dim elements per token per K|V
+    std::uint32_t layers;
+};
+
+PoolView view(kk_kv_pools const& p)
+{
+    PoolView v{};
+    v.micro = static_cast<__half*>(p.micro);
+    v.extent = static_cast<__half*>(p.extent);
+    v.row = p.kv_heads * p.head_dim;
+    v.micro_page = std::uint64_t(p.layers) * 2u * 8u * v.row;
+    v.extent_page = std::uint64_t(p.layers) * 2u * 64u * v.row;
+    v.micro_slots = p.micro == nullptr ? 0 : p.micro_capacity;
+    v.extent_slots = p.extent == nullptr ? 0 : p.extent_capacity;
+    v.layers = p.layers;
+    return v;
+}
+
+// Start of the (layer, component) block of a page; nullptr if out of bounds.
+__device__ __forceinline__ __half* block_of(PoolView const& v, std::uint32_t kind,
+    std::uint32_t slot, std::uint32_t layer, std::uint32_t component)
+{
+    bool const micro = kind == 0;
+    if (micro ? slot >= v.micro_slots : slot >= v.extent_slots) {
+        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        return nullptr;
+    }
+    std::uint32_t const cap = micro ? 8u : 64u;
+    __half* page = micro ? v.micro + std::uint64_t(slot) * v.micro_page
+                         : v.extent + std::uint64_t(slot) * v.extent_page;
+    return page + (std::uint64_t(layer) * 2u + component) * cap * v.row;
+}
+
+// grid: (num_lanes, layer_count, 2); one warp per row, 8 elements per thread step.
+__global__ void kv_write_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_slot const* slots,
+    __half const* key, __half const* value, std::uint64_t lane_stride, std::uint64_t layer_stride)
+{
+    pdl_wait();
+    std::uint32_t const lane_idx = blockIdx.x;
+    std::uint32_t const layer_off = blockIdx.y;
+    std::uint32_t const component = blockIdx.z;
+    kk_kv_slot const s = slots[lane_idx];
+    if (!s.active) {
+        return;
+    }
+    std::uint32_t const cap = s.kind == 0 ? 8u : 64u;
+    if (s.page_token >= cap) {
+        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        return;
+    }
+    __half* dst = block_of(v, s.kind, s.slot, layer_begin + layer_off, component);
+    if (dst == nullptr) {
+        return;
+    }
+    dst += std::uint64_t(s.page_token) * v.row;
+    __half const* src = (component == 0 ? key : value) + lane_idx * lane_stride
+        + layer_off * layer_stride;
+    for (std::uint32_t i = threadIdx.x * 8u; i < v.row; i += blockDim.x * 8u) {
+        *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4 const*>(src + i);
+    }
+}
+
+// grid: (num_copies, layer_count, 2): copies tokens*row contiguous elements.
+__global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy const* copies)
+{
+    pdl_wait();
+    kk_kv_copy const c = copies[blockIdx.x];
+    std::uint32_t const layer = layer_begin + blockIdx.y;
+    std::uint32_t const component = blockIdx.z;
+    std::uint32_t const src_cap = c.src_kind == 0 ? 8u : 64u;
+    std::uint32_t const dst_cap = c.dst_kind == 0 ? 8u : 64u;
+    if (c.tokens > src_cap || c.tokens > dst_cap) {
+        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        return;
+    }
+    __half const* src = block_of(v, c.src_kind, c.src_slot, layer, component);
+    __half* dst = block_of(v, c.dst_kind, c.dst_slot, layer, component);
+    if (src == nullptr || dst == nullptr) {
+        return;
+    }
+    std::uint64_t const n = std::uint64_t(c.tokens) * v.row;
+    for (std::uint64_t i = threadIdx.x * 8u; i < n; i += blockDim.x * 8u) {
+        *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4 const*>(src + i);
+    }
+}
+
+bool poolsOk(kk_kv_pools const* p)
+{
+    return p != nullptr && p->layers != 0 && p->kv_heads != 0 && p->head_dim != 0
+        && (p->kv_heads * p->head_dim) % 8 == 0;
+}
+
+} // namespace
+} // namespace kk
+
+extern "C" {
+
+int kk_kv_write(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t layer_count,
+    const kk_kv_slot* slots, uint32_t num_lanes, const uint16_t* key, const uint16_t* value,
+    uint64_t lane_stride, uint64_t layer_stride, void* stream)
+{
+    using namespace kk;
+    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
+        || slots == nullptr || key == nullptr || value == nullptr || lane_stride % 8 != 0
+        || layer_stride % 8 != 0 || num_lanes > 65535u) {
+        return KK_EINVAL;
+    }
+    if (num_lanes == 0) {
+        return 0;
+    }
+    return static_cast<int>(launch(kv_write_kernel, dim3(num_lanes, layer_count, 2), dim3(64), 0,
+        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, slots,
+        reinterpret_cast<__half const*>(key), reinterpret_cast<__half const*>(value), lane_stride,
+        layer_stride));
+}
+
+int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t layer_count,
+    const kk_kv_copy* copies, uint32_t num_copies, void* stream)
+{
+    using namespace kk;
+    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
+        || copies == nullptr || num_copies > 65535u) {
+        return KK_EINVAL;
+    }
+    if (num_copies == 0) {
+        return 0;
+    }
+    return static_cast<int>(launch(kv_copy_kernel, dim3(num_copies, layer_count, 2), dim3(128), 0,
+        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, copies));
+}
+
+} // extern "C"
+
+namespace kk {
+int pagesStatus(cudaStream_t stream) { return readStatus(&g_pages_status, stream); }
+} // namespace kk

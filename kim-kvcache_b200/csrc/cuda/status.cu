@@ -1,0 +1,31 @@
+// Device status words of the kernel modules and the PDL switch.
+#include "../../../include/kk_kernels.h"
+#include "launch.cuh"
+
+namespace kk {
+
+thread_local bool g_pdl_enabled = false;
+
+int attentionStatus(cudaStream_t stream);
+int pagesStatus(cudaStream_t stream);
+int gemmStatus(cudaStream_t stream);
+
+} // namespace kk
+
+extern "C" {
+
+int kk_device_status(void* stream)
+{
+    cudaStream_t const s = static_cast<cudaStream_t>(stream);
+    int const codes[3] = {kk::attentionStatus(s), kk::pagesStatus(s), kk::gemmStatus(s)};
+    for (int c : codes) {
+        if (c != 0) {
+            return c;
+        }
+    }
+    return 0;
+}
+
+void kk_set_pdl(int enabled) { kk::g_pdl_enabled = enabled != 0; }
+
+} // extern "C"

@@ -1,0 +1,259 @@
+"""GPU numerics of the sm_100a kernels through the C ABI (include/kk_kernels.h),
+each against a plain PyTorch FP32 reference of the same op. Tolerances are
+written per test; integer / byte work (KV writes, copies, argmax) is exact."""
+import ctypes as C
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import (attention_ref, build_tables, descs_and_lanes, gather_kv, make_pools, p,
+                      rope_ref, to_device_bytes)
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+
+@pytest.fixture(scope="module")
+def K(kk):
+    return kk.kernels()
+
+
+def sync_ok(K):
+    torch.cuda.synchronize()
+    assert K["device_status"](None) == 0
+
+
+def gemm(kk, K, w, x, epi, out=None, out_stride=0, split=0, **extra):
+    d = kk.GemmDesc()
+    d.weight, d.M, d.K = p(w), w.shape[0], w.shape[1]
+    d.x, d.N, d.x_stride, d.x_rows = p(x), extra.pop("N", x.shape[0]), x.shape[1], x.shape[0]
+    d.epilogue, d.out, d.out_stride, d.split_k = epi, p(out), out_stride, split
+    for k_, v in extra.items():
+        setattr(d, k_, v)
+    rc = K["gemm"](C.byref(d), None)
+    assert rc == 0, f"kk_gemm returned {rc}"
+
+
+@pytest.mark.parametrize("M,Kd,N,split", [
+    (128, 64, 16, 1), (256, 2048, 32, 0), (300, 1000, 7, 3), (2560, 2048, 32, 0),
+    (2048, 5632, 64, 0), (640, 512, 1, 2), (11264, 2048, 33, 0), (100, 256, 64, 4)])
+def test_gemm_store_f32_matches_torch(kk, K, M, Kd, N, split):
+    g = torch.Generator().manual_seed(M * 7 + Kd + N)
+    w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
+    x = torch.randn(N, Kd, generator=g).half().cuda()
+    out = torch.full((N, M), float("nan"), device="cuda")
+    gemm(kk, K, w, x, kk.EPI_STORE_F32, out, M, split)
+    sync_ok(K)
+    ref = (x.float() @ w.float().T)
+    torch.testing.assert_close(out, ref, atol=2e-3, rtol=1e-3)  # FP32 accumulation
+
+
+def test_gemm_store_f16_and_residual(kk, K):
+    g = torch.Generator().manual_seed(3)
+    M, Kd, N = 512, 768, 24
+    w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
+    x = torch.randn(N, Kd, generator=g).half().cuda()
+    acc = (x.float() @ w.float().T)
+    out = torch.zeros(N, M, dtype=torch.half, device="cuda")
+    gemm(kk, K, w, x, kk.EPI_STORE_F16, out, M)
+    h = torch.randn(N, M, generator=g).half().cuda()
+    h2 = h.clone()
+    gemm(kk, K, w, x, kk.EPI_RESIDUAL, h2, M)
+    sync_ok(K)
+    # rounding point: half(acc), then an FP16 add; allow one FP16 ulp of slack
+    torch.testing.assert_close(out.float(), acc.half().float(), atol=2e-3, rtol=2e-3)
+    torch.testing.assert_close(h2.float(), (h.float() + acc.half().float()).half().float(),
+                               atol=4e-3, rtol=2e-3)
+
+
+def test_gemm_silu_pairs(kk, K):
+    g = torch.Generator().manual_seed(5)
+    inter, Kd, N = 384, 512, 9
+    wg = (torch.randn(inter, Kd, generator=g) * 0.05).half()
+    wu = (torch.randn(inter, Kd, generator=g) * 0.05).half()
+    w = torch.stack([wg, wu], dim=1).reshape(2 * inter, Kd).cuda()  # row 2i gate, 2i+1 up
+    x = torch.randn(N, Kd, generator=g).half().cuda()
+    out = torch.zeros(N, inter, dtype=torch.half, device="cuda")
+    gemm(kk, K, w, x, kk.EPI_SILU_PAIRS, out, inter)
+    sync_ok(K)
+    gate = (x.float() @ wg.cuda().float().T).half().float()
+    up = (x.float() @ wu.cuda().float().T).half().float()
+    ref = (gate / (1 + torch.exp(-gate)) * up).half()
+    torch.testing.assert_close(out.float(), ref.float(), atol=5e-3, rtol=5e-3)
+
+
+def test_gemm_qkv_rope_writes_q_and_pages(kk, K):
+    layers, hkv, hq, D, hidden = 3, 2, 8, 64, 256
+    pools, micro, extent = make_pools(kk, layers, hkv, D, 16, 4, seed=1)
+    g = torch.Generator().manual_seed(9)
+    M = (hq + 2 * hkv) * D
+    w = (torch.randn(M, hidden, generator=g) * 0.05).half().cuda()
+    N = 5
+    x = torch.randn(16, hidden, generator=g).half().cuda()
+    positions = torch.tensor([0, 7, 100, 513, 2047], dtype=torch.int32).cuda()
+    slots = (kk.KvSlot * N)(*[kk.KvSlot(s, t, kd, 1) for s, t, kd in
+                              [(3, 0, 0), (5, 7, 0), (1, 36, 1), (9, 2, 0), (2, 63, 1)]])
+    slots_dev = to_device_bytes(slots)
+    q_out = torch.zeros(N, hq * D, dtype=torch.half, device="cuda")
+    layer = 1
+    before_micro, before_extent = micro.clone(), extent.clone()
+    gemm(kk, K, w, x, kk.EPI_QKV_ROPE, q_out, hq * D, N=N, positions=p(positions),
+         slots=p(slots_dev), pools=pools, layer=layer, q_rows=hq * D, kv_rows=hkv * D,
+         head_dim=D, rope_theta=10000.0)
+    sync_ok(K)
+    acc = (x[:N].float() @ w.float().T).half()  # [N, M] rounded projection outputs
+    q_ref = rope_ref(acc[:, :hq * D].reshape(N, hq, D), positions, 10000.0).reshape(N, -1)
+    k_ref = rope_ref(acc[:, hq * D:(hq + hkv) * D].reshape(N, hkv, D), positions, 10000.0)
+    v_ref = acc[:, (hq + hkv) * D:].reshape(N, hkv, D)
+    torch.testing.assert_close(q_out.float(), q_ref.float(), atol=4e-3, rtol=4e-3)
+    for n in range(N):
+        s = slots[n]
+        pool = micro if s.kind == 0 else extent
+        torch.testing.assert_close(pool[s.slot, layer, 0, s.page_token].float(), k_ref[n].float(),
+                                   atol=4e-3, rtol=4e-3)
+        assert torch.equal(pool[s.slot, layer, 1, s.page_token], v_ref[n])
+    # nothing else in the pools changed
+    mask_m = torch.ones_like(micro, dtype=torch.bool)
+    mask_e = torch.ones_like(extent, dtype=torch.bool)
+    for n in range(N):
+        s = slots[n]
+        (mask_m if s.kind == 0 else mask_e)[s.slot, layer, :, s.page_token] = False
+    assert torch.equal(micro[mask_m], before_micro[mask_m])
+    assert torch.equal(extent[mask_e], before_extent[mask_e])
+
+
+@pytest.mark.parametrize("V,N", [(32000, 4), (1000, 33), (130, 1)])
+def test_gemm_argmax_matches_numpy(kk, K, V, N):
+    g = torch.Generator().manual_seed(V + N)
+    Kd = 256
+    w = (torch.randn(V, Kd, generator=g) * 0.05).half().cuda()
+    x = torch.randn(64, Kd, generator=g).half().cuda()
+    if V == 130:
+        w[7] = w[100]  # exact tie between rows 7 and 100 -> lowest index wins
+        w[100, 0] = w[7, 0]
+    tokens = torch.zeros(N, dtype=torch.int32, device="cuda")
+    ws = torch.zeros(K["argmax_workspace_bytes"](V, N), dtype=torch.uint8, device="cuda")
+    logits = torch.zeros(N, V, device="cuda")
+    for _ in range(2):  # the completion counter must reset itself between launches
+        gemm(kk, K, w, x, kk.EPI_ARGMAX, logits, V, N=N, tokens=p(tokens), argmax_workspace=p(ws))
+        sync_ok(K)
+        ref = np.argmax(logits.cpu().numpy(), axis=1)
+        assert tokens.cpu().numpy().tolist() == ref.tolist()
+    torch.testing.assert_close(logits, x[:N].float() @ w.float().T, atol=2e-3, rtol=1e-3)
+
+
+@pytest.mark.parametrize("contexts,target", [
+    ([17, 100, 513, 2000], 256), ([1, 8, 9, 64, 65], 64), ([4096, 1024, 3000], 512),
+    ([33], 8)])
+@pytest.mark.parametrize("hkv,hq", [(4, 32), (2, 8), (1, 16)])
+def test_paged_attention_matches_torch(kk, K, contexts, target, hkv, hq):
+    layers, D = 2, 64
+    rng = random.Random(sum(contexts) + hq)
+    micro_cap = sum((c % 64 + 7) // 8 for c in contexts) + 16
+    extent_cap = sum(c // 64 for c in contexts) + 4
+    pools, micro, extent = make_pools(kk, layers, hkv, D, micro_cap, extent_cap, seed=len(contexts))
+    tables = build_tables(contexts, micro_cap, extent_cap, rng)
+    descs, lanes = descs_and_lanes(kk, tables)
+    max_items = 4096
+    items = (kk.AttnItem * max_items)()
+    n_items = K["attention_plan"](descs, lanes, len(tables), target, items, max_items)
+    B = len(contexts)
+    q = (torch.randn(B, hq * D) / 8).half().cuda()
+    out = torch.zeros(B, hq * D, dtype=torch.half, device="cuda")
+    ws_bytes = K["attention_workspace_bytes"](B, n_items, hq, D)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    d_descs, d_lanes, d_items = to_device_bytes(descs), to_device_bytes(lanes), to_device_bytes(items)
+    scale = 1.0 / 8.0
+    for layer in range(layers):
+        rc = K["paged_decode_attention"](C.byref(pools), layer, hq, p(d_descs), p(d_lanes), B,
+                                         p(d_items), n_items, p(q), hq * D, p(out), hq * D,
+                                         scale, p(ws), ws_bytes, None)
+        assert rc == 0
+        sync_ok(K)
+        for b, tbl in enumerate(tables):
+            k, v = gather_kv(micro, extent, tbl, layer)
+            ref = attention_ref(q[b].view(hq, D), k, v, scale)
+            torch.testing.assert_close(out[b].view(hq, D).float(), ref, atol=2e-3, rtol=2e-2)
+
+
+def test_kv_write_and_copy_are_exact(kk, K):
+    layers, hkv, D = 4, 4, 64
+    pools, micro, extent = make_pools(kk, layers, hkv, D, 12, 3, seed=11)
+    B = 3
+    key = torch.randn(B, layers, hkv * D).half().cuda()
+    val = torch.randn(B, layers, hkv * D).half().cuda()
+    slots = (kk.KvSlot * B)(kk.KvSlot(2, 5, 0, 1), kk.KvSlot(1, 40, 1, 1), kk.KvSlot(7, 0, 0, 0))
+    d_slots = to_device_bytes(slots)
+    m0, e0 = micro.clone(), extent.clone()
+    rc = K["kv_write"](C.byref(pools), 1, 2, p(d_slots), B, p(key[:, 1]), p(val[:, 1]),
+                       layers * hkv * D, hkv * D, None)
+    assert rc == 0
+    sync_ok(K)
+    for li, layer in enumerate([1, 2]):
+        assert torch.equal(micro[2, layer, 0, 5].flatten(), key[0, layer])
+        assert torch.equal(micro[2, layer, 1, 5].flatten(), val[0, layer])
+        assert torch.equal(extent[1, layer, 0, 40].flatten(), key[1, layer])
+        assert torch.equal(extent[1, layer, 1, 40].flatten(), val[1, layer])
+    assert torch.equal(micro[7], m0[7])  # inactive lane untouched
+    assert torch.equal(micro[2, 0], m0[2, 0]) and torch.equal(micro[2, 3], m0[2, 3])
+    copies = (kk.KvCopy * 2)(kk.KvCopy(2, 9, 6, 0, 0), kk.KvCopy(1, 2, 8, 1, 1))
+    d_copies = to_device_bytes(copies)
+    m1, e1 = micro.clone(), extent.clone()
+    assert K["kv_copy_tokens"](C.byref(pools), 0, layers, p(d_copies), 2, None) == 0
+    sync_ok(K)
+    assert torch.equal(micro[9, :, :, :6], m1[2, :, :, :6])
+    assert torch.equal(micro[9, :, :, 6:], m1[9, :, :, 6:])
+    assert torch.equal(extent[2, :, :, :8], e1[1, :, :, :8])
+    assert torch.equal(extent[2, :, :, 8:], e1[2, :, :, 8:])
+
+
+def test_rmsnorm_embedding_rope_silu_residual(kk, K):
+    g = torch.Generator().manual_seed(21)
+    rows, cols, V = 6, 2048, 100
+    embed = torch.randn(V, cols, generator=g).half().cuda()
+    weight = (1 + 0.1 * torch.randn(cols, generator=g)).half().cuda()
+    tokens = torch.tensor([3, 99, 0, 3, 50, 7], dtype=torch.int32).cuda()
+    hidden = torch.zeros(rows, cols, dtype=torch.half, device="cuda")
+    y = torch.zeros_like(hidden)
+    assert K["embed_rmsnorm"](p(embed), p(tokens), p(weight), p(hidden), p(y), rows, cols, 1e-5, None) == 0
+    y2 = torch.zeros_like(hidden)
+    assert K["rmsnorm"](p(hidden), p(weight), p(y2), rows, cols, 1e-5, None) == 0
+    sync_ok(K)
+    x = embed[tokens.long()].float()
+    ref = (x * torch.rsqrt((x * x).mean(-1, keepdim=True) + 1e-5) * weight.float()).half()
+    assert torch.equal(hidden, embed[tokens.long()])
+    torch.testing.assert_close(y.float(), ref.float(), atol=2e-3, rtol=2e-3)
+    assert torch.equal(y, y2)
+    hq, hkv, D = 4, 2, 64
+    q = torch.randn(rows, hq * D, generator=g).half().cuda()
+    k = torch.randn(rows, hkv * D, generator=g).half().cuda()
+    pos = torch.tensor([0, 1, 17, 400, 2047, 4000], dtype=torch.int32).cuda()
+    q_ref = rope_ref(q.view(rows, hq, D), pos, 10000.0).view(rows, -1)
+    k_ref = rope_ref(k.view(rows, hkv, D), pos, 10000.0).view(rows, -1)
+    assert K["rope"](p(q), hq * D, p(k), hkv * D, p(pos), rows, hq, hkv, D, 10000.0, None) == 0
+    gate = torch.randn(rows, 512, generator=g).half().cuda()
+    up = torch.randn(rows, 512, generator=g).half().cuda()
+    act = torch.zeros_like(gate)
+    assert K["silu_mul"](p(gate), p(up), p(act), rows, 512, None) == 0
+    h = torch.randn(rows, 512, generator=g).half().cuda()
+    h0 = h.clone()
+    assert K["residual_add"](p(h), p(up), rows * 512, None) == 0
+    sync_ok(K)
+    torch.testing.assert_close(q.float(), q_ref.float(), atol=4e-3, rtol=4e-3)
+    torch.testing.assert_close(k.float(), k_ref.float(), atol=4e-3, rtol=4e-3)
+    gf = gate.float()
+    torch.testing.assert_close(act.float(), (gf / (1 + torch.exp(-gf)) * up.float()).half().float(),
+                               atol=4e-3, rtol=4e-3)
+    torch.testing.assert_close(h.float(), (h0 + up).float(), atol=4e-3, rtol=1e-3)
+
+
+def test_invalid_arguments_are_rejected_without_launch(kk, K):
+    d = kk.GemmDesc()
+    assert K["gemm"](C.byref(d), None) == kk.KK_EINVAL
+    pools = kk.KvPools(0, 0, 0, 0, 1, 4, 64, 0)
+    assert K["paged_decode_attention"](C.byref(pools), 0, 32, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0.125,
+                                       0, 0, None) == kk.KK_EINVAL
