@@ -115,7 +115,9 @@ def test_gemm_qkv_rope_writes_q_and_pages(kk, K):
         pool = micro if s.kind == 0 else extent
         torch.testing.assert_close(pool[s.slot, layer, 0, s.page_token].float(), k_ref[n].float(),
                                    atol=4e-3, rtol=4e-3)
-        assert torch.equal(pool[s.slot, layer, 1, s.page_token], v_ref[n])
+        # V is the rounded projection itself; FP32 summation order may move it by one ulp
+        torch.testing.assert_close(pool[s.slot, layer, 1, s.page_token].float(), v_ref[n].float(),
+                                   atol=2e-3, rtol=2e-3)
     # nothing else in the pools changed
     mask_m = torch.ones_like(micro, dtype=torch.bool)
     mask_e = torch.ones_like(extent, dtype=torch.bool)
