@@ -128,6 +128,16 @@ KK_KAPI int kk_kv_write(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t
 KK_KAPI int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin,
     uint32_t layer_count, const kk_kv_copy* copies, uint32_t num_copies, void* stream);
 
+/* Promotion copy: the 8 micro pages micro_slots[0..7] (all layers) become the
+ * extent page extent_slot, tokens 8k..8k+7 <- micro page k (replaces
+ * launchPromotion, src/cuda/kv/page_kernels.cu:129-182). */
+KK_KAPI int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots_host,
+    uint32_t extent_slot, void* stream);
+/* Deterministic pseudo-random FP16 fill (uniform in [-scale, scale)) for
+ * synthetic KV pages and test tensors; same (seed, index) -> same value. */
+KK_KAPI int kk_fill_fp16(uint16_t* data, uint64_t count, uint64_t seed, float scale,
+    void* stream);
+
 /* ---- K3: norms, RoPE, SiLU gate, residual -------------------------------------
  * Replace launchRmsNorm(Batch), launchRope(Batch), launchSwiGlu, launchResidualAdd,
  * launchEmbedding(Batch) (src/cuda/model/kernels.cu:16-218). */

@@ -138,6 +138,144 @@ KK_API int kkrt_mgr_check_invariants(void* mgr);
 KK_API uint16_t kkrt_float_to_half(float value);
 KK_API float kkrt_half_to_float(uint16_t value);
 
+
+/* ---- CUDA KV backend (include/kim-kv/cuda/cuda_engine_kv_backend.h:11-29) ---- */
+
+typedef struct kk_backend_snapshot {  /* reference EngineKvBackendSnapshot (engine_kv.h:372-391) */
+    uint64_t request_count;
+    uint64_t active_transaction_count;
+    uint64_t committed_token_count;
+    uint64_t batched_attention_submissions;
+    uint64_t batched_attention_lanes;
+    uint32_t allocated_micro_pages;
+    uint32_t allocated_extent_pages;
+    uint64_t storage_reserved_bytes;
+} kk_backend_snapshot;
+
+/* createHeterogeneousCudaEngineKvBackend (backend.cpp:557): NULL on failure. */
+KK_API void* kkrt_backend_create(uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
+    uint32_t q_heads, uint64_t attention_workspace_bytes, uint32_t micro_capacity,
+    uint32_t extent_capacity);
+KK_API void kkrt_backend_destroy(void* backend);
+/* createRequest / forkRequest / releaseRequest (backend.cpp:341-384): EngineKvError. */
+KK_API int kkrt_backend_create_request(void* backend, uint64_t request_id);
+KK_API int kkrt_backend_fork(void* backend, uint64_t source_id, uint64_t child_id);
+KK_API int kkrt_backend_release(void* backend, uint64_t request_id);
+KK_API int kkrt_backend_check_invariants(void* backend);
+KK_API void kkrt_backend_snapshot(void* backend, kk_backend_snapshot* out);
+/* injectCudaEngineFailureOnce (backend.cpp:600): point 0 submission, 1 completion. */
+KK_API int kkrt_backend_inject_failure(void* backend, int point);
+/* Device page pools of the backend (this library's kernel ABI view). */
+KK_API int kkrt_backend_pools(void* backend, void* pools_out /* kk_kv_pools* */);
+/* Committed block table of a request (1 = found). */
+KK_API int kkrt_backend_block_table(void* backend, uint64_t request_id, kk_table_out* out);
+/* Library extensions for building long prefixes without running the model:
+ * metadata append of n tokens (KvCacheManager::append, kv_cache_append.cpp:12),
+ * sealTail (kv_cache_lifecycle.cpp:12), and one promotion of the 8 micro pages
+ * at logical_begin into an extent page, data copy included
+ * (CudaKvCache::promote, src/cuda/kv/cache.cpp:172-229). EngineKvError. */
+KK_API int kkrt_backend_append(void* backend, uint64_t request_id, uint32_t token_count);
+KK_API int kkrt_backend_seal(void* backend, uint64_t request_id);
+KK_API int kkrt_backend_promote(void* backend, uint64_t request_id, uint32_t logical_begin,
+    void* stream);
+
+/* ---- per-layer token transactions (engine_kv.h:255-351) ---- */
+/* reserveToken: returns a transaction handle or NULL; *status = EngineKvError. */
+KK_API void* kkrt_txn_reserve(void* backend, uint64_t request_id, uint32_t expected_committed,
+    void* stream, int* status);
+KK_API int kkrt_txn_write_layer(void* txn, uint32_t layer, const void* device_key,
+    const void* device_value);
+KK_API int kkrt_txn_attend_layer(void* txn, uint32_t layer, const void* device_query,
+    void* device_output, void* device_workspace, uint64_t workspace_bytes, float scale);
+/* attendLayerBatch over n transactions; queries/outputs are rows of one buffer each
+ * (row stride row_bytes); statuses receives one EngineKvError per lane. */
+KK_API void kkrt_txn_attend_batch(void* const* txns, uint32_t n, uint32_t layer,
+    const void* device_query, void* device_output, uint64_t row_bytes, void* device_workspace,
+    uint64_t workspace_bytes, float scale, int* statuses);
+KK_API int kkrt_txn_commit(void* txn);
+KK_API int kkrt_txn_rollback(void* txn);
+/* TokenTransactionPhase (engine_kv.h:210-218). */
+KK_API int kkrt_txn_phase(void* txn);
+KK_API void kkrt_txn_destroy(void* txn);   /* rolls back if still active */
+
+/* ---- CUDA TinyLlama runner (include/kim-kv/cuda/cuda_model_runner.h:178-184) ---- */
+KK_API void* kkrt_runner_create(const char* manifest_path, const char* data_path, void* backend,
+    void* stream, uint32_t max_batch_size, int use_cuda_graphs, int verify_checksums,
+    int* status, char* detail, uint32_t detail_capacity);
+KK_API void kkrt_runner_destroy(void* runner);
+/* generationForwardBatch (runner.cpp:410): per lane ok flag + greedy token.
+ * Returns 1 when the batch result is well formed. */
+KK_API int kkrt_runner_forward_batch(void* runner, uint32_t n, const uint64_t* request_ids,
+    const uint32_t* token_ids, const uint32_t* positions, uint32_t* out_tokens, uint8_t* out_ok);
+/* forwardToken (runner.cpp:53) with optional captures (each may be NULL):
+ * logits [vocab] f32, embedding / final_hidden [hidden] f16, layer_hidden
+ * [n_layers][hidden] f16 for the listed layers. Returns CudaModelRunnerError. */
+KK_API int kkrt_runner_forward_token(void* runner, uint64_t request_id, uint32_t token_id,
+    uint32_t position, uint32_t* out_token, float* logits, uint16_t* embedding,
+    uint16_t* final_hidden, const uint32_t* layers, uint32_t n_layers, uint16_t* layer_hidden);
+KK_API float kkrt_runner_last_step_ms(void* runner);
+KK_API uint32_t kkrt_runner_last_launches(void* runner);
+
+/* ---- generation loops (generation.h:178-202, iteration_scheduler.h:139-181) ---- */
+typedef struct kk_terminal {
+    uint64_t request_id;
+    uint8_t reason;            /* GenerationTerminalReason */
+    uint8_t error;             /* GenerationError */
+    uint16_t reserved;
+    uint32_t token_count;
+    uint32_t prompt_tokens;
+    uint32_t completion_tokens;
+    uint64_t ttft_ns;
+    uint64_t tpot_ns;
+    uint64_t e2e_ns;
+} kk_terminal;
+
+typedef struct kk_iteration {
+    uint64_t iteration;
+    uint32_t model_forward_tokens;
+    uint32_t model_forward_batches;
+    uint32_t prefill_tokens;
+    uint32_t decode_tokens;
+    uint32_t terminals_produced;
+    uint32_t reserved;
+} kk_iteration;
+
+/* model_runner: a runner handle from kkrt_runner_create or kkrt_fake_runner_create. */
+KK_API void* kkrt_sched_create(void* backend, void* model_runner, uint32_t max_active,
+    uint32_t max_batched_tokens, uint64_t max_kv_tokens, uint32_t prefill_chunk);
+KK_API void kkrt_sched_destroy(void* sched);
+/* submit: returns SchedulerAdmissionError (0 accepted). eos < 0: model default. */
+KK_API int kkrt_sched_submit(void* sched, uint64_t request_id, const uint32_t* prompt,
+    uint32_t prompt_len, uint32_t max_new_tokens, int64_t eos);
+KK_API int kkrt_sched_cancel(void* sched, uint64_t request_id);
+KK_API void kkrt_sched_run_iteration(void* sched, kk_iteration* out);
+KK_API void kkrt_sched_stop(void* sched);
+KK_API int kkrt_sched_idle(void* sched);
+/* drain / takeTerminals: fills up to cap terminals and their output tokens
+ * (concatenated, token_capacity total); returns the number of terminals. */
+KK_API uint32_t kkrt_sched_drain(void* sched, kk_terminal* out, uint32_t cap, uint32_t* tokens,
+    uint32_t token_capacity);
+KK_API uint32_t kkrt_sched_take_terminals(void* sched, kk_terminal* out, uint32_t cap,
+    uint32_t* tokens, uint32_t token_capacity);
+/* SingleRequestGenerationRuntime::generate; returns 1 and fills out/tokens. */
+KK_API int kkrt_generate(void* backend, void* model_runner, uint64_t request_id,
+    const uint32_t* prompt, uint32_t prompt_len, uint32_t max_new_tokens, int64_t eos,
+    kk_terminal* out, uint32_t* tokens, uint32_t token_capacity);
+
+/* ---- SPI test doubles (no device): the reference contract tests' fakes ---- */
+/* A KV backend that only tracks request lifecycles. */
+KK_API void* kkrt_fake_backend_create(void);
+KK_API void kkrt_fake_backend_destroy(void* backend);
+/* A model runner whose greedy token is a fixed hash of (request, token,
+ * position) mod vocab; it logs every batch it receives. fail_request: a
+ * request id whose steps fail (0 = none). */
+KK_API void* kkrt_fake_runner_create(uint32_t vocab, uint32_t max_batch, uint32_t eos,
+    uint32_t max_positions, uint64_t fail_request);
+KK_API void kkrt_fake_runner_destroy(void* runner);
+/* Batch log: sizes of the batches so far and their items (request, token, position). */
+KK_API uint32_t kkrt_fake_runner_log(void* runner, uint32_t* batch_sizes, uint32_t cap_batches,
+    uint64_t* items, uint32_t cap_items);
+
 #ifdef __cplusplus
 }
 #endif

@@ -308,3 +308,140 @@ def kernels() -> dict:
     if _KERNELS is None:
         _KERNELS = bind(load_library(), "kk_", KERNEL_SIGNATURES)
     return _KERNELS
+
+
+# ---- runtime C ABI (include/kk_runtime.h): backend, transactions, runner, scheduler ----
+
+class BackendSnapshot(C.Structure):
+    _fields_ = [("request_count", C.c_uint64), ("active_transaction_count", C.c_uint64),
+                ("committed_token_count", C.c_uint64), ("batched_attention_submissions", C.c_uint64),
+                ("batched_attention_lanes", C.c_uint64), ("allocated_micro_pages", C.c_uint32),
+                ("allocated_extent_pages", C.c_uint32), ("storage_reserved_bytes", C.c_uint64)]
+
+
+class Terminal(C.Structure):
+    _fields_ = [("request_id", C.c_uint64), ("reason", C.c_uint8), ("error", C.c_uint8),
+                ("reserved", C.c_uint16), ("token_count", C.c_uint32),
+                ("prompt_tokens", C.c_uint32), ("completion_tokens", C.c_uint32),
+                ("ttft_ns", C.c_uint64), ("tpot_ns", C.c_uint64), ("e2e_ns", C.c_uint64)]
+
+
+class Iteration(C.Structure):
+    _fields_ = [("iteration", C.c_uint64), ("model_forward_tokens", C.c_uint32),
+                ("model_forward_batches", C.c_uint32), ("prefill_tokens", C.c_uint32),
+                ("decode_tokens", C.c_uint32), ("terminals_produced", C.c_uint32),
+                ("reserved", C.c_uint32)]
+
+
+_I64, _F = C.c_int64, C.c_float
+_PU32, _PU64 = C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)
+RUNTIME_SIGNATURES = {
+    "backend_create": (_VP, [_U32, _U32, _U32, _U32, _U64, _U32, _U32]),
+    "backend_destroy": (None, [_VP]),
+    "backend_create_request": (_I, [_VP, _U64]),
+    "backend_fork": (_I, [_VP, _U64, _U64]),
+    "backend_release": (_I, [_VP, _U64]),
+    "backend_check_invariants": (_I, [_VP]),
+    "backend_snapshot": (None, [_VP, C.POINTER(BackendSnapshot)]),
+    "backend_inject_failure": (_I, [_VP, _I]),
+    "backend_pools": (_I, [_VP, C.POINTER(KvPools)]),
+    "backend_block_table": (_I, [_VP, _U64, C.POINTER(KkTableOut)]),
+    "backend_append": (_I, [_VP, _U64, _U32]),
+    "backend_seal": (_I, [_VP, _U64]),
+    "backend_promote": (_I, [_VP, _U64, _U32, _VP]),
+    "txn_reserve": (_VP, [_VP, _U64, _U32, _VP, C.POINTER(_I)]),
+    "txn_write_layer": (_I, [_VP, _U32, _VP, _VP]),
+    "txn_attend_layer": (_I, [_VP, _U32, _VP, _VP, _VP, _U64, _F]),
+    "txn_attend_batch": (None, [C.POINTER(_VP), _U32, _U32, _VP, _VP, _U64, _VP, _U64, _F,
+                                C.POINTER(_I)]),
+    "txn_commit": (_I, [_VP]),
+    "txn_rollback": (_I, [_VP]),
+    "txn_phase": (_I, [_VP]),
+    "txn_destroy": (None, [_VP]),
+    "runner_create": (_VP, [C.c_char_p, C.c_char_p, _VP, _VP, _U32, _I, _I, C.POINTER(_I),
+                            C.c_char_p, _U32]),
+    "runner_destroy": (None, [_VP]),
+    "runner_forward_batch": (_I, [_VP, _U32, _PU64, _PU32, _PU32, _PU32, C.POINTER(C.c_uint8)]),
+    "runner_forward_token": (_I, [_VP, _U64, _U32, _U32, _PU32, C.POINTER(C.c_float),
+                                  C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), _PU32, _U32,
+                                  C.POINTER(C.c_uint16)]),
+    "runner_last_step_ms": (_F, [_VP]),
+    "runner_last_launches": (_U32, [_VP]),
+    "sched_create": (_VP, [_VP, _VP, _U32, _U32, _U64, _U32]),
+    "sched_destroy": (None, [_VP]),
+    "sched_submit": (_I, [_VP, _U64, _PU32, _U32, _U32, _I64]),
+    "sched_cancel": (_I, [_VP, _U64]),
+    "sched_run_iteration": (None, [_VP, C.POINTER(Iteration)]),
+    "sched_stop": (None, [_VP]),
+    "sched_idle": (_I, [_VP]),
+    "sched_drain": (_U32, [_VP, C.POINTER(Terminal), _U32, _PU32, _U32]),
+    "sched_take_terminals": (_U32, [_VP, C.POINTER(Terminal), _U32, _PU32, _U32]),
+    "generate": (_I, [_VP, _VP, _U64, _PU32, _U32, _U32, _I64, C.POINTER(Terminal), _PU32, _U32]),
+    "fake_backend_create": (_VP, []),
+    "fake_backend_destroy": (None, [_VP]),
+    "fake_runner_create": (_VP, [_U32, _U32, _U32, _U32, _U64]),
+    "fake_runner_destroy": (None, [_VP]),
+    "fake_runner_log": (_U32, [_VP, _PU32, _U32, _PU64, _U32]),
+}
+
+_RUNTIME = None
+
+
+def runtime() -> dict:
+    """name -> ctypes function for every kkrt_* runtime entry point."""
+    global _RUNTIME
+    if _RUNTIME is None:
+        _RUNTIME = bind(load_library(), "kkrt_", RUNTIME_SIGNATURES)
+    return _RUNTIME
+
+
+def _u32(seq):
+    return (C.c_uint32 * max(len(seq), 1))(*seq)
+
+
+def terminals_from(n, terms, tokens) -> list[dict]:
+    out, at = [], 0
+    for i in range(n):
+        t = terms[i]
+        out.append(dict(request_id=t.request_id, reason=t.reason, error=t.error,
+                        tokens=list(tokens[at:at + t.token_count]), prompt_tokens=t.prompt_tokens,
+                        completion_tokens=t.completion_tokens, ttft_ns=t.ttft_ns,
+                        tpot_ns=t.tpot_ns, e2e_ns=t.e2e_ns))
+        at += t.token_count
+    return out
+
+
+class Scheduler:
+    """IterationSchedulerRuntime through the C ABI (kkrt_ = this library; the
+    reference shim exposes the same calls with the kref_ prefix)."""
+
+    def __init__(self, fns: dict, backend, runner, max_active, max_batched_tokens, max_kv_tokens,
+                 prefill_chunk):
+        self.f = fns
+        self.h = fns["sched_create"](backend, runner, max_active, max_batched_tokens,
+                                     max_kv_tokens, prefill_chunk)
+
+    def submit(self, rid, prompt, max_new, eos=-1):
+        return self.f["sched_submit"](self.h, rid, _u32(prompt), len(prompt), max_new, eos)
+
+    def cancel(self, rid):
+        return self.f["sched_cancel"](self.h, rid)
+
+    def run_iteration(self):
+        it = Iteration()
+        self.f["sched_run_iteration"](self.h, C.byref(it))
+        return _struct_tuple(it)
+
+    def drain(self, cap=4096, token_cap=1 << 20):
+        terms = (Terminal * cap)()
+        toks = (C.c_uint32 * token_cap)()
+        n = self.f["sched_drain"](self.h, terms, cap, toks, token_cap)
+        return terminals_from(n, terms, toks)
+
+    def stop(self):
+        self.f["sched_stop"](self.h)
+
+    def close(self):
+        if self.h:
+            self.f["sched_destroy"](self.h)
+            self.h = None

@@ -19,6 +19,7 @@
 //    items are combined by the last CTA to finish (completion counter), which
 //    writes the FP16 output.
 #include "../../../include/kk_kernels.h"
+#include "kernels_internal.h"
 #include "launch.cuh"
 
 #include <cmath>
@@ -51,6 +52,7 @@ struct AttnArgs {
     kk_attn_lane const* lanes;
     kk_attn_item const* items;
     std::uint32_t num_items;
+    std::uint32_t const* num_items_dev;  // when set, the item count is read from here
     __half const* query;
     std::uint32_t query_stride;
     __half* output;
@@ -181,7 +183,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_attention_kernel(Att
     std::uint32_t const G = a.group;
     float const kNegInf = -INFINITY;
 
-    for (std::uint32_t it = blockIdx.x; it < a.num_items; it += gridDim.x) {
+    std::uint32_t const num_items = a.num_items_dev != nullptr
+        ? (*a.num_items_dev < a.num_items ? *a.num_items_dev : a.num_items) : a.num_items;
+    for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
         kk_attn_item const item = a.items[it];
         kk_attn_lane const ln = a.lanes[item.lane];
 
@@ -430,6 +434,69 @@ int numSms()
 } // namespace
 } // namespace kk
 
+namespace {
+int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
+    const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, std::uint32_t const* num_items_dev,
+    const uint16_t* query, uint32_t query_stride,
+    uint16_t* output, uint32_t output_stride, float scale, void* workspace,
+    uint64_t workspace_bytes, cudaStream_t stream)
+{
+    using namespace kk;
+    if (pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
+        || (pools->kv_heads != 1 && pools->kv_heads != 2 && pools->kv_heads != 4
+            && pools->kv_heads != 8)
+        || q_heads % pools->kv_heads != 0 || q_heads / pools->kv_heads > 16
+        || q_heads / pools->kv_heads == 0 || !(scale > 0.f) || query == nullptr
+        || output == nullptr || descs == nullptr || lanes == nullptr || items == nullptr
+        || query_stride % 8 != 0 || output_stride % 8 != 0) {
+        return KK_EINVAL;
+    }
+    // The workspace (completion counters + partial states) is only touched
+    // when some lane is split over several items.
+    if (num_items > num_lanes
+        && (workspace == nullptr
+            || workspace_bytes < kk_attention_workspace_bytes(num_lanes, num_items, q_heads, kHeadDim))) {
+        return KK_EINVAL;
+    }
+    if (num_items == 0) {
+        return 0;
+    }
+    AttnArgs a{};
+    a.micro = static_cast<__half const*>(pools->micro);
+    a.extent = static_cast<__half const*>(pools->extent);
+    std::uint64_t const row = std::uint64_t(pools->kv_heads) * kHeadDim;
+    a.micro_page = std::uint64_t(pools->layers) * 2u * kMicroTokens * row;
+    a.extent_page = std::uint64_t(pools->layers) * 2u * kExtentTokens * row;
+    a.micro_slots = pools->micro == nullptr ? 0 : pools->micro_capacity;
+    a.extent_slots = pools->extent == nullptr ? 0 : pools->extent_capacity;
+    a.layer = layer;
+    a.kv_heads = pools->kv_heads;
+    a.group = q_heads / pools->kv_heads;
+    a.q_heads = q_heads;
+    a.descs = descs;
+    a.lanes = lanes;
+    a.items = items;
+    a.num_items = num_items;
+    a.num_items_dev = num_items_dev;
+    a.query = reinterpret_cast<__half const*>(query);
+    a.query_stride = query_stride;
+    a.output = reinterpret_cast<__half*>(output);
+    a.output_stride = output_stride;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    char* ws = static_cast<char*>(workspace);
+    a.counters = reinterpret_cast<std::uint32_t*>(ws);
+    ws += align256(std::uint64_t(num_lanes) * 4u);
+    a.part_o = reinterpret_cast<float*>(ws);
+    ws += align256(std::uint64_t(num_items) * q_heads * kHeadDim * 4u);
+    a.part_ml = reinterpret_cast<float*>(ws);
+    unsigned const grid = num_items < unsigned(numSms()) ? num_items : unsigned(numSms());
+    return static_cast<int>(launch(paged_decode_attention_kernel, dim3(grid), dim3(kThreads), 0,
+        stream, 1, a));
+}
+
+} // namespace
+
 extern "C" {
 
 uint32_t kk_attention_plan(const kk_page_desc* descs, kk_attn_lane* lanes, uint32_t num_lanes,
@@ -484,55 +551,28 @@ int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer, uint32_t
     uint16_t* output, uint32_t output_stride, float scale, void* workspace,
     uint64_t workspace_bytes, void* stream)
 {
-    using namespace kk;
-    if (pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
-        || (pools->kv_heads != 1 && pools->kv_heads != 2 && pools->kv_heads != 4
-            && pools->kv_heads != 8)
-        || q_heads % pools->kv_heads != 0 || q_heads / pools->kv_heads > 16
-        || q_heads / pools->kv_heads == 0 || !(scale > 0.f) || query == nullptr
-        || output == nullptr || descs == nullptr || lanes == nullptr || items == nullptr
-        || workspace == nullptr
-        || workspace_bytes < kk_attention_workspace_bytes(num_lanes, num_items, q_heads, kHeadDim)
-        || query_stride % 8 != 0 || output_stride % 8 != 0) {
-        return KK_EINVAL;
-    }
-    if (num_items == 0) {
-        return 0;
-    }
-    AttnArgs a{};
-    a.micro = static_cast<__half const*>(pools->micro);
-    a.extent = static_cast<__half const*>(pools->extent);
-    std::uint64_t const row = std::uint64_t(pools->kv_heads) * kHeadDim;
-    a.micro_page = std::uint64_t(pools->layers) * 2u * kMicroTokens * row;
-    a.extent_page = std::uint64_t(pools->layers) * 2u * kExtentTokens * row;
-    a.micro_slots = pools->micro == nullptr ? 0 : pools->micro_capacity;
-    a.extent_slots = pools->extent == nullptr ? 0 : pools->extent_capacity;
-    a.layer = layer;
-    a.kv_heads = pools->kv_heads;
-    a.group = q_heads / pools->kv_heads;
-    a.q_heads = q_heads;
-    a.descs = descs;
-    a.lanes = lanes;
-    a.items = items;
-    a.num_items = num_items;
-    a.query = reinterpret_cast<__half const*>(query);
-    a.query_stride = query_stride;
-    a.output = reinterpret_cast<__half*>(output);
-    a.output_stride = output_stride;
-    a.scale_log2 = scale * 1.4426950408889634f;
-    char* ws = static_cast<char*>(workspace);
-    a.counters = reinterpret_cast<std::uint32_t*>(ws);
-    ws += align256(std::uint64_t(num_lanes) * 4u);
-    a.part_o = reinterpret_cast<float*>(ws);
-    ws += align256(std::uint64_t(num_items) * q_heads * kHeadDim * 4u);
-    a.part_ml = reinterpret_cast<float*>(ws);
-    unsigned const grid = num_items < unsigned(numSms()) ? num_items : unsigned(numSms());
-    return static_cast<int>(launch(paged_decode_attention_kernel, dim3(grid), dim3(kThreads), 0,
-        static_cast<cudaStream_t>(stream), 1, a));
+    return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
+        nullptr, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
+        static_cast<cudaStream_t>(stream));
 }
 
 } // extern "C"
 
 namespace kk {
 int attentionStatus(cudaStream_t stream) { return readStatus(&g_attn_status, stream); }
+
+int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
+    std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
+    std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
+    cudaStream_t stream)
+{
+    if (num_items == nullptr) {
+        return KK_EINVAL;
+    }
+    return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, max_items,
+        num_items, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
+        stream);
+}
 } // namespace kk

@@ -1,0 +1,884 @@
+// CUDA heterogeneous KV backend (reference semantics:
+// src/cuda/engine/backend.cpp:19-610, src/cuda/engine/transaction.cpp:1-425,
+// src/cuda/kv/storage.cpp:99-234). See cuda_backend.h for the design.
+#include "cuda_backend.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cstring>
+#include <limits>
+#include <mutex>
+#include <optional>
+#include <unordered_map>
+#include <vector>
+
+namespace kimkvcache {
+namespace {
+
+EngineKvStatus mapMetadata(KvCacheError e) noexcept
+{
+    switch (e) {
+    case KvCacheError::None: return {};
+    case KvCacheError::InvalidArgument: return {EngineKvError::InvalidArgument};
+    case KvCacheError::RequestNotFound: return {EngineKvError::RequestNotFound};
+    case KvCacheError::RequestAlreadyExists: return {EngineKvError::RequestAlreadyExists};
+    case KvCacheError::RequestConflict:
+    case KvCacheError::PromotionConflict: return {EngineKvError::RequestConflict};
+    case KvCacheError::ResourceExhausted: return {EngineKvError::ResourceExhausted};
+    case KvCacheError::InvalidState: return {EngineKvError::InvalidState};
+    default: return {EngineKvError::InternalError};
+    }
+}
+
+EngineKvStatus mapCuda(CudaStatus s) noexcept
+{
+    switch (s.error) {
+    case CudaError::None: return {};
+    case CudaError::InvalidArgument: return {EngineKvError::InvalidArgument};
+    case CudaError::AllocationFailed: return {EngineKvError::ResourceExhausted};
+    case CudaError::SubmissionFailed: return {EngineKvError::SubmissionFailed};
+    case CudaError::ExecutionFailed: return {EngineKvError::ExecutionFailed};
+    default: return {EngineKvError::InternalError};
+    }
+}
+
+CudaStatus submitError(int code) noexcept
+{
+    return code == KK_EINVAL ? CudaStatus{CudaError::InvalidArgument, code}
+                             : CudaStatus{CudaError::SubmissionFailed, code};
+}
+
+// Device page pools: [capacity][layers][K/V][tokens][kv_heads][dim] FP16, zeroed.
+struct Storage {
+    kk_kv_pools pools{};
+    CudaStatus status{};
+    std::size_t micro_bytes{0};
+    std::size_t extent_bytes{0};
+
+    Storage(KvLayout layout, std::uint32_t micro_cap, std::uint32_t extent_cap)
+    {
+        std::size_t micro_page = 0, extent_page = 0;
+        if (!layout.pageElements(PageKind::Micro, micro_page)
+            || !layout.pageElements(PageKind::Extent, extent_page)) {
+            status = {CudaError::InvalidArgument, 0};
+            return;
+        }
+        micro_bytes = micro_page * 2 * micro_cap;
+        extent_bytes = extent_page * 2 * extent_cap;
+        void* micro = nullptr;
+        void* extent = nullptr;
+        cudaError_t e = cudaMalloc(&micro, micro_bytes);
+        if (e == cudaSuccess) {
+            e = cudaMalloc(&extent, extent_bytes);
+        }
+        if (e == cudaSuccess) {
+            e = cudaMemset(micro, 0, micro_bytes);
+        }
+        if (e == cudaSuccess) {
+            e = cudaMemset(extent, 0, extent_bytes);
+        }
+        pools = kk_kv_pools{micro, extent, micro_cap, extent_cap, layout.layer_count,
+            layout.kv_head_count, layout.head_dimension, 0};
+        if (e != cudaSuccess) {
+            status = {CudaError::AllocationFailed, static_cast<int>(e)};
+        }
+    }
+
+    ~Storage()
+    {
+        cudaDeviceSynchronize();
+        cudaFree(pools.micro);
+        cudaFree(pools.extent);
+    }
+};
+
+// Preallocated per-transaction device metadata for the per-layer SPI path.
+struct Arena {
+    static constexpr std::uint32_t kSlots = 64;
+    static constexpr std::size_t kHeader = 96;  // kv_slot | copy | lane | item
+    std::uint32_t max_desc{0};
+    std::size_t slot_bytes{0};
+    std::uint8_t* dev{nullptr};
+    std::uint8_t* host{nullptr};
+    std::vector<std::uint32_t> free_slots;
+
+    bool init(std::uint32_t descriptors)
+    {
+        max_desc = descriptors;
+        slot_bytes = (kHeader + std::size_t(descriptors) * sizeof(kk_page_desc) + 255) & ~std::size_t(255);
+        if (cudaMalloc(reinterpret_cast<void**>(&dev), slot_bytes * kSlots) != cudaSuccess
+            || cudaMallocHost(reinterpret_cast<void**>(&host), slot_bytes * kSlots) != cudaSuccess) {
+            return false;
+        }
+        for (std::uint32_t i = kSlots; i > 0; --i) {
+            free_slots.push_back(i - 1);
+        }
+        return true;
+    }
+
+    ~Arena()
+    {
+        cudaFree(dev);
+        cudaFreeHost(host);
+    }
+
+    // Offsets inside a slot.
+    static constexpr std::size_t kSlotOff = 0, kCopyOff = 16, kLaneOff = 32, kItemOff = 64,
+                                 kDescOff = kHeader;
+};
+
+struct State {
+    EngineKvConfig config;
+    KvCacheManager mgr;
+    Storage storage;
+    Arena arena;
+    std::unordered_map<RequestId, std::uint32_t> committed_lengths;
+    std::uint64_t active{0};
+    std::atomic<std::uint64_t> batched_submissions{0};
+    std::atomic<std::uint64_t> batched_lanes{0};
+    mutable std::mutex mutex;
+
+    std::mutex fault_mutex;
+    bool fail_submission{false};
+    bool fail_completion{false};
+
+    std::atomic<std::uint64_t> submit_seq{0};
+    std::mutex sync_mutex;
+    std::unordered_map<void*, std::uint64_t> completed_seq;
+
+    State(EngineKvConfig c, std::uint32_t micro_cap, std::uint32_t extent_cap)
+        : config(c), mgr(micro_cap, extent_cap), storage(c.kv_layout, micro_cap, extent_cap)
+    {
+        if (storage.status.ok() && !arena.init(micro_cap + extent_cap)) {
+            storage.status = {CudaError::AllocationFailed, 0};
+        }
+    }
+
+    bool consumeFailure(CudaFailurePoint point)
+    {
+        std::lock_guard<std::mutex> lock(fault_mutex);
+        bool& flag = point == CudaFailurePoint::Submission ? fail_submission : fail_completion;
+        bool const was = flag;
+        flag = false;
+        return was;
+    }
+
+    bool completed(void* stream, std::uint64_t seq)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        auto const f = completed_seq.find(stream);
+        return f != completed_seq.end() && f->second >= seq;
+    }
+};
+
+class CudaTxn final : public TokenTransactionBackend {
+public:
+    CudaTxn(std::shared_ptr<State> st, KvTokenReservationId reservation, RequestId request,
+        PageLeaseId lease, BlockTable before, BlockTable reserved, void* stream)
+        : st_(std::move(st)), reservation_(reservation), request_(request), lease_(lease)
+        , before_(std::move(before)), reserved_(std::move(reserved)), stream_(stream)
+    {
+    }
+
+    ~CudaTxn() override { freeArenaSlot(); }
+
+    BlockTable const& before() const noexcept { return before_; }
+    BlockTable const& reserved() const noexcept { return reserved_; }
+    State* state() const noexcept { return st_.get(); }
+
+    EngineKvStatus writeLayer(LayerKvWrite const& write, EngineStream) override
+    {
+        if (!submission_.ok()) {
+            return mapCuda(submission_);
+        }
+        if (write.layer >= st_->config.kv_layout.layer_count || write.device_key == nullptr
+            || write.device_value == nullptr) {
+            return {EngineKvError::InvalidArgument};
+        }
+        if (st_->consumeFailure(CudaFailurePoint::Submission)) {
+            return fail({CudaError::SubmissionFailed, 0});
+        }
+        if (!upload()) {
+            return mapCuda(submission_);
+        }
+        std::uint8_t* const dev = slotDev();
+        cudaStream_t const s = static_cast<cudaStream_t>(stream_);
+        int rc = 0;
+        if (needs_copy_) {
+            rc = kk_kv_copy_tokens(&st_->storage.pools, write.layer, 1,
+                reinterpret_cast<kk_kv_copy const*>(dev + Arena::kCopyOff), 1, s);
+        }
+        if (rc == 0) {
+            rc = kk_kv_write(&st_->storage.pools, write.layer, 1,
+                reinterpret_cast<kk_kv_slot const*>(dev + Arena::kSlotOff), 1, write.device_key,
+                write.device_value, 0, 0, s);
+        }
+        if (rc != 0) {
+            return fail(submitError(rc));
+        }
+        markSubmitted();
+        return {};
+    }
+
+    EngineKvStatus attendLayer(PagedDecodeRequest const& r, EngineStream) override
+    {
+        CudaStatus const checked = prepareAttention(r);
+        if (!checked.ok()) {
+            return mapCuda(checked);
+        }
+        std::uint8_t* const dev = slotDev();
+        std::uint32_t const hq = st_->config.query_head_count;
+        std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
+        int const rc = kk_paged_decode_attention(&st_->storage.pools, r.layer, hq,
+            reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
+            reinterpret_cast<kk_attn_lane const*>(dev + Arena::kLaneOff), 1,
+            reinterpret_cast<kk_attn_item const*>(dev + Arena::kItemOff), 1, r.device_query, row,
+            r.device_output, row, r.attention_scale, r.device_workspace, r.workspace_bytes,
+            static_cast<cudaStream_t>(stream_));
+        if (rc != 0) {
+            return fail(submitError(rc));
+        }
+        markSubmitted();
+        return {};
+    }
+
+    void attendLayerBatch(PagedDecodeBatch& batch) override;
+
+    EngineKvStatus submitFusedLayers(EngineStream) override
+    {
+        if (!submission_.ok()) {
+            return mapCuda(submission_);
+        }
+        if (st_->consumeFailure(CudaFailurePoint::Submission)) {
+            return fail({CudaError::SubmissionFailed, 0});
+        }
+        markSubmitted();
+        return {};
+    }
+
+    EngineKvStatus commit(EngineStream) override
+    {
+        CudaStatus const done = complete();
+        if (!done.ok()) {
+            return mapCuda(done);
+        }
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        EngineKvStatus const lease = releaseLeaseLocked();
+        if (!lease.ok()) {
+            return lease;
+        }
+        KvCacheError const committed = st_->mgr.commitTokenReservation(reservation_);
+        if (committed != KvCacheError::None) {
+            return mapMetadata(committed);
+        }
+        auto length = st_->committed_lengths.find(request_);
+        if (length == st_->committed_lengths.end()) {
+            return {EngineKvError::InternalError};
+        }
+        ++length->second;
+        --st_->active;
+        resolved_ = true;
+        return {};
+    }
+
+    void rollback(EngineStream) noexcept override
+    {
+        if (resolved_) {
+            return;
+        }
+        static_cast<void>(complete());
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        static_cast<void>(releaseLeaseLocked());
+        static_cast<void>(st_->mgr.rollbackTokenReservation(reservation_));
+        if (st_->active != 0) {
+            --st_->active;
+        }
+        resolved_ = true;
+    }
+
+    // Attention preconditions of the reference (transaction.cpp:43-82).
+    CudaStatus prepareAttention(PagedDecodeRequest const& r)
+    {
+        if (!submission_.ok()) {
+            return submission_;
+        }
+        std::uint32_t const tokens = reserved_.tokenCount();
+        std::size_t const scores = std::size_t(st_->config.query_head_count) * tokens;
+        if (r.layer >= st_->config.kv_layout.layer_count || r.device_query == nullptr
+            || r.device_output == nullptr || r.device_workspace == nullptr
+            || !(r.attention_scale > 0.0F) || tokens == 0
+            || r.workspace_bytes < scores * sizeof(float)) {
+            return {CudaError::InvalidArgument, 0};
+        }
+        if (st_->consumeFailure(CudaFailurePoint::Submission)) {
+            submission_ = final_ = {CudaError::SubmissionFailed, 0};
+            return submission_;
+        }
+        if (!upload()) {
+            return submission_;
+        }
+        return {};
+    }
+
+    std::uint8_t* slotDev() const noexcept
+    {
+        return st_->arena.dev + std::size_t(slot_) * st_->arena.slot_bytes;
+    }
+    std::uint32_t descOffset() const noexcept
+    {
+        return static_cast<std::uint32_t>(
+            (std::size_t(slot_) * st_->arena.slot_bytes) / sizeof(kk_page_desc));
+    }
+    EngineKvStatus fail(CudaStatus s) noexcept
+    {
+        submission_ = final_ = s;
+        return mapCuda(s);
+    }
+    void markSubmitted() noexcept { last_submit_ = ++st_->submit_seq; }
+
+private:
+    // Copies this transaction's write target, COW record, lane and descriptors
+    // into its arena slot (first per-layer SPI use only).
+    bool upload()
+    {
+        if (uploaded_) {
+            return true;
+        }
+        {
+            std::lock_guard<std::mutex> lock(st_->mutex);
+            if (st_->arena.free_slots.empty()) {
+                submission_ = final_ = {CudaError::SubmissionFailed, 0};
+                return false;
+            }
+            slot_ = static_cast<int>(st_->arena.free_slots.back());
+            st_->arena.free_slots.pop_back();
+        }
+        auto const& entries = reserved_.entries();
+        if (entries.size() > st_->arena.max_desc) {
+            submission_ = final_ = {CudaError::InvalidArgument, 0};
+            return false;
+        }
+        std::uint8_t* const host = st_->arena.host + std::size_t(slot_) * st_->arena.slot_bytes;
+        MappingEntry const& target = entries.back();
+        kk_kv_slot ks{target.handle.slot,
+            static_cast<std::uint16_t>(reserved_.tokenCount() - 1 - target.logical_token_begin),
+            static_cast<std::uint8_t>(target.kind), 1};
+        std::memcpy(host + Arena::kSlotOff, &ks, sizeof(ks));
+        kk_kv_copy copy{};
+        needs_copy_ = false;
+        if (!before_.entries().empty()) {
+            MappingEntry const& old_tail = before_.entries().back();
+            if (old_tail.logical_token_begin == target.logical_token_begin
+                && old_tail.handle != target.handle) {
+                copy = kk_kv_copy{old_tail.handle.slot, target.handle.slot, old_tail.valid_tokens,
+                    static_cast<std::uint8_t>(old_tail.kind), static_cast<std::uint8_t>(target.kind)};
+                needs_copy_ = true;
+            }
+        }
+        std::memcpy(host + Arena::kCopyOff, &copy, sizeof(copy));
+        kk_attn_lane lane{descOffset() + static_cast<std::uint32_t>(Arena::kDescOff / sizeof(kk_page_desc)),
+            static_cast<std::uint32_t>(entries.size()), reserved_.tokenCount(), 0, 1, 0, {0, 0}};
+        std::memcpy(host + Arena::kLaneOff, &lane, sizeof(lane));
+        kk_attn_item item{0, lane.desc_offset, lane.desc_offset + lane.desc_count, 0};
+        std::memcpy(host + Arena::kItemOff, &item, sizeof(item));
+        auto* descs = reinterpret_cast<kk_page_desc*>(host + Arena::kDescOff);
+        for (std::size_t i = 0; i < entries.size(); ++i) {
+            descs[i] = kk_page_desc{entries[i].handle.slot, entries[i].logical_token_begin,
+                entries[i].valid_tokens, static_cast<std::uint8_t>(entries[i].kind), 0, 0};
+        }
+        std::size_t const bytes = Arena::kDescOff + entries.size() * sizeof(kk_page_desc);
+        cudaError_t const e = cudaMemcpyAsync(slotDev(), host, bytes, cudaMemcpyHostToDevice,
+            static_cast<cudaStream_t>(stream_));
+        if (e != cudaSuccess) {
+            submission_ = final_ = {CudaError::SubmissionFailed, static_cast<int>(e)};
+            return false;
+        }
+        uploaded_ = true;
+        return true;
+    }
+
+    CudaStatus complete() noexcept
+    {
+        if (finished_) {
+            return final_;
+        }
+        finished_ = true;
+        if (!submission_.ok()) {
+            cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
+            final_ = submission_;
+            return final_;
+        }
+        if (!st_->completed(stream_, last_submit_)) {
+            cudaError_t const e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
+            if (e != cudaSuccess) {
+                final_ = {CudaError::ExecutionFailed, static_cast<int>(e)};
+                return final_;
+            }
+        }
+        if (st_->consumeFailure(CudaFailurePoint::Completion)) {
+            final_ = {CudaError::ExecutionFailed, static_cast<int>(cudaErrorUnknown)};
+            return final_;
+        }
+        final_ = {};
+        return final_;
+    }
+
+    EngineKvStatus releaseLeaseLocked() noexcept
+    {
+        if (lease_ == kInvalidPageLeaseId) {
+            return {};
+        }
+        KvCacheError const released = st_->mgr.releasePageLease(lease_);
+        if (released == KvCacheError::None) {
+            lease_ = kInvalidPageLeaseId;
+        }
+        return mapMetadata(released);
+    }
+
+    void freeArenaSlot() noexcept
+    {
+        if (slot_ >= 0) {
+            std::lock_guard<std::mutex> lock(st_->mutex);
+            st_->arena.free_slots.push_back(static_cast<std::uint32_t>(slot_));
+            slot_ = -1;
+        }
+    }
+
+    std::shared_ptr<State> st_;
+    KvTokenReservationId reservation_;
+    RequestId request_;
+    PageLeaseId lease_;
+    BlockTable before_;
+    BlockTable reserved_;
+    void* stream_;
+    int slot_{-1};
+    bool uploaded_{false};
+    bool needs_copy_{false};
+    CudaStatus submission_{};
+    CudaStatus final_{};
+    bool finished_{false};
+    bool resolved_{false};
+    std::uint64_t last_submit_{0};
+
+    friend void batchAttend(CudaTxn& self, PagedDecodeBatch& batch);
+};
+
+// One ragged launch for all lanes when their queries/outputs are rows of one
+// buffer each (as the reference runner lays them out); otherwise per lane.
+void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
+{
+    std::vector<std::size_t> idx;
+    std::vector<CudaTxn*> txns;
+    for (std::size_t i = 0; i < batch.item_count; ++i) {
+        PagedDecodeBatchItem const& item = batch.items[i];
+        if (!item.status.ok()) {
+            continue;
+        }
+        auto* t = dynamic_cast<CudaTxn*>(batchBackend(item));
+        if (t == nullptr || t->st_ != st_ || (!txns.empty() && batchStream(item) != txns[0]->stream_)
+            || item.request.layer != batch.items[idx.empty() ? i : idx[0]].request.layer) {
+            TokenTransactionBackend::attendLayerBatch(batch);
+            return;
+        }
+        idx.push_back(i);
+        txns.push_back(t);
+    }
+    if (txns.size() < 2) {
+        TokenTransactionBackend::attendLayerBatch(batch);
+        return;
+    }
+    std::uint32_t const hq = st_->config.query_head_count;
+    std::size_t const row_bytes = std::size_t(hq) * st_->config.kv_layout.head_dimension * 2;
+    auto const* q0 = reinterpret_cast<std::uint8_t const*>(batch.items[idx[0]].request.device_query);
+    auto const* o0 = reinterpret_cast<std::uint8_t const*>(batch.items[idx[0]].request.device_output);
+    std::uint8_t const* qmin = q0;
+    std::uint8_t const* omin = o0;
+    for (std::size_t i : idx) {
+        qmin = std::min(qmin, reinterpret_cast<std::uint8_t const*>(batch.items[i].request.device_query));
+        omin = std::min(omin, reinterpret_cast<std::uint8_t const*>(batch.items[i].request.device_output));
+    }
+    std::size_t const lanes_bytes = txns.size() * (sizeof(kk_attn_lane) + sizeof(kk_attn_item));
+    bool strided = batch.item_capacity * sizeof(DevicePagedDecodeBatchItem) >= lanes_bytes;
+    for (std::size_t i : idx) {
+        PagedDecodeRequest const& r = batch.items[i].request;
+        std::ptrdiff_t const dq = reinterpret_cast<std::uint8_t const*>(r.device_query) - qmin;
+        std::ptrdiff_t const dout = reinterpret_cast<std::uint8_t const*>(r.device_output) - omin;
+        strided = strided && dq % row_bytes == 0 && dout == dq && r.attention_scale
+            == batch.items[idx[0]].request.attention_scale;
+    }
+    if (!strided) {
+        TokenTransactionBackend::attendLayerBatch(batch);
+        return;
+    }
+    // Validate and upload every lane first (per-lane status like the reference).
+    std::vector<std::size_t> ready;
+    for (std::size_t k = 0; k < idx.size(); ++k) {
+        CudaStatus const s = txns[k]->prepareAttention(batch.items[idx[k]].request);
+        batch.items[idx[k]].status = mapCuda(s);
+        if (s.ok()) {
+            ready.push_back(k);
+        }
+    }
+    if (ready.empty()) {
+        return;
+    }
+    auto* host = reinterpret_cast<std::uint8_t*>(batch.host_items);
+    auto* lanes = reinterpret_cast<kk_attn_lane*>(host);
+    auto* items = reinterpret_cast<kk_attn_item*>(host + ready.size() * sizeof(kk_attn_lane));
+    for (std::size_t j = 0; j < ready.size(); ++j) {
+        CudaTxn* t = txns[ready[j]];
+        PagedDecodeRequest const& r = batch.items[idx[ready[j]]].request;
+        std::uint32_t const off = t->descOffset() + static_cast<std::uint32_t>(Arena::kDescOff / sizeof(kk_page_desc));
+        std::uint32_t const count = static_cast<std::uint32_t>(t->reserved_.entries().size());
+        std::uint32_t const row = static_cast<std::uint32_t>(
+            (reinterpret_cast<std::uint8_t const*>(r.device_query) - qmin) / row_bytes);
+        lanes[j] = kk_attn_lane{off, count, t->reserved_.tokenCount(), static_cast<std::uint32_t>(j), 1, row, {0, 0}};
+        items[j] = kk_attn_item{static_cast<std::uint32_t>(j), off, off + count, 0};
+    }
+    cudaStream_t const s = static_cast<cudaStream_t>(stream_);
+    std::size_t const bytes = ready.size() * (sizeof(kk_attn_lane) + sizeof(kk_attn_item));
+    int rc = static_cast<int>(cudaMemcpyAsync(batch.device_items, batch.host_items, bytes,
+        cudaMemcpyHostToDevice, s));
+    if (rc == 0) {
+        auto* dev = reinterpret_cast<std::uint8_t*>(batch.device_items);
+        PagedDecodeRequest const& r0 = batch.items[idx[ready[0]]].request;
+        std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
+        rc = kk_paged_decode_attention(&st_->storage.pools, r0.layer, hq,
+            reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
+            reinterpret_cast<kk_attn_lane const*>(dev), static_cast<std::uint32_t>(ready.size()),
+            reinterpret_cast<kk_attn_item const*>(dev + ready.size() * sizeof(kk_attn_lane)),
+            static_cast<std::uint32_t>(ready.size()), reinterpret_cast<std::uint16_t const*>(qmin),
+            row, reinterpret_cast<std::uint16_t*>(const_cast<std::uint8_t*>(omin)), row,
+            r0.attention_scale, r0.device_workspace, r0.workspace_bytes, s);
+    }
+    std::uint64_t ok_lanes = 0;
+    for (std::size_t k : ready) {
+        if (rc != 0) {
+            batch.items[idx[k]].status = txns[k]->fail(submitError(rc));
+        } else {
+            txns[k]->markSubmitted();
+            ++ok_lanes;
+        }
+    }
+    if (ok_lanes != 0) {
+        st_->batched_submissions.fetch_add(1, std::memory_order_relaxed);
+        st_->batched_lanes.fetch_add(ok_lanes, std::memory_order_relaxed);
+    }
+}
+
+class CudaBackend final : public EngineKvBackend {
+public:
+    explicit CudaBackend(std::shared_ptr<State> st) : st_(std::move(st)) {}
+
+    EngineKvBackendKind kind() const noexcept override { return EngineKvBackendKind::Heterogeneous; }
+    EngineKvConfig config() const noexcept override { return st_->config; }
+
+    EngineKvStatus createRequest(RequestId id) override
+    {
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        if (!st_->config.valid() || !st_->storage.status.ok()) {
+            return {EngineKvError::InvalidState};
+        }
+        KvCacheError const e = st_->mgr.createRequest(id);
+        if (e == KvCacheError::None) {
+            st_->committed_lengths.emplace(id, 0);
+        }
+        return mapMetadata(e);
+    }
+
+    EngineKvStatus forkRequest(RequestId source, RequestId child) override
+    {
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        auto const src = st_->committed_lengths.find(source);
+        if (src == st_->committed_lengths.end()) {
+            return {EngineKvError::RequestNotFound};
+        }
+        std::uint32_t const length = src->second;
+        KvCacheError const e = st_->mgr.forkRequest(source, child);
+        if (e == KvCacheError::None) {
+            st_->committed_lengths.emplace(child, length);
+        }
+        return mapMetadata(e);
+    }
+
+    EngineKvStatus releaseRequest(RequestId id) override
+    {
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        KvCacheError const e = st_->mgr.releaseRequest(id);
+        if (e == KvCacheError::None) {
+            st_->committed_lengths.erase(id);
+        }
+        return mapMetadata(e);
+    }
+
+    TokenReserveResult reserveToken(ReserveTokenRequest const& request) override
+    {
+        TokenReserveResult result;
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        auto const length = st_->committed_lengths.find(request.request_id);
+        if (request.request_id == kInvalidRequestId) {
+            result.status = {EngineKvError::InvalidArgument};
+            return result;
+        }
+        if (length == st_->committed_lengths.end()) {
+            result.status = {EngineKvError::RequestNotFound};
+            return result;
+        }
+        TokenReservationResult reservation =
+            st_->mgr.reserveToken(request.request_id, request.expected_committed_tokens);
+        if (!reservation.ok()) {
+            result.status = mapMetadata(reservation.error);
+            return result;
+        }
+        PageLeaseAcquireResult const lease =
+            st_->mgr.acquireTokenReservationLease(reservation.reservation_id);
+        if (!lease.ok()) {
+            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
+            result.status = mapMetadata(lease.error);
+            return result;
+        }
+        CudaStatus const begun = beginChecks(reservation);
+        if (!begun.ok()) {
+            static_cast<void>(st_->mgr.releasePageLease(lease.lease_id));
+            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
+            result.status = mapCuda(begun);
+            return result;
+        }
+        std::unique_ptr<CudaTxn> txn;
+        try {
+            txn = std::make_unique<CudaTxn>(st_, reservation.reservation_id, reservation.request_id,
+                lease.lease_id, std::move(reservation.before), std::move(reservation.reserved),
+                request.stream);
+        } catch (...) {
+            static_cast<void>(st_->mgr.releasePageLease(lease.lease_id));
+            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
+            result.status = {EngineKvError::ResourceExhausted};
+            return result;
+        }
+        result.transaction = TokenTransaction(std::move(txn), reservation.reservation_id,
+            reservation.request_id, reservation.logical_token_position,
+            st_->config.kv_layout.layer_count, request.stream);
+        if (!result.transaction.valid()) {
+            result.status = {EngineKvError::InternalError};
+            return result;
+        }
+        ++st_->active;
+        result.status = {};
+        return result;
+    }
+
+    EngineKvBackendSnapshot snapshot() const override
+    {
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        EngineKvBackendSnapshot r;
+        std::uint64_t committed = 0;
+        for (auto const& e : st_->committed_lengths) {
+            committed += e.second;
+        }
+        r.request_count = st_->committed_lengths.size();
+        r.active_transaction_count = st_->active;
+        r.committed_token_count = committed;
+        r.batched_attention_submissions = st_->batched_submissions.load(std::memory_order_relaxed);
+        r.batched_attention_lanes = st_->batched_lanes.load(std::memory_order_relaxed);
+        r.storage_reserved_bytes = st_->storage.micro_bytes + st_->storage.extent_bytes;
+        KvCacheManagerSnapshot const m = st_->mgr.snapshot();
+        r.primary_page_tokens = kMicroPageTokenCapacity;
+        r.secondary_page_tokens = kExtentPageTokenCapacity;
+        r.primary_page_capacity = m.micro_pool.total_slots;
+        r.secondary_page_capacity = m.extent_pool.total_slots;
+        r.allocated_primary_pages = m.micro_pool.allocated_slots;
+        r.allocated_secondary_pages = m.extent_pool.allocated_slots;
+        r.successful_primary_allocations = m.micro_pool.successful_allocations;
+        r.successful_secondary_allocations = m.extent_pool.successful_allocations;
+        r.failed_primary_allocations = m.micro_pool.failed_allocations;
+        r.failed_secondary_allocations = m.extent_pool.failed_allocations;
+        return r;
+    }
+
+    bool checkInvariants() const override
+    {
+        std::lock_guard<std::mutex> lock(st_->mutex);
+        return st_->config.valid() && st_->storage.status.ok() && st_->mgr.checkInvariants()
+            && st_->active == st_->mgr.snapshot().token_reservation_count;
+    }
+
+    State* state() const noexcept { return st_.get(); }
+
+private:
+    // Storage-side checks of a new transaction (reference
+    // CudaKvStorage::beginEngineTransaction, transaction.cpp:336-370).
+    CudaStatus beginChecks(TokenReservationResult const& r)
+    {
+        if (!st_->storage.status.ok()) {
+            return st_->storage.status;
+        }
+        auto valid = [this](BlockTable const& t) {
+            if (!t.checkInvariants()) {
+                return false;
+            }
+            for (MappingEntry const& e : t.entries()) {
+                std::uint32_t const cap = e.kind == PageKind::Micro ? st_->storage.pools.micro_capacity
+                                                                    : st_->storage.pools.extent_capacity;
+                if (e.handle.slot >= cap) {
+                    return false;
+                }
+            }
+            return true;
+        };
+        std::uint32_t const kv = st_->config.kv_layout.kv_head_count;
+        if (!valid(r.before) || !valid(r.reserved) || r.reserved.tokenCount() != r.before.tokenCount() + 1
+            || st_->config.query_head_count < kv || st_->config.query_head_count % kv != 0
+            || r.reserved.entries().empty()) {
+            return {CudaError::InvalidArgument, 0};
+        }
+        if (st_->consumeFailure(CudaFailurePoint::Submission)) {
+            return {CudaError::SubmissionFailed, 0};
+        }
+        return {};
+    }
+
+    std::shared_ptr<State> st_;
+};
+
+} // namespace
+
+std::unique_ptr<EngineKvBackend> createHeterogeneousCudaEngineKvBackend(
+    EngineKvConfig config, std::uint32_t micro_cap, std::uint32_t extent_cap)
+{
+    if (!config.valid() || micro_cap == 0 || extent_cap == 0) {
+        return nullptr;
+    }
+    try {
+        return std::make_unique<CudaBackend>(std::make_shared<State>(config, micro_cap, extent_cap));
+    } catch (...) {
+        return nullptr;
+    }
+}
+
+bool injectCudaEngineFailureOnce(EngineKvBackend& backend, CudaFailurePoint point) noexcept
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr) {
+        return false;
+    }
+    std::lock_guard<std::mutex> lock(b->state()->fault_mutex);
+    (point == CudaFailurePoint::Submission ? b->state()->fail_submission
+                                           : b->state()->fail_completion) = true;
+    return true;
+}
+
+kk_kv_pools const* cudaBackendPools(EngineKvBackend const& backend) noexcept
+{
+    auto const* b = dynamic_cast<CudaBackend const*>(&backend);
+    return b == nullptr ? nullptr : &b->state()->storage.pools;
+}
+
+bool fusedLane(TokenTransaction const& transaction, FusedLane& out) noexcept
+{
+    auto const* t = dynamic_cast<CudaTxn const*>(transaction.backend());
+    if (t == nullptr) {
+        return false;
+    }
+    out.before = &t->before();
+    out.reserved = &t->reserved();
+    return true;
+}
+
+bool cudaBackendTable(EngineKvBackend const& backend, RequestId id, BlockTable& out)
+{
+    auto const* b = dynamic_cast<CudaBackend const*>(&backend);
+    if (b == nullptr) {
+        return false;
+    }
+    std::optional<BlockTable> t = b->state()->mgr.blockTable(id);
+    if (!t) {
+        return false;
+    }
+    out = std::move(*t);
+    return true;
+}
+
+EngineKvStatus cudaBackendAppend(EngineKvBackend& backend, RequestId id, std::uint32_t n)
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr) {
+        return {EngineKvError::InvalidArgument};
+    }
+    State* st = b->state();
+    std::lock_guard<std::mutex> lock(st->mutex);
+    auto length = st->committed_lengths.find(id);
+    if (length == st->committed_lengths.end()) {
+        return {EngineKvError::RequestNotFound};
+    }
+    KvCacheError const e = st->mgr.append(id, n);
+    if (e == KvCacheError::None) {
+        length->second += n;
+    }
+    return mapMetadata(e);
+}
+
+EngineKvStatus cudaBackendSeal(EngineKvBackend& backend, RequestId id)
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr) {
+        return {EngineKvError::InvalidArgument};
+    }
+    std::lock_guard<std::mutex> lock(b->state()->mutex);
+    return mapMetadata(b->state()->mgr.sealTail(id));
+}
+
+EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::uint32_t begin,
+    CudaStream stream)
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr) {
+        return {EngineKvError::InvalidArgument};
+    }
+    State* st = b->state();
+    PromotionPrepareResult prepared;
+    PageLeaseAcquireResult lease;
+    {
+        std::lock_guard<std::mutex> lock(st->mutex);
+        prepared = st->mgr.preparePromotion(id, begin);
+        if (!prepared.ok()) {
+            return mapMetadata(prepared.error);
+        }
+        lease = st->mgr.acquirePromotionIoLease(prepared.promotion_id);
+        if (!lease.ok()) {
+            static_cast<void>(st->mgr.rollbackPromotion(prepared.promotion_id));
+            return mapMetadata(lease.error);
+        }
+    }
+    std::uint32_t slots[8];
+    for (int k = 0; k < 8; ++k) {
+        slots[k] = prepared.source_handles[k].slot;
+    }
+    cudaStream_t const s = static_cast<cudaStream_t>(stream);
+    int rc = kk_kv_promote(&st->storage.pools, slots, prepared.target_handle.slot, s);
+    if (rc == 0) {
+        rc = static_cast<int>(cudaStreamSynchronize(s));
+    }
+    std::lock_guard<std::mutex> lock(st->mutex);
+    static_cast<void>(st->mgr.releasePageLease(lease.lease_id));
+    if (rc != 0) {
+        static_cast<void>(st->mgr.rollbackPromotion(prepared.promotion_id));
+        return {EngineKvError::ExecutionFailed};
+    }
+    return mapMetadata(st->mgr.commitPromotion(prepared.promotion_id));
+}
+
+void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr) {
+        return;
+    }
+    State* st = b->state();
+    std::uint64_t const seq = st->submit_seq.load();
+    std::lock_guard<std::mutex> lock(st->sync_mutex);
+    st->completed_seq[stream] = seq;
+}
+
+} // namespace kimkvcache

@@ -1,0 +1,86 @@
+// CUDA heterogeneous KV backend behind the EngineKvBackend SPI.
+//
+// Public factory and fault hook follow the reference
+// (include/kim-kv/cuda/cuda_engine_kv_backend.h:11-29, cuda_status.h:9-82):
+// createHeterogeneousCudaEngineKvBackend owns a KvCacheManager and two device
+// page pools; reserveToken = metadata reservation + page lease + a
+// transaction object; commit = completion check + lease release + metadata
+// commit; rollback = wait + lease release + metadata rollback.
+//
+// B200 design differences (same observable semantics):
+//  * no per-token cudaMalloc / event: per-transaction device metadata lives in
+//    a preallocated arena and is uploaded only if the per-layer SPI is used;
+//  * the fused decode step of this library's model runner reads the
+//    transaction tables directly (fusedLane) and advances the state machine
+//    with TokenTransaction::submitFusedLayers; the runner synchronises its
+//    stream once per step and tells the backend (noteStreamCompleted), so
+//    commits do not synchronise again.
+#pragma once
+
+#include "../host/engine_kv.h"
+#include "../../../include/kk_kernels.h"
+
+#include <cstdint>
+#include <memory>
+#include <string_view>
+
+namespace kimkvcache {
+
+using CudaStream = void*;
+
+enum class CudaError : std::uint8_t {
+    None,
+    InvalidArgument,
+    RuntimeUnavailable,
+    AllocationFailed,
+    SubmissionFailed,
+    NotReady,
+    ExecutionFailed,
+    InternalError,
+};
+
+struct CudaStatus final {
+    CudaError error{CudaError::None};
+    int native_error{0};
+    [[nodiscard]] constexpr bool ok() const noexcept { return error == CudaError::None; }
+};
+
+enum class CudaFailurePoint : std::uint8_t { Submission, Completion };
+
+[[nodiscard]] std::unique_ptr<EngineKvBackend> createHeterogeneousCudaEngineKvBackend(
+    EngineKvConfig config, std::uint32_t micro_page_capacity, std::uint32_t extent_page_capacity);
+
+[[nodiscard]] bool injectCudaEngineFailureOnce(EngineKvBackend& backend, CudaFailurePoint point) noexcept;
+
+// ---- library-internal hooks used by the CUDA model runner ---------------------
+
+// What the fused step needs to know about one lane's reserved token.
+struct FusedLane final {
+    BlockTable const* before{nullptr};
+    BlockTable const* reserved{nullptr};
+};
+
+// Device pools of a CUDA backend created by this library (nullptr otherwise).
+[[nodiscard]] kk_kv_pools const* cudaBackendPools(EngineKvBackend const& backend) noexcept;
+
+// Lane view of a transaction reserved from a CUDA backend of this library.
+[[nodiscard]] bool fusedLane(TokenTransaction const& transaction, FusedLane& out) noexcept;
+
+// The runner synchronised `stream`: every transaction submitted on it so far
+// has completed (commits then skip their own synchronisation).
+void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept;
+
+// Library extensions for building long prefixes without running the model
+// (used by the synthetic workloads and tests; the reference builds such
+// tables with KvCacheManager::append and the promotion path of CudaKvCache):
+[[nodiscard]] bool cudaBackendTable(EngineKvBackend const& backend, RequestId id, BlockTable& out);
+// Metadata append of n tokens (KV contents are written separately).
+[[nodiscard]] EngineKvStatus cudaBackendAppend(EngineKvBackend& backend, RequestId id, std::uint32_t n);
+[[nodiscard]] EngineKvStatus cudaBackendSeal(EngineKvBackend& backend, RequestId id);
+// prepare -> IO lease -> device copy (8 micro -> 1 extent) -> wait -> release
+// -> commit, rolled back on any failure (reference CudaKvCache::promote,
+// src/cuda/kv/cache.cpp:172-229).
+[[nodiscard]] EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id,
+    std::uint32_t logical_begin, CudaStream stream);
+
+} // namespace kimkvcache

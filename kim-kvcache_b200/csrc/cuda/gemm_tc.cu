@@ -23,6 +23,7 @@
 // then runs the fused epilogue for those columns.
 // No TMA multicast is used anywhere.
 #include "../../../include/kk_kernels.h"
+#include "kernels_internal.h"
 #include "launch.cuh"
 
 #include <cfloat>
@@ -415,24 +416,8 @@ bool makeMap(CUtensorMap* map, void const* base, std::uint64_t cols, std::uint64
 
 int g_sms = 0;
 
-template <int BN>
-int launchGemm(kk_gemm_desc const& d, GemmArgs args, cudaStream_t stream)
+int numSms()
 {
-    static bool configured = false;
-    std::size_t const smem = smemBytes<BN>();
-    if (!configured) {
-        cudaError_t const e = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
-            cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        if (e != cudaSuccess) {
-            return static_cast<int>(e);
-        }
-        configured = true;
-    }
-    CUtensorMap tm_w{}, tm_x{};
-    if (!makeMap(&tm_w, d.weight, d.K, d.M, d.K, kBM)
-        || !makeMap(&tm_x, d.x, d.K, d.x_rows, d.x_stride, BN)) {
-        return KK_EINVAL;
-    }
     if (g_sms == 0) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -441,35 +426,33 @@ int launchGemm(kk_gemm_desc const& d, GemmArgs args, cudaStream_t stream)
             g_sms = 148;
         }
     }
-    std::uint32_t const tiles = (d.M + kBM - 1) / kBM;
-    std::uint32_t split = d.split_k;
-    if (split == 0) {
-        // Aim for roughly two CTAs per SM across the launch.
-        std::uint32_t const target = 2u * static_cast<std::uint32_t>(g_sms);
-        split = target / tiles;
-    }
-    std::uint32_t const max_split = args.kb_total < 8u ? args.kb_total : 8u;
-    split = split < 1u ? 1u : (split > max_split ? max_split : split);
-    args.split = split;
-    args.epi.num_m_tiles = tiles;
-    return static_cast<int>(launch(gemm_tc_kernel<BN>, dim3(split, tiles), dim3(kThreads), smem,
-        stream, split, tm_w, tm_x, args));
+    return g_sms;
+}
+
+template <int BN>
+cudaError_t configure()
+{
+    static cudaError_t status = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<BN>()));
+    return status;
 }
 
 } // namespace
-} // namespace kk
 
-extern "C" {
+struct GemmPlan {
+    CUtensorMap tm_w;
+    CUtensorMap tm_x;
+    GemmArgs args;
+    std::uint32_t tiles;
+    int bn;
+};
 
-uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N)
+void GemmPlanDeleter::operator()(GemmPlan* p) const noexcept { delete p; }
+
+namespace {
+
+int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
 {
-    std::uint64_t const tiles = (M + 127u) / 128u;
-    return 256u + tiles * N * 8u;
-}
-
-int kk_gemm(const kk_gemm_desc* d, void* stream)
-{
-    using namespace kk;
     if (d == nullptr || d->weight == nullptr || d->x == nullptr || d->M == 0 || d->K == 0
         || d->K % 8 != 0 || d->N == 0 || d->N > 64 || d->x_rows < d->N || d->x_stride < d->K
         || d->x_stride % 8 != 0 || d->epilogue > KK_EPI_ARGMAX
@@ -477,7 +460,7 @@ int kk_gemm(const kk_gemm_desc* d, void* stream)
         || (reinterpret_cast<std::uintptr_t>(d->x) & 15u) != 0) {
         return KK_EINVAL;
     }
-    GemmArgs args{};
+    args = GemmArgs{};
     args.M = d->M;
     args.K = d->K;
     args.N = d->N;
@@ -525,18 +508,74 @@ int kk_gemm(const kk_gemm_desc* d, void* stream)
         e.part_idx = reinterpret_cast<std::uint32_t*>(ws + 256 + tiles * d->N * 4u);
         e.tokens = d->tokens;
     }
-    cudaStream_t const s = static_cast<cudaStream_t>(stream);
-    if (d->N <= 16) {
-        return launchGemm<16>(*d, args, s);
+    return 0;
+}
+
+template <int BN>
+int runGemm(GemmPlan const& plan, cudaStream_t stream)
+{
+    cudaError_t const c = configure<BN>();
+    if (c != cudaSuccess) {
+        return static_cast<int>(c);
     }
-    if (d->N <= 32) {
-        return launchGemm<32>(*d, args, s);
-    }
-    return launchGemm<64>(*d, args, s);
+    return static_cast<int>(launch(gemm_tc_kernel<BN>, dim3(plan.args.split, plan.tiles),
+        dim3(kThreads), smemBytes<BN>(), stream, plan.args.split, plan.tm_w, plan.tm_x, plan.args));
+}
+
+} // namespace
+} // namespace kk
+
+extern "C" {
+
+uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N)
+{
+    std::uint64_t const tiles = (M + 127u) / 128u;
+    return 256u + tiles * N * 8u;
+}
+
+int kk_gemm(const kk_gemm_desc* d, void* stream)
+{
+    int rc = 0;
+    kk::GemmPlanPtr const plan = kk::gemmPlan(*d, rc);
+    return plan ? kk::gemmRun(*plan, static_cast<cudaStream_t>(stream)) : rc;
 }
 
 } // extern "C"
 
 namespace kk {
 int gemmStatus(cudaStream_t stream) { return readStatus(&g_gemm_status, stream); }
+
+GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
+{
+    GemmPlanPtr plan(new GemmPlan{});
+    rc = buildArgs(&d, plan->args);
+    if (rc != 0) {
+        return nullptr;
+    }
+    plan->bn = d.N <= 16 ? 16 : (d.N <= 32 ? 32 : 64);
+    if (!makeMap(&plan->tm_w, d.weight, d.K, d.M, d.K, kBM)
+        || !makeMap(&plan->tm_x, d.x, d.K, d.x_rows, d.x_stride, static_cast<std::uint32_t>(plan->bn))) {
+        rc = KK_EINVAL;
+        return nullptr;
+    }
+    plan->tiles = (d.M + kBM - 1) / kBM;
+    std::uint32_t split = d.split_k;
+    if (split == 0) {
+        split = 2u * static_cast<std::uint32_t>(numSms()) / plan->tiles;  // ~2 CTAs per SM
+    }
+    std::uint32_t const max_split = plan->args.kb_total < 8u ? plan->args.kb_total : 8u;
+    split = split < 1u ? 1u : (split > max_split ? max_split : split);
+    plan->args.split = split;
+    plan->args.epi.num_m_tiles = plan->tiles;
+    return plan;
+}
+
+int gemmRun(GemmPlan const& plan, cudaStream_t stream)
+{
+    switch (plan.bn) {
+    case 16: return runGemm<16>(plan, stream);
+    case 32: return runGemm<32>(plan, stream);
+    default: return runGemm<64>(plan, stream);
+    }
+}
 } // namespace kk

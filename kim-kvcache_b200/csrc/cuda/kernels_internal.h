@@ -1,0 +1,41 @@
+// Library-internal launch variants used by the model runner:
+//  * counts read from device memory (so one captured CUDA graph serves every
+//    step of a batch size: work lists change, kernel parameters do not);
+//  * prepared GEMMs whose TMA tensor maps are encoded once at load.
+#pragma once
+
+#include "../../../include/kk_kernels.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+
+namespace kk {
+
+// kk_paged_decode_attention with the item count in device memory; items
+// beyond *num_items (<= max_items) are ignored. The grid is sized for max_items.
+int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
+    std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
+    std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
+    cudaStream_t stream);
+
+// kk_kv_copy_tokens with the copy count in device memory (<= max_copies).
+int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_copy const* copies, std::uint32_t const* num_copies, std::uint32_t max_copies,
+    cudaStream_t stream);
+
+struct GemmPlan;
+struct GemmPlanDeleter {
+    void operator()(GemmPlan* p) const noexcept;
+};
+using GemmPlanPtr = std::unique_ptr<GemmPlan, GemmPlanDeleter>;
+
+// Validates the descriptor, encodes its tensor maps and picks the split; rc
+// receives 0 or the kk_gemm error code.
+GemmPlanPtr gemmPlan(kk_gemm_desc const& desc, int& rc);
+int gemmRun(GemmPlan const& plan, cudaStream_t stream);
+
+} // namespace kk

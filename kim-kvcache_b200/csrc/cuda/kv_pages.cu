@@ -9,6 +9,7 @@
 // copyLayerTokensKernel / copyPageTokensKernel, paged_decode_kernels.cu:29-63,
 // page_kernels.cu:46-75). Both are bandwidth-bound byte movers.
 #include "../../../include/kk_kernels.h"
+#include "kernels_internal.h"
 #include "launch.cuh"
 
 namespace kk {
@@ -87,9 +88,13 @@ __global__ void kv_write_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_slo
 }
 
 // grid: (num_copies, layer_count, 2): copies tokens*row contiguous elements.
-__global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy const* copies)
+__global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy const* copies,
+    std::uint32_t const* count)
 {
     pdl_wait();
+    if (count != nullptr && blockIdx.x >= *count) {
+        return;
+    }
     kk_kv_copy const c = copies[blockIdx.x];
     std::uint32_t const layer = layer_begin + blockIdx.y;
     std::uint32_t const component = blockIdx.z;
@@ -107,6 +112,48 @@ __global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy
     std::uint64_t const n = std::uint64_t(c.tokens) * v.row;
     for (std::uint64_t i = threadIdx.x * 8u; i < n; i += blockDim.x * 8u) {
         *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4 const*>(src + i);
+    }
+}
+
+struct PromoteSlots {
+    std::uint32_t micro[8];
+};
+
+// grid (8 source pages, layers, 2): 8 tokens x row elements per block.
+__global__ void kv_promote_kernel(PoolView v, PromoteSlots src, std::uint32_t extent_slot)
+{
+    pdl_wait();
+    std::uint32_t const k = blockIdx.x;
+    std::uint32_t const layer = blockIdx.y;
+    std::uint32_t const component = blockIdx.z;
+    __half const* from = block_of(v, 0, src.micro[k], layer, component);
+    __half* to = block_of(v, 1, extent_slot, layer, component);
+    if (from == nullptr || to == nullptr) {
+        return;
+    }
+    to += std::uint64_t(8u * k) * v.row;
+    std::uint64_t const n = 8ull * v.row;
+    for (std::uint64_t i = threadIdx.x * 8u; i < n; i += blockDim.x * 8u) {
+        *reinterpret_cast<uint4*>(to + i) = *reinterpret_cast<uint4 const*>(from + i);
+    }
+}
+
+// SplitMix64 finaliser: a well-mixed 64-bit hash of (seed, index).
+__device__ __forceinline__ std::uint64_t mix64(std::uint64_t x)
+{
+    x += 0x9e3779b97f4a7c15ull;
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+}
+
+__global__ void fill_fp16_kernel(__half* data, std::uint64_t count, std::uint64_t seed, float scale)
+{
+    for (std::uint64_t i = blockIdx.x * std::uint64_t(blockDim.x) + threadIdx.x; i < count;
+         i += std::uint64_t(gridDim.x) * blockDim.x) {
+        std::uint64_t const h = mix64(seed * 0x100000001b3ull + i);
+        float const u = static_cast<float>(h >> 40) * (1.0f / 16777216.0f);  // [0, 1)
+        data[i] = __float2half_rn((2.0f * u - 1.0f) * scale);
     }
 }
 
@@ -152,11 +199,58 @@ int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t l
         return 0;
     }
     return static_cast<int>(launch(kv_copy_kernel, dim3(num_copies, layer_count, 2), dim3(128), 0,
-        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, copies));
+        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, copies,
+        static_cast<std::uint32_t const*>(nullptr)));
+}
+
+int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots, uint32_t extent_slot,
+    void* stream)
+{
+    using namespace kk;
+    if (!poolsOk(pools) || micro_slots == nullptr || pools->extent == nullptr
+        || extent_slot >= pools->extent_capacity) {
+        return KK_EINVAL;
+    }
+    PromoteSlots src{};
+    for (int k = 0; k < 8; ++k) {
+        if (micro_slots[k] >= pools->micro_capacity) {
+            return KK_EINVAL;
+        }
+        src.micro[k] = micro_slots[k];
+    }
+    return static_cast<int>(launch(kv_promote_kernel, dim3(8, pools->layers, 2), dim3(128), 0,
+        static_cast<cudaStream_t>(stream), 1, view(*pools), src, extent_slot));
+}
+
+int kk_fill_fp16(uint16_t* data, uint64_t count, uint64_t seed, float scale, void* stream)
+{
+    using namespace kk;
+    if (data == nullptr) {
+        return KK_EINVAL;
+    }
+    if (count == 0) {
+        return 0;
+    }
+    std::uint64_t blocks = (count + 255) / 256;
+    blocks = blocks > 8192 ? 8192 : blocks;
+    return static_cast<int>(launch(fill_fp16_kernel, dim3(static_cast<unsigned>(blocks)), dim3(256),
+        0, static_cast<cudaStream_t>(stream), 1, reinterpret_cast<__half*>(data), count, seed, scale));
 }
 
 } // extern "C"
 
 namespace kk {
 int pagesStatus(cudaStream_t stream) { return readStatus(&g_pages_status, stream); }
+
+int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_copy const* copies, std::uint32_t const* num_copies, std::uint32_t max_copies,
+    cudaStream_t stream)
+{
+    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
+        || copies == nullptr || num_copies == nullptr || max_copies == 0 || max_copies > 65535u) {
+        return KK_EINVAL;
+    }
+    return static_cast<int>(launch(kv_copy_kernel, dim3(max_copies, layer_count, 2), dim3(128), 0,
+        stream, 1, view(*pools), layer_begin, copies, num_copies));
+}
 } // namespace kk

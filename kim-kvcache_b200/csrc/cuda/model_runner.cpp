@@ -1,0 +1,756 @@
+// CUDA TinyLlama runner on the sm_100a kernels. Reference behaviour:
+// src/cuda/model/runner.cpp:53-880 (forwardToken, generationForwardBatch),
+// src/cuda/model/runner_factory.cpp:12-194 (load), runner_support.cpp (workspace).
+#include "model_runner.h"
+
+#include "kernels_internal.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <fstream>
+#include <unordered_map>
+#include <unordered_set>
+
+namespace kimkvcache {
+namespace {
+
+CudaModelRunnerStatus failure(CudaModelRunnerError e, int code, std::string detail)
+{
+    return CudaModelRunnerStatus{e, code, std::move(detail)};
+}
+
+CudaModelRunnerStatus cudaFailure(int code, std::string const& what)
+{
+    return failure(code == KK_EINVAL ? CudaModelRunnerError::InvalidArgument
+                                     : CudaModelRunnerError::SubmissionFailed,
+        code, what + ": " + (code == KK_EINVAL ? "invalid kernel arguments"
+                                                : cudaGetErrorString(static_cast<cudaError_t>(code))));
+}
+
+CudaModelRunnerStatus kvFailure(EngineKvStatus s, std::string const& what)
+{
+    return failure(CudaModelRunnerError::KvBackendFailed, static_cast<int>(s.error),
+        what + " failed: " + std::string(toString(s.error)));
+}
+
+constexpr std::uint32_t kAttentionTargetTokens = 256;
+
+std::size_t align256(std::size_t x) { return (x + 255) & ~std::size_t(255); }
+
+struct LayerWeights {
+    std::uint16_t const* in_norm;
+    std::uint16_t const* post_norm;
+    std::uint16_t const* w_qkv;   // [(Hq + 2 Hkv) D][H]: q rows, k rows, v rows
+    std::uint16_t const* w_o;     // [H][H]
+    std::uint16_t const* w_gu;    // [2 I][H]: row 2i = gate_i, row 2i+1 = up_i
+    std::uint16_t const* w_down;  // [H][I]
+};
+
+// Prepared projections of one batch size.
+struct BatchPlans {
+    std::vector<kk::GemmPlanPtr> qkv, o, gu, down;
+    kk::GemmPlanPtr lm_head;
+    kk::GemmPlanPtr lm_head_logits;  // same, also storing FP32 logits
+};
+
+} // namespace
+
+struct CudaTinyLlamaModelRunner::Impl {
+    TinyLlamaConfig cfg{};
+    WeightManifest manifest{};
+    EngineKvBackend* kv{nullptr};
+    cudaStream_t stream{nullptr};
+    CudaModelRunnerOptions options{};
+    kk_kv_pools pools{};
+
+    std::uint8_t* weights{nullptr};
+    std::uint64_t weight_bytes{0};
+    std::uint16_t const* embed{nullptr};
+    std::uint16_t const* lm_head{nullptr};
+    std::uint16_t const* final_norm{nullptr};
+    std::vector<LayerWeights> layers;
+
+    // Workspace (device).
+    std::uint8_t* ws{nullptr};
+    std::uint64_t ws_bytes{0};
+    std::uint32_t bpad{0};
+    std::uint16_t* hidden{nullptr};
+    std::uint16_t* normed{nullptr};
+    std::uint16_t* q{nullptr};
+    std::uint16_t* attn{nullptr};
+    std::uint16_t* act{nullptr};
+    float* logits{nullptr};
+    std::uint32_t* out_tokens{nullptr};
+    void* attn_ws{nullptr};
+    std::uint64_t attn_ws_bytes{0};
+    void* argmax_ws{nullptr};
+
+    // Step inputs: one region on the device, a pinned mirror on the host.
+    std::uint32_t max_items{0};
+    std::uint32_t max_descs{0};
+    std::size_t off_counts{0}, off_tokens{0}, off_positions{0}, off_slots{0}, off_copies{0},
+        off_lanes{0}, off_items{0}, off_descs{0}, step_bytes{0};
+    std::uint8_t* step_dev{nullptr};
+    std::uint8_t* step_host{nullptr};
+    std::uint32_t* host_tokens{nullptr};
+
+    cudaEvent_t ev_begin{nullptr};
+    cudaEvent_t ev_end{nullptr};
+    float last_ms{0.f};
+    std::uint32_t last_launches{0};
+
+    std::unordered_map<std::uint32_t, BatchPlans> plans;
+    std::unordered_map<std::uint32_t, cudaGraphExec_t> graphs;
+
+    ~Impl()
+    {
+        if (stream != nullptr) {
+            cudaStreamSynchronize(stream);
+        }
+        for (auto& g : graphs) {
+            cudaGraphExecDestroy(g.second);
+        }
+        plans.clear();
+        cudaFree(weights);
+        cudaFree(ws);
+        cudaFree(step_dev);
+        cudaFreeHost(step_host);
+        cudaFreeHost(host_tokens);
+        if (ev_begin != nullptr) cudaEventDestroy(ev_begin);
+        if (ev_end != nullptr) cudaEventDestroy(ev_end);
+    }
+
+    template <typename T>
+    T* stepHost(std::size_t off) { return reinterpret_cast<T*>(step_host + off); }
+    template <typename T>
+    T* stepDev(std::size_t off) { return reinterpret_cast<T*>(step_dev + off); }
+
+    CudaModelRunnerStatus buildPlans(std::uint32_t batch, BatchPlans& out);
+    CudaModelRunnerStatus enqueueForward(std::uint32_t batch, bool has_copies, BatchPlans const& p,
+        bool want_logits, ModelRunnerDebugCapture* debug);
+    CudaModelRunnerStatus runStep(std::uint32_t batch, bool has_copies, bool want_logits,
+        ModelRunnerDebugCapture* debug);
+};
+
+CudaTinyLlamaModelRunner::CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept
+    : impl_(std::move(impl))
+{
+}
+
+CudaTinyLlamaModelRunner::~CudaTinyLlamaModelRunner() = default;
+
+TinyLlamaConfig CudaTinyLlamaModelRunner::config() const noexcept { return impl_->cfg; }
+TinyLlamaConfig CudaTinyLlamaModelRunner::generationConfig() const noexcept { return impl_->cfg; }
+std::uint64_t CudaTinyLlamaModelRunner::deviceWeightBytes() const noexcept { return impl_->weight_bytes; }
+std::uint64_t CudaTinyLlamaModelRunner::deviceWorkspaceBytes() const noexcept
+{
+    return impl_->ws_bytes + impl_->step_bytes;
+}
+std::uint32_t CudaTinyLlamaModelRunner::maxBatchSize() const noexcept { return impl_->options.max_batch_size; }
+std::uint32_t CudaTinyLlamaModelRunner::generationMaxBatchSize() const noexcept
+{
+    return impl_->options.max_batch_size;
+}
+float CudaTinyLlamaModelRunner::lastStepDeviceMs() const noexcept { return impl_->last_ms; }
+std::uint32_t CudaTinyLlamaModelRunner::lastStepLaunches() const noexcept { return impl_->last_launches; }
+
+CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t batch, BatchPlans& out)
+{
+    TinyLlamaConfig const& c = cfg;
+    std::uint32_t const qkv_rows = (c.attention_head_count + 2 * c.kv_head_count) * c.head_dimension;
+    auto make = [&](kk_gemm_desc const& d, kk::GemmPlanPtr& slot) -> bool {
+        int rc = 0;
+        slot = kk::gemmPlan(d, rc);
+        return slot != nullptr;
+    };
+    auto base = [&](std::uint16_t const* w, std::uint32_t m, std::uint32_t k, std::uint16_t const* x,
+                    std::uint32_t epi, void* o, std::uint32_t ostride) {
+        kk_gemm_desc d{};
+        d.weight = w;
+        d.M = m;
+        d.K = k;
+        d.x = x;
+        d.N = batch;
+        d.x_stride = k;
+        d.x_rows = bpad;
+        d.epilogue = epi;
+        d.out = o;
+        d.out_stride = ostride;
+        return d;
+    };
+    for (std::uint32_t l = 0; l < c.layer_count; ++l) {
+        LayerWeights const& w = layers[l];
+        kk_gemm_desc d = base(w.w_qkv, qkv_rows, c.hidden_size, normed, KK_EPI_QKV_ROPE, q, c.hidden_size);
+        d.positions = stepDev<std::uint32_t>(off_positions);
+        d.slots = stepDev<kk_kv_slot>(off_slots);
+        d.pools = pools;
+        d.layer = l;
+        d.q_rows = c.attention_head_count * c.head_dimension;
+        d.kv_rows = c.kv_head_count * c.head_dimension;
+        d.head_dim = c.head_dimension;
+        d.rope_theta = c.rope_theta;
+        out.qkv.emplace_back();
+        out.o.emplace_back();
+        out.gu.emplace_back();
+        out.down.emplace_back();
+        if (!make(d, out.qkv.back())
+            || !make(base(w.w_o, c.hidden_size, c.hidden_size, attn, KK_EPI_RESIDUAL, hidden, c.hidden_size), out.o.back())
+            || !make(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, normed, KK_EPI_SILU_PAIRS, act,
+                          c.intermediate_size), out.gu.back())
+            || !make(base(w.w_down, c.hidden_size, c.intermediate_size, act, KK_EPI_RESIDUAL, hidden,
+                          c.hidden_size), out.down.back())) {
+            return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "projection plan rejected");
+        }
+    }
+    kk_gemm_desc lm = base(lm_head, c.vocabulary_size, c.hidden_size, normed, KK_EPI_ARGMAX, nullptr, 0);
+    lm.tokens = out_tokens;
+    lm.argmax_workspace = argmax_ws;
+    kk_gemm_desc lm_logits = lm;
+    lm_logits.out = logits;
+    lm_logits.out_stride = c.vocabulary_size;
+    if (!make(lm, out.lm_head) || !make(lm_logits, out.lm_head_logits)) {
+        return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "LM head plan rejected");
+    }
+    return {};
+}
+
+CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(std::uint32_t batch,
+    bool has_copies, BatchPlans const& p, bool want_logits, ModelRunnerDebugCapture* debug)
+{
+    TinyLlamaConfig const& c = cfg;
+    std::uint32_t const H = c.hidden_size;
+    std::uint32_t const qrow = c.attention_head_count * c.head_dimension;
+    float const scale = 1.0f / std::sqrt(static_cast<float>(c.head_dimension));
+    std::uint32_t launches = 0;
+    auto check = [&](int rc, char const* what) {
+        ++launches;
+        return rc == 0 ? CudaModelRunnerStatus{} : cudaFailure(rc, what);
+    };
+    CudaModelRunnerStatus s;
+    if (has_copies) {
+        s = check(kk::kvCopyDevCount(&pools, 0, c.layer_count, stepDev<kk_kv_copy>(off_copies),
+                      stepDev<std::uint32_t>(off_counts) + 1, batch, stream), "copy-on-write");
+        if (!s.ok()) return s;
+    }
+    s = check(kk_embed_rmsnorm(embed, stepDev<std::uint32_t>(off_tokens), layers[0].in_norm, hidden,
+                  normed, batch, H, c.rms_norm_epsilon, stream), "embedding + rmsnorm");
+    if (!s.ok()) return s;
+    std::unordered_map<std::uint32_t, std::size_t> capture;
+    if (debug != nullptr) {
+        cudaMemcpyAsync(debug->embedding.data(), hidden, H * 2, cudaMemcpyDeviceToHost, stream);
+        for (std::size_t i = 0; i < debug->layer_indices.size(); ++i) {
+            capture.emplace(debug->layer_indices[i], i);
+        }
+    }
+    for (std::uint32_t l = 0; l < c.layer_count; ++l) {
+        LayerWeights const& w = layers[l];
+        if (!(s = check(kk::gemmRun(*p.qkv[l], stream), "qkv projection")).ok()
+            || !(s = check(kk::attentionDevCount(&pools, l, c.attention_head_count,
+                     stepDev<kk_page_desc>(off_descs), stepDev<kk_attn_lane>(off_lanes), batch,
+                     stepDev<kk_attn_item>(off_items), stepDev<std::uint32_t>(off_counts), max_items,
+                     q, qrow, attn, qrow, scale, attn_ws, attn_ws_bytes, stream), "paged attention")).ok()
+            || !(s = check(kk::gemmRun(*p.o[l], stream), "output projection")).ok()
+            || !(s = check(kk_rmsnorm(hidden, w.post_norm, normed, batch, H, c.rms_norm_epsilon, stream),
+                     "post-attention rmsnorm")).ok()
+            || !(s = check(kk::gemmRun(*p.gu[l], stream), "gate/up projection")).ok()
+            || !(s = check(kk::gemmRun(*p.down[l], stream), "down projection")).ok()) {
+            return s;
+        }
+        if (debug != nullptr) {
+            auto const f = capture.find(l);
+            if (f != capture.end()) {
+                cudaMemcpyAsync(debug->layer_hidden_states[f->second].data(), hidden, H * 2,
+                    cudaMemcpyDeviceToHost, stream);
+            }
+        }
+        std::uint16_t const* next_norm = l + 1 < c.layer_count ? layers[l + 1].in_norm : final_norm;
+        s = check(kk_rmsnorm(hidden, next_norm, normed, batch, H, c.rms_norm_epsilon, stream), "rmsnorm");
+        if (!s.ok()) return s;
+    }
+    s = check(kk::gemmRun(want_logits ? *p.lm_head_logits : *p.lm_head, stream), "lm head + argmax");
+    if (!s.ok()) return s;
+    if (debug != nullptr) {
+        cudaMemcpyAsync(debug->final_hidden_state.data(), normed, H * 2, cudaMemcpyDeviceToHost, stream);
+    }
+    last_launches = launches;
+    return {};
+}
+
+CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::runStep(std::uint32_t batch, bool has_copies,
+    bool want_logits, ModelRunnerDebugCapture* debug)
+{
+    auto found = plans.find(batch);
+    if (found == plans.end()) {
+        BatchPlans fresh;
+        CudaModelRunnerStatus const built = buildPlans(batch, fresh);
+        if (!built.ok()) {
+            return built;
+        }
+        found = plans.emplace(batch, std::move(fresh)).first;
+    }
+    kk_set_pdl(1);
+    cudaEventRecord(ev_begin, stream);
+    bool const graphable = options.use_cuda_graphs && debug == nullptr && !want_logits;
+    CudaModelRunnerStatus s;
+    if (graphable) {
+        std::uint32_t const key = batch * 2 + (has_copies ? 1u : 0u);
+        auto g = graphs.find(key);
+        if (g == graphs.end()) {
+            cudaGraph_t graph = nullptr;
+            cudaError_t e = cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal);
+            if (e == cudaSuccess) {
+                s = enqueueForward(batch, has_copies, found->second, false, nullptr);
+                e = cudaStreamEndCapture(stream, &graph);
+            }
+            cudaGraphExec_t exec = nullptr;
+            if (e == cudaSuccess && s.ok()) {
+                e = cudaGraphInstantiate(&exec, graph, 0);
+            }
+            if (graph != nullptr) {
+                cudaGraphDestroy(graph);
+            }
+            if (!s.ok()) {
+                kk_set_pdl(0);
+                return s;
+            }
+            if (e != cudaSuccess) {
+                kk_set_pdl(0);
+                return cudaFailure(static_cast<int>(e), "capture decode graph");
+            }
+            g = graphs.emplace(key, exec).first;
+        }
+        cudaError_t const e = cudaGraphLaunch(g->second, stream);
+        if (e != cudaSuccess) {
+            s = cudaFailure(static_cast<int>(e), "launch decode graph");
+        }
+    } else {
+        s = enqueueForward(batch, has_copies, found->second, want_logits, debug);
+    }
+    kk_set_pdl(0);
+    cudaEventRecord(ev_end, stream);
+    return s;
+}
+
+// One fused step over every valid lane of `items`.
+GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
+    std::vector<GenerationBatchItem> const& items, bool want_logits, ModelRunnerDebugCapture* debug,
+    std::vector<float>* logits_out)
+{
+    GenerationBatchResult result;
+    TinyLlamaConfig const& c = im.cfg;
+    if (items.empty() || items.size() > im.options.max_batch_size) {
+        result.detail = "generation batch is empty or exceeds max batch size";
+        return result;
+    }
+    result.steps.resize(items.size());
+    std::vector<std::size_t> lane_index;
+    std::vector<TokenTransaction> txns;
+    lane_index.reserve(items.size());
+    txns.reserve(items.size());
+    for (std::size_t i = 0; i < items.size(); ++i) {
+        GenerationBatchItem const& it = items[i];
+        if (it.request_id == kInvalidRequestId || it.token_id >= c.vocabulary_size
+            || it.expected_position >= c.max_position_embeddings) {
+            result.steps[i] = {false, 0, "request, token, or position is out of range"};
+            continue;
+        }
+        TokenReserveResult reserved = im.kv->reserveToken(
+            ReserveTokenRequest{it.request_id, it.expected_position, im.stream});
+        if (!reserved.ok()) {
+            result.steps[i] = {false, 0, kvFailure(reserved.status, "reserve token").detail};
+            continue;
+        }
+        EngineKvStatus const submitted = reserved.transaction.submitFusedLayers();
+        if (!submitted.ok()) {
+            result.steps[i] = {false, 0, kvFailure(submitted, "submit fused layers").detail};
+            continue;  // the transaction rolls back when it goes out of scope
+        }
+        lane_index.push_back(i);
+        txns.push_back(std::move(reserved.transaction));
+    }
+    result.success = true;
+    std::uint32_t const B = static_cast<std::uint32_t>(txns.size());
+    if (B == 0) {
+        return result;
+    }
+
+    // Step inputs into the pinned mirror.
+    auto* tokens = im.stepHost<std::uint32_t>(im.off_tokens);
+    auto* positions = im.stepHost<std::uint32_t>(im.off_positions);
+    auto* slots = im.stepHost<kk_kv_slot>(im.off_slots);
+    auto* copies = im.stepHost<kk_kv_copy>(im.off_copies);
+    auto* lanes = im.stepHost<kk_attn_lane>(im.off_lanes);
+    auto* descs = im.stepHost<kk_page_desc>(im.off_descs);
+    std::uint32_t n_copies = 0;
+    std::uint32_t n_descs = 0;
+    for (std::uint32_t b = 0; b < B; ++b) {
+        FusedLane lane{};
+        if (!fusedLane(txns[b], lane)) {
+            result.success = false;
+            result.detail = "KV backend does not support the fused decode step";
+            return result;
+        }
+        GenerationBatchItem const& it = items[lane_index[b]];
+        tokens[b] = it.token_id;
+        positions[b] = it.expected_position;
+        auto const& entries = lane.reserved->entries();
+        MappingEntry const& target = entries.back();
+        slots[b] = kk_kv_slot{target.handle.slot,
+            static_cast<std::uint16_t>(lane.reserved->tokenCount() - 1 - target.logical_token_begin),
+            static_cast<std::uint8_t>(target.kind), 1};
+        if (!lane.before->entries().empty()) {
+            MappingEntry const& old_tail = lane.before->entries().back();
+            if (old_tail.logical_token_begin == target.logical_token_begin
+                && old_tail.handle != target.handle) {
+                copies[n_copies++] = kk_kv_copy{old_tail.handle.slot, target.handle.slot,
+                    old_tail.valid_tokens, static_cast<std::uint8_t>(old_tail.kind),
+                    static_cast<std::uint8_t>(target.kind)};
+            }
+        }
+        if (n_descs + entries.size() > im.max_descs) {
+            result.success = false;
+            result.detail = "step descriptor capacity exceeded";
+            return result;
+        }
+        lanes[b] = kk_attn_lane{n_descs, static_cast<std::uint32_t>(entries.size()),
+            lane.reserved->tokenCount(), 0, 0, b, {0, 0}};
+        for (MappingEntry const& e : entries) {
+            descs[n_descs++] = kk_page_desc{e.handle.slot, e.logical_token_begin, e.valid_tokens,
+                static_cast<std::uint8_t>(e.kind), 0, 0};
+        }
+    }
+    std::uint32_t const n_items = kk_attention_plan(descs, lanes, B, kAttentionTargetTokens,
+        im.stepHost<kk_attn_item>(im.off_items), im.max_items);
+    if (n_items > im.max_items) {
+        result.success = false;
+        result.detail = "attention work list capacity exceeded";
+        return result;
+    }
+    auto* counts = im.stepHost<std::uint32_t>(im.off_counts);
+    counts[0] = n_items;
+    counts[1] = n_copies;
+    std::size_t const bytes = im.off_descs + std::size_t(n_descs) * sizeof(kk_page_desc);
+    std::string fail_detail;
+    cudaError_t e = cudaMemcpyAsync(im.step_dev, im.step_host, bytes, cudaMemcpyHostToDevice, im.stream);
+    CudaModelRunnerStatus s = e == cudaSuccess
+        ? im.runStep(B, n_copies != 0, want_logits, debug)
+        : cudaFailure(static_cast<int>(e), "upload step inputs");
+    if (s.ok()) {
+        e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, B * 4u, cudaMemcpyDeviceToHost, im.stream);
+        if (e == cudaSuccess && logits_out != nullptr) {
+            logits_out->resize(c.vocabulary_size);
+            e = cudaMemcpyAsync(logits_out->data(), im.logits, c.vocabulary_size * 4u,
+                cudaMemcpyDeviceToHost, im.stream);
+        }
+        if (e == cudaSuccess) {
+            e = cudaStreamSynchronize(im.stream);
+        }
+        if (e != cudaSuccess) {
+            s = failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
+                std::string("decode step failed: ") + cudaGetErrorString(e));
+        }
+    }
+    if (s.ok()) {
+        noteStreamCompleted(*im.kv, im.stream);
+        cudaEventElapsedTime(&im.last_ms, im.ev_begin, im.ev_end);
+    }
+    for (std::uint32_t b = 0; b < B; ++b) {
+        std::size_t const i = lane_index[b];
+        if (!s.ok()) {
+            result.steps[i] = {false, 0, s.detail};
+            continue;  // rolled back by the transaction destructor
+        }
+        EngineKvStatus const committed = txns[b].commit();
+        result.steps[i] = committed.ok()
+            ? GenerationStepResult{true, im.host_tokens[b], {}}
+            : GenerationStepResult{false, 0, kvFailure(committed, "commit batched model token").detail};
+    }
+    return result;
+}
+
+ModelTokenResult CudaTinyLlamaModelRunner::forwardToken(RequestId request_id,
+    std::uint32_t token_id, std::uint32_t expected_position, ModelRunnerDebugCapture* debug,
+    ModelRunnerOutputOptions output)
+{
+    ModelTokenResult result;
+    TinyLlamaConfig const& c = impl_->cfg;
+    if (request_id == kInvalidRequestId || token_id >= c.vocabulary_size
+        || expected_position >= c.max_position_embeddings) {
+        result.status = failure(CudaModelRunnerError::InvalidArgument, 0,
+            "request, token, or position is out of range");
+        return result;
+    }
+    if (debug != nullptr) {
+        std::unordered_set<std::uint32_t> seen;
+        for (std::uint32_t l : debug->layer_indices) {
+            if (l >= c.layer_count || !seen.insert(l).second) {
+                result.status = failure(CudaModelRunnerError::InvalidArgument, 0,
+                    "debug layer is duplicated or out of range");
+                return result;
+            }
+        }
+        debug->embedding.assign(c.hidden_size, 0);
+        debug->final_hidden_state.assign(c.hidden_size, 0);
+        debug->layer_hidden_states.assign(debug->layer_indices.size(),
+            std::vector<KvScalar>(c.hidden_size, 0));
+    }
+    GenerationBatchResult batch;
+    std::vector<GenerationBatchItem> items{GenerationBatchItem{request_id, token_id, expected_position}};
+    // The single-token path shares the batched implementation.
+    std::vector<float> logits;
+    batch = runBatch(*impl_, items, output.copy_logits, debug, output.copy_logits ? &logits : nullptr);
+    if (!batch.success || batch.steps.size() != 1) {
+        result.status = failure(CudaModelRunnerError::ExecutionFailed, 0, batch.detail);
+        return result;
+    }
+    if (!batch.steps[0].success) {
+        result.status = failure(CudaModelRunnerError::KvBackendFailed, 0, batch.steps[0].detail);
+        return result;
+    }
+    result.greedy_token_id = batch.steps[0].greedy_token_id;
+    result.logits = std::move(logits);
+    return result;
+}
+
+GenerationBatchResult CudaTinyLlamaModelRunner::generationForwardBatch(
+    std::vector<GenerationBatchItem> const& batch)
+{
+    return runBatch(*impl_, batch, false, nullptr, nullptr);
+}
+
+GenerationStepResult CudaTinyLlamaModelRunner::generationForwardToken(RequestId request_id,
+    std::uint32_t token_id, std::uint32_t expected_position)
+{
+    GenerationBatchResult r = runBatch(*impl_, {GenerationBatchItem{request_id, token_id, expected_position}},
+        false, nullptr, nullptr);
+    if (!r.success || r.steps.size() != 1) {
+        return {false, 0, r.detail.empty() ? "single-token batch returned an invalid result" : r.detail};
+    }
+    return std::move(r.steps[0]);
+}
+
+// ---- construction ---------------------------------------------------------------------
+
+CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& manifest_path,
+    std::string const& data_path, EngineKvBackend& kv_backend, EngineStream stream,
+    CudaModelRunnerOptions options)
+{
+    CudaModelRunnerCreateResult out;
+    if (!options.valid()) {
+        out.status = failure(CudaModelRunnerError::InvalidArgument, 0, "invalid runner options");
+        return out;
+    }
+    WeightManifestLoadResult loaded = loadWeightManifest(manifest_path);
+    if (!loaded.ok()) {
+        out.status = failure(CudaModelRunnerError::ManifestError, static_cast<int>(loaded.status.error),
+            loaded.status.detail);
+        return out;
+    }
+    if (options.verify_checksums) {
+        WeightManifestStatus const data = validateWeightDataFile(loaded.manifest, data_path);
+        if (!data.ok()) {
+            out.status = failure(CudaModelRunnerError::DataFileError, static_cast<int>(data.error), data.detail);
+            return out;
+        }
+    }
+    TinyLlamaConfig const c = loaded.manifest.config;
+    EngineKvConfig const kvc = kv_backend.config();
+    if (kvc.kv_layout.layer_count != c.layer_count || kvc.kv_layout.kv_head_count != c.kv_head_count
+        || kvc.kv_layout.head_dimension != c.head_dimension
+        || kvc.query_head_count != c.attention_head_count) {
+        out.status = failure(CudaModelRunnerError::InvalidArgument, 0,
+            "KV backend layout does not match the model");
+        return out;
+    }
+    kk_kv_pools const* pools = cudaBackendPools(kv_backend);
+    if (pools == nullptr) {
+        out.status = failure(CudaModelRunnerError::InvalidArgument, 0,
+            "the fused decode step needs a CUDA KV backend of this library");
+        return out;
+    }
+    std::uint32_t const group = c.attention_head_count / c.kv_head_count;
+    if (c.head_dimension != 64 || (c.kv_head_count != 1 && c.kv_head_count != 2 && c.kv_head_count != 4)
+        || group > 16 || c.hidden_size % 64 != 0 || c.intermediate_size % 8 != 0) {
+        out.status = failure(CudaModelRunnerError::InvalidArgument, 0,
+            "model shape outside the sm_100a kernels (head_dim 64, kv_heads 1/2/4, group <= 16)");
+        return out;
+    }
+    auto im = std::make_unique<CudaTinyLlamaModelRunner::Impl>();
+    im->cfg = c;
+    im->manifest = loaded.manifest;
+    im->kv = &kv_backend;
+    im->stream = static_cast<cudaStream_t>(stream);
+    im->options = options;
+    im->pools = *pools;
+
+    // Weights: one device allocation in the fused layout.
+    std::uint64_t const H = c.hidden_size, I = c.intermediate_size, V = c.vocabulary_size;
+    std::uint64_t const kvr = std::uint64_t(c.kv_head_count) * c.head_dimension;
+    std::uint64_t const qkv_rows = H + 2 * kvr;
+    auto pad = [](std::uint64_t n) { return (n + 63) & ~std::uint64_t(63); };  // 128-byte aligned tensors
+    std::uint64_t const padded = 2 * pad(V * H) + pad(H)
+        + c.layer_count * (2 * pad(H) + pad(qkv_rows * H) + pad(H * H) + pad(2 * I * H) + pad(H * I));
+    im->weight_bytes = padded * 2;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&im->weights), im->weight_bytes);
+    if (e != cudaSuccess) {
+        out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "weight allocation");
+        return out;
+    }
+    std::uint16_t* w16 = reinterpret_cast<std::uint16_t*>(im->weights);
+    std::uint64_t cursor = 0;
+    auto take = [&](std::uint64_t elems) {
+        std::uint16_t* p = w16 + cursor;
+        cursor += pad(elems);
+        return p;
+    };
+    std::uint16_t* embed = take(V * H);
+    std::uint16_t* lm = take(V * H);
+    std::uint16_t* fnorm = take(H);
+    im->embed = embed;
+    im->lm_head = lm;
+    im->final_norm = fnorm;
+    struct Dest {
+        std::uint16_t* base;
+        std::uint64_t row_pitch;  // destination row pitch (elements); 0 = contiguous
+        std::uint64_t rows;
+    };
+    std::unordered_map<std::string, Dest> dest;
+    dest["model.embed_tokens.weight"] = {embed, 0, 0};
+    dest["lm_head.weight"] = {lm, 0, 0};
+    dest["model.norm.weight"] = {fnorm, 0, 0};
+    for (std::uint32_t l = 0; l < c.layer_count; ++l) {
+        std::string const p = "model.layers." + std::to_string(l) + ".";
+        LayerWeights lw{};
+        std::uint16_t* in_norm = take(H);
+        std::uint16_t* post_norm = take(H);
+        std::uint16_t* qkv = take(qkv_rows * H);
+        std::uint16_t* o = take(H * H);
+        std::uint16_t* gu = take(2 * I * H);
+        std::uint16_t* down = take(H * I);
+        lw = LayerWeights{in_norm, post_norm, qkv, o, gu, down};
+        im->layers.push_back(lw);
+        dest[p + "input_layernorm.weight"] = {in_norm, 0, 0};
+        dest[p + "post_attention_layernorm.weight"] = {post_norm, 0, 0};
+        dest[p + "self_attn.q_proj.weight"] = {qkv, 0, 0};
+        dest[p + "self_attn.k_proj.weight"] = {qkv + H * H, 0, 0};
+        dest[p + "self_attn.v_proj.weight"] = {qkv + (H + kvr) * H, 0, 0};
+        dest[p + "self_attn.o_proj.weight"] = {o, 0, 0};
+        dest[p + "mlp.gate_proj.weight"] = {gu, 2 * H, I};      // rows 0, 2, 4, ...
+        dest[p + "mlp.up_proj.weight"] = {gu + H, 2 * H, I};    // rows 1, 3, 5, ...
+        dest[p + "mlp.down_proj.weight"] = {down, 0, 0};
+    }
+    {
+        std::ifstream in(data_path, std::ios::binary);
+        if (!in) {
+            out.status = failure(CudaModelRunnerError::DataFileError, 0, "cannot open " + data_path);
+            return out;
+        }
+        std::vector<char> staging;
+        for (WeightTensorDescriptor const& t : im->manifest.tensors) {
+            auto const d = dest.find(t.name);
+            if (d == dest.end()) {
+                continue;
+            }
+            staging.resize(t.byte_size);
+            in.seekg(static_cast<std::streamoff>(t.offset));
+            in.read(staging.data(), static_cast<std::streamsize>(t.byte_size));
+            if (in.gcount() != static_cast<std::streamsize>(t.byte_size)) {
+                out.status = failure(CudaModelRunnerError::DataFileError, 0, "short read: " + t.name);
+                return out;
+            }
+            if (d->second.row_pitch == 0) {
+                e = cudaMemcpy(d->second.base, staging.data(), t.byte_size, cudaMemcpyHostToDevice);
+            } else {
+                std::uint64_t const width = t.byte_size / d->second.rows;
+                e = cudaMemcpy2D(d->second.base, d->second.row_pitch * 2, staging.data(), width, width,
+                    d->second.rows, cudaMemcpyHostToDevice);
+            }
+            if (e != cudaSuccess) {
+                out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e),
+                    "weight upload: " + t.name);
+                return out;
+            }
+        }
+    }
+
+    // Workspace.
+    std::uint32_t const bmax = options.max_batch_size;
+    im->bpad = std::max<std::uint32_t>(64, (bmax + 15) / 16 * 16);
+    std::uint32_t const positions_cap = c.max_position_embeddings + 8;
+    im->max_descs = bmax * (positions_cap / 8 + 2);
+    im->max_items = bmax * (positions_cap / kAttentionTargetTokens + 2) + positions_cap / 8;
+    std::size_t off = 0;
+    auto region = [&](std::size_t bytes) {
+        std::size_t const at = off;
+        off = align256(off + bytes);
+        return at;
+    };
+    std::size_t const o_hidden = region(std::size_t(im->bpad) * H * 2);
+    std::size_t const o_normed = region(std::size_t(im->bpad) * H * 2);
+    std::size_t const o_q = region(std::size_t(im->bpad) * H * 2);
+    std::size_t const o_attn = region(std::size_t(im->bpad) * H * 2);
+    std::size_t const o_act = region(std::size_t(im->bpad) * I * 2);
+    std::size_t const o_logits = region(std::size_t(bmax) * V * 4);
+    std::size_t const o_tok = region(std::size_t(bmax) * 4);
+    im->attn_ws_bytes = kk_attention_workspace_bytes(bmax, im->max_items, c.attention_head_count,
+        c.head_dimension);
+    std::size_t const o_attn_ws = region(im->attn_ws_bytes);
+    std::size_t const o_argmax = region(kk_argmax_workspace_bytes(c.vocabulary_size, bmax));
+    im->ws_bytes = off;
+    e = cudaMalloc(reinterpret_cast<void**>(&im->ws), im->ws_bytes);
+    if (e == cudaSuccess) {
+        e = cudaMemset(im->ws, 0, im->ws_bytes);
+    }
+    if (e != cudaSuccess) {
+        out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "workspace");
+        return out;
+    }
+    im->hidden = reinterpret_cast<std::uint16_t*>(im->ws + o_hidden);
+    im->normed = reinterpret_cast<std::uint16_t*>(im->ws + o_normed);
+    im->q = reinterpret_cast<std::uint16_t*>(im->ws + o_q);
+    im->attn = reinterpret_cast<std::uint16_t*>(im->ws + o_attn);
+    im->act = reinterpret_cast<std::uint16_t*>(im->ws + o_act);
+    im->logits = reinterpret_cast<float*>(im->ws + o_logits);
+    im->out_tokens = reinterpret_cast<std::uint32_t*>(im->ws + o_tok);
+    im->attn_ws = im->ws + o_attn_ws;
+    im->argmax_ws = im->ws + o_argmax;
+
+    off = 0;
+    im->off_counts = region(16);
+    im->off_tokens = region(std::size_t(bmax) * 4);
+    im->off_positions = region(std::size_t(bmax) * 4);
+    im->off_slots = region(std::size_t(bmax) * sizeof(kk_kv_slot));
+    im->off_copies = region(std::size_t(bmax) * sizeof(kk_kv_copy));
+    im->off_lanes = region(std::size_t(bmax) * sizeof(kk_attn_lane));
+    im->off_items = region(std::size_t(im->max_items) * sizeof(kk_attn_item));
+    im->off_descs = region(std::size_t(im->max_descs) * sizeof(kk_page_desc));
+    im->step_bytes = off;
+    e = cudaMalloc(reinterpret_cast<void**>(&im->step_dev), im->step_bytes);
+    if (e == cudaSuccess) {
+        e = cudaMallocHost(reinterpret_cast<void**>(&im->step_host), im->step_bytes);
+    }
+    if (e == cudaSuccess) {
+        e = cudaMallocHost(reinterpret_cast<void**>(&im->host_tokens), std::size_t(bmax) * 4);
+    }
+    if (e == cudaSuccess) {
+        e = cudaEventCreate(&im->ev_begin);
+    }
+    if (e == cudaSuccess) {
+        e = cudaEventCreate(&im->ev_end);
+    }
+    if (e == cudaSuccess) {
+        std::memset(im->step_host, 0, im->step_bytes);
+        e = cudaDeviceSynchronize();
+    }
+    if (e != cudaSuccess) {
+        out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "step buffers");
+        return out;
+    }
+    out.runner.reset(new CudaTinyLlamaModelRunner(std::move(im)));
+    return out;
+}
+
+} // namespace kimkvcache

@@ -1,0 +1,124 @@
+// TinyLlama-shaped FP16 decoder runner on the B200 kernels.
+//
+// Public API follows the reference CUDA runner
+// (include/kim-kv/cuda/cuda_model_runner.h:14-186): factory from a weight
+// manifest + archive, an EngineKvBackend and a stream; forwardToken with
+// optional debug capture; the GenerationModelRunner SPI.
+//
+// Execution: one model batch (all lanes) runs as one fused device step:
+// COW copies -> embedding+RMSNorm -> per layer [QKV projection with RoPE and
+// KV-page write fused in its epilogue, paged attention over all lanes, O
+// projection + residual, RMSNorm, gate/up projection + SiLU gate, down
+// projection + residual, RMSNorm] -> LM head + greedy argmax -> token ids to
+// host. Host work per step: reserve each lane, one upload of the step inputs
+// (tokens, positions, write slots, page descriptors, attention work list),
+// one stream synchronisation, commit each lane. With graphs enabled the
+// device part is replayed from a CUDA graph captured per batch size.
+#pragma once
+
+#include "../host/generation.h"
+#include "cuda_backend.h"
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace kimkvcache {
+
+enum class CudaModelRunnerError : std::uint8_t {
+    None,
+    InvalidArgument,
+    InvalidState,
+    ManifestError,
+    DataFileError,
+    AllocationFailed,
+    CublasFailed,  // kept for API compatibility; never produced (no cuBLAS)
+    SubmissionFailed,
+    ExecutionFailed,
+    KvBackendFailed,
+};
+
+struct CudaModelRunnerStatus final {
+    CudaModelRunnerError error{CudaModelRunnerError::None};
+    int native_code{0};
+    std::string detail{};
+    [[nodiscard]] bool ok() const noexcept { return error == CudaModelRunnerError::None; }
+    [[nodiscard]] explicit operator bool() const noexcept { return ok(); }
+};
+
+struct ModelRunnerDebugCapture final {
+    std::vector<std::uint32_t> layer_indices{};
+    std::vector<KvScalar> embedding{};
+    std::vector<std::vector<KvScalar>> layer_hidden_states{};
+    std::vector<KvScalar> final_hidden_state{};
+};
+
+struct ModelTokenResult final {
+    CudaModelRunnerStatus status{};
+    std::uint32_t greedy_token_id{0};
+    std::vector<float> logits{};
+    [[nodiscard]] bool ok() const noexcept { return status.ok(); }
+};
+
+struct ModelRunnerOutputOptions final {
+    bool copy_logits{true};
+};
+
+struct CudaModelRunnerOptions final {
+    std::uint32_t max_batch_size{8};   // at most 64 lanes per model batch
+    bool use_cuda_graphs{true};        // replay the device step from a CUDA graph
+    bool verify_checksums{true};       // SHA-256 of every tensor at load
+    [[nodiscard]] constexpr bool valid() const noexcept
+    {
+        return max_batch_size != 0 && max_batch_size <= 64;
+    }
+};
+
+struct CudaModelRunnerCreateResult;
+
+class CudaTinyLlamaModelRunner final : public GenerationModelRunner {
+public:
+    struct Impl;
+    ~CudaTinyLlamaModelRunner() override;
+
+    [[nodiscard]] TinyLlamaConfig config() const noexcept;
+    [[nodiscard]] std::uint64_t deviceWeightBytes() const noexcept;
+    [[nodiscard]] std::uint64_t deviceWorkspaceBytes() const noexcept;
+    [[nodiscard]] std::uint32_t maxBatchSize() const noexcept;
+
+    [[nodiscard]] ModelTokenResult forwardToken(RequestId request_id, std::uint32_t token_id,
+        std::uint32_t expected_position, ModelRunnerDebugCapture* debug_capture = nullptr,
+        ModelRunnerOutputOptions output_options = {});
+
+    [[nodiscard]] TinyLlamaConfig generationConfig() const noexcept override;
+    [[nodiscard]] GenerationStepResult generationForwardToken(RequestId request_id,
+        std::uint32_t token_id, std::uint32_t expected_position) override;
+    [[nodiscard]] GenerationBatchResult generationForwardBatch(
+        std::vector<GenerationBatchItem> const& batch) override;
+    [[nodiscard]] std::uint32_t generationMaxBatchSize() const noexcept override;
+
+    // Device time of the last fused step (ms, from CUDA events), 0 if unknown.
+    [[nodiscard]] float lastStepDeviceMs() const noexcept;
+    // Kernels launched by the last fused step.
+    [[nodiscard]] std::uint32_t lastStepLaunches() const noexcept;
+
+private:
+    explicit CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept;
+    std::unique_ptr<Impl> impl_;
+    friend CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const&,
+        std::string const&, EngineKvBackend&, EngineStream, CudaModelRunnerOptions);
+};
+
+struct CudaModelRunnerCreateResult final {
+    CudaModelRunnerStatus status{};
+    std::unique_ptr<CudaTinyLlamaModelRunner> runner{};
+    [[nodiscard]] bool ok() const noexcept { return status.ok() && runner != nullptr; }
+};
+
+// kv_backend and stream are borrowed and must outlive the runner.
+[[nodiscard]] CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(
+    std::string const& manifest_path, std::string const& data_path, EngineKvBackend& kv_backend,
+    EngineStream stream, CudaModelRunnerOptions options = {});
+
+} // namespace kimkvcache

@@ -1,0 +1,91 @@
+"""Seeded random-init TinyLlama-shaped weight archives in the reference's
+manifest format (reference src/model/weight_manifest.cpp:361-600;
+converter scripts/convert_tinyllama_weights.py writes the same format).
+
+There is no network and no checkpoint, so benchmarks and tests use
+random-init weights of the exact architecture: matrices ~ N(0, std) in FP16
+(std 0.02 by default) and RMSNorm weights = 1.0 (a N(0, 0.02) norm scale
+would shrink every activation and leave the top-2 logit gap below the FP16
+comparison tolerance).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+from pathlib import Path
+
+import numpy as np
+
+TINYLLAMA = dict(hidden=2048, intermediate=5632, layers=22, q_heads=32, kv_heads=4, head_dim=64,
+                 vocab=32000, max_positions=2048, eps=1e-5, theta=10000.0, bos=1, eos=2)
+
+
+def tensor_list(cfg: dict) -> list[tuple[str, tuple[int, ...]]]:
+    """(name, shape) in the oracle's order: embed, lm_head, final norm, then per
+    layer input norm, post norm, q, k, v, o, gate, up, down."""
+    H, I, V = cfg["hidden"], cfg["intermediate"], cfg["vocab"]
+    KV = cfg["kv_heads"] * cfg["head_dim"]
+    out = [("model.embed_tokens.weight", (V, H)), ("lm_head.weight", (V, H)),
+           ("model.norm.weight", (H,))]
+    for l in range(cfg["layers"]):
+        p = f"model.layers.{l}."
+        out += [(p + "input_layernorm.weight", (H,)), (p + "post_attention_layernorm.weight", (H,)),
+                (p + "self_attn.q_proj.weight", (H, H)), (p + "self_attn.k_proj.weight", (KV, H)),
+                (p + "self_attn.v_proj.weight", (KV, H)), (p + "self_attn.o_proj.weight", (H, H)),
+                (p + "mlp.gate_proj.weight", (cfg["intermediate"], H)),
+                (p + "mlp.up_proj.weight", (cfg["intermediate"], H)),
+                (p + "mlp.down_proj.weight", (H, I))]
+    return out
+
+
+def make_tensor(name: str, shape, rng: np.random.Generator, std: float) -> np.ndarray:
+    if name.endswith("norm.weight"):
+        return np.full(shape, 1.0, dtype=np.float16).view(np.uint16)
+    vals = rng.standard_normal(int(np.prod(shape)), dtype=np.float32) * np.float32(std)
+    return vals.astype(np.float16).view(np.uint16).reshape(shape)
+
+
+def write_archive(directory: str | os.PathLike, cfg: dict, seed: int, std: float = 0.02,
+                  keep_weights: bool = False):
+    """Writes model.manifest + model.weights under `directory` (reused when an
+    identical archive is already there). Returns (manifest, data, weights)
+    where weights is the oracle-ordered list of uint16 arrays if requested."""
+    d = Path(directory)
+    d.mkdir(parents=True, exist_ok=True)
+    manifest, data = d / "model.manifest", d / "model.weights"
+    stamp = d / "stamp.json"
+    key = json.dumps({"cfg": cfg, "seed": seed, "std": std}, sort_keys=True)
+    tensors = tensor_list(cfg)
+    rng = np.random.default_rng(seed)
+    if stamp.exists() and stamp.read_text() == key and manifest.exists() and data.exists():
+        if not keep_weights:
+            return str(manifest), str(data), None
+        return str(manifest), str(data), [make_tensor(n, s, rng, std) for n, s in tensors]
+    records, kept = [], []
+    offset = 0
+    with open(data, "wb") as f:
+        for name, shape in tensors:
+            t = make_tensor(name, shape, rng, std)
+            raw = t.tobytes()
+            f.write(raw)
+            records.append((name, offset, len(raw), shape, hashlib.sha256(raw).hexdigest()))
+            offset += len(raw)
+            if keep_weights:
+                kept.append(t)
+    lines = ["version=1", "checkpoint=synthetic/tinyllama-shape",
+             f"checkpoint_revision=seed{seed}", f"tokenizer_revision=seed{seed}",
+             "config_sha256=" + hashlib.sha256(key.encode()).hexdigest(), "dtype=fp16",
+             f"data_file={data.name}", f"data_bytes={offset}",
+             f"hidden_size={cfg['hidden']}", f"intermediate_size={cfg['intermediate']}",
+             f"layer_count={cfg['layers']}", f"attention_head_count={cfg['q_heads']}",
+             f"kv_head_count={cfg['kv_heads']}", f"head_dimension={cfg['head_dim']}",
+             f"vocabulary_size={cfg['vocab']}", f"max_position_embeddings={cfg['max_positions']}",
+             f"bos_token_id={cfg.get('bos', 1)}", f"eos_token_id={cfg.get('eos', 2)}",
+             f"rms_norm_epsilon={cfg['eps']}", f"rope_theta={cfg['theta']}",
+             "tied_word_embeddings=0", f"tensor_count={len(records)}"]
+    for name, off, size, shape, digest in records:
+        lines.append(f"tensor={name}|{off}|{size}|{','.join(map(str, shape))}|{digest}")
+    manifest.write_text("\n".join(lines) + "\n")
+    stamp.write_text(key)
+    return str(manifest), str(data), (kept if keep_weights else None)
