@@ -134,6 +134,13 @@ KK_API int kkrt_mgr_page_metadata(void* mgr, kk_handle handle, kk_page_meta* out
 KK_API void kkrt_mgr_snapshot(void* mgr, kk_mgr_snapshot* out);
 KK_API int kkrt_mgr_check_invariants(void* mgr);
 
+/* ---- weight manifest (include/kim-kv/model/weight_manifest.h:111-134) ---- */
+/* loadWeightManifest, then validateWeightDataFile when data_path is not NULL;
+ * returns the WeightManifestError of the first failing step (0 = valid). */
+KK_API int kkrt_manifest_check(const char* manifest_path, const char* data_path);
+/* computeWeightDataSha256: lower-case hex digest into out (65 bytes). */
+KK_API int kkrt_sha256_range(const char* data_path, uint64_t offset, uint64_t byte_size, char* out);
+
 /* ---- FP16 codec (include/kim-kv/reference/kv_reference.h:10-13) ---- */
 KK_API uint16_t kkrt_float_to_half(float value);
 KK_API float kkrt_half_to_float(uint16_t value);

@@ -3,6 +3,9 @@
 #include "../../../include/kk_runtime.h"
 #include "../host/fp16_codec.h"
 #include "../host/kv_cache_manager.h"
+#include "../host/weight_manifest.h"
+
+#include <cstring>
 
 #include <new>
 
@@ -180,6 +183,29 @@ void kkrt_mgr_snapshot(void* mgr, kk_mgr_snapshot* out)
 }
 
 int kkrt_mgr_check_invariants(void* mgr) { return M(mgr)->checkInvariants() ? 1 : 0; }
+
+int kkrt_manifest_check(const char* manifest_path, const char* data_path)
+{
+    WeightManifestLoadResult const loaded = loadWeightManifest(manifest_path);
+    if (!loaded.ok()) {
+        return static_cast<int>(loaded.status.error);
+    }
+    if (data_path == nullptr) {
+        return 0;
+    }
+    return static_cast<int>(validateWeightDataFile(loaded.manifest, data_path).error);
+}
+
+int kkrt_sha256_range(const char* data_path, uint64_t offset, uint64_t bytes, char* out)
+{
+    std::string digest;
+    WeightManifestStatus const s = computeWeightDataSha256(data_path, offset, bytes, digest);
+    if (!s.ok()) {
+        return static_cast<int>(s.error);
+    }
+    std::memcpy(out, digest.c_str(), digest.size() + 1);
+    return 0;
+}
 
 uint16_t kkrt_float_to_half(float value) { return floatToKvScalar(value); }
 float kkrt_half_to_float(uint16_t value) { return kvScalarToFloat(value); }
