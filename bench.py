@@ -1,0 +1,431 @@
+"""Decode-throughput benchmark of the kim-kvcache token loop on B200.
+
+Workload (default, config c4): TinyLlama-1.1B-shaped random-init FP16 decoder,
+32 lanes per GPU, per-lane context ~ U[1024, 4096] stored as 64-token extent
+pages (built by append + promotion) with 8-token micro-page tails; each step
+decodes one token for every lane through the reference-facing runner API
+(generationForwardBatch) and the fused sm_100a step. N GPUs = N independent
+replicas (one process per GPU, no collective on the data path).
+
+Prints one JSON line (rank 0): value = whole-job decode tok/s from the device
+time of the fused steps (CUDA events, max over ranks); e2e = the same through
+the host API with the per-step host->device input upload and device->host
+token readback inside the CUDA-event-timed region; roofline of the dominant
+kernel; the CPU oracle baseline on this box's host cores; SM clocks sampled
+during the timed region.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--config c4|c2|c5]
+  python bench.py --impl reference ...   # the reference path on the host CPU
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import importlib.util
+import json
+import math
+import os
+import random
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "decode tok/s/GPU TinyLlama-shape c4/c32; paged-attn HBM GB/s vs 8 TB/s"
+SEED = 0x4B564341434845  # the reference benchmark seed (include/kim-kv/benchmark/benchmark.h:123)
+
+
+def load_pkg(name, path):
+    spec = importlib.util.spec_from_file_location(name, path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def workload(config: str, rank: int):
+    rng = random.Random(SEED + 7919 * rank)
+    if config == "c2":
+        return dict(name="c2: TinyLlama-shape greedy decode, batch 1, prompt 6 (+32 new)",
+                    batch=1, contexts=[6])
+    if config == "c5":
+        return dict(name="c5: TinyLlama-shape decode replicas, 64 requests/GPU, ctx~U[64,1024]",
+                    batch=64, contexts=[rng.randint(64, 1024) for _ in range(64)])
+    return dict(name="c4: TinyLlama-shape decode, 32 lanes/GPU, ctx~U[1024,4096] extent+micro pages",
+                batch=32, contexts=[rng.randint(1024, 4096) for _ in range(32)])
+
+
+def gpu_id(torch, dev) -> str:
+    """nvidia-smi --id of this process's GPU (UUID: immune to CUDA_VISIBLE_DEVICES)."""
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        return uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+    except Exception:
+        return str(dev.index)
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks / throttle reasons sampled while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        self.file.flush()
+        rows = [r.split(",") for r in open(self.file.name).read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows if len(r) >= 9 for i in range(4)
+                          if r[5 + i].strip().lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    return 6650.0, "fallback 6.65 TB/s"
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+
+    wl = workload(args.config, rank)
+    B = wl["batch"]
+    contexts = wl["contexts"]
+    cfg = dict(synth.TINYLLAMA)
+    cfg["max_positions"] = max(4608, max(contexts) + args.steps + args.warmup + 8)
+    archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
+    if rank == 0 or dist is None:
+        manifest, data, _ = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31))
+    if dist is not None:
+        dist.barrier()
+        manifest, data = str(archive_dir / "model.manifest"), str(archive_dir / "model.weights")
+
+    K = kk.kernels()
+    R = kk.runtime()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    total_tokens = sum(contexts) + B * (args.steps + args.warmup + 2)
+    extent_cap = sum(c // 64 for c in contexts) + B
+    micro_cap = B * 16 + total_tokens // 8 + 64
+    hq, hkv, D, L = cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["layers"]
+    backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
+    assert backend, "backend allocation failed"
+    pools = kk.KvPools()
+    assert R["backend_pools"](backend, C.byref(pools))
+
+    # Prefix state: append ctx tokens, seal, promote every full 64-token run.
+    for i, ctx in enumerate(contexts):
+        rid = i + 1
+        assert R["backend_create_request"](backend, rid) == 0
+        assert R["backend_append"](backend, rid, ctx) == 0
+        R["backend_seal"](backend, rid)
+        for begin in range(0, (ctx // 64) * 64, 64):
+            assert R["backend_promote"](backend, rid, begin, sptr) == 0
+    # Synthetic KV contents for every page (the prefix K/V of a real prefill).
+    row = hkv * D
+    micro_elems = micro_cap * L * 2 * 8 * row
+    extent_elems = extent_cap * L * 2 * 64 * row
+    assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, SEED + rank, 0.35, sptr) == 0
+    assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, SEED + 1 + rank, 0.35, sptr) == 0
+    torch.cuda.synchronize(dev)
+
+    status = C.c_int(0)
+    detail = C.create_string_buffer(512)
+    runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr, max(B, 1),
+                                1, 1, C.byref(status), detail, 512)
+    assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
+
+    ids = (C.c_uint64 * B)(*range(1, B + 1))
+    tokens = (C.c_uint32 * B)(*[random.Random(SEED + b).randrange(3, 32000) for b in range(B)])
+    positions = (C.c_uint32 * B)(*contexts)
+    out_tok = (C.c_uint32 * B)()
+    out_ok = (C.c_uint8 * B)()
+
+    def step():
+        ok = R["runner_forward_batch"](runner, B, ids, tokens, positions, out_tok, out_ok)
+        assert ok and all(out_ok[i] for i in range(B)), "decode step failed"
+        for i in range(B):
+            tokens[i] = out_tok[i]
+            positions[i] += 1
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    sampler = ClockSampler(gpu_id(torch, dev))
+    sampler.start()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    device_ms = []
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+        device_ms.append(R["runner_last_step_ms"](runner))
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    launches = R["runner_last_launches"](runner)
+    dev_ms = sum(device_ms)
+
+    # Dominant-kernel roofline: replay the attention of one step (all 22 layers,
+    # same work list) and time it with CUDA events on the launching stream.
+    roof = attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr)
+
+    t = torch.tensor([dev_ms, e2e_ms], device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    dev_ms, e2e_ms = float(t[0]), float(t[1])
+    R["runner_destroy"](runner)
+    R["backend_destroy"](backend)
+    if dist is not None:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    tokens_total = B * args.steps * world
+    line = {
+        "metric": METRIC,
+        "value": round(tokens_total / (dev_ms / 1e3), 1),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dev_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "fp16",
+        "data": "synthetic (random-init TinyLlama-shape weights, seeded contexts and KV)",
+        "config": {
+            "workload": wl["name"],
+            "model": "TinyLlama-1.1B shape (22 layers, hidden 2048, 32q/4kv heads, vocab 32000)",
+            "global_batch": B * world,
+            "batch_per_gpu": B,
+            "ctx_mean": round(sum(contexts) / len(contexts), 1),
+            "parallelism": f"replicas x{world}",
+            "l2": "inputs larger than L2 every step (2.07 GB weights + paged KV)",
+            "cuda_graphs": True,
+        },
+        "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": h2d_bytes(B, contexts), "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": launches * args.steps,
+        "roofline": roof,
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline(kk, synth, cfg, contexts, manifest, args)
+    return line
+
+
+def h2d_bytes(B, contexts):
+    """Per-step upload of the fused step: counts, tokens, positions, write slots,
+    copies, lanes, work list and page descriptors (entries of every lane)."""
+    entries = sum(c // 64 + math.ceil((c % 64 + 1) / 8) for c in contexts)
+    items = sum(max(1, math.ceil((c + 1) / 256)) for c in contexts)
+    return 16 + B * (4 + 4 + 8 + 12 + 32) + items * 16 + entries * 16
+
+
+def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr):
+    import torch
+    hq, D, L = cfg["q_heads"], cfg["head_dim"], cfg["layers"]
+    # Current block tables of all lanes (committed prefix = what attention reads).
+    descs_list, lanes = [], (kk.AttnLane * B)()
+    buf = (kk.KkEntry * 8192)()
+    for b in range(B):
+        t = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 8192, 0, 0)
+        assert R["backend_block_table"](backend, b + 1, C.byref(t))
+        lanes[b].desc_offset = len(descs_list)
+        lanes[b].desc_count = t.count
+        lanes[b].token_count = sum(buf[i].valid_tokens for i in range(t.count))
+        lanes[b].query_row = b
+        for i in range(t.count):
+            e = buf[i]
+            descs_list.append(kk.PageDesc(e.slot, e.logical_token_begin, e.valid_tokens, e.kind, 0, 0))
+    descs = (kk.PageDesc * len(descs_list))(*descs_list)
+    items = (kk.AttnItem * 16384)()
+    n_items = K["attention_plan"](descs, lanes, B, 256, items, 16384)
+    tokens = sum(lanes[b].token_count for b in range(B))
+    to_dev = lambda arr: torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+    d_descs, d_lanes, d_items = to_dev(descs), to_dev(lanes), to_dev(items)
+    q = torch.randn(B, hq * D, device="cuda").half() / 8
+    out = torch.empty_like(q)
+    ws_b = K["attention_workspace_bytes"](B, n_items, hq, D)
+    ws = torch.zeros(ws_b, dtype=torch.uint8, device="cuda")
+
+    def launch_all():
+        for layer in range(L):
+            rc = K["paged_decode_attention"](C.byref(pools), layer, hq, d_descs.data_ptr(),
+                                             d_lanes.data_ptr(), B, d_items.data_ptr(), n_items,
+                                             q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125,
+                                             ws.data_ptr(), ws_b, sptr)
+            assert rc == 0
+    for _ in range(3):
+        launch_all()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record(stream)
+    for _ in range(reps):
+        launch_all()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    avg_ms = e0.elapsed_time(e1) / (reps * L)
+    bytes_per_launch = tokens * cfg["kv_heads"] * D * 2 * 2  # K and V of every attended token
+    peak, peak_note = measured_peaks()
+    achieved = bytes_per_launch / (avg_ms / 1e3) / 1e9
+    return {"kernel": "paged_decode_attention_kernel (K1), one layer, all lanes",
+            "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_note,
+            "algorithmic_bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 2),
+            "traffic": None}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle baseline / reference arm
+
+
+def cpu_model(synth, cfg, threads):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import kk_oracle_py as ko
+    archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
+    _, _, weights = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31), keep_weights=True)
+    return ko, ko.Model(cfg, weights, threads=threads)
+
+
+def cpu_decode_sample(ko, model, cfg, contexts, lanes, steps):
+    import numpy as np
+    L, row = cfg["layers"], cfg["kv_heads"] * cfg["head_dim"]
+    rng = np.random.default_rng(5)
+    for b in range(lanes):
+        model.create(b + 1)
+        ctx = contexts[b]
+        k = (rng.uniform(-0.35, 0.35, (ctx, L, row))).astype(np.float16).view(np.uint16)
+        v = (rng.uniform(-0.35, 0.35, (ctx, L, row))).astype(np.float16).view(np.uint16)
+        model.append_kv(b + 1, k, v)
+    toks = [3 + b for b in range(lanes)]
+    pos = list(contexts[:lanes])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        greedy, _, _ = model.forward(list(range(1, lanes + 1)), toks, pos, want_logits=False,
+                                     want_hidden=False)
+        toks = [int(x) for x in greedy]
+        pos = [p + 1 for p in pos]
+    dt = time.perf_counter() - t0
+    return lanes * steps / dt, dt
+
+
+def cpu_baseline(kk, synth, cfg, contexts, manifest, args):
+    threads = os.cpu_count() or 1
+    ko, model = cpu_model(synth, cfg, threads)
+    lanes, steps = min(4, len(contexts)), 1
+    rate, dt = cpu_decode_sample(ko, model, cfg, contexts, lanes, steps)
+    model.close()
+    return {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": f"{lanes} lanes x {steps} decode step(s) of the same workload "
+                      f"(contexts {contexts[:lanes]}), C oracle, {dt:.1f} s"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    wl = workload(args.config, 0)
+    cfg = dict(synth.TINYLLAMA)
+    cfg["max_positions"] = max(4608, max(wl["contexts"]) + args.steps + args.warmup + 8)
+    threads = os.cpu_count() or 1
+    ko, model = cpu_model(synth, cfg, threads)
+    lanes = min(2, wl["batch"])
+    total_tok, total_t = 0, 0.0
+    for i in range(args.warmup + args.steps):
+        if i == args.warmup:
+            total_tok, total_t = 0, 0.0
+        rate, dt = cpu_decode_sample(ko, model, cfg, wl["contexts"][2 * (i % 2):], lanes, 1)
+        for b in range(lanes):
+            model.release(b + 1)
+        total_tok += lanes
+        total_t += dt
+    model.close()
+    value = total_tok / total_t
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_t / max(args.steps, 1) * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": wl["name"] + f" (bounded sample: {lanes} lanes per step)"},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads,
+                             "kind": "port",
+                             "sample": f"{lanes} lanes x 1 decode step per timed step, "
+                                       "C restatement of the reference FP16 decoder"},
+            "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
+        args, rank, world, local_rank)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -201,6 +201,9 @@ KK_API void kkrt_txn_attend_batch(void* const* txns, uint32_t n, uint32_t layer,
     uint64_t workspace_bytes, float scale, int* statuses);
 KK_API int kkrt_txn_commit(void* txn);
 KK_API int kkrt_txn_rollback(void* txn);
+/* Reserved block table of a transaction from this library's CUDA backend
+ * (committed prefix + the current token; TokenReservationResult::reserved). */
+KK_API int kkrt_txn_reserved_table(void* txn, kk_table_out* out);
 /* TokenTransactionPhase (engine_kv.h:210-218). */
 KK_API int kkrt_txn_phase(void* txn);
 KK_API void kkrt_txn_destroy(void* txn);   /* rolls back if still active */

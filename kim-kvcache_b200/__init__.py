@@ -295,6 +295,8 @@ KERNEL_SIGNATURES = {
     "residual_add": (_I, [_VP, _VP, _U64, _VP]),
     "argmax_workspace_bytes": (_U64, [_U32, _U32]),
     "gemm": (_I, [C.POINTER(GemmDesc), _VP]),
+    "kv_promote": (_I, [C.POINTER(KvPools), C.POINTER(_U32), _U32, _VP]),
+    "fill_fp16": (_I, [_VP, _U64, _U64, C.c_float, _VP]),
     "device_status": (_I, [_VP]),
     "set_pdl": (None, [_I]),
 }
@@ -354,6 +356,7 @@ RUNTIME_SIGNATURES = {
     "txn_attend_layer": (_I, [_VP, _U32, _VP, _VP, _VP, _U64, _F]),
     "txn_attend_batch": (None, [C.POINTER(_VP), _U32, _U32, _VP, _VP, _U64, _VP, _U64, _F,
                                 C.POINTER(_I)]),
+    "txn_reserved_table": (_I, [_VP, C.POINTER(KkTableOut)]),
     "txn_commit": (_I, [_VP]),
     "txn_rollback": (_I, [_VP]),
     "txn_phase": (_I, [_VP]),

@@ -247,6 +247,14 @@ void kkrt_txn_attend_batch(void* const* txns, uint32_t n, uint32_t layer, const 
     }
 }
 
+int kkrt_txn_reserved_table(void* t, kk_table_out* out)
+{
+    FusedLane lane{};
+    if (!fusedLane(*T(t), lane)) return 0;
+    tableOut(*lane.reserved, out);
+    return 1;
+}
+
 int kkrt_txn_commit(void* t) { return int(T(t)->commit().error); }
 int kkrt_txn_rollback(void* t) { return int(T(t)->rollback().error); }
 int kkrt_txn_phase(void* t) { return int(T(t)->snapshot().phase); }

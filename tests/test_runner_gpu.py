@@ -1,0 +1,314 @@
+"""End-to-end parity of the fused sm_100a decode step (runner + CUDA KV
+backend, through the C ABI) against the CPU oracle, the restatement of the
+reference's FP16-rounding decoder (tests/cuda/cuda_model_runner_test.cpp
+:213-457). Tolerances: hidden states and logits within
+2e-2 absolute; greedy tokens identical wherever the oracle's top-2 logit gap
+exceeds 2e-2; page tables and commit bookkeeping exact."""
+import ctypes as C
+import importlib.util
+import random
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import kk_oracle_py as ko
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+ROOT = Path(__file__).resolve().parent.parent
+TOL = 2e-2
+SMALL = dict(hidden=512, intermediate=1024, layers=3, q_heads=8, kv_heads=2, head_dim=64, vocab=1000,
+             max_positions=512, eps=1e-5, theta=10000.0, bos=1, eos=2)
+
+
+def synth():
+    spec = importlib.util.spec_from_file_location("kk_synth", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+class Stack:
+    """Backend + runner + oracle for one model config."""
+
+    def __init__(self, kk, tmp, cfg, seed=1, std=0.05, batch=8, graphs=1, micro=256, extent=16):
+        self.kk, self.cfg = kk, cfg
+        self.R = kk.runtime()
+        man, data, w = synth().write_archive(tmp, cfg, seed=seed, std=std, keep_weights=True)
+        self.stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+        self.backend = self.R["backend_create"](cfg["layers"], cfg["kv_heads"], cfg["head_dim"],
+                                                cfg["q_heads"], cfg["q_heads"] * cfg["max_positions"] * 4,
+                                                micro, extent)
+        st, det = C.c_int(0), C.create_string_buffer(256)
+        self.runner = self.R["runner_create"](man.encode(), data.encode(), self.backend, self.stream,
+                                              batch, graphs, 1, C.byref(st), det, 256)
+        assert self.runner, det.value.decode()
+        self.oracle = ko.Model(cfg, w, threads=8)
+
+    def close(self):
+        self.R["runner_destroy"](self.runner)
+        self.R["backend_destroy"](self.backend)
+        self.oracle.close()
+
+    def create(self, rid):
+        assert self.R["backend_create_request"](self.backend, rid) == 0
+        self.oracle.create(rid)
+
+    def batch(self, ids, toks, pos):
+        n = len(ids)
+        out, ok = (C.c_uint32 * n)(), (C.c_uint8 * n)()
+        assert self.R["runner_forward_batch"](self.runner, n, (C.c_uint64 * n)(*ids),
+                                              (C.c_uint32 * n)(*toks), (C.c_uint32 * n)(*pos), out, ok)
+        return [out[i] for i in range(n)], [ok[i] for i in range(n)]
+
+    def snapshot(self):
+        s = self.kk.BackendSnapshot()
+        self.R["backend_snapshot"](self.backend, C.byref(s))
+        return s
+
+
+def assert_greedy(got, want, logits):
+    for g, w, row in zip(got, want, logits):
+        top = np.sort(row)[-2:]
+        if top[1] - top[0] > TOL:
+            assert g == w, f"greedy {g} != oracle {w} (gap {top[1] - top[0]:.4f})"
+
+
+@pytest.mark.parametrize("graphs", [0, 1])
+def test_forward_token_logits_and_hidden_match_oracle(kk, tmp_path, graphs):
+    s = Stack(kk, tmp_path, SMALL, graphs=graphs)
+    s.create(41)
+    cfg = SMALL
+    for pos, tok in enumerate([1, 7, 999, 3, 500]):
+        logits = np.zeros(cfg["vocab"], np.float32)
+        emb = np.zeros(cfg["hidden"], np.uint16)
+        fin = np.zeros(cfg["hidden"], np.uint16)
+        layers = (C.c_uint32 * 2)(0, 2)
+        lh = np.zeros((2, cfg["hidden"]), np.uint16)
+        out = C.c_uint32(0)
+        rc = s.R["runner_forward_token"](s.runner, 41, tok, pos, C.byref(out), ko.ptr(logits, C.c_float),
+                                         ko.ptr(emb, C.c_uint16), ko.ptr(fin, C.c_uint16), layers, 2,
+                                         ko.ptr(lh, C.c_uint16))
+        assert rc == 0
+        want, ref_logits, ref_hidden = s.oracle.forward([41], [tok], [pos])
+        assert np.max(np.abs(logits - ref_logits[0])) < TOL
+        fh = fin.view(np.float16).astype(np.float32)
+        rh = ref_hidden[0].view(np.float16).astype(np.float32)
+        assert np.max(np.abs(fh - rh)) < TOL
+        assert_greedy([out.value], want, ref_logits)
+    snap = s.snapshot()
+    assert snap.committed_token_count == 5 and snap.active_transaction_count == 0
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
+def test_batched_decode_with_fork_and_partial_tail_cow(kk, tmp_path):
+    s = Stack(kk, tmp_path, SMALL)
+    rng = random.Random(3)
+    prompts = {1: [rng.randrange(3, 1000) for _ in range(13)], 2: [rng.randrange(3, 1000) for _ in range(6)],
+               3: [rng.randrange(3, 1000) for _ in range(21)]}
+    for rid in prompts:
+        s.create(rid)
+    pos, nxt = {r: 0 for r in prompts}, {}
+
+    def step(ids):
+        toks = [prompts[r][pos[r]] if pos[r] < len(prompts[r]) else nxt[r] for r in ids]
+        ps = [pos[r] for r in ids]
+        got, ok = s.batch(ids, toks, ps)
+        want, logits, _ = s.oracle.forward(ids, toks, ps, want_hidden=False)
+        assert all(ok)
+        assert_greedy(got, want, logits)
+        for i, r in enumerate(ids):
+            nxt[r] = int(want[i])
+            pos[r] += 1
+
+    for _ in range(11):
+        step([1, 2, 3])
+    # fork request 1 at 11 tokens (a partial 3-token tail page): both sides
+    # continue, each next write copies the shared tail first
+    assert s.R["backend_fork"](s.backend, 1, 9) == 0
+    s.oracle.fork(1, 9)
+    prompts[9], pos[9], nxt[9] = prompts[1], pos[1], nxt[1]
+    for _ in range(14):
+        step([1, 2, 3, 9])
+    tbl = (kk.KkEntry * 64)()
+    t = kk.KkTableOut(C.cast(tbl, C.POINTER(kk.KkEntry)), 64, 0, 0)
+    assert s.R["backend_block_table"](s.backend, 9, C.byref(t)) == 1
+    assert sum(tbl[i].valid_tokens for i in range(t.count)) == pos[9]
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    for rid in (1, 2, 3, 9):
+        assert s.R["backend_release"](s.backend, rid) == 0
+    assert s.snapshot().allocated_micro_pages == 0
+    s.close()
+
+
+def test_scheduler_end_to_end_matches_oracle_generation(kk, tmp_path):
+    s = Stack(kk, tmp_path, SMALL, batch=4)
+    rng = random.Random(8)
+    reqs = {rid: [rng.randrange(3, 1000) for _ in range(rng.randint(3, 40))] for rid in (1, 2, 3, 4, 5)}
+    sched = kk.Scheduler(s.R, s.backend, s.runner, 4, 16, 10 ** 6, 8)
+    for rid, prompt in reqs.items():
+        assert sched.submit(rid, prompt, 12) == 0
+    terms = {t["request_id"]: t for t in sched.drain()}
+    sched.close()
+    for rid, prompt in reqs.items():
+        s.oracle.create(100 + rid)
+        tok = None
+        for p, t in enumerate(prompt):
+            g, lg, _ = s.oracle.forward([100 + rid], [t], [p], want_hidden=False)
+            tok = int(g[0])
+        out = []
+        gaps_ok = True
+        for i in range(12):
+            out.append(tok)
+            if tok == SMALL["eos"] or i == 11:
+                break
+            g, lg, _ = s.oracle.forward([100 + rid], [tok], [len(prompt) + i], want_hidden=False)
+            top = np.sort(lg[0])[-2:]
+            gaps_ok = gaps_ok and top[1] - top[0] > TOL
+            tok = int(g[0])
+        got = terms[rid]["tokens"]
+        if gaps_ok:
+            assert got == out, f"request {rid}: {got} vs oracle {out}"
+        assert terms[rid]["error"] == 0
+    assert s.snapshot().request_count == 0
+    s.close()
+
+
+def test_injected_failures_roll_back_one_lane(kk, tmp_path):
+    s = Stack(kk, tmp_path, SMALL)
+    for rid in (1, 2):
+        s.create(rid)
+    got, ok = s.batch([1, 2], [5, 6], [0, 0])
+    assert ok == [1, 1]
+    assert s.R["backend_inject_failure"](s.backend, 0) == 1          # submission
+    got, ok = s.batch([1, 2], [7, 8], [1, 1])
+    assert sorted(ok) == [0, 1]
+    failed = [1, 2][ok.index(0)]
+    assert s.R["backend_inject_failure"](s.backend, 1) == 1          # completion
+    pos = {1: 2 if failed != 1 else 1, 2: 2 if failed != 2 else 1}
+    got, ok = s.batch([1, 2], [9, 9], [pos[1], pos[2]])
+    assert sorted(ok) == [0, 1]
+    assert s.snapshot().active_transaction_count == 0
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
+class _DevArray:
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<u2", "data": (ptr, False),
+                                         "version": 3}
+
+
+def dev_view(ptr, n):
+    """Zero-copy uint16 view of device memory owned by the library."""
+    return torch.as_tensor(_DevArray(ptr, n), device="cuda")
+
+
+def test_per_layer_spi_write_attend_matches_oracle(kk, tmp_path):
+    """The reference-facing per-layer transaction SPI (writeLayer / attendLayer /
+    attendLayerBatch, reference tests/cuda/cuda_engine_kv_backend_test.cpp:258-345)
+    on this backend, against the oracle's paged GQA attention over the
+    reserved table (prefix + the token just written)."""
+    R = kk.runtime()
+    L, hkv, D, hq = 2, 4, 64, 32
+    micro_cap, extent_cap = 128, 8
+    backend = R["backend_create"](L, hkv, D, hq, hq * 512 * 4, micro_cap, extent_cap)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    pools = kk.KvPools()
+    assert R["backend_pools"](backend, C.byref(pools))
+    row = hkv * D
+    micro = dev_view(pools.micro, micro_cap * L * 2 * 8 * row)
+    extent = dev_view(pools.extent, extent_cap * L * 2 * 64 * row)
+    K = kk.kernels()
+    K["fill_fp16"](C.c_void_p(pools.micro), micro.numel(), 5, 0.3, stream)
+    K["fill_fp16"](C.c_void_p(pools.extent), extent.numel(), 6, 0.3, stream)
+    g = torch.Generator().manual_seed(2)
+    lengths = {1: 0, 2: 70, 3: 131}
+    for rid, n in lengths.items():
+        assert R["backend_create_request"](backend, rid) == 0
+        if n:
+            assert R["backend_append"](backend, rid, n) == 0
+    R["backend_seal"](backend, 3)
+    assert R["backend_promote"](backend, 3, 0, stream) == 0
+    assert R["backend_promote"](backend, 3, 64, stream) == 0
+    assert R["backend_fork"](backend, 2, 4) == 0   # shared partial tail -> COW on next write
+    lengths[4] = 70
+    ids = [1, 2, 3, 4]
+    for step in range(3):
+        txns, st = [], C.c_int(0)
+        for rid in ids:
+            t = R["txn_reserve"](backend, rid, lengths[rid], stream, C.byref(st))
+            assert t and st.value == 0
+            txns.append(t)
+        tables = []
+        for t in txns:
+            buf = (kk.KkEntry * 64)()
+            tt = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 64, 0, 0)
+            assert R["txn_reserved_table"](t, C.byref(tt)) == 1
+            tables.append([(buf[j].slot, buf[j].logical_token_begin, buf[j].valid_tokens, buf[j].kind)
+                           for j in range(tt.count)])
+        q = (torch.randn(len(ids), hq * D, generator=g) / 8).half().cuda()
+        out = torch.zeros_like(q)
+        ws = torch.zeros(hq * 512 * 4, dtype=torch.uint8, device="cuda")
+        for layer in range(L):
+            for t in txns:
+                k = (torch.randn(row, generator=g) / 8).half().cuda()
+                v = (torch.randn(row, generator=g) / 8).half().cuda()
+                assert R["txn_write_layer"](t, layer, k.data_ptr(), v.data_ptr()) == 0
+            if step % 2 == 0:
+                statuses = (C.c_int * len(ids))()
+                R["txn_attend_batch"]((C.c_void_p * len(ids))(*txns), len(ids), layer, q.data_ptr(),
+                                      out.data_ptr(), hq * D * 2, ws.data_ptr(), ws.numel(), 0.125,
+                                      statuses)
+                assert list(statuses) == [0] * len(ids)
+            else:
+                for i, t in enumerate(txns):
+                    assert R["txn_attend_layer"](t, layer, q[i].data_ptr(), out[i].data_ptr(),
+                                                 ws.data_ptr(), ws.numel(), 0.125) == 0
+            torch.cuda.synchronize()
+            hm, he = micro.cpu().numpy(), extent.cpu().numpy()
+            for i in range(len(ids)):
+                ref = ko.paged_attention(hm, he, L, hkv, D, layer, hq, tables[i],
+                                         q[i].cpu().view(torch.int16).numpy().view(np.uint16))
+                got = out[i].cpu().float().numpy()
+                assert np.max(np.abs(got - ref.view(np.float16).astype(np.float32))) < TOL
+        for t in txns:
+            assert R["txn_commit"](t) == 0
+            R["txn_destroy"](t)
+        for rid in lengths:
+            lengths[rid] += 1
+    assert R["backend_check_invariants"](backend) == 1
+    snap = kk.BackendSnapshot()
+    R["backend_snapshot"](backend, C.byref(snap))
+    assert snap.batched_attention_submissions == 2 * L
+    R["backend_destroy"](backend)
+
+
+@pytest.mark.slow
+def test_tinyllama_shape_greedy_decode_config2(kk, tmp_path):
+    """TinyLlama-1.1B shape, batch 1, 6 seeded prompt ids
+    uniform in [3, 32000), 32 new tokens; greedy tokens vs the oracle."""
+    cfg = dict(synth().TINYLLAMA)
+    s = Stack(kk, tmp_path, cfg, seed=2, std=0.02, batch=1, micro=64, extent=4)
+    rng = random.Random(0x4B564341434845)
+    prompt = [rng.randrange(3, 32000) for _ in range(6)]
+    s.create(1)
+    tok, got, want_all = None, [], []
+    for p in range(6 + 31):
+        t = prompt[p] if p < 6 else tok
+        g, ok = s.batch([1], [t], [p])
+        w, logits, _ = s.oracle.forward([1], [t], [p], want_hidden=False)
+        assert ok == [1]
+        if p >= 5:
+            got.append(g[0])
+            want_all.append((int(w[0]), logits[0]))
+        tok = int(w[0])
+    mism = [(i, a, b) for i, (a, (b, lg)) in enumerate(zip(got, want_all))
+            if a != b and np.diff(np.sort(lg)[-2:])[0] > TOL]
+    assert not mism, mism
+    s.close()
