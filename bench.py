@@ -189,7 +189,10 @@ def run_ours(args, rank, world, local_rank):
 
     def step():
         ok = R["runner_forward_batch"](runner, B, ids, tokens, positions, out_tok, out_ok)
-        assert ok and all(out_ok[i] for i in range(B)), "decode step failed"
+        if not (ok and all(out_ok[i] for i in range(B))):
+            buf = C.create_string_buffer(512)
+            R["runner_last_error"](runner, buf, 512)
+            raise RuntimeError(f"decode step failed: {buf.value.decode()}")
         for i in range(B):
             tokens[i] = out_tok[i]
             positions[i] += 1

@@ -225,6 +225,8 @@ KK_API int kkrt_runner_forward_token(void* runner, uint64_t request_id, uint32_t
     uint16_t* final_hidden, const uint32_t* layers, uint32_t n_layers, uint16_t* layer_hidden);
 KK_API float kkrt_runner_last_step_ms(void* runner);
 KK_API uint32_t kkrt_runner_last_launches(void* runner);
+/* Detail text of the last failed fused step into out (NUL-terminated); returns its length. */
+KK_API uint32_t kkrt_runner_last_error(void* runner, char* out, uint32_t capacity);
 
 /* ---- generation loops (generation.h:178-202, iteration_scheduler.h:139-181) ---- */
 typedef struct kk_terminal {

@@ -329,6 +329,17 @@ float kkrt_runner_last_step_ms(void* r)
     return runner == nullptr ? 0.f : runner->lastStepDeviceMs();
 }
 
+uint32_t kkrt_runner_last_error(void* r, char* out, uint32_t cap)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    std::string const e = runner == nullptr ? std::string("not a CUDA runner") : runner->lastError();
+    if (out != nullptr && cap != 0) {
+        std::strncpy(out, e.c_str(), cap - 1);
+        out[cap - 1] = 0;
+    }
+    return static_cast<uint32_t>(e.size());
+}
+
 uint32_t kkrt_runner_last_launches(void* r)
 {
     auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));

@@ -558,6 +558,12 @@ GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
         rc = KK_EINVAL;
         return nullptr;
     }
+    cudaError_t const configured = plan->bn == 16 ? configure<16>()
+        : (plan->bn == 32 ? configure<32>() : configure<64>());
+    if (configured != cudaSuccess) {
+        rc = static_cast<int>(configured);
+        return nullptr;
+    }
     plan->tiles = (d.M + kBM - 1) / kBM;
     std::uint32_t split = d.split_k;
     if (split == 0) {

@@ -99,6 +99,10 @@ struct CudaTinyLlamaModelRunner::Impl {
 
     cudaEvent_t ev_begin{nullptr};
     cudaEvent_t ev_end{nullptr};
+    // Graphs are captured on this private stream (capture is not allowed on
+    // the legacy default stream a caller may pass) and replayed on `stream`.
+    cudaStream_t capture_stream{nullptr};
+    std::string last_error;
     float last_ms{0.f};
     std::uint32_t last_launches{0};
 
@@ -119,6 +123,7 @@ struct CudaTinyLlamaModelRunner::Impl {
         cudaFree(step_dev);
         cudaFreeHost(step_host);
         cudaFreeHost(host_tokens);
+        if (capture_stream != nullptr) cudaStreamDestroy(capture_stream);
         if (ev_begin != nullptr) cudaEventDestroy(ev_begin);
         if (ev_end != nullptr) cudaEventDestroy(ev_end);
     }
@@ -129,8 +134,8 @@ struct CudaTinyLlamaModelRunner::Impl {
     T* stepDev(std::size_t off) { return reinterpret_cast<T*>(step_dev + off); }
 
     CudaModelRunnerStatus buildPlans(std::uint32_t batch, BatchPlans& out);
-    CudaModelRunnerStatus enqueueForward(std::uint32_t batch, bool has_copies, BatchPlans const& p,
-        bool want_logits, ModelRunnerDebugCapture* debug);
+    CudaModelRunnerStatus enqueueForward(cudaStream_t on, std::uint32_t batch, bool has_copies,
+        BatchPlans const& p, bool want_logits, ModelRunnerDebugCapture* debug);
     CudaModelRunnerStatus runStep(std::uint32_t batch, bool has_copies, bool want_logits,
         ModelRunnerDebugCapture* debug);
 };
@@ -155,6 +160,7 @@ std::uint32_t CudaTinyLlamaModelRunner::generationMaxBatchSize() const noexcept
     return impl_->options.max_batch_size;
 }
 float CudaTinyLlamaModelRunner::lastStepDeviceMs() const noexcept { return impl_->last_ms; }
+std::string CudaTinyLlamaModelRunner::lastError() const { return impl_->last_error; }
 std::uint32_t CudaTinyLlamaModelRunner::lastStepLaunches() const noexcept { return impl_->last_launches; }
 
 CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t batch, BatchPlans& out)
@@ -217,8 +223,9 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
     return {};
 }
 
-CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(std::uint32_t batch,
-    bool has_copies, BatchPlans const& p, bool want_logits, ModelRunnerDebugCapture* debug)
+CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_t stream,
+    std::uint32_t batch, bool has_copies, BatchPlans const& p, bool want_logits,
+    ModelRunnerDebugCapture* debug)
 {
     TinyLlamaConfig const& c = cfg;
     std::uint32_t const H = c.hidden_size;
@@ -300,10 +307,11 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::runStep(std::uint32_t batc
         auto g = graphs.find(key);
         if (g == graphs.end()) {
             cudaGraph_t graph = nullptr;
-            cudaError_t e = cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal);
+            cudaError_t e = cudaStreamBeginCapture(capture_stream, cudaStreamCaptureModeThreadLocal);
             if (e == cudaSuccess) {
-                s = enqueueForward(batch, has_copies, found->second, false, nullptr);
-                e = cudaStreamEndCapture(stream, &graph);
+                s = enqueueForward(capture_stream, batch, has_copies, found->second, false, nullptr);
+                cudaError_t const ended = cudaStreamEndCapture(capture_stream, &graph);
+                e = s.ok() ? ended : cudaSuccess;
             }
             cudaGraphExec_t exec = nullptr;
             if (e == cudaSuccess && s.ok()) {
@@ -327,7 +335,7 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::runStep(std::uint32_t batc
             s = cudaFailure(static_cast<int>(e), "launch decode graph");
         }
     } else {
-        s = enqueueForward(batch, has_copies, found->second, want_logits, debug);
+        s = enqueueForward(stream, batch, has_copies, found->second, want_logits, debug);
     }
     kk_set_pdl(0);
     cudaEventRecord(ev_end, stream);
@@ -452,6 +460,9 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
             s = failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
                 std::string("decode step failed: ") + cudaGetErrorString(e));
         }
+    }
+    if (!s.ok()) {
+        im.last_error = s.detail;
     }
     if (s.ok()) {
         noteStreamCompleted(*im.kv, im.stream);
@@ -734,6 +745,9 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     }
     if (e == cudaSuccess) {
         e = cudaMallocHost(reinterpret_cast<void**>(&im->host_tokens), std::size_t(bmax) * 4);
+    }
+    if (e == cudaSuccess) {
+        e = cudaStreamCreateWithFlags(&im->capture_stream, cudaStreamNonBlocking);
     }
     if (e == cudaSuccess) {
         e = cudaEventCreate(&im->ev_begin);

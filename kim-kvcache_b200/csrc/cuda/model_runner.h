@@ -100,6 +100,8 @@ public:
 
     // Device time of the last fused step (ms, from CUDA events), 0 if unknown.
     [[nodiscard]] float lastStepDeviceMs() const noexcept;
+    // Detail of the last failed fused step (empty if none).
+    [[nodiscard]] std::string lastError() const;
     // Kernels launched by the last fused step.
     [[nodiscard]] std::uint32_t lastStepLaunches() const noexcept;
 

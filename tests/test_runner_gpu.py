@@ -63,6 +63,10 @@ class Stack:
         out, ok = (C.c_uint32 * n)(), (C.c_uint8 * n)()
         assert self.R["runner_forward_batch"](self.runner, n, (C.c_uint64 * n)(*ids),
                                               (C.c_uint32 * n)(*toks), (C.c_uint32 * n)(*pos), out, ok)
+        if not all(ok[i] for i in range(n)):
+            buf = C.create_string_buffer(512)
+            self.R["runner_last_error"](self.runner, buf, 512)
+            print("fused step failure:", buf.value.decode())
         return [out[i] for i in range(n)], [ok[i] for i in range(n)]
 
     def snapshot(self):
