@@ -411,6 +411,82 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_kernel_only(args):
+    """Small standalone cases of the hot kernels for profiling (no model):
+    attention = one layer of K1 over config-4 shaped paged tables (32 lanes,
+    ctx ~ U[1024, 4096], 22-layer pages so the pools exceed L2);
+    gemm = the gate/up projection shape (11264 x 2048, N = 32)."""
+    import torch
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    K = kk.kernels()
+    torch.cuda.set_device(0)
+    stream = torch.cuda.current_stream()
+    sptr = C.c_void_p(stream.cuda_stream)
+    if args.kernel_only == "gemm":
+        M, Kd, N = 11264, 2048, 32
+        w = (torch.randn(M, Kd, device="cuda") * 0.02).half()
+        x = torch.randn(64, Kd, device="cuda").half()
+        out = torch.empty(64, M // 2, device="cuda", dtype=torch.half)
+        d = kk.GemmDesc()
+        d.weight, d.M, d.K, d.x, d.N, d.x_stride, d.x_rows = w.data_ptr(), M, Kd, x.data_ptr(), N, Kd, 64
+        d.epilogue, d.out, d.out_stride = kk.EPI_SILU_PAIRS, out.data_ptr(), M // 2
+        launch = lambda: K["gemm"](C.byref(d), sptr)
+        nbytes = M * Kd * 2
+    else:
+        rng = random.Random(SEED)
+        contexts = [rng.randint(1024, 4096) for _ in range(32)]
+        L, hkv, D, hq = 22, 4, 64, 32
+        extent_cap = sum(c // 64 for c in contexts)
+        micro_cap = 32 * 8 + 8
+        row = hkv * D
+        micro = torch.empty(micro_cap * L * 2 * 8 * row, dtype=torch.int16, device="cuda")
+        extent = torch.empty(extent_cap * L * 2 * 64 * row, dtype=torch.int16, device="cuda")
+        K["fill_fp16"](C.c_void_p(micro.data_ptr()), micro.numel(), 1, 0.35, sptr)
+        K["fill_fp16"](C.c_void_p(extent.data_ptr()), extent.numel(), 2, 0.35, sptr)
+        pools = kk.KvPools(micro.data_ptr(), extent.data_ptr(), micro_cap, extent_cap, L, hkv, D, 0)
+        descs_list, lanes = [], (kk.AttnLane * 32)()
+        es, ms = list(range(extent_cap)), list(range(micro_cap))
+        rng.shuffle(es)
+        rng.shuffle(ms)
+        for b, ctx in enumerate(contexts):
+            lanes[b].desc_offset, lanes[b].query_row, lanes[b].token_count = len(descs_list), b, ctx
+            t = 0
+            while t + 64 <= ctx:
+                descs_list.append(kk.PageDesc(es.pop(), t, 64, 1, 0, 0))
+                t += 64
+            while t < ctx:
+                n = min(8, ctx - t)
+                descs_list.append(kk.PageDesc(ms.pop(), t, n, 0, 0, 0))
+                t += n
+            lanes[b].desc_count = len(descs_list) - lanes[b].desc_offset
+        descs = (kk.PageDesc * len(descs_list))(*descs_list)
+        items = (kk.AttnItem * 8192)()
+        n_items = K["attention_plan"](descs, lanes, 32, 256, items, 8192)
+        to_dev = lambda arr: torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
+        dd, dl, di = to_dev(descs), to_dev(lanes), to_dev(items)
+        q = (torch.randn(32, hq * D, device="cuda") / 8).half()
+        out = torch.empty_like(q)
+        ws_b = K["attention_workspace_bytes"](32, n_items, hq, D)
+        ws = torch.zeros(ws_b, dtype=torch.uint8, device="cuda")
+        launch = lambda: K["paged_decode_attention"](
+            C.byref(pools), 7, hq, dd.data_ptr(), dl.data_ptr(), 32, di.data_ptr(), n_items,
+            q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125, ws.data_ptr(), ws_b, sptr)
+        nbytes = sum(contexts) * row * 2 * 2
+    for _ in range(args.warmup):
+        assert launch() == 0
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        assert launch() == 0
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    peak, _ = measured_peaks()
+    print(json.dumps({"kernel": args.kernel_only, "avg_us": round(us, 2), "bytes": nbytes,
+                      "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 4)}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -419,11 +495,16 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", choices=["attention", "gemm"], default=None,
+                    help="time one hot kernel on a standalone case (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.kernel_only:
+        run_kernel_only(args)
+        return
     line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
         args, rank, world, local_rank)
     if line is not None:

@@ -154,7 +154,7 @@ def test_scheduler_end_to_end_matches_oracle_generation(kk, tmp_path):
     s = Stack(kk, tmp_path, SMALL, batch=4)
     rng = random.Random(8)
     reqs = {rid: [rng.randrange(3, 1000) for _ in range(rng.randint(3, 40))] for rid in (1, 2, 3, 4, 5)}
-    sched = kk.Scheduler(s.R, s.backend, s.runner, 4, 16, 10 ** 6, 8)
+    sched = kk.Scheduler(s.R, s.backend, s.runner, 8, 16, 10 ** 6, 8)
     for rid, prompt in reqs.items():
         assert sched.submit(rid, prompt, 12) == 0
     terms = {t["request_id"]: t for t in sched.drain()}
