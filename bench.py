@@ -411,28 +411,64 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+GEMM_SHAPES = {  # name: (M, K, epilogue) of the TinyLlama projections at N = 32
+    "qkv": (2560, 2048, "f16"), "o": (2048, 2048, "f16"), "gu": (11264, 2048, "silu"),
+    "down": (2048, 5632, "f16"), "lm": (32000, 2048, "f32"),
+}
+
+
 def run_kernel_only(args):
     """Small standalone cases of the hot kernels for profiling (no model):
     attention = one layer of K1 over config-4 shaped paged tables (32 lanes,
     ctx ~ U[1024, 4096], 22-layer pages so the pools exceed L2);
-    gemm = the gate/up projection shape (11264 x 2048, N = 32)."""
+    gemm = one projection shape (--shape) at N = 32, cycling through enough
+    weight copies that every launch streams its weights from HBM."""
     import torch
     kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
     K = kk.kernels()
     torch.cuda.set_device(0)
     stream = torch.cuda.current_stream()
     sptr = C.c_void_p(stream.cuda_stream)
+    label = {"kernel": args.kernel_only}
     if args.kernel_only == "gemm":
-        M, Kd, N = 11264, 2048, 32
-        w = (torch.randn(M, Kd, device="cuda") * 0.02).half()
-        x = torch.randn(64, Kd, device="cuda").half()
-        out = torch.empty(64, M // 2, device="cuda", dtype=torch.half)
-        d = kk.GemmDesc()
-        d.weight, d.M, d.K, d.x, d.N, d.x_stride, d.x_rows = w.data_ptr(), M, Kd, x.data_ptr(), N, Kd, 64
-        d.epilogue, d.out, d.out_stride = kk.EPI_SILU_PAIRS, out.data_ptr(), M // 2
-        launch = lambda: K["gemm"](C.byref(d), sptr)
+        M, Kd, epi = GEMM_SHAPES[args.shape]
+        N = 32
+        packed = args.layout == "packed"
         nbytes = M * Kd * 2
+        copies = max(2, -(-256 * 2**20 // nbytes))
+        x = torch.randn(64, Kd, device="cuda").half()
+        out = torch.empty(64, M, device="cuda", dtype=torch.float32)
+        descs = []
+        keep = []
+        for i in range(copies):
+            w = torch.empty(M * Kd, dtype=torch.int16, device="cuda")
+            K["fill_fp16"](C.c_void_p(w.data_ptr()), w.numel(), 10 + i, 0.02, sptr)
+            d = kk.GemmDesc()
+            if packed:
+                pk = torch.empty(K["gemm_packed_bytes"](M, Kd) // 2, dtype=torch.int16, device="cuda")
+                assert K["gemm_pack_weight"](w.data_ptr(), M, Kd, pk.data_ptr(), sptr) == 0
+                d.weight, d.weight_layout = pk.data_ptr(), kk.W_PACKED
+                keep.append(pk)
+                del w
+            else:
+                d.weight = w.data_ptr()
+                keep.append(w)
+            d.M, d.K, d.x, d.N, d.x_stride, d.x_rows = M, Kd, x.data_ptr(), N, Kd, 64
+            d.epilogue = {"f16": kk.EPI_STORE_F16, "silu": kk.EPI_SILU_PAIRS,
+                          "f32": kk.EPI_STORE_F32}[epi]
+            d.out, d.out_stride = out.data_ptr(), M // 2 if epi == "silu" else M
+            descs.append(d)
+        state = {"i": 0}
+
+        def launch():
+            d = descs[state["i"] % copies]
+            state["i"] += 1
+            return K["gemm"](C.byref(d), sptr)
+        label.update(shape=args.shape, layout=args.layout, M=M, K=Kd, N=N, weight_copies=copies)
     else:
+        variant = {"auto": kk.ATTN_AUTO, "direct": kk.ATTN_DIRECT, "tma": kk.ATTN_TMA}[args.variant]
+        assert K["attention_set_variant"](variant) == 0
+        label.update(variant=args.variant)
         rng = random.Random(SEED)
         contexts = [rng.randint(1024, 4096) for _ in range(32)]
         L, hkv, D, hq = 22, 4, 64, 32
@@ -461,17 +497,26 @@ def run_kernel_only(args):
             lanes[b].desc_count = len(descs_list) - lanes[b].desc_offset
         descs = (kk.PageDesc * len(descs_list))(*descs_list)
         items = (kk.AttnItem * 8192)()
-        n_items = K["attention_plan"](descs, lanes, 32, 256, items, 8192)
+        if args.plan == "balanced":
+            n_items = K["attention_plan_balanced"](descs, lanes, 32, torch.cuda.get_device_properties(0).multi_processor_count, items, 8192)
+        else:
+            n_items = K["attention_plan"](descs, lanes, 32, args.target_tokens, items, 8192)
         to_dev = lambda arr: torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
         dd, dl, di = to_dev(descs), to_dev(lanes), to_dev(items)
         q = (torch.randn(32, hq * D, device="cuda") / 8).half()
         out = torch.empty_like(q)
         ws_b = K["attention_workspace_bytes"](32, n_items, hq, D)
         ws = torch.zeros(ws_b, dtype=torch.uint8, device="cuda")
-        launch = lambda: K["paged_decode_attention"](
-            C.byref(pools), 7, hq, dd.data_ptr(), dl.data_ptr(), 32, di.data_ptr(), n_items,
-            q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125, ws.data_ptr(), ws_b, sptr)
+        state = {"i": 0}
+
+        def launch():
+            layer = state["i"] % L  # a different layer's K/V every launch: HBM, not L2
+            state["i"] += 1
+            return K["paged_decode_attention"](
+                C.byref(pools), layer, hq, dd.data_ptr(), dl.data_ptr(), 32, di.data_ptr(), n_items,
+                q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125, ws.data_ptr(), ws_b, sptr)
         nbytes = sum(contexts) * row * 2 * 2
+        label.update(items=n_items, plan=args.plan, target_tokens=args.target_tokens)
     for _ in range(args.warmup):
         assert launch() == 0
     torch.cuda.synchronize()
@@ -483,8 +528,10 @@ def run_kernel_only(args):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) / args.steps * 1e3
     peak, _ = measured_peaks()
-    print(json.dumps({"kernel": args.kernel_only, "avg_us": round(us, 2), "bytes": nbytes,
-                      "gbs": round(nbytes / us / 1e3, 1), "frac": round(nbytes / us / 1e3 / peak, 4)}))
+    assert K["device_status"](sptr) == 0
+    label.update(avg_us=round(us, 2), bytes=nbytes, gbs=round(nbytes / us / 1e3, 1),
+                 frac=round(nbytes / us / 1e3 / peak, 4))
+    print(json.dumps(label))
 
 
 def main():
@@ -497,6 +544,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", choices=["attention", "gemm"], default=None,
                     help="time one hot kernel on a standalone case (profiling)")
+    ap.add_argument("--shape", default="gu", choices=sorted(GEMM_SHAPES),
+                    help="--kernel-only gemm: projection shape")
+    ap.add_argument("--layout", default="packed", choices=["packed", "rowmajor"],
+                    help="--kernel-only gemm: weight layout")
+    ap.add_argument("--variant", default="auto", choices=["auto", "direct", "tma"],
+                    help="--kernel-only attention: kernel variant")
+    ap.add_argument("--target-tokens", type=int, default=256,
+                    help="--kernel-only attention: tokens per work item (--plan lane)")
+    ap.add_argument("--plan", default="balanced", choices=["balanced", "lane"],
+                    help="--kernel-only attention: one token-balanced run per SM, or per-lane items")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))

@@ -87,12 +87,16 @@ typedef struct kk_attn_lane {
     uint32_t reserved[2];
 } kk_attn_lane;
 
-/* A split-KV work item: a run of one lane's descriptors. */
+/* A split-KV work item: a run [desc_begin, desc_end) of the descriptor array.
+ * Items of kk_attention_plan lie inside one lane (flags 0); items of
+ * kk_attention_plan_balanced may continue from `lane` into the following
+ * lanes when their descriptors are contiguous (flags KK_ATTN_ITEM_MULTI_LANE). */
+#define KK_ATTN_ITEM_MULTI_LANE 1u
 typedef struct kk_attn_item {
-    uint32_t lane;
+    uint32_t lane;             /* first lane of the item */
     uint32_t desc_begin;
     uint32_t desc_end;
-    uint32_t reserved;
+    uint32_t reserved;         /* flags */
 } kk_attn_item;
 
 /* ---- K1: fused GQA paged decode attention ------------------------------------
@@ -104,6 +108,15 @@ typedef struct kk_attn_item {
  * query/output rows: [q_heads][head_dim] fp16 at row stride *_stride elements. */
 KK_KAPI uint32_t kk_attention_plan(const kk_page_desc* host_descs, kk_attn_lane* host_lanes,
     uint32_t num_lanes, uint32_t target_tokens, kk_attn_item* host_items, uint32_t max_items);
+/* Token-balanced plan (no counterpart in the reference): cuts the batch's
+ * token stream, lane after lane, into about num_parts runs of equal token
+ * count at page granularity (use the SM count: one run per SM). Runs may span
+ * lanes; a lane split across runs is combined by the split-KV combine. Fills
+ * item_offset/item_count of every lane; returns the item count (items beyond
+ * max_items are counted, not written). Served by the TMA kernel only. */
+KK_KAPI uint32_t kk_attention_plan_balanced(const kk_page_desc* host_descs,
+    kk_attn_lane* host_lanes, uint32_t num_lanes, uint32_t num_parts, kk_attn_item* host_items,
+    uint32_t max_items);
 KK_KAPI uint64_t kk_attention_workspace_bytes(uint32_t num_lanes, uint32_t num_items,
     uint32_t q_heads, uint32_t head_dim);
 /* Zero-fills the per-lane completion counters of a fresh workspace (once). */
@@ -113,6 +126,24 @@ KK_KAPI int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer,
     const kk_attn_item* items, uint32_t num_items, const uint16_t* query, uint32_t query_stride,
     uint16_t* output, uint32_t output_stride, float scale, void* workspace,
     uint64_t workspace_bytes, void* stream);
+
+/* Kernel used by kk_paged_decode_attention (process-wide; default AUTO). No
+ * counterpart in the reference (it has one attention implementation).
+ *  KK_ATTN_AUTO   : the TMA kernel where supported (kv_heads in {1,2,4,8},
+ *                   which is every shape the direct-load kernel serves);
+ *  KK_ATTN_DIRECT : always the direct-load kernel (warps load K/V rows into
+ *                   registers);
+ *  KK_ATTN_TMA    : always the TMA kernel (persistent, warp-specialised, K/V
+ *                   staged through a 5-stage shared-memory ring); calls it
+ *                   cannot serve return KK_EINVAL.
+ * The direct-load kernel rejects multi-lane items (device status
+ * kErrBadArgument = 3, items skipped).
+ * Both produce the same results within FP32 rounding of the softmax sums.
+ * Returns 0 or KK_EINVAL for an unknown value. */
+#define KK_ATTN_AUTO 0
+#define KK_ATTN_DIRECT 1
+#define KK_ATTN_TMA 2
+KK_KAPI int kk_attention_set_variant(int variant);
 
 /* ---- K2: batched KV append / copy-on-write -----------------------------------
  * kk_kv_write replaces launchWriteLayerToken (paged_decode_kernels.cu:65-99) and
@@ -196,7 +227,20 @@ typedef struct kk_gemm_desc {
     /* KK_EPI_ARGMAX */
     uint32_t* tokens;          /* [N] greedy ids */
     void* argmax_workspace;    /* kk_argmax_workspace_bytes(M, N) bytes, zeroed once */
+    uint32_t weight_layout;    /* KK_W_ROW_MAJOR, or KK_W_PACKED: weight holds
+                                  kk_gemm_pack_weight output for (M, K) */
 } kk_gemm_desc;
+
+#define KK_W_ROW_MAJOR 0
+#define KK_W_PACKED 1
+/* Weight packing (no counterpart in the reference, whose cuBLAS calls read the
+ * row-major tensors): W [M][K] row-major (K % 8 == 0, 16-byte aligned) ->
+ * 128x64 tiles of 16 KB, each contiguous and pre-swizzled, so that the GEMM
+ * streams one tile per untiled bulk copy. Rows and columns are zero-padded to
+ * multiples of 128 and 64. Done once at weight load. */
+KK_KAPI uint64_t kk_gemm_packed_bytes(uint32_t M, uint32_t K);
+KK_KAPI int kk_gemm_pack_weight(const uint16_t* weight, uint32_t M, uint32_t K,
+    uint16_t* packed, void* stream);
 
 KK_KAPI uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N);
 KK_KAPI int kk_gemm(const kk_gemm_desc* desc, void* stream);

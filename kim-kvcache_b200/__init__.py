@@ -231,6 +231,9 @@ class Manager:
 # ---- kernel C ABI (include/kk_kernels.h) ------------------------------------
 
 KK_EINVAL = 1000
+ATTN_AUTO, ATTN_DIRECT, ATTN_TMA = 0, 1, 2
+ATTN_ITEM_MULTI_LANE = 1
+W_ROW_MAJOR, W_PACKED = 0, 1
 EPI_STORE_F16, EPI_STORE_F32, EPI_RESIDUAL, EPI_SILU_PAIRS, EPI_QKV_ROPE, EPI_ARGMAX = range(6)
 
 
@@ -275,13 +278,16 @@ class GemmDesc(C.Structure):
                 ("split_k", C.c_uint32), ("positions", C.c_void_p), ("slots", C.c_void_p),
                 ("pools", KvPools), ("layer", C.c_uint32), ("q_rows", C.c_uint32),
                 ("kv_rows", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
-                ("tokens", C.c_void_p), ("argmax_workspace", C.c_void_p)]
+                ("tokens", C.c_void_p), ("argmax_workspace", C.c_void_p),
+                ("weight_layout", C.c_uint32)]
 
 
 _VP = C.c_void_p
 KERNEL_SIGNATURES = {
     "attention_plan": (_U32, [C.POINTER(PageDesc), C.POINTER(AttnLane), _U32, _U32,
                               C.POINTER(AttnItem), _U32]),
+    "attention_plan_balanced": (_U32, [C.POINTER(PageDesc), C.POINTER(AttnLane), _U32, _U32,
+                                       C.POINTER(AttnItem), _U32]),
     "attention_workspace_bytes": (_U64, [_U32, _U32, _U32, _U32]),
     "attention_workspace_init": (_I, [_VP, _U32, _VP]),
     "paged_decode_attention": (_I, [C.POINTER(KvPools), _U32, _U32, _VP, _VP, _U32, _VP, _U32,
@@ -295,10 +301,13 @@ KERNEL_SIGNATURES = {
     "residual_add": (_I, [_VP, _VP, _U64, _VP]),
     "argmax_workspace_bytes": (_U64, [_U32, _U32]),
     "gemm": (_I, [C.POINTER(GemmDesc), _VP]),
+    "gemm_packed_bytes": (_U64, [_U32, _U32]),
+    "gemm_pack_weight": (_I, [_VP, _U32, _U32, _VP, _VP]),
     "kv_promote": (_I, [C.POINTER(KvPools), C.POINTER(_U32), _U32, _VP]),
     "fill_fp16": (_I, [_VP, _U64, _U64, C.c_float, _VP]),
     "device_status": (_I, [_VP]),
     "set_pdl": (None, [_I]),
+    "attention_set_variant": (_I, [_I]),
 }
 
 _KERNELS = None

@@ -22,12 +22,16 @@
 #include "kernels_internal.h"
 #include "launch.cuh"
 
+#include <atomic>
 #include <cmath>
 #include <vector>
 
 namespace kk {
 
 __device__ unsigned int g_attn_status;
+
+// Kernel choice for kk_paged_decode_attention (KK_ATTN_*), process-wide.
+std::atomic<int> g_attention_variant{KK_ATTN_AUTO};
 
 namespace {
 
@@ -167,6 +171,7 @@ __device__ __forceinline__ std::uint32_t word(uint4 const (&w)[2], int i)
 
 __global__ void __launch_bounds__(kThreads, 1) paged_decode_attention_kernel(AttnArgs a)
 {
+    pdl_launch_dependents();  // dependents only prefetch weights before their own wait
     pdl_wait();
     __shared__ float s_m[kWarps][16];
     __shared__ float s_l[kWarps][16];
@@ -187,6 +192,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_attention_kernel(Att
         ? (*a.num_items_dev < a.num_items ? *a.num_items_dev : a.num_items) : a.num_items;
     for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
         kk_attn_item const item = a.items[it];
+        if (item.reserved & KK_ATTN_ITEM_MULTI_LANE) {
+            // Items that may span lanes are served by the TMA kernel only.
+            if (threadIdx.x == 0) {
+                atomicCAS(&g_attn_status, kErrNone, kErrBadArgument);
+            }
+            continue;
+        }
         kk_attn_lane const ln = a.lanes[item.lane];
 
         // Q rows quad and quad+8 of this head's GQA group, dims 16*c4 .. +15.
@@ -440,7 +452,7 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     const kk_attn_item* items, uint32_t num_items, std::uint32_t const* num_items_dev,
     const uint16_t* query, uint32_t query_stride,
     uint16_t* output, uint32_t output_stride, float scale, void* workspace,
-    uint64_t workspace_bytes, cudaStream_t stream)
+    uint64_t workspace_bytes, int variant, cudaStream_t stream)
 {
     using namespace kk;
     if (pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
@@ -488,8 +500,17 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     a.counters = reinterpret_cast<std::uint32_t*>(ws);
     ws += align256(std::uint64_t(num_lanes) * 4u);
     a.part_o = reinterpret_cast<float*>(ws);
-    ws += align256(std::uint64_t(num_items) * q_heads * kHeadDim * 4u);
+    ws += align256(2ull * num_items * q_heads * kHeadDim * 4u);
     a.part_ml = reinterpret_cast<float*>(ws);
+    bool const tma_ok = attentionTmaSupported(pools, q_heads);
+    if (variant == KK_ATTN_TMA && !tma_ok) {
+        return KK_EINVAL;
+    }
+    if (tma_ok && variant != KK_ATTN_DIRECT) {
+        return attentionTmaLaunch(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
+            num_items_dev, query, query_stride, output, output_stride, scale, a.counters, a.part_o,
+            a.part_ml, stream);
+    }
     unsigned const grid = num_items < unsigned(numSms()) ? num_items : unsigned(numSms());
     return static_cast<int>(launch(paged_decode_attention_kernel, dim3(grid), dim3(kThreads), 0,
         stream, 1, a));
@@ -530,13 +551,71 @@ uint32_t kk_attention_plan(const kk_page_desc* descs, kk_attn_lane* lanes, uint3
     return count;
 }
 
+uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lanes,
+    uint32_t num_lanes, uint32_t num_parts, kk_attn_item* items, uint32_t max_items)
+{
+    if (num_parts == 0) {
+        num_parts = 1;
+    }
+    std::uint64_t total = 0;
+    for (std::uint32_t b = 0; b < num_lanes; ++b) {
+        for (std::uint32_t e = lanes[b].desc_offset; e < lanes[b].desc_offset + lanes[b].desc_count; ++e) {
+            total += descs[e].valid_tokens;
+        }
+    }
+    std::uint64_t const per = total == 0 ? 1 : (total + num_parts - 1) / num_parts;
+    std::uint32_t count = 0;
+    kk_attn_item cur{};
+    bool open = false;
+    std::uint64_t acc = 0;
+    auto flush = [&]() {
+        if (open && count - 1 < max_items) {
+            items[count - 1] = cur;
+        }
+        open = false;
+    };
+    for (std::uint32_t b = 0; b < num_lanes; ++b) {
+        kk_attn_lane& ln = lanes[b];
+        ln.item_offset = count;
+        ln.item_count = 0;
+        std::uint32_t const end = ln.desc_offset + ln.desc_count;
+        // An item only continues into this lane when the descriptors are contiguous.
+        if (open && cur.desc_end != ln.desc_offset) {
+            flush();
+        }
+        for (std::uint32_t e = ln.desc_offset; e < end; ++e) {
+            if (!open) {
+                cur = kk_attn_item{b, e, e, KK_ATTN_ITEM_MULTI_LANE};
+                open = true;
+                acc = 0;
+                ++count;
+            }
+            if (ln.item_count == 0 || ln.item_offset + ln.item_count != count) {
+                if (ln.item_count == 0) {
+                    ln.item_offset = count - 1;
+                }
+                ++ln.item_count;
+            }
+            cur.desc_end = e + 1;
+            acc += descs[e].valid_tokens;
+            if (acc >= per) {
+                flush();
+            }
+        }
+    }
+    flush();
+    return count;
+}
+
 uint64_t kk_attention_workspace_bytes(uint32_t num_lanes, uint32_t num_items, uint32_t q_heads,
     uint32_t head_dim)
 {
     using kk::align256;
+    // Two partial slots per item: an item of kk_attention_plan_balanced may
+    // split both its first and its last lane.
     return align256(std::uint64_t(num_lanes) * 4u)
-        + align256(std::uint64_t(num_items) * q_heads * head_dim * 4u)
-        + align256(std::uint64_t(num_items) * q_heads * 2u * 4u);
+        + align256(2ull * num_items * q_heads * head_dim * 4u)
+        + align256(2ull * num_items * q_heads * 2u * 4u);
 }
 
 int kk_attention_workspace_init(void* workspace, uint32_t num_lanes, void* stream)
@@ -553,7 +632,16 @@ int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer, uint32_t
 {
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
         nullptr, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
-        static_cast<cudaStream_t>(stream));
+        kk::g_attention_variant.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
+}
+
+int kk_attention_set_variant(int variant)
+{
+    if (variant < KK_ATTN_AUTO || variant > KK_ATTN_TMA) {
+        return KK_EINVAL;
+    }
+    kk::g_attention_variant.store(variant, std::memory_order_relaxed);
+    return 0;
 }
 
 } // extern "C"
@@ -571,8 +659,12 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     if (num_items == nullptr) {
         return KK_EINVAL;
     }
+    // The runner plans with kk_attention_plan_balanced wherever the TMA kernel
+    // serves the shape, so the kernel choice here does not follow the
+    // process-wide variant switch.
+    int const variant = attentionTmaSupported(pools, q_heads) ? KK_ATTN_TMA : KK_ATTN_DIRECT;
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, max_items,
         num_items, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
-        stream);
+        variant, stream);
 }
 } // namespace kk

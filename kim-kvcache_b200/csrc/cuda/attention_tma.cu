@@ -1,0 +1,865 @@
+// K1 (TMA variant) — persistent, TMA-fed GQA paged decode attention for sm_100a.
+//
+// Same numerics as the direct-load kernel in attention.cu (one pass: QK^T,
+// online softmax in FP32, PV, split-KV with a last-CTA combine), organised so
+// that every SM streams K/V at close to the HBM read rate:
+//
+//  * Warp-specialised CTA of 288 threads, one per SM: warp 8 is the producer
+//    (the whole warp walks the descriptors in lock step, lane 0 issues the
+//    copies), warps 0-7 are consumers.
+//  * A stage holds Ts = min(64, 128 / kv_heads) tokens of every KV head, K
+//    then V, each laid out [kv_head][token][64 dims] with the 128-byte swizzle
+//    (32 KB per stage, 5 stages). An extent page fills a stage with ONE tensor
+//    load for K and one for V: the extent tensor map views the pool as
+//    [slot][layer*2+kv][kv_head][token][dim] (strides permuted, so the box
+//    lands head-major), box 64 dims x Ts tokens x kv_heads. A micro page
+//    occupies one 8-token group of a stage and is loaded per head.
+//  * Consumer warp w owns KV head w % kv_heads and the 16-token slice
+//    w / kv_heads of each stage; its GQA query heads are the rows of m16n8k16
+//    tiles (ldmatrix for K as the B operand of QK^T, ldmatrix.trans for V as
+//    the B operand of PV), conflict-free thanks to the swizzle.
+//  * Work items may span lanes (kk_attention_plan_balanced cuts the batch's
+//    token stream into one equal run per SM): a stage never mixes lanes, the
+//    producer flags the last stage of each lane segment, and consumers merge
+//    and store (or park a partial for the split combine) at that point, then
+//    continue with the next lane. A lane's segments use partial slots
+//    2*item (first lane of the item) and 2*item+1 (last lane).
+//  * Work lists (items, lanes, descriptors) are read before
+//    griddepcontrol.wait: under the runner's programmatic dependent launch
+//    they come from host copies that precede the whole step. K/V pages and
+//    queries are only touched after it.
+//  * Every wait is bounded and abort-aware, the consumers' own barrier
+//    included (an mbarrier, not a named barrier): a wait that runs out of
+//    time records kErrWaitTimeout and raises a CTA-wide abort flag, after
+//    which every wait returns at once and all warps run to the end.
+#include "../../../include/kk_kernels.h"
+#include "kernels_internal.h"
+#include "launch.cuh"
+
+#include <cmath>
+#include <mutex>
+#include <vector>
+
+namespace kk {
+
+__device__ unsigned int g_attn_tma_status;
+
+namespace {
+
+constexpr int kHeadDim = 64;
+constexpr int kConsumerWarps = 8;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+constexpr int kStages = 5;
+constexpr std::uint32_t kStageBytes = 32768;           // K 16 KB + V 16 KB
+constexpr std::uint32_t kRowBytes = kHeadDim * 2;      // one head x one token
+constexpr std::uint32_t kORow = kHeadDim + 4;          // padded merge row (floats)
+
+constexpr std::uint32_t kSegEnd = 1u;    // last stage of a lane segment
+constexpr std::uint32_t kItemEnd = 2u;   // last stage of the item
+
+struct StageMeta {
+    std::uint8_t valid[8];  // valid tokens of each 8-token group slot (0 = empty slot)
+    std::uint32_t lane;     // lane whose tokens the stage holds
+    std::uint32_t flags;    // kSegEnd | kItemEnd
+    std::uint32_t next_lane;  // lane of the item's next segment (kSegEnd without kItemEnd)
+    std::uint32_t pad[3];
+};
+
+struct TmaArgs {
+    std::uint32_t micro_slots;
+    std::uint32_t extent_slots;
+    std::uint32_t layer;
+    std::uint32_t kv_heads;
+    std::uint32_t group;          // query heads per KV head
+    std::uint32_t q_heads;
+    std::uint32_t ts;             // tokens per stage
+    std::uint32_t extent_per_head;  // 1: the extent map has per-head boxes (fallback)
+    kk_page_desc const* descs;
+    kk_attn_lane const* lanes;
+    std::uint32_t num_lanes;
+    kk_attn_item const* items;
+    std::uint32_t num_items;
+    std::uint32_t const* num_items_dev;
+    __half const* query;
+    std::uint32_t query_stride;
+    __half* output;
+    std::uint32_t output_stride;
+    float scale_log2;
+    std::uint32_t* counters;
+    float* part_o;
+    float* part_ml;
+};
+
+__device__ __forceinline__ void tma_load_5d(void* dst, CUtensorMap const* map, std::uint64_t* bar,
+    int c0, int c1, int c2, int c3, int c4)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(map)), "r"(smem_u32(bar)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(std::uint64_t* bar, std::uint32_t bytes)
+{
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(std::uint32_t addr, std::uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4_t(std::uint32_t addr, std::uint32_t (&r)[4])
+{
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], std::uint32_t a0, std::uint32_t a1,
+    std::uint32_t a2, std::uint32_t a3, std::uint32_t b0, std::uint32_t b1)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ std::uint32_t pack_half2(float lo, float hi)
+{
+    __half2 const h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<std::uint32_t const*>(&h);
+}
+
+// Bounded wait (suspending polls, wall-time limit) that also gives up as soon
+// as another warp raised the CTA's abort flag.
+__device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t phase,
+    int volatile* abort)
+{
+    if (mbar_try_wait_suspend(bar, phase)) {
+        return true;
+    }
+    std::uint64_t const t0 = global_ns();
+    for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+        if (mbar_try_wait_suspend(bar, phase)) {
+            return true;
+        }
+        if (*abort) {
+            return false;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+            break;
+        }
+    }
+    *abort = 1;
+    atomicCAS(&g_attn_tma_status, kErrNone, kErrWaitTimeout);
+    return false;
+}
+
+__device__ __forceinline__ void store_row8(__half* out, float const (&acc)[8], float inv)
+{
+    __align__(16) __half vals[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        vals[e] = __float2half_rn(acc[e] * inv);
+    }
+    *reinterpret_cast<uint4*>(out) = *reinterpret_cast<uint4 const*>(vals);
+}
+
+__device__ __forceinline__ std::uint32_t lane_desc_end(kk_attn_lane const& ln)
+{
+    return ln.desc_offset + ln.desc_count;
+}
+
+// Query rows quad and quad+8 of one KV head's GQA group, as m16n8k16 A fragments.
+__device__ __forceinline__ void load_query(TmaArgs const& a, std::uint32_t row, std::uint32_t head,
+    std::uint32_t quad, std::uint32_t c4, std::uint32_t (&qa)[4][2], std::uint32_t (&qb)[4][2])
+{
+    __half const* q = a.query + static_cast<std::uint64_t>(row) * a.query_stride
+        + static_cast<std::uint64_t>(head * a.group) * kHeadDim;
+#pragma unroll
+    for (int k16 = 0; k16 < 4; ++k16) {
+#pragma unroll
+        for (int hi = 0; hi < 2; ++hi) {
+            std::uint32_t const col = k16 * 16 + hi * 8 + c4 * 2;
+            qa[k16][hi] = quad < a.group
+                ? *reinterpret_cast<std::uint32_t const*>(q + quad * kHeadDim + col) : 0u;
+            qb[k16][hi] = quad + 8 < a.group
+                ? *reinterpret_cast<std::uint32_t const*>(q + (quad + 8) * kHeadDim + col) : 0u;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
+    const __grid_constant__ CUtensorMap tm_micro, const __grid_constant__ CUtensorMap tm_extent,
+    TmaArgs a)
+{
+    extern __shared__ std::uint8_t smem_raw[];
+    // The 128-byte swizzle pattern repeats every 1 KB: align the ring to 1 KB.
+    std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    std::uint8_t* ring = smem_raw + pad;
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(ring + kStages * kStageBytes);
+    std::uint64_t* empty = full + kStages;
+    StageMeta* meta = reinterpret_cast<StageMeta*>(empty + kStages);
+    float* s_m = reinterpret_cast<float*>(meta + kStages);    // [warp][16]
+    float* s_l = s_m + kConsumerWarps * 16;                    // [warp][16]
+    float* s_o = s_l + kConsumerWarps * 16;                    // [warp][16][kORow]
+    int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 16 * kORow);
+    int volatile* s_abort = s_last + 1;
+    // Barrier of the consumer threads (the producer never joins). An mbarrier
+    // rather than a named barrier, so that its waits are bounded too.
+    std::uint64_t* cbar = reinterpret_cast<std::uint64_t*>(s_last + 2);
+
+    std::uint32_t const warp = threadIdx.x / 32;
+    std::uint32_t const lane = threadIdx.x % 32;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kConsumerWarps);
+        }
+        mbar_init(cbar, kConsumerWarps * 32);
+        *s_abort = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();  // dependents only prefetch weights before their own wait
+    std::uint32_t num_items = a.num_items;
+    if (a.num_items_dev != nullptr && *a.num_items_dev < num_items) {
+        num_items = *a.num_items_dev;
+    }
+    std::uint32_t const Hkv = a.kv_heads;
+    std::uint32_t const Ts = a.ts;
+    std::uint32_t const groups_per_stage = Ts / 8u;
+    std::uint32_t const v_offset = Hkv * Ts * kRowBytes;  // V half of a stage
+
+    if (warp == kConsumerWarps) {
+        // ------------------------------ producer ------------------------------
+        if (lane == 0) {
+            prefetch_tensormap(&tm_micro);
+            prefetch_tensormap(&tm_extent);
+        }
+        bool waited = false;
+        std::uint32_t stage = 0;
+        for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
+            kk_attn_item const item = a.items[it];
+            std::uint32_t b = item.lane;
+            if (b >= a.num_lanes) {
+                if (lane == 0) {
+                    atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+                }
+                b = 0;
+            }
+            std::uint32_t seg_end = lane_desc_end(a.lanes[b]);
+            seg_end = seg_end < item.desc_end ? seg_end : item.desc_end;
+            // 32 descriptors at a time, one per lane, broadcast with shuffles.
+            std::uint32_t win = item.desc_begin;
+            std::uint32_t w_slot = 0, w_word = 0;
+            auto load_window = [&]() {
+                std::uint32_t const i = win + lane;
+                if (i < item.desc_end) {
+                    std::uint32_t const* d = reinterpret_cast<std::uint32_t const*>(a.descs + i);
+                    w_slot = d[0];
+                    w_word = d[2];
+                } else {
+                    w_slot = 0;
+                    w_word = 0;
+                }
+            };
+            load_window();
+            // Cursor over the segment's non-empty, in-bounds descriptors. A
+            // descriptor outside its pool or over its page capacity
+            // contributes nothing and is reported.
+            std::uint32_t e = item.desc_begin;
+            std::uint32_t vt = 0, tok = 0;
+            int slot = 0;
+            bool micro = true;
+            bool have = false;
+            auto seek = [&]() {
+                have = false;
+                for (; e < seg_end; ++e) {
+                    if (e >= win + 32u) {
+                        win += 32u;
+                        load_window();
+                    }
+                    std::uint32_t const j = e - win;
+                    std::uint32_t const d_slot = __shfl_sync(0xffffffffu, w_slot, j);
+                    std::uint32_t const d_word = __shfl_sync(0xffffffffu, w_word, j);
+                    std::uint32_t const valid = d_word & 0xffffu;
+                    bool const m = ((d_word >> 16) & 0xffu) == 0;
+                    bool const ok = (m ? d_slot < a.micro_slots : d_slot < a.extent_slots)
+                        && valid <= (m ? 8u : 64u);
+                    if (!ok) {
+                        if (lane == 0) {
+                            atomicCAS(&g_attn_tma_status, kErrNone, kErrBadDescriptor);
+                        }
+                        continue;
+                    }
+                    if (valid != 0) {
+                        vt = valid;
+                        tok = 0;
+                        slot = static_cast<int>(d_slot);
+                        micro = m;
+                        have = true;
+                        return;
+                    }
+                }
+            };
+            seek();
+            if (!waited) {
+                pdl_wait();  // K/V pages of this layer are written by the previous kernel
+                waited = true;
+            }
+            for (;;) {
+                std::uint32_t const s = stage % kStages;
+                bool const ready = stage < kStages
+                    || wait_or_abort(&empty[s], ((stage / kStages) - 1u) & 1u, s_abort);
+                if (!__all_sync(0xffffffffu, ready)) {
+                    return;
+                }
+                StageMeta m{};
+                m.lane = b;
+                std::uint8_t* base = ring + s * kStageBytes;
+                std::uint32_t const kv = a.layer * 2u;
+                std::uint32_t n = 0;
+                while (have && n < groups_per_stage) {
+                    if (!micro) {
+                        if (n != 0) {
+                            break;  // an extent chunk always starts a fresh stage
+                        }
+#pragma unroll
+                        for (std::uint32_t j = 0; j < 8; ++j) {
+                            std::uint32_t const first = tok + 8u * j;
+                            std::uint32_t const left = j < groups_per_stage && first < vt ? vt - first : 0u;
+                            m.valid[j] = static_cast<std::uint8_t>(left < 8u ? left : 8u);
+                        }
+                        if (lane == 0) {
+                            mbar_expect_tx(&full[s], 2u * Hkv * Ts * kRowBytes);
+                            if (a.extent_per_head == 0) {
+                                tma_load_5d(base, &tm_extent, &full[s], 0, static_cast<int>(tok), 0,
+                                    static_cast<int>(kv), slot);
+                                tma_load_5d(base + v_offset, &tm_extent, &full[s], 0, static_cast<int>(tok),
+                                    0, static_cast<int>(kv + 1), slot);
+                            } else {
+                                for (std::uint32_t h = 0; h < Hkv; ++h) {
+                                    std::uint8_t* dst = base + h * Ts * kRowBytes;
+                                    tma_load_5d(dst, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                        static_cast<int>(tok), static_cast<int>(kv), slot);
+                                    tma_load_5d(dst + v_offset, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                        static_cast<int>(tok), static_cast<int>(kv + 1), slot);
+                                }
+                            }
+                        }
+                        n = groups_per_stage;
+                        tok += Ts;
+                        if (tok >= vt) {
+                            ++e;
+                            seek();
+                        }
+                    } else {
+                        m.valid[n] = static_cast<std::uint8_t>(vt);
+                        if (lane == 0) {
+                            mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
+                            for (std::uint32_t h = 0; h < Hkv; ++h) {
+                                std::uint8_t* dst = base + (h * Ts + n * 8u) * kRowBytes;
+                                tma_load_5d(dst, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
+                                    static_cast<int>(kv), slot);
+                                tma_load_5d(dst + v_offset, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
+                                    static_cast<int>(kv + 1), slot);
+                            }
+                        }
+                        ++n;
+                        ++e;
+                        seek();
+                    }
+                }
+                bool item_done = false;
+                if (!have) {
+                    // This lane's segment is exhausted: the next one starts at
+                    // the next lane with descriptors (lanes are contiguous in
+                    // the descriptor array inside a multi-lane item).
+                    m.flags |= kSegEnd;
+                    e = seg_end;
+                    if (e >= item.desc_end) {
+                        m.flags |= kItemEnd;
+                        item_done = true;
+                    } else {
+                        std::uint32_t nb = b + 1;
+                        while (nb < a.num_lanes && a.lanes[nb].desc_count == 0) {
+                            ++nb;
+                        }
+                        if (nb >= a.num_lanes || a.lanes[nb].desc_offset != e) {
+                            if (lane == 0) {
+                                atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+                            }
+                            m.flags |= kItemEnd;
+                            item_done = true;
+                        } else {
+                            b = nb;
+                            m.next_lane = b;
+                            seg_end = lane_desc_end(a.lanes[b]);
+                            seg_end = seg_end < item.desc_end ? seg_end : item.desc_end;
+                        }
+                    }
+                }
+                if (lane == 0) {
+                    meta[s] = m;
+                    mbar_arrive(&full[s]);  // releases meta[s]; the phase ends when the bytes land
+                }
+                ++stage;
+                if (item_done) {
+                    break;
+                }
+                if (!have) {
+                    seek();
+                }
+            }
+        }
+        return;
+    }
+
+    // ------------------------------ consumers ------------------------------
+    std::uint32_t const quad = lane >> 2;
+    std::uint32_t const c4 = lane & 3;
+    std::uint32_t const head = warp % Hkv;
+    std::uint32_t const chunk = warp / Hkv;  // 16-token slice of each stage
+    bool const active = chunk * 16u < Ts;
+    std::uint32_t const warps_per_head = kConsumerWarps / Hkv;
+    std::uint32_t const G = a.group;
+    std::uint32_t const tid = threadIdx.x;  // 0 .. 255
+    float const kNegInf = -INFINITY;
+    std::uint32_t const ring_base = smem_u32(ring);
+    std::uint32_t const mi = lane >> 3;  // ldmatrix: which 8x8 matrix this lane addresses
+    std::uint32_t const r8 = lane & 7;
+    std::uint32_t stage = 0;
+    bool waited = false;
+    std::uint32_t cphase = 0;
+    auto consumer_sync = [&]() {
+        mbar_arrive(cbar);
+        wait_or_abort(cbar, cphase, s_abort);
+        cphase ^= 1u;
+    };
+
+    for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
+        kk_attn_item const item = a.items[it];
+        std::uint32_t b = item.lane < a.num_lanes ? item.lane : 0u;
+        kk_attn_lane ln = a.lanes[b];
+        if (!waited) {
+            pdl_wait();  // queries are written by the previous kernel
+            waited = true;
+        }
+        std::uint32_t qa[4][2], qb[4][2];
+        load_query(a, ln.query_row, head, quad, c4, qa, qb);
+        float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
+        float o[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        }
+        for (;;) {
+            std::uint32_t const s = stage % kStages;
+            if (*s_abort || !wait_or_abort(&full[s], (stage / kStages) & 1u, s_abort)) {
+                break;
+            }
+            StageMeta const m = meta[s];
+            std::uint32_t const v0 = active ? m.valid[2 * chunk] : 0u;
+            std::uint32_t const v1 = active ? m.valid[2 * chunk + 1] : 0u;
+            if (v0 + v1 != 0) {
+                std::uint32_t const kbase =
+                    ring_base + s * kStageBytes + (head * Ts + chunk * 16u) * kRowBytes;
+                std::uint32_t const vbase = kbase + v_offset;
+                // S = Q K^T over the slice's 16 tokens (two n8 tiles).
+                float s0[4] = {0.f, 0.f, 0.f, 0.f};
+                float s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (std::uint32_t k16 = 0; k16 < 4; ++k16) {
+                    std::uint32_t const row = (mi >> 1) * 8u + r8;
+                    std::uint32_t const ch = 2u * k16 + (mi & 1u);
+                    std::uint32_t kb[4];
+                    ldsm_x4(kbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), kb);
+                    mma16816(s0, qa[k16][0], qb[k16][0], qa[k16][1], qb[k16][1], kb[0], kb[1]);
+                    mma16816(s1, qa[k16][0], qb[k16][0], qa[k16][1], qb[k16][1], kb[2], kb[3]);
+                }
+                bool const t00 = 2 * c4 < v0, t01 = 2 * c4 + 1 < v0;
+                bool const t10 = 2 * c4 < v1, t11 = 2 * c4 + 1 < v1;
+                float x[2][4];
+                x[0][0] = t00 ? s0[0] * a.scale_log2 : kNegInf;
+                x[0][1] = t01 ? s0[1] * a.scale_log2 : kNegInf;
+                x[0][2] = t10 ? s1[0] * a.scale_log2 : kNegInf;
+                x[0][3] = t11 ? s1[1] * a.scale_log2 : kNegInf;
+                x[1][0] = t00 ? s0[2] * a.scale_log2 : kNegInf;
+                x[1][1] = t01 ? s0[3] * a.scale_log2 : kNegInf;
+                x[1][2] = t10 ? s1[2] * a.scale_log2 : kNegInf;
+                x[1][3] = t11 ? s1[3] * a.scale_log2 : kNegInf;
+                float p[2][4];
+                float alpha[2];
+#pragma unroll
+                for (int rr = 0; rr < 2; ++rr) {
+                    float& mrow = rr == 0 ? m0 : m1;
+                    float& lrow = rr == 0 ? l0 : l1;
+                    float mx = fmaxf(fmaxf(x[rr][0], x[rr][1]), fmaxf(x[rr][2], x[rr][3]));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    float const m_new = fmaxf(mrow, mx);
+                    float const m_use = m_new == kNegInf ? 0.f : m_new;
+                    alpha[rr] = exp2f(mrow - m_use);
+                    float sum = 0.f;
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        p[rr][t] = exp2f(x[rr][t] - m_use);
+                        sum += p[rr][t];
+                    }
+                    lrow = lrow * alpha[rr] + sum;
+                    mrow = m_new;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    o[j][0] *= alpha[0];
+                    o[j][1] *= alpha[0];
+                    o[j][2] *= alpha[1];
+                    o[j][3] *= alpha[1];
+                }
+                std::uint32_t const pa0 = pack_half2(p[0][0], p[0][1]);
+                std::uint32_t const pa1 = pack_half2(p[1][0], p[1][1]);
+                std::uint32_t const pa2 = pack_half2(p[0][2], p[0][3]);
+                std::uint32_t const pa3 = pack_half2(p[1][2], p[1][3]);
+                // V halves of masked tokens are zeroed as well: bytes past a
+                // page's valid tokens are never trusted (0 * NaN would be NaN).
+                std::uint32_t const mask0 = (t00 ? 0x0000ffffu : 0u) | (t01 ? 0xffff0000u : 0u);
+                std::uint32_t const mask1 = (t10 ? 0x0000ffffu : 0u) | (t11 ? 0xffff0000u : 0u);
+#pragma unroll
+                for (std::uint32_t jp = 0; jp < 4; ++jp) {
+                    std::uint32_t const row = (mi & 1u) * 8u + r8;
+                    std::uint32_t const ch = 2u * jp + (mi >> 1);
+                    std::uint32_t vb[4];
+                    ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), vb);
+                    mma16816(o[2 * jp], pa0, pa1, pa2, pa3, vb[0] & mask0, vb[1] & mask1);
+                    mma16816(o[2 * jp + 1], pa0, pa1, pa2, pa3, vb[2] & mask0, vb[3] & mask1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&empty[s]);
+            }
+            ++stage;
+            if ((m.flags & kSegEnd) == 0) {
+                continue;
+            }
+
+            // ---- end of lane b's segment: merge the warps of each KV head ----
+            l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+            l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+            if (c4 == 0) {
+                s_m[warp * 16 + quad] = m0;
+                s_l[warp * 16 + quad] = l0;
+                s_m[warp * 16 + quad + 8] = m1;
+                s_l[warp * 16 + quad + 8] = l1;
+            }
+            float* row0 = s_o + (warp * 16 + quad) * kORow;
+            float* row1 = s_o + (warp * 16 + quad + 8) * kORow;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                row0[j * 8 + 2 * c4] = o[j][0];
+                row0[j * 8 + 2 * c4 + 1] = o[j][1];
+                row1[j * 8 + 2 * c4] = o[j][2];
+                row1[j * 8 + 2 * c4 + 1] = o[j][3];
+            }
+            consumer_sync();
+            bool const split = ln.item_count > 1;
+            std::uint64_t const pslot = 2ull * it + (b == item.lane ? 0u : 1u);
+            for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
+                std::uint32_t const qh = idx / 8u;
+                std::uint32_t const d0 = (idx % 8u) * 8u;
+                std::uint32_t const h = qh / G;
+                std::uint32_t const g = qh % G;
+                float M = kNegInf;
+                for (std::uint32_t sub = 0; sub < warps_per_head; ++sub) {
+                    M = fmaxf(M, s_m[(sub * Hkv + h) * 16 + g]);
+                }
+                float const m_use = M == kNegInf ? 0.f : M;
+                float L = 0.f;
+                float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                for (std::uint32_t sub = 0; sub < warps_per_head; ++sub) {
+                    std::uint32_t const w = sub * Hkv + h;
+                    float const f = exp2f(s_m[w * 16 + g] - m_use);
+                    L += s_l[w * 16 + g] * f;
+                    float const* src = s_o + (w * 16 + g) * kORow + d0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        acc[e] += src[e] * f;
+                    }
+                }
+                if (!split) {
+                    store_row8(a.output + static_cast<std::uint64_t>(ln.query_row) * a.output_stride
+                            + qh * kHeadDim + d0, acc, 1.f / L);
+                } else {
+                    std::uint64_t const prow = pslot * a.q_heads + qh;
+                    float* po = a.part_o + prow * kHeadDim + d0;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        po[e] = acc[e];
+                    }
+                    if (d0 == 0) {
+                        a.part_ml[prow * 2] = M;
+                        a.part_ml[prow * 2 + 1] = L;
+                    }
+                }
+            }
+            if (split) {
+                __threadfence();
+                consumer_sync();
+                if (tid == 0) {
+                    std::uint32_t const done = atomicAdd(&a.counters[b], 1u);
+                    *s_last = done + 1 == ln.item_count;
+                }
+                consumer_sync();
+                if (*s_last) {
+                    __threadfence();
+                    for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
+                        std::uint32_t const qh = idx / 8u;
+                        std::uint32_t const d0 = (idx % 8u) * 8u;
+                        float M = kNegInf;
+                        for (std::uint32_t i = 0; i < ln.item_count; ++i) {
+                            std::uint32_t const j = ln.item_offset + i;
+                            std::uint64_t const sl = 2ull * j + (a.items[j].lane == b ? 0u : 1u);
+                            M = fmaxf(M, __ldcg(a.part_ml + (sl * a.q_heads + qh) * 2));
+                        }
+                        float const m_use = M == kNegInf ? 0.f : M;
+                        float L = 0.f;
+                        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+                        for (std::uint32_t i = 0; i < ln.item_count; ++i) {
+                            std::uint32_t const j = ln.item_offset + i;
+                            std::uint64_t const sl = 2ull * j + (a.items[j].lane == b ? 0u : 1u);
+                            std::uint64_t const prow = sl * a.q_heads + qh;
+                            float const f = exp2f(__ldcg(a.part_ml + prow * 2) - m_use);
+                            L += __ldcg(a.part_ml + prow * 2 + 1) * f;
+                            float const* po = a.part_o + prow * kHeadDim + d0;
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                acc[e] += __ldcg(po + e) * f;
+                            }
+                        }
+                        store_row8(a.output + static_cast<std::uint64_t>(ln.query_row) * a.output_stride
+                                + qh * kHeadDim + d0, acc, 1.f / L);
+                    }
+                    if (tid == 0) {
+                        a.counters[b] = 0;  // ready for the next launch
+                    }
+                }
+            }
+            consumer_sync();  // s_m / s_l / s_o / s_last are reused by the next segment
+            if (m.flags & kItemEnd) {
+                break;
+            }
+            // Next lane of this item.
+            b = m.next_lane < a.num_lanes ? m.next_lane : 0u;
+            ln = a.lanes[b];
+            load_query(a, ln.query_row, head, quad, c4, qa, qb);
+            m0 = kNegInf;
+            m1 = kNegInf;
+            l0 = 0.f;
+            l1 = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+            }
+        }
+        if (*s_abort) {
+            break;
+        }
+    }
+}
+
+constexpr std::size_t kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8
+    + kStages * sizeof(StageMeta) + 2 * kConsumerWarps * 16 * 4
+    + kConsumerWarps * 16 * kORow * 4 + 24;
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+    cuuint64_t const*, cuuint64_t const*, cuuint32_t const*, cuuint32_t const*,
+    CUtensorMapInterleave, CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encodeFn()
+{
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess
+            && q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+        }
+    });
+    return fn;
+}
+
+bool encode(CUtensorMap* map, void const* base, cuuint64_t const (&dims)[5],
+    cuuint64_t const (&strides)[4], cuuint32_t const (&box)[5])
+{
+    EncodeTiledFn const fn = encodeFn();
+    cuuint32_t const elem[5] = {1, 1, 1, 1, 1};
+    return fn != nullptr
+        && fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(base), dims, strides, box, elem,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE)
+        == CUDA_SUCCESS;
+}
+
+// Natural view [slot][layer*2+kv][token][kv_head][dim] of a pool of `cap`-token
+// pages, box = one head x box_tokens tokens.
+bool encodePerHead(CUtensorMap* map, void const* base, std::uint32_t pages, std::uint32_t cap,
+    std::uint32_t layers, std::uint32_t heads, std::uint32_t box_tokens)
+{
+    cuuint64_t const row = kRowBytes;
+    cuuint64_t const dims[5] = {kHeadDim, heads, cap, 2ull * layers, pages};
+    cuuint64_t const strides[4] = {row, row * heads, row * heads * cap, row * heads * cap * 2ull * layers};
+    cuuint32_t const box[5] = {kHeadDim, 1, box_tokens, 1, 1};
+    return encode(map, base, dims, strides, box);
+}
+
+// Head-major view [slot][layer*2+kv][kv_head][token][dim] of the extent pool
+// (token and head strides swapped), box = all heads x box_tokens tokens, so
+// that one load lands [head][token][dim] in shared memory.
+bool encodeHeadMajor(CUtensorMap* map, void const* base, std::uint32_t pages, std::uint32_t layers,
+    std::uint32_t heads, std::uint32_t box_tokens)
+{
+    cuuint64_t const row = kRowBytes;
+    cuuint64_t const dims[5] = {kHeadDim, 64, heads, 2ull * layers, pages};
+    cuuint64_t const strides[4] = {row * heads, row, row * heads * 64, row * heads * 64 * 2ull * layers};
+    cuuint32_t const box[5] = {kHeadDim, box_tokens, heads, 1, 1};
+    return encode(map, base, dims, strides, box);
+}
+
+struct PoolMaps {
+    kk_kv_pools pools;
+    int device;
+    CUtensorMap micro;
+    CUtensorMap extent;
+    bool extent_per_head;
+};
+
+std::uint32_t stageTokens(std::uint32_t kv_heads)
+{
+    std::uint32_t const t = 128u / kv_heads;
+    return t < 64u ? t : 64u;
+}
+
+// Tensor maps are encoded once per (device, pool set) and reused.
+bool poolMaps(kk_kv_pools const& p, PoolMaps& out)
+{
+    static std::mutex mutex;
+    static std::vector<PoolMaps> cache;
+    int device = 0;
+    cudaGetDevice(&device);
+    std::lock_guard<std::mutex> lock(mutex);
+    for (PoolMaps const& e : cache) {
+        if (e.device == device && e.pools.micro == p.micro && e.pools.extent == p.extent
+            && e.pools.micro_capacity == p.micro_capacity
+            && e.pools.extent_capacity == p.extent_capacity && e.pools.layers == p.layers
+            && e.pools.kv_heads == p.kv_heads) {
+            out = e;
+            return true;
+        }
+    }
+    PoolMaps e{p, device, {}, {}, false};
+    std::uint32_t const ts = stageTokens(p.kv_heads);
+    if (!encodePerHead(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+        return false;
+    }
+    if (p.extent == nullptr || p.extent_capacity == 0) {
+        // No descriptor can select the extent map (extent_slots is 0).
+        e.extent = e.micro;
+        e.extent_per_head = true;
+    } else if (encodeHeadMajor(&e.extent, p.extent, p.extent_capacity, p.layers, p.kv_heads, ts)) {
+        e.extent_per_head = false;
+    } else if (encodePerHead(&e.extent, p.extent, p.extent_capacity, 64, p.layers, p.kv_heads, ts)) {
+        e.extent_per_head = true;
+    } else {
+        return false;
+    }
+    if (cache.size() >= 64) {
+        cache.erase(cache.begin());
+    }
+    cache.push_back(e);
+    out = e;
+    return true;
+}
+
+int smCount()
+{
+    int device = 0;
+    int sms = 0;
+    cudaGetDevice(&device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms > 0 ? sms : 148;
+}
+
+} // namespace
+
+bool attentionTmaSupported(kk_kv_pools const* pools, std::uint32_t q_heads)
+{
+    return pools != nullptr && pools->head_dim == kHeadDim && pools->micro != nullptr
+        && pools->micro_capacity != 0
+        && (pools->kv_heads == 1 || pools->kv_heads == 2 || pools->kv_heads == 4 || pools->kv_heads == 8)
+        && q_heads % pools->kv_heads == 0 && q_heads / pools->kv_heads <= 16;
+}
+
+int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
+    std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
+    std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
+    cudaStream_t stream)
+{
+    PoolMaps maps{};
+    if (!poolMaps(*pools, maps)) {
+        return KK_EINVAL;
+    }
+    static cudaError_t const attr = cudaFuncSetAttribute(paged_attention_tma_kernel,
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (attr != cudaSuccess) {
+        return static_cast<int>(attr);
+    }
+    TmaArgs a{};
+    a.micro_slots = pools->micro_capacity;
+    a.extent_slots = pools->extent == nullptr ? 0 : pools->extent_capacity;
+    a.layer = layer;
+    a.kv_heads = pools->kv_heads;
+    a.group = q_heads / pools->kv_heads;
+    a.q_heads = q_heads;
+    a.ts = stageTokens(pools->kv_heads);
+    a.extent_per_head = maps.extent_per_head ? 1u : 0u;
+    a.descs = descs;
+    a.lanes = lanes;
+    a.num_lanes = num_lanes;
+    a.items = items;
+    a.num_items = num_items;
+    a.num_items_dev = num_items_dev;
+    a.query = reinterpret_cast<__half const*>(query);
+    a.query_stride = query_stride;
+    a.output = reinterpret_cast<__half*>(output);
+    a.output_stride = output_stride;
+    a.scale_log2 = scale * 1.4426950408889634f;
+    a.counters = counters;
+    a.part_o = part_o;
+    a.part_ml = part_ml;
+    static int const sms = smCount();
+    unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
+    return static_cast<int>(launch(paged_attention_tma_kernel, dim3(grid), dim3(kThreads),
+        kSmemBytes, stream, 1, maps.micro, maps.extent, a));
+}
+
+int attentionTmaStatus(cudaStream_t stream) { return readStatus(&g_attn_tma_status, stream); }
+
+} // namespace kk

@@ -24,7 +24,10 @@ enum DeviceError : unsigned int {
     kErrBadArgument = 3,
 };
 
-constexpr std::uint32_t kMaxWaitPolls = 1u << 24;  // with the backoff below: ~1-2 s at most
+// A wait gives up after this much wall time (read from %globaltimer) or this
+// many polls, whichever comes first.
+constexpr std::uint64_t kWaitLimitNs = 2000000000ull;
+constexpr std::uint32_t kMaxWaitPolls = 1u << 26;
 
 __device__ __forceinline__ std::uint32_t smem_u32(void const* p)
 {
@@ -79,17 +82,44 @@ __device__ __forceinline__ bool mbar_try_wait(std::uint64_t* bar, std::uint32_t 
     return done != 0;
 }
 
-// Bounded wait on an mbarrier phase: non-blocking polls, then polls with a
-// short sleep. Returns false (and records the error) when the budget runs out.
+__device__ __forceinline__ std::uint64_t global_ns()
+{
+    std::uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Potentially suspending test of an mbarrier phase: the thread sleeps in
+// hardware until the phase completes or a short system time limit passes,
+// instead of spinning through issue slots.
+__device__ __forceinline__ bool mbar_try_wait_suspend(std::uint64_t* bar, std::uint32_t phase)
+{
+    std::uint32_t done = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(phase)
+        : "memory");
+    return done != 0;
+}
+
+// Bounded wait on an mbarrier phase (suspending polls, limited by wall time
+// and poll count). Returns false, and records the error, when it gives up.
 __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, std::uint32_t phase,
     unsigned int* status)
 {
+    if (mbar_try_wait_suspend(bar, phase)) {
+        return true;
+    }
+    std::uint64_t const t0 = global_ns();
     for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
-        if (mbar_try_wait(bar, phase)) {
+        if (mbar_try_wait_suspend(bar, phase)) {
             return true;
         }
-        if (i >= 4096) {
-            __nanosleep(64);
+        if (global_ns() - t0 > kWaitLimitNs) {
+            break;
         }
     }
     if (status != nullptr) {
@@ -119,6 +149,19 @@ __device__ __forceinline__ void tma_load_2d_hint(void* dst, CUtensorMap const* m
         ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;"
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(map)), "r"(smem_u32(bar)),
         "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast): size and both addresses
+// must be multiples of 16 bytes.
+__device__ __forceinline__ void bulk_load_hint(void* dst, void const* src, std::uint32_t bytes,
+    std::uint64_t* bar, std::uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1], %2, [%3], %4;"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(src)), "r"(bytes),
+        "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 

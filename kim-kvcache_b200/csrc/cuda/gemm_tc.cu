@@ -7,12 +7,21 @@
 // follow them (RoPE, KV write, SwiGLU, residual add, argmax; src/cuda/model/
 // kernels.cu, src/cuda/attention/paged_decode_kernels.cu:65-99).
 //
+// Weights come in one of two layouts:
+//  * row-major [M][K]: 128x64 W tiles are fetched with 2-D TMA tensor loads
+//    (128 rows of 128 bytes, K*2 bytes apart);
+//  * packed (kk_gemm_pack_weight): every 128x64 tile is one contiguous 16 KB
+//    block, already in the 128-byte-swizzled K-major arrangement the MMA
+//    reads, and the K blocks of a row tile follow each other. A tile is then
+//    one 16 KB untiled bulk copy and a CTA's K range one sequential stream,
+//    which keeps DRAM pages open instead of touching 128 rows per tile.
+//
 // Structure of one CTA (128 threads):
-//  * warp 0 / lane 0 issues TMA loads of 128x64 W tiles and BNx64 X tiles
+//  * warp 0 / lane 0 issues the W tile loads and TMA loads of BNx64 X tiles
 //    (128-byte swizzle) into an NS-stage mbarrier ring; W tiles for the first
-//    stages are requested before griddepcontrol.wait, so under programmatic
-//    dependent launch the weight stream starts while the previous kernel is
-//    still finishing;
+//    stages are requested before griddepcontrol.wait, and every CTA triggers
+//    its dependents as soon as it starts, so under programmatic dependent
+//    launch the next kernel's weight stream starts while this one finishes;
 //  * warp 1 / lane 0 issues tcgen05.mma (M=128, N=BN, K=16, FP16 in, FP32
 //    accumulate in TMEM) and releases stages with tcgen05.commit;
 //  * all 4 warps drain TMEM with tcgen05.ld.
@@ -38,8 +47,15 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
-constexpr int kStages = 4;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
+constexpr std::size_t kCtaSmemBudget = 113 * 1024;   // two CTAs per SM
+
+// Ring depth: as many W+X stages as fit two CTAs per SM.
+template <int BN>
+constexpr int stagesFor()
+{
+    return static_cast<int>((kCtaSmemBudget - 2048) / (kTileWBytes + BN * 128));
+}
 
 struct EpiArgs {
     std::uint32_t kind;
@@ -68,6 +84,7 @@ struct EpiArgs {
 };
 
 struct GemmArgs {
+    std::uint8_t const* w_packed;   // packed weight tiles, or null for row-major + TMA
     std::uint32_t M;
     std::uint32_t K;
     std::uint32_t N;
@@ -90,7 +107,8 @@ constexpr std::uint32_t tmemCols()
 template <int BN>
 constexpr std::size_t smemBytes()
 {
-    return 1024 /* alignment slack */ + kStages * (kTileWBytes + BN * 128) + 1024 /* barriers + scratch */;
+    return 1024 /* alignment slack */ + stagesFor<BN>() * (kTileWBytes + BN * 128)
+        + 1024 /* barriers + scratch */;
 }
 
 template <int BN>
@@ -98,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
     GemmArgs args)
 {
+    constexpr int kStages = stagesFor<BN>();
     extern __shared__ std::uint8_t smem_raw[];
     std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     std::uint8_t* smem = smem_raw + pad;
@@ -140,16 +159,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     __syncthreads();
     tc_fence_after();
     std::uint32_t const tmem = *tmem_slot;
+    // Dependents may launch now: they only prefetch weights before their own
+    // griddepcontrol.wait, which returns once this grid has completed.
+    pdl_launch_dependents();
 
     if (warp == 0 && lane == 0) {
         // Producer. Weights never depend on the previous kernel: request them
         // before waiting for it; activations only after.
         std::uint32_t const pre = nk < kStages ? nk : kStages;
         std::uint64_t const policy = l2_policy_evict_first();
+        std::uint8_t const* wp = args.w_packed == nullptr ? nullptr
+            : args.w_packed + (std::uint64_t(m_tile) * args.kb_total + kb_begin) * kTileWBytes;
+        auto load_w = [&](std::uint32_t s, std::uint32_t i) {
+            if (wp != nullptr) {
+                bulk_load_hint(w_stage + s * kTileWBytes, wp + std::uint64_t(i) * kTileWBytes,
+                    kTileWBytes, &full[s], policy);
+            } else {
+                tma_load_2d_hint(w_stage + s * kTileWBytes, &tm_w, &full[s],
+                    static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
+            }
+        };
         for (std::uint32_t i = 0; i < pre; ++i) {
             mbar_arrive_expect_tx(&full[i], kStageBytes);
-            tma_load_2d_hint(w_stage + i * kTileWBytes, &tm_w, &full[i],
-                static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
+            load_w(i, i);
         }
         pdl_wait();
         for (std::uint32_t i = 0; i < pre; ++i) {
@@ -162,8 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 break;
             }
             mbar_arrive_expect_tx(&full[s], kStageBytes);
-            tma_load_2d_hint(w_stage + s * kTileWBytes, &tm_w, &full[s],
-                static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
+            load_w(s, i);
             tma_load_2d(x_stage + s * BN * 128, &tm_x, &full[s],
                 static_cast<int>((kb_begin + i) * kBK), 0);
         }
@@ -187,10 +218,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         }
         tc_commit(accum);
     }
+    // Lanes 1-31 of the producer and MMA warps park here (not in a polling
+    // loop) until their lane 0 has finished its role.
+    __syncwarp();
     pdl_wait();
     bool const have_acc = mbar_wait(accum, 0, &g_gemm_status);
     tc_fence_after();
-    pdl_launch_dependents();
 
     // TMEM -> this CTA's FP32 partial tile, column-major [BN][128] (aliases the
     // W stages: every MMA that read them has completed).
@@ -375,6 +408,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     }
 }
 
+// Packs W [M][K] (row-major, K % 8 == 0) into 128x64 tiles, tile (t, b) at
+// ((t * kb_total + b) * 16 KB): row r, 16-byte chunk c of the tile lands at
+// r * 128 + ((c ^ (r % 8)) * 16), the 128-byte swizzle the MMA descriptors
+// expect; rows >= M and columns >= K are zero. One thread per 16-byte chunk.
+__global__ void pack_weight_kernel(std::uint16_t const* __restrict__ w, std::uint32_t M,
+    std::uint32_t K, std::uint32_t kb_total, std::uint64_t chunks, uint4* __restrict__ out)
+{
+    std::uint64_t const i = std::uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= chunks) {
+        return;
+    }
+    std::uint64_t const block = i / 1024u;      // (tile, kb) block
+    std::uint32_t const within = static_cast<std::uint32_t>(i % 1024u);
+    std::uint32_t const r = within / 8u;
+    std::uint32_t const c = within % 8u;
+    std::uint64_t const t = block / kb_total;
+    std::uint32_t const b = static_cast<std::uint32_t>(block % kb_total);
+    std::uint64_t const row = t * kBM + r;
+    std::uint32_t const col = b * kBK + c * 8u;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < M && col < K) {
+        v = *reinterpret_cast<uint4 const*>(w + row * K + col);
+    }
+    out[block * 1024u + r * 8u + (c ^ (r & 7u))] = v;
+}
+
 // ---- host side ------------------------------------------------------------------
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -460,7 +519,12 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
         || (reinterpret_cast<std::uintptr_t>(d->x) & 15u) != 0) {
         return KK_EINVAL;
     }
+    if (d->weight_layout > KK_W_PACKED) {
+        return KK_EINVAL;
+    }
     args = GemmArgs{};
+    args.w_packed = d->weight_layout == KK_W_PACKED ? reinterpret_cast<std::uint8_t const*>(d->weight)
+                                                    : nullptr;
     args.M = d->M;
     args.K = d->K;
     args.N = d->N;
@@ -527,6 +591,29 @@ int runGemm(GemmPlan const& plan, cudaStream_t stream)
 
 extern "C" {
 
+uint64_t kk_gemm_packed_bytes(uint32_t M, uint32_t K)
+{
+    std::uint64_t const tiles = (std::uint64_t(M) + kk::kBM - 1) / kk::kBM;
+    std::uint64_t const kb = (std::uint64_t(K) + kk::kBK - 1) / kk::kBK;
+    return tiles * kb * kk::kTileWBytes;
+}
+
+int kk_gemm_pack_weight(const uint16_t* weight, uint32_t M, uint32_t K, uint16_t* packed,
+    void* stream)
+{
+    if (weight == nullptr || packed == nullptr || M == 0 || K == 0 || K % 8 != 0
+        || (reinterpret_cast<std::uintptr_t>(weight) & 15u) != 0
+        || (reinterpret_cast<std::uintptr_t>(packed) & 15u) != 0) {
+        return KK_EINVAL;
+    }
+    std::uint32_t const kb = (K + kk::kBK - 1) / kk::kBK;
+    std::uint64_t const chunks = kk_gemm_packed_bytes(M, K) / 16u;
+    std::uint64_t const blocks = (chunks + 255u) / 256u;
+    kk::pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        weight, M, K, kb, chunks, reinterpret_cast<uint4*>(packed));
+    return static_cast<int>(cudaGetLastError());
+}
+
 uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N)
 {
     std::uint64_t const tiles = (M + 127u) / 128u;
@@ -553,7 +640,7 @@ GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
         return nullptr;
     }
     plan->bn = d.N <= 16 ? 16 : (d.N <= 32 ? 32 : 64);
-    if (!makeMap(&plan->tm_w, d.weight, d.K, d.M, d.K, kBM)
+    if ((d.weight_layout == KK_W_ROW_MAJOR && !makeMap(&plan->tm_w, d.weight, d.K, d.M, d.K, kBM))
         || !makeMap(&plan->tm_x, d.x, d.K, d.x_rows, d.x_stride, static_cast<std::uint32_t>(plan->bn))) {
         rc = KK_EINVAL;
         return nullptr;

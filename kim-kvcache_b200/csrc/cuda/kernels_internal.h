@@ -22,6 +22,18 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
     cudaStream_t stream);
 
+// TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
+// KV heads, up to 16 query heads per KV head; serves both plan kinds
+// (kk_attention_plan and kk_attention_plan_balanced). Arguments are validated
+// by the caller; the workspace parts are as for the direct-load kernel.
+bool attentionTmaSupported(kk_kv_pools const* pools, std::uint32_t q_heads);
+int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
+    std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
+    std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
+    cudaStream_t stream);
+
 // kk_kv_copy_tokens with the copy count in device memory (<= max_copies).
 int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
     kk_kv_copy const* copies, std::uint32_t const* num_copies, std::uint32_t max_copies,

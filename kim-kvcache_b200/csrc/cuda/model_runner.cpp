@@ -36,13 +36,13 @@ CudaModelRunnerStatus kvFailure(EngineKvStatus s, std::string const& what)
         what + " failed: " + std::string(toString(s.error)));
 }
 
-constexpr std::uint32_t kAttentionTargetTokens = 256;
 
 std::size_t align256(std::size_t x) { return (x + 255) & ~std::size_t(255); }
 
 struct LayerWeights {
     std::uint16_t const* in_norm;
     std::uint16_t const* post_norm;
+    // Projection matrices, packed by kk_gemm_pack_weight (16 KB swizzled tiles).
     std::uint16_t const* w_qkv;   // [(Hq + 2 Hkv) D][H]: q rows, k rows, v rows
     std::uint16_t const* w_o;     // [H][H]
     std::uint16_t const* w_gu;    // [2 I][H]: row 2i = gate_i, row 2i+1 = up_i
@@ -66,7 +66,8 @@ struct CudaTinyLlamaModelRunner::Impl {
     CudaModelRunnerOptions options{};
     kk_kv_pools pools{};
 
-    std::uint8_t* weights{nullptr};
+    std::uint8_t* weights{nullptr};   // embedding table and norm weights (row-major)
+    std::uint8_t* packed{nullptr};    // projection matrices and LM head, packed tiles
     std::uint64_t weight_bytes{0};
     std::uint16_t const* embed{nullptr};
     std::uint16_t const* lm_head{nullptr};
@@ -90,6 +91,7 @@ struct CudaTinyLlamaModelRunner::Impl {
 
     // Step inputs: one region on the device, a pinned mirror on the host.
     std::uint32_t max_items{0};
+    std::uint32_t sm_count{148};
     std::uint32_t max_descs{0};
     std::size_t off_counts{0}, off_tokens{0}, off_positions{0}, off_slots{0}, off_copies{0},
         off_lanes{0}, off_items{0}, off_descs{0}, step_bytes{0};
@@ -119,6 +121,7 @@ struct CudaTinyLlamaModelRunner::Impl {
         }
         plans.clear();
         cudaFree(weights);
+        cudaFree(packed);
         cudaFree(ws);
         cudaFree(step_dev);
         cudaFreeHost(step_host);
@@ -185,6 +188,7 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         d.epilogue = epi;
         d.out = o;
         d.out_stride = ostride;
+        d.weight_layout = KK_W_PACKED;
         return d;
     };
     for (std::uint32_t l = 0; l < c.layer_count; ++l) {
@@ -430,7 +434,9 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
                 static_cast<std::uint8_t>(e.kind), 0, 0};
         }
     }
-    std::uint32_t const n_items = kk_attention_plan(descs, lanes, B, kAttentionTargetTokens,
+    // One token-balanced run per SM (the TMA attention kernel serves every
+    // shape this runner accepts).
+    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, B, im.sm_count,
         im.stepHost<kk_attn_item>(im.off_items), im.max_items);
     if (n_items > im.max_items) {
         result.success = false;
@@ -687,12 +693,87 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         }
     }
 
+    // Pack the projection matrices into 16 KB swizzled tiles (one allocation),
+    // move the embedding table and norm weights into a compact row-major
+    // allocation, and release the upload buffer.
+    {
+        struct PackJob {
+            std::uint16_t const* src;
+            std::uint32_t M, K;
+            std::uint16_t const** dst;
+        };
+        std::vector<PackJob> jobs;
+        jobs.push_back({im->lm_head, static_cast<std::uint32_t>(V), static_cast<std::uint32_t>(H), &im->lm_head});
+        for (LayerWeights& lw : im->layers) {
+            jobs.push_back({lw.w_qkv, static_cast<std::uint32_t>(qkv_rows), static_cast<std::uint32_t>(H), &lw.w_qkv});
+            jobs.push_back({lw.w_o, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(H), &lw.w_o});
+            jobs.push_back({lw.w_gu, static_cast<std::uint32_t>(2 * I), static_cast<std::uint32_t>(H), &lw.w_gu});
+            jobs.push_back({lw.w_down, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(I), &lw.w_down});
+        }
+        std::uint64_t packed_bytes = 0;
+        for (PackJob const& j : jobs) {
+            packed_bytes += kk_gemm_packed_bytes(j.M, j.K);
+        }
+        std::uint64_t const small_elems = pad(V * H) + pad(H) + 2 * c.layer_count * pad(H);
+        std::uint8_t* small = nullptr;
+        e = cudaMalloc(reinterpret_cast<void**>(&im->packed), packed_bytes);
+        if (e == cudaSuccess) {
+            e = cudaMalloc(reinterpret_cast<void**>(&small), small_elems * 2);
+        }
+        if (e != cudaSuccess) {
+            cudaFree(small);
+            out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "packed weight allocation");
+            return out;
+        }
+        std::uint64_t at = 0;
+        for (PackJob const& j : jobs) {
+            std::uint16_t* dst = reinterpret_cast<std::uint16_t*>(im->packed + at);
+            int const rc = kk_gemm_pack_weight(j.src, j.M, j.K, dst, nullptr);
+            if (rc != 0) {
+                cudaFree(small);
+                out.status = failure(CudaModelRunnerError::AllocationFailed, rc, "weight packing");
+                return out;
+            }
+            *j.dst = dst;
+            at += kk_gemm_packed_bytes(j.M, j.K);
+        }
+        std::uint16_t* s16 = reinterpret_cast<std::uint16_t*>(small);
+        std::uint64_t scur = 0;
+        auto move = [&](std::uint16_t const* src, std::uint64_t elems) {
+            std::uint16_t* d = s16 + scur;
+            scur += pad(elems);
+            cudaMemcpy(d, src, elems * 2, cudaMemcpyDeviceToDevice);
+            return d;
+        };
+        im->embed = move(im->embed, V * H);
+        im->final_norm = move(im->final_norm, H);
+        for (LayerWeights& lw : im->layers) {
+            lw.in_norm = move(lw.in_norm, H);
+            lw.post_norm = move(lw.post_norm, H);
+        }
+        e = cudaDeviceSynchronize();
+        cudaFree(im->weights);
+        im->weights = small;
+        im->weight_bytes = packed_bytes + small_elems * 2;
+        if (e != cudaSuccess) {
+            out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "weight packing");
+            return out;
+        }
+    }
+
     // Workspace.
     std::uint32_t const bmax = options.max_batch_size;
     im->bpad = std::max<std::uint32_t>(64, (bmax + 15) / 16 * 16);
     std::uint32_t const positions_cap = c.max_position_embeddings + 8;
     im->max_descs = bmax * (positions_cap / 8 + 2);
-    im->max_items = bmax * (positions_cap / kAttentionTargetTokens + 2) + positions_cap / 8;
+    {
+        int dev = 0;
+        int sms = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        im->sm_count = sms > 0 ? static_cast<std::uint32_t>(sms) : 148u;
+    }
+    im->max_items = im->sm_count + bmax + 8;
     std::size_t off = 0;
     auto region = [&](std::size_t bytes) {
         std::size_t const at = off;

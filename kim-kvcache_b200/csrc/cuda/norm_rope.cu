@@ -36,6 +36,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(__half const* x,
     __half const* embed, std::uint32_t const* tokens, __half const* weight, __half* hidden,
     __half* y, std::uint32_t cols, float eps)
 {
+    pdl_launch_dependents();  // dependents only prefetch weights before their own wait
     pdl_wait();
     __shared__ float scratch[kNormThreads / 32];
     std::uint32_t const row = blockIdx.x;

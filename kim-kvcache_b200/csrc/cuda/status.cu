@@ -7,6 +7,7 @@ namespace kk {
 thread_local bool g_pdl_enabled = false;
 
 int attentionStatus(cudaStream_t stream);
+int attentionTmaStatus(cudaStream_t stream);
 int pagesStatus(cudaStream_t stream);
 int gemmStatus(cudaStream_t stream);
 
@@ -17,7 +18,8 @@ extern "C" {
 int kk_device_status(void* stream)
 {
     cudaStream_t const s = static_cast<cudaStream_t>(stream);
-    int const codes[3] = {kk::attentionStatus(s), kk::pagesStatus(s), kk::gemmStatus(s)};
+    int const codes[4] = {kk::attentionStatus(s), kk::attentionTmaStatus(s), kk::pagesStatus(s),
+        kk::gemmStatus(s)};
     for (int c : codes) {
         if (c != 0) {
             return c;

@@ -1,0 +1,138 @@
+"""CPU checks of the C ABI: every function declared in include/*.h is exported
+by lib/libkk_b200.so, and the host-side attention planners
+(kk_attention_plan, kk_attention_plan_balanced) produce work lists that
+cover every page descriptor exactly once, in order, with consistent per-lane
+item ranges. No kernel is launched."""
+import ctypes as C
+import random
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    names = []
+    for header in sorted((ROOT / "include").glob("*.h")):
+        text = header.read_text()
+        for m in re.finditer(r"^(?:KK_KAPI|KK_API)\s+[\w\s\*]+?\b(\w+)\s*\(", text, re.M):
+            names.append((header.name, m.group(1)))
+    return names
+
+
+def test_every_declared_function_is_exported(kk_lib):
+    decl = declared_functions()
+    assert len(decl) > 60
+    missing = [f"{h}:{n}" for h, n in decl if not hasattr(kk_lib, n)]
+    assert not missing, missing
+
+
+def test_bindings_cover_the_kernel_header(kk):
+    names = {n for h, n in declared_functions() if h == "kk_kernels.h"}
+    bound = {"kk_" + k for k in kk.KERNEL_SIGNATURES}
+    assert names <= bound, sorted(names - bound)
+
+
+def make_tables(kk, contexts, seed):
+    rng = random.Random(seed)
+    descs, lanes = [], (kk.AttnLane * len(contexts))()
+    slot = 0
+    for b, ctx in enumerate(contexts):
+        lanes[b].desc_offset, lanes[b].query_row, lanes[b].token_count = len(descs), b, ctx
+        t = 0
+        while t + 64 <= ctx and rng.random() < 0.9:
+            descs.append(kk.PageDesc(slot, t, 64, 1, 0, 0))
+            slot += 1
+            t += 64
+        while t < ctx:
+            n = min(8, ctx - t)
+            descs.append(kk.PageDesc(slot, t, n, 0, 0, 0))
+            slot += 1
+            t += n
+        lanes[b].desc_count = len(descs) - lanes[b].desc_offset
+    arr = (kk.PageDesc * max(len(descs), 1))(*descs)
+    return arr, lanes, len(descs)
+
+
+def check_cover(kk, descs, lanes, items, n_items, multi_lane):
+    """Items tile the descriptor array in order; lane ranges match the items."""
+    nl = len(lanes)
+    pos = 0
+    touched = {b: [] for b in range(nl)}
+    for i in range(n_items):
+        it = items[i]
+        assert it.desc_begin == pos and it.desc_end > it.desc_begin
+        assert (it.reserved == kk.ATTN_ITEM_MULTI_LANE) == multi_lane
+        b = it.lane
+        e = it.desc_begin
+        while e < it.desc_end:
+            while lanes[b].desc_offset + lanes[b].desc_count <= e:
+                b += 1
+                assert multi_lane, "per-lane items never cross a lane"
+            assert lanes[b].desc_offset <= e
+            if not touched[b] or touched[b][-1] != i:
+                touched[b].append(i)
+            e += 1
+        pos = it.desc_end
+    assert pos == sum(lanes[b].desc_count for b in range(nl))
+    for b in range(nl):
+        got = list(range(lanes[b].item_offset, lanes[b].item_offset + lanes[b].item_count))
+        assert got == touched[b], (b, got, touched[b])
+
+
+@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.parametrize("parts", [1, 3, 7, 148, 5000])
+def test_balanced_plan_covers_and_balances(kk, seed, parts):
+    K = kk.kernels()
+    rng = random.Random(seed)
+    contexts = [rng.choice([0, 1, 7, 8, 9, 63, 64, 65, rng.randint(1, 4096)]) for _ in range(rng.randint(1, 40))]
+    descs, lanes, nd = make_tables(kk, contexts, seed)
+    items = (kk.AttnItem * 8192)()
+    n = K["attention_plan_balanced"](descs, lanes, len(contexts), parts, items, 8192)
+    total = sum(contexts)
+    if total == 0:
+        assert n == 0
+        return
+    check_cover(kk, descs, lanes, items, n, multi_lane=True)
+    per = -(-total // parts)
+    sizes = [sum(descs[e].valid_tokens for e in range(items[i].desc_begin, items[i].desc_end))
+             for i in range(n)]
+    # every cut is made as soon as the run reaches `per` tokens: no run exceeds
+    # per + one page, and all runs but the last reach `per`
+    assert max(sizes) < per + 64
+    assert all(s >= per for s in sizes[:-1])
+    assert n <= parts
+
+
+def test_balanced_plan_counts_items_beyond_capacity(kk):
+    K = kk.kernels()
+    descs, lanes, nd = make_tables(kk, [640, 640], 1)
+    items = (kk.AttnItem * 2)()
+    n = K["attention_plan_balanced"](descs, lanes, 2, 20, items, 2)
+    assert n == 20  # 1280 tokens in runs of 64
+    assert items[1].desc_begin == 1
+
+
+def test_balanced_plan_does_not_join_non_contiguous_lanes(kk):
+    K = kk.kernels()
+    descs = (kk.PageDesc * 4)(*[kk.PageDesc(i, 0, 8, 0, 0, 0) for i in range(4)])
+    lanes = (kk.AttnLane * 2)()
+    lanes[0].desc_offset, lanes[0].desc_count = 2, 2   # lane 0 uses descriptors 2, 3
+    lanes[1].desc_offset, lanes[1].desc_count = 0, 2   # lane 1 uses descriptors 0, 1
+    items = (kk.AttnItem * 8)()
+    n = K["attention_plan_balanced"](descs, lanes, 2, 1, items, 8)
+    assert n == 2
+    assert (items[0].lane, items[0].desc_begin, items[0].desc_end) == (0, 2, 4)
+    assert (items[1].lane, items[1].desc_begin, items[1].desc_end) == (1, 0, 2)
+
+
+@pytest.mark.parametrize("target", [8, 64, 256, 1000])
+def test_per_lane_plan_covers(kk, target):
+    K = kk.kernels()
+    contexts = [17, 100, 513, 2000, 0, 64, 4096]
+    descs, lanes, nd = make_tables(kk, contexts, 7)
+    items = (kk.AttnItem * 8192)()
+    n = K["attention_plan"](descs, lanes, len(contexts), target, items, 8192)
+    check_cover(kk, descs, lanes, items, n, multi_lane=False)

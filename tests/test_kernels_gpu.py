@@ -22,14 +22,42 @@ def K(kk):
     return kk.kernels()
 
 
+@pytest.fixture
+def attn_variant(K):
+    """Selects the attention kernel for one test and restores AUTO after it."""
+    yield lambda v: K["attention_set_variant"](v) == 0 or pytest.fail("variant rejected")
+    K["attention_set_variant"](0)
+
+
 def sync_ok(K):
     torch.cuda.synchronize()
     assert K["device_status"](None) == 0
 
 
-def gemm(kk, K, w, x, epi, out=None, out_stride=0, split=0, **extra):
+@pytest.fixture(params=[0, 1], ids=["rowmajor", "packed"])
+def wlayout(request):
+    return request.param
+
+
+_PACKED = {}
+
+
+def packed_weight(kk, K, w):
+    """kk_gemm_pack_weight output for w (cached per tensor for the test's lifetime)."""
+    key = (w.data_ptr(), tuple(w.shape))
+    if key not in _PACKED or _PACKED[key][0] is not w:
+        buf = torch.empty(K["gemm_packed_bytes"](*w.shape) // 2, dtype=torch.half, device="cuda")
+        assert K["gemm_pack_weight"](p(w), w.shape[0], w.shape[1], p(buf), None) == 0
+        _PACKED.clear()
+        _PACKED[key] = (w, buf)
+    return _PACKED[key][1]
+
+
+def gemm(kk, K, w, x, epi, out=None, out_stride=0, split=0, layout=0, **extra):
     d = kk.GemmDesc()
     d.weight, d.M, d.K = p(w), w.shape[0], w.shape[1]
+    if layout == kk.W_PACKED:
+        d.weight, d.weight_layout = p(packed_weight(kk, K, w)), layout
     d.x, d.N, d.x_stride, d.x_rows = p(x), extra.pop("N", x.shape[0]), x.shape[1], x.shape[0]
     d.epilogue, d.out, d.out_stride, d.split_k = epi, p(out), out_stride, split
     for k_, v in extra.items():
@@ -41,28 +69,28 @@ def gemm(kk, K, w, x, epi, out=None, out_stride=0, split=0, **extra):
 @pytest.mark.parametrize("M,Kd,N,split", [
     (128, 64, 16, 1), (256, 2048, 32, 0), (300, 1000, 7, 3), (2560, 2048, 32, 0),
     (2048, 5632, 64, 0), (640, 512, 1, 2), (11264, 2048, 33, 0), (100, 256, 64, 4)])
-def test_gemm_store_f32_matches_torch(kk, K, M, Kd, N, split):
+def test_gemm_store_f32_matches_torch(kk, K, M, Kd, N, split, wlayout):
     g = torch.Generator().manual_seed(M * 7 + Kd + N)
     w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
     x = torch.randn(N, Kd, generator=g).half().cuda()
     out = torch.full((N, M), float("nan"), device="cuda")
-    gemm(kk, K, w, x, kk.EPI_STORE_F32, out, M, split)
+    gemm(kk, K, w, x, kk.EPI_STORE_F32, out, M, split, layout=wlayout)
     sync_ok(K)
     ref = (x.float() @ w.float().T)
     torch.testing.assert_close(out, ref, atol=2e-3, rtol=1e-3)  # FP32 accumulation
 
 
-def test_gemm_store_f16_and_residual(kk, K):
+def test_gemm_store_f16_and_residual(kk, K, wlayout):
     g = torch.Generator().manual_seed(3)
     M, Kd, N = 512, 768, 24
     w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
     x = torch.randn(N, Kd, generator=g).half().cuda()
     acc = (x.float() @ w.float().T)
     out = torch.zeros(N, M, dtype=torch.half, device="cuda")
-    gemm(kk, K, w, x, kk.EPI_STORE_F16, out, M)
+    gemm(kk, K, w, x, kk.EPI_STORE_F16, out, M, layout=wlayout)
     h = torch.randn(N, M, generator=g).half().cuda()
     h2 = h.clone()
-    gemm(kk, K, w, x, kk.EPI_RESIDUAL, h2, M)
+    gemm(kk, K, w, x, kk.EPI_RESIDUAL, h2, M, layout=wlayout)
     sync_ok(K)
     # rounding point: half(acc), then an FP16 add; allow one FP16 ulp of slack
     torch.testing.assert_close(out.float(), acc.half().float(), atol=2e-3, rtol=2e-3)
@@ -70,7 +98,7 @@ def test_gemm_store_f16_and_residual(kk, K):
                                atol=4e-3, rtol=2e-3)
 
 
-def test_gemm_silu_pairs(kk, K):
+def test_gemm_silu_pairs(kk, K, wlayout):
     g = torch.Generator().manual_seed(5)
     inter, Kd, N = 384, 512, 9
     wg = (torch.randn(inter, Kd, generator=g) * 0.05).half()
@@ -78,7 +106,7 @@ def test_gemm_silu_pairs(kk, K):
     w = torch.stack([wg, wu], dim=1).reshape(2 * inter, Kd).cuda()  # row 2i gate, 2i+1 up
     x = torch.randn(N, Kd, generator=g).half().cuda()
     out = torch.zeros(N, inter, dtype=torch.half, device="cuda")
-    gemm(kk, K, w, x, kk.EPI_SILU_PAIRS, out, inter)
+    gemm(kk, K, w, x, kk.EPI_SILU_PAIRS, out, inter, layout=wlayout)
     sync_ok(K)
     gate = (x.float() @ wg.cuda().float().T).half().float()
     up = (x.float() @ wu.cuda().float().T).half().float()
@@ -86,7 +114,7 @@ def test_gemm_silu_pairs(kk, K):
     torch.testing.assert_close(out.float(), ref.float(), atol=5e-3, rtol=5e-3)
 
 
-def test_gemm_qkv_rope_writes_q_and_pages(kk, K):
+def test_gemm_qkv_rope_writes_q_and_pages(kk, K, wlayout):
     layers, hkv, hq, D, hidden = 3, 2, 8, 64, 256
     pools, micro, extent = make_pools(kk, layers, hkv, D, 16, 4, seed=1)
     g = torch.Generator().manual_seed(9)
@@ -103,7 +131,7 @@ def test_gemm_qkv_rope_writes_q_and_pages(kk, K):
     before_micro, before_extent = micro.clone(), extent.clone()
     gemm(kk, K, w, x, kk.EPI_QKV_ROPE, q_out, hq * D, N=N, positions=p(positions),
          slots=p(slots_dev), pools=pools, layer=layer, q_rows=hq * D, kv_rows=hkv * D,
-         head_dim=D, rope_theta=10000.0)
+         head_dim=D, rope_theta=10000.0, layout=wlayout)
     sync_ok(K)
     acc = (x[:N].float() @ w.float().T).half()  # [N, M] rounded projection outputs
     q_ref = rope_ref(acc[:, :hq * D].reshape(N, hq, D), positions, 10000.0).reshape(N, -1)
@@ -129,7 +157,7 @@ def test_gemm_qkv_rope_writes_q_and_pages(kk, K):
 
 
 @pytest.mark.parametrize("V,N", [(32000, 4), (1000, 33), (130, 1)])
-def test_gemm_argmax_matches_numpy(kk, K, V, N):
+def test_gemm_argmax_matches_numpy(kk, K, V, N, wlayout):
     g = torch.Generator().manual_seed(V + N)
     Kd = 256
     w = (torch.randn(V, Kd, generator=g) * 0.05).half().cuda()
@@ -141,24 +169,52 @@ def test_gemm_argmax_matches_numpy(kk, K, V, N):
     ws = torch.zeros(K["argmax_workspace_bytes"](V, N), dtype=torch.uint8, device="cuda")
     logits = torch.zeros(N, V, device="cuda")
     for _ in range(2):  # the completion counter must reset itself between launches
-        gemm(kk, K, w, x, kk.EPI_ARGMAX, logits, V, N=N, tokens=p(tokens), argmax_workspace=p(ws))
+        gemm(kk, K, w, x, kk.EPI_ARGMAX, logits, V, N=N, tokens=p(tokens), argmax_workspace=p(ws),
+             layout=wlayout)
         sync_ok(K)
         ref = np.argmax(logits.cpu().numpy(), axis=1)
         assert tokens.cpu().numpy().tolist() == ref.tolist()
     torch.testing.assert_close(logits, x[:N].float() @ w.float().T, atol=2e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("M,Kd", [(128, 64), (300, 1000), (32000, 256), (2560, 2048)])
+def test_gemm_pack_weight_layout_is_exact(kk, K, M, Kd):
+    """Tile (t, b) holds rows t*128.., columns b*64.. with 16-byte chunk c of row r
+    at r*128 + ((c ^ (r % 8)) * 16); padding is zero."""
+    g = torch.Generator().manual_seed(M + Kd)
+    w = torch.randn(M, Kd, generator=g).half().cuda()
+    packed = packed_weight(kk, K, w).view(torch.int16).cpu()
+    tiles, kb = (M + 127) // 128, (Kd + 63) // 64
+    assert packed.numel() == tiles * kb * 128 * 64
+    wp = torch.zeros(tiles * 128, kb * 64, dtype=torch.int16)
+    wp[:M, :Kd] = w.view(torch.int16).cpu()
+    ref = wp.view(tiles, 128, kb, 8, 8).permute(0, 2, 1, 3, 4).contiguous()  # [t, b, r, c, 8]
+    r = torch.arange(128)[:, None]
+    c = torch.arange(8)[None, :]
+    swz = torch.empty_like(ref)
+    swz[:, :, r, c ^ (r % 8)] = ref[:, :, r, c]
+    assert torch.equal(packed.view(tiles, kb, 128, 8, 8), swz)
+
+
 @pytest.mark.parametrize("contexts,target", [
     ([17, 100, 513, 2000], 256), ([1, 8, 9, 64, 65], 64), ([4096, 1024, 3000], 512),
     ([33], 8)])
-@pytest.mark.parametrize("hkv,hq", [(4, 32), (2, 8), (1, 16)])
-def test_paged_attention_matches_torch(kk, K, contexts, target, hkv, hq):
+@pytest.mark.parametrize("hkv,hq", [(4, 32), (2, 8), (1, 16), (8, 64)])
+@pytest.mark.parametrize("variant", [1, 2], ids=["direct", "tma"])
+def test_paged_attention_matches_torch(kk, K, attn_variant, contexts, target, hkv, hq, variant,
+                                       poison=False):
+    attn_variant(variant)
     layers, D = 2, 64
     rng = random.Random(sum(contexts) + hq)
     micro_cap = sum((c % 64 + 7) // 8 for c in contexts) + 16
     extent_cap = sum(c // 64 for c in contexts) + 4
     pools, micro, extent = make_pools(kk, layers, hkv, D, micro_cap, extent_cap, seed=len(contexts))
     tables = build_tables(contexts, micro_cap, extent_cap, rng)
+    if poison:
+        # Bytes past a page's valid tokens must never reach the output.
+        for tbl in tables:
+            for slot, _, valid, kind in tbl:
+                (micro if kind == 0 else extent)[slot, :, :, valid:] = float("nan")
     descs, lanes = descs_and_lanes(kk, tables)
     max_items = 4096
     items = (kk.AttnItem * max_items)()
@@ -180,6 +236,106 @@ def test_paged_attention_matches_torch(kk, K, contexts, target, hkv, hq):
             k, v = gather_kv(micro, extent, tbl, layer)
             ref = attention_ref(q[b].view(hq, D), k, v, scale)
             torch.testing.assert_close(out[b].view(hq, D).float(), ref, atol=2e-3, rtol=2e-2)
+
+
+@pytest.mark.parametrize("contexts,parts", [
+    ([17, 100, 513, 2000], 3), ([1, 8, 9, 64, 65, 0, 300], 4), ([4096, 1024, 3000], 148),
+    ([33], 1), ([2000] * 8, 5), ([0, 70, 0, 0, 129], 2)])
+@pytest.mark.parametrize("hkv,hq", [(4, 32), (2, 8), (1, 16), (8, 64)])
+def test_paged_attention_balanced_plan_matches_torch(kk, K, attn_variant, contexts, parts, hkv, hq):
+    """Token-balanced items that span lanes (TMA kernel): every non-empty lane
+    matches the FP32 reference, whether it is whole inside one item or split."""
+    attn_variant(kk.ATTN_TMA)
+    layers, D = 2, 64
+    rng = random.Random(sum(contexts) + parts)
+    micro_cap = sum((c % 64 + 7) // 8 for c in contexts) + 16
+    extent_cap = sum(c // 64 for c in contexts) + 4
+    pools, micro, extent = make_pools(kk, layers, hkv, D, micro_cap, extent_cap, seed=parts)
+    tables = build_tables(contexts, micro_cap, extent_cap, rng)
+    descs, lanes = descs_and_lanes(kk, tables)
+    items = (kk.AttnItem * 4096)()
+    B = len(contexts)
+    n_items = K["attention_plan_balanced"](descs, lanes, B, parts, items, 4096)
+    assert 0 < n_items <= parts
+    q = (torch.randn(B, hq * D) / 8).half().cuda()
+    out = torch.zeros(B, hq * D, dtype=torch.half, device="cuda")
+    ws_bytes = K["attention_workspace_bytes"](B, n_items, hq, D)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    d_descs, d_lanes, d_items = to_device_bytes(descs), to_device_bytes(lanes), to_device_bytes(items)
+    for layer in range(layers):
+        for _ in range(2):  # completion counters must reset themselves
+            rc = K["paged_decode_attention"](C.byref(pools), layer, hq, p(d_descs), p(d_lanes), B,
+                                             p(d_items), n_items, p(q), hq * D, p(out), hq * D,
+                                             0.125, p(ws), ws_bytes, None)
+            assert rc == 0
+            sync_ok(K)
+            for b, tbl in enumerate(tables):
+                if not tbl:
+                    continue
+                k, v = gather_kv(micro, extent, tbl, layer)
+                ref = attention_ref(q[b].view(hq, D), k, v, 0.125)
+                torch.testing.assert_close(out[b].view(hq, D).float(), ref, atol=2e-3, rtol=2e-2)
+
+
+def test_direct_kernel_rejects_multi_lane_items(kk, K, attn_variant):
+    attn_variant(kk.ATTN_DIRECT)
+    pools, micro, extent = make_pools(kk, 1, 4, 64, 8, 2, seed=5)
+    tables = [[(0, 0, 8, 0)], [(1, 0, 8, 0)]]
+    descs, lanes = descs_and_lanes(kk, tables)
+    items = (kk.AttnItem * 4)()
+    n_items = K["attention_plan_balanced"](descs, lanes, 2, 1, items, 4)
+    assert n_items == 1 and items[0].desc_end == 2
+    q = (torch.randn(2, 32 * 64) / 8).half().cuda()
+    out = torch.zeros(2, 32 * 64, dtype=torch.half, device="cuda")
+    ws = torch.zeros(K["attention_workspace_bytes"](2, n_items, 32, 64), dtype=torch.uint8,
+                     device="cuda")
+    d_descs, d_lanes, d_items = to_device_bytes(descs), to_device_bytes(lanes), to_device_bytes(items)
+    rc = K["paged_decode_attention"](C.byref(pools), 0, 32, p(d_descs), p(d_lanes), 2, p(d_items),
+                                     n_items, p(q), 32 * 64, p(out), 32 * 64, 0.125, p(ws),
+                                     ws.numel(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert K["device_status"](None) == 3  # kErrBadArgument, then cleared
+    assert K["device_status"](None) == 0
+    assert torch.count_nonzero(out) == 0
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["direct", "tma"])
+def test_paged_attention_ignores_page_tails(kk, K, attn_variant, variant):
+    test_paged_attention_matches_torch(kk, K, attn_variant, [5, 70, 130, 1001], 64, 4, 32, variant,
+                                       poison=True)
+
+
+@pytest.mark.parametrize("variant", [1, 2], ids=["direct", "tma"])
+def test_paged_attention_reports_bad_descriptor(kk, K, attn_variant, variant):
+    """A descriptor outside its pool is never dereferenced; the launch reports it."""
+    attn_variant(variant)
+    pools, micro, extent = make_pools(kk, 1, 4, 64, 8, 2, seed=3)
+    tables = [[(1, 0, 64, 1), (7, 64, 5, 0)], [(9, 0, 8, 0), (0, 8, 3, 0)]]  # slot 9 > micro_cap
+    descs, lanes = descs_and_lanes(kk, tables)
+    items = (kk.AttnItem * 8)()
+    n_items = K["attention_plan"](descs, lanes, 2, 256, items, 8)
+    q = (torch.randn(2, 32 * 64) / 8).half().cuda()
+    out = torch.zeros(2, 32 * 64, dtype=torch.half, device="cuda")
+    ws = torch.zeros(K["attention_workspace_bytes"](2, n_items, 32, 64), dtype=torch.uint8,
+                     device="cuda")
+    d_descs, d_lanes, d_items = to_device_bytes(descs), to_device_bytes(lanes), to_device_bytes(items)
+    rc = K["paged_decode_attention"](C.byref(pools), 0, 32, p(d_descs), p(d_lanes), 2, p(d_items),
+                                     n_items, p(q), 32 * 64, p(out), 32 * 64, 0.125, p(ws),
+                                     ws.numel(), None)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert K["device_status"](None) == 2  # kErrBadDescriptor, then cleared
+    assert K["device_status"](None) == 0
+    k, v = gather_kv(micro, extent, tables[0], 0)
+    ref = attention_ref(q[0].view(32, 64), k, v, 0.125)
+    torch.testing.assert_close(out[0].view(32, 64).float(), ref, atol=2e-3, rtol=2e-2)
+    # lane 1's output is unspecified (its table is corrupt); the other lanes are unaffected
+
+
+def test_attention_variant_switch_rejects_unknown(kk, K, attn_variant):
+    assert K["attention_set_variant"](7) == kk.KK_EINVAL
+    assert K["attention_set_variant"](-1) == kk.KK_EINVAL
 
 
 def test_kv_write_and_copy_are_exact(kk, K):
