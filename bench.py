@@ -276,6 +276,12 @@ def h2d_bytes(B, contexts):
     return 16 + B * (4 + 4 + 8 + 12 + 32) + items * 16 + entries * 16
 
 
+# DRAM traffic / algorithmic K+V bytes of one K1 launch, from an ncu capture of
+# `bench.py --kernel-only attention --variant tma --plan balanced` (the same
+# kernel, balanced work list and context distribution as the c4 step).
+K1_TRAFFIC_PER_ALGORITHMIC_BYTE = 80.74752 / 78.297088
+
+
 def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr):
     import torch
     hq, D, L = cfg["q_heads"], cfg["head_dim"], cfg["layers"]
@@ -294,7 +300,9 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
             descs_list.append(kk.PageDesc(e.slot, e.logical_token_begin, e.valid_tokens, e.kind, 0, 0))
     descs = (kk.PageDesc * len(descs_list))(*descs_list)
     items = (kk.AttnItem * 16384)()
-    n_items = K["attention_plan"](descs, lanes, B, 256, items, 16384)
+    # the runner's own work list: one token-balanced run per SM
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    n_items = K["attention_plan_balanced"](descs, lanes, B, sms, items, 16384)
     tokens = sum(lanes[b].token_count for b in range(B))
     to_dev = lambda arr: torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8).cuda()
     d_descs, d_lanes, d_items = to_dev(descs), to_dev(lanes), to_dev(items)
@@ -303,32 +311,43 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
     ws_b = K["attention_workspace_bytes"](B, n_items, hq, D)
     ws = torch.zeros(ws_b, dtype=torch.uint8, device="cuda")
 
-    def launch_all():
+    def launch_all(sp):
         for layer in range(L):
             rc = K["paged_decode_attention"](C.byref(pools), layer, hq, d_descs.data_ptr(),
                                              d_lanes.data_ptr(), B, d_items.data_ptr(), n_items,
                                              q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125,
-                                             ws.data_ptr(), ws_b, sptr)
+                                             ws.data_ptr(), ws_b, sp)
             assert rc == 0
     for _ in range(3):
-        launch_all()
+        launch_all(sptr)
+    torch.cuda.synchronize()
+    # One launch per layer, replayed from a CUDA graph (as in the decode step),
+    # timed with events on the stream the graph runs on.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        launch_all(C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    graph.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 5
     e0.record(stream)
     for _ in range(reps):
-        launch_all()
+        graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
+    assert K["device_status"](sptr) == 0
     avg_ms = e0.elapsed_time(e1) / (reps * L)
     bytes_per_launch = tokens * cfg["kv_heads"] * D * 2 * 2  # K and V of every attended token
     peak, peak_note = measured_peaks()
     achieved = bytes_per_launch / (avg_ms / 1e3) / 1e9
-    return {"kernel": "paged_decode_attention_kernel (K1), one layer, all lanes",
+    return {"kernel": "paged_attention_tma_kernel (K1), one layer, all lanes, balanced plan",
             "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4), "peak_source": peak_note,
             "algorithmic_bytes_per_launch": bytes_per_launch, "avg_launch_us": round(avg_ms * 1e3, 2),
-            "traffic": None}
+            "traffic": round(bytes_per_launch * K1_TRAFFIC_PER_ALGORITHMIC_BYTE),
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of "
+                              "the same kernel and work list on the kernel-only c4 case "
+                              "(80.75 MB for 78.30 MB algorithmic), scaled by the bytes processed"}
 
 
 # ---------------------------------------------------------------------------
@@ -463,7 +482,7 @@ def run_kernel_only(args):
         def launch():
             d = descs[state["i"] % copies]
             state["i"] += 1
-            return K["gemm"](C.byref(d), sptr)
+            return K["gemm"](C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream))
         label.update(shape=args.shape, layout=args.layout, M=M, K=Kd, N=N, weight_copies=copies)
     else:
         variant = {"auto": kk.ATTN_AUTO, "direct": kk.ATTN_DIRECT, "tma": kk.ATTN_TMA}[args.variant]
@@ -514,18 +533,29 @@ def run_kernel_only(args):
             state["i"] += 1
             return K["paged_decode_attention"](
                 C.byref(pools), layer, hq, dd.data_ptr(), dl.data_ptr(), 32, di.data_ptr(), n_items,
-                q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125, ws.data_ptr(), ws_b, sptr)
+                q.data_ptr(), hq * D, out.data_ptr(), hq * D, 0.125, ws.data_ptr(), ws_b,
+                C.c_void_p(torch.cuda.current_stream().cuda_stream))
         nbytes = sum(contexts) * row * 2 * 2
         label.update(items=n_items, plan=args.plan, target_tokens=args.target_tokens)
     for _ in range(args.warmup):
         assert launch() == 0
     torch.cuda.synchronize()
+    # The timed launches are replayed from a CUDA graph, so the device time is
+    # not inflated by host launch overhead between short kernels.
+    graph = torch.cuda.CUDAGraph()
+    K["set_pdl"](1 if args.pdl else 0)
+    with torch.cuda.graph(graph):
+        for _ in range(args.steps):
+            assert launch() == 0
+    K["set_pdl"](0)
+    graph.replay()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
-        assert launch() == 0
+    graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
+    label.update(pdl=bool(args.pdl))
     us = e0.elapsed_time(e1) / args.steps * 1e3
     peak, _ = measured_peaks()
     assert K["device_status"](sptr) == 0
@@ -552,6 +582,8 @@ def main():
                     help="--kernel-only attention: kernel variant")
     ap.add_argument("--target-tokens", type=int, default=256,
                     help="--kernel-only attention: tokens per work item (--plan lane)")
+    ap.add_argument("--pdl", action="store_true",
+                    help="--kernel-only: launch with programmatic dependent launch (as the runner does)")
     ap.add_argument("--plan", default="balanced", choices=["balanced", "lane"],
                     help="--kernel-only attention: one token-balanced run per SM, or per-lane items")
     args = ap.parse_args()

@@ -369,6 +369,24 @@ def test_kv_write_and_copy_are_exact(kk, K):
     assert torch.equal(extent[2, :, :, 8:], e1[2, :, :, 8:])
 
 
+def test_kv_promote_is_exact(kk, K):
+    """8 micro pages -> 1 extent, every layer, K and V: extent token 8k+t is
+    micro page k's token t; other extents and the micro pages are untouched."""
+    layers, hkv, D = 3, 4, 64
+    pools, micro, extent = make_pools(kk, layers, hkv, D, 16, 3, seed=13)
+    m0, e0 = micro.clone(), extent.clone()
+    slots = (C.c_uint32 * 8)(*[11, 3, 0, 7, 15, 2, 9, 4])
+    assert K["kv_promote"](C.byref(pools), slots, 1, None) == 0
+    sync_ok(K)
+    for k, sl in enumerate(slots):
+        assert torch.equal(extent[1, :, :, 8 * k:8 * k + 8], m0[sl])
+    assert torch.equal(extent[0], e0[0]) and torch.equal(extent[2], e0[2])
+    assert torch.equal(micro, m0)
+    bad = (C.c_uint32 * 8)(*[11, 3, 0, 7, 15, 2, 9, 16])  # slot 16 is outside the pool
+    assert K["kv_promote"](C.byref(pools), bad, 1, None) == kk.KK_EINVAL
+    assert K["kv_promote"](C.byref(pools), slots, 3, None) == kk.KK_EINVAL
+
+
 def test_rmsnorm_embedding_rope_silu_residual(kk, K):
     g = torch.Generator().manual_seed(21)
     rows, cols, V = 6, 2048, 100
