@@ -127,6 +127,39 @@ KK_KAPI int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer,
     uint16_t* output, uint32_t output_stride, float scale, void* workspace,
     uint64_t workspace_bytes, void* stream);
 
+/* kk_paged_decode_attention without a caller workspace. No counterpart in
+ * the reference, which allocates attention scratch per call.
+ *
+ * It is for callers that cannot allocate device memory for the workspace:
+ *  - hosts that reach the library through an FFI (cgo, JNI, ctypes) with only
+ *    raw stream handles and no device allocator of their own;
+ *  - serving loops that must not call cudaMalloc per step, because it
+ *    synchronizes the device and its latency is unbounded.
+ *
+ * The completion counters and partial softmax states live in one fixed
+ * device array of KK_ATTN_SCRATCH_BYTES (4 MiB) per device, created with the
+ * library's module. A call that needs more,
+ * kk_attention_workspace_bytes(num_lanes, num_items, q_heads, 64) >
+ * KK_ATTN_SCRATCH_BYTES, is rejected with KK_ENOSCRATCH and launches
+ * nothing. For scale: 64 lanes x 148 items x 32 query heads need 2.5 MB.
+ *
+ * The per-lane completion counters at the start of the scratch must be zero
+ * when a kernel starts. This entry point zeroes them on `stream` before every
+ * launch. Nothing else needs initial values.
+ *
+ * The first call on each device looks up the scratch address; make it
+ * before any stream capture. Calls that can overlap on one device (different
+ * streams, or several host threads) share the one scratch array and race:
+ * serialize them on one stream, or use kk_paged_decode_attention with a
+ * workspace per stream. Other arguments, results and errors are those of
+ * kk_paged_decode_attention. */
+#define KK_ATTN_SCRATCH_BYTES (4u << 20)
+#define KK_ENOSCRATCH 1001
+KK_KAPI int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t layer,
+    uint32_t q_heads, const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, const uint16_t* query, uint32_t query_stride,
+    uint16_t* output, uint32_t output_stride, float scale, void* stream);
+
 /* Kernel used by kk_paged_decode_attention (process-wide; default AUTO). No
  * counterpart in the reference (it has one attention implementation).
  *  KK_ATTN_AUTO   : the TMA kernel where supported (kv_heads in {1,2,4,8},

@@ -231,6 +231,8 @@ class Manager:
 # ---- kernel C ABI (include/kk_kernels.h) ------------------------------------
 
 KK_EINVAL = 1000
+KK_ENOSCRATCH = 1001
+ATTN_SCRATCH_BYTES = 4 << 20
 ATTN_AUTO, ATTN_DIRECT, ATTN_TMA = 0, 1, 2
 ATTN_ITEM_MULTI_LANE = 1
 W_ROW_MAJOR, W_PACKED = 0, 1
@@ -286,6 +288,8 @@ _VP = C.c_void_p
 KERNEL_SIGNATURES = {
     "attention_plan": (_U32, [C.POINTER(PageDesc), C.POINTER(AttnLane), _U32, _U32,
                               C.POINTER(AttnItem), _U32]),
+    "paged_decode_attention_noalloc": (_I, [C.POINTER(KvPools), _U32, _U32, _VP, _VP, _U32, _VP,
+                                            _U32, _VP, _U32, _VP, _U32, C.c_float, _VP]),
     "attention_plan_balanced": (_U32, [C.POINTER(PageDesc), C.POINTER(AttnLane), _U32, _U32,
                                        C.POINTER(AttnItem), _U32]),
     "attention_workspace_bytes": (_U64, [_U32, _U32, _U32, _U32]),

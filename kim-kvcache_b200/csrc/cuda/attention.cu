@@ -24,6 +24,7 @@
 
 #include <atomic>
 #include <cmath>
+#include <mutex>
 #include <vector>
 
 namespace kk {
@@ -32,6 +33,44 @@ __device__ unsigned int g_attn_status;
 
 // Kernel choice for kk_paged_decode_attention (KK_ATTN_*), process-wide.
 std::atomic<int> g_attention_variant{KK_ATTN_AUTO};
+
+// Scratch of kk_paged_decode_attention_noalloc: the per-lane completion
+// counters and partial softmax states live in this fixed device array (one
+// per device, created with the module) instead of in caller memory.
+static __device__ __align__(256) unsigned char g_attn_scratch[KK_ATTN_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Device address of g_attn_scratch on the current device, looked up once per
+// device (the first call on a device does the lookup).
+int scratchAddress(void** out)
+{
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) {
+        return static_cast<int>(e);
+    }
+    if (device < 0 || device >= kMaxDevices) {
+        return KK_EINVAL;
+    }
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (g_scratch_address[device] == nullptr) {
+        void* address = nullptr;
+        e = cudaGetSymbolAddress(&address, g_attn_scratch);
+        if (e != cudaSuccess) {
+            return static_cast<int>(e);
+        }
+        g_scratch_address[device] = address;
+    }
+    *out = g_scratch_address[device];
+    return 0;
+}
+
+} // namespace
 
 namespace {
 
@@ -632,6 +671,31 @@ int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer, uint32_t
 {
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
         nullptr, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
+        kk::g_attention_variant.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
+}
+
+int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
+    const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, const uint16_t* query, uint32_t query_stride,
+    uint16_t* output, uint32_t output_stride, float scale, void* stream)
+{
+    std::uint64_t const need = kk_attention_workspace_bytes(num_lanes, num_items, q_heads, 64);
+    if (need > KK_ATTN_SCRATCH_BYTES) {
+        return KK_ENOSCRATCH;
+    }
+    void* scratch = nullptr;
+    int const rc = kk::scratchAddress(&scratch);
+    if (rc != 0) {
+        return rc;
+    }
+    // The completion counters must be zero when the kernel starts.
+    cudaError_t const e = cudaMemsetAsync(scratch, 0, kk::align256(std::uint64_t(num_lanes) * 4u),
+        static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        return static_cast<int>(e);
+    }
+    return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
+        nullptr, query, query_stride, output, output_stride, scale, scratch, KK_ATTN_SCRATCH_BYTES,
         kk::g_attention_variant.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
 }
 
