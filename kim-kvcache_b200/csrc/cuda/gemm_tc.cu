@@ -126,10 +126,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint64_t* empty = full + kStages;
     std::uint64_t* accum = empty + kStages;
     std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(accum + 1);
-    float* xchg = reinterpret_cast<float*>(tmem_slot + 4);          // [128]
-    float* amax_v = xchg + kBM;                                      // [4]
-    std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4);  // [4]
-    int* flag = reinterpret_cast<int*>(amax_i + 4);
+    int* flag = reinterpret_cast<int*>(tmem_slot + 4);
 
     std::uint32_t const tid = threadIdx.x;
     std::uint32_t const warp = tid / 32;
@@ -246,64 +243,103 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
 
     std::uint32_t const n0 = rank * args.N / S;
     std::uint32_t const n1 = (rank + 1) * args.N / S;
+    std::uint32_t const cols = n1 - n0;
     std::uint32_t const m = m_tile * kBM + row;
     EpiArgs const& e = args.epi;
-    std::uint32_t remote[8];
-    for (std::uint32_t r = 0; r < S && r < 8; ++r) {
-        remote[r] = S > 1 ? cluster_map(part, r) : smem_u32(part);
+    // This CTA reduces columns [n0, n1) of the tile over the cluster's K
+    // slices, in rank order, into red[n - n0][row] (the ring is idle now and
+    // `part` stays untouched for the peers still reading it). Remote loads of
+    // four columns are issued before any is summed.
+    float* red = part + BN * kBM;
+    float* amax_v = red + BN * kBM;                                          // [4][BN]
+    std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4 * BN);  // [4][BN]
+    {
+        std::uint32_t remote[8];
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            remote[r] = (S > 1 && static_cast<std::uint32_t>(r) < S) ? cluster_map(part, r) : smem_u32(part);
+        }
+        for (std::uint32_t n = n0; n < n1; n += 4) {
+            float vals[4][8];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    vals[j][r] = 0.f;
+                    if (n + j < n1 && static_cast<std::uint32_t>(r) < S) {
+                        vals[j][r] = S > 1 ? ld_cluster_f32(remote[r] + ((n + j) * kBM + row) * 4u)
+                                           : part[(n + j) * kBM + row];
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                float acc = 0.f;
+#pragma unroll
+                for (int r = 0; r < 8; ++r) {
+                    if (static_cast<std::uint32_t>(r) < S) {
+                        acc += vals[j][r];
+                    }
+                }
+                if (n + j < n1) {
+                    red[(n + j - n0) * kBM + row] = acc;
+                }
+            }
+        }
     }
-    for (std::uint32_t n = n0; n < n1; ++n) {
-        float acc = 0.f;
-        if (S > 1) {
-            for (std::uint32_t r = 0; r < S; ++r) {
-                acc += ld_cluster_f32(remote[r] + (n * kBM + row) * 4u);
+    __syncthreads();
+
+    switch (e.kind) {
+    case KK_EPI_STORE_F16:
+        if (m < args.M) {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] =
+                    __float2half_rn(red[j * kBM + row]);
             }
-        } else {
-            acc = part[n * kBM + row];
         }
-        switch (e.kind) {
-        case KK_EPI_STORE_F16:
-            if (m < args.M) {
-                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + m] = __float2half_rn(acc);
+        break;
+    case KK_EPI_STORE_F32:
+        if (m < args.M) {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
             }
-            break;
-        case KK_EPI_STORE_F32:
-            if (m < args.M) {
-                static_cast<float*>(e.out)[std::uint64_t(n) * e.out_stride + m] = acc;
+        }
+        break;
+    case KK_EPI_RESIDUAL:
+        if (m < args.M) {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                __half* h = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
+                *h = __hadd(*h, __float2half_rn(red[j * kBM + row]));
             }
-            break;
-        case KK_EPI_RESIDUAL:
-            if (m < args.M) {
-                __half* h = static_cast<__half*>(e.out) + std::uint64_t(n) * e.out_stride + m;
-                *h = __hadd(*h, __float2half_rn(acc));
+        }
+        break;
+    case KK_EPI_SILU_PAIRS:
+        // Rows 2i / 2i+1 hold gate_i / up_i.
+        if ((m & 1u) == 0 && m < args.M) {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                float const g = __half2float(__float2half_rn(red[j * kBM + row]));
+                float const u = __half2float(__float2half_rn(red[j * kBM + (row ^ 1u)]));
+                static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m / 2] =
+                    __float2half_rn(g / (1.0f + expf(-g)) * u);
             }
-            break;
-        case KK_EPI_SILU_PAIRS: {
-            float const mine = __half2float(__float2half_rn(acc));
-            float const other = __shfl_xor_sync(0xffffffffu, mine, 1);
-            if ((m & 1u) == 0 && m < args.M) {
-                float const g = mine;
-                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + m / 2] =
-                    __float2half_rn(g / (1.0f + expf(-g)) * other);
-            }
+        }
+        break;
+    case KK_EPI_QKV_ROPE: {
+        std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
+        if (m >= args.M || m >= kv_end) {
             break;
         }
-        case KK_EPI_QKV_ROPE: {
-            float const mine = __half2float(__float2half_rn(acc));
-            xchg[row] = mine;
-            __syncthreads();
-            float const other = xchg[row ^ 32u];
-            __syncthreads();
-            std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
-            if (m >= args.M || m >= kv_end) {
-                break;
-            }
-            bool const is_v = m >= e.q_rows + e.kv_rows;
-            std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
+        // RoPE pairs dims d and d+32 of a head: rows row and row^32 of the tile.
+        bool const is_v = m >= e.q_rows + e.kv_rows;
+        std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
+        std::uint32_t const d = idx & 63u;
+        float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+        for (std::uint32_t j = 0; j < cols; ++j) {
+            std::uint32_t const n = n0 + j;
+            float const mine = __half2float(__float2half_rn(red[j * kBM + row]));
             float out = mine;
             if (!is_v) {
-                std::uint32_t const d = idx & 63u;
-                float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+                float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
                 float const angle = static_cast<float>(e.positions[n]) * inv_freq;
                 float const c = cosf(angle);
                 float const s = sinf(angle);
@@ -327,14 +363,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     atomicCAS(&g_gemm_status, kErrNone, kErrBadDescriptor);
                 }
             }
-            break;
         }
-        case KK_EPI_ARGMAX: {
-            bool const valid = m < args.M;
-            if (valid && e.out != nullptr) {
-                static_cast<float*>(e.out)[std::uint64_t(n) * e.out_stride + m] = acc;
+        break;
+    }
+    case KK_EPI_ARGMAX: {
+        bool const valid = m < args.M;
+        if (valid && e.out != nullptr) {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
             }
-            float bv = valid ? acc : -INFINITY;
+        }
+        // Per warp, every column's winner over its 32 rows; then per column
+        // over the 4 warps. Ties keep the lowest index.
+        for (std::uint32_t j = 0; j < cols; ++j) {
+            float bv = valid ? red[j * kBM + row] : -INFINITY;
             std::uint32_t bi = valid ? m : 0xffffffffu;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {
@@ -346,26 +388,27 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 }
             }
             if (lane == 0) {
-                amax_v[warp] = bv;
-                amax_i[warp] = bi;
+                amax_v[warp * BN + j] = bv;
+                amax_i[warp * BN + j] = bi;
             }
-            __syncthreads();
-            if (tid == 0) {
-                for (int w = 1; w < 4; ++w) {
-                    if (better(amax_v[w], amax_i[w], bv, bi)) {
-                        bv = amax_v[w];
-                        bi = amax_i[w];
-                    }
+        }
+        __syncthreads();
+        if (tid < cols) {
+            float bv = amax_v[tid];
+            std::uint32_t bi = amax_i[tid];
+            for (int w = 1; w < 4; ++w) {
+                if (better(amax_v[w * BN + tid], amax_i[w * BN + tid], bv, bi)) {
+                    bv = amax_v[w * BN + tid];
+                    bi = amax_i[w * BN + tid];
                 }
-                e.part_val[std::uint64_t(m_tile) * args.N + n] = bv;
-                e.part_idx[std::uint64_t(m_tile) * args.N + n] = bi;
             }
-            __syncthreads();
-            break;
+            e.part_val[std::uint64_t(m_tile) * args.N + n0 + tid] = bv;
+            e.part_idx[std::uint64_t(m_tile) * args.N + n0 + tid] = bi;
         }
-        default:
-            break;
-        }
+        break;
+    }
+    default:
+        break;
     }
 
     if (e.kind == KK_EPI_ARGMAX) {
