@@ -180,6 +180,9 @@ def run_ours(args, rank, world, local_rank):
     runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr, max(B, 1),
                                 1, 1, C.byref(status), detail, 512)
     assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
+    # Fold each lane's 8 sealed micro pages into an extent whenever decode
+    # completes a 64-token run, so tails stay short (8 micro -> 1 extent).
+    assert R["runner_set_auto_promote"](runner, 1) == 1
 
     ids = (C.c_uint64 * B)(*range(1, B + 1))
     tokens = (C.c_uint32 * B)(*[random.Random(SEED + b).randrange(3, 32000) for b in range(B)])

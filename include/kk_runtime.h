@@ -212,6 +212,12 @@ KK_API void kkrt_txn_destroy(void* txn);   /* rolls back if still active */
 KK_API void* kkrt_runner_create(const char* manifest_path, const char* data_path, void* backend,
     void* stream, uint32_t max_batch_size, int use_cuda_graphs, int verify_checksums,
     int* status, char* detail, uint32_t detail_capacity);
+/* Auto-promotion in the generation path (no counterpart in the reference,
+ * which never promotes while generating): after a step commits a lane's
+ * 64th token of a 64-aligned run, its 8 sealed micro pages become one extent
+ * page (reference promotion semantics, src/runtime/promotion.cpp:80-457).
+ * Returns 1 for a CUDA runner, 0 otherwise. Off by default. */
+KK_API int kkrt_runner_set_auto_promote(void* runner, int enabled);
 KK_API void kkrt_runner_destroy(void* runner);
 /* generationForwardBatch (runner.cpp:410): per lane ok flag + greedy token.
  * Returns 1 when the batch result is well formed. */

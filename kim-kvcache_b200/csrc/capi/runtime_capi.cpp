@@ -329,6 +329,16 @@ float kkrt_runner_last_step_ms(void* r)
     return runner == nullptr ? 0.f : runner->lastStepDeviceMs();
 }
 
+int kkrt_runner_set_auto_promote(void* r, int enabled)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    if (runner == nullptr) {
+        return 0;
+    }
+    runner->setAutoPromote(enabled != 0);
+    return 1;
+}
+
 uint32_t kkrt_runner_last_error(void* r, char* out, uint32_t cap)
 {
     auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));

@@ -180,25 +180,39 @@ __device__ __forceinline__ std::uint32_t lane_desc_end(kk_attn_lane const& ln)
     return ln.desc_offset + ln.desc_count;
 }
 
-// Query rows quad and quad+8 of one KV head's GQA group, as m16n8k16 A fragments.
+// The GQA group's queries as m16n8k16 B fragments of Q^T (k = dim, n = query
+// head): n-tile nt holds heads nt*8 .. nt*8+7 of KV head `head`; thread
+// (g = lane/4, c = lane%4) holds dims 2c, 2c+1 and 2c+8, 2c+9 of each 16-dim
+// k step for head nt*8+g. Heads past the group are zero.
+template <int NT>
 __device__ __forceinline__ void load_query(TmaArgs const& a, std::uint32_t row, std::uint32_t head,
-    std::uint32_t quad, std::uint32_t c4, std::uint32_t (&qa)[4][2], std::uint32_t (&qb)[4][2])
+    std::uint32_t g, std::uint32_t c4, std::uint32_t (&qf)[NT][4][2])
 {
     __half const* q = a.query + static_cast<std::uint64_t>(row) * a.query_stride
         + static_cast<std::uint64_t>(head * a.group) * kHeadDim;
 #pragma unroll
-    for (int k16 = 0; k16 < 4; ++k16) {
+    for (int nt = 0; nt < NT; ++nt) {
+        std::uint32_t const qh = nt * 8u + g;
 #pragma unroll
-        for (int hi = 0; hi < 2; ++hi) {
-            std::uint32_t const col = k16 * 16 + hi * 8 + c4 * 2;
-            qa[k16][hi] = quad < a.group
-                ? *reinterpret_cast<std::uint32_t const*>(q + quad * kHeadDim + col) : 0u;
-            qb[k16][hi] = quad + 8 < a.group
-                ? *reinterpret_cast<std::uint32_t const*>(q + (quad + 8) * kHeadDim + col) : 0u;
+        for (int k16 = 0; k16 < 4; ++k16) {
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+                std::uint32_t const col = k16 * 16 + hi * 8 + c4 * 2;
+                qf[nt][k16][hi] = qh < a.group
+                    ? *reinterpret_cast<std::uint32_t const*>(q + qh * kHeadDim + col) : 0u;
+            }
         }
     }
 }
 
+__device__ __forceinline__ std::uint32_t transpose8x8(std::uint32_t x)
+{
+    std::uint32_t y;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+    return y;
+}
+
+template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     const __grid_constant__ CUtensorMap tm_micro, const __grid_constant__ CUtensorMap tm_extent,
     TmaArgs a)
@@ -427,7 +441,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     }
 
     // ------------------------------ consumers ------------------------------
-    std::uint32_t const quad = lane >> 2;
+    // Scores are computed transposed, S^T = K Q^T (rows = 16 tokens of the
+    // slice, columns = up to 8*NT query heads), and the output as
+    // O^T = V^T P^T (rows = 16 dims per m-tile, columns = query heads), so no
+    // MMA row is spent on padding when a GQA group has 8 heads.
+    std::uint32_t const g = lane >> 2;   // token (or dim) row within an 8-row block
     std::uint32_t const c4 = lane & 3;
     std::uint32_t const head = warp % Hkv;
     std::uint32_t const chunk = warp / Hkv;  // 16-token slice of each stage
@@ -456,13 +474,20 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             pdl_wait();  // queries are written by the previous kernel
             waited = true;
         }
-        std::uint32_t qa[4][2], qb[4][2];
-        load_query(a, ln.query_row, head, quad, c4, qa, qb);
-        float m0 = kNegInf, m1 = kNegInf, l0 = 0.f, l1 = 0.f;
-        float o[8][4];
+        std::uint32_t qf[NT][4][2];
+        load_query<NT>(a, ln.query_row, head, g, c4, qf);
+        // Per query head (nt*8 + 2*c4 + e): running max (same in all 8 g-lanes)
+        // and this lane's share of the softmax denominator.
+        float mrow[NT][2], lrow[NT][2];
+        float o[NT][4][4];  // [nt][dim m-tile][dim g|g+8 x head e]
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        for (int nt = 0; nt < NT; ++nt) {
+            mrow[nt][0] = mrow[nt][1] = kNegInf;
+            lrow[nt][0] = lrow[nt][1] = 0.f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.f;
+            }
         }
         for (;;) {
             std::uint32_t const s = stage % kStages;
@@ -476,73 +501,71 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 std::uint32_t const kbase =
                     ring_base + s * kStageBytes + (head * Ts + chunk * 16u) * kRowBytes;
                 std::uint32_t const vbase = kbase + v_offset;
-                // S = Q K^T over the slice's 16 tokens (two n8 tiles).
-                float s0[4] = {0.f, 0.f, 0.f, 0.f};
-                float s1[4] = {0.f, 0.f, 0.f, 0.f};
+                // S^T = K Q^T over the slice's 16 tokens: K rows are the A operand.
+                float st[NT][4];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    st[nt][0] = st[nt][1] = st[nt][2] = st[nt][3] = 0.f;
+                }
 #pragma unroll
                 for (std::uint32_t k16 = 0; k16 < 4; ++k16) {
-                    std::uint32_t const row = (mi >> 1) * 8u + r8;
-                    std::uint32_t const ch = 2u * k16 + (mi & 1u);
-                    std::uint32_t kb[4];
-                    ldsm_x4(kbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), kb);
-                    mma16816(s0, qa[k16][0], qb[k16][0], qa[k16][1], qb[k16][1], kb[0], kb[1]);
-                    mma16816(s1, qa[k16][0], qb[k16][0], qa[k16][1], qb[k16][1], kb[2], kb[3]);
-                }
-                bool const t00 = 2 * c4 < v0, t01 = 2 * c4 + 1 < v0;
-                bool const t10 = 2 * c4 < v1, t11 = 2 * c4 + 1 < v1;
-                float x[2][4];
-                x[0][0] = t00 ? s0[0] * a.scale_log2 : kNegInf;
-                x[0][1] = t01 ? s0[1] * a.scale_log2 : kNegInf;
-                x[0][2] = t10 ? s1[0] * a.scale_log2 : kNegInf;
-                x[0][3] = t11 ? s1[1] * a.scale_log2 : kNegInf;
-                x[1][0] = t00 ? s0[2] * a.scale_log2 : kNegInf;
-                x[1][1] = t01 ? s0[3] * a.scale_log2 : kNegInf;
-                x[1][2] = t10 ? s1[2] * a.scale_log2 : kNegInf;
-                x[1][3] = t11 ? s1[3] * a.scale_log2 : kNegInf;
-                float p[2][4];
-                float alpha[2];
-#pragma unroll
-                for (int rr = 0; rr < 2; ++rr) {
-                    float& mrow = rr == 0 ? m0 : m1;
-                    float& lrow = rr == 0 ? l0 : l1;
-                    float mx = fmaxf(fmaxf(x[rr][0], x[rr][1]), fmaxf(x[rr][2], x[rr][3]));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                    float const m_new = fmaxf(mrow, mx);
-                    float const m_use = m_new == kNegInf ? 0.f : m_new;
-                    alpha[rr] = exp2f(mrow - m_use);
-                    float sum = 0.f;
-#pragma unroll
-                    for (int t = 0; t < 4; ++t) {
-                        p[rr][t] = exp2f(x[rr][t] - m_use);
-                        sum += p[rr][t];
-                    }
-                    lrow = lrow * alpha[rr] + sum;
-                    mrow = m_new;
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    o[j][0] *= alpha[0];
-                    o[j][1] *= alpha[0];
-                    o[j][2] *= alpha[1];
-                    o[j][3] *= alpha[1];
-                }
-                std::uint32_t const pa0 = pack_half2(p[0][0], p[0][1]);
-                std::uint32_t const pa1 = pack_half2(p[1][0], p[1][1]);
-                std::uint32_t const pa2 = pack_half2(p[0][2], p[0][3]);
-                std::uint32_t const pa3 = pack_half2(p[1][2], p[1][3]);
-                // V halves of masked tokens are zeroed as well: bytes past a
-                // page's valid tokens are never trusted (0 * NaN would be NaN).
-                std::uint32_t const mask0 = (t00 ? 0x0000ffffu : 0u) | (t01 ? 0xffff0000u : 0u);
-                std::uint32_t const mask1 = (t10 ? 0x0000ffffu : 0u) | (t11 ? 0xffff0000u : 0u);
-#pragma unroll
-                for (std::uint32_t jp = 0; jp < 4; ++jp) {
                     std::uint32_t const row = (mi & 1u) * 8u + r8;
-                    std::uint32_t const ch = 2u * jp + (mi >> 1);
-                    std::uint32_t vb[4];
-                    ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), vb);
-                    mma16816(o[2 * jp], pa0, pa1, pa2, pa3, vb[0] & mask0, vb[1] & mask1);
-                    mma16816(o[2 * jp + 1], pa0, pa1, pa2, pa3, vb[2] & mask0, vb[3] & mask1);
+                    std::uint32_t const ch = 2u * k16 + (mi >> 1);
+                    std::uint32_t ka[4];
+                    ldsm_x4(kbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), ka);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816(st[nt], ka[0], ka[1], ka[2], ka[3], qf[nt][k16][0], qf[nt][k16][1]);
+                    }
+                }
+                bool const tg = g < v0;       // token g of the slice
+                bool const tg8 = g < v1;      // token g + 8
+                // V^T rows are the A operand of O^T += V^T P^T. V halves of
+                // masked tokens are zeroed: bytes past a page's valid tokens
+                // are never trusted (0 * NaN would be NaN).
+                std::uint32_t const mask0 = (2 * c4 < v0 ? 0x0000ffffu : 0u) | (2 * c4 + 1 < v0 ? 0xffff0000u : 0u);
+                std::uint32_t const mask1 = (2 * c4 < v1 ? 0x0000ffffu : 0u) | (2 * c4 + 1 < v1 ? 0xffff0000u : 0u);
+                std::uint32_t pb[NT][2];
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    float p[4];
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        float const xa = tg ? st[nt][e] * a.scale_log2 : kNegInf;
+                        float const xb = tg8 ? st[nt][2 + e] * a.scale_log2 : kNegInf;
+                        float mx = fmaxf(xa, xb);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                        float const m_new = fmaxf(mrow[nt][e], mx);
+                        float const m_use = m_new == kNegInf ? 0.f : m_new;
+                        float const alpha = exp2f(mrow[nt][e] - m_use);
+                        p[e] = exp2f(xa - m_use);
+                        p[2 + e] = exp2f(xb - m_use);
+                        lrow[nt][e] = lrow[nt][e] * alpha + p[e] + p[2 + e];
+                        mrow[nt][e] = m_new;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            o[nt][j][e] *= alpha;
+                            o[nt][j][2 + e] *= alpha;
+                        }
+                    }
+                    // P^T fragments (token rows, head columns) transposed into
+                    // the B layout of the PV product (k = token, n = head).
+                    pb[nt][0] = transpose8x8(pack_half2(p[0], p[1]));
+                    pb[nt][1] = transpose8x8(pack_half2(p[2], p[3]));
+                }
+#pragma unroll
+                for (std::uint32_t j = 0; j < 4; ++j) {
+                    std::uint32_t const row = (mi >> 1) * 8u + r8;
+                    std::uint32_t const ch = 2u * j + (mi & 1u);
+                    std::uint32_t va[4];
+                    ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), va);
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) {
+                        mma16816(o[nt][j], va[0] & mask0, va[1] & mask0, va[2] & mask1, va[3] & mask1,
+                            pb[nt][0], pb[nt][1]);
+                    }
                 }
             }
             __syncwarp();
@@ -555,24 +578,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             }
 
             // ---- end of lane b's segment: merge the warps of each KV head ----
-            l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-            l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-            l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-            l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-            if (c4 == 0) {
-                s_m[warp * 16 + quad] = m0;
-                s_l[warp * 16 + quad] = l0;
-                s_m[warp * 16 + quad + 8] = m1;
-                s_l[warp * 16 + quad + 8] = l1;
-            }
-            float* row0 = s_o + (warp * 16 + quad) * kORow;
-            float* row1 = s_o + (warp * 16 + quad + 8) * kORow;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                row0[j * 8 + 2 * c4] = o[j][0];
-                row0[j * 8 + 2 * c4 + 1] = o[j][1];
-                row1[j * 8 + 2 * c4] = o[j][2];
-                row1[j * 8 + 2 * c4 + 1] = o[j][3];
+            for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    float l = lrow[nt][e];
+                    l += __shfl_xor_sync(0xffffffffu, l, 4);
+                    l += __shfl_xor_sync(0xffffffffu, l, 8);
+                    l += __shfl_xor_sync(0xffffffffu, l, 16);
+                    std::uint32_t const qh = nt * 8u + 2u * c4 + e;
+                    if (g == 0) {
+                        s_m[warp * 16 + qh] = mrow[nt][e];
+                        s_l[warp * 16 + qh] = l;
+                    }
+                    float* dst = s_o + (warp * 16 + qh) * kORow;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        dst[16 * j + g] = o[nt][j][e];
+                        dst[16 * j + 8 + g] = o[nt][j][2 + e];
+                    }
+                }
             }
             consumer_sync();
             bool const split = ln.item_count > 1;
@@ -664,14 +689,15 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             // Next lane of this item.
             b = m.next_lane < a.num_lanes ? m.next_lane : 0u;
             ln = a.lanes[b];
-            load_query(a, ln.query_row, head, quad, c4, qa, qb);
-            m0 = kNegInf;
-            m1 = kNegInf;
-            l0 = 0.f;
-            l1 = 0.f;
+            load_query<NT>(a, ln.query_row, head, g, c4, qf);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+            for (int nt = 0; nt < NT; ++nt) {
+                mrow[nt][0] = mrow[nt][1] = kNegInf;
+                lrow[nt][0] = lrow[nt][1] = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    o[nt][j][0] = o[nt][j][1] = o[nt][j][2] = o[nt][j][3] = 0.f;
+                }
             }
         }
         if (*s_abort) {
@@ -826,10 +852,12 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     if (!poolMaps(*pools, maps)) {
         return KK_EINVAL;
     }
-    static cudaError_t const attr = cudaFuncSetAttribute(paged_attention_tma_kernel,
+    static cudaError_t const attr1 = cudaFuncSetAttribute(paged_attention_tma_kernel<1>,
         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
-    if (attr != cudaSuccess) {
-        return static_cast<int>(attr);
+    static cudaError_t const attr2 = cudaFuncSetAttribute(paged_attention_tma_kernel<2>,
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (attr1 != cudaSuccess || attr2 != cudaSuccess) {
+        return static_cast<int>(attr1 != cudaSuccess ? attr1 : attr2);
     }
     TmaArgs a{};
     a.micro_slots = pools->micro_capacity;
@@ -856,8 +884,9 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.part_ml = part_ml;
     static int const sms = smCount();
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
-    return static_cast<int>(launch(paged_attention_tma_kernel, dim3(grid), dim3(kThreads),
-        kSmemBytes, stream, 1, maps.micro, maps.extent, a));
+    auto const kernel = a.group <= 8 ? paged_attention_tma_kernel<1> : paged_attention_tma_kernel<2>;
+    return static_cast<int>(launch(kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, 1,
+        maps.micro, maps.extent, a));
 }
 
 int attentionTmaStatus(cudaStream_t stream) { return readStatus(&g_attn_tma_status, stream); }

@@ -869,6 +869,66 @@ EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::u
     return mapMetadata(st->mgr.commitPromotion(prepared.promotion_id));
 }
 
+std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
+    std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream)
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr || runs.empty()) {
+        return 0;
+    }
+    State* st = b->state();
+    struct Pending {
+        PromotionPrepareResult prepared;
+        PageLeaseAcquireResult lease;
+    };
+    std::vector<Pending> pending;
+    pending.reserve(runs.size());
+    {
+        std::lock_guard<std::mutex> lock(st->mutex);
+        for (auto const& run : runs) {
+            Pending p;
+            p.prepared = st->mgr.preparePromotion(run.first, run.second);
+            if (!p.prepared.ok()) {
+                continue;
+            }
+            p.lease = st->mgr.acquirePromotionIoLease(p.prepared.promotion_id);
+            if (!p.lease.ok()) {
+                static_cast<void>(st->mgr.rollbackPromotion(p.prepared.promotion_id));
+                continue;
+            }
+            pending.push_back(p);
+        }
+    }
+    if (pending.empty()) {
+        return 0;
+    }
+    cudaStream_t const s = static_cast<cudaStream_t>(stream);
+    int rc = 0;
+    for (Pending const& p : pending) {
+        std::uint32_t slots[8];
+        for (int k = 0; k < 8; ++k) {
+            slots[k] = p.prepared.source_handles[k].slot;
+        }
+        if (rc == 0) {
+            rc = kk_kv_promote(&st->storage.pools, slots, p.prepared.target_handle.slot, s);
+        }
+    }
+    if (rc == 0) {
+        rc = static_cast<int>(cudaStreamSynchronize(s));
+    }
+    std::uint32_t committed = 0;
+    std::lock_guard<std::mutex> lock(st->mutex);
+    for (Pending const& p : pending) {
+        static_cast<void>(st->mgr.releasePageLease(p.lease.lease_id));
+        if (rc != 0) {
+            static_cast<void>(st->mgr.rollbackPromotion(p.prepared.promotion_id));
+        } else if (st->mgr.commitPromotion(p.prepared.promotion_id) == KvCacheError::None) {
+            ++committed;
+        }
+    }
+    return committed;
+}
+
 void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept
 {
     auto* b = dynamic_cast<CudaBackend*>(&backend);

@@ -21,6 +21,8 @@
 #include "../../../include/kk_kernels.h"
 
 #include <cstdint>
+#include <utility>
+#include <vector>
 #include <memory>
 #include <string_view>
 
@@ -82,5 +84,11 @@ void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept;
 // src/cuda/kv/cache.cpp:172-229).
 [[nodiscard]] EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id,
     std::uint32_t logical_begin, CudaStream stream);
+// The same for several (request, logical_begin) runs with one device wait:
+// every promotion that prepares is copied, then all are committed (or rolled
+// back if the copies failed). Runs that cannot be promoted (not 8 sealed,
+// full, unshared micro pages) are skipped. Returns how many were committed.
+[[nodiscard]] std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
+    std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream);
 
 } // namespace kimkvcache

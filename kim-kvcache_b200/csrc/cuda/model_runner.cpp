@@ -105,6 +105,7 @@ struct CudaTinyLlamaModelRunner::Impl {
     // the legacy default stream a caller may pass) and replayed on `stream`.
     cudaStream_t capture_stream{nullptr};
     std::string last_error;
+    bool auto_promote{false};
     float last_ms{0.f};
     std::uint32_t last_launches{0};
 
@@ -163,6 +164,7 @@ std::uint32_t CudaTinyLlamaModelRunner::generationMaxBatchSize() const noexcept
     return impl_->options.max_batch_size;
 }
 float CudaTinyLlamaModelRunner::lastStepDeviceMs() const noexcept { return impl_->last_ms; }
+void CudaTinyLlamaModelRunner::setAutoPromote(bool enabled) noexcept { impl_->auto_promote = enabled; }
 std::string CudaTinyLlamaModelRunner::lastError() const { return impl_->last_error; }
 std::uint32_t CudaTinyLlamaModelRunner::lastStepLaunches() const noexcept { return impl_->last_launches; }
 
@@ -474,6 +476,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         noteStreamCompleted(*im.kv, im.stream);
         cudaEventElapsedTime(&im.last_ms, im.ev_begin, im.ev_end);
     }
+    std::vector<std::pair<RequestId, std::uint32_t>> promote;
     for (std::uint32_t b = 0; b < B; ++b) {
         std::size_t const i = lane_index[b];
         if (!s.ok()) {
@@ -484,6 +487,15 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         result.steps[i] = committed.ok()
             ? GenerationStepResult{true, im.host_tokens[b], {}}
             : GenerationStepResult{false, 0, kvFailure(committed, "commit batched model token").detail};
+        std::uint32_t const length = items[i].expected_position + 1;
+        if (committed.ok() && im.auto_promote && length % 64 == 0) {
+            promote.emplace_back(items[i].request_id, length - 64);
+        }
+    }
+    if (!promote.empty()) {
+        // The last 8 micro pages of each lane just filled a 64-token run:
+        // fold them into one extent page (skipped when they are shared).
+        static_cast<void>(cudaBackendPromoteMany(*im.kv, promote, im.stream));
     }
     return result;
 }
@@ -601,6 +613,7 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     im->kv = &kv_backend;
     im->stream = static_cast<cudaStream_t>(stream);
     im->options = options;
+    im->auto_promote = options.auto_promote;
     im->pools = *pools;
 
     // Weights: one device allocation in the fused layout.

@@ -69,6 +69,11 @@ struct CudaModelRunnerOptions final {
     std::uint32_t max_batch_size{8};   // at most 64 lanes per model batch
     bool use_cuda_graphs{true};        // replay the device step from a CUDA graph
     bool verify_checksums{true};       // SHA-256 of every tensor at load
+    // After a step commits the 64th token of a 64-aligned run, fold that
+    // run's 8 sealed micro pages into one extent page (8 micro -> 1 extent
+    // promotion), so decode tails stay under 64 tokens of micro pages. The
+    // reference never promotes during generation; off by default.
+    bool auto_promote{false};
     [[nodiscard]] constexpr bool valid() const noexcept
     {
         return max_batch_size != 0 && max_batch_size <= 64;
@@ -104,6 +109,8 @@ public:
     [[nodiscard]] std::string lastError() const;
     // Kernels launched by the last fused step.
     [[nodiscard]] std::uint32_t lastStepLaunches() const noexcept;
+    // Turns auto-promotion (CudaModelRunnerOptions::auto_promote) on or off.
+    void setAutoPromote(bool enabled) noexcept;
 
 private:
     explicit CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept;

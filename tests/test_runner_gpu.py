@@ -293,6 +293,48 @@ def test_per_layer_spi_write_attend_matches_oracle(kk, tmp_path):
     R["backend_destroy"](backend)
 
 
+def test_auto_promotion_folds_full_runs_and_keeps_outputs(kk, tmp_path):
+    """With auto-promotion on, every 64-aligned run of 8 sealed micro pages
+    becomes one extent page as generation crosses it; greedy tokens and
+    logits still follow the oracle, and the pool accounting stays valid."""
+    cfg = dict(SMALL, max_positions=256)
+    s = Stack(kk, tmp_path, cfg, batch=4, micro=128, extent=8)
+    assert s.R["runner_set_auto_promote"](s.runner, 1) == 1
+    ids = [1, 2, 3]
+    for rid in ids:
+        s.create(rid)
+    pos = {1: 0, 2: 0, 3: 0}
+    tok = {1: 5, 2: 9, 3: 77}
+    start = {1: 0, 2: 20, 3: 60}   # lanes cross 64-token boundaries at different steps
+    for rid in ids:
+        for p in range(start[rid]):
+            g, ok = s.batch([rid], [tok[rid]], [p])
+            w, _, _ = s.oracle.forward([rid], [tok[rid]], [p], want_hidden=False)
+            assert ok == [1]
+            tok[rid] = int(w[0])
+        pos[rid] = start[rid]
+    for step in range(140):
+        toks = [tok[r] for r in ids]
+        ps = [pos[r] for r in ids]
+        got, ok = s.batch(ids, toks, ps)
+        want, logits, _ = s.oracle.forward(ids, toks, ps, want_hidden=False)
+        assert ok == [1, 1, 1]
+        assert_greedy(got, want, logits)
+        for i, r in enumerate(ids):
+            tok[r] = int(want[i])
+            pos[r] += 1
+    buf = (kk.KkEntry * 512)()
+    for r in ids:
+        t = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 512, 0, 0)
+        assert s.R["backend_block_table"](s.backend, r, C.byref(t))
+        kinds = [buf[i].kind for i in range(t.count)]
+        extents = sum(1 for k in kinds if k == 1)
+        assert extents == pos[r] // 64, (r, pos[r], kinds)
+        assert all(k == 1 for k in kinds[:extents]) and all(k == 0 for k in kinds[extents:])
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
 @pytest.mark.slow
 def test_tinyllama_shape_greedy_decode_config2(kk, tmp_path):
     """TinyLlama-1.1B shape, batch 1, 6 seeded prompt ids
