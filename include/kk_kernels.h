@@ -167,7 +167,7 @@ KK_KAPI int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t
  *  KK_ATTN_DIRECT : always the direct-load kernel (warps load K/V rows into
  *                   registers);
  *  KK_ATTN_TMA    : always the TMA kernel (persistent, warp-specialised, K/V
- *                   staged through a 5-stage shared-memory ring); calls it
+ *                   staged through a 3-stage shared-memory ring); calls it
  *                   cannot serve return KK_EINVAL.
  * The direct-load kernel rejects multi-lane items (device status
  * kErrBadArgument = 3, items skipped).

@@ -9,7 +9,7 @@
 //    copies), warps 0-7 are consumers.
 //  * A stage holds Ts = min(64, 128 / kv_heads) tokens of every KV head, K
 //    then V, each laid out [kv_head][token][64 dims] with the 128-byte swizzle
-//    (32 KB per stage, 5 stages). An extent page fills a stage with ONE tensor
+//    (32 KB per stage, 3 stages). An extent page fills a stage with ONE tensor
 //    load for K and one for V: the extent tensor map views the pool as
 //    [slot][layer*2+kv][kv_head][token][dim] (strides permuted, so the box
 //    lands head-major), box 64 dims x Ts tokens x kv_heads. A micro page
@@ -49,7 +49,7 @@ namespace {
 constexpr int kHeadDim = 64;
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kStages = 5;
+constexpr int kStages = 3;
 constexpr std::uint32_t kStageBytes = 32768;           // K 16 KB + V 16 KB
 constexpr std::uint32_t kRowBytes = kHeadDim * 2;      // one head x one token
 constexpr std::uint32_t kORow = kHeadDim + 4;          // padded merge row (floats)
@@ -226,8 +226,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     StageMeta* meta = reinterpret_cast<StageMeta*>(empty + kStages);
     float* s_m = reinterpret_cast<float*>(meta + kStages);    // [warp][16]
     float* s_l = s_m + kConsumerWarps * 16;                    // [warp][16]
-    float* s_o = s_l + kConsumerWarps * 16;                    // [warp][16][kORow]
-    int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 16 * kORow);
+    float* s_o = s_l + kConsumerWarps * 16;                    // [warp][8*NT][kORow]
+    int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 8 * NT * kORow);
     int volatile* s_abort = s_last + 1;
     // Barrier of the consumer threads (the producer never joins). An mbarrier
     // rather than a named barrier, so that its waits are bounded too.
@@ -591,7 +591,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         s_m[warp * 16 + qh] = mrow[nt][e];
                         s_l[warp * 16 + qh] = l;
                     }
-                    float* dst = s_o + (warp * 16 + qh) * kORow;
+                    float* dst = s_o + (warp * 8 * NT + qh) * kORow;
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         dst[16 * j + g] = o[nt][j][e];
@@ -618,7 +618,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     std::uint32_t const w = sub * Hkv + h;
                     float const f = exp2f(s_m[w * 16 + g] - m_use);
                     L += s_l[w * 16 + g] * f;
-                    float const* src = s_o + (w * 16 + g) * kORow + d0;
+                    float const* src = s_o + (w * 8 * NT + g) * kORow + d0;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         acc[e] += src[e] * f;
@@ -706,10 +706,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     }
 }
 
-constexpr std::size_t kSmemBytes = 1024 + kStages * kStageBytes + 2 * kStages * 8
-    + kStages * sizeof(StageMeta) + 2 * kConsumerWarps * 16 * 4
-    + kConsumerWarps * 16 * kORow * 4 + 24;
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+// Small enough (about 118 KB with NT = 1) that a projection CTA of the
+// neighbouring kernels fits on the same SM, so programmatic dependent launch
+// can overlap their prologues and tails with this kernel.
+template <int NT>
+constexpr std::size_t smemBytes()
+{
+    return 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * sizeof(StageMeta)
+        + 2 * kConsumerWarps * 16 * 4 + kConsumerWarps * 8 * NT * kORow * 4 + 24;
+}
+static_assert(smemBytes<2>() <= 227 * 1024, "shared memory budget");
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
     cuuint64_t const*, cuuint64_t const*, cuuint32_t const*, cuuint32_t const*,
@@ -853,9 +859,9 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
         return KK_EINVAL;
     }
     static cudaError_t const attr1 = cudaFuncSetAttribute(paged_attention_tma_kernel<1>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<1>()));
     static cudaError_t const attr2 = cudaFuncSetAttribute(paged_attention_tma_kernel<2>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<2>()));
     if (attr1 != cudaSuccess || attr2 != cudaSuccess) {
         return static_cast<int>(attr1 != cudaSuccess ? attr1 : attr2);
     }
@@ -884,8 +890,10 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.part_ml = part_ml;
     static int const sms = smCount();
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
-    auto const kernel = a.group <= 8 ? paged_attention_tma_kernel<1> : paged_attention_tma_kernel<2>;
-    return static_cast<int>(launch(kernel, dim3(grid), dim3(kThreads), kSmemBytes, stream, 1,
+    bool const narrow = a.group <= 8;
+    auto const kernel = narrow ? paged_attention_tma_kernel<1> : paged_attention_tma_kernel<2>;
+    std::size_t const smem = narrow ? smemBytes<1>() : smemBytes<2>();
+    return static_cast<int>(launch(kernel, dim3(grid), dim3(kThreads), smem, stream, 1,
         maps.micro, maps.extent, a));
 }
 
