@@ -262,6 +262,14 @@ typedef struct kk_gemm_desc {
     void* argmax_workspace;    /* kk_argmax_workspace_bytes(M, N) bytes, zeroed once */
     uint32_t weight_layout;    /* KK_W_ROW_MAJOR, or KK_W_PACKED: weight holds
                                   kk_gemm_pack_weight output for (M, K) */
+    /* Fused RMSNorm of the input rows (replaces a separate rmsNormBatchKernel,
+     * src/cuda/model/kernels.cu:48-124): when norm_input is set, every output
+     * column n is scaled by rsqrt(mean_k norm_input[n][k]^2 + norm_eps) before
+     * the epilogue. With x = norm_input and W packed with the norm weights as
+     * column scale (kk_gemm_pack_weight_scaled), Y = RMSNorm(x) W^T. */
+    const uint16_t* norm_input; /* [N][norm_stride] fp16, 16-byte aligned, or NULL */
+    uint32_t norm_stride;
+    float norm_eps;
 } kk_gemm_desc;
 
 #define KK_W_ROW_MAJOR 0
@@ -274,6 +282,11 @@ typedef struct kk_gemm_desc {
 KK_KAPI uint64_t kk_gemm_packed_bytes(uint32_t M, uint32_t K);
 KK_KAPI int kk_gemm_pack_weight(const uint16_t* weight, uint32_t M, uint32_t K,
     uint16_t* packed, void* stream);
+/* The same with every column k scaled by col_scale[k] (fp16, 16-byte aligned)
+ * before packing, W'[m][k] = half(W[m][k] * col_scale[k]): folds an RMSNorm
+ * weight into the projection that consumes the normalised rows. */
+KK_KAPI int kk_gemm_pack_weight_scaled(const uint16_t* weight, uint32_t M, uint32_t K,
+    const uint16_t* col_scale, uint16_t* packed, void* stream);
 
 KK_KAPI uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N);
 KK_KAPI int kk_gemm(const kk_gemm_desc* desc, void* stream);

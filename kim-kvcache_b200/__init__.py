@@ -281,7 +281,8 @@ class GemmDesc(C.Structure):
                 ("pools", KvPools), ("layer", C.c_uint32), ("q_rows", C.c_uint32),
                 ("kv_rows", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
                 ("tokens", C.c_void_p), ("argmax_workspace", C.c_void_p),
-                ("weight_layout", C.c_uint32)]
+                ("weight_layout", C.c_uint32), ("norm_input", C.c_void_p),
+                ("norm_stride", C.c_uint32), ("norm_eps", C.c_float)]
 
 
 _VP = C.c_void_p
@@ -307,6 +308,7 @@ KERNEL_SIGNATURES = {
     "gemm": (_I, [C.POINTER(GemmDesc), _VP]),
     "gemm_packed_bytes": (_U64, [_U32, _U32]),
     "gemm_pack_weight": (_I, [_VP, _U32, _U32, _VP, _VP]),
+    "gemm_pack_weight_scaled": (_I, [_VP, _U32, _U32, _VP, _VP, _VP]),
     "kv_promote": (_I, [C.POINTER(KvPools), C.POINTER(_U32), _U32, _VP]),
     "fill_fp16": (_I, [_VP, _U64, _U64, C.c_float, _VP]),
     "device_status": (_I, [_VP]),

@@ -90,6 +90,9 @@ struct GemmArgs {
     std::uint32_t N;
     std::uint32_t split;
     std::uint32_t kb_total;
+    __half const* norm_x;           // RMS-normalise the output by the rows of norm_x (or null)
+    std::uint32_t norm_stride;
+    float norm_eps;
     EpiArgs epi;
 };
 
@@ -127,6 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint64_t* accum = empty + kStages;
     std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(accum + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 4);
+    float* rnorm = reinterpret_cast<float*>(flag + 4);  // [BN] per-column RMS factors
 
     std::uint32_t const tid = threadIdx.x;
     std::uint32_t const warp = tid / 32;
@@ -219,6 +223,32 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     // loop) until their lane 0 has finished its role.
     __syncwarp();
     pdl_wait();
+    if (args.norm_x != nullptr && warp >= 2) {
+        // While the tile streams: RMSNorm factors of this CTA's output columns,
+        // r[n] = rsqrt(mean_k x[n][k]^2 + eps), one warp per column.
+        std::uint32_t const c0n = rank * args.N / S;
+        std::uint32_t const c1n = (rank + 1) * args.N / S;
+        for (std::uint32_t n = c0n + (warp - 2u); n < c1n; n += 2u) {
+            __half const* xr = args.norm_x + std::uint64_t(n) * args.norm_stride;
+            float sum = 0.f;
+            for (std::uint32_t k = lane * 8u; k < args.K; k += 256u) {
+                uint4 const raw = *reinterpret_cast<uint4 const*>(xr + k);
+                __half const* h = reinterpret_cast<__half const*>(&raw);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    float const f = __half2float(h[e]);
+                    sum += f * f;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            }
+            if (lane == 0) {
+                rnorm[n - c0n] = rsqrtf(sum / static_cast<float>(args.K) + args.norm_eps);
+            }
+        }
+    }
     bool const have_acc = mbar_wait(accum, 0, &g_gemm_status);
     tc_fence_after();
 
@@ -282,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     }
                 }
                 if (n + j < n1) {
-                    red[(n + j - n0) * kBM + row] = acc;
+                    red[(n + j - n0) * kBM + row] = args.norm_x != nullptr ? acc * rnorm[n + j - n0] : acc;
                 }
             }
         }
@@ -456,7 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
 // r * 128 + ((c ^ (r % 8)) * 16), the 128-byte swizzle the MMA descriptors
 // expect; rows >= M and columns >= K are zero. One thread per 16-byte chunk.
 __global__ void pack_weight_kernel(std::uint16_t const* __restrict__ w, std::uint32_t M,
-    std::uint32_t K, std::uint32_t kb_total, std::uint64_t chunks, uint4* __restrict__ out)
+    std::uint32_t K, std::uint32_t kb_total, std::uint64_t chunks, uint4* __restrict__ out,
+    __half const* __restrict__ col_scale)
 {
     std::uint64_t const i = std::uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= chunks) {
@@ -473,6 +504,16 @@ __global__ void pack_weight_kernel(std::uint16_t const* __restrict__ w, std::uin
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < M && col < K) {
         v = *reinterpret_cast<uint4 const*>(w + row * K + col);
+        if (col_scale != nullptr) {
+            // W[m][k] * g[k], rounded once to FP16 (an RMSNorm weight folded in).
+            uint4 const gs = *reinterpret_cast<uint4 const*>(col_scale + col);
+            __half* hv = reinterpret_cast<__half*>(&v);
+            __half const* hg = reinterpret_cast<__half const*>(&gs);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                hv[e] = __float2half_rn(__half2float(hv[e]) * __half2float(hg[e]));
+            }
+        }
     }
     out[block * 1024u + r * 8u + (c ^ (r & 7u))] = v;
 }
@@ -572,6 +613,15 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
     args.K = d->K;
     args.N = d->N;
     args.kb_total = (d->K + kBK - 1) / kBK;
+    if (d->norm_input != nullptr) {
+        if (d->norm_stride < d->K || d->norm_stride % 8 != 0 || d->K % 8 != 0
+            || (reinterpret_cast<std::uintptr_t>(d->norm_input) & 15u) != 0 || !(d->norm_eps >= 0.f)) {
+            return KK_EINVAL;
+        }
+        args.norm_x = reinterpret_cast<__half const*>(d->norm_input);
+        args.norm_stride = d->norm_stride;
+        args.norm_eps = d->norm_eps;
+    }
     EpiArgs& e = args.epi;
     e.kind = d->epilogue;
     e.out = d->out;
@@ -644,16 +694,24 @@ uint64_t kk_gemm_packed_bytes(uint32_t M, uint32_t K)
 int kk_gemm_pack_weight(const uint16_t* weight, uint32_t M, uint32_t K, uint16_t* packed,
     void* stream)
 {
+    return kk_gemm_pack_weight_scaled(weight, M, K, nullptr, packed, stream);
+}
+
+int kk_gemm_pack_weight_scaled(const uint16_t* weight, uint32_t M, uint32_t K,
+    const uint16_t* col_scale, uint16_t* packed, void* stream)
+{
     if (weight == nullptr || packed == nullptr || M == 0 || K == 0 || K % 8 != 0
         || (reinterpret_cast<std::uintptr_t>(weight) & 15u) != 0
-        || (reinterpret_cast<std::uintptr_t>(packed) & 15u) != 0) {
+        || (reinterpret_cast<std::uintptr_t>(packed) & 15u) != 0
+        || (reinterpret_cast<std::uintptr_t>(col_scale) & 15u) != 0) {
         return KK_EINVAL;
     }
     std::uint32_t const kb = (K + kk::kBK - 1) / kk::kBK;
     std::uint64_t const chunks = kk_gemm_packed_bytes(M, K) / 16u;
     std::uint64_t const blocks = (chunks + 255u) / 256u;
     kk::pack_weight_kernel<<<static_cast<unsigned>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        weight, M, K, kb, chunks, reinterpret_cast<uint4*>(packed));
+        weight, M, K, kb, chunks, reinterpret_cast<uint4*>(packed),
+        reinterpret_cast<__half const*>(col_scale));
     return static_cast<int>(cudaGetLastError());
 }
 

@@ -193,9 +193,18 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         d.weight_layout = KK_W_PACKED;
         return d;
     };
+    // RMSNorm fused into the projection: rows of the residual stream are
+    // normalised inside the GEMM (the norm weight is folded into W).
+    auto normedInput = [&](kk_gemm_desc d) {
+        d.norm_input = hidden;
+        d.norm_stride = c.hidden_size;
+        d.norm_eps = c.rms_norm_epsilon;
+        return d;
+    };
     for (std::uint32_t l = 0; l < c.layer_count; ++l) {
         LayerWeights const& w = layers[l];
-        kk_gemm_desc d = base(w.w_qkv, qkv_rows, c.hidden_size, normed, KK_EPI_QKV_ROPE, q, c.hidden_size);
+        kk_gemm_desc d = normedInput(base(w.w_qkv, qkv_rows, c.hidden_size, hidden, KK_EPI_QKV_ROPE, q,
+            c.hidden_size));
         d.positions = stepDev<std::uint32_t>(off_positions);
         d.slots = stepDev<kk_kv_slot>(off_slots);
         d.pools = pools;
@@ -210,14 +219,15 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         out.down.emplace_back();
         if (!make(d, out.qkv.back())
             || !make(base(w.w_o, c.hidden_size, c.hidden_size, attn, KK_EPI_RESIDUAL, hidden, c.hidden_size), out.o.back())
-            || !make(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, normed, KK_EPI_SILU_PAIRS, act,
-                          c.intermediate_size), out.gu.back())
+            || !make(normedInput(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, hidden,
+                          KK_EPI_SILU_PAIRS, act, c.intermediate_size)), out.gu.back())
             || !make(base(w.w_down, c.hidden_size, c.intermediate_size, act, KK_EPI_RESIDUAL, hidden,
                           c.hidden_size), out.down.back())) {
             return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "projection plan rejected");
         }
     }
-    kk_gemm_desc lm = base(lm_head, c.vocabulary_size, c.hidden_size, normed, KK_EPI_ARGMAX, nullptr, 0);
+    kk_gemm_desc lm = normedInput(base(lm_head, c.vocabulary_size, c.hidden_size, hidden, KK_EPI_ARGMAX,
+        nullptr, 0));
     lm.tokens = out_tokens;
     lm.argmax_workspace = argmax_ws;
     kk_gemm_desc lm_logits = lm;
@@ -248,8 +258,10 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
                       stepDev<std::uint32_t>(off_counts) + 1, batch, stream), "copy-on-write");
         if (!s.ok()) return s;
     }
+    // Embedding gather starts the residual stream (the first projection
+    // normalises its rows itself; `normed` is written but not read).
     s = check(kk_embed_rmsnorm(embed, stepDev<std::uint32_t>(off_tokens), layers[0].in_norm, hidden,
-                  normed, batch, H, c.rms_norm_epsilon, stream), "embedding + rmsnorm");
+                  normed, batch, H, c.rms_norm_epsilon, stream), "embedding");
     if (!s.ok()) return s;
     std::unordered_map<std::uint32_t, std::size_t> capture;
     if (debug != nullptr) {
@@ -266,8 +278,6 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
                      stepDev<kk_attn_item>(off_items), stepDev<std::uint32_t>(off_counts), max_items,
                      q, qrow, attn, qrow, scale, attn_ws, attn_ws_bytes, stream), "paged attention")).ok()
             || !(s = check(kk::gemmRun(*p.o[l], stream), "output projection")).ok()
-            || !(s = check(kk_rmsnorm(hidden, w.post_norm, normed, batch, H, c.rms_norm_epsilon, stream),
-                     "post-attention rmsnorm")).ok()
             || !(s = check(kk::gemmRun(*p.gu[l], stream), "gate/up projection")).ok()
             || !(s = check(kk::gemmRun(*p.down[l], stream), "down projection")).ok()) {
             return s;
@@ -279,13 +289,14 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
                     cudaMemcpyDeviceToHost, stream);
             }
         }
-        std::uint16_t const* next_norm = l + 1 < c.layer_count ? layers[l + 1].in_norm : final_norm;
-        s = check(kk_rmsnorm(hidden, next_norm, normed, batch, H, c.rms_norm_epsilon, stream), "rmsnorm");
-        if (!s.ok()) return s;
     }
     s = check(kk::gemmRun(want_logits ? *p.lm_head_logits : *p.lm_head, stream), "lm head + argmax");
     if (!s.ok()) return s;
     if (debug != nullptr) {
+        // The decode step never materialises the final normalised rows (the
+        // LM head normalises internally); the debug capture computes them.
+        s = check(kk_rmsnorm(hidden, final_norm, normed, batch, H, c.rms_norm_epsilon, stream), "final rmsnorm");
+        if (!s.ok()) return s;
         cudaMemcpyAsync(debug->final_hidden_state.data(), normed, H * 2, cudaMemcpyDeviceToHost, stream);
     }
     last_launches = launches;
@@ -710,18 +721,26 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     // move the embedding table and norm weights into a compact row-major
     // allocation, and release the upload buffer.
     {
+        // The RMSNorm weight that precedes a projection is folded into its
+        // columns (qkv: input norm, gate/up: post-attention norm, LM head:
+        // final norm); the GEMM applies the per-row rsqrt factor itself.
         struct PackJob {
             std::uint16_t const* src;
             std::uint32_t M, K;
             std::uint16_t const** dst;
+            std::uint16_t const* col_scale;
         };
         std::vector<PackJob> jobs;
-        jobs.push_back({im->lm_head, static_cast<std::uint32_t>(V), static_cast<std::uint32_t>(H), &im->lm_head});
+        jobs.push_back({im->lm_head, static_cast<std::uint32_t>(V), static_cast<std::uint32_t>(H), &im->lm_head,
+            im->final_norm});
         for (LayerWeights& lw : im->layers) {
-            jobs.push_back({lw.w_qkv, static_cast<std::uint32_t>(qkv_rows), static_cast<std::uint32_t>(H), &lw.w_qkv});
-            jobs.push_back({lw.w_o, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(H), &lw.w_o});
-            jobs.push_back({lw.w_gu, static_cast<std::uint32_t>(2 * I), static_cast<std::uint32_t>(H), &lw.w_gu});
-            jobs.push_back({lw.w_down, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(I), &lw.w_down});
+            jobs.push_back({lw.w_qkv, static_cast<std::uint32_t>(qkv_rows), static_cast<std::uint32_t>(H), &lw.w_qkv,
+                lw.in_norm});
+            jobs.push_back({lw.w_o, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(H), &lw.w_o, nullptr});
+            jobs.push_back({lw.w_gu, static_cast<std::uint32_t>(2 * I), static_cast<std::uint32_t>(H), &lw.w_gu,
+                lw.post_norm});
+            jobs.push_back({lw.w_down, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(I), &lw.w_down,
+                nullptr});
         }
         std::uint64_t packed_bytes = 0;
         for (PackJob const& j : jobs) {
@@ -741,7 +760,7 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         std::uint64_t at = 0;
         for (PackJob const& j : jobs) {
             std::uint16_t* dst = reinterpret_cast<std::uint16_t*>(im->packed + at);
-            int const rc = kk_gemm_pack_weight(j.src, j.M, j.K, dst, nullptr);
+            int const rc = kk_gemm_pack_weight_scaled(j.src, j.M, j.K, j.col_scale, dst, nullptr);
             if (rc != 0) {
                 cudaFree(small);
                 out.status = failure(CudaModelRunnerError::AllocationFailed, rc, "weight packing");

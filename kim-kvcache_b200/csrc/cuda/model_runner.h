@@ -6,11 +6,12 @@
 // optional debug capture; the GenerationModelRunner SPI.
 //
 // Execution: one model batch (all lanes) runs as one fused device step:
-// COW copies -> embedding+RMSNorm -> per layer [QKV projection with RoPE and
-// KV-page write fused in its epilogue, paged attention over all lanes, O
-// projection + residual, RMSNorm, gate/up projection + SiLU gate, down
-// projection + residual, RMSNorm] -> LM head + greedy argmax -> token ids to
-// host. Host work per step: reserve each lane, one upload of the step inputs
+// COW copies -> embedding -> per layer [QKV projection (input RMSNorm fused,
+// RoPE and KV-page write in its epilogue), paged attention over all lanes, O
+// projection + residual, gate/up projection (post-attention RMSNorm fused) +
+// SiLU gate, down projection + residual] -> LM head (final RMSNorm fused) +
+// greedy argmax -> token ids to host. The norm weights are folded into the
+// packed projection weights; each projection computes its rows' rsqrt factor. Host work per step: reserve each lane, one upload of the step inputs
 // (tokens, positions, write slots, page descriptors, attention work list),
 // one stream synchronisation, commit each lane. With graphs enabled the
 // device part is replayed from a CUDA graph captured per batch size.

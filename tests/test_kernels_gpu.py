@@ -177,6 +177,50 @@ def test_gemm_argmax_matches_numpy(kk, K, V, N, wlayout):
     torch.testing.assert_close(logits, x[:N].float() @ w.float().T, atol=2e-3, rtol=1e-3)
 
 
+@pytest.mark.parametrize("M,Kd,N,epi", [(2560, 2048, 32, "f32"), (11264, 2048, 7, "silu"),
+                                         (32000, 2048, 4, "argmax"), (300, 512, 33, "f32")])
+def test_gemm_fused_rmsnorm_matches_torch(kk, K, M, Kd, N, epi):
+    """norm_input + column-scaled packing = RMSNorm(x) (weight g) followed by
+    the projection, in one kernel."""
+    g = torch.Generator().manual_seed(M + N)
+    w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
+    gw = (1.0 + 0.1 * torch.randn(Kd, generator=g)).half().cuda()
+    x = (torch.randn(64, Kd, generator=g) * 3).half().cuda()
+    packed = torch.empty(K["gemm_packed_bytes"](M, Kd) // 2, dtype=torch.half, device="cuda")
+    assert K["gemm_pack_weight_scaled"](p(w), M, Kd, p(gw), p(packed), None) == 0
+    eps = 1e-5
+    xf = x[:N].float()
+    normed = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * gw.float()).half().float()
+    ref = normed @ w.float().T
+    d = kk.GemmDesc()
+    d.weight, d.weight_layout, d.M, d.K = p(packed), kk.W_PACKED, M, Kd
+    d.x, d.N, d.x_stride, d.x_rows = p(x), N, Kd, 64
+    d.norm_input, d.norm_stride, d.norm_eps = p(x), Kd, eps
+    if epi == "f32":
+        out = torch.zeros(N, M, device="cuda")
+        d.epilogue, d.out, d.out_stride = kk.EPI_STORE_F32, p(out), M
+        assert K["gemm"](C.byref(d), None) == 0
+        sync_ok(K)
+        torch.testing.assert_close(out, ref, atol=3e-2, rtol=2e-2)
+    elif epi == "silu":
+        out = torch.zeros(N, M // 2, dtype=torch.half, device="cuda")
+        d.epilogue, d.out, d.out_stride = kk.EPI_SILU_PAIRS, p(out), M // 2
+        assert K["gemm"](C.byref(d), None) == 0
+        sync_ok(K)
+        gate, up = ref[:, 0::2].half().float(), ref[:, 1::2].half().float()
+        torch.testing.assert_close(out.float(), (gate / (1 + torch.exp(-gate)) * up), atol=3e-2, rtol=2e-2)
+    else:
+        tokens = torch.zeros(N, dtype=torch.int32, device="cuda")
+        ws = torch.zeros(K["argmax_workspace_bytes"](M, N), dtype=torch.uint8, device="cuda")
+        logits = torch.zeros(N, M, device="cuda")
+        d.epilogue, d.out, d.out_stride = kk.EPI_ARGMAX, p(logits), M
+        d.tokens, d.argmax_workspace = p(tokens), p(ws)
+        assert K["gemm"](C.byref(d), None) == 0
+        sync_ok(K)
+        torch.testing.assert_close(logits, ref, atol=3e-2, rtol=2e-2)
+        assert tokens.cpu().tolist() == logits.argmax(-1).int().cpu().tolist()
+
+
 @pytest.mark.parametrize("M,Kd", [(128, 64), (300, 1000), (32000, 256), (2560, 2048)])
 def test_gemm_pack_weight_layout_is_exact(kk, K, M, Kd):
     """Tile (t, b) holds rows t*128.., columns b*64.. with 16-byte chunk c of row r
