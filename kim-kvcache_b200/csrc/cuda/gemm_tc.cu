@@ -48,13 +48,14 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
-constexpr std::size_t kCtaSmemBudget = 113 * 1024;   // two CTAs per SM
-
-// Ring depth: as many W+X stages as fit two CTAs per SM.
+// Three W+X stages: about 60 KB at N <= 32, so three CTAs fit on an SM and
+// the next kernel's CTAs are resident (prefetching their weights under
+// programmatic dependent launch) while this kernel drains. The epilogue's
+// partial and reduced tiles reuse the ring (at most 66 KB, BN = 64).
 template <int BN>
 constexpr int stagesFor()
 {
-    return static_cast<int>((kCtaSmemBudget - 2048) / (kTileWBytes + BN * 128));
+    return 3;
 }
 
 struct EpiArgs {
