@@ -48,14 +48,15 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
-// Three W+X stages: about 60 KB at N <= 32, so three CTAs fit on an SM and
-// the next kernel's CTAs are resident (prefetching their weights under
-// programmatic dependent launch) while this kernel drains. The epilogue's
+// Four W+X stages: about 82 KB at N <= 32, so an attention CTA or a second
+// kernel's projection CTA fits beside this one on an SM and can start (and
+// prefetch its weights under programmatic dependent launch) while this
+// kernel drains. Measured on the decode step, 4 beats 3 and 5. The epilogue's
 // partial and reduced tiles reuse the ring (at most 66 KB, BN = 64).
 template <int BN>
 constexpr int stagesFor()
 {
-    return 3;
+    return 4;
 }
 
 struct EpiArgs {
