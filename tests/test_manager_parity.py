@@ -188,7 +188,10 @@ def test_promotion_heavy_streams_match_reference(kk, kk_lib, ref_lib, seed):
 def test_prefill_promote_decode_sequence(kk, kk_lib, ref_lib):
     """The config-1/config-4 table build: append a body, seal, promote every
     aligned 64-token run, then decode one token at a time with forks."""
-    pair = Pair(kk, kk_lib, ref_lib, 4096, 128)
+    prefill_promote_decode(Pair(kk, kk_lib, ref_lib, 4096, 128))
+
+
+def prefill_promote_decode(pair: Pair):
     for rid, ctx in [(1, 17), (2, 100), (3, 513), (4, 2000)]:
         pair.same("create", rid)
         pair.same("append", rid, ctx)

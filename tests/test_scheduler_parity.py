@@ -12,12 +12,13 @@ import random
 import pytest
 
 
+def bind_scheduler(kk, lib, prefix):
+    return kk.bind(lib, prefix, {k: v for k, v in kk.RUNTIME_SIGNATURES.items()
+                                 if k.startswith(("sched_", "fake_", "generate"))})
+
+
 def both(kk, kk_lib, ref_lib):
-    return [kk.bind(kk_lib, "kkrt_", kk.RUNTIME_SIGNATURES.__class__(
-                {k: v for k, v in kk.RUNTIME_SIGNATURES.items()
-                 if k.startswith(("sched_", "fake_", "generate"))})),
-            kk.bind(ref_lib, "kref_", {k: v for k, v in kk.RUNTIME_SIGNATURES.items()
-                                       if k.startswith(("sched_", "fake_", "generate"))})]
+    return [bind_scheduler(kk, kk_lib, "kkrt_"), bind_scheduler(kk, ref_lib, "kref_")]
 
 
 def batch_log(f, runner):
@@ -72,32 +73,7 @@ def check(kk, kk_lib, ref_lib, *args, **kw):
     return ra
 
 
-def test_fifo_chunked_prefill_and_decode(kk, kk_lib, ref_lib):
-    cfg = dict(max_active=4, max_tokens=16, max_kv=100000, chunk=4)
-    reqs = [(1, [3, 4, 6, 7, 8, 9, 10], 5, -1), (2, [11] * 12, 3, -1), (3, [12], 8, -1),
-            (4, [13, 14], 1, -1)]
-    admissions, iters, terms, log = check(kk, kk_lib, ref_lib, cfg, reqs, [])
-    assert admissions == [0, 0, 0, 0]
-    assert {t[0] for t in terms} == {1, 2, 3, 4}
-
-
-def test_admission_gates_and_late_join(kk, kk_lib, ref_lib):
-    cfg = dict(max_active=2, max_tokens=6, max_kv=40, chunk=3)
-    reqs = [(1, [3] * 10, 10, -1), (2, [4] * 20, 5, -1), (3, [5] * 30, 30, -1), (0, [1], 1, -1),
-            (1, [3], 1, -1), (7, [], 1, -1), (8, [96, 97], 1, -1)]
-    actions = [("submit", 3, (9, [6, 7], 4, -1)), ("submit", 6, (10, [8], 3, -1))]
-    check(kk, kk_lib, ref_lib, cfg, reqs, actions)
-
-
-def test_cancel_stop_and_model_failure(kk, kk_lib, ref_lib):
-    cfg = dict(max_active=8, max_tokens=8, max_kv=10 ** 6, chunk=2)
-    reqs = [(i, [i + 3] * (i % 5 + 1), 6, -1) for i in range(1, 9)]
-    check(kk, kk_lib, ref_lib, cfg, reqs, [("cancel", 2, 3), ("cancel", 4, 6)], fail=5)
-    check(kk, kk_lib, ref_lib, cfg, reqs, [("stop", 3, None)])
-
-
-@pytest.mark.parametrize("seed", range(8))
-def test_random_workloads(kk, kk_lib, ref_lib, seed):
+def _random_scenario(seed):
     rng = random.Random(seed)
     cfg = dict(max_active=rng.randint(1, 10), max_tokens=rng.randint(1, 40),
                max_kv=rng.randint(50, 2000), chunk=rng.randint(1, 16))
@@ -106,8 +82,40 @@ def test_random_workloads(kk, kk_lib, ref_lib, seed):
         reqs.append((rid, [rng.randrange(0, 97) for _ in range(rng.randint(1, 40))],
                      rng.randint(1, 20), rng.choice([-1, -1, 5, 96, 200])))
     actions = [("cancel", rng.randint(0, 20), rng.randint(1, 14)) for _ in range(rng.randint(0, 3))]
-    check(kk, kk_lib, ref_lib, cfg, reqs, actions, vocab=97, max_batch=rng.randint(1, 8),
-          eos=rng.choice([5, 60]), fail=rng.choice([0, 0, 3]))
+    return (cfg, reqs, actions), dict(vocab=97, max_batch=rng.randint(1, 8), eos=rng.choice([5, 60]),
+                                      fail=rng.choice([0, 0, 3]))
+
+
+_CANCEL_CFG = dict(max_active=8, max_tokens=8, max_kv=10 ** 6, chunk=2)
+_CANCEL_REQS = [(i, [i + 3] * (i % 5 + 1), 6, -1) for i in range(1, 9)]
+
+# (name, positional args after `fns`, keyword args) of every scheduler
+# scenario; shared with the golden-fixture generator (tests/golden).
+SCENARIOS = [
+    ("fifo_chunked_prefill", (dict(max_active=4, max_tokens=16, max_kv=100000, chunk=4),
+                              [(1, [3, 4, 6, 7, 8, 9, 10], 5, -1), (2, [11] * 12, 3, -1), (3, [12], 8, -1),
+                               (4, [13, 14], 1, -1)], []), {}),
+    ("admission_gates_late_join", (dict(max_active=2, max_tokens=6, max_kv=40, chunk=3),
+                                   [(1, [3] * 10, 10, -1), (2, [4] * 20, 5, -1), (3, [5] * 30, 30, -1),
+                                    (0, [1], 1, -1), (1, [3], 1, -1), (7, [], 1, -1), (8, [96, 97], 1, -1)],
+                                   [("submit", 3, (9, [6, 7], 4, -1)), ("submit", 6, (10, [8], 3, -1))]), {}),
+    ("cancel_and_model_failure", (_CANCEL_CFG, _CANCEL_REQS, [("cancel", 2, 3), ("cancel", 4, 6)]),
+     dict(fail=5)),
+    ("stop", (_CANCEL_CFG, _CANCEL_REQS, [("stop", 3, None)]), {}),
+] + [(f"random_{seed}",) + _random_scenario(seed) for seed in range(8)]
+
+
+def test_fifo_chunked_prefill_and_decode(kk, kk_lib, ref_lib):
+    _, args, kw = SCENARIOS[0]
+    admissions, iters, terms, log = check(kk, kk_lib, ref_lib, *args, **kw)
+    assert admissions == [0, 0, 0, 0]
+    assert {t[0] for t in terms} == {1, 2, 3, 4}
+
+
+@pytest.mark.parametrize("index", range(1, len(SCENARIOS)), ids=[s[0] for s in SCENARIOS[1:]])
+def test_scenarios_match_reference(kk, kk_lib, ref_lib, index):
+    _, args, kw = SCENARIOS[index]
+    check(kk, kk_lib, ref_lib, *args, **kw)
 
 
 def test_single_request_generation(kk, kk_lib, ref_lib):
