@@ -487,6 +487,36 @@ def run_kernel_only(args):
             state["i"] += 1
             return K["gemm"](C.byref(d), C.c_void_p(torch.cuda.current_stream().cuda_stream))
         label.update(shape=args.shape, layout=args.layout, M=M, K=Kd, N=N, weight_copies=copies)
+    elif args.kernel_only == "gather":
+        # K6: one 4096-token sequence (extent body + micro tail) of the
+        # 22-layer TinyLlama KV gathered into a contiguous tensor.
+        L, hkv, D, T = 22, 4, 64, 4096 + 40
+        n_ext, n_mic = T // 64, (T % 64 + 7) // 8
+        row = hkv * D
+        micro = torch.empty(n_mic * 2 * L * 2 * 8 * row, dtype=torch.int16, device="cuda")
+        extent = torch.empty(n_ext * 2 * L * 2 * 64 * row, dtype=torch.int16, device="cuda")
+        K["fill_fp16"](C.c_void_p(micro.data_ptr()), micro.numel(), 1, 0.35, sptr)
+        K["fill_fp16"](C.c_void_p(extent.data_ptr()), extent.numel(), 2, 0.35, sptr)
+        pools = kk.KvPools(micro.data_ptr(), extent.data_ptr(), n_mic * 2, n_ext * 2, L, hkv, D, 0)
+        rng = random.Random(SEED)
+        es, ms = rng.sample(range(n_ext * 2), n_ext), rng.sample(range(n_mic * 2), n_mic)
+        descs_list, t = [], 0
+        for slot in es:
+            descs_list.append(kk.PageDesc(slot, t, 64, 1, 0, 0))
+            t += 64
+        for slot in ms:
+            n = min(8, T - t)
+            descs_list.append(kk.PageDesc(slot, t, n, 0, 0, 0))
+            t += n
+        descs = (kk.PageDesc * len(descs_list))(*descs_list)
+        dd = torch.frombuffer(bytearray(bytes(descs)), dtype=torch.uint8).cuda()
+        out = torch.empty(L * 2 * T * row, dtype=torch.int16, device="cuda")
+
+        def launch():
+            return K["kv_gather"](C.byref(pools), dd.data_ptr(), len(descs_list), T, out.data_ptr(),
+                                  C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        nbytes = 2 * L * 2 * T * row * 2  # read + write
+        label.update(tokens=T, descriptors=len(descs_list), note="bytes = read + write")
     else:
         variant = {"auto": kk.ATTN_AUTO, "direct": kk.ATTN_DIRECT, "tma": kk.ATTN_TMA}[args.variant]
         assert K["attention_set_variant"](variant) == 0
@@ -575,7 +605,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-only", choices=["attention", "gemm"], default=None,
+    ap.add_argument("--kernel-only", choices=["attention", "gemm", "gather"], default=None,
                     help="time one hot kernel on a standalone case (profiling)")
     ap.add_argument("--shape", default="gu", choices=sorted(GEMM_SHAPES),
                     help="--kernel-only gemm: projection shape")

@@ -197,6 +197,22 @@ KK_KAPI int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin,
  * launchPromotion, src/cuda/kv/page_kernels.cu:129-182). */
 KK_KAPI int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots_host,
     uint32_t extent_slot, void* stream);
+/* K6 data path between pages and a contiguous KV tensor
+ * [layer][K|V][token][head][dim] fp16 (16-byte aligned).
+ * kk_kv_gather replaces gatherAsync / launchGather (src/cuda/kv/gather.cpp:9-107,
+ * page_kernels.cu:184-242): every descriptor's valid tokens are copied to
+ * out at their logical positions; tokens of [0, total_tokens) not covered by
+ * any descriptor are left untouched. Descriptors must not overlap.
+ * kk_kv_scatter is the inverse for appended tokens (appendAsync segment
+ * copies, launchAppendTokens, page_kernels.cu:77-127): `in` holds the
+ * [layer][K|V][token_count][head][dim] values of logical tokens
+ * [first_token, first_token + token_count), written into the pages that the
+ * descriptors map there. One CTA per (descriptor, layer, K|V). A descriptor
+ * outside its pool is skipped and reported by kk_device_status. */
+KK_KAPI int kk_kv_gather(const kk_kv_pools* pools, const kk_page_desc* descs, uint32_t num_descs,
+    uint32_t total_tokens, uint16_t* out, void* stream);
+KK_KAPI int kk_kv_scatter(const kk_kv_pools* pools, const kk_page_desc* descs, uint32_t num_descs,
+    uint32_t first_token, uint32_t token_count, const uint16_t* in, void* stream);
 /* Deterministic pseudo-random FP16 fill (uniform in [-scale, scale)) for
  * synthetic KV pages and test tensors; same (seed, index) -> same value. */
 KK_KAPI int kk_fill_fp16(uint16_t* data, uint64_t count, uint64_t seed, float scale,

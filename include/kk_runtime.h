@@ -185,6 +185,11 @@ KK_API int kkrt_backend_append(void* backend, uint64_t request_id, uint32_t toke
 KK_API int kkrt_backend_seal(void* backend, uint64_t request_id);
 KK_API int kkrt_backend_promote(void* backend, uint64_t request_id, uint32_t logical_begin,
     void* stream);
+/* K6 gather (CudaKvCache::gather, src/cuda/kv/gather.cpp:9-107): the
+ * request's committed KV as one contiguous [layer][K|V][token][head][dim] fp16
+ * tensor at device_output (16-byte aligned, committed-token-count tokens),
+ * under a read lease; waits for the copy. Returns EngineKvError. */
+KK_API int kkrt_backend_gather(void* backend, uint64_t request_id, void* device_output, void* stream);
 
 /* ---- per-layer token transactions (engine_kv.h:255-351) ---- */
 /* reserveToken: returns a transaction handle or NULL; *status = EngineKvError. */

@@ -310,6 +310,8 @@ KERNEL_SIGNATURES = {
     "gemm_pack_weight": (_I, [_VP, _U32, _U32, _VP, _VP]),
     "gemm_pack_weight_scaled": (_I, [_VP, _U32, _U32, _VP, _VP, _VP]),
     "kv_promote": (_I, [C.POINTER(KvPools), C.POINTER(_U32), _U32, _VP]),
+    "kv_gather": (_I, [C.POINTER(KvPools), _VP, _U32, _U32, _VP, _VP]),
+    "kv_scatter": (_I, [C.POINTER(KvPools), _VP, _U32, _U32, _U32, _VP, _VP]),
     "fill_fp16": (_I, [_VP, _U64, _U64, C.c_float, _VP]),
     "device_status": (_I, [_VP]),
     "set_pdl": (None, [_I]),
@@ -366,6 +368,7 @@ RUNTIME_SIGNATURES = {
     "backend_append": (_I, [_VP, _U64, _U32]),
     "backend_seal": (_I, [_VP, _U64]),
     "backend_promote": (_I, [_VP, _U64, _U32, _VP]),
+    "backend_gather": (_I, [_VP, _U64, _VP, _VP]),
     "txn_reserve": (_VP, [_VP, _U64, _U32, _VP, C.POINTER(_I)]),
     "txn_write_layer": (_I, [_VP, _U32, _VP, _VP]),
     "txn_attend_layer": (_I, [_VP, _U32, _VP, _VP, _VP, _U64, _F]),

@@ -201,6 +201,11 @@ int kkrt_backend_promote(void* b, uint64_t id, uint32_t begin, void* stream)
     return int(cudaBackendPromote(*KV(b), id, begin, stream).error);
 }
 
+int kkrt_backend_gather(void* b, uint64_t id, void* device_output, void* stream)
+{
+    return int(cudaBackendGather(*KV(b), id, device_output, stream).error);
+}
+
 void* kkrt_txn_reserve(void* b, uint64_t id, uint32_t expected, void* stream, int* status)
 {
     TokenReserveResult r = KV(b)->reserveToken(ReserveTokenRequest{id, expected, stream});

@@ -869,6 +869,58 @@ EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::u
     return mapMetadata(st->mgr.commitPromotion(prepared.promotion_id));
 }
 
+EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id, void* device_output,
+    CudaStream stream)
+{
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr || device_output == nullptr) {
+        return {EngineKvError::InvalidArgument};
+    }
+    State* st = b->state();
+    std::vector<kk_page_desc> descs;
+    std::uint32_t tokens = 0;
+    PageLeaseAcquireResult lease;
+    {
+        std::lock_guard<std::mutex> lock(st->mutex);
+        lease = st->mgr.acquireRequestReadLease(id);
+        if (!lease.ok()) {
+            return mapMetadata(lease.error);
+        }
+        std::optional<BlockTable> const table = st->mgr.blockTable(id);
+        if (table) {
+            tokens = table->tokenCount();
+            for (MappingEntry const& e : table->entries()) {
+                descs.push_back(kk_page_desc{e.handle.slot, e.logical_token_begin, e.valid_tokens,
+                    static_cast<std::uint8_t>(e.kind), 0, 0});
+            }
+        }
+    }
+    cudaStream_t const s = static_cast<cudaStream_t>(stream);
+    int rc = 0;
+    if (!descs.empty()) {
+        void* d_descs = nullptr;
+        std::size_t const bytes = descs.size() * sizeof(kk_page_desc);
+        rc = static_cast<int>(cudaMallocAsync(&d_descs, bytes, s));
+        if (rc == 0) {
+            rc = static_cast<int>(cudaMemcpyAsync(d_descs, descs.data(), bytes, cudaMemcpyHostToDevice, s));
+            if (rc == 0) {
+                rc = kk_kv_gather(&st->storage.pools, static_cast<kk_page_desc const*>(d_descs),
+                    static_cast<std::uint32_t>(descs.size()), tokens, static_cast<std::uint16_t*>(device_output), s);
+            }
+            cudaFreeAsync(d_descs, s);
+        }
+        if (rc == 0) {
+            rc = static_cast<int>(cudaStreamSynchronize(s));
+        }
+    }
+    std::lock_guard<std::mutex> lock(st->mutex);
+    static_cast<void>(st->mgr.releasePageLease(lease.lease_id));
+    if (descs.empty()) {
+        return {EngineKvError::InvalidArgument};  // nothing committed to gather
+    }
+    return rc == 0 ? EngineKvStatus{} : EngineKvStatus{EngineKvError::ExecutionFailed};
+}
+
 std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
     std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream)
 {

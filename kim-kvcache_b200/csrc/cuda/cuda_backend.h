@@ -84,6 +84,13 @@ void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept;
 // src/cuda/kv/cache.cpp:172-229).
 [[nodiscard]] EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id,
     std::uint32_t logical_begin, CudaStream stream);
+// K6 gather (reference CudaKvCache::gather / CudaKvStorage::gatherAsync,
+// src/cuda/kv/gather.cpp:9-107): the request's committed KV as one
+// contiguous [layer][K|V][token][head][dim] FP16 tensor at device_output
+// (tokenCount() tokens). Pages are pinned by a read lease for the copy; the
+// call waits for it.
+[[nodiscard]] EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id,
+    void* device_output, CudaStream stream);
 // The same for several (request, logical_begin) runs with one device wait:
 // every promotion that prepares is copied, then all are committed (or rolled
 // back if the copies failed). Runs that cannot be promoted (not 8 sealed,

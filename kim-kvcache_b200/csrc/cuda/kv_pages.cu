@@ -138,6 +138,55 @@ __global__ void kv_promote_kernel(PoolView v, PromoteSlots src, std::uint32_t ex
     }
 }
 
+// K6 gather / scatter between pages and a contiguous KV tensor
+// [layer][K|V][token][head][dim] (the reference's gatherKernel and
+// appendTokensKernel, src/cuda/kv/page_kernels.cu:77-127, :184-242, which
+// search the descriptor list per element). Here one CTA moves one page's
+// (layer, K|V) block: valid_tokens contiguous rows, 16-byte accesses.
+// Scatter copies only the tokens of [first, first + count) into the pages.
+// grid (descriptors, layers * 2).
+__global__ void kv_gather_kernel(PoolView v, kk_page_desc const* descs, std::uint32_t total_tokens,
+    __half* out, __half const* in, std::uint32_t first, std::uint32_t count)
+{
+    pdl_wait();
+    kk_page_desc const d = descs[blockIdx.x];
+    std::uint32_t const layer = blockIdx.y / 2u;
+    std::uint32_t const component = blockIdx.y % 2u;
+    bool const micro = d.kind == 0;
+    std::uint32_t const cap = micro ? 8u : 64u;
+    std::uint32_t const begin = d.logical_token_begin;
+    std::uint32_t const end = begin + d.valid_tokens;
+    __half* page = block_of(v, micro ? 0 : 1, d.slot, layer, component);
+    bool const bad = page == nullptr || d.valid_tokens > cap || d.kind > 1
+        || (in == nullptr ? end > total_tokens : false);
+    if (bad) {
+        if (threadIdx.x == 0) {
+            atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        }
+        return;
+    }
+    std::uint64_t const row = v.row;
+    if (in == nullptr) {
+        __half* dst = out + ((std::uint64_t(layer) * 2u + component) * total_tokens + begin) * row;
+        std::uint64_t const n = std::uint64_t(d.valid_tokens) * row;
+        for (std::uint64_t i = threadIdx.x * 8u; i < n; i += blockDim.x * 8u) {
+            *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4 const*>(page + i);
+        }
+        return;
+    }
+    std::uint32_t const lo = begin > first ? begin : first;
+    std::uint32_t const hi = end < first + count ? end : first + count;
+    if (lo >= hi) {
+        return;
+    }
+    __half const* src = in + ((std::uint64_t(layer) * 2u + component) * count + (lo - first)) * row;
+    __half* dst = page + std::uint64_t(lo - begin) * row;
+    std::uint64_t const n = std::uint64_t(hi - lo) * row;
+    for (std::uint64_t i = threadIdx.x * 8u; i < n; i += blockDim.x * 8u) {
+        *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<uint4 const*>(src + i);
+    }
+}
+
 // SplitMix64 finaliser: a well-mixed 64-bit hash of (seed, index).
 __device__ __forceinline__ std::uint64_t mix64(std::uint64_t x)
 {
@@ -220,6 +269,38 @@ int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots, uint32_
     }
     return static_cast<int>(launch(kv_promote_kernel, dim3(8, pools->layers, 2), dim3(128), 0,
         static_cast<cudaStream_t>(stream), 1, view(*pools), src, extent_slot));
+}
+
+int kk_kv_gather(const kk_kv_pools* pools, const kk_page_desc* descs, uint32_t num_descs,
+    uint32_t total_tokens, uint16_t* out, void* stream)
+{
+    using namespace kk;
+    if (!poolsOk(pools) || (num_descs != 0 && (descs == nullptr || out == nullptr))
+        || (reinterpret_cast<std::uintptr_t>(out) & 15u) != 0) {
+        return KK_EINVAL;
+    }
+    if (num_descs == 0) {
+        return 0;
+    }
+    return static_cast<int>(launch(kv_gather_kernel, dim3(num_descs, pools->layers * 2u), dim3(256), 0,
+        static_cast<cudaStream_t>(stream), 1, view(*pools), descs, total_tokens,
+        reinterpret_cast<__half*>(out), static_cast<__half const*>(nullptr), 0u, 0u));
+}
+
+int kk_kv_scatter(const kk_kv_pools* pools, const kk_page_desc* descs, uint32_t num_descs,
+    uint32_t first_token, uint32_t token_count, const uint16_t* in, void* stream)
+{
+    using namespace kk;
+    if (!poolsOk(pools) || (num_descs != 0 && (descs == nullptr || in == nullptr))
+        || (reinterpret_cast<std::uintptr_t>(in) & 15u) != 0) {
+        return KK_EINVAL;
+    }
+    if (num_descs == 0 || token_count == 0) {
+        return 0;
+    }
+    return static_cast<int>(launch(kv_gather_kernel, dim3(num_descs, pools->layers * 2u), dim3(256), 0,
+        static_cast<cudaStream_t>(stream), 1, view(*pools), descs, 0u, static_cast<__half*>(nullptr),
+        reinterpret_cast<__half const*>(in), first_token, token_count));
 }
 
 int kk_fill_fp16(uint16_t* data, uint64_t count, uint64_t seed, float scale, void* stream)

@@ -413,6 +413,46 @@ def test_kv_write_and_copy_are_exact(kk, K):
     assert torch.equal(extent[2, :, :, 8:], e1[2, :, :, 8:])
 
 
+def test_kv_gather_and_scatter_are_exact(kk, K):
+    """K6: pages -> contiguous [layer][K|V][token][head][dim] and back."""
+    layers, hkv, D = 3, 4, 64
+    contexts = [17, 100, 513, 2000]
+    micro_cap = sum((c % 64 + 7) // 8 for c in contexts) + 8
+    extent_cap = sum(c // 64 for c in contexts) + 2
+    pools, micro, extent = make_pools(kk, layers, hkv, D, micro_cap, extent_cap, seed=21)
+    tables = build_tables(contexts, micro_cap, extent_cap, random.Random(5))
+    for tbl, T in zip(tables, contexts):
+        descs, _ = descs_and_lanes(kk, [tbl])
+        d_descs = to_device_bytes(descs)
+        out = torch.full((layers, 2, T, hkv, D), float("nan"), dtype=torch.half, device="cuda")
+        assert K["kv_gather"](C.byref(pools), p(d_descs), len(tbl), T, p(out), None) == 0
+        sync_ok(K)
+        for layer in range(layers):
+            k, v = gather_kv(micro, extent, tbl, layer)
+            assert torch.equal(out[layer, 0].float(), k) and torch.equal(out[layer, 1].float(), v)
+        # scatter a window of new values back and check exactly those tokens changed
+        first, count = T // 3, min(70, T - T // 3)
+        new = torch.randn(layers, 2, count, hkv, D, generator=torch.Generator().manual_seed(T)).half().cuda()
+        m0, e0 = micro.clone(), extent.clone()
+        assert K["kv_scatter"](C.byref(pools), p(d_descs), len(tbl), first, count, p(new), None) == 0
+        sync_ok(K)
+        out2 = torch.empty_like(out)
+        assert K["kv_gather"](C.byref(pools), p(d_descs), len(tbl), T, p(out2), None) == 0
+        sync_ok(K)
+        expect = out.clone()
+        expect[:, :, first:first + count] = new
+        assert torch.equal(out2, expect)
+        changed = (micro != m0).sum() + (extent != e0).sum()
+        assert int(changed) <= new.numel()
+    bad = (kk.PageDesc * 1)(kk.PageDesc(micro_cap + 3, 0, 8, 0, 0, 0))
+    out = torch.zeros(layers, 2, 8, hkv, D, dtype=torch.half, device="cuda")
+    d_bad = to_device_bytes(bad)
+    assert K["kv_gather"](C.byref(pools), p(d_bad), 1, 8, p(out), None) == 0
+    torch.cuda.synchronize()
+    assert K["device_status"](None) == 2
+    assert int(out.count_nonzero()) == 0
+
+
 def test_kv_promote_is_exact(kk, K):
     """8 micro pages -> 1 extent, every layer, K and V: extent token 8k+t is
     micro page k's token t; other extents and the micro pages are untouched."""

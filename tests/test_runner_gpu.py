@@ -293,6 +293,40 @@ def test_per_layer_spi_write_attend_matches_oracle(kk, tmp_path):
     R["backend_destroy"](backend)
 
 
+def test_backend_gather_returns_committed_kv(kk):
+    """kkrt_backend_gather: the committed KV of a request (extent body after
+    promotion + micro tail) as one contiguous tensor."""
+    R = kk.runtime()
+    L, hkv, D = 2, 4, 64
+    backend = R["backend_create"](L, hkv, D, 32, 1 << 20, 64, 8)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert R["backend_create_request"](backend, 7) == 0
+    assert R["backend_append"](backend, 7, 150) == 0
+    R["backend_seal"](backend, 7)
+    assert R["backend_promote"](backend, 7, 0, stream) == 0
+    assert R["backend_promote"](backend, 7, 64, stream) == 0
+    pools = kk.KvPools()
+    assert R["backend_pools"](backend, C.byref(pools))
+    K = kk.kernels()
+    for ptr, cap, tokens in [(pools.micro, pools.micro_capacity, 8), (pools.extent, pools.extent_capacity, 64)]:
+        assert K["fill_fp16"](C.c_void_p(ptr), cap * L * 2 * tokens * hkv * D, 17 + tokens, 0.5, stream) == 0
+    out = torch.zeros(L, 2, 150, hkv, D, dtype=torch.half, device="cuda")
+    assert R["backend_gather"](backend, 7, out.data_ptr(), stream) == 0
+    buf = (kk.KkEntry * 64)()
+    t = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 64, 0, 0)
+    assert R["backend_block_table"](backend, 7, C.byref(t))
+    entries = [buf[i] for i in range(t.count)]
+    assert [e.kind for e in entries][:2] == [1, 1]
+    micro = dev_view(pools.micro, pools.micro_capacity * L * 2 * 8 * hkv * D).view(torch.half).view(
+        pools.micro_capacity, L, 2, 8, hkv, D)
+    extent = dev_view(pools.extent, pools.extent_capacity * L * 2 * 64 * hkv * D).view(torch.half).view(
+        pools.extent_capacity, L, 2, 64, hkv, D)
+    for e in entries:
+        src = (micro if e.kind == 0 else extent)[e.slot, :, :, :e.valid_tokens]
+        assert torch.equal(out[:, :, e.logical_token_begin:e.logical_token_begin + e.valid_tokens], src)
+    R["backend_destroy"](backend)
+
+
 def test_auto_promotion_folds_full_runs_and_keeps_outputs(kk, tmp_path):
     """With auto-promotion on, every 64-aligned run of 8 sealed micro pages
     becomes one extent page as generation crosses it; greedy tokens and
