@@ -228,6 +228,17 @@ KK_API void kkrt_runner_destroy(void* runner);
  * Returns 1 when the batch result is well formed. */
 KK_API int kkrt_runner_forward_batch(void* runner, uint32_t n, const uint64_t* request_ids,
     const uint32_t* token_ids, const uint32_t* positions, uint32_t* out_tokens, uint8_t* out_ok);
+/* Fused multi-token prefill (no counterpart in the reference, which feeds a
+ * prompt one position per scheduler wave): appends n prompt tokens of one
+ * request at positions first_position.. (KvCacheManager::append semantics,
+ * partial-tail copy-on-write included) and runs them through the decode step
+ * in chunks of up to max_batch_size consecutive positions, each position
+ * attending causally to the request's tokens [0, p]. The committed length
+ * must equal first_position. *out_token receives the greedy token after the
+ * last prompt position. Returns 1 on success, 0 on failure (detail via
+ * kkrt_runner_last_error); a device failure releases the request. */
+KK_API int kkrt_runner_prefill(void* runner, uint64_t request_id, const uint32_t* token_ids, uint32_t n,
+    uint32_t first_position, uint32_t* out_token);
 /* forwardToken (runner.cpp:53) with optional captures (each may be NULL):
  * logits [vocab] f32, embedding / final_hidden [hidden] f16, layer_hidden
  * [n_layers][hidden] f16 for the listed layers. Returns CudaModelRunnerError. */

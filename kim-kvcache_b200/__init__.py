@@ -383,6 +383,7 @@ RUNTIME_SIGNATURES = {
                             C.c_char_p, _U32]),
     "runner_destroy": (None, [_VP]),
     "runner_set_auto_promote": (_I, [_VP, _I]),
+    "runner_prefill": (_I, [_VP, C.c_uint64, _PU32, _U32, _U32, _PU32]),
     "runner_forward_batch": (_I, [_VP, _U32, _PU64, _PU32, _PU32, _PU32, C.POINTER(C.c_uint8)]),
     "runner_forward_token": (_I, [_VP, _U64, _U32, _U32, _PU32, C.POINTER(C.c_float),
                                   C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), _PU32, _U32,

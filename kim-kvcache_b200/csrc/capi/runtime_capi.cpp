@@ -334,6 +334,23 @@ float kkrt_runner_last_step_ms(void* r)
     return runner == nullptr ? 0.f : runner->lastStepDeviceMs();
 }
 
+int kkrt_runner_prefill(void* r, uint64_t id, const uint32_t* tokens, uint32_t n, uint32_t first_position,
+    uint32_t* out_token)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    if (runner == nullptr || tokens == nullptr || n == 0) {
+        return 0;
+    }
+    GenerationStepResult const res = runner->prefill(id, std::vector<uint32_t>(tokens, tokens + n), first_position);
+    if (!res.success) {
+        return 0;
+    }
+    if (out_token != nullptr) {
+        *out_token = res.greedy_token_id;
+    }
+    return 1;
+}
+
 int kkrt_runner_set_auto_promote(void* r, int enabled)
 {
     auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));

@@ -921,7 +921,38 @@ EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id, void* d
     return rc == 0 ? EngineKvStatus{} : EngineKvStatus{EngineKvError::ExecutionFailed};
 }
 
+namespace {
+
+std::uint32_t promoteWave(EngineKvBackend& backend,
+    std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream);
+
+} // namespace
+
 std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
+    std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream)
+{
+    // A request with a prepared promotion holds a reservation, so a second
+    // run of the same request cannot be prepared until the first commits:
+    // promote in waves holding at most one run per request, in run order.
+    std::vector<std::pair<RequestId, std::uint32_t>> rest = runs;
+    std::uint32_t committed = 0;
+    while (!rest.empty()) {
+        std::vector<std::pair<RequestId, std::uint32_t>> wave;
+        std::vector<std::pair<RequestId, std::uint32_t>> later;
+        for (auto const& run : rest) {
+            bool const taken = std::any_of(wave.begin(), wave.end(),
+                [&run](auto const& w) { return w.first == run.first; });
+            (taken ? later : wave).push_back(run);
+        }
+        committed += promoteWave(backend, wave, stream);
+        rest.swap(later);
+    }
+    return committed;
+}
+
+namespace {
+
+std::uint32_t promoteWave(EngineKvBackend& backend,
     std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream)
 {
     auto* b = dynamic_cast<CudaBackend*>(&backend);
@@ -980,6 +1011,8 @@ std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
     }
     return committed;
 }
+
+} // namespace
 
 void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept
 {

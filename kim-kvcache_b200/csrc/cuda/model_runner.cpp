@@ -555,6 +555,154 @@ ModelTokenResult CudaTinyLlamaModelRunner::forwardToken(RequestId request_id,
     return result;
 }
 
+// One fused step over `n` consecutive prompt tokens of one request whose
+// metadata was just appended (table `before` -> `after`).
+GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId id,
+    std::uint32_t const* tokens_in, std::uint32_t n, std::uint32_t first, BlockTable const& before,
+    BlockTable const& after)
+{
+    auto* tokens = im.stepHost<std::uint32_t>(im.off_tokens);
+    auto* positions = im.stepHost<std::uint32_t>(im.off_positions);
+    auto* slots = im.stepHost<kk_kv_slot>(im.off_slots);
+    auto* copies = im.stepHost<kk_kv_copy>(im.off_copies);
+    auto* lanes = im.stepHost<kk_attn_lane>(im.off_lanes);
+    auto* descs = im.stepHost<kk_page_desc>(im.off_descs);
+    auto const& entries = after.entries();
+    std::uint32_t n_copies = 0;
+    // Partial-tail copy-on-write: the old tail's tokens move to the new page
+    // at the same logical begin before the new tokens land there.
+    if (!before.entries().empty()) {
+        MappingEntry const& old_tail = before.entries().back();
+        for (MappingEntry const& e : entries) {
+            if (e.logical_token_begin == old_tail.logical_token_begin && e.handle != old_tail.handle) {
+                copies[n_copies++] = kk_kv_copy{old_tail.handle.slot, e.handle.slot, old_tail.valid_tokens,
+                    static_cast<std::uint8_t>(old_tail.kind), static_cast<std::uint8_t>(e.kind)};
+            }
+        }
+    }
+    std::uint32_t n_descs = 0;
+    for (std::uint32_t i = 0; i < n; ++i) {
+        std::uint32_t const p = first + i;
+        tokens[i] = tokens_in[i];
+        positions[i] = p;
+        std::uint32_t const lane_first = n_descs;
+        bool placed = false;
+        for (MappingEntry const& e : entries) {
+            if (e.logical_token_begin > p) {
+                break;
+            }
+            std::uint32_t const end = e.logical_token_begin + e.valid_tokens;
+            if (p < end) {
+                slots[i] = kk_kv_slot{e.handle.slot, static_cast<std::uint16_t>(p - e.logical_token_begin),
+                    static_cast<std::uint8_t>(e.kind), 1};
+                placed = true;
+            }
+            if (n_descs >= im.max_descs) {
+                return {false, 0, "step descriptor capacity exceeded"};
+            }
+            // Causal: position p attends to tokens [0, p].
+            std::uint32_t const valid = p < end ? p + 1 - e.logical_token_begin : e.valid_tokens;
+            descs[n_descs++] = kk_page_desc{e.handle.slot, e.logical_token_begin,
+                static_cast<std::uint16_t>(valid), static_cast<std::uint8_t>(e.kind), 0, 0};
+        }
+        if (!placed) {
+            return {false, 0, "appended table does not cover the prompt position"};
+        }
+        lanes[i] = kk_attn_lane{lane_first, n_descs - lane_first, p + 1, 0, 0, i, {0, 0}};
+    }
+    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, n, im.sm_count,
+        im.stepHost<kk_attn_item>(im.off_items), im.max_items);
+    if (n_items > im.max_items) {
+        return {false, 0, "attention work list capacity exceeded"};
+    }
+    auto* counts = im.stepHost<std::uint32_t>(im.off_counts);
+    counts[0] = n_items;
+    counts[1] = n_copies;
+    std::size_t const bytes = im.off_descs + std::size_t(n_descs) * sizeof(kk_page_desc);
+    cudaError_t e = cudaMemcpyAsync(im.step_dev, im.step_host, bytes, cudaMemcpyHostToDevice, im.stream);
+    CudaModelRunnerStatus s = e == cudaSuccess ? im.runStep(n, n_copies != 0, false, nullptr)
+                                               : cudaFailure(static_cast<int>(e), "upload step inputs");
+    if (s.ok()) {
+        e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, n * 4u, cudaMemcpyDeviceToHost, im.stream);
+        if (e == cudaSuccess) {
+            e = cudaStreamSynchronize(im.stream);
+        }
+        if (e != cudaSuccess) {
+            s = failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
+                std::string("prefill step failed: ") + cudaGetErrorString(e));
+        }
+    }
+    if (!s.ok()) {
+        im.last_error = s.detail;
+        return {false, 0, s.detail};
+    }
+    noteStreamCompleted(*im.kv, im.stream);
+    cudaEventElapsedTime(&im.last_ms, im.ev_begin, im.ev_end);
+    static_cast<void>(id);
+    return {true, im.host_tokens[n - 1], {}};
+}
+
+GenerationStepResult CudaTinyLlamaModelRunner::prefill(RequestId request_id,
+    std::vector<std::uint32_t> const& prompt, std::uint32_t first_position)
+{
+    GenerationStepResult r = prefillChunks(request_id, prompt, first_position);
+    if (!r.success) {
+        impl_->last_error = r.detail;
+    }
+    return r;
+}
+
+GenerationStepResult CudaTinyLlamaModelRunner::prefillChunks(RequestId request_id,
+    std::vector<std::uint32_t> const& prompt, std::uint32_t first_position)
+{
+    Impl& im = *impl_;
+    TinyLlamaConfig const& c = im.cfg;
+    if (request_id == kInvalidRequestId || prompt.empty()
+        || first_position + prompt.size() > c.max_position_embeddings) {
+        return {false, 0, "request, prompt, or position is out of range"};
+    }
+    for (std::uint32_t t : prompt) {
+        if (t >= c.vocabulary_size) {
+            return {false, 0, "token id is out of range"};
+        }
+    }
+    GenerationStepResult last{false, 0, "empty prompt"};
+    std::uint32_t const chunk = im.options.max_batch_size;
+    std::vector<std::pair<RequestId, std::uint32_t>> promote;
+    for (std::size_t done = 0; done < prompt.size(); done += chunk) {
+        std::uint32_t const n = static_cast<std::uint32_t>(std::min<std::size_t>(chunk, prompt.size() - done));
+        std::uint32_t const first = first_position + static_cast<std::uint32_t>(done);
+        BlockTable before;
+        if (!cudaBackendTable(*im.kv, request_id, before) || before.tokenCount() != first) {
+            return {false, 0, "request not found or its committed length differs from the prompt position"};
+        }
+        EngineKvStatus const appended = cudaBackendAppend(*im.kv, request_id, n);
+        if (!appended.ok()) {
+            return {false, 0, kvFailure(appended, "append prompt tokens").detail};
+        }
+        BlockTable after;
+        if (!cudaBackendTable(*im.kv, request_id, after)) {
+            return {false, 0, "request vanished during prefill"};
+        }
+        last = prefillStep(im, request_id, prompt.data() + done, n, first, before, after);
+        if (!last.success) {
+            // As the reference's append data path does after a device failure:
+            // the request's pages cannot be trusted any more, release it.
+            static_cast<void>(im.kv->releaseRequest(request_id));
+            return last;
+        }
+        if (im.auto_promote) {
+            for (std::uint32_t end = (first / 64 + 1) * 64; end <= first + n; end += 64) {
+                promote.emplace_back(request_id, end - 64);
+            }
+        }
+    }
+    if (!promote.empty()) {
+        static_cast<void>(cudaBackendPromoteMany(*im.kv, promote, im.stream));
+    }
+    return last;
+}
+
 GenerationBatchResult CudaTinyLlamaModelRunner::generationForwardBatch(
     std::vector<GenerationBatchItem> const& batch)
 {

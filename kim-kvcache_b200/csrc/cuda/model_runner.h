@@ -104,6 +104,20 @@ public:
         std::vector<GenerationBatchItem> const& batch) override;
     [[nodiscard]] std::uint32_t generationMaxBatchSize() const noexcept override;
 
+    // Fused multi-token prefill (no counterpart in the reference, which feeds
+    // prompts one position per wave): the prompt tokens at positions
+    // first_position.. of one request run through the decode step as one
+    // batch of up to max_batch_size consecutive positions per step. The
+    // metadata is appended up front (KvCacheManager::append, with partial-tail
+    // copy-on-write), every token's K/V is written by the QKV projection, and
+    // position p attends causally to tokens [0, p] of the request. The
+    // request's committed length must equal first_position; on success it
+    // grows by prompt.size() and the result carries the greedy token after
+    // the last prompt position. A device failure releases the request, as
+    // the reference's append data path does.
+    [[nodiscard]] GenerationStepResult prefill(RequestId request_id,
+        std::vector<std::uint32_t> const& prompt, std::uint32_t first_position);
+
     // Device time of the last fused step (ms, from CUDA events), 0 if unknown.
     [[nodiscard]] float lastStepDeviceMs() const noexcept;
     // Detail of the last failed fused step (empty if none).
@@ -116,6 +130,10 @@ public:
 private:
     explicit CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept;
     std::unique_ptr<Impl> impl_;
+    [[nodiscard]] GenerationStepResult prefillChunks(RequestId request_id,
+        std::vector<std::uint32_t> const& prompt, std::uint32_t first_position);
+    friend GenerationStepResult prefillStep(Impl&, RequestId, std::uint32_t const*, std::uint32_t,
+        std::uint32_t, BlockTable const&, BlockTable const&);
     friend CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const&,
         std::string const&, EngineKvBackend&, EngineStream, CudaModelRunnerOptions);
 };

@@ -392,3 +392,112 @@ def test_tinyllama_shape_greedy_decode_config2(kk, tmp_path):
             if a != b and np.diff(np.sort(lg)[-2:])[0] > TOL]
     assert not mism, mism
     s.close()
+
+
+def _prefill(s, rid, toks, first):
+    n = len(toks)
+    out = C.c_uint32(0)
+    ok = s.R["runner_prefill"](s.runner, rid, (C.c_uint32 * n)(*toks), n, first, C.byref(out))
+    if not ok:
+        buf = C.create_string_buffer(512)
+        s.R["runner_last_error"](s.runner, buf, 512)
+        return None, buf.value.decode()
+    return out.value, ""
+
+
+def _oracle_prompt(s, rid, toks, first):
+    """The oracle fed one position at a time, as the reference's scheduler
+    feeds a prompt; returns the greedy token and logits after the last one."""
+    for i, t in enumerate(toks):
+        want, logits, _ = s.oracle.forward([rid], [t], [first + i], want_hidden=False)
+    return int(want[0]), logits
+
+
+@pytest.mark.parametrize("batch,lengths", [(8, [150]), (16, [13, 37, 1, 64, 9]), (32, [200])])
+def test_fused_prefill_matches_per_position_oracle(kk, tmp_path, batch, lengths):
+    """kkrt_runner_prefill: the prompt runs as chunks of up to max_batch_size
+    consecutive positions of one request, each attending causally to tokens
+    [0, p]. The greedy token after every prefill call and the decode tokens
+    that follow match the oracle fed one position at a time; the page table
+    covers exactly the prompt."""
+    s = Stack(kk, tmp_path, SMALL, batch=batch)
+    rng = random.Random(batch + sum(lengths))
+    s.create(5)
+    pos = 0
+    for n in lengths:
+        toks = [rng.randrange(3, 1000) for _ in range(n)]
+        got, err = _prefill(s, 5, toks, pos)
+        assert got is not None, err
+        want, logits = _oracle_prompt(s, 5, toks, pos)
+        assert_greedy([got], [want], logits)
+        pos += n
+        tok = want
+    for _ in range(12):
+        g, ok = s.batch([5], [tok], [pos])
+        w, logits, _ = s.oracle.forward([5], [tok], [pos], want_hidden=False)
+        assert ok == [1]
+        assert_greedy(g, w, logits)
+        tok, pos = int(w[0]), pos + 1
+    tbl = (kk.KkEntry * 128)()
+    t = kk.KkTableOut(C.cast(tbl, C.POINTER(kk.KkEntry)), 128, 0, 0)
+    assert s.R["backend_block_table"](s.backend, 5, C.byref(t)) == 1
+    assert sum(tbl[i].valid_tokens for i in range(t.count)) == pos
+    assert s.snapshot().committed_token_count == pos
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
+def test_fused_prefill_after_fork_copies_the_shared_tail(kk, tmp_path):
+    """A child forked at 11 tokens shares a 3-token partial tail; the child's
+    prefill appends through partial-tail copy-on-write, and both the parent's
+    decode and the child's prefill continue to follow the oracle."""
+    s = Stack(kk, tmp_path, SMALL, batch=16)
+    rng = random.Random(17)
+    s.create(1)
+    head = [rng.randrange(3, 1000) for _ in range(11)]
+    got, err = _prefill(s, 1, head, 0)
+    assert got is not None, err
+    want, _ = _oracle_prompt(s, 1, head, 0)
+    assert s.R["backend_fork"](s.backend, 1, 2) == 0
+    s.oracle.fork(1, 2)
+    tail = [rng.randrange(3, 1000) for _ in range(29)]
+    got2, err = _prefill(s, 2, tail, 11)
+    assert got2 is not None, err
+    want2, logits2 = _oracle_prompt(s, 2, tail, 11)
+    assert_greedy([got2], [want2], logits2)
+    # the parent still sees its own (unmodified) tail
+    g, ok = s.batch([1, 2], [want, want2], [11, 40])
+    w, logits, _ = s.oracle.forward([1, 2], [want, want2], [11, 40], want_hidden=False)
+    assert ok == [1, 1]
+    assert_greedy(g, w, logits)
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
+def test_fused_prefill_auto_promotes_and_rejects_bad_calls(kk, tmp_path):
+    cfg = dict(SMALL, max_positions=256)
+    s = Stack(kk, tmp_path, cfg, batch=32, micro=128, extent=8)
+    assert s.R["runner_set_auto_promote"](s.runner, 1) == 1
+    rng = random.Random(23)
+    s.create(7)
+    toks = [rng.randrange(3, 1000) for _ in range(150)]
+    got, err = _prefill(s, 7, toks, 0)
+    assert got is not None, err
+    want, logits = _oracle_prompt(s, 7, toks, 0)
+    assert_greedy([got], [want], logits)
+    buf = (kk.KkEntry * 64)()
+    t = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 64, 0, 0)
+    assert s.R["backend_block_table"](s.backend, 7, C.byref(t)) == 1
+    assert [buf[i].kind for i in range(t.count)][:2] == [1, 1]
+    assert sum(1 for i in range(t.count) if buf[i].kind == 1) == 2
+    # wrong first position, unknown request, out-of-range token: rejected, state intact
+    assert _prefill(s, 7, [5], 149)[0] is None
+    assert _prefill(s, 99, [5], 0)[0] is None
+    assert _prefill(s, 7, [cfg["vocab"]], 150)[0] is None
+    assert s.snapshot().committed_token_count == 150
+    g, ok = s.batch([7], [want], [150])
+    w, logits, _ = s.oracle.forward([7], [want], [150], want_hidden=False)
+    assert ok == [1]
+    assert_greedy(g, w, logits)
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
