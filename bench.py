@@ -433,6 +433,77 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_prefill(args):
+    """Prompt throughput of the fused multi-token prefill (kkrt_runner_prefill):
+    --prefill-requests prompts of --prompt tokens each, every prompt fed in
+    chunks of --prefill-chunk consecutive positions (the runner's batch size),
+    causal attention over the request's pages. Timed with CUDA events around
+    the API calls, so the prompt upload and the per-chunk token readback are
+    inside the timed region (value = e2e)."""
+    import torch
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = dict(synth.TINYLLAMA)
+    P, nreq, chunk = args.prompt, args.prefill_requests, args.prefill_chunk
+    cfg["max_positions"] = max(4608, P + 8)
+    archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
+    manifest, data, _ = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31))
+    R = kk.runtime()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    hq, hkv, D, L = cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["layers"]
+    micro_cap = (nreq + 1) * (P // 8 + 2)
+    extent_cap = (nreq + 1) * (P // 64 + 1)
+    backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
+    assert backend, "backend allocation failed"
+    status, detail = C.c_int(0), C.create_string_buffer(512)
+    runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr, chunk, 1, 1,
+                                C.byref(status), detail, 512)
+    assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
+    assert R["runner_set_auto_promote"](runner, 1) == 1
+    rng = random.Random(SEED)
+    prompts = [(C.c_uint32 * P)(*[rng.randrange(3, 32000) for _ in range(P)]) for _ in range(nreq + 1)]
+    out = C.c_uint32(0)
+
+    def prefill(rid, prompt):
+        assert R["backend_create_request"](backend, rid) == 0
+        if not R["runner_prefill"](runner, rid, prompt, P, 0, C.byref(out)):
+            buf = C.create_string_buffer(512)
+            R["runner_last_error"](runner, buf, 512)
+            raise RuntimeError(f"prefill failed: {buf.value.decode()}")
+
+    for w in range(max(1, args.warmup // 3)):
+        prefill(1000 + w, prompts[-1])
+        assert R["backend_release"](backend, 1000 + w) == 0
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id(torch, dev))
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for r in range(nreq):
+        prefill(r + 1, prompts[r])
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    R["runner_destroy"](runner)
+    R["backend_destroy"](backend)
+    tok = nreq * P
+    steps = nreq * -(-P // chunk)
+    print(json.dumps({
+        "metric": "prefill prompt tok/s/GPU TinyLlama-shape (fused causal chunks)",
+        "value": round(tok / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1, "steps": steps,
+        "warmup": max(1, args.warmup // 3), "ms_per_step": round(ms / steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": f"prefill: {nreq} prompts x {P} tokens, chunk {chunk}",
+                   "model": "TinyLlama-1.1B shape", "auto_promote": True},
+        "e2e": {"value": round(tok / (ms / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": None, "d2h_bytes_per_step": 4 * chunk},
+        "clocks": clocks}), flush=True)
+
+
 GEMM_SHAPES = {  # name: (M, K, epilogue) of the TinyLlama projections at N = 32
     "qkv": (2560, 2048, "f16"), "o": (2048, 2048, "f16"), "gu": (11264, 2048, "silu"),
     "down": (2048, 5632, "f16"), "lm": (32000, 2048, "f32"),
@@ -619,6 +690,12 @@ def main():
                     help="--kernel-only: launch with programmatic dependent launch (as the runner does)")
     ap.add_argument("--plan", default="balanced", choices=["balanced", "lane"],
                     help="--kernel-only attention: one token-balanced run per SM, or per-lane items")
+    ap.add_argument("--prefill", action="store_true",
+                    help="time the fused multi-token prefill instead of decode (one GPU)")
+    ap.add_argument("--prompt", type=int, default=1024, help="--prefill: tokens per prompt")
+    ap.add_argument("--prefill-requests", type=int, default=8, help="--prefill: prompts timed")
+    ap.add_argument("--prefill-chunk", type=int, default=128,
+                    help="--prefill: positions per fused step (the runner batch size)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", "0"))
@@ -626,6 +703,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.kernel_only:
         run_kernel_only(args)
+        return
+    if args.prefill:
+        run_prefill(args)
         return
     line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
         args, rank, world, local_rank)

@@ -134,6 +134,41 @@ KK_API int kkrt_mgr_page_metadata(void* mgr, kk_handle handle, kk_page_meta* out
 KK_API void kkrt_mgr_snapshot(void* mgr, kk_mgr_snapshot* out);
 KK_API int kkrt_mgr_check_invariants(void* mgr);
 
+/* ---- FixedPageManager (include/kim-kv/fixed/fixed_page_manager.h:30-166) ----
+ * The single-kind page runtime (Fixed-8/16/32/64): same create / append /
+ * reserve / seal / fork / partial-tail COW / release semantics with every page
+ * holding tokens_per_page tokens; no promotion, no leases. Return values are
+ * KvCacheError values. Every kkrt_fixed_* has a kref_fixed_* twin in the
+ * parity oracle. */
+typedef struct kk_fixed_snapshot {
+    uint64_t request_count;
+    uint64_t successful_allocations;
+    uint64_t peak_allocated_pages;
+    uint64_t token_reservation_count;
+    kk_pool_snapshot pool;
+} kk_fixed_snapshot;
+
+/* Constructor (fixed_page_manager.cpp:28): NULL when tokens_per_page or
+ * page_capacity is 0. */
+KK_API void* kkrt_fixed_create(uint16_t tokens_per_page, uint32_t page_capacity);
+KK_API void kkrt_fixed_destroy(void* mgr);
+KK_API uint32_t kkrt_fixed_tokens_per_page(void* mgr);
+KK_API int kkrt_fixed_create_request(void* mgr, uint64_t request_id);
+/* append (fixed_page_manager.cpp:218): multi-token append with partial-tail COW. */
+KK_API int kkrt_fixed_append(void* mgr, uint64_t request_id, uint32_t token_count);
+/* reserveToken / commit / rollback (fixed_token_reservation.cpp:32, :172, :250). */
+KK_API int kkrt_fixed_reserve_token(void* mgr, uint64_t request_id, uint32_t expected_committed,
+    uint64_t* reservation_id, kk_table_out* before, kk_table_out* reserved);
+KK_API int kkrt_fixed_commit_reservation(void* mgr, uint64_t reservation_id);
+KK_API int kkrt_fixed_rollback_reservation(void* mgr, uint64_t reservation_id);
+KK_API int kkrt_fixed_seal_tail(void* mgr, uint64_t request_id);
+KK_API int kkrt_fixed_fork(void* mgr, uint64_t source_id, uint64_t child_id);
+KK_API int kkrt_fixed_release(void* mgr, uint64_t request_id);
+/* blockTable: returns 1 when the request exists. */
+KK_API int kkrt_fixed_block_table(void* mgr, uint64_t request_id, kk_table_out* out);
+KK_API void kkrt_fixed_snapshot(void* mgr, kk_fixed_snapshot* out);
+KK_API int kkrt_fixed_check_invariants(void* mgr);
+
 /* ---- weight manifest (include/kim-kv/model/weight_manifest.h:111-134) ---- */
 /* loadWeightManifest, then validateWeightDataFile when data_path is not NULL;
  * returns the WeightManifestError of the first failing step (0 = valid). */

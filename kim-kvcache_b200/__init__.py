@@ -52,6 +52,12 @@ class KkMgrSnapshot(C.Structure):
                 ("micro_pool", KkPoolSnapshot), ("extent_pool", KkPoolSnapshot)]
 
 
+class KkFixedSnapshot(C.Structure):
+    _fields_ = [("request_count", C.c_uint64), ("successful_allocations", C.c_uint64),
+                ("peak_allocated_pages", C.c_uint64), ("token_reservation_count", C.c_uint64),
+                ("pool", KkPoolSnapshot)]
+
+
 class KkTableOut(C.Structure):
     _fields_ = [("entries", C.POINTER(KkEntry)), ("capacity", C.c_uint32),
                 ("count", C.c_uint32), ("version", C.c_uint64)]
@@ -95,6 +101,25 @@ MANAGER_SIGNATURES = {
     "mgr_check_invariants": (_I, [_P]),
     "float_to_half": (C.c_uint16, [C.c_float]),
     "half_to_float": (C.c_float, [C.c_uint16]),
+}
+
+
+FIXED_SIGNATURES = {
+    "fixed_create": (_P, [C.c_uint16, _U32]),
+    "fixed_destroy": (None, [_P]),
+    "fixed_tokens_per_page": (_U32, [_P]),
+    "fixed_create_request": (_I, [_P, _U64]),
+    "fixed_append": (_I, [_P, _U64, _U32]),
+    "fixed_reserve_token": (_I, [_P, _U64, _U32, C.POINTER(_U64), C.POINTER(KkTableOut),
+                                 C.POINTER(KkTableOut)]),
+    "fixed_commit_reservation": (_I, [_P, _U64]),
+    "fixed_rollback_reservation": (_I, [_P, _U64]),
+    "fixed_seal_tail": (_I, [_P, _U64]),
+    "fixed_fork": (_I, [_P, _U64, _U64]),
+    "fixed_release": (_I, [_P, _U64]),
+    "fixed_block_table": (_I, [_P, _U64, C.POINTER(KkTableOut)]),
+    "fixed_snapshot": (None, [_P, C.POINTER(KkFixedSnapshot)]),
+    "fixed_check_invariants": (_I, [_P]),
 }
 
 
@@ -226,6 +251,74 @@ class Manager:
 
     def invariants(self):
         return bool(self.f["mgr_check_invariants"](self.h))
+
+
+class FixedManager:
+    """FixedPageManager through a C ABI (kkrt_ = this library, kref_ = the
+    reference oracle twin). Same method names and result tuples as Manager."""
+
+    MAX_ENTRIES = 4096
+
+    def __init__(self, lib: C.CDLL, prefix: str, tokens_per_page: int, capacity: int):
+        self.f = bind(lib, prefix, FIXED_SIGNATURES)
+        self.h = self.f["fixed_create"](tokens_per_page, capacity)
+        if not self.h:
+            raise ValueError("invalid page size or capacity")
+        self._buf = [(KkEntry * self.MAX_ENTRIES)() for _ in range(2)]
+
+    def close(self):
+        if self.h:
+            self.f["fixed_destroy"](self.h)
+            self.h = None
+
+    __del__ = close
+
+    def _table(self, i=0):
+        return KkTableOut(C.cast(self._buf[i], C.POINTER(KkEntry)), self.MAX_ENTRIES, 0, 0)
+
+    def tokens_per_page(self):
+        return self.f["fixed_tokens_per_page"](self.h)
+
+    def create(self, rid):
+        return self.f["fixed_create_request"](self.h, rid)
+
+    def append(self, rid, n):
+        return self.f["fixed_append"](self.h, rid, n)
+
+    def reserve(self, rid, expected):
+        r = C.c_uint64(0)
+        b, v = self._table(0), self._table(1)
+        err = self.f["fixed_reserve_token"](self.h, rid, expected, C.byref(r), C.byref(b), C.byref(v))
+        return err, r.value, Manager._entries(b, self._buf[0]), Manager._entries(v, self._buf[1])
+
+    def commit(self, res_id):
+        return self.f["fixed_commit_reservation"](self.h, res_id)
+
+    def rollback(self, res_id):
+        return self.f["fixed_rollback_reservation"](self.h, res_id)
+
+    def seal(self, rid):
+        return self.f["fixed_seal_tail"](self.h, rid)
+
+    def fork(self, src, child):
+        return self.f["fixed_fork"](self.h, src, child)
+
+    def release(self, rid):
+        return self.f["fixed_release"](self.h, rid)
+
+    def table(self, rid):
+        t = self._table(0)
+        if not self.f["fixed_block_table"](self.h, rid, C.byref(t)):
+            return None
+        return Manager._entries(t, self._buf[0])
+
+    def snapshot(self):
+        s = KkFixedSnapshot()
+        self.f["fixed_snapshot"](self.h, C.byref(s))
+        return _struct_tuple(s)
+
+    def invariants(self):
+        return bool(self.f["fixed_check_invariants"](self.h))
 
 
 # ---- kernel C ABI (include/kk_kernels.h) ------------------------------------

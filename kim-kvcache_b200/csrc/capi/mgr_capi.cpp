@@ -1,6 +1,7 @@
 // C ABI over KvCacheManager (declarations and reference citations in
 // include/kk_runtime.h).
 #include "../../../include/kk_runtime.h"
+#include "../host/fixed_page_manager.h"
 #include "../host/fp16_codec.h"
 #include "../host/kv_cache_manager.h"
 #include "../host/weight_manifest.h"
@@ -14,6 +15,7 @@ using namespace kimkvcache;
 namespace {
 
 KvCacheManager* M(void* mgr) { return static_cast<KvCacheManager*>(mgr); }
+FixedPageManager* F(void* mgr) { return static_cast<FixedPageManager*>(mgr); }
 
 void writeTable(BlockTable const& table, kk_table_out* out)
 {
@@ -183,6 +185,63 @@ void kkrt_mgr_snapshot(void* mgr, kk_mgr_snapshot* out)
 }
 
 int kkrt_mgr_check_invariants(void* mgr) { return M(mgr)->checkInvariants() ? 1 : 0; }
+
+void* kkrt_fixed_create(uint16_t tokens_per_page, uint32_t page_capacity)
+{
+    try {
+        return new FixedPageManager(tokens_per_page, page_capacity);
+    } catch (...) {
+        return nullptr;
+    }
+}
+
+void kkrt_fixed_destroy(void* mgr) { delete F(mgr); }
+uint32_t kkrt_fixed_tokens_per_page(void* mgr) { return F(mgr)->tokensPerPage(); }
+int kkrt_fixed_create_request(void* mgr, uint64_t id) { return int(F(mgr)->createRequest(id)); }
+int kkrt_fixed_append(void* mgr, uint64_t id, uint32_t n) { return int(F(mgr)->append(id, n)); }
+
+int kkrt_fixed_reserve_token(void* mgr, uint64_t request_id, uint32_t expected,
+    uint64_t* reservation_id, kk_table_out* before, kk_table_out* reserved)
+{
+    TokenReservationResult const r = F(mgr)->reserveToken(request_id, expected);
+    if (reservation_id != nullptr) {
+        *reservation_id = r.reservation_id;
+    }
+    writeTable(r.before, before);
+    writeTable(r.reserved, reserved);
+    return static_cast<int>(r.error);
+}
+
+int kkrt_fixed_commit_reservation(void* mgr, uint64_t id) { return int(F(mgr)->commitTokenReservation(id)); }
+int kkrt_fixed_rollback_reservation(void* mgr, uint64_t id)
+{
+    return int(F(mgr)->rollbackTokenReservation(id));
+}
+int kkrt_fixed_seal_tail(void* mgr, uint64_t id) { return int(F(mgr)->sealTail(id)); }
+int kkrt_fixed_fork(void* mgr, uint64_t s, uint64_t c) { return int(F(mgr)->forkRequest(s, c)); }
+int kkrt_fixed_release(void* mgr, uint64_t id) { return int(F(mgr)->releaseRequest(id)); }
+
+int kkrt_fixed_block_table(void* mgr, uint64_t id, kk_table_out* out)
+{
+    std::optional<BlockTable> const t = F(mgr)->blockTable(id);
+    if (!t) {
+        return 0;
+    }
+    writeTable(*t, out);
+    return 1;
+}
+
+void kkrt_fixed_snapshot(void* mgr, kk_fixed_snapshot* out)
+{
+    FixedPageManagerSnapshot const s = F(mgr)->snapshot();
+    out->request_count = s.request_count;
+    out->successful_allocations = s.successful_allocations;
+    out->peak_allocated_pages = s.peak_allocated_pages;
+    out->token_reservation_count = s.token_reservation_count;
+    poolOut(s.pool, &out->pool);
+}
+
+int kkrt_fixed_check_invariants(void* mgr) { return F(mgr)->checkInvariants() ? 1 : 0; }
 
 int kkrt_manifest_check(const char* manifest_path, const char* data_path)
 {

@@ -535,13 +535,23 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     a.output = reinterpret_cast<__half*>(output);
     a.output_stride = output_stride;
     a.scale_log2 = scale * 1.4426950408889634f;
-    char* ws = static_cast<char*>(workspace);
-    a.counters = reinterpret_cast<std::uint32_t*>(ws);
-    ws += align256(std::uint64_t(num_lanes) * 4u);
-    a.part_o = reinterpret_cast<float*>(ws);
-    ws += align256(2ull * num_items * q_heads * kHeadDim * 4u);
-    a.part_ml = reinterpret_cast<float*>(ws);
-    bool const tma_ok = attentionTmaSupported(pools, q_heads);
+    // Partial states are read and written as float2/float4.
+    if (reinterpret_cast<std::uintptr_t>(workspace) % 16u != 0) {
+        return KK_EINVAL;
+    }
+    // Without a workspace the kernels see null partial pointers: a lane that
+    // turns out to be split is then reported (bad argument), never written.
+    if (workspace != nullptr) {
+        char* ws = static_cast<char*>(workspace);
+        a.counters = reinterpret_cast<std::uint32_t*>(ws);
+        ws += align256(std::uint64_t(num_lanes) * 4u);
+        a.part_o = reinterpret_cast<float*>(ws);
+        ws += align256(2ull * num_items * q_heads * kHeadDim * 4u);
+        a.part_ml = reinterpret_cast<float*>(ws);
+    }
+    // The TMA kernel copies each query row with one bulk copy (16-byte aligned source).
+    bool const tma_ok = attentionTmaSupported(pools, q_heads)
+        && reinterpret_cast<std::uintptr_t>(query) % 16u == 0;
     if (variant == KK_ATTN_TMA && !tma_ok) {
         return KK_EINVAL;
     }
@@ -596,17 +606,29 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
     if (num_parts == 0) {
         num_parts = 1;
     }
+    // Cost model of the token stream, in tokens: every token, plus a fixed
+    // charge per lane for the merge and partial write a CTA makes at the end
+    // of each lane segment (about one and a half 32-token stages).
+    constexpr std::uint64_t kSegmentCost = 48;
     std::uint64_t total = 0;
     for (std::uint32_t b = 0; b < num_lanes; ++b) {
+        if (lanes[b].desc_count != 0) {
+            total += kSegmentCost;
+        }
         for (std::uint32_t e = lanes[b].desc_offset; e < lanes[b].desc_offset + lanes[b].desc_count; ++e) {
             total += descs[e].valid_tokens;
         }
     }
-    std::uint64_t const per = total == 0 ? 1 : (total + num_parts - 1) / num_parts;
+    // Cut k of num_parts - 1 lands on the page boundary nearest to
+    // k * total / num_parts, so the runs are equal to within half a page.
+    std::uint64_t const whole = total / num_parts;
+    std::uint64_t const rest = total % num_parts;
+    auto target = [&](std::uint64_t k) { return whole * k + rest * k / num_parts; };
     std::uint32_t count = 0;
     kk_attn_item cur{};
     bool open = false;
-    std::uint64_t acc = 0;
+    std::uint64_t pos = 0;
+    std::uint32_t next_cut = 1;
     auto flush = [&]() {
         if (open && count - 1 < max_items) {
             items[count - 1] = cur;
@@ -622,11 +644,28 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
         if (open && cur.desc_end != ln.desc_offset) {
             flush();
         }
+        if (ln.desc_count != 0) {
+            pos += kSegmentCost;
+        }
         for (std::uint32_t e = ln.desc_offset; e < end; ++e) {
+            std::uint64_t const c = descs[e].valid_tokens;
+            bool cut_before = false;
+            bool cut_after = false;
+            while (next_cut < num_parts && target(next_cut) < pos + c) {
+                std::uint64_t const t = target(next_cut);
+                if (2 * t < 2 * pos + c) {
+                    cut_before = true;
+                } else {
+                    cut_after = true;
+                }
+                ++next_cut;
+            }
+            if (cut_before) {
+                flush();
+            }
             if (!open) {
                 cur = kk_attn_item{b, e, e, KK_ATTN_ITEM_MULTI_LANE};
                 open = true;
-                acc = 0;
                 ++count;
             }
             if (ln.item_count == 0 || ln.item_offset + ln.item_count != count) {
@@ -636,8 +675,8 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
                 ++ln.item_count;
             }
             cur.desc_end = e + 1;
-            acc += descs[e].valid_tokens;
-            if (acc >= per) {
+            pos += c;
+            if (cut_after) {
                 flush();
             }
         }

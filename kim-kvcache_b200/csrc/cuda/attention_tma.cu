@@ -49,20 +49,41 @@ namespace {
 constexpr int kHeadDim = 64;
 constexpr int kConsumerWarps = 8;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
+#ifdef KK_ATTN_STAGES
+constexpr int kStages = KK_ATTN_STAGES;
+#else
 constexpr int kStages = 3;
+#endif
 constexpr std::uint32_t kStageBytes = 32768;           // K 16 KB + V 16 KB
 constexpr std::uint32_t kRowBytes = kHeadDim * 2;      // one head x one token
 constexpr std::uint32_t kORow = kHeadDim + 4;          // padded merge row (floats)
 
 constexpr std::uint32_t kSegEnd = 1u;    // last stage of a lane segment
 constexpr std::uint32_t kItemEnd = 2u;   // last stage of the item
+// The stage holds micro pages loaded whole ([head][8 tokens] per page, page
+// n at rows n*kv_heads*8): one load for K and one for V per page.
+constexpr std::uint32_t kMicroStage = 4u;
 
 struct StageMeta {
-    std::uint8_t valid[8];  // valid tokens of each 8-token group slot (0 = empty slot)
+    // Valid tokens of each 8-token group slot, one byte per slot (0 = empty
+    // slot). Packed in one word so neither side indexes an array with a
+    // runtime index (that would place it in local memory).
+    std::uint64_t valid;
     std::uint32_t lane;     // lane whose tokens the stage holds
     std::uint32_t flags;    // kSegEnd | kItemEnd
     std::uint32_t next_lane;  // lane of the item's next segment (kSegEnd without kItemEnd)
     std::uint32_t pad[3];
+};
+
+// One lane segment of a work item, published by the producer with the
+// segment's query row.
+struct SegInfo {
+    std::uint32_t lane;
+    std::uint32_t query_row;
+    std::uint32_t item_offset;  // the lane's items (split-KV combine)
+    std::uint32_t item_count;
+    std::uint32_t first_sub;    // partial slot parity of the lane's first item
+    std::uint32_t part_slot;    // partial slot this segment writes when split
 };
 
 struct TmaArgs {
@@ -74,6 +95,7 @@ struct TmaArgs {
     std::uint32_t q_heads;
     std::uint32_t ts;             // tokens per stage
     std::uint32_t extent_per_head;  // 1: the extent map has per-head boxes (fallback)
+    std::uint32_t micro_per_head;   // 1: the micro map has per-head boxes (fallback)
     kk_page_desc const* descs;
     kk_attn_lane const* lanes;
     std::uint32_t num_lanes;
@@ -98,6 +120,14 @@ __device__ __forceinline__ void tma_load_5d(void* dst, CUtensorMap const* map, s
         " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
         ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(map)), "r"(smem_u32(bar)),
         "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, void const* src, std::uint32_t bytes, std::uint64_t* bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
 }
 
@@ -184,27 +214,6 @@ __device__ __forceinline__ std::uint32_t lane_desc_end(kk_attn_lane const& ln)
 // head): n-tile nt holds heads nt*8 .. nt*8+7 of KV head `head`; thread
 // (g = lane/4, c = lane%4) holds dims 2c, 2c+1 and 2c+8, 2c+9 of each 16-dim
 // k step for head nt*8+g. Heads past the group are zero.
-template <int NT>
-__device__ __forceinline__ void load_query(TmaArgs const& a, std::uint32_t row, std::uint32_t head,
-    std::uint32_t g, std::uint32_t c4, std::uint32_t (&qf)[NT][4][2])
-{
-    __half const* q = a.query + static_cast<std::uint64_t>(row) * a.query_stride
-        + static_cast<std::uint64_t>(head * a.group) * kHeadDim;
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        std::uint32_t const qh = nt * 8u + g;
-#pragma unroll
-        for (int k16 = 0; k16 < 4; ++k16) {
-#pragma unroll
-            for (int hi = 0; hi < 2; ++hi) {
-                std::uint32_t const col = k16 * 16 + hi * 8 + c4 * 2;
-                qf[nt][k16][hi] = qh < a.group
-                    ? *reinterpret_cast<std::uint32_t const*>(q + qh * kHeadDim + col) : 0u;
-            }
-        }
-    }
-}
-
 __device__ __forceinline__ std::uint32_t transpose8x8(std::uint32_t x)
 {
     std::uint32_t y;
@@ -221,17 +230,22 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     // The 128-byte swizzle pattern repeats every 1 KB: align the ring to 1 KB.
     std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     std::uint8_t* ring = smem_raw + pad;
-    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(ring + kStages * kStageBytes);
+    std::uint32_t const q_bytes = a.q_heads * kRowBytes;  // one query row, all heads
+    std::uint8_t* qbuf = ring + kStages * kStageBytes;     // [2][q_bytes], per lane segment
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(qbuf + 2 * q_bytes);
     std::uint64_t* empty = full + kStages;
-    StageMeta* meta = reinterpret_cast<StageMeta*>(empty + kStages);
-    float* s_m = reinterpret_cast<float*>(meta + kStages);    // [warp][16]
-    float* s_l = s_m + kConsumerWarps * 16;                    // [warp][16]
-    float* s_o = s_l + kConsumerWarps * 16;                    // [warp][8*NT][kORow]
-    int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 8 * NT * kORow);
-    int volatile* s_abort = s_last + 1;
+    std::uint64_t* q_full = empty + kStages;   // [2]: query row + SegInfo landed
+    std::uint64_t* q_empty = q_full + 2;       // [2]: every consumer warp took its query
     // Barrier of the consumer threads (the producer never joins). An mbarrier
     // rather than a named barrier, so that its waits are bounded too.
-    std::uint64_t* cbar = reinterpret_cast<std::uint64_t*>(s_last + 2);
+    std::uint64_t* cbar = q_empty + 2;
+    StageMeta* meta = reinterpret_cast<StageMeta*>(cbar + 1);
+    SegInfo* seg = reinterpret_cast<SegInfo*>(meta + kStages);  // [2]
+    float* s_m = reinterpret_cast<float*>(seg + 2);             // [warp][16]
+    float* s_l = s_m + kConsumerWarps * 16;                      // [warp][16]
+    float* s_o = s_l + kConsumerWarps * 16;                      // [warp][8*NT][kORow]
+    int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 8 * NT * kORow);
+    int volatile* s_abort = s_last + 1;
 
     std::uint32_t const warp = threadIdx.x / 32;
     std::uint32_t const lane = threadIdx.x % 32;
@@ -239,6 +253,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
+        }
+        for (int p = 0; p < 2; ++p) {
+            mbar_init(&q_full[p], 1);
+            mbar_init(&q_empty[p], kConsumerWarps);
         }
         mbar_init(cbar, kConsumerWarps * 32);
         *s_abort = 0;
@@ -263,7 +281,34 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         }
         bool waited = false;
         std::uint32_t stage = 0;
+        std::uint32_t qk = 0;  // lane segments started by this CTA
+        // Publishes lane segment qk to the consumers: its bookkeeping in
+        // seg[qk & 1] and its query row (all heads) copied into qbuf[qk & 1]
+        // by one bulk copy, both covered by q_full[qk & 1]. Consumers only
+        // read shared memory, so a new segment costs them no global round
+        // trip.
+        auto start_segment = [&](std::uint32_t it_, std::uint32_t first_lane, std::uint32_t lane_b) -> bool {
+            std::uint32_t const p = qk & 1u;
+            bool const ready = qk < 2u || wait_or_abort(&q_empty[p], ((qk >> 1) - 1u) & 1u, s_abort);
+            if (!__all_sync(0xffffffffu, ready)) {
+                return false;
+            }
+            kk_attn_lane const L = a.lanes[lane_b];
+            std::uint32_t const off = L.item_offset < num_items ? L.item_offset : 0u;
+            std::uint32_t const first_sub = a.items[off].lane == lane_b ? 0u : 1u;
+            if (lane == 0) {
+                seg[p] = SegInfo{lane_b, L.query_row, L.item_offset, L.item_count, first_sub,
+                    2u * it_ + (lane_b == first_lane ? 0u : 1u)};
+                mbar_expect_tx(&q_full[p], q_bytes);
+                bulk_load(qbuf + p * q_bytes,
+                    a.query + static_cast<std::uint64_t>(L.query_row) * a.query_stride, q_bytes, &q_full[p]);
+                mbar_arrive(&q_full[p]);  // releases seg[p]; the phase ends when the row lands
+            }
+            ++qk;
+            return true;
+        };
         for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
+
             kk_attn_item const item = a.items[it];
             std::uint32_t b = item.lane;
             if (b >= a.num_lanes) {
@@ -329,8 +374,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             };
             seek();
             if (!waited) {
-                pdl_wait();  // K/V pages of this layer are written by the previous kernel
+                pdl_wait();  // K/V pages and queries are written by the previous kernel
                 waited = true;
+            }
+            if (!start_segment(it, item.lane, b)) {
+                return;
             }
             for (;;) {
                 std::uint32_t const s = stage % kStages;
@@ -353,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         for (std::uint32_t j = 0; j < 8; ++j) {
                             std::uint32_t const first = tok + 8u * j;
                             std::uint32_t const left = j < groups_per_stage && first < vt ? vt - first : 0u;
-                            m.valid[j] = static_cast<std::uint8_t>(left < 8u ? left : 8u);
+                            m.valid |= std::uint64_t(left < 8u ? left : 8u) << (8u * j);
                         }
                         if (lane == 0) {
                             mbar_expect_tx(&full[s], 2u * Hkv * Ts * kRowBytes);
@@ -379,8 +427,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             seek();
                         }
                     } else {
-                        m.valid[n] = static_cast<std::uint8_t>(vt);
-                        if (lane == 0) {
+                        m.valid |= std::uint64_t(vt) << (8u * n);
+                        if (a.micro_per_head == 0) {
+                            m.flags |= kMicroStage;
+                            if (lane == 0) {
+                                mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
+                                std::uint8_t* dst = base + n * Hkv * 8u * kRowBytes;
+                                tma_load_5d(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot);
+                                tma_load_5d(dst + v_offset, &tm_micro, &full[s], 0, 0, 0,
+                                    static_cast<int>(kv + 1), slot);
+                            }
+                        } else if (lane == 0) {
                             mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
                             for (std::uint32_t h = 0; h < Hkv; ++h) {
                                 std::uint8_t* dst = base + (h * Ts + n * 8u) * kRowBytes;
@@ -396,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     }
                 }
                 bool item_done = false;
+                bool next_segment = false;
                 if (!have) {
                     // This lane's segment is exhausted: the next one starts at
                     // the next lane with descriptors (lanes are contiguous in
@@ -421,6 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             m.next_lane = b;
                             seg_end = lane_desc_end(a.lanes[b]);
                             seg_end = seg_end < item.desc_end ? seg_end : item.desc_end;
+                            next_segment = true;
                         }
                     }
                 }
@@ -431,6 +490,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 ++stage;
                 if (item_done) {
                     break;
+                }
+                if (next_segment && !start_segment(it, item.lane, b)) {
+                    return;
                 }
                 if (!have) {
                     seek();
@@ -458,24 +520,124 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     std::uint32_t const mi = lane >> 3;  // ldmatrix: which 8x8 matrix this lane addresses
     std::uint32_t const r8 = lane & 7;
     std::uint32_t stage = 0;
-    bool waited = false;
+    std::uint32_t ck = 0;  // lane segments consumed
     std::uint32_t cphase = 0;
     auto consumer_sync = [&]() {
         mbar_arrive(cbar);
         wait_or_abort(cbar, cphase, s_abort);
         cphase ^= 1u;
     };
+    // Takes lane segment ck from the producer: its bookkeeping and this
+    // warp's query fragments (B operand of S^T = K Q^T), then hands the query
+    // buffer back.
+    std::uint32_t qf[NT][4][2];
+    SegInfo si{};
+    auto begin_segment = [&]() -> bool {
+        std::uint32_t const p = ck & 1u;
+        if (*s_abort || !wait_or_abort(&q_full[p], (ck >> 1) & 1u, s_abort)) {
+            return false;
+        }
+        si = seg[p];
+        std::uint8_t const* q = qbuf + p * q_bytes + head * G * kRowBytes;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            std::uint32_t const qh = nt * 8u + g;
+#pragma unroll
+            for (int k16 = 0; k16 < 4; ++k16) {
+#pragma unroll
+                for (int hi = 0; hi < 2; ++hi) {
+                    std::uint32_t const col = k16 * 16 + hi * 8 + c4 * 2;
+                    qf[nt][k16][hi] = qh < G
+                        ? *reinterpret_cast<std::uint32_t const*>(q + qh * kRowBytes + col * 2u) : 0u;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&q_empty[p]);
+        }
+        ++ck;
+        return true;
+    };
+    // A split lane's completion count is taken at its segment end, but the
+    // answer (was this CTA the lane's last?) is read only at the next segment
+    // end or at the end of the CTA's work, so the atomic's round trip is off
+    // the critical path. The combine runs when the answer is read.
+    bool pending = false;
+    SegInfo pend{};
+    std::uint32_t pend_done = 0;  // meaningful in thread 0
+    auto combine = [&](SegInfo const& sg) {
+        // Every partial of lane sg.lane: item j = item_offset + i wrote slot
+        // 2j, except the lane's first item, which wrote slot 2j + 1 when it
+        // started with an earlier lane. Loads of four items are issued
+        // together and folded with an online rescale, so the combine costs a
+        // few L2 round trips whatever the lane's item count.
+        std::uint32_t const first = sg.item_offset;
+        std::uint32_t const count = sg.item_count;
+        for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
+            std::uint32_t const qh = idx / 8u;
+            std::uint32_t const d0 = (idx % 8u) * 8u;
+            float M = kNegInf;
+            float L = 0.f;
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (std::uint32_t i0 = 0; i0 < count; i0 += 4u) {
+                float2 ml[4];
+                float4 lo[4], hi[4];
+#pragma unroll
+                for (std::uint32_t k = 0; k < 4; ++k) {
+                    std::uint32_t const i = i0 + k;
+                    if (i < count) {
+                        std::uint64_t const sl = 2ull * (first + i) + (i == 0 ? sg.first_sub : 0u);
+                        std::uint64_t const prow = sl * a.q_heads + qh;
+                        ml[k] = __ldcg(reinterpret_cast<float2 const*>(a.part_ml) + prow);
+                        float4 const* po = reinterpret_cast<float4 const*>(a.part_o + prow * kHeadDim + d0);
+                        lo[k] = __ldcg(po);
+                        hi[k] = __ldcg(po + 1);
+                    } else {
+                        ml[k] = make_float2(kNegInf, 0.f);
+                        lo[k] = hi[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    }
+                }
+#pragma unroll
+                for (std::uint32_t k = 0; k < 4; ++k) {
+                    float const m_new = fmaxf(M, ml[k].x);
+                    float const m_use = m_new == kNegInf ? 0.f : m_new;
+                    float const fo = exp2f(M - m_use);       // rescale of what is folded so far
+                    float const fk = exp2f(ml[k].x - m_use);  // weight of partial k
+                    L = L * fo + ml[k].y * fk;
+                    acc[0] = acc[0] * fo + lo[k].x * fk;
+                    acc[1] = acc[1] * fo + lo[k].y * fk;
+                    acc[2] = acc[2] * fo + lo[k].z * fk;
+                    acc[3] = acc[3] * fo + lo[k].w * fk;
+                    acc[4] = acc[4] * fo + hi[k].x * fk;
+                    acc[5] = acc[5] * fo + hi[k].y * fk;
+                    acc[6] = acc[6] * fo + hi[k].z * fk;
+                    acc[7] = acc[7] * fo + hi[k].w * fk;
+                    M = m_new;
+                }
+            }
+            store_row8(a.output + static_cast<std::uint64_t>(sg.query_row) * a.output_stride
+                    + qh * kHeadDim + d0, acc, 1.f / L);
+        }
+        if (tid == 0) {
+            a.counters[sg.lane] = 0;  // ready for the next launch
+        }
+    };
+    // Reads the pending lane's answer (thread 0 wrote s_last before calling)
+    // and combines it if this CTA was the lane's last.
+    auto resolve_pending = [&]() {
+        consumer_sync();
+        if (*s_last) {
+            __threadfence();
+            combine(pend);
+        }
+        pending = false;
+    };
 
     for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
-        kk_attn_item const item = a.items[it];
-        std::uint32_t b = item.lane < a.num_lanes ? item.lane : 0u;
-        kk_attn_lane ln = a.lanes[b];
-        if (!waited) {
-            pdl_wait();  // queries are written by the previous kernel
-            waited = true;
+        if (!begin_segment()) {
+            break;
         }
-        std::uint32_t qf[NT][4][2];
-        load_query<NT>(a, ln.query_row, head, g, c4, qf);
         // Per query head (nt*8 + 2*c4 + e): running max (same in all 8 g-lanes)
         // and this lane's share of the softmax denominator.
         float mrow[NT][2], lrow[NT][2];
@@ -490,16 +652,23 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             }
         }
         for (;;) {
+
             std::uint32_t const s = stage % kStages;
             if (*s_abort || !wait_or_abort(&full[s], (stage / kStages) & 1u, s_abort)) {
                 break;
             }
             StageMeta const m = meta[s];
-            std::uint32_t const v0 = active ? m.valid[2 * chunk] : 0u;
-            std::uint32_t const v1 = active ? m.valid[2 * chunk + 1] : 0u;
+            std::uint32_t const pair =
+                chunk < 4u ? static_cast<std::uint32_t>(m.valid >> (16u * chunk)) & 0xffffu : 0u;
+            std::uint32_t const v0 = active ? (pair & 0xffu) : 0u;
+            std::uint32_t const v1 = active ? (pair >> 8) : 0u;
             if (v0 + v1 != 0) {
-                std::uint32_t const kbase =
-                    ring_base + s * kStageBytes + (head * Ts + chunk * 16u) * kRowBytes;
+                // Row of slice token r: r itself in an extent stage; in a
+                // micro stage token r lives in page 2*chunk + r/8, whose
+                // [head][8 tokens] block starts every kv_heads*8 rows.
+                std::uint32_t const step8 = (m.flags & kMicroStage) ? Hkv * 8u : 8u;
+                std::uint32_t const kbase = ring_base + s * kStageBytes
+                    + (head * ((m.flags & kMicroStage) ? 8u : Ts) + chunk * 2u * step8) * kRowBytes;
                 std::uint32_t const vbase = kbase + v_offset;
                 // S^T = K Q^T over the slice's 16 tokens: K rows are the A operand.
                 float st[NT][4];
@@ -509,10 +678,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
 #pragma unroll
                 for (std::uint32_t k16 = 0; k16 < 4; ++k16) {
-                    std::uint32_t const row = (mi & 1u) * 8u + r8;
+                    std::uint32_t const row = (mi & 1u) * step8 + r8;
                     std::uint32_t const ch = 2u * k16 + (mi >> 1);
                     std::uint32_t ka[4];
-                    ldsm_x4(kbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), ka);
+                    ldsm_x4(kbase + row * kRowBytes + ((ch ^ r8) << 4), ka);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
                         mma16816(st[nt], ka[0], ka[1], ka[2], ka[3], qf[nt][k16][0], qf[nt][k16][1]);
@@ -557,10 +726,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
 #pragma unroll
                 for (std::uint32_t j = 0; j < 4; ++j) {
-                    std::uint32_t const row = (mi >> 1) * 8u + r8;
+                    std::uint32_t const row = (mi >> 1) * step8 + r8;
                     std::uint32_t const ch = 2u * j + (mi & 1u);
                     std::uint32_t va[4];
-                    ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ (row & 7u)) << 4), va);
+                    ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ r8) << 4), va);
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) {
                         mma16816(o[nt][j], va[0] & mask0, va[1] & mask0, va[2] & mask1, va[3] & mask1,
@@ -600,96 +769,76 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
             }
             consumer_sync();
-            bool const split = ln.item_count > 1;
-            std::uint64_t const pslot = 2ull * it + (b == item.lane ? 0u : 1u);
+            // A split lane needs the caller's workspace; without one it is
+            // reported and its partial is dropped.
+            bool const split = si.item_count > 1 && a.part_o != nullptr;
+            if (si.item_count > 1 && a.part_o == nullptr && tid == 0) {
+                atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+            }
+            bool const keep = si.item_count <= 1 || split;
             for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
                 std::uint32_t const qh = idx / 8u;
                 std::uint32_t const d0 = (idx % 8u) * 8u;
                 std::uint32_t const h = qh / G;
-                std::uint32_t const g = qh % G;
+                std::uint32_t const gq = qh % G;
                 float M = kNegInf;
                 for (std::uint32_t sub = 0; sub < warps_per_head; ++sub) {
-                    M = fmaxf(M, s_m[(sub * Hkv + h) * 16 + g]);
+                    M = fmaxf(M, s_m[(sub * Hkv + h) * 16 + gq]);
                 }
                 float const m_use = M == kNegInf ? 0.f : M;
                 float L = 0.f;
                 float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
                 for (std::uint32_t sub = 0; sub < warps_per_head; ++sub) {
                     std::uint32_t const w = sub * Hkv + h;
-                    float const f = exp2f(s_m[w * 16 + g] - m_use);
-                    L += s_l[w * 16 + g] * f;
-                    float const* src = s_o + (w * 8 * NT + g) * kORow + d0;
+                    float const f = exp2f(s_m[w * 16 + gq] - m_use);
+                    L += s_l[w * 16 + gq] * f;
+                    float const* src = s_o + (w * 8 * NT + gq) * kORow + d0;
 #pragma unroll
                     for (int e = 0; e < 8; ++e) {
                         acc[e] += src[e] * f;
                     }
                 }
                 if (!split) {
-                    store_row8(a.output + static_cast<std::uint64_t>(ln.query_row) * a.output_stride
-                            + qh * kHeadDim + d0, acc, 1.f / L);
-                } else {
-                    std::uint64_t const prow = pslot * a.q_heads + qh;
-                    float* po = a.part_o + prow * kHeadDim + d0;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) {
-                        po[e] = acc[e];
-                    }
-                    if (d0 == 0) {
-                        a.part_ml[prow * 2] = M;
-                        a.part_ml[prow * 2 + 1] = L;
-                    }
-                }
-            }
-            if (split) {
-                __threadfence();
-                consumer_sync();
-                if (tid == 0) {
-                    std::uint32_t const done = atomicAdd(&a.counters[b], 1u);
-                    *s_last = done + 1 == ln.item_count;
-                }
-                consumer_sync();
-                if (*s_last) {
-                    __threadfence();
-                    for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
-                        std::uint32_t const qh = idx / 8u;
-                        std::uint32_t const d0 = (idx % 8u) * 8u;
-                        float M = kNegInf;
-                        for (std::uint32_t i = 0; i < ln.item_count; ++i) {
-                            std::uint32_t const j = ln.item_offset + i;
-                            std::uint64_t const sl = 2ull * j + (a.items[j].lane == b ? 0u : 1u);
-                            M = fmaxf(M, __ldcg(a.part_ml + (sl * a.q_heads + qh) * 2));
-                        }
-                        float const m_use = M == kNegInf ? 0.f : M;
-                        float L = 0.f;
-                        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-                        for (std::uint32_t i = 0; i < ln.item_count; ++i) {
-                            std::uint32_t const j = ln.item_offset + i;
-                            std::uint64_t const sl = 2ull * j + (a.items[j].lane == b ? 0u : 1u);
-                            std::uint64_t const prow = sl * a.q_heads + qh;
-                            float const f = exp2f(__ldcg(a.part_ml + prow * 2) - m_use);
-                            L += __ldcg(a.part_ml + prow * 2 + 1) * f;
-                            float const* po = a.part_o + prow * kHeadDim + d0;
-#pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                acc[e] += __ldcg(po + e) * f;
-                            }
-                        }
-                        store_row8(a.output + static_cast<std::uint64_t>(ln.query_row) * a.output_stride
+                    if (keep) {
+                        store_row8(a.output + static_cast<std::uint64_t>(si.query_row) * a.output_stride
                                 + qh * kHeadDim + d0, acc, 1.f / L);
                     }
-                    if (tid == 0) {
-                        a.counters[b] = 0;  // ready for the next launch
+                } else {
+                    std::uint64_t const prow = std::uint64_t(si.part_slot) * a.q_heads + qh;
+                    float4* po = reinterpret_cast<float4*>(a.part_o + prow * kHeadDim + d0);
+                    po[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                    po[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+                    if (d0 == 0) {
+                        reinterpret_cast<float2*>(a.part_ml)[prow] = make_float2(M, L);
                     }
                 }
             }
-            consumer_sync();  // s_m / s_l / s_o / s_last are reused by the next segment
+            // This segment's partial is written (CTA scope) and s_m / s_l / s_o
+            // are free for the next segment once every consumer is here.
+            consumer_sync();
+            if (tid == 0) {
+                if (pending) {
+                    *s_last = pend_done + 1 == pend.item_count;
+                }
+                if (split) {
+                    __threadfence();  // cumulative: publishes every thread's partial
+                    pend_done = atomicAdd(&a.counters[si.lane], 1u);
+                }
+            }
+            if (pending) {
+                resolve_pending();
+            }
+            if (split) {
+                pending = true;
+                pend = si;
+            }
             if (m.flags & kItemEnd) {
                 break;
             }
             // Next lane of this item.
-            b = m.next_lane < a.num_lanes ? m.next_lane : 0u;
-            ln = a.lanes[b];
-            load_query<NT>(a, ln.query_row, head, g, c4, qf);
+            if (!begin_segment()) {
+                break;
+            }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 mrow[nt][0] = mrow[nt][1] = kNegInf;
@@ -704,18 +853,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             break;
         }
     }
+    if (pending && !*s_abort) {
+        if (tid == 0) {
+            *s_last = pend_done + 1 == pend.item_count;
+        }
+        resolve_pending();
+    }
 }
 
-// Small enough (about 118 KB with NT = 1) that a projection CTA of the
-// neighbouring kernels fits on the same SM, so programmatic dependent launch
-// can overlap their prologues and tails with this kernel.
+// About 122 KB with NT = 1 at 32 query heads: small enough that a
+// projection CTA of the neighbouring kernels fits on the same SM, so
+// programmatic dependent launch can overlap their prologues and tails with
+// this kernel.
 template <int NT>
-constexpr std::size_t smemBytes()
+constexpr std::size_t smemBytes(std::uint32_t q_heads)
 {
-    return 1024 + kStages * kStageBytes + 2 * kStages * 8 + kStages * sizeof(StageMeta)
-        + 2 * kConsumerWarps * 16 * 4 + kConsumerWarps * 8 * NT * kORow * 4 + 24;
+    return 1024 + kStages * kStageBytes + 2ull * q_heads * kRowBytes
+        + (2 * kStages + 5) * 8 + kStages * sizeof(StageMeta) + 2 * sizeof(SegInfo)
+        + 2 * kConsumerWarps * 16 * 4 + kConsumerWarps * 8 * NT * kORow * 4 + 8;
 }
-static_assert(smemBytes<2>() <= 227 * 1024, "shared memory budget");
+static_assert(smemBytes<2>(128) <= 227 * 1024, "shared memory budget");
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
     cuuint64_t const*, cuuint64_t const*, cuuint32_t const*, cuuint32_t const*,
@@ -760,15 +917,16 @@ bool encodePerHead(CUtensorMap* map, void const* base, std::uint32_t pages, std:
     return encode(map, base, dims, strides, box);
 }
 
-// Head-major view [slot][layer*2+kv][kv_head][token][dim] of the extent pool
-// (token and head strides swapped), box = all heads x box_tokens tokens, so
-// that one load lands [head][token][dim] in shared memory.
-bool encodeHeadMajor(CUtensorMap* map, void const* base, std::uint32_t pages, std::uint32_t layers,
-    std::uint32_t heads, std::uint32_t box_tokens)
+// Head-major view [slot][layer*2+kv][kv_head][token][dim] of a pool of
+// `cap`-token pages (token and head strides swapped), box = all heads x
+// box_tokens tokens, so that one load lands [head][token][dim] in shared
+// memory.
+bool encodeHeadMajor(CUtensorMap* map, void const* base, std::uint32_t pages, std::uint32_t cap,
+    std::uint32_t layers, std::uint32_t heads, std::uint32_t box_tokens)
 {
     cuuint64_t const row = kRowBytes;
-    cuuint64_t const dims[5] = {kHeadDim, 64, heads, 2ull * layers, pages};
-    cuuint64_t const strides[4] = {row * heads, row, row * heads * 64, row * heads * 64 * 2ull * layers};
+    cuuint64_t const dims[5] = {kHeadDim, cap, heads, 2ull * layers, pages};
+    cuuint64_t const strides[4] = {row * heads, row, row * heads * cap, row * heads * cap * 2ull * layers};
     cuuint32_t const box[5] = {kHeadDim, box_tokens, heads, 1, 1};
     return encode(map, base, dims, strides, box);
 }
@@ -779,6 +937,7 @@ struct PoolMaps {
     CUtensorMap micro;
     CUtensorMap extent;
     bool extent_per_head;
+    bool micro_per_head;
 };
 
 std::uint32_t stageTokens(std::uint32_t kv_heads)
@@ -804,16 +963,20 @@ bool poolMaps(kk_kv_pools const& p, PoolMaps& out)
             return true;
         }
     }
-    PoolMaps e{p, device, {}, {}, false};
+    PoolMaps e{p, device, {}, {}, false, false};
     std::uint32_t const ts = stageTokens(p.kv_heads);
-    if (!encodePerHead(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+    if (encodeHeadMajor(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+        e.micro_per_head = false;
+    } else if (encodePerHead(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+        e.micro_per_head = true;
+    } else {
         return false;
     }
     if (p.extent == nullptr || p.extent_capacity == 0) {
         // No descriptor can select the extent map (extent_slots is 0).
         e.extent = e.micro;
         e.extent_per_head = true;
-    } else if (encodeHeadMajor(&e.extent, p.extent, p.extent_capacity, p.layers, p.kv_heads, ts)) {
+    } else if (encodeHeadMajor(&e.extent, p.extent, p.extent_capacity, 64, p.layers, p.kv_heads, ts)) {
         e.extent_per_head = false;
     } else if (encodePerHead(&e.extent, p.extent, p.extent_capacity, 64, p.layers, p.kv_heads, ts)) {
         e.extent_per_head = true;
@@ -859,9 +1022,9 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
         return KK_EINVAL;
     }
     static cudaError_t const attr1 = cudaFuncSetAttribute(paged_attention_tma_kernel<1>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<1>()));
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<1>(128)));
     static cudaError_t const attr2 = cudaFuncSetAttribute(paged_attention_tma_kernel<2>,
-        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<2>()));
+        cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<2>(128)));
     if (attr1 != cudaSuccess || attr2 != cudaSuccess) {
         return static_cast<int>(attr1 != cudaSuccess ? attr1 : attr2);
     }
@@ -874,6 +1037,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.q_heads = q_heads;
     a.ts = stageTokens(pools->kv_heads);
     a.extent_per_head = maps.extent_per_head ? 1u : 0u;
+    a.micro_per_head = maps.micro_per_head ? 1u : 0u;
     a.descs = descs;
     a.lanes = lanes;
     a.num_lanes = num_lanes;
@@ -892,7 +1056,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
     bool const narrow = a.group <= 8;
     auto const kernel = narrow ? paged_attention_tma_kernel<1> : paged_attention_tma_kernel<2>;
-    std::size_t const smem = narrow ? smemBytes<1>() : smemBytes<2>();
+    std::size_t const smem = narrow ? smemBytes<1>(q_heads) : smemBytes<2>(q_heads);
     return static_cast<int>(launch(kernel, dim3(grid), dim3(kThreads), smem, stream, 1,
         maps.micro, maps.extent, a));
 }

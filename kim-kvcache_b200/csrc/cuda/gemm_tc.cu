@@ -56,7 +56,11 @@ constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
 template <int BN>
 constexpr int stagesFor()
 {
+#ifdef KK_GEMM_STAGES
+    return KK_GEMM_STAGES;
+#else
     return 4;
+#endif
 }
 
 struct EpiArgs {

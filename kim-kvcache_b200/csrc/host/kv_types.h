@@ -223,6 +223,7 @@ public:
 
 private:
     friend class KvCacheManager;
+    friend class FixedPageManager;
     std::vector<MappingEntry> entries_;
     std::uint64_t version_{0};
 };

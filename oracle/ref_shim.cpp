@@ -8,6 +8,7 @@
 // identical operation streams on the reference and on the product runtime.
 #include "../include/kk_runtime.h"
 
+#include "kim-kv/fixed/fixed_page_manager.h"
 #include "kim-kv/model/weight_manifest.h"
 #include "kim-kv/reference/kv_reference.h"
 #include "kim-kv/runtime/kv_cache_manager.h"
@@ -20,6 +21,7 @@ using namespace kimkvcache;
 namespace {
 
 KvCacheManager* M(void* p) { return static_cast<KvCacheManager*>(p); }
+FixedPageManager* F(void* p) { return static_cast<FixedPageManager*>(p); }
 
 void tableOut(BlockTable const& t, kk_table_out* out)
 {
@@ -201,5 +203,52 @@ KK_API int kref_sha256_range(char const* data_path, uint64_t offset, uint64_t by
     std::memcpy(out, digest.c_str(), digest.size() + 1);
     return 0;
 }
+
+KK_API void* kref_fixed_create(uint16_t tokens, uint32_t capacity)
+{
+    try {
+        return new FixedPageManager(tokens, capacity);
+    } catch (...) {
+        return nullptr;
+    }
+}
+KK_API void kref_fixed_destroy(void* p) { delete F(p); }
+KK_API uint32_t kref_fixed_tokens_per_page(void* p) { return F(p)->tokensPerPage(); }
+KK_API int kref_fixed_create_request(void* p, uint64_t id) { return int(F(p)->createRequest(id)); }
+KK_API int kref_fixed_append(void* p, uint64_t id, uint32_t n) { return int(F(p)->append(id, n)); }
+KK_API int kref_fixed_reserve_token(void* p, uint64_t id, uint32_t expected, uint64_t* rid,
+    kk_table_out* before, kk_table_out* reserved)
+{
+    TokenReservationResult const r = F(p)->reserveToken(id, expected);
+    if (rid != nullptr) *rid = r.reservation_id;
+    tableOut(r.before, before);
+    tableOut(r.reserved, reserved);
+    return int(r.error);
+}
+KK_API int kref_fixed_commit_reservation(void* p, uint64_t id) { return int(F(p)->commitTokenReservation(id)); }
+KK_API int kref_fixed_rollback_reservation(void* p, uint64_t id)
+{
+    return int(F(p)->rollbackTokenReservation(id));
+}
+KK_API int kref_fixed_seal_tail(void* p, uint64_t id) { return int(F(p)->sealTail(id)); }
+KK_API int kref_fixed_fork(void* p, uint64_t s, uint64_t c) { return int(F(p)->forkRequest(s, c)); }
+KK_API int kref_fixed_release(void* p, uint64_t id) { return int(F(p)->releaseRequest(id)); }
+KK_API int kref_fixed_block_table(void* p, uint64_t id, kk_table_out* out)
+{
+    std::optional<BlockTable> const t = F(p)->blockTable(id);
+    if (!t) return 0;
+    tableOut(*t, out);
+    return 1;
+}
+KK_API void kref_fixed_snapshot(void* p, kk_fixed_snapshot* out)
+{
+    FixedPageManagerSnapshot const s = F(p)->snapshot();
+    out->request_count = s.request_count;
+    out->successful_allocations = s.successful_allocations;
+    out->peak_allocated_pages = s.peak_allocated_pages;
+    out->token_reservation_count = s.token_reservation_count;
+    poolOut(s.pool, &out->pool);
+}
+KK_API int kref_fixed_check_invariants(void* p) { return F(p)->checkInvariants() ? 1 : 0; }
 
 } // extern "C"

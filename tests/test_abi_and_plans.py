@@ -96,23 +96,33 @@ def test_balanced_plan_covers_and_balances(kk, seed, parts):
         assert n == 0
         return
     check_cover(kk, descs, lanes, items, n, multi_lane=True)
-    per = -(-total // parts)
-    sizes = [sum(descs[e].valid_tokens for e in range(items[i].desc_begin, items[i].desc_end))
-             for i in range(n)]
-    # every cut is made as soon as the run reaches `per` tokens: no run exceeds
-    # per + one page, and all runs but the last reach `per`
-    assert max(sizes) < per + 64
-    assert all(s >= per for s in sizes[:-1])
+    # Cost model: every token plus SEG per lane segment start. Each cut is the
+    # page boundary nearest to k * total_cost / parts, off by at most half a
+    # page plus one segment charge.
+    SEG = 48
+    starts = {lanes[b].desc_offset for b in range(len(contexts)) if lanes[b].desc_count}
+    total_cost = total + SEG * len(starts)
+    per = total_cost / parts
+    costs = [sum(descs[e].valid_tokens + (SEG if e in starts else 0)
+                 for e in range(items[i].desc_begin, items[i].desc_end)) for i in range(n)]
     assert n <= parts
+    assert max(costs) <= per + 2 * (32 + SEG) + 1
+    if per >= 128:
+        assert n == parts
+        assert min(costs) >= per - 2 * (32 + SEG) - 1
 
 
 def test_balanced_plan_counts_items_beyond_capacity(kk):
     K = kk.kernels()
     descs, lanes, nd = make_tables(kk, [640, 640], 1)
+    full = (kk.AttnItem * 64)()
+    n_full = K["attention_plan_balanced"](descs, lanes, 2, 20, full, 64)
     items = (kk.AttnItem * 2)()
     n = K["attention_plan_balanced"](descs, lanes, 2, 20, items, 2)
-    assert n == 20  # 1280 tokens in runs of 64
-    assert items[1].desc_begin == 1
+    assert n == n_full and n > 2   # counted, not written
+    for i in range(2):
+        assert (items[i].lane, items[i].desc_begin, items[i].desc_end) == \
+            (full[i].lane, full[i].desc_begin, full[i].desc_end)
 
 
 def test_balanced_plan_does_not_join_non_contiguous_lanes(kk):

@@ -413,7 +413,7 @@ def _oracle_prompt(s, rid, toks, first):
     return int(want[0]), logits
 
 
-@pytest.mark.parametrize("batch,lengths", [(8, [150]), (16, [13, 37, 1, 64, 9]), (32, [200])])
+@pytest.mark.parametrize("batch,lengths", [(8, [150]), (16, [13, 37, 1, 64, 9]), (32, [200]), (64, [300, 77])])
 def test_fused_prefill_matches_per_position_oracle(kk, tmp_path, batch, lengths):
     """kkrt_runner_prefill: the prompt runs as chunks of up to max_batch_size
     consecutive positions of one request, each attending causally to tokens
