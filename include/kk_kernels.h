@@ -84,7 +84,9 @@ typedef struct kk_attn_lane {
     uint32_t item_offset;      /* filled by kk_attention_plan */
     uint32_t item_count;       /* filled by kk_attention_plan */
     uint32_t query_row;        /* row of query / output used by this lane */
-    uint32_t reserved[2];
+    uint32_t first_item_shared; /* filled by the planners: 1 when the lane's first item
+                                   begins in an earlier lane */
+    uint32_t reserved;
 } kk_attn_lane;
 
 /* A split-KV work item: a run [desc_begin, desc_end) of the descriptor array.
@@ -112,7 +114,7 @@ KK_KAPI uint32_t kk_attention_plan(const kk_page_desc* host_descs, kk_attn_lane*
  * token stream, lane after lane, into about num_parts runs of equal token
  * count at page granularity (use the SM count: one run per SM). Runs may span
  * lanes; a lane split across runs is combined by the split-KV combine. Fills
- * item_offset/item_count of every lane; returns the item count (items beyond
+ * item_offset/item_count/first_item_shared of every lane; returns the item count (items beyond
  * max_items are counted, not written). Served by the TMA kernel only. */
 KK_KAPI uint32_t kk_attention_plan_balanced(const kk_page_desc* host_descs,
     kk_attn_lane* host_lanes, uint32_t num_lanes, uint32_t num_parts, kk_attn_item* host_items,

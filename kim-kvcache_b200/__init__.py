@@ -358,7 +358,7 @@ class AttnLane(C.Structure):
     _fields_ = [("desc_offset", C.c_uint32), ("desc_count", C.c_uint32),
                 ("token_count", C.c_uint32), ("item_offset", C.c_uint32),
                 ("item_count", C.c_uint32), ("query_row", C.c_uint32),
-                ("reserved", C.c_uint32 * 2)]
+                ("first_item_shared", C.c_uint32), ("reserved", C.c_uint32)]
 
 
 class AttnItem(C.Structure):

@@ -580,6 +580,7 @@ uint32_t kk_attention_plan(const kk_page_desc* descs, kk_attn_lane* lanes, uint3
         kk_attn_lane& ln = lanes[b];
         ln.item_offset = count;
         ln.item_count = 0;
+        ln.first_item_shared = 0;
         std::uint32_t begin = ln.desc_offset;
         std::uint32_t tokens = 0;
         std::uint32_t const end = ln.desc_offset + ln.desc_count;
@@ -607,9 +608,14 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
         num_parts = 1;
     }
     // Cost model of the token stream, in tokens: every token, plus a fixed
-    // charge per lane for the merge and partial write a CTA makes at the end
-    // of each lane segment (about one and a half 32-token stages).
-    constexpr std::uint64_t kSegmentCost = 48;
+    // charge per lane for what a CTA spends at the end of each lane segment
+    // (merge, partial write, completion count and combine), measured at
+    // about four and a half 32-token stages on B200.
+#ifdef KK_PLAN_SEGMENT_COST
+    constexpr std::uint64_t kSegmentCost = KK_PLAN_SEGMENT_COST;
+#else
+    constexpr std::uint64_t kSegmentCost = 144;
+#endif
     std::uint64_t total = 0;
     for (std::uint32_t b = 0; b < num_lanes; ++b) {
         if (lanes[b].desc_count != 0) {
@@ -639,6 +645,7 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
         kk_attn_lane& ln = lanes[b];
         ln.item_offset = count;
         ln.item_count = 0;
+        ln.first_item_shared = 0;
         std::uint32_t const end = ln.desc_offset + ln.desc_count;
         // An item only continues into this lane when the descriptors are contiguous.
         if (open && cur.desc_end != ln.desc_offset) {
@@ -671,6 +678,7 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
             if (ln.item_count == 0 || ln.item_offset + ln.item_count != count) {
                 if (ln.item_count == 0) {
                     ln.item_offset = count - 1;
+                    ln.first_item_shared = cur.lane != b ? 1u : 0u;
                 }
                 ++ln.item_count;
             }

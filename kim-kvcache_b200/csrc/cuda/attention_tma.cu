@@ -82,7 +82,7 @@ struct SegInfo {
     std::uint32_t query_row;
     std::uint32_t item_offset;  // the lane's items (split-KV combine)
     std::uint32_t item_count;
-    std::uint32_t first_sub;    // partial slot parity of the lane's first item
+    std::uint32_t first_sub;    // 1: the lane's first item wrote its second slot
     std::uint32_t part_slot;    // partial slot this segment writes when split
 };
 
@@ -287,18 +287,15 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         // by one bulk copy, both covered by q_full[qk & 1]. Consumers only
         // read shared memory, so a new segment costs them no global round
         // trip.
-        auto start_segment = [&](std::uint32_t it_, std::uint32_t first_lane, std::uint32_t lane_b) -> bool {
+        auto start_segment = [&](kk_attn_lane const& L, std::uint32_t lane_b, std::uint32_t part_slot) -> bool {
             std::uint32_t const p = qk & 1u;
             bool const ready = qk < 2u || wait_or_abort(&q_empty[p], ((qk >> 1) - 1u) & 1u, s_abort);
             if (!__all_sync(0xffffffffu, ready)) {
                 return false;
             }
-            kk_attn_lane const L = a.lanes[lane_b];
-            std::uint32_t const off = L.item_offset < num_items ? L.item_offset : 0u;
-            std::uint32_t const first_sub = a.items[off].lane == lane_b ? 0u : 1u;
             if (lane == 0) {
-                seg[p] = SegInfo{lane_b, L.query_row, L.item_offset, L.item_count, first_sub,
-                    2u * it_ + (lane_b == first_lane ? 0u : 1u)};
+                seg[p] = SegInfo{lane_b, L.query_row, L.item_offset, L.item_count, L.first_item_shared ? 1u : 0u,
+                    part_slot};
                 mbar_expect_tx(&q_full[p], q_bytes);
                 bulk_load(qbuf + p * q_bytes,
                     a.query + static_cast<std::uint64_t>(L.query_row) * a.query_stride, q_bytes, &q_full[p]);
@@ -317,7 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
                 b = 0;
             }
-            std::uint32_t seg_end = lane_desc_end(a.lanes[b]);
+            // Lane records are read before griddepcontrol.wait (host data),
+            // and the next lane's record is requested one segment ahead.
+            kk_attn_lane cur_lane = a.lanes[b];
+            kk_attn_lane next_lane = a.lanes[b + 1 < a.num_lanes ? b + 1 : b];
+            std::uint32_t seg_end = lane_desc_end(cur_lane);
             seg_end = seg_end < item.desc_end ? seg_end : item.desc_end;
             // 32 descriptors at a time, one per lane, broadcast with shuffles.
             std::uint32_t win = item.desc_begin;
@@ -377,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 pdl_wait();  // K/V pages and queries are written by the previous kernel
                 waited = true;
             }
-            if (!start_segment(it, item.lane, b)) {
+            if (!start_segment(cur_lane, b, 2u * it)) {
                 return;
             }
             for (;;) {
@@ -465,10 +466,13 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         item_done = true;
                     } else {
                         std::uint32_t nb = b + 1;
-                        while (nb < a.num_lanes && a.lanes[nb].desc_count == 0) {
-                            ++nb;
+                        if (nb < a.num_lanes) {
+                            cur_lane = next_lane;  // lanes[b + 1], requested a segment ago
+                            while (cur_lane.desc_count == 0 && ++nb < a.num_lanes) {
+                                cur_lane = a.lanes[nb];
+                            }
                         }
-                        if (nb >= a.num_lanes || a.lanes[nb].desc_offset != e) {
+                        if (nb >= a.num_lanes || cur_lane.desc_offset != e) {
                             if (lane == 0) {
                                 atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
                             }
@@ -477,7 +481,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         } else {
                             b = nb;
                             m.next_lane = b;
-                            seg_end = lane_desc_end(a.lanes[b]);
+                            next_lane = a.lanes[b + 1 < a.num_lanes ? b + 1 : b];
+                            seg_end = lane_desc_end(cur_lane);
                             seg_end = seg_end < item.desc_end ? seg_end : item.desc_end;
                             next_segment = true;
                         }
@@ -491,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 if (item_done) {
                     break;
                 }
-                if (next_segment && !start_segment(it, item.lane, b)) {
+                if (next_segment && !start_segment(cur_lane, b, 2u * it + 1u)) {
                     return;
                 }
                 if (!have) {
@@ -566,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     bool pending = false;
     SegInfo pend{};
     std::uint32_t pend_done = 0;  // meaningful in thread 0
+    std::uint32_t pend_stage = 0;
     auto combine = [&](SegInfo const& sg) {
         // Every partial of lane sg.lane: item j = item_offset + i wrote slot
         // 2j, except the lane's first item, which wrote slot 2j + 1 when it
@@ -743,6 +749,15 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             }
             ++stage;
             if ((m.flags & kSegEnd) == 0) {
+                // Two stages after a split lane's completion count was taken
+                // its answer has arrived: combine now, while the producer
+                // keeps the ring full, rather than at the next segment end.
+                if (pending && stage == pend_stage + 2u) {
+                    if (tid == 0) {
+                        *s_last = pend_done + 1 == pend.item_count;
+                    }
+                    resolve_pending();
+                }
                 continue;
             }
 
@@ -831,6 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             if (split) {
                 pending = true;
                 pend = si;
+                pend_stage = stage;
             }
             if (m.flags & kItemEnd) {
                 break;

@@ -379,7 +379,7 @@ private:
         }
         std::memcpy(host + Arena::kCopyOff, &copy, sizeof(copy));
         kk_attn_lane lane{descOffset() + static_cast<std::uint32_t>(Arena::kDescOff / sizeof(kk_page_desc)),
-            static_cast<std::uint32_t>(entries.size()), reserved_.tokenCount(), 0, 1, 0, {0, 0}};
+            static_cast<std::uint32_t>(entries.size()), reserved_.tokenCount(), 0, 1, 0, 0, 0};
         std::memcpy(host + Arena::kLaneOff, &lane, sizeof(lane));
         kk_attn_item item{0, lane.desc_offset, lane.desc_offset + lane.desc_count, 0};
         std::memcpy(host + Arena::kItemOff, &item, sizeof(item));
@@ -534,7 +534,7 @@ void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
         std::uint32_t const count = static_cast<std::uint32_t>(t->reserved_.entries().size());
         std::uint32_t const row = static_cast<std::uint32_t>(
             (reinterpret_cast<std::uint8_t const*>(r.device_query) - qmin) / row_bytes);
-        lanes[j] = kk_attn_lane{off, count, t->reserved_.tokenCount(), static_cast<std::uint32_t>(j), 1, row, {0, 0}};
+        lanes[j] = kk_attn_lane{off, count, t->reserved_.tokenCount(), static_cast<std::uint32_t>(j), 1, row, 0, 0};
         items[j] = kk_attn_item{static_cast<std::uint32_t>(j), off, off + count, 0};
     }
     cudaStream_t const s = static_cast<cudaStream_t>(stream_);

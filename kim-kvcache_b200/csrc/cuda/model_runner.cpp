@@ -441,7 +441,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
             return result;
         }
         lanes[b] = kk_attn_lane{n_descs, static_cast<std::uint32_t>(entries.size()),
-            lane.reserved->tokenCount(), 0, 0, b, {0, 0}};
+            lane.reserved->tokenCount(), 0, 0, b, 0, 0};
         for (MappingEntry const& e : entries) {
             descs[n_descs++] = kk_page_desc{e.handle.slot, e.logical_token_begin, e.valid_tokens,
                 static_cast<std::uint8_t>(e.kind), 0, 0};
@@ -608,7 +608,7 @@ GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId i
         if (!placed) {
             return {false, 0, "appended table does not cover the prompt position"};
         }
-        lanes[i] = kk_attn_lane{lane_first, n_descs - lane_first, p + 1, 0, 0, i, {0, 0}};
+        lanes[i] = kk_attn_lane{lane_first, n_descs - lane_first, p + 1, 0, 0, i, 0, 0};
     }
     std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, n, im.sm_count,
         im.stepHost<kk_attn_item>(im.off_items), im.max_items);

@@ -80,6 +80,9 @@ def check_cover(kk, descs, lanes, items, n_items, multi_lane):
     for b in range(nl):
         got = list(range(lanes[b].item_offset, lanes[b].item_offset + lanes[b].item_count))
         assert got == touched[b], (b, got, touched[b])
+        # the lane's first item begins in an earlier lane exactly when flagged
+        shared = bool(got) and items[got[0]].lane != b
+        assert lanes[b].first_item_shared == int(shared), b
 
 
 @pytest.mark.parametrize("seed", range(6))
@@ -99,7 +102,7 @@ def test_balanced_plan_covers_and_balances(kk, seed, parts):
     # Cost model: every token plus SEG per lane segment start. Each cut is the
     # page boundary nearest to k * total_cost / parts, off by at most half a
     # page plus one segment charge.
-    SEG = 48
+    SEG = 144
     starts = {lanes[b].desc_offset for b in range(len(contexts)) if lanes[b].desc_count}
     total_cost = total + SEG * len(starts)
     per = total_cost / parts
