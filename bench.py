@@ -324,11 +324,14 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
     for _ in range(3):
         launch_all(sptr)
     torch.cuda.synchronize()
-    # One launch per layer, replayed from a CUDA graph (as in the decode step),
-    # timed with events on the stream the graph runs on.
+    # One launch per layer, replayed from a CUDA graph with programmatic
+    # dependent launch (as in the decode step), timed with events on the
+    # stream the graph runs on.
     graph = torch.cuda.CUDAGraph()
+    K["set_pdl"](1)
     with torch.cuda.graph(graph):
         launch_all(C.c_void_p(torch.cuda.current_stream().cuda_stream))
+    K["set_pdl"](0)
     graph.replay()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

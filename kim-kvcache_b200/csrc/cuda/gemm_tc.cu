@@ -26,10 +26,14 @@
 //    accumulate in TMEM) and releases stages with tcgen05.commit;
 //  * all 4 warps drain TMEM with tcgen05.ld.
 // The K dimension is split across the CTAs of a thread-block cluster (up to 8);
-// each CTA parks its FP32 partial tile in shared memory and, after a cluster
-// barrier, reduces a disjoint subset of the batch columns over all CTAs'
-// partials through distributed shared memory (fixed order: deterministic),
-// then runs the fused epilogue for those columns.
+// each CTA owns a disjoint subset of the batch columns. After a cluster
+// barrier every CTA pushes each owner's columns of its FP32 partial tile into
+// the owner's receive buffer with one bulk shared::cluster copy per owner
+// (completion counted on the owner's mbarrier), so the reduction reads only
+// local shared memory, in rank order (deterministic), and then runs the fused
+// epilogue for those columns. Epilogue inputs (residual rows, RoPE positions,
+// KV slots) are requested right after the dependency wait, while the tile
+// streams.
 // No TMA multicast is used anywhere.
 #include "../../../include/kk_kernels.h"
 #include "kernels_internal.h"
@@ -48,11 +52,12 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
-// Four W+X stages: about 82 KB at N <= 32, so an attention CTA or a second
-// kernel's projection CTA fits beside this one on an SM and can start (and
-// prefetch its weights under programmatic dependent launch) while this
-// kernel drains. Measured on the decode step, 4 beats 3 and 5. The epilogue's
-// partial and reduced tiles reuse the ring (at most 66 KB, BN = 64).
+// Four W+X stages: with the split-K receive buffer about 102 KB at N <= 32,
+// so an attention CTA or a second projection CTA fits beside this one on an
+// SM and can start (and prefetch its weights under programmatic dependent
+// launch) while this kernel drains. Measured on the decode step, 4 beats 3
+// and 5. The epilogue's partial and reduced tiles reuse the ring (at most
+// 66 KB, BN = 64).
 template <int BN>
 constexpr int stagesFor()
 {
@@ -102,6 +107,35 @@ struct GemmArgs {
     EpiArgs epi;
 };
 
+// Generic-proxy writes to shared memory, made visible to bulk copies that
+// read it afterwards (async proxy).
+__device__ __forceinline__ void fence_proxy_async_smem()
+{
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Bulk copy of `bytes` from this CTA's shared memory into another CTA of the
+// cluster (dst and bar are shared::cluster addresses from mapa); completion
+// is counted on the destination CTA's mbarrier.
+__device__ __forceinline__ void bulk_copy_to_peer(std::uint32_t dst, void const* src, std::uint32_t bytes,
+    std::uint32_t bar)
+{
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void cluster_arrive()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void cluster_wait()
+{
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ bool better(float v, std::uint32_t i, float bv, std::uint32_t bi)
 {
     return v > bv || (v == bv && i < bi);
@@ -113,10 +147,19 @@ constexpr std::uint32_t tmemCols()
     return BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
 }
 
+// Receive buffer of the split-K reduction, outside the ring so that peers
+// can push into it while this CTA's MMAs still read the ring: one slot of
+// ceil(N/S) FP32 columns per source rank, at most (BN + 7) columns in all.
+template <int BN>
+constexpr std::size_t recvBytes()
+{
+    return std::size_t(BN + 7) * kBM * 4;
+}
+
 template <int BN>
 constexpr std::size_t smemBytes()
 {
-    return 1024 /* alignment slack */ + stagesFor<BN>() * (kTileWBytes + BN * 128)
+    return 1024 /* alignment slack */ + stagesFor<BN>() * (kTileWBytes + BN * 128) + recvBytes<BN>()
         + 1024 /* barriers + scratch */;
 }
 
@@ -131,10 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint8_t* smem = smem_raw + pad;
     std::uint8_t* w_stage = smem;
     std::uint8_t* x_stage = smem + kStages * kTileWBytes;
-    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(x_stage + kStages * BN * 128);
+    float* recv = reinterpret_cast<float*>(x_stage + kStages * BN * 128);
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(reinterpret_cast<std::uint8_t*>(recv) + recvBytes<BN>());
     std::uint64_t* empty = full + kStages;
     std::uint64_t* accum = empty + kStages;
-    std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(accum + 1);
+    std::uint64_t* rbar = accum + 1;  // this CTA's receive buffer is complete
+    std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(rbar + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 4);
     float* rnorm = reinterpret_cast<float*>(flag + 4);  // [BN] per-column RMS factors
 
@@ -154,6 +199,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             mbar_init(&empty[s], 1);
         }
         mbar_init(accum, 1);
+        mbar_init(rbar, 1);
+        if (S > 1) {
+            // Armed now: peers may push as soon as their own partial is ready.
+            mbar_arrive_expect_tx(rbar, ((rank + 1) * args.N / S - rank * args.N / S) * S * kBM * 4u);
+        }
         fence_barrier_init();
         prefetch_tensormap(&tm_w);
         prefetch_tensormap(&tm_x);
@@ -165,6 +215,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (S > 1) {
+        // Cluster barrier phase 1, arrive: this CTA's barriers are initialised
+        // and armed. The matching wait comes just before the first push.
+        cluster_arrive();
+    }
     std::uint32_t const tmem = *tmem_slot;
     // Dependents may launch now: they only prefetch weights before their own
     // griddepcontrol.wait, which returns once this grid has completed.
@@ -229,6 +284,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     // loop) until their lane 0 has finished its role.
     __syncwarp();
     pdl_wait();
+    // Epilogue inputs of this CTA's columns, requested now so that they are
+    // in registers when the reduced tile is ready: the residual rows (written
+    // by the previous kernel, hence after the wait) and the RoPE positions
+    // and KV slots of the QKV epilogue.
+    constexpr std::uint32_t kPre = 8;
+    std::uint32_t const pn0 = rank * args.N / S;
+    std::uint32_t const pcols = (rank + 1) * args.N / S - pn0;
+    std::uint32_t const pm = m_tile * kBM + tid;
+    bool const prefetched = pcols <= kPre;
+    __half resid[kPre];
+    std::uint32_t pos[kPre];
+    kk_kv_slot kvs[kPre];
+#pragma unroll
+    for (std::uint32_t j = 0; j < kPre; ++j) {
+        resid[j] = __float2half_rn(0.f);
+        pos[j] = 0;
+        kvs[j] = kk_kv_slot{0, 0, 0, 0};
+        if (prefetched && j < pcols) {
+            std::uint32_t const n = pn0 + j;
+            if (args.epi.kind == KK_EPI_RESIDUAL && pm < args.M) {
+                resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(n) * args.epi.out_stride + pm];
+            } else if (args.epi.kind == KK_EPI_QKV_ROPE) {
+                pos[j] = args.epi.positions[n];
+                kvs[j] = args.epi.slots[n];
+            }
+        }
+    }
     if (args.norm_x != nullptr && warp >= 2) {
         // While the tile streams: RMSNorm factors of this CTA's output columns,
         // r[n] = rsqrt(mean_k x[n][k]^2 + eps), one warp per column.
@@ -271,56 +353,52 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             part[(c0 + j) * kBM + row] = have_acc && nk != 0 ? v[j] : 0.f;
         }
     }
-    tc_fence_before();
-    __syncthreads();
-    if (S > 1) {
-        cluster_sync();
-    }
-
     std::uint32_t const n0 = rank * args.N / S;
     std::uint32_t const n1 = (rank + 1) * args.N / S;
     std::uint32_t const cols = n1 - n0;
     std::uint32_t const m = m_tile * kBM + row;
     EpiArgs const& e = args.epi;
-    // This CTA reduces columns [n0, n1) of the tile over the cluster's K
-    // slices, in rank order, into red[n - n0][row] (the ring is idle now and
-    // `part` stays untouched for the peers still reading it). Remote loads of
-    // four columns are issued before any is summed.
+    // The receive buffer holds one slot of up to cw columns per source rank;
+    // the reduced columns and the argmax scratch follow the partial in the
+    // (now idle) ring.
+    std::uint32_t const cw = (args.N + S - 1) / S;
     float* red = part + BN * kBM;
-    float* amax_v = red + BN * kBM;                                          // [4][BN]
+    float* amax_v = red + (S > 1 ? cw : static_cast<std::uint32_t>(BN)) * kBM;  // [4][BN]
     std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4 * BN);  // [4][BN]
-    {
-        std::uint32_t remote[8];
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            remote[r] = (S > 1 && static_cast<std::uint32_t>(r) < S) ? cluster_map(part, r) : smem_u32(part);
+    if (S > 1) {
+        fence_proxy_async_smem();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (S > 1) {
+        // The partial is written; every peer's receive buffer is armed (phase
+        // 1 of the cluster barrier, long complete by now). Thread r pushes
+        // owner r's columns.
+        cluster_wait();
+        if (tid < S) {
+            std::uint32_t const r0 = tid * args.N / S;
+            std::uint32_t const r1 = (tid + 1) * args.N / S;
+            if (r1 > r0) {
+                bulk_copy_to_peer(cluster_map(recv + rank * cw * kBM, tid), part + r0 * kBM,
+                    (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
+            }
         }
-        for (std::uint32_t n = n0; n < n1; n += 4) {
-            float vals[4][8];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    vals[j][r] = 0.f;
-                    if (n + j < n1 && static_cast<std::uint32_t>(r) < S) {
-                        vals[j][r] = S > 1 ? ld_cluster_f32(remote[r] + ((n + j) * kBM + row) * 4u)
-                                           : part[(n + j) * kBM + row];
-                    }
-                }
+        bool const got = mbar_wait(rbar, 0, &g_gemm_status);
+        // Sum over the K slices in rank order (deterministic).
+        for (std::uint32_t j = 0; j < cols; ++j) {
+            float acc = 0.f;
+            for (std::uint32_t r = 0; r < S; ++r) {
+                acc += got ? recv[(r * cw + j) * kBM + row] : 0.f;
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float acc = 0.f;
-#pragma unroll
-                for (int r = 0; r < 8; ++r) {
-                    if (static_cast<std::uint32_t>(r) < S) {
-                        acc += vals[j][r];
-                    }
-                }
-                if (n + j < n1) {
-                    red[(n + j - n0) * kBM + row] = args.norm_x != nullptr ? acc * rnorm[n + j - n0] : acc;
-                }
-            }
+            red[j * kBM + row] = args.norm_x != nullptr ? acc * rnorm[j] : acc;
+        }
+        // Cluster barrier phase 2, arrive: this CTA has received everything,
+        // so the senders' partials may go.
+        cluster_arrive();
+    } else {
+        for (std::uint32_t j = 0; j < cols; ++j) {
+            float const acc = part[(n0 + j) * kBM + row];
+            red[j * kBM + row] = args.norm_x != nullptr ? acc * rnorm[j] : acc;
         }
     }
     __syncthreads();
@@ -343,9 +421,19 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         break;
     case KK_EPI_RESIDUAL:
         if (m < args.M) {
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                __half* h = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
-                *h = __hadd(*h, __float2half_rn(red[j * kBM + row]));
+            if (prefetched) {
+#pragma unroll
+                for (std::uint32_t j = 0; j < kPre; ++j) {
+                    if (j < cols) {
+                        static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] =
+                            __hadd(resid[j], __float2half_rn(red[j * kBM + row]));
+                    }
+                }
+            } else {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    __half* h = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
+                    *h = __hadd(*h, __float2half_rn(red[j * kBM + row]));
+                }
             }
         }
         break;
@@ -370,13 +458,28 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
         std::uint32_t const d = idx & 63u;
         float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+#pragma unroll 1
         for (std::uint32_t j = 0; j < cols; ++j) {
             std::uint32_t const n = n0 + j;
+            // Prefetched values when the CTA owns at most kPre columns.
+            std::uint32_t position = 0;
+            kk_kv_slot slot_rec{0, 0, 0, 0};
+#pragma unroll
+            for (std::uint32_t q = 0; q < kPre; ++q) {
+                if (prefetched && q == j) {
+                    position = pos[q];
+                    slot_rec = kvs[q];
+                }
+            }
+            if (!prefetched) {
+                position = e.positions[n];
+                slot_rec = e.slots[n];
+            }
             float const mine = __half2float(__float2half_rn(red[j * kBM + row]));
             float out = mine;
             if (!is_v) {
                 float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
-                float const angle = static_cast<float>(e.positions[n]) * inv_freq;
+                float const angle = static_cast<float>(position) * inv_freq;
                 float const c = cosf(angle);
                 float const s = sinf(angle);
                 out = d < 32u ? mine * c - other * s : mine * c + other * s;
@@ -385,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             if (m < e.q_rows) {
                 static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + idx] = hv;
             } else {
-                kk_kv_slot const sl = e.slots[n];
+                kk_kv_slot const sl = slot_rec;
                 bool const micro = sl.kind == 0;
                 std::uint32_t const cap = micro ? 8u : 64u;
                 if (sl.active && sl.page_token < cap
@@ -478,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     }
 
     if (S > 1) {
-        cluster_sync();  // keep this CTA's partial alive until every peer has read it
+        cluster_wait();  // this CTA's partial stays alive until every owner has received it
     }
     __syncthreads();
     if (warp == 2) {

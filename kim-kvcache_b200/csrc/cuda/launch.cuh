@@ -11,6 +11,13 @@ namespace kk {
 // Set by kk_set_pdl(); read when a launch is issued on this host thread.
 extern thread_local bool g_pdl_enabled;
 
+// Asks, once per kernel, for the largest shared-memory carveout. CTAs of
+// different kernels share an SM only when the SM's L1/shared split fits
+// both; with every kernel of the decode step on the maximum split, a CTA of
+// the next kernel (launched early under programmatic dependent launch) can
+// sit beside one of the current kernel and prefetch its weights.
+void preferMaxSharedCarveout(void const* kernel);
+
 template <typename... KArgs, typename... Args>
 cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, std::size_t smem,
     cudaStream_t stream, unsigned cluster_x, Args&&... args)
@@ -36,6 +43,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, std::size_t 
     }
     config.attrs = attrs;
     config.numAttrs = n;
+    preferMaxSharedCarveout(reinterpret_cast<void const*>(kernel));
     return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
 }
 

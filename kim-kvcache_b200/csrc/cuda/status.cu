@@ -1,10 +1,29 @@
-// Device status words of the kernel modules and the PDL switch.
+// Device status words of the kernel modules, the PDL switch and the
+// shared-memory carveout requests of the launch helper.
 #include "../../../include/kk_kernels.h"
 #include "launch.cuh"
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
 
 namespace kk {
 
 thread_local bool g_pdl_enabled = false;
+
+void preferMaxSharedCarveout(void const* kernel)
+{
+    static std::mutex mutex;
+    static std::vector<void const*> done;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (std::find(done.begin(), done.end(), kernel) != done.end()) {
+        return;
+    }
+    // A hint: a failure leaves the default split, which only costs overlap.
+    static_cast<void>(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+        cudaSharedmemCarveoutMaxShared));
+    done.push_back(kernel);
+}
 
 int attentionStatus(cudaStream_t stream);
 int attentionTmaStatus(cudaStream_t stream);
