@@ -480,8 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             if (!is_v) {
                 float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
                 float const angle = static_cast<float>(position) * inv_freq;
-                float const c = cosf(angle);
-                float const s = sinf(angle);
+                float s, c;
+                sincosf(angle, &s, &c);
                 out = d < 32u ? mine * c - other * s : mine * c + other * s;
             }
             __half const hv = __float2half_rn(out);
