@@ -231,17 +231,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     std::uint8_t* ring = smem_raw + pad;
     std::uint32_t const q_bytes = a.q_heads * kRowBytes;  // one query row, all heads
-    std::uint8_t* qbuf = ring + kStages * kStageBytes;     // [2][q_bytes], per lane segment
-    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(qbuf + 2 * q_bytes);
+    std::uint8_t* qbuf = ring + kStages * kStageBytes;     // [q_bytes], the current lane segment
+    std::uint64_t* full = reinterpret_cast<std::uint64_t*>(qbuf + q_bytes);
     std::uint64_t* empty = full + kStages;
-    std::uint64_t* q_full = empty + kStages;   // [2]: query row + SegInfo landed
-    std::uint64_t* q_empty = q_full + 2;       // [2]: every consumer warp took its query
+    std::uint64_t* q_full = empty + kStages;   // query row + SegInfo landed
+    std::uint64_t* q_empty = q_full + 1;       // every consumer warp took its query
     // Barrier of the consumer threads (the producer never joins). An mbarrier
     // rather than a named barrier, so that its waits are bounded too.
-    std::uint64_t* cbar = q_empty + 2;
+    std::uint64_t* cbar = q_empty + 1;
     StageMeta* meta = reinterpret_cast<StageMeta*>(cbar + 1);
-    SegInfo* seg = reinterpret_cast<SegInfo*>(meta + kStages);  // [2]
-    float* s_m = reinterpret_cast<float*>(seg + 2);             // [warp][16]
+    SegInfo* seg = reinterpret_cast<SegInfo*>(meta + kStages);
+    float* s_m = reinterpret_cast<float*>(seg + 1);             // [warp][16]
     float* s_l = s_m + kConsumerWarps * 16;                      // [warp][16]
     float* s_o = s_l + kConsumerWarps * 16;                      // [warp][8*NT][kORow]
     int* s_last = reinterpret_cast<int*>(s_o + kConsumerWarps * 8 * NT * kORow);
@@ -254,10 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
-        for (int p = 0; p < 2; ++p) {
-            mbar_init(&q_full[p], 1);
-            mbar_init(&q_empty[p], kConsumerWarps);
-        }
+        mbar_init(q_full, 1);
+        mbar_init(q_empty, kConsumerWarps);
         mbar_init(cbar, kConsumerWarps * 32);
         *s_abort = 0;
         fence_barrier_init();
@@ -282,24 +280,23 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         bool waited = false;
         std::uint32_t stage = 0;
         std::uint32_t qk = 0;  // lane segments started by this CTA
-        // Publishes lane segment qk to the consumers: its bookkeeping in
-        // seg[qk & 1] and its query row (all heads) copied into qbuf[qk & 1]
-        // by one bulk copy, both covered by q_full[qk & 1]. Consumers only
-        // read shared memory, so a new segment costs them no global round
-        // trip.
+        // Publishes lane segment qk to the consumers: its bookkeeping in seg
+        // and its query row (all heads) copied into qbuf by one bulk copy,
+        // both covered by q_full, once the consumers took segment qk - 1's
+        // query (q_empty). Consumers only read shared memory, so a new
+        // segment costs them no global round trip.
         auto start_segment = [&](kk_attn_lane const& L, std::uint32_t lane_b, std::uint32_t part_slot) -> bool {
-            std::uint32_t const p = qk & 1u;
-            bool const ready = qk < 2u || wait_or_abort(&q_empty[p], ((qk >> 1) - 1u) & 1u, s_abort);
+            bool const ready = qk == 0u || wait_or_abort(q_empty, (qk - 1u) & 1u, s_abort);
             if (!__all_sync(0xffffffffu, ready)) {
                 return false;
             }
             if (lane == 0) {
-                seg[p] = SegInfo{lane_b, L.query_row, L.item_offset, L.item_count, L.first_item_shared ? 1u : 0u,
+                *seg = SegInfo{lane_b, L.query_row, L.item_offset, L.item_count, L.first_item_shared ? 1u : 0u,
                     part_slot};
-                mbar_expect_tx(&q_full[p], q_bytes);
-                bulk_load(qbuf + p * q_bytes,
-                    a.query + static_cast<std::uint64_t>(L.query_row) * a.query_stride, q_bytes, &q_full[p]);
-                mbar_arrive(&q_full[p]);  // releases seg[p]; the phase ends when the row lands
+                mbar_expect_tx(q_full, q_bytes);
+                bulk_load(qbuf, a.query + static_cast<std::uint64_t>(L.query_row) * a.query_stride, q_bytes,
+                    q_full);
+                mbar_arrive(q_full);  // releases seg; the phase ends when the row lands
             }
             ++qk;
             return true;
@@ -538,12 +535,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     std::uint32_t qf[NT][4][2];
     SegInfo si{};
     auto begin_segment = [&]() -> bool {
-        std::uint32_t const p = ck & 1u;
-        if (*s_abort || !wait_or_abort(&q_full[p], (ck >> 1) & 1u, s_abort)) {
+        if (*s_abort || !wait_or_abort(q_full, ck & 1u, s_abort)) {
             return false;
         }
-        si = seg[p];
-        std::uint8_t const* q = qbuf + p * q_bytes + head * G * kRowBytes;
+        si = *seg;
+        std::uint8_t const* q = qbuf + head * G * kRowBytes;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             std::uint32_t const qh = nt * 8u + g;
@@ -559,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         }
         __syncwarp();
         if (lane == 0) {
-            mbar_arrive(&q_empty[p]);
+            mbar_arrive(q_empty);
         }
         ++ck;
         return true;
@@ -878,14 +874,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
 }
 
 // About 122 KB with NT = 1 at 32 query heads: small enough that a
-// projection CTA of the neighbouring kernels fits on the same SM, so
+// projection CTA (99 KB) of the neighbouring kernels fits on the same SM, so
 // programmatic dependent launch can overlap their prologues and tails with
 // this kernel.
 template <int NT>
 constexpr std::size_t smemBytes(std::uint32_t q_heads)
 {
-    return 1024 + kStages * kStageBytes + 2ull * q_heads * kRowBytes
-        + (2 * kStages + 5) * 8 + kStages * sizeof(StageMeta) + 2 * sizeof(SegInfo)
+    return 1024 + kStages * kStageBytes + std::size_t(q_heads) * kRowBytes
+        + (2 * kStages + 3) * 8 + kStages * sizeof(StageMeta) + sizeof(SegInfo)
         + 2 * kConsumerWarps * 16 * 4 + kConsumerWarps * 8 * NT * kORow * 4 + 8;
 }
 static_assert(smemBytes<2>(128) <= 227 * 1024, "shared memory budget");

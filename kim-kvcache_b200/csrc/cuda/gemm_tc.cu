@@ -52,7 +52,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
-// Four W+X stages: with the split-K receive buffer about 102 KB at N <= 32,
+// Four W+X stages: with the split-K receive buffer about 99 KB at N <= 32,
 // so an attention CTA or a second projection CTA fits beside this one on an
 // SM and can start (and prefetch its weights under programmatic dependent
 // launch) while this kernel drains. Measured on the decode step, 4 beats 3
@@ -149,11 +149,18 @@ constexpr std::uint32_t tmemCols()
 
 // Receive buffer of the split-K reduction, outside the ring so that peers
 // can push into it while this CTA's MMAs still read the ring: one slot of
-// ceil(N/S) FP32 columns per source rank, at most (BN + 7) columns in all.
+// ceil(N/S) FP32 columns per source rank, S * ceil(N/S) <= BN + 1 columns in
+// all (the planner lowers S until that holds). Sized so that a CTA (98.5 KB
+// at BN = 32) and an attention CTA share an SM.
+constexpr std::uint32_t recvCols(std::uint32_t bn)
+{
+    return bn + 1u;
+}
+
 template <int BN>
 constexpr std::size_t recvBytes()
 {
-    return std::size_t(BN + 7) * kBM * 4;
+    return std::size_t(recvCols(BN)) * kBM * 4;
 }
 
 template <int BN>
@@ -868,6 +875,9 @@ GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
     }
     std::uint32_t const max_split = plan->args.kb_total < 8u ? plan->args.kb_total : 8u;
     split = split < 1u ? 1u : (split > max_split ? max_split : split);
+    while (split > 1u && split * ((d.N + split - 1u) / split) > recvCols(plan->bn)) {
+        --split;
+    }
     plan->args.split = split;
     plan->args.epi.num_m_tiles = plan->tiles;
     return plan;
