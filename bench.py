@@ -151,7 +151,9 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     sptr = C.c_void_p(stream.cuda_stream)
     total_tokens = sum(contexts) + B * (args.steps + args.warmup + 2)
-    extent_cap = sum(c // 64 for c in contexts) + B
+    # Room for every 64-token run that auto-promotion folds during the run:
+    # with too few extents, promotion fails and the tails grow as micro pages.
+    extent_cap = sum((c + args.steps + args.warmup + 2) // 64 for c in contexts) + B
     micro_cap = B * 16 + total_tokens // 8 + 64
     hq, hkv, D, L = cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["layers"]
     backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)

@@ -43,6 +43,10 @@
 namespace kk {
 
 __device__ unsigned int g_attn_tma_status;
+#ifdef KK_TRACE
+__device__ TraceRec g_attn_trace[kTraceCap];
+__device__ unsigned int g_attn_trace_n;
+#endif
 
 namespace {
 
@@ -110,7 +114,28 @@ struct TmaArgs {
     std::uint32_t* counters;
     float* part_o;
     float* part_ml;
+    // L2 prefetch (both optional). kv_pf_bytes: the first pages of each CTA's
+    // first item (this layer's K and V), requested before the dependency
+    // wait, while the previous kernel runs. l2_pf: a share of a byte range
+    // that a later kernel of the step streams, requested stage by stage.
+    std::uint8_t const* micro_base;
+    std::uint8_t const* extent_base;
+    std::uint32_t layers;
+    std::uint32_t kv_pf_bytes;
+    void const* l2_pf;
+    std::uint64_t l2_pf_bytes;
 };
+
+__device__ __forceinline__ void tma_load_5d_hint(void* dst, CUtensorMap const* map, std::uint64_t* bar,
+    int c0, int c1, int c2, int c3, int c4, std::uint64_t policy)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;"
+        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<std::uint64_t>(map)), "r"(smem_u32(bar)),
+        "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4), "l"(policy)
+        : "memory");
+}
 
 __device__ __forceinline__ void tma_load_5d(void* dst, CUtensorMap const* map, std::uint64_t* bar,
     int c0, int c1, int c2, int c3, int c4)
@@ -249,6 +274,26 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
 
     std::uint32_t const warp = threadIdx.x / 32;
     std::uint32_t const lane = threadIdx.x % 32;
+#ifdef KK_TRACE
+    __shared__ TraceRec* s_tr;
+    if (threadIdx.x == 0) {
+        std::uint32_t const slot = atomicAdd(&g_attn_trace_n, 1u);
+        s_tr = slot < kTraceCap ? &g_attn_trace[slot] : nullptr;
+        if (s_tr != nullptr) {
+            s_tr->tag = (0xA0u << 16) | a.layer;
+            s_tr->block = blockIdx.x;
+            s_tr->smid = sm_id();
+            s_tr->aux = 0;
+            s_tr->t[0] = global_ns();
+        }
+    }
+#define KK_ATTN_STAMP(i)                 \
+    if (s_tr != nullptr) {               \
+        s_tr->t[i] = global_ns();        \
+    }
+#else
+#define KK_ATTN_STAMP(i)
+#endif
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
@@ -277,6 +322,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             prefetch_tensormap(&tm_micro);
             prefetch_tensormap(&tm_extent);
         }
+        // K/V of a layer is read once per step: first to go from L2, so that
+        // lines prefetched for later kernels stay.
+        std::uint64_t const kv_policy = l2_policy_evict_first();
+        L2PrefetchShare wpf;
+        wpf.init(a.l2_pf, a.l2_pf_bytes, blockIdx.x, gridDim.x);
         bool waited = false;
         std::uint32_t stage = 0;
         std::uint32_t qk = 0;  // lane segments started by this CTA
@@ -371,9 +421,42 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
             };
             seek();
+            if (!waited && a.kv_pf_bytes != 0) {
+                // The first pages of this CTA's first item, into L2 while the
+                // previous kernel still runs. That kernel writes only each
+                // lane's newest token, and its writes land in L2 too, so
+                // lines fetched early stay coherent.
+                std::uint32_t const i = item.desc_begin + lane;
+                std::uint32_t bytes = 0;
+                std::uint8_t const* src = nullptr;
+                if (i < item.desc_end) {
+                    kk_page_desc const d = a.descs[i];
+                    bool const m = d.kind == 0;
+                    std::uint32_t const cap = m ? 8u : 64u;
+                    if ((m ? d.slot < a.micro_slots : d.slot < a.extent_slots) && d.valid_tokens != 0
+                        && d.valid_tokens <= cap) {
+                        std::uint64_t const run = 2ull * cap * Hkv * kRowBytes;  // K then V of a layer
+                        src = (m ? a.micro_base : a.extent_base)
+                            + (std::uint64_t(d.slot) * a.layers + a.layer) * run;
+                        bytes = static_cast<std::uint32_t>(run);
+                    }
+                }
+                std::uint32_t upto = bytes;
+#pragma unroll
+                for (std::uint32_t o = 1; o < 32; o <<= 1) {
+                    std::uint32_t const t = __shfl_up_sync(0xffffffffu, upto, o);
+                    upto += lane >= o ? t : 0u;
+                }
+                if (bytes != 0 && src != nullptr && upto <= a.kv_pf_bytes) {
+                    l2_prefetch_bulk(src, bytes);
+                }
+            }
             if (!waited) {
                 pdl_wait();  // K/V pages and queries are written by the previous kernel
                 waited = true;
+                if (lane == 0) {
+                    KK_ATTN_STAMP(1)
+                }
             }
             if (!start_segment(cur_lane, b, 2u * it)) {
                 return;
@@ -404,17 +487,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         if (lane == 0) {
                             mbar_expect_tx(&full[s], 2u * Hkv * Ts * kRowBytes);
                             if (a.extent_per_head == 0) {
-                                tma_load_5d(base, &tm_extent, &full[s], 0, static_cast<int>(tok), 0,
-                                    static_cast<int>(kv), slot);
-                                tma_load_5d(base + v_offset, &tm_extent, &full[s], 0, static_cast<int>(tok),
-                                    0, static_cast<int>(kv + 1), slot);
+                                tma_load_5d_hint(base, &tm_extent, &full[s], 0, static_cast<int>(tok), 0,
+                                    static_cast<int>(kv), slot, kv_policy);
+                                tma_load_5d_hint(base + v_offset, &tm_extent, &full[s], 0, static_cast<int>(tok),
+                                    0, static_cast<int>(kv + 1), slot, kv_policy);
                             } else {
                                 for (std::uint32_t h = 0; h < Hkv; ++h) {
                                     std::uint8_t* dst = base + h * Ts * kRowBytes;
-                                    tma_load_5d(dst, &tm_extent, &full[s], 0, static_cast<int>(h),
-                                        static_cast<int>(tok), static_cast<int>(kv), slot);
-                                    tma_load_5d(dst + v_offset, &tm_extent, &full[s], 0, static_cast<int>(h),
-                                        static_cast<int>(tok), static_cast<int>(kv + 1), slot);
+                                    tma_load_5d_hint(dst, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                        static_cast<int>(tok), static_cast<int>(kv), slot, kv_policy);
+                                    tma_load_5d_hint(dst + v_offset, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                        static_cast<int>(tok), static_cast<int>(kv + 1), slot, kv_policy);
                                 }
                             }
                         }
@@ -431,18 +514,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             if (lane == 0) {
                                 mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
                                 std::uint8_t* dst = base + n * Hkv * 8u * kRowBytes;
-                                tma_load_5d(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot);
-                                tma_load_5d(dst + v_offset, &tm_micro, &full[s], 0, 0, 0,
-                                    static_cast<int>(kv + 1), slot);
+                                tma_load_5d_hint(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot, kv_policy);
+                                tma_load_5d_hint(dst + v_offset, &tm_micro, &full[s], 0, 0, 0,
+                                    static_cast<int>(kv + 1), slot, kv_policy);
                             }
                         } else if (lane == 0) {
                             mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
                             for (std::uint32_t h = 0; h < Hkv; ++h) {
                                 std::uint8_t* dst = base + (h * Ts + n * 8u) * kRowBytes;
-                                tma_load_5d(dst, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
-                                    static_cast<int>(kv), slot);
-                                tma_load_5d(dst + v_offset, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
-                                    static_cast<int>(kv + 1), slot);
+                                tma_load_5d_hint(dst, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
+                                    static_cast<int>(kv), slot, kv_policy);
+                                tma_load_5d_hint(dst + v_offset, &tm_micro, &full[s], 0, static_cast<int>(h), 0,
+                                    static_cast<int>(kv + 1), slot, kv_policy);
                             }
                         }
                         ++n;
@@ -488,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 if (lane == 0) {
                     meta[s] = m;
                     mbar_arrive(&full[s]);  // releases meta[s]; the phase ends when the bytes land
+                    wpf.issue(32768u);
                 }
                 ++stage;
                 if (item_done) {
@@ -500,6 +584,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     seek();
                 }
             }
+        }
+        while (lane == 0 && wpf.issue(32768u)) {
+        }
+        if (lane == 0) {
+            KK_ATTN_STAMP(2)
         }
         return;
     }
@@ -659,6 +748,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             if (*s_abort || !wait_or_abort(&full[s], (stage / kStages) & 1u, s_abort)) {
                 break;
             }
+#ifdef KK_TRACE
+            if (stage == 0 && threadIdx.x == 0) {
+                KK_ATTN_STAMP(3)
+            }
+#endif
             StageMeta const m = meta[s];
             std::uint32_t const pair =
                 chunk < 4u ? static_cast<std::uint32_t>(m.valid >> (16u * chunk)) & 0xffffu : 0u;
@@ -865,12 +959,25 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             break;
         }
     }
+#ifdef KK_TRACE
+    if (tid == 0) {
+        KK_ATTN_STAMP(4)
+    }
+#endif
     if (pending && !*s_abort) {
         if (tid == 0) {
             *s_last = pend_done + 1 == pend.item_count;
         }
         resolve_pending();
     }
+#ifdef KK_TRACE
+    if (tid == 0) {
+        KK_ATTN_STAMP(5)
+        if (s_tr != nullptr) {
+            s_tr->aux = (pending ? 0x80000000u : 0u) | stage;
+        }
+    }
+#endif
 }
 
 // About 122 KB with NT = 1 at 32 query heads: small enough that a
@@ -1027,7 +1134,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream)
+    cudaStream_t stream, AttnPrefetch const* pf)
 {
     PoolMaps maps{};
     if (!poolMaps(*pools, maps)) {
@@ -1064,6 +1171,16 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.counters = counters;
     a.part_o = part_o;
     a.part_ml = part_ml;
+    a.micro_base = static_cast<std::uint8_t const*>(pools->micro);
+    a.extent_base = static_cast<std::uint8_t const*>(pools->extent);
+    a.layers = pools->layers;
+    if (pf != nullptr) {
+        a.kv_pf_bytes = pf->kv_bytes;
+        if (pf->ptr != nullptr && (reinterpret_cast<std::uintptr_t>(pf->ptr) & 15u) == 0) {
+            a.l2_pf = pf->ptr;
+            a.l2_pf_bytes = pf->bytes & ~std::uint64_t(15);
+        }
+    }
     static int const sms = smCount();
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
     bool const narrow = a.group <= 8;
@@ -1074,5 +1191,24 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
 }
 
 int attentionTmaStatus(cudaStream_t stream) { return readStatus(&g_attn_tma_status, stream); }
+
+#ifdef KK_TRACE
+extern "C" KK_KAPI std::uint32_t kk_trace_read_attn(void* host, std::uint32_t cap, int reset)
+{
+    unsigned int n = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(&n, g_attn_trace_n, sizeof(n));
+    n = n < kTraceCap ? n : kTraceCap;
+    n = n < cap ? n : cap;
+    if (host != nullptr && n != 0) {
+        cudaMemcpyFromSymbol(host, g_attn_trace, n * sizeof(TraceRec));
+    }
+    if (reset != 0) {
+        unsigned int const zero = 0;
+        cudaMemcpyToSymbol(g_attn_trace_n, &zero, sizeof(zero));
+    }
+    return n;
+}
+#endif
 
 } // namespace kk

@@ -89,6 +89,28 @@ __device__ __forceinline__ std::uint64_t global_ns()
     return t;
 }
 
+#ifdef KK_TRACE
+// Phase trace, compiled only into instrumented builds (-DKK_TRACE): each CTA
+// of an instrumented kernel fills one record with %globaltimer stamps of its
+// phases. Each translation unit keeps its own record array and exports a
+// reader (kk_trace_read_*).
+struct TraceRec {
+    std::uint32_t tag;    // kernel kind and layer
+    std::uint32_t block;  // blockIdx.y << 16 | blockIdx.x
+    std::uint32_t smid;
+    std::uint32_t aux;
+    std::uint64_t t[10];
+};
+constexpr std::uint32_t kTraceCap = 1u << 16;
+
+__device__ __forceinline__ std::uint32_t sm_id()
+{
+    std::uint32_t r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
+#endif
+
 // Potentially suspending test of an mbarrier phase: the thread sleeps in
 // hardware until the phase completes or a short system time limit passes,
 // instead of spinning through issue slots.
@@ -171,6 +193,47 @@ __device__ __forceinline__ std::uint64_t l2_policy_evict_first()
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
     return policy;
 }
+
+// Asks L2 to fetch [src, src + bytes) from DRAM: no shared-memory destination
+// and nothing to wait for. src and bytes are multiples of 16.
+__device__ __forceinline__ void l2_prefetch_bulk(void const* src, std::uint32_t bytes)
+{
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;"
+                 ::"l"(reinterpret_cast<std::uint64_t>(src)), "r"(bytes)
+                 : "memory");
+}
+
+// One CTA's share of an L2 prefetch of a byte range that a later kernel of
+// the step reads (weights of a projection that is still a few kernels away).
+// The range is cut into `parts` contiguous 16-byte-aligned shares; issue()
+// requests the next piece of this share.
+struct L2PrefetchShare {
+    std::uint8_t const* cur;
+    std::uint8_t const* end;
+
+    __device__ __forceinline__ void init(void const* base, std::uint64_t bytes, std::uint32_t part,
+        std::uint32_t parts)
+    {
+        std::uint64_t const units = bytes / 16u;
+        std::uint8_t const* b = static_cast<std::uint8_t const*>(base);
+        cur = b + units * part / parts * 16u;
+        end = b + units * (part + 1u) / parts * 16u;
+        if (base == nullptr) {
+            cur = end = nullptr;
+        }
+    }
+    __device__ __forceinline__ bool issue(std::uint32_t max_bytes)
+    {
+        if (cur >= end) {
+            return false;
+        }
+        std::uint64_t const left = static_cast<std::uint64_t>(end - cur);
+        std::uint32_t const n = left < max_bytes ? static_cast<std::uint32_t>(left) : max_bytes;
+        l2_prefetch_bulk(cur, n);
+        cur += n;
+        return true;
+    }
+};
 
 __device__ __forceinline__ void prefetch_tensormap(CUtensorMap const* map)
 {

@@ -45,6 +45,16 @@
 namespace kk {
 
 __device__ unsigned int g_gemm_status;
+#ifdef KK_TRACE
+__device__ TraceRec g_gemm_trace[kTraceCap];
+__device__ unsigned int g_gemm_trace_n;
+#define KK_GEMM_STAMP(i) \
+    if (tid == 0) {     \
+        tr[i] = global_ns(); \
+    }
+#else
+#define KK_GEMM_STAMP(i)
+#endif
 
 namespace {
 
@@ -52,6 +62,7 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
+constexpr std::uint32_t kSqStride = 64;  // columns per row of a sums-of-squares array
 // Four W+X stages: with the split-K receive buffer about 99 KB at N <= 32,
 // so an attention CTA or a second projection CTA fits beside this one on an
 // SM and can start (and prefetch its weights under programmatic dependent
@@ -104,6 +115,19 @@ struct GemmArgs {
     __half const* norm_x;           // RMS-normalise the output by the rows of norm_x (or null)
     std::uint32_t norm_stride;
     float norm_eps;
+    // L2 prefetch of bytes that a later kernel of the step reads (or null):
+    // every CTA requests its share after the dependency wait, while this
+    // kernel's own weights are already on chip.
+    void const* l2_pf;
+    std::uint64_t l2_pf_bytes;
+    // Runner path of the fused RMSNorm: column n's factor comes from per-row-
+    // tile sums of squares, rsqrt(sum_t sq_in[t * kSqStride + n] / K + eps),
+    // written by the kernel that produced the rows (null: reduce norm_x rows).
+    float const* sq_in;
+    std::uint32_t sq_tiles;
+    // KK_EPI_RESIDUAL: sums of squares of the new FP16 rows over this tile,
+    // sq_out[m_tile * kSqStride + n] (or null).
+    float* sq_out;
     EpiArgs epi;
 };
 
@@ -129,6 +153,13 @@ __device__ __forceinline__ void bulk_copy_to_peer(std::uint32_t dst, void const*
 __device__ __forceinline__ void cluster_arrive()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+
+// Arrive without release semantics: for a barrier phase that orders nothing
+// in memory (the data it guards was handed over through mbarriers).
+__device__ __forceinline__ void cluster_arrive_relaxed()
+{
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void cluster_wait()
@@ -170,7 +201,10 @@ constexpr std::size_t smemBytes()
         + 1024 /* barriers + scratch */;
 }
 
-template <int BN>
+// One instance per (N tile, epilogue kind): each instance carries only its
+// own epilogue, which keeps the code that runs after the main loop small
+// (instruction fetches after the main loop are on the critical path).
+template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
     GemmArgs args)
@@ -193,6 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint32_t const tid = threadIdx.x;
     std::uint32_t const warp = tid / 32;
     std::uint32_t const lane = tid % 32;
+#ifdef KK_TRACE
+    std::uint64_t tr[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+#endif
+    KK_GEMM_STAMP(0)
     std::uint32_t const S = args.split;
     std::uint32_t const rank = S > 1 ? cluster_rank() : 0;
     std::uint32_t const m_tile = blockIdx.y;
@@ -253,9 +291,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             load_w(i, i);
         }
         pdl_wait();
+        KK_GEMM_STAMP(1)
         for (std::uint32_t i = 0; i < pre; ++i) {
             tma_load_2d(x_stage + i * BN * 128, &tm_x, &full[i],
                 static_cast<int>((kb_begin + i) * kBK), 0);
+        }
+        if (args.l2_pf != nullptr) {
+            L2PrefetchShare pf;
+            pf.init(args.l2_pf, args.l2_pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+            while (pf.issue(32768u)) {
+            }
         }
         for (std::uint32_t i = pre; i < nk; ++i) {
             std::uint32_t const s = i % kStages;
@@ -310,15 +355,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         kvs[j] = kk_kv_slot{0, 0, 0, 0};
         if (prefetched && j < pcols) {
             std::uint32_t const n = pn0 + j;
-            if (args.epi.kind == KK_EPI_RESIDUAL && pm < args.M) {
+            if (EPI == KK_EPI_RESIDUAL && pm < args.M) {
                 resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(n) * args.epi.out_stride + pm];
-            } else if (args.epi.kind == KK_EPI_QKV_ROPE) {
+            } else if (EPI == KK_EPI_QKV_ROPE) {
                 pos[j] = args.epi.positions[n];
                 kvs[j] = args.epi.slots[n];
             }
         }
     }
-    if (args.norm_x != nullptr && warp >= 2) {
+    if (args.norm_x != nullptr && args.sq_in != nullptr && warp >= 2) {
+        // While the tile streams: RMSNorm factors of this CTA's output columns
+        // from the producer's per-tile sums of squares, one thread per column,
+        // every partial requested at once and summed in tile order.
+        std::uint32_t const c0n = rank * args.N / S;
+        std::uint32_t const c1n = (rank + 1) * args.N / S;
+        for (std::uint32_t j = tid - 64u; c0n + j < c1n; j += 64u) {
+            float sum = 0.f;
+            for (std::uint32_t t0 = 0; t0 < args.sq_tiles; t0 += 16u) {
+                float v[16];
+#pragma unroll
+                for (std::uint32_t t = 0; t < 16u; ++t) {
+                    v[t] = t0 + t < args.sq_tiles ? args.sq_in[(t0 + t) * kSqStride + c0n + j] : 0.f;
+                }
+#pragma unroll
+                for (std::uint32_t t = 0; t < 16u; ++t) {
+                    sum += v[t];
+                }
+            }
+            rnorm[j] = rsqrtf(sum / static_cast<float>(args.K) + args.norm_eps);
+        }
+    } else if (args.norm_x != nullptr && warp >= 2) {
         // While the tile streams: RMSNorm factors of this CTA's output columns,
         // r[n] = rsqrt(mean_k x[n][k]^2 + eps), one warp per column.
         std::uint32_t const c0n = rank * args.N / S;
@@ -346,6 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     }
     bool const have_acc = mbar_wait(accum, 0, &g_gemm_status);
     tc_fence_after();
+    KK_GEMM_STAMP(2)
 
     // TMEM -> this CTA's FP32 partial tile, column-major [BN][128] (aliases the
     // W stages: every MMA that read them has completed).
@@ -377,11 +444,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     }
     tc_fence_before();
     __syncthreads();
+    KK_GEMM_STAMP(3)
     if (S > 1) {
         // The partial is written; every peer's receive buffer is armed (phase
         // 1 of the cluster barrier, long complete by now). Thread r pushes
         // owner r's columns.
         cluster_wait();
+        KK_GEMM_STAMP(4)
         if (tid < S) {
             std::uint32_t const r0 = tid * args.N / S;
             std::uint32_t const r1 = (tid + 1) * args.N / S;
@@ -391,6 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         }
         bool const got = mbar_wait(rbar, 0, &g_gemm_status);
+        KK_GEMM_STAMP(5)
         // Sum over the K slices in rank order (deterministic).
         for (std::uint32_t j = 0; j < cols; ++j) {
             float acc = 0.f;
@@ -399,9 +469,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
             red[j * kBM + row] = args.norm_x != nullptr ? acc * rnorm[j] : acc;
         }
-        // Cluster barrier phase 2, arrive: this CTA has received everything,
-        // so the senders' partials may go.
-        cluster_arrive();
+        // Cluster barrier phase 2, arrive: this CTA has received everything
+        // (the receive mbarrier completed), so the senders' partials may go.
+        // Relaxed: no memory needs ordering here, and a release arrive waits
+        // for this CTA's outstanding memory operations.
+        cluster_arrive_relaxed();
     } else {
         for (std::uint32_t j = 0; j < cols; ++j) {
             float const acc = part[(n0 + j) * kBM + row];
@@ -409,8 +481,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         }
     }
     __syncthreads();
+    KK_GEMM_STAMP(6)
 
-    switch (e.kind) {
+    switch (EPI) {
     case KK_EPI_STORE_F16:
         if (m < args.M) {
             for (std::uint32_t j = 0; j < cols; ++j) {
@@ -426,24 +499,63 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         }
         break;
-    case KK_EPI_RESIDUAL:
-        if (m < args.M) {
-            if (prefetched) {
+    case KK_EPI_RESIDUAL: {
+        // New rows h = half(resid + half(acc)); with sq_out, also the tile's
+        // sum of h^2 per column (the next RMSNorm's statistics), reduced in a
+        // fixed order: lanes by shuffles, then the four warps in turn.
+        float* wsq = amax_v;  // [4][BN], idle in this epilogue
+        bool const want_sq = args.sq_out != nullptr;
+        if (prefetched) {
 #pragma unroll
-                for (std::uint32_t j = 0; j < kPre; ++j) {
-                    if (j < cols) {
-                        static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] =
-                            __hadd(resid[j], __float2half_rn(red[j * kBM + row]));
+            for (std::uint32_t j = 0; j < kPre; ++j) {
+                if (j < cols) {
+                    __half const h = __hadd(resid[j], __float2half_rn(red[j * kBM + row]));
+                    if (m < args.M) {
+                        static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = h;
+                    }
+                    if (want_sq) {
+                        float const f = m < args.M ? __half2float(h) : 0.f;
+                        float q = f * f;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            q += __shfl_xor_sync(0xffffffffu, q, o);
+                        }
+                        if (lane == 0) {
+                            wsq[warp * BN + j] = q;
+                        }
                     }
                 }
-            } else {
-                for (std::uint32_t j = 0; j < cols; ++j) {
-                    __half* h = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
-                    *h = __hadd(*h, __float2half_rn(red[j * kBM + row]));
+            }
+        } else {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                float f = 0.f;
+                if (m < args.M) {
+                    __half* hp = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
+                    __half const h = __hadd(*hp, __float2half_rn(red[j * kBM + row]));
+                    *hp = h;
+                    f = __half2float(h);
+                }
+                if (want_sq) {
+                    float q = f * f;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+                        q += __shfl_xor_sync(0xffffffffu, q, o);
+                    }
+                    if (lane == 0) {
+                        wsq[warp * BN + j] = q;
+                    }
                 }
             }
         }
+        if (want_sq) {
+            __syncthreads();
+            if (tid < cols) {
+                args.sq_out[m_tile * kSqStride + n0 + tid] =
+                    ((wsq[tid] + wsq[BN + tid]) + wsq[2 * BN + tid]) + wsq[3 * BN + tid];
+            }
+        }
         break;
+    }
     case KK_EPI_SILU_PAIRS:
         // Rows 2i / 2i+1 hold gate_i / up_i.
         if ((m & 1u) == 0 && m < args.M) {
@@ -557,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         break;
     }
 
-    if (e.kind == KK_EPI_ARGMAX) {
+    if (EPI == KK_EPI_ARGMAX) {
         // The last CTA of the launch folds the per-tile winners of every column.
         __threadfence();
         __syncthreads();
@@ -587,6 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         }
     }
 
+    KK_GEMM_STAMP(7)
     if (S > 1) {
         cluster_wait();  // this CTA's partial stays alive until every owner has received it
     }
@@ -595,6 +708,22 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         tc_fence_after();
         tmem_dealloc(tmem, tmemCols<BN>());
     }
+#ifdef KK_TRACE
+    if (tid == 0) {
+        tr[8] = global_ns();
+        std::uint32_t const slot = atomicAdd(&g_gemm_trace_n, 1u);
+        if (slot < kTraceCap) {
+            TraceRec& r = g_gemm_trace[slot];
+            r.tag = (static_cast<std::uint32_t>(EPI) << 16) | e.layer;
+            r.block = (blockIdx.y << 16) | blockIdx.x;
+            r.smid = sm_id();
+            r.aux = args.K;
+            for (int i = 0; i < 10; ++i) {
+                r.t[i] = tr[i];
+            }
+        }
+    }
+#endif
 }
 
 // Packs W [M][K] (row-major, K % 8 == 0) into 128x64 tiles, tile (t, b) at
@@ -688,12 +817,25 @@ int numSms()
     return g_sms;
 }
 
-template <int BN>
-cudaError_t configure()
+template <int BN, int EPI>
+cudaError_t configureOne()
 {
-    static cudaError_t status = cudaFuncSetAttribute(gemm_tc_kernel<BN>,
+    static cudaError_t status = cudaFuncSetAttribute(gemm_tc_kernel<BN, EPI>,
         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smemBytes<BN>()));
     return status;
+}
+
+template <int BN>
+cudaError_t configure(std::uint32_t epi)
+{
+    switch (epi) {
+    case KK_EPI_STORE_F16: return configureOne<BN, KK_EPI_STORE_F16>();
+    case KK_EPI_STORE_F32: return configureOne<BN, KK_EPI_STORE_F32>();
+    case KK_EPI_RESIDUAL: return configureOne<BN, KK_EPI_RESIDUAL>();
+    case KK_EPI_SILU_PAIRS: return configureOne<BN, KK_EPI_SILU_PAIRS>();
+    case KK_EPI_QKV_ROPE: return configureOne<BN, KK_EPI_QKV_ROPE>();
+    default: return configureOne<BN, KK_EPI_ARGMAX>();
+    }
 }
 
 } // namespace
@@ -740,6 +882,7 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
     }
     EpiArgs& e = args.epi;
     e.kind = d->epilogue;
+    e.layer = d->layer;
     e.out = d->out;
     e.out_stride = d->out_stride;
     if (d->epilogue != KK_EPI_ARGMAX && d->out == nullptr) {
@@ -784,15 +927,28 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
     return 0;
 }
 
-template <int BN>
-int runGemm(GemmPlan const& plan, cudaStream_t stream)
+template <int BN, int EPI>
+int runGemmOne(GemmPlan const& plan, cudaStream_t stream)
 {
-    cudaError_t const c = configure<BN>();
+    cudaError_t const c = configureOne<BN, EPI>();
     if (c != cudaSuccess) {
         return static_cast<int>(c);
     }
-    return static_cast<int>(launch(gemm_tc_kernel<BN>, dim3(plan.args.split, plan.tiles),
+    return static_cast<int>(launch(gemm_tc_kernel<BN, EPI>, dim3(plan.args.split, plan.tiles),
         dim3(kThreads), smemBytes<BN>(), stream, plan.args.split, plan.tm_w, plan.tm_x, plan.args));
+}
+
+template <int BN>
+int runGemm(GemmPlan const& plan, cudaStream_t stream)
+{
+    switch (plan.args.epi.kind) {
+    case KK_EPI_STORE_F16: return runGemmOne<BN, KK_EPI_STORE_F16>(plan, stream);
+    case KK_EPI_STORE_F32: return runGemmOne<BN, KK_EPI_STORE_F32>(plan, stream);
+    case KK_EPI_RESIDUAL: return runGemmOne<BN, KK_EPI_RESIDUAL>(plan, stream);
+    case KK_EPI_SILU_PAIRS: return runGemmOne<BN, KK_EPI_SILU_PAIRS>(plan, stream);
+    case KK_EPI_QKV_ROPE: return runGemmOne<BN, KK_EPI_QKV_ROPE>(plan, stream);
+    default: return runGemmOne<BN, KK_EPI_ARGMAX>(plan, stream);
+    }
 }
 
 } // namespace
@@ -862,8 +1018,8 @@ GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
         rc = KK_EINVAL;
         return nullptr;
     }
-    cudaError_t const configured = plan->bn == 16 ? configure<16>()
-        : (plan->bn == 32 ? configure<32>() : configure<64>());
+    cudaError_t const configured = plan->bn == 16 ? configure<16>(d.epilogue)
+        : (plan->bn == 32 ? configure<32>(d.epilogue) : configure<64>(d.epilogue));
     if (configured != cudaSuccess) {
         rc = static_cast<int>(configured);
         return nullptr;
@@ -882,6 +1038,52 @@ GemmPlanPtr gemmPlan(kk_gemm_desc const& d, int& rc)
     plan->args.epi.num_m_tiles = plan->tiles;
     return plan;
 }
+
+bool gemmSetNormPartials(GemmPlan& plan, float const* sq_in, std::uint32_t tiles)
+{
+    if (plan.args.norm_x == nullptr || sq_in == nullptr || tiles == 0
+        || (reinterpret_cast<std::uintptr_t>(sq_in) & 3u) != 0) {
+        return false;
+    }
+    plan.args.sq_in = sq_in;
+    plan.args.sq_tiles = tiles;
+    return true;
+}
+
+bool gemmSetSumSquaresOut(GemmPlan& plan, float* sq_out)
+{
+    if (plan.args.epi.kind != KK_EPI_RESIDUAL || sq_out == nullptr) {
+        return false;
+    }
+    plan.args.sq_out = sq_out;
+    return true;
+}
+
+void gemmSetL2Prefetch(GemmPlan& plan, void const* ptr, std::uint64_t bytes)
+{
+    bool const ok = ptr != nullptr && (reinterpret_cast<std::uintptr_t>(ptr) & 15u) == 0 && bytes >= 16;
+    plan.args.l2_pf = ok ? ptr : nullptr;
+    plan.args.l2_pf_bytes = ok ? bytes & ~std::uint64_t(15) : 0;
+}
+
+#ifdef KK_TRACE
+extern "C" KK_KAPI std::uint32_t kk_trace_read_gemm(void* host, std::uint32_t cap, int reset)
+{
+    unsigned int n = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpyFromSymbol(&n, g_gemm_trace_n, sizeof(n));
+    n = n < kTraceCap ? n : kTraceCap;
+    n = n < cap ? n : cap;
+    if (host != nullptr && n != 0) {
+        cudaMemcpyFromSymbol(host, g_gemm_trace, n * sizeof(TraceRec));
+    }
+    if (reset != 0) {
+        unsigned int const zero = 0;
+        cudaMemcpyToSymbol(g_gemm_trace_n, &zero, sizeof(zero));
+    }
+    return n;
+}
+#endif
 
 int gemmRun(GemmPlan const& plan, cudaStream_t stream)
 {

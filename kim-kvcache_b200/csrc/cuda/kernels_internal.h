@@ -13,6 +13,17 @@
 
 namespace kk {
 
+// L2 prefetch requests of one attention launch (TMA kernel only): each CTA
+// asks L2 for the first kv_bytes of its first work item's pages (this
+// layer's K and V) before its dependency wait, and for its share of
+// [ptr, ptr + bytes), bytes that a later kernel of the step streams, one
+// piece per stage.
+struct AttnPrefetch {
+    std::uint32_t kv_bytes;
+    void const* ptr;
+    std::uint64_t bytes;
+};
+
 // kk_paged_decode_attention with the item count in device memory; items
 // beyond *num_items (<= max_items) are ignored. The grid is sized for max_items.
 int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
@@ -20,7 +31,7 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
-    cudaStream_t stream);
+    cudaStream_t stream, AttnPrefetch const* pf = nullptr);
 
 // TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
 // KV heads, up to 16 query heads per KV head; serves both plan kinds
@@ -32,7 +43,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream);
+    cudaStream_t stream, AttnPrefetch const* pf = nullptr);
 
 // kk_kv_copy_tokens with the copy count in device memory (<= max_copies).
 int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
@@ -49,5 +60,24 @@ using GemmPlanPtr = std::unique_ptr<GemmPlan, GemmPlanDeleter>;
 // receives 0 or the kk_gemm error code.
 GemmPlanPtr gemmPlan(kk_gemm_desc const& desc, int& rc);
 int gemmRun(GemmPlan const& plan, cudaStream_t stream);
+// Every CTA of the plan's launches also asks L2 for its share of
+// [ptr, ptr + bytes) once its own inputs are requested: bytes that a later
+// kernel of the step streams (null or 0 clears it).
+void gemmSetL2Prefetch(GemmPlan& plan, void const* ptr, std::uint64_t bytes);
+
+// Sums of squares for the fused RMSNorm, kept in arrays of rows of 64 floats
+// (one row per 128-row tile of the producing projection, one column per
+// batch row). A KK_EPI_RESIDUAL plan given an output writes, for each of its
+// row tiles t and batch rows n, sq[t * 64 + n] = sum over the tile's rows of
+// the new value squared; a plan with a normalised input given `tiles` such
+// rows takes its RMS factors from them instead of re-reading the input rows.
+bool gemmSetNormPartials(GemmPlan& plan, float const* sq_in, std::uint32_t tiles);
+bool gemmSetSumSquaresOut(GemmPlan& plan, float* sq_out);
+
+// kk_embed_rmsnorm that also writes each row's sum of squares of the
+// gathered embedding to sq_out[row] (one tile's row of a sums-of-squares
+// array); y may be null.
+int embedSumSquares(std::uint16_t const* embed, std::uint32_t const* tokens, std::uint16_t* hidden,
+    float* sq_out, std::uint32_t rows, std::uint32_t cols, cudaStream_t stream);
 
 } // namespace kk

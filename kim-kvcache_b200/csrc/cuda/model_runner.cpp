@@ -88,6 +88,14 @@ struct CudaTinyLlamaModelRunner::Impl {
     void* attn_ws{nullptr};
     std::uint64_t attn_ws_bytes{0};
     void* argmax_ws{nullptr};
+    // RMSNorm statistics handed from the kernel that writes the residual rows
+    // to the projection that normalises them: per 128-row tile and batch row,
+    // the sum of squares (rows of 64 floats). sq_embed: the embedding rows
+    // (one tile), sq_attn_out: after the output projection, sq_mlp_out:
+    // after the down projection.
+    float* sq_embed{nullptr};
+    float* sq_attn_out{nullptr};
+    float* sq_mlp_out{nullptr};
 
     // Step inputs: one region on the device, a pinned mirror on the host.
     std::uint32_t max_items{0};
@@ -217,14 +225,40 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         out.o.emplace_back();
         out.gu.emplace_back();
         out.down.emplace_back();
+        auto atLayer = [l](kk_gemm_desc x) {
+            x.layer = l;
+            return x;
+        };
         if (!make(d, out.qkv.back())
-            || !make(base(w.w_o, c.hidden_size, c.hidden_size, attn, KK_EPI_RESIDUAL, hidden, c.hidden_size), out.o.back())
-            || !make(normedInput(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, hidden,
-                          KK_EPI_SILU_PAIRS, act, c.intermediate_size)), out.gu.back())
-            || !make(base(w.w_down, c.hidden_size, c.intermediate_size, act, KK_EPI_RESIDUAL, hidden,
-                          c.hidden_size), out.down.back())) {
+            || !make(atLayer(base(w.w_o, c.hidden_size, c.hidden_size, attn, KK_EPI_RESIDUAL, hidden,
+                          c.hidden_size)), out.o.back())
+            || !make(atLayer(normedInput(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, hidden,
+                          KK_EPI_SILU_PAIRS, act, c.intermediate_size))), out.gu.back())
+            || !make(atLayer(base(w.w_down, c.hidden_size, c.intermediate_size, act, KK_EPI_RESIDUAL, hidden,
+                          c.hidden_size)), out.down.back())) {
             return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "projection plan rejected");
         }
+    }
+    // RMSNorm statistics travel with the residual rows (see sq_* above).
+    std::uint32_t const sq_tiles = (c.hidden_size + 127) / 128;
+    for (std::uint32_t l = 0; l < c.layer_count; ++l) {
+        if (!kk::gemmSetNormPartials(*out.qkv[l], l == 0 ? sq_embed : sq_mlp_out, l == 0 ? 1u : sq_tiles)
+            || !kk::gemmSetSumSquaresOut(*out.o[l], sq_attn_out)
+            || !kk::gemmSetNormPartials(*out.gu[l], sq_attn_out, sq_tiles)
+            || !kk::gemmSetSumSquaresOut(*out.down[l], sq_mlp_out)) {
+            return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "norm statistics rejected");
+        }
+    }
+    // L2 prefetch: the output projection's weights are already on chip when
+    // its dependency wait returns (its CTAs load them while attention runs),
+    // and HBM then idles while it exchanges partials; its CTAs use that time
+    // to fetch the down projection's weights into L2. (Measured on the c4
+    // step: fetching the gate/up weights during attention, or attention's
+    // first pages during the QKV projection, did not pay: attention streams
+    // at the HBM rate already.)
+    for (std::uint32_t l = 0; l < c.layer_count; ++l) {
+        kk::gemmSetL2Prefetch(*out.o[l], layers[l].w_down,
+            kk_gemm_packed_bytes(c.hidden_size, c.intermediate_size));
     }
     kk_gemm_desc lm = normedInput(base(lm_head, c.vocabulary_size, c.hidden_size, hidden, KK_EPI_ARGMAX,
         nullptr, 0));
@@ -233,7 +267,9 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
     kk_gemm_desc lm_logits = lm;
     lm_logits.out = logits;
     lm_logits.out_stride = c.vocabulary_size;
-    if (!make(lm, out.lm_head) || !make(lm_logits, out.lm_head_logits)) {
+    if (!make(lm, out.lm_head) || !make(lm_logits, out.lm_head_logits)
+        || !kk::gemmSetNormPartials(*out.lm_head, sq_mlp_out, sq_tiles)
+        || !kk::gemmSetNormPartials(*out.lm_head_logits, sq_mlp_out, sq_tiles)) {
         return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "LM head plan rejected");
     }
     return {};
@@ -258,10 +294,10 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
                       stepDev<std::uint32_t>(off_counts) + 1, batch, stream), "copy-on-write");
         if (!s.ok()) return s;
     }
-    // Embedding gather starts the residual stream (the first projection
-    // normalises its rows itself; `normed` is written but not read).
-    s = check(kk_embed_rmsnorm(embed, stepDev<std::uint32_t>(off_tokens), layers[0].in_norm, hidden,
-                  normed, batch, H, c.rms_norm_epsilon, stream), "embedding");
+    // Embedding gather starts the residual stream; the first projection
+    // normalises its rows with the sums of squares written here.
+    s = check(kk::embedSumSquares(embed, stepDev<std::uint32_t>(off_tokens), hidden, sq_embed, batch, H,
+                  stream), "embedding");
     if (!s.ok()) return s;
     std::unordered_map<std::uint32_t, std::size_t> capture;
     if (debug != nullptr) {
@@ -971,6 +1007,10 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         c.head_dimension);
     std::size_t const o_attn_ws = region(im->attn_ws_bytes);
     std::size_t const o_argmax = region(kk_argmax_workspace_bytes(c.vocabulary_size, bmax));
+    std::size_t const sq_bytes = std::size_t((H + 127) / 128) * 64 * 4;
+    std::size_t const o_sq_embed = region(sq_bytes);
+    std::size_t const o_sq_attn = region(sq_bytes);
+    std::size_t const o_sq_mlp = region(sq_bytes);
     im->ws_bytes = off;
     e = cudaMalloc(reinterpret_cast<void**>(&im->ws), im->ws_bytes);
     if (e == cudaSuccess) {
@@ -989,6 +1029,9 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     im->out_tokens = reinterpret_cast<std::uint32_t*>(im->ws + o_tok);
     im->attn_ws = im->ws + o_attn_ws;
     im->argmax_ws = im->ws + o_argmax;
+    im->sq_embed = reinterpret_cast<float*>(im->ws + o_sq_embed);
+    im->sq_attn_out = reinterpret_cast<float*>(im->ws + o_sq_attn);
+    im->sq_mlp_out = reinterpret_cast<float*>(im->ws + o_sq_mlp);
 
     off = 0;
     im->off_counts = region(16);

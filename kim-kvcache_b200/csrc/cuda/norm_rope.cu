@@ -5,6 +5,7 @@
 // In the decode step RoPE and the SiLU gate run fused in the projection
 // epilogues (gemm_tc.cu); the standalone kernels serve the per-layer SPI path.
 #include "../../../include/kk_kernels.h"
+#include "kernels_internal.h"
 #include "launch.cuh"
 
 namespace kk {
@@ -31,10 +32,11 @@ __device__ __forceinline__ float block_sum(float v, float* scratch)
     return total;
 }
 
-// One CTA per row; 8 FP16 per thread per step (cols % 8 == 0).
+// One CTA per row; 8 FP16 per thread per step (cols % 8 == 0). y (the
+// normalised row) and sq_out (the row's sum of squares) are optional.
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(__half const* x,
     __half const* embed, std::uint32_t const* tokens, __half const* weight, __half* hidden,
-    __half* y, std::uint32_t cols, float eps)
+    __half* y, std::uint32_t cols, float eps, float* sq_out)
 {
     pdl_launch_dependents();  // dependents only prefetch weights before their own wait
     pdl_wait();
@@ -56,7 +58,14 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(__half const* x,
             *reinterpret_cast<uint4*>(hidden + std::uint64_t(row) * cols + i) = raw;
         }
     }
-    float const scale = rsqrtf(block_sum(sum, scratch) / static_cast<float>(cols) + eps);
+    float const total = block_sum(sum, scratch);
+    if (sq_out != nullptr && threadIdx.x == 0) {
+        sq_out[row] = total;
+    }
+    if (y == nullptr) {
+        return;
+    }
+    float const scale = rsqrtf(total / static_cast<float>(cols) + eps);
     for (std::uint32_t i = threadIdx.x * 8u; i < cols; i += kNormThreads * 8u) {
         uint4 const raw = *reinterpret_cast<uint4 const*>(src + i);
         uint4 const wraw = *reinterpret_cast<uint4 const*>(weight + i);
@@ -142,7 +151,7 @@ int kk_rmsnorm(const uint16_t* x, const uint16_t* weight, uint16_t* y, uint32_t 
         static_cast<cudaStream_t>(stream), 1, reinterpret_cast<__half const*>(x),
         static_cast<__half const*>(nullptr), static_cast<std::uint32_t const*>(nullptr),
         reinterpret_cast<__half const*>(weight), static_cast<__half*>(nullptr),
-        reinterpret_cast<__half*>(y), cols, eps));
+        reinterpret_cast<__half*>(y), cols, eps, static_cast<float*>(nullptr)));
 }
 
 int kk_embed_rmsnorm(const uint16_t* embed, const uint32_t* tokens, const uint16_t* weight,
@@ -158,7 +167,8 @@ int kk_embed_rmsnorm(const uint16_t* embed, const uint32_t* tokens, const uint16
     return static_cast<int>(kk::launch(kk::rmsnorm_kernel, dim3(rows), dim3(kk::kNormThreads), 0,
         static_cast<cudaStream_t>(stream), 1, static_cast<__half const*>(nullptr),
         reinterpret_cast<__half const*>(embed), tokens, reinterpret_cast<__half const*>(weight),
-        reinterpret_cast<__half*>(hidden), reinterpret_cast<__half*>(y), cols, eps));
+        reinterpret_cast<__half*>(hidden), reinterpret_cast<__half*>(y), cols, eps,
+        static_cast<float*>(nullptr)));
 }
 
 int kk_rope(uint16_t* q, uint32_t q_stride, uint16_t* k, uint32_t k_stride,
@@ -207,3 +217,21 @@ int kk_residual_add(uint16_t* hidden, const uint16_t* update, uint64_t count, vo
 }
 
 } // extern "C"
+
+namespace kk {
+int embedSumSquares(std::uint16_t const* embed, std::uint32_t const* tokens, std::uint16_t* hidden,
+    float* sq_out, std::uint32_t rows, std::uint32_t cols, cudaStream_t stream)
+{
+    if (embed == nullptr || tokens == nullptr || hidden == nullptr || sq_out == nullptr || cols == 0
+        || cols % 8 != 0) {
+        return KK_EINVAL;
+    }
+    if (rows == 0) {
+        return 0;
+    }
+    return static_cast<int>(launch(rmsnorm_kernel, dim3(rows), dim3(kNormThreads), 0, stream, 1,
+        static_cast<__half const*>(nullptr), reinterpret_cast<__half const*>(embed), tokens,
+        static_cast<__half const*>(nullptr), reinterpret_cast<__half*>(hidden), static_cast<__half*>(nullptr),
+        cols, 1.0f, sq_out));
+}
+} // namespace kk
