@@ -212,10 +212,15 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     device_ms = []
+    h2d, d2h = C.c_uint64(0), C.c_uint64(0)
+    h2d_total = d2h_total = 0
     ev0.record(stream)
     for _ in range(args.steps):
         step()
         device_ms.append(R["runner_last_step_ms"](runner))
+        R["runner_last_transfer_bytes"](runner, C.byref(h2d), C.byref(d2h))
+        h2d_total += h2d.value
+        d2h_total += d2h.value
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = ev0.elapsed_time(ev1)
@@ -263,7 +268,7 @@ def run_ours(args, rank, world, local_rank):
             "cuda_graphs": True,
         },
         "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tok/s",
-                "h2d_bytes_per_step": h2d_bytes(B, contexts), "d2h_bytes_per_step": 4 * B},
+                "h2d_bytes_per_step": round(h2d_total / args.steps), "d2h_bytes_per_step": round(d2h_total / args.steps)},
         "gpu_launches": launches * args.steps,
         "roofline": roof,
         "clocks": clocks,
@@ -271,14 +276,6 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = cpu_baseline(kk, synth, cfg, contexts, manifest, args)
     return line
-
-
-def h2d_bytes(B, contexts):
-    """Per-step upload of the fused step: counts, tokens, positions, write slots,
-    copies, lanes, work list and page descriptors (entries of every lane)."""
-    entries = sum(c // 64 + math.ceil((c % 64 + 1) / 8) for c in contexts)
-    items = sum(max(1, math.ceil((c + 1) / 256)) for c in contexts)
-    return 16 + B * (4 + 4 + 8 + 12 + 32) + items * 16 + entries * 16
 
 
 # DRAM traffic / algorithmic K+V bytes of one K1 launch, from an ncu capture of

@@ -282,6 +282,10 @@ KK_API int kkrt_runner_forward_token(void* runner, uint64_t request_id, uint32_t
     uint16_t* final_hidden, const uint32_t* layers, uint32_t n_layers, uint16_t* layer_hidden);
 KK_API float kkrt_runner_last_step_ms(void* runner);
 KK_API uint32_t kkrt_runner_last_launches(void* runner);
+/* Host<->device bytes of the last fused step: the step-record upload and the
+ * token (and logits) readback. Returns 0 for a non-CUDA runner. No counterpart
+ * in the reference (its per-lane uploads are not aggregated). */
+KK_API int kkrt_runner_last_transfer_bytes(void* runner, uint64_t* h2d, uint64_t* d2h);
 /* Detail text of the last failed fused step into out (NUL-terminated); returns its length. */
 KK_API uint32_t kkrt_runner_last_error(void* runner, char* out, uint32_t capacity);
 

@@ -378,6 +378,21 @@ uint32_t kkrt_runner_last_launches(void* r)
     return runner == nullptr ? 0 : runner->lastStepLaunches();
 }
 
+int kkrt_runner_last_transfer_bytes(void* r, uint64_t* h2d, uint64_t* d2h)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    if (runner == nullptr) {
+        return 0;
+    }
+    if (h2d != nullptr) {
+        *h2d = runner->lastStepH2dBytes();
+    }
+    if (d2h != nullptr) {
+        *d2h = runner->lastStepD2hBytes();
+    }
+    return 1;
+}
+
 void* kkrt_sched_create(void* b, void* r, uint32_t max_active, uint32_t max_tokens, uint64_t max_kv,
     uint32_t chunk)
 {

@@ -116,6 +116,8 @@ struct CudaTinyLlamaModelRunner::Impl {
     bool auto_promote{false};
     float last_ms{0.f};
     std::uint32_t last_launches{0};
+    std::uint64_t last_h2d{0};
+    std::uint64_t last_d2h{0};
 
     std::unordered_map<std::uint32_t, BatchPlans> plans;
     std::unordered_map<std::uint32_t, cudaGraphExec_t> graphs;
@@ -175,6 +177,8 @@ float CudaTinyLlamaModelRunner::lastStepDeviceMs() const noexcept { return impl_
 void CudaTinyLlamaModelRunner::setAutoPromote(bool enabled) noexcept { impl_->auto_promote = enabled; }
 std::string CudaTinyLlamaModelRunner::lastError() const { return impl_->last_error; }
 std::uint32_t CudaTinyLlamaModelRunner::lastStepLaunches() const noexcept { return impl_->last_launches; }
+std::uint64_t CudaTinyLlamaModelRunner::lastStepH2dBytes() const noexcept { return impl_->last_h2d; }
+std::uint64_t CudaTinyLlamaModelRunner::lastStepD2hBytes() const noexcept { return impl_->last_d2h; }
 
 CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t batch, BatchPlans& out)
 {
@@ -498,15 +502,19 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
     std::size_t const bytes = im.off_descs + std::size_t(n_descs) * sizeof(kk_page_desc);
     std::string fail_detail;
     cudaError_t e = cudaMemcpyAsync(im.step_dev, im.step_host, bytes, cudaMemcpyHostToDevice, im.stream);
+    im.last_h2d = bytes;
+    im.last_d2h = 0;
     CudaModelRunnerStatus s = e == cudaSuccess
         ? im.runStep(B, n_copies != 0, want_logits, debug)
         : cudaFailure(static_cast<int>(e), "upload step inputs");
     if (s.ok()) {
         e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, B * 4u, cudaMemcpyDeviceToHost, im.stream);
+        im.last_d2h += B * 4u;
         if (e == cudaSuccess && logits_out != nullptr) {
             logits_out->resize(c.vocabulary_size);
             e = cudaMemcpyAsync(logits_out->data(), im.logits, c.vocabulary_size * 4u,
                 cudaMemcpyDeviceToHost, im.stream);
+            im.last_d2h += c.vocabulary_size * 4u;
         }
         if (e == cudaSuccess) {
             e = cudaStreamSynchronize(im.stream);
@@ -656,10 +664,13 @@ GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId i
     counts[1] = n_copies;
     std::size_t const bytes = im.off_descs + std::size_t(n_descs) * sizeof(kk_page_desc);
     cudaError_t e = cudaMemcpyAsync(im.step_dev, im.step_host, bytes, cudaMemcpyHostToDevice, im.stream);
+    im.last_h2d = bytes;
+    im.last_d2h = 0;
     CudaModelRunnerStatus s = e == cudaSuccess ? im.runStep(n, n_copies != 0, false, nullptr)
                                                : cudaFailure(static_cast<int>(e), "upload step inputs");
     if (s.ok()) {
         e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, n * 4u, cudaMemcpyDeviceToHost, im.stream);
+        im.last_d2h += n * 4u;
         if (e == cudaSuccess) {
             e = cudaStreamSynchronize(im.stream);
         }

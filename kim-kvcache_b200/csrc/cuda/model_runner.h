@@ -124,6 +124,10 @@ public:
     [[nodiscard]] std::string lastError() const;
     // Kernels launched by the last fused step.
     [[nodiscard]] std::uint32_t lastStepLaunches() const noexcept;
+    // Bytes the last fused step copied host -> device (the step record) and
+    // device -> host (greedy token ids, plus logits or captures when asked).
+    [[nodiscard]] std::uint64_t lastStepH2dBytes() const noexcept;
+    [[nodiscard]] std::uint64_t lastStepD2hBytes() const noexcept;
     // Turns auto-promotion (CudaModelRunnerOptions::auto_promote) on or off.
     void setAutoPromote(bool enabled) noexcept;
 

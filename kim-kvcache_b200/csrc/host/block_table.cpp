@@ -3,6 +3,8 @@
 #include "kv_types.h"
 
 #include <algorithm>
+#include <cstdint>
+#include <vector>
 
 namespace kimkvcache {
 namespace {
@@ -28,13 +30,38 @@ bool tableIsWellFormed(std::vector<MappingEntry> const& entries,
         if (next_begin > std::numeric_limits<std::uint32_t>::max()) {
             return false;
         }
-        for (std::size_t j = 0; j < i; ++j) {
-            if (entries[j].handle == entry.handle) {
-                return false;  // one physical page mapped twice
-            }
-        }
     }
-    return true;
+    // One physical page mapped twice: the same verdict as comparing every
+    // pair of entries, from a sorted copy of the handles (tables of a few
+    // thousand tokens hold tens of entries and are checked on every token
+    // reservation, where the pairwise scan dominated the host time).
+    std::uint64_t local[128];
+    std::vector<std::uint64_t> heap;
+    std::uint64_t* keys = local;
+    if (entries.size() > 128) {
+        heap.resize(entries.size());
+        keys = heap.data();
+    }
+    std::size_t n = 0;
+    for (MappingEntry const& entry : entries) {
+        // kind (8 bits) | slot (32 bits) | generation (24 low bits): equal
+        // keys only for equal handles when generations fit 24 bits; larger
+        // generations fall back to the exact pairwise comparison below.
+        if (entry.handle.generation >= (1u << 24)) {
+            for (std::size_t i = 1; i < entries.size(); ++i) {
+                for (std::size_t j = 0; j < i; ++j) {
+                    if (entries[j].handle == entries[i].handle) {
+                        return false;
+                    }
+                }
+            }
+            return true;
+        }
+        keys[n++] = (static_cast<std::uint64_t>(static_cast<std::uint8_t>(entry.handle.kind)) << 56)
+            | (static_cast<std::uint64_t>(entry.handle.slot) << 24) | entry.handle.generation;
+    }
+    std::sort(keys, keys + n);
+    return std::adjacent_find(keys, keys + n) == keys + n;
 }
 
 } // namespace

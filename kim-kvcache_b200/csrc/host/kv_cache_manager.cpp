@@ -18,24 +18,6 @@ KvCacheManager::KvCacheManager(std::uint32_t micro_capacity, std::uint32_t exten
 {
 }
 
-KvCacheManager::Page* KvCacheManager::page(PageHandle handle) noexcept
-{
-    return const_cast<Page*>(static_cast<KvCacheManager const*>(this)->page(handle));
-}
-
-KvCacheManager::Page const* KvCacheManager::page(PageHandle handle) const noexcept
-{
-    if (!handle.isStructurallyValid()) {
-        return nullptr;
-    }
-    std::vector<Page> const& pages =
-        handle.kind == PageKind::Micro ? micro_pages_ : extent_pages_;
-    if (handle.slot >= pages.size() || pages[handle.slot].generation != handle.generation) {
-        return nullptr;
-    }
-    return &pages[handle.slot];
-}
-
 // Takes a fresh micro page for a staged copy-on-write or growth target. The
 // page stays CopyTarget (unreferenced) until the owning operation commits.
 KvCacheError KvCacheManager::stageMicro(std::uint16_t initial_valid_tokens, PageHandle& out)

@@ -245,5 +245,25 @@ private:
 
     mutable std::mutex mutex_;
 };
+// Page records by handle (inline: every lease pins and releases each page of
+// a table, so this runs tens of times per token reservation).
+inline KvCacheManager::Page const* KvCacheManager::page(PageHandle handle) const noexcept
+{
+    if (!handle.isStructurallyValid()) {
+        return nullptr;
+    }
+    std::vector<Page> const& pages =
+        handle.kind == PageKind::Micro ? micro_pages_ : extent_pages_;
+    if (handle.slot >= pages.size() || pages[handle.slot].generation != handle.generation) {
+        return nullptr;
+    }
+    return &pages[handle.slot];
+}
+
+inline KvCacheManager::Page* KvCacheManager::page(PageHandle handle) noexcept
+{
+    return const_cast<Page*>(static_cast<KvCacheManager const*>(this)->page(handle));
+}
+
 
 } // namespace kimkvcache
