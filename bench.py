@@ -228,6 +228,9 @@ def run_ours(args, rank, world, local_rank):
     launches = R["runner_last_launches"](runner)
     dev_ms = sum(device_ms)
 
+    if args.trace:
+        trace_step(kk, step, torch, dev, args.trace)
+
     # Dominant-kernel roofline: replay the attention of one step (all 22 layers,
     # same work list) and time it with CUDA events on the launching stream.
     roof = attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr)
@@ -353,6 +356,79 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of "
                               "the same kernel and work list on the kernel-only c4 case "
                               "(80.72 MB for 78.30 MB algorithmic), scaled by the bytes processed"}
+
+
+# ---------------------------------------------------------------------------
+# Phase trace (library built with `build.py --trace`)
+
+# Stamps of a projection CTA: entry, dependency wait returned, accumulator
+# complete, partial tile in shared memory, cluster wait passed, peers'
+# partials received, reduced, epilogue stored, exit. Attention CTA: entry,
+# producer's wait returned, producer done, first stage taken, consumers done,
+# exit (aux = stages | split-combine flag << 31).
+GEMM_PHASES = ["wait", "acc", "part", "cl_wait", "recv", "reduced", "epi", "exit"]
+ATTN_PHASES = ["wait", "prod_done", "first_stage", "cons_done", "exit"]
+
+
+def trace_step(kk, step, torch, dev, path):
+    """One decode step with per-CTA phase stamps: saves the records to `path`
+    (.npz) and prints, per kernel, the median time of each phase after the
+    launch's first dependency-wait return (medians over CTAs, then over the
+    inner layers), the launch's span to its last exit, and the hand-off from
+    the previous launch's last exit."""
+    import numpy as np
+    lib = kk.load_library()
+    if not hasattr(lib, "kk_trace_read_gemm"):
+        raise SystemExit("--trace needs the trace build: python kim-kvcache_b200/build.py --trace")
+    rec = np.dtype([("tag", "<u4"), ("block", "<u4"), ("smid", "<u4"), ("aux", "<u4"), ("t", "<u8", 10)])
+    readers = {"gemm": lib.kk_trace_read_gemm, "attn": lib.kk_trace_read_attn}
+    for fn in readers.values():
+        fn.restype = C.c_uint32
+        fn.argtypes = [C.c_void_p, C.c_uint32, C.c_int]
+        fn(None, 0, 1)
+    step()
+    torch.cuda.synchronize(dev)
+    out = {}
+    for name, fn in readers.items():
+        buf = np.zeros(1 << 16, dtype=rec)
+        out[name] = buf[:fn(C.c_void_p(buf.ctypes.data), 1 << 16, 1)]
+    np.savez(path, **out)
+    g, a = out["gemm"], out["attn"]
+    kind, layer = g["tag"] >> 16, g["tag"] & 0xFFFF
+    launches = []  # (start, name, layer, records)
+    names = {4: "qkv", 3: "gate/up", 5: "lm_head"}
+    for key in sorted(set(zip(kind.tolist(), layer.tolist(), g["aux"].tolist()))):
+        k, l, kd = key
+        nm = names.get(k, "o" if kd == 2048 else "down")
+        r = g[(kind == k) & (layer == l) & (g["aux"] == kd)]
+        launches.append((int(r["t"][:, 0].min()), nm, l, r, GEMM_PHASES))
+    al = a["tag"] & 0xFFFF
+    for l in sorted(set(al.tolist())):
+        r = a[al == l]
+        launches.append((int(r["t"][:, 0].min()), "attention", l, r, ATTN_PHASES))
+    launches.sort(key=lambda x: x[0])
+    rows, prev_end = {}, None
+    for _, nm, l, r, phases in launches:
+        t = r["t"].astype(np.int64)
+        waits = t[:, 1][t[:, 1] > 0]
+        w0 = int(waits.min()) if len(waits) else int(t[:, 0].min())
+        cols = [1, 2, 3, 4, 5, 6, 7, 8] if phases is GEMM_PHASES else [1, 2, 3, 4, 5]
+        med = [float(np.median(t[:, c][t[:, c] > 0] - w0)) / 1e3 if (t[:, c] > 0).any() else float("nan")
+               for c in cols]
+        end = int(t[:, 8 if phases is GEMM_PHASES else 5].max())
+        handoff = (w0 - prev_end) / 1e3 if prev_end is not None else float("nan")
+        prev_end = end
+        if 0 < l < max(layer.max(), al.max()):
+            rows.setdefault(nm, []).append(med + [(end - w0) / 1e3, handoff, len(r)])
+    print(f"phase trace of one step -> {path} (us after the launch's first dependency-wait return; "
+          "medians over CTAs and over the inner layers)")
+    for nm in ["qkv", "attention", "o", "gate/up", "down"]:
+        if nm not in rows:
+            continue
+        m = np.nanmedian(np.array(rows[nm], dtype=float), axis=0)
+        phases = ATTN_PHASES if nm == "attention" else GEMM_PHASES
+        cells = "  ".join(f"{p} {v:.2f}" for p, v in zip(phases, m[:len(phases)]))
+        print(f"  {nm:9s} CTAs {int(m[-1]):4d} | {cells} | span {m[-3]:.2f} | hand-off {m[-2]:.2f}")
 
 
 # ---------------------------------------------------------------------------
@@ -692,6 +768,9 @@ def main():
                     help="--kernel-only: launch with programmatic dependent launch (as the runner does)")
     ap.add_argument("--plan", default="balanced", choices=["balanced", "lane"],
                     help="--kernel-only attention: one token-balanced run per SM, or per-lane items")
+    ap.add_argument("--trace", default=None, metavar="OUT.npz",
+                    help="after the timed steps, record per-CTA phase stamps of one more step "
+                         "(needs the library built with build.py --trace)")
     ap.add_argument("--prefill", action="store_true",
                     help="time the fused multi-token prefill instead of decode (one GPU)")
     ap.add_argument("--prompt", type=int, default=1024, help="--prefill: tokens per prompt")

@@ -1,7 +1,12 @@
 """Builds libkk_b200.so in-tree: the host token-loop runtime (C++17), the
 sm_100a CUDA kernels and their C ABI, in one shared library.
 
-Usage: python kim-kvcache_b200/build.py [--force] [-j N]
+Usage: python kim-kvcache_b200/build.py [--force] [-j N] [--trace]
+
+--trace builds the same library with phase tracing compiled in (-DKK_TRACE,
+objects in _build_trace/): every CTA of the projection and attention kernels
+records %globaltimer stamps of its phases, read back by
+`python bench.py --trace OUT`. Rebuild without --trace for measurements.
 
 Objects go to kim-kvcache_b200/_build/, the library to
 kim-kvcache_b200/lib/libkk_b200.so (both git-ignored; the .so travels to the
@@ -48,8 +53,9 @@ def newest_header() -> float:
     return max(stamps, default=0.0)
 
 
-def compile_one(src: Path, force: bool, hdr_time: float, extra: list[str]) -> tuple[Path, str]:
-    obj = OBJ / (src.relative_to(CSRC).as_posix().replace("/", "__") + ".o")
+def compile_one(src: Path, force: bool, hdr_time: float, extra: list[str],
+                obj_dir: Path = OBJ) -> tuple[Path, str]:
+    obj = obj_dir / (src.relative_to(CSRC).as_posix().replace("/", "__") + ".o")
     if (not force and obj.exists() and obj.stat().st_mtime >= src.stat().st_mtime
             and obj.stat().st_mtime >= hdr_time):
         return obj, ""
@@ -64,25 +70,34 @@ def compile_one(src: Path, force: bool, hdr_time: float, extra: list[str]) -> tu
 
 
 def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
-          ptxas_info: bool = False) -> Path:
-    OBJ.mkdir(parents=True, exist_ok=True)
+          ptxas_info: bool = False, trace: bool = False) -> Path:
+    obj_dir = PKG / "_build_trace" if trace else OBJ
+    obj_dir.mkdir(parents=True, exist_ok=True)
     LIB.parent.mkdir(parents=True, exist_ok=True)
     hdr_time = newest_header()
     extra = ["-Xptxas", "-v"] if ptxas_info else []
+    if trace:
+        extra.append("-DKK_TRACE")
     srcs = sources()
     jobs = jobs or min(8, os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(jobs) as pool:
-        results = list(pool.map(lambda s: compile_one(s, force, hdr_time, extra), srcs))
+        results = list(pool.map(lambda s: compile_one(s, force, hdr_time, extra, obj_dir), srcs))
     objs = [r[0] for r in results]
     for (obj, log) in results:
         if log and (verbose or ptxas_info):
             print(f"[{obj.name}]\n{log}")
     lib_time = LIB.stat().st_mtime if LIB.exists() else 0.0
-    if force or not LIB.exists() or any(o.stat().st_mtime > lib_time for o in objs):
+    # The library is relinked whenever it was last linked from the other
+    # object set (plain vs trace), recorded beside it.
+    stamp = LIB.parent / ".variant"
+    variant = "trace" if trace else "plain"
+    switched = not stamp.exists() or stamp.read_text() != variant
+    if force or switched or not LIB.exists() or any(o.stat().st_mtime > lib_time for o in objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+        stamp.write_text(variant)
     return LIB
 
 
@@ -92,9 +107,10 @@ if __name__ == "__main__":
     ap.add_argument("-j", type=int, default=None)
     ap.add_argument("-v", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
+    ap.add_argument("--trace", action="store_true")
     a = ap.parse_args()
     try:
-        print(build(a.force, a.j, a.v, a.ptxas_info))
+        print(build(a.force, a.j, a.v, a.ptxas_info, a.trace))
     except RuntimeError as e:
         print(e, file=sys.stderr)
         sys.exit(1)

@@ -491,7 +491,7 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     const kk_attn_item* items, uint32_t num_items, std::uint32_t const* num_items_dev,
     const uint16_t* query, uint32_t query_stride,
     uint16_t* output, uint32_t output_stride, float scale, void* workspace,
-    uint64_t workspace_bytes, int variant, cudaStream_t stream, kk::AttnPrefetch const* pf = nullptr)
+    uint64_t workspace_bytes, int variant, cudaStream_t stream)
 {
     using namespace kk;
     if (pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
@@ -558,7 +558,7 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     if (tma_ok && variant != KK_ATTN_DIRECT) {
         return attentionTmaLaunch(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
             num_items_dev, query, query_stride, output, output_stride, scale, a.counters, a.part_o,
-            a.part_ml, stream, pf);
+            a.part_ml, stream);
     }
     unsigned const grid = num_items < unsigned(numSms()) ? num_items : unsigned(numSms());
     return static_cast<int>(launch(paged_decode_attention_kernel, dim3(grid), dim3(kThreads), 0,
@@ -765,7 +765,7 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
-    cudaStream_t stream, AttnPrefetch const* pf)
+    cudaStream_t stream)
 {
     if (num_items == nullptr) {
         return KK_EINVAL;
@@ -776,6 +776,6 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     int const variant = attentionTmaSupported(pools, q_heads) ? KK_ATTN_TMA : KK_ATTN_DIRECT;
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, max_items,
         num_items, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
-        variant, stream, pf);
+        variant, stream);
 }
 } // namespace kk

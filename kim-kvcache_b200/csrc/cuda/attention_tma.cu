@@ -114,16 +114,6 @@ struct TmaArgs {
     std::uint32_t* counters;
     float* part_o;
     float* part_ml;
-    // L2 prefetch (both optional). kv_pf_bytes: the first pages of each CTA's
-    // first item (this layer's K and V), requested before the dependency
-    // wait, while the previous kernel runs. l2_pf: a share of a byte range
-    // that a later kernel of the step streams, requested stage by stage.
-    std::uint8_t const* micro_base;
-    std::uint8_t const* extent_base;
-    std::uint32_t layers;
-    std::uint32_t kv_pf_bytes;
-    void const* l2_pf;
-    std::uint64_t l2_pf_bytes;
 };
 
 __device__ __forceinline__ void tma_load_5d_hint(void* dst, CUtensorMap const* map, std::uint64_t* bar,
@@ -322,11 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             prefetch_tensormap(&tm_micro);
             prefetch_tensormap(&tm_extent);
         }
-        // K/V of a layer is read once per step: first to go from L2, so that
-        // lines prefetched for later kernels stay.
+        // K/V of a layer is read once per step: first to go from L2. Measured
+        // on the c4 step, this keeps the small data that the other kernels
+        // re-read (activations, partials, norm statistics, descriptors) in L2
+        // (the step is ~3% slower with default priority), although a replay
+        // of attention alone is ~1.5% faster without it.
         std::uint64_t const kv_policy = l2_policy_evict_first();
-        L2PrefetchShare wpf;
-        wpf.init(a.l2_pf, a.l2_pf_bytes, blockIdx.x, gridDim.x);
         bool waited = false;
         std::uint32_t stage = 0;
         std::uint32_t qk = 0;  // lane segments started by this CTA
@@ -421,36 +412,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
             };
             seek();
-            if (!waited && a.kv_pf_bytes != 0) {
-                // The first pages of this CTA's first item, into L2 while the
-                // previous kernel still runs. That kernel writes only each
-                // lane's newest token, and its writes land in L2 too, so
-                // lines fetched early stay coherent.
-                std::uint32_t const i = item.desc_begin + lane;
-                std::uint32_t bytes = 0;
-                std::uint8_t const* src = nullptr;
-                if (i < item.desc_end) {
-                    kk_page_desc const d = a.descs[i];
-                    bool const m = d.kind == 0;
-                    std::uint32_t const cap = m ? 8u : 64u;
-                    if ((m ? d.slot < a.micro_slots : d.slot < a.extent_slots) && d.valid_tokens != 0
-                        && d.valid_tokens <= cap) {
-                        std::uint64_t const run = 2ull * cap * Hkv * kRowBytes;  // K then V of a layer
-                        src = (m ? a.micro_base : a.extent_base)
-                            + (std::uint64_t(d.slot) * a.layers + a.layer) * run;
-                        bytes = static_cast<std::uint32_t>(run);
-                    }
-                }
-                std::uint32_t upto = bytes;
-#pragma unroll
-                for (std::uint32_t o = 1; o < 32; o <<= 1) {
-                    std::uint32_t const t = __shfl_up_sync(0xffffffffu, upto, o);
-                    upto += lane >= o ? t : 0u;
-                }
-                if (bytes != 0 && src != nullptr && upto <= a.kv_pf_bytes) {
-                    l2_prefetch_bulk(src, bytes);
-                }
-            }
             if (!waited) {
                 pdl_wait();  // K/V pages and queries are written by the previous kernel
                 waited = true;
@@ -571,7 +532,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 if (lane == 0) {
                     meta[s] = m;
                     mbar_arrive(&full[s]);  // releases meta[s]; the phase ends when the bytes land
-                    wpf.issue(32768u);
                 }
                 ++stage;
                 if (item_done) {
@@ -584,8 +544,6 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     seek();
                 }
             }
-        }
-        while (lane == 0 && wpf.issue(32768u)) {
         }
         if (lane == 0) {
             KK_ATTN_STAMP(2)
@@ -1134,7 +1092,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream, AttnPrefetch const* pf)
+    cudaStream_t stream)
 {
     PoolMaps maps{};
     if (!poolMaps(*pools, maps)) {
@@ -1171,16 +1129,6 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.counters = counters;
     a.part_o = part_o;
     a.part_ml = part_ml;
-    a.micro_base = static_cast<std::uint8_t const*>(pools->micro);
-    a.extent_base = static_cast<std::uint8_t const*>(pools->extent);
-    a.layers = pools->layers;
-    if (pf != nullptr) {
-        a.kv_pf_bytes = pf->kv_bytes;
-        if (pf->ptr != nullptr && (reinterpret_cast<std::uintptr_t>(pf->ptr) & 15u) == 0) {
-            a.l2_pf = pf->ptr;
-            a.l2_pf_bytes = pf->bytes & ~std::uint64_t(15);
-        }
-    }
     static int const sms = smCount();
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
     bool const narrow = a.group <= 8;

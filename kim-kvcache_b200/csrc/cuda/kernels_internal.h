@@ -13,17 +13,6 @@
 
 namespace kk {
 
-// L2 prefetch requests of one attention launch (TMA kernel only): each CTA
-// asks L2 for the first kv_bytes of its first work item's pages (this
-// layer's K and V) before its dependency wait, and for its share of
-// [ptr, ptr + bytes), bytes that a later kernel of the step streams, one
-// piece per stage.
-struct AttnPrefetch {
-    std::uint32_t kv_bytes;
-    void const* ptr;
-    std::uint64_t bytes;
-};
-
 // kk_paged_decode_attention with the item count in device memory; items
 // beyond *num_items (<= max_items) are ignored. The grid is sized for max_items.
 int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
@@ -31,7 +20,7 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
-    cudaStream_t stream, AttnPrefetch const* pf = nullptr);
+    cudaStream_t stream);
 
 // TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
 // KV heads, up to 16 query heads per KV head; serves both plan kinds
@@ -43,7 +32,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream, AttnPrefetch const* pf = nullptr);
+    cudaStream_t stream);
 
 // kk_kv_copy_tokens with the copy count in device memory (<= max_copies).
 int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
