@@ -284,7 +284,7 @@ def run_ours(args, rank, world, local_rank):
 # DRAM traffic / algorithmic K+V bytes of one K1 launch, from an ncu capture of
 # `bench.py --kernel-only attention --variant tma --plan balanced` (the same
 # kernel, balanced work list and context distribution as the c4 step).
-K1_TRAFFIC_PER_ALGORITHMIC_BYTE = 80.717056 / 78.297088
+K1_TRAFFIC_PER_ALGORITHMIC_BYTE = 80.686848 / 78.297088
 
 
 def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr):
@@ -355,7 +355,7 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
             "traffic": round(bytes_per_launch * K1_TRAFFIC_PER_ALGORITHMIC_BYTE),
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch of "
                               "the same kernel and work list on the kernel-only c4 case "
-                              "(80.72 MB for 78.30 MB algorithmic), scaled by the bytes processed"}
+                              "(80.69 MB for 78.30 MB algorithmic), scaled by the bytes processed"}
 
 
 # ---------------------------------------------------------------------------
