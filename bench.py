@@ -151,30 +151,45 @@ def run_ours(args, rank, world, local_rank):
     stream = torch.cuda.current_stream(dev)
     sptr = C.c_void_p(stream.cuda_stream)
     total_tokens = sum(contexts) + B * (args.steps + args.warmup + 2)
-    # Room for every 64-token run that auto-promotion folds during the run:
-    # with too few extents, promotion fails and the tails grow as micro pages.
-    extent_cap = sum((c + args.steps + args.warmup + 2) // 64 for c in contexts) + B
-    micro_cap = B * 16 + total_tokens // 8 + 64
     hq, hkv, D, L = cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["layers"]
-    backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
-    assert backend, "backend allocation failed"
-    pools = kk.KvPools()
-    assert R["backend_pools"](backend, C.byref(pools))
-
-    # Prefix state: append ctx tokens, seal, promote every full 64-token run.
-    for i, ctx in enumerate(contexts):
-        rid = i + 1
-        assert R["backend_create_request"](backend, rid) == 0
-        assert R["backend_append"](backend, rid, ctx) == 0
-        R["backend_seal"](backend, rid)
-        for begin in range(0, (ctx // 64) * 64, 64):
-            assert R["backend_promote"](backend, rid, begin, sptr) == 0
-    # Synthetic KV contents for every page (the prefix K/V of a real prefill).
     row = hkv * D
-    micro_elems = micro_cap * L * 2 * 8 * row
-    extent_elems = extent_cap * L * 2 * 64 * row
-    assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, SEED + rank, 0.35, sptr) == 0
-    assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, SEED + 1 + rank, 0.35, sptr) == 0
+    fixed = 0 if args.pages == "hetero" else int(args.pages[len("fixed"):])
+    if fixed:
+        # Fixed-page backend: every page holds `fixed` tokens (the reference's
+        # strategy baseline); prefixes are appended, nothing is promoted.
+        page_cap = sum(-(-(c + args.steps + args.warmup + 2) // fixed) for c in contexts) + B
+        backend = R["fixed_backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, fixed, page_cap)
+        assert backend, "backend allocation failed"
+        for i, ctx in enumerate(contexts):
+            assert R["backend_create_request"](backend, i + 1) == 0
+            assert R["backend_append"](backend, i + 1, ctx) == 0
+        pools = kk.KvPools()
+        assert R["backend_pools"](backend, C.byref(pools))
+        assert K["fill_fp16"](C.c_void_p(pools.micro), page_cap * L * 2 * fixed * row, SEED + rank, 0.35,
+                              sptr) == 0
+    else:
+        # Room for every 64-token run that auto-promotion folds during the run:
+        # with too few extents, promotion fails and the tails grow as micro pages.
+        extent_cap = sum((c + args.steps + args.warmup + 2) // 64 for c in contexts) + B
+        micro_cap = B * 16 + total_tokens // 8 + 64
+        backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
+        assert backend, "backend allocation failed"
+        pools = kk.KvPools()
+        assert R["backend_pools"](backend, C.byref(pools))
+
+        # Prefix state: append ctx tokens, seal, promote every full 64-token run.
+        for i, ctx in enumerate(contexts):
+            rid = i + 1
+            assert R["backend_create_request"](backend, rid) == 0
+            assert R["backend_append"](backend, rid, ctx) == 0
+            R["backend_seal"](backend, rid)
+            for begin in range(0, (ctx // 64) * 64, 64):
+                assert R["backend_promote"](backend, rid, begin, sptr) == 0
+        # Synthetic KV contents for every page (the prefix K/V of a real prefill).
+        micro_elems = micro_cap * L * 2 * 8 * row
+        extent_elems = extent_cap * L * 2 * 64 * row
+        assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, SEED + rank, 0.35, sptr) == 0
+        assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, SEED + 1 + rank, 0.35, sptr) == 0
     torch.cuda.synchronize(dev)
 
     status = C.c_int(0)
@@ -184,7 +199,7 @@ def run_ours(args, rank, world, local_rank):
     assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
     # Fold each lane's 8 sealed micro pages into an extent whenever decode
     # completes a 64-token run, so tails stay short (8 micro -> 1 extent).
-    assert R["runner_set_auto_promote"](runner, 1) == 1
+    assert R["runner_set_auto_promote"](runner, 0 if fixed else 1) == 1
 
     ids = (C.c_uint64 * B)(*range(1, B + 1))
     tokens = (C.c_uint32 * B)(*[random.Random(SEED + b).randrange(3, 32000) for b in range(B)])
@@ -267,6 +282,7 @@ def run_ours(args, rank, world, local_rank):
             "batch_per_gpu": B,
             "ctx_mean": round(sum(contexts) / len(contexts), 1),
             "parallelism": f"replicas x{world}",
+            "pages": "micro 8 + extent 64, auto-promotion" if not fixed else f"fixed {fixed}-token pages",
             "l2": "inputs larger than L2 every step (2.07 GB weights + paged KV)",
             "cuda_graphs": True,
         },
@@ -768,6 +784,9 @@ def main():
                     help="--kernel-only: launch with programmatic dependent launch (as the runner does)")
     ap.add_argument("--plan", default="balanced", choices=["balanced", "lane"],
                     help="--kernel-only attention: one token-balanced run per SM, or per-lane items")
+    ap.add_argument("--pages", default="hetero", choices=["hetero", "fixed8", "fixed16", "fixed32", "fixed64"],
+                    help="KV backend of the decode step: two pools (8-token micro + 64-token extent pages, "
+                         "the default) or a fixed-page backend (reference Fixed-8/16/32/64)")
     ap.add_argument("--trace", default=None, metavar="OUT.npz",
                     help="after the timed steps, record per-CTA phase stamps of one more step "
                          "(needs the library built with build.py --trace)")

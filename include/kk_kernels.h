@@ -36,14 +36,19 @@ extern "C" {
 #define KK_EINVAL 1000
 
 typedef struct kk_kv_pools {
-    void* micro;               /* micro_capacity pages of layers*2*8*kv_heads*head_dim fp16 */
+    void* micro;               /* micro_capacity pages of layers*2*T*kv_heads*head_dim fp16,
+                                  T = micro_page_tokens (8 when 0) */
     void* extent;              /* extent_capacity pages of layers*2*64*kv_heads*head_dim fp16 */
     uint32_t micro_capacity;
     uint32_t extent_capacity;
     uint32_t layers;
     uint32_t kv_heads;
     uint32_t head_dim;
-    uint32_t reserved;
+    uint32_t micro_page_tokens; /* tokens per micro page: 0 or 8 (the two-pool runtime), or
+                                   16/32/64 for a fixed-page backend's pool (reference
+                                   EngineBackendState(config, tokens_per_page, capacity),
+                                   src/cuda/engine/backend.cpp:91-106); the extent pool is then
+                                   unused (extent_capacity 0) */
 } kk_kv_pools;
 
 /* One block-table entry as the kernels read it (reference DeviceBlockDescriptor,

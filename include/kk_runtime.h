@@ -198,6 +198,16 @@ typedef struct kk_backend_snapshot {  /* reference EngineKvBackendSnapshot (engi
 KK_API void* kkrt_backend_create(uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
     uint32_t q_heads, uint64_t attention_workspace_bytes, uint32_t micro_capacity,
     uint32_t extent_capacity);
+/* createFixedCudaEngineKvBackend (include/kim-kv/cuda/cuda_engine_kv_backend.h:19-22,
+ * src/cuda/engine/backend.cpp:579-598): FixedPageManager metadata and one device pool of
+ * page_capacity pages of tokens_per_page (8, 16, 32 or 64) tokens; NULL on failure.
+ * Every kkrt_backend_* call, the runner and the scheduler accept it; promotion does not
+ * apply (kkrt_backend_promote returns EngineKvError::InvalidArgument). */
+KK_API void* kkrt_fixed_backend_create(uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
+    uint32_t q_heads, uint64_t attention_workspace_bytes, uint32_t tokens_per_page,
+    uint32_t page_capacity);
+/* EngineKvBackend::kind(): 0 heterogeneous (two pools), 1 fixed-page. */
+KK_API int kkrt_backend_kind(void* backend);
 KK_API void kkrt_backend_destroy(void* backend);
 /* createRequest / forkRequest / releaseRequest (backend.cpp:341-384): EngineKvError. */
 KK_API int kkrt_backend_create_request(void* backend, uint64_t request_id);

@@ -335,7 +335,7 @@ EPI_STORE_F16, EPI_STORE_F32, EPI_RESIDUAL, EPI_SILU_PAIRS, EPI_QKV_ROPE, EPI_AR
 class KvPools(C.Structure):
     _fields_ = [("micro", C.c_void_p), ("extent", C.c_void_p), ("micro_capacity", C.c_uint32),
                 ("extent_capacity", C.c_uint32), ("layers", C.c_uint32), ("kv_heads", C.c_uint32),
-                ("head_dim", C.c_uint32), ("reserved", C.c_uint32)]
+                ("head_dim", C.c_uint32), ("micro_page_tokens", C.c_uint32)]
 
 
 class PageDesc(C.Structure):
@@ -449,6 +449,8 @@ _I64, _F = C.c_int64, C.c_float
 _PU32, _PU64 = C.POINTER(C.c_uint32), C.POINTER(C.c_uint64)
 RUNTIME_SIGNATURES = {
     "backend_create": (_VP, [_U32, _U32, _U32, _U32, _U64, _U32, _U32]),
+    "fixed_backend_create": (_VP, [_U32, _U32, _U32, _U32, _U64, _U32, _U32]),
+    "backend_kind": (_I, [_VP]),
     "backend_destroy": (None, [_VP]),
     "backend_create_request": (_I, [_VP, _U64]),
     "backend_fork": (_I, [_VP, _U64, _U64]),

@@ -158,6 +158,16 @@ void* kkrt_backend_create(uint32_t layers, uint32_t kv_heads, uint32_t head_dim,
     EngineKvConfig const c{KvLayout{layers, kv_heads, head_dim}, q_heads, static_cast<std::size_t>(ws_bytes)};
     return createHeterogeneousCudaEngineKvBackend(c, micro, extent).release();
 }
+void* kkrt_fixed_backend_create(uint32_t layers, uint32_t kv_heads, uint32_t head_dim, uint32_t q_heads,
+    uint64_t ws_bytes, uint32_t tokens_per_page, uint32_t page_capacity)
+{
+    if (tokens_per_page > 0xffffu) {
+        return nullptr;
+    }
+    EngineKvConfig const c{KvLayout{layers, kv_heads, head_dim}, q_heads, static_cast<std::size_t>(ws_bytes)};
+    return createFixedCudaEngineKvBackend(c, static_cast<std::uint16_t>(tokens_per_page), page_capacity).release();
+}
+int kkrt_backend_kind(void* b) { return static_cast<int>(KV(b)->kind()); }
 void kkrt_backend_destroy(void* b) { delete KV(b); }
 int kkrt_backend_create_request(void* b, uint64_t id) { return int(KV(b)->createRequest(id).error); }
 int kkrt_backend_fork(void* b, uint64_t s, uint64_t c) { return int(KV(b)->forkRequest(s, c).error); }

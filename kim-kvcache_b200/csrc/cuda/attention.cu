@@ -87,6 +87,7 @@ struct AttnArgs {
     std::uint64_t extent_page;
     std::uint32_t micro_slots;       // pool capacities (pages), for bounds checks
     std::uint32_t extent_slots;
+    std::uint32_t micro_cap;         // tokens per micro page
     std::uint32_t layer;
     std::uint32_t kv_heads;
     std::uint32_t group;             // query heads per KV head
@@ -172,7 +173,7 @@ __device__ __forceinline__ void load_group(GroupRegs& g, AttnArgs const& a, Curs
     }
     kk_page_desc const d = a.descs[c.entry];
     bool const micro = d.kind == 0;
-    std::uint32_t const cap = micro ? kMicroTokens : kExtentTokens;
+    std::uint32_t const cap = micro ? a.micro_cap : kExtentTokens;
     if ((micro ? d.slot >= a.micro_slots : d.slot >= a.extent_slots)
         || d.valid_tokens > cap) {
         atomicCAS(&g_attn_status, kErrNone, kErrBadDescriptor);
@@ -500,7 +501,7 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
         || q_heads % pools->kv_heads != 0 || q_heads / pools->kv_heads > 16
         || q_heads / pools->kv_heads == 0 || !(scale > 0.f) || query == nullptr
         || output == nullptr || descs == nullptr || lanes == nullptr || items == nullptr
-        || query_stride % 8 != 0 || output_stride % 8 != 0) {
+        || query_stride % 8 != 0 || output_stride % 8 != 0 || !microPageTokensValid(*pools)) {
         return KK_EINVAL;
     }
     // The workspace (completion counters + partial states) is only touched
@@ -517,7 +518,8 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     a.micro = static_cast<__half const*>(pools->micro);
     a.extent = static_cast<__half const*>(pools->extent);
     std::uint64_t const row = std::uint64_t(pools->kv_heads) * kHeadDim;
-    a.micro_page = std::uint64_t(pools->layers) * 2u * kMicroTokens * row;
+    a.micro_cap = microPageTokens(*pools);
+    a.micro_page = std::uint64_t(pools->layers) * 2u * a.micro_cap * row;
     a.extent_page = std::uint64_t(pools->layers) * 2u * kExtentTokens * row;
     a.micro_slots = pools->micro == nullptr ? 0 : pools->micro_capacity;
     a.extent_slots = pools->extent == nullptr ? 0 : pools->extent_capacity;

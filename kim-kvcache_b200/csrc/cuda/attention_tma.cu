@@ -67,6 +67,10 @@ constexpr std::uint32_t kItemEnd = 2u;   // last stage of the item
 // The stage holds micro pages loaded whole ([head][8 tokens] per page, page
 // n at rows n*kv_heads*8): one load for K and one for V per page.
 constexpr std::uint32_t kMicroStage = 4u;
+// With kMicroStage: the pages are 16-token pages of a fixed-page pool (page n
+// at rows n*kv_heads*16, [head][16 tokens] each), so a 16-token slice is one
+// page and its second 8 tokens follow its first within the head's block.
+constexpr std::uint32_t kPage16 = 8u;
 
 struct StageMeta {
     // Valid tokens of each 8-token group slot, one byte per slot (0 = empty
@@ -99,7 +103,10 @@ struct TmaArgs {
     std::uint32_t q_heads;
     std::uint32_t ts;             // tokens per stage
     std::uint32_t extent_per_head;  // 1: the extent map has per-head boxes (fallback)
-    std::uint32_t micro_per_head;   // 1: the micro map has per-head boxes (fallback)
+    std::uint32_t micro_per_head;   // 1: the micro map has per-head boxes
+    std::uint32_t micro_cap;        // tokens per micro page (8, or 16/32/64 for a fixed-page pool)
+    std::uint32_t micro_box;        // tokens per micro-map box when micro pages are loaded in chunks
+    std::uint32_t micro_packed;     // 1: several whole micro pages share a stage (8- and 16-token pages)
     kk_page_desc const* descs;
     kk_attn_lane const* lanes;
     std::uint32_t num_lanes;
@@ -394,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     std::uint32_t const valid = d_word & 0xffffu;
                     bool const m = ((d_word >> 16) & 0xffu) == 0;
                     bool const ok = (m ? d_slot < a.micro_slots : d_slot < a.extent_slots)
-                        && valid <= (m ? 8u : 64u);
+                        && valid <= (m ? a.micro_cap : 64u);
                     if (!ok) {
                         if (lane == 0) {
                             atomicCAS(&g_attn_tma_status, kErrNone, kErrBadDescriptor);
@@ -435,10 +442,17 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 std::uint32_t const kv = a.layer * 2u;
                 std::uint32_t n = 0;
                 while (have && n < groups_per_stage) {
-                    if (!micro) {
+                    if (!micro || a.micro_packed == 0) {
+                        // A chunk of up to Ts tokens of one page: an extent
+                        // page, or a page of a fixed-page micro pool (16-64
+                        // tokens; a page shorter than a stage fills the first
+                        // rows of each head's block, per-head boxes).
                         if (n != 0) {
-                            break;  // an extent chunk always starts a fresh stage
+                            break;  // a chunk always starts a fresh stage
                         }
+                        CUtensorMap const* map = micro ? &tm_micro : &tm_extent;
+                        bool const per_head = micro ? a.micro_per_head != 0 : a.extent_per_head != 0;
+                        std::uint32_t const bt = micro ? a.micro_box : Ts;
 #pragma unroll
                         for (std::uint32_t j = 0; j < 8; ++j) {
                             std::uint32_t const first = tok + 8u * j;
@@ -446,18 +460,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             m.valid |= std::uint64_t(left < 8u ? left : 8u) << (8u * j);
                         }
                         if (lane == 0) {
-                            mbar_expect_tx(&full[s], 2u * Hkv * Ts * kRowBytes);
-                            if (a.extent_per_head == 0) {
-                                tma_load_5d_hint(base, &tm_extent, &full[s], 0, static_cast<int>(tok), 0,
+                            mbar_expect_tx(&full[s], 2u * Hkv * bt * kRowBytes);
+                            if (!per_head) {
+                                tma_load_5d_hint(base, map, &full[s], 0, static_cast<int>(tok), 0,
                                     static_cast<int>(kv), slot, kv_policy);
-                                tma_load_5d_hint(base + v_offset, &tm_extent, &full[s], 0, static_cast<int>(tok),
+                                tma_load_5d_hint(base + v_offset, map, &full[s], 0, static_cast<int>(tok),
                                     0, static_cast<int>(kv + 1), slot, kv_policy);
                             } else {
                                 for (std::uint32_t h = 0; h < Hkv; ++h) {
                                     std::uint8_t* dst = base + h * Ts * kRowBytes;
-                                    tma_load_5d_hint(dst, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                    tma_load_5d_hint(dst, map, &full[s], 0, static_cast<int>(h),
                                         static_cast<int>(tok), static_cast<int>(kv), slot, kv_policy);
-                                    tma_load_5d_hint(dst + v_offset, &tm_extent, &full[s], 0, static_cast<int>(h),
+                                    tma_load_5d_hint(dst + v_offset, map, &full[s], 0, static_cast<int>(h),
                                         static_cast<int>(tok), static_cast<int>(kv + 1), slot, kv_policy);
                                 }
                             }
@@ -468,6 +482,22 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             ++e;
                             seek();
                         }
+                    } else if (a.micro_cap == 16u) {
+                        // A whole 16-token page (two groups) per box; pages
+                        // of this pool start at even groups.
+                        std::uint32_t const lo = vt < 8u ? vt : 8u;
+                        m.valid |= (std::uint64_t(lo) << (8u * n)) | (std::uint64_t(vt - lo) << (8u * (n + 1u)));
+                        m.flags |= kMicroStage | kPage16;
+                        if (lane == 0) {
+                            mbar_expect_tx(&full[s], 2u * Hkv * 16u * kRowBytes);
+                            std::uint8_t* dst = base + n * Hkv * 8u * kRowBytes;
+                            tma_load_5d_hint(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot, kv_policy);
+                            tma_load_5d_hint(dst + v_offset, &tm_micro, &full[s], 0, 0, 0,
+                                static_cast<int>(kv + 1), slot, kv_policy);
+                        }
+                        n += 2u;
+                        ++e;
+                        seek();
                     } else {
                         m.valid |= std::uint64_t(vt) << (8u * n);
                         if (a.micro_per_head == 0) {
@@ -721,8 +751,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 // micro stage token r lives in page 2*chunk + r/8, whose
                 // [head][8 tokens] block starts every kv_heads*8 rows.
                 std::uint32_t const step8 = (m.flags & kMicroStage) ? Hkv * 8u : 8u;
+                std::uint32_t const gstep = (m.flags & kPage16) ? 8u : step8;  // second 8 tokens of the slice
+                std::uint32_t const hrows = (m.flags & kMicroStage) ? ((m.flags & kPage16) ? 16u : 8u) : Ts;
                 std::uint32_t const kbase = ring_base + s * kStageBytes
-                    + (head * ((m.flags & kMicroStage) ? 8u : Ts) + chunk * 2u * step8) * kRowBytes;
+                    + (head * hrows + chunk * 2u * step8) * kRowBytes;
                 std::uint32_t const vbase = kbase + v_offset;
                 // S^T = K Q^T over the slice's 16 tokens: K rows are the A operand.
                 float st[NT][4];
@@ -732,7 +764,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
 #pragma unroll
                 for (std::uint32_t k16 = 0; k16 < 4; ++k16) {
-                    std::uint32_t const row = (mi & 1u) * step8 + r8;
+                    std::uint32_t const row = (mi & 1u) * gstep + r8;
                     std::uint32_t const ch = 2u * k16 + (mi >> 1);
                     std::uint32_t ka[4];
                     ldsm_x4(kbase + row * kRowBytes + ((ch ^ r8) << 4), ka);
@@ -780,7 +812,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
 #pragma unroll
                 for (std::uint32_t j = 0; j < 4; ++j) {
-                    std::uint32_t const row = (mi >> 1) * step8 + r8;
+                    std::uint32_t const row = (mi >> 1) * gstep + r8;
                     std::uint32_t const ch = 2u * j + (mi & 1u);
                     std::uint32_t va[4];
                     ldsm_x4_t(vbase + row * kRowBytes + ((ch ^ r8) << 4), va);
@@ -1015,6 +1047,8 @@ struct PoolMaps {
     CUtensorMap extent;
     bool extent_per_head;
     bool micro_per_head;
+    std::uint32_t micro_box;
+    bool micro_packed;
 };
 
 std::uint32_t stageTokens(std::uint32_t kv_heads)
@@ -1035,17 +1069,39 @@ bool poolMaps(kk_kv_pools const& p, PoolMaps& out)
         if (e.device == device && e.pools.micro == p.micro && e.pools.extent == p.extent
             && e.pools.micro_capacity == p.micro_capacity
             && e.pools.extent_capacity == p.extent_capacity && e.pools.layers == p.layers
-            && e.pools.kv_heads == p.kv_heads) {
+            && e.pools.kv_heads == p.kv_heads && e.pools.micro_page_tokens == p.micro_page_tokens) {
             out = e;
             return true;
         }
     }
-    PoolMaps e{p, device, {}, {}, false, false};
+    PoolMaps e{p, device, {}, {}, false, false, 8, false};
     std::uint32_t const ts = stageTokens(p.kv_heads);
-    if (encodeHeadMajor(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+    std::uint32_t const mcap = microPageTokens(p);
+    if (mcap == 16u && ts > 16u
+        && encodeHeadMajor(&e.micro, p.micro, p.micro_capacity, 16, p.layers, p.kv_heads, 16)) {
+        // 16-token pages packed whole, several per stage (like 8-token pages).
         e.micro_per_head = false;
+        e.micro_packed = true;
+        e.micro_box = 16;
+    } else if (mcap != 8u) {
+        // Pages of a fixed-page pool, loaded in chunks like extent pages:
+        // one box per stage when a page fills a stage, per-head boxes of the
+        // whole page otherwise.
+        e.micro_box = mcap < ts ? mcap : ts;
+        if (e.micro_box == ts
+            && encodeHeadMajor(&e.micro, p.micro, p.micro_capacity, mcap, p.layers, p.kv_heads, ts)) {
+            e.micro_per_head = false;
+        } else if (encodePerHead(&e.micro, p.micro, p.micro_capacity, mcap, p.layers, p.kv_heads, e.micro_box)) {
+            e.micro_per_head = true;
+        } else {
+            return false;
+        }
+    } else if (encodeHeadMajor(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
+        e.micro_per_head = false;
+        e.micro_packed = true;
     } else if (encodePerHead(&e.micro, p.micro, p.micro_capacity, 8, p.layers, p.kv_heads, 8)) {
         e.micro_per_head = true;
+        e.micro_packed = true;
     } else {
         return false;
     }
@@ -1082,7 +1138,7 @@ int smCount()
 bool attentionTmaSupported(kk_kv_pools const* pools, std::uint32_t q_heads)
 {
     return pools != nullptr && pools->head_dim == kHeadDim && pools->micro != nullptr
-        && pools->micro_capacity != 0
+        && pools->micro_capacity != 0 && microPageTokensValid(*pools)
         && (pools->kv_heads == 1 || pools->kv_heads == 2 || pools->kv_heads == 4 || pools->kv_heads == 8)
         && q_heads % pools->kv_heads == 0 && q_heads / pools->kv_heads <= 16;
 }
@@ -1115,6 +1171,9 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.ts = stageTokens(pools->kv_heads);
     a.extent_per_head = maps.extent_per_head ? 1u : 0u;
     a.micro_per_head = maps.micro_per_head ? 1u : 0u;
+    a.micro_cap = microPageTokens(*pools);
+    a.micro_box = maps.micro_box;
+    a.micro_packed = maps.micro_packed ? 1u : 0u;
     a.descs = descs;
     a.lanes = lanes;
     a.num_lanes = num_lanes;

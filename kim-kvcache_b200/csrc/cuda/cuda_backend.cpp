@@ -3,6 +3,8 @@
 // src/cuda/kv/storage.cpp:99-234). See cuda_backend.h for the design.
 #include "cuda_backend.h"
 
+#include "../host/fixed_page_manager.h"
+
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -86,6 +88,31 @@ struct Storage {
         }
     }
 
+    // Fixed-page storage: one pool of page_capacity pages of tokens_per_page
+    // tokens (reference EngineBackendState(config, tokens_per_page,
+    // page_capacity), src/cuda/engine/backend.cpp:91-106); no extent pool.
+    Storage(KvLayout layout, std::uint16_t tokens_per_page, std::uint32_t page_capacity)
+    {
+        if (!layout.valid() || (tokens_per_page != 8 && tokens_per_page != 16 && tokens_per_page != 32
+                                   && tokens_per_page != 64)) {
+            status = {CudaError::InvalidArgument, 0};
+            return;
+        }
+        std::size_t const page = std::size_t(layout.layer_count) * 2u * tokens_per_page
+            * layout.kv_head_count * layout.head_dimension;
+        micro_bytes = page * 2 * page_capacity;
+        void* micro = nullptr;
+        cudaError_t e = cudaMalloc(&micro, micro_bytes);
+        if (e == cudaSuccess) {
+            e = cudaMemset(micro, 0, micro_bytes);
+        }
+        pools = kk_kv_pools{micro, nullptr, page_capacity, 0, layout.layer_count, layout.kv_head_count,
+            layout.head_dimension, tokens_per_page};
+        if (e != cudaSuccess) {
+            status = {CudaError::AllocationFailed, static_cast<int>(e)};
+        }
+    }
+
     ~Storage()
     {
         cudaDeviceSynchronize();
@@ -131,7 +158,11 @@ struct Arena {
 
 struct State {
     EngineKvConfig config;
-    KvCacheManager mgr;
+    EngineKvBackendKind kind;
+    // Exactly one metadata runtime: the two-pool manager (heterogeneous
+    // backend) or the fixed-page manager.
+    std::unique_ptr<KvCacheManager> mgr;
+    std::unique_ptr<FixedPageManager> fixed;
     Storage storage;
     Arena arena;
     std::unordered_map<RequestId, std::uint32_t> committed_lengths;
@@ -149,11 +180,53 @@ struct State {
     std::unordered_map<void*, std::uint64_t> completed_seq;
 
     State(EngineKvConfig c, std::uint32_t micro_cap, std::uint32_t extent_cap)
-        : config(c), mgr(micro_cap, extent_cap), storage(c.kv_layout, micro_cap, extent_cap)
+        : config(c), kind(EngineKvBackendKind::Heterogeneous)
+        , mgr(std::make_unique<KvCacheManager>(micro_cap, extent_cap))
+        , storage(c.kv_layout, micro_cap, extent_cap)
     {
         if (storage.status.ok() && !arena.init(micro_cap + extent_cap)) {
             storage.status = {CudaError::AllocationFailed, 0};
         }
+    }
+
+    State(EngineKvConfig c, std::uint16_t tokens_per_page, std::uint32_t page_capacity, bool)
+        : config(c), kind(EngineKvBackendKind::Fixed)
+        , fixed(std::make_unique<FixedPageManager>(tokens_per_page, page_capacity))
+        , storage(c.kv_layout, tokens_per_page, page_capacity)
+    {
+        if (storage.status.ok() && !arena.init(page_capacity)) {
+            storage.status = {CudaError::AllocationFailed, 0};
+        }
+    }
+
+    // Metadata operations of whichever runtime this backend holds.
+    KvCacheError create(RequestId id) { return mgr ? mgr->createRequest(id) : fixed->createRequest(id); }
+    KvCacheError fork(RequestId s, RequestId c) { return mgr ? mgr->forkRequest(s, c) : fixed->forkRequest(s, c); }
+    KvCacheError release(RequestId id) { return mgr ? mgr->releaseRequest(id) : fixed->releaseRequest(id); }
+    KvCacheError append(RequestId id, std::uint32_t n) { return mgr ? mgr->append(id, n) : fixed->append(id, n); }
+    KvCacheError seal(RequestId id) { return mgr ? mgr->sealTail(id) : fixed->sealTail(id); }
+    TokenReservationResult reserve(RequestId id, std::uint32_t expected)
+    {
+        return mgr ? mgr->reserveToken(id, expected) : fixed->reserveToken(id, expected);
+    }
+    KvCacheError commit(KvTokenReservationId id)
+    {
+        return mgr ? mgr->commitTokenReservation(id) : fixed->commitTokenReservation(id);
+    }
+    KvCacheError rollback(KvTokenReservationId id)
+    {
+        return mgr ? mgr->rollbackTokenReservation(id) : fixed->rollbackTokenReservation(id);
+    }
+    std::optional<BlockTable> table(RequestId id) const { return mgr ? mgr->blockTable(id) : fixed->blockTable(id); }
+    bool metadataConsistent() const
+    {
+        return mgr ? mgr->checkInvariants() && active == mgr->snapshot().token_reservation_count
+                   : fixed->checkInvariants() && active == fixed->snapshot().token_reservation_count;
+    }
+    // A block table's structure, checked against the page size of its pool.
+    bool tableWellFormed(BlockTable const& t) const
+    {
+        return fixed ? t.checkInvariants(fixed->tokensPerPage()) : t.checkInvariants();
     }
 
     bool consumeFailure(CudaFailurePoint point)
@@ -269,7 +342,7 @@ public:
         if (!lease.ok()) {
             return lease;
         }
-        KvCacheError const committed = st_->mgr.commitTokenReservation(reservation_);
+        KvCacheError const committed = st_->commit(reservation_);
         if (committed != KvCacheError::None) {
             return mapMetadata(committed);
         }
@@ -291,7 +364,7 @@ public:
         static_cast<void>(complete());
         std::lock_guard<std::mutex> lock(st_->mutex);
         static_cast<void>(releaseLeaseLocked());
-        static_cast<void>(st_->mgr.rollbackTokenReservation(reservation_));
+        static_cast<void>(st_->rollback(reservation_));
         if (st_->active != 0) {
             --st_->active;
         }
@@ -430,7 +503,7 @@ private:
         if (lease_ == kInvalidPageLeaseId) {
             return {};
         }
-        KvCacheError const released = st_->mgr.releasePageLease(lease_);
+        KvCacheError const released = st_->mgr->releasePageLease(lease_);
         if (released == KvCacheError::None) {
             lease_ = kInvalidPageLeaseId;
         }
@@ -572,7 +645,7 @@ class CudaBackend final : public EngineKvBackend {
 public:
     explicit CudaBackend(std::shared_ptr<State> st) : st_(std::move(st)) {}
 
-    EngineKvBackendKind kind() const noexcept override { return EngineKvBackendKind::Heterogeneous; }
+    EngineKvBackendKind kind() const noexcept override { return st_->kind; }
     EngineKvConfig config() const noexcept override { return st_->config; }
 
     EngineKvStatus createRequest(RequestId id) override
@@ -581,7 +654,7 @@ public:
         if (!st_->config.valid() || !st_->storage.status.ok()) {
             return {EngineKvError::InvalidState};
         }
-        KvCacheError const e = st_->mgr.createRequest(id);
+        KvCacheError const e = st_->create(id);
         if (e == KvCacheError::None) {
             st_->committed_lengths.emplace(id, 0);
         }
@@ -596,7 +669,7 @@ public:
             return {EngineKvError::RequestNotFound};
         }
         std::uint32_t const length = src->second;
-        KvCacheError const e = st_->mgr.forkRequest(source, child);
+        KvCacheError const e = st_->fork(source, child);
         if (e == KvCacheError::None) {
             st_->committed_lengths.emplace(child, length);
         }
@@ -606,7 +679,7 @@ public:
     EngineKvStatus releaseRequest(RequestId id) override
     {
         std::lock_guard<std::mutex> lock(st_->mutex);
-        KvCacheError const e = st_->mgr.releaseRequest(id);
+        KvCacheError const e = st_->release(id);
         if (e == KvCacheError::None) {
             st_->committed_lengths.erase(id);
         }
@@ -626,23 +699,30 @@ public:
             result.status = {EngineKvError::RequestNotFound};
             return result;
         }
-        TokenReservationResult reservation =
-            st_->mgr.reserveToken(request.request_id, request.expected_committed_tokens);
+        TokenReservationResult reservation = st_->reserve(request.request_id, request.expected_committed_tokens);
         if (!reservation.ok()) {
             result.status = mapMetadata(reservation.error);
             return result;
         }
-        PageLeaseAcquireResult const lease =
-            st_->mgr.acquireTokenReservationLease(reservation.reservation_id);
-        if (!lease.ok()) {
-            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
-            result.status = mapMetadata(lease.error);
-            return result;
+        // The two-pool runtime pins the reservation's pages with a lease; the
+        // fixed-page runtime has none (its pages cannot be promoted away, and
+        // its device work is waited for under the backend lock, as in the
+        // reference's FixedCudaKvCache).
+        PageLeaseAcquireResult lease;
+        if (st_->mgr) {
+            lease = st_->mgr->acquireTokenReservationLease(reservation.reservation_id);
+            if (!lease.ok()) {
+                static_cast<void>(st_->rollback(reservation.reservation_id));
+                result.status = mapMetadata(lease.error);
+                return result;
+            }
         }
         CudaStatus const begun = beginChecks(reservation);
         if (!begun.ok()) {
-            static_cast<void>(st_->mgr.releasePageLease(lease.lease_id));
-            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
+            if (st_->mgr) {
+                static_cast<void>(st_->mgr->releasePageLease(lease.lease_id));
+            }
+            static_cast<void>(st_->rollback(reservation.reservation_id));
             result.status = mapCuda(begun);
             return result;
         }
@@ -652,8 +732,10 @@ public:
                 lease.lease_id, std::move(reservation.before), std::move(reservation.reserved),
                 request.stream);
         } catch (...) {
-            static_cast<void>(st_->mgr.releasePageLease(lease.lease_id));
-            static_cast<void>(st_->mgr.rollbackTokenReservation(reservation.reservation_id));
+            if (st_->mgr) {
+                static_cast<void>(st_->mgr->releasePageLease(lease.lease_id));
+            }
+            static_cast<void>(st_->rollback(reservation.reservation_id));
             result.status = {EngineKvError::ResourceExhausted};
             return result;
         }
@@ -683,7 +765,17 @@ public:
         r.batched_attention_submissions = st_->batched_submissions.load(std::memory_order_relaxed);
         r.batched_attention_lanes = st_->batched_lanes.load(std::memory_order_relaxed);
         r.storage_reserved_bytes = st_->storage.micro_bytes + st_->storage.extent_bytes;
-        KvCacheManagerSnapshot const m = st_->mgr.snapshot();
+        if (st_->fixed) {
+            FixedPageManagerSnapshot const f = st_->fixed->snapshot();
+            r.primary_page_tokens = st_->fixed->tokensPerPage();
+            r.secondary_page_tokens = 0;
+            r.primary_page_capacity = f.pool.total_slots;
+            r.allocated_primary_pages = f.pool.allocated_slots;
+            r.successful_primary_allocations = f.pool.successful_allocations;
+            r.failed_primary_allocations = f.pool.failed_allocations;
+            return r;
+        }
+        KvCacheManagerSnapshot const m = st_->mgr->snapshot();
         r.primary_page_tokens = kMicroPageTokenCapacity;
         r.secondary_page_tokens = kExtentPageTokenCapacity;
         r.primary_page_capacity = m.micro_pool.total_slots;
@@ -700,8 +792,7 @@ public:
     bool checkInvariants() const override
     {
         std::lock_guard<std::mutex> lock(st_->mutex);
-        return st_->config.valid() && st_->storage.status.ok() && st_->mgr.checkInvariants()
-            && st_->active == st_->mgr.snapshot().token_reservation_count;
+        return st_->config.valid() && st_->storage.status.ok() && st_->metadataConsistent();
     }
 
     State* state() const noexcept { return st_.get(); }
@@ -715,7 +806,7 @@ private:
             return st_->storage.status;
         }
         auto valid = [this](BlockTable const& t) {
-            if (!t.checkInvariants()) {
+            if (!st_->tableWellFormed(t)) {
                 return false;
             }
             for (MappingEntry const& e : t.entries()) {
@@ -757,6 +848,20 @@ std::unique_ptr<EngineKvBackend> createHeterogeneousCudaEngineKvBackend(
     }
 }
 
+std::unique_ptr<EngineKvBackend> createFixedCudaEngineKvBackend(
+    EngineKvConfig config, std::uint16_t tokens_per_page, std::uint32_t page_capacity)
+{
+    if (!config.valid() || tokens_per_page == 0 || page_capacity == 0) {
+        return nullptr;
+    }
+    try {
+        return std::make_unique<CudaBackend>(
+            std::make_shared<State>(config, tokens_per_page, page_capacity, true));
+    } catch (...) {
+        return nullptr;
+    }
+}
+
 bool injectCudaEngineFailureOnce(EngineKvBackend& backend, CudaFailurePoint point) noexcept
 {
     auto* b = dynamic_cast<CudaBackend*>(&backend);
@@ -792,7 +897,7 @@ bool cudaBackendTable(EngineKvBackend const& backend, RequestId id, BlockTable& 
     if (b == nullptr) {
         return false;
     }
-    std::optional<BlockTable> t = b->state()->mgr.blockTable(id);
+    std::optional<BlockTable> t = b->state()->table(id);
     if (!t) {
         return false;
     }
@@ -812,7 +917,7 @@ EngineKvStatus cudaBackendAppend(EngineKvBackend& backend, RequestId id, std::ui
     if (length == st->committed_lengths.end()) {
         return {EngineKvError::RequestNotFound};
     }
-    KvCacheError const e = st->mgr.append(id, n);
+    KvCacheError const e = st->append(id, n);
     if (e == KvCacheError::None) {
         length->second += n;
     }
@@ -826,7 +931,7 @@ EngineKvStatus cudaBackendSeal(EngineKvBackend& backend, RequestId id)
         return {EngineKvError::InvalidArgument};
     }
     std::lock_guard<std::mutex> lock(b->state()->mutex);
-    return mapMetadata(b->state()->mgr.sealTail(id));
+    return mapMetadata(b->state()->seal(id));
 }
 
 EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::uint32_t begin,
@@ -837,17 +942,20 @@ EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::u
         return {EngineKvError::InvalidArgument};
     }
     State* st = b->state();
+    if (!st->mgr) {
+        return {EngineKvError::InvalidArgument};  // fixed pages have no extent pool
+    }
     PromotionPrepareResult prepared;
     PageLeaseAcquireResult lease;
     {
         std::lock_guard<std::mutex> lock(st->mutex);
-        prepared = st->mgr.preparePromotion(id, begin);
+        prepared = st->mgr->preparePromotion(id, begin);
         if (!prepared.ok()) {
             return mapMetadata(prepared.error);
         }
-        lease = st->mgr.acquirePromotionIoLease(prepared.promotion_id);
+        lease = st->mgr->acquirePromotionIoLease(prepared.promotion_id);
         if (!lease.ok()) {
-            static_cast<void>(st->mgr.rollbackPromotion(prepared.promotion_id));
+            static_cast<void>(st->mgr->rollbackPromotion(prepared.promotion_id));
             return mapMetadata(lease.error);
         }
     }
@@ -861,12 +969,12 @@ EngineKvStatus cudaBackendPromote(EngineKvBackend& backend, RequestId id, std::u
         rc = static_cast<int>(cudaStreamSynchronize(s));
     }
     std::lock_guard<std::mutex> lock(st->mutex);
-    static_cast<void>(st->mgr.releasePageLease(lease.lease_id));
+    static_cast<void>(st->mgr->releasePageLease(lease.lease_id));
     if (rc != 0) {
-        static_cast<void>(st->mgr.rollbackPromotion(prepared.promotion_id));
+        static_cast<void>(st->mgr->rollbackPromotion(prepared.promotion_id));
         return {EngineKvError::ExecutionFailed};
     }
-    return mapMetadata(st->mgr.commitPromotion(prepared.promotion_id));
+    return mapMetadata(st->mgr->commitPromotion(prepared.promotion_id));
 }
 
 EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id, void* device_output,
@@ -880,13 +988,26 @@ EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id, void* d
     std::vector<kk_page_desc> descs;
     std::uint32_t tokens = 0;
     PageLeaseAcquireResult lease;
+    // The fixed-page runtime has no leases: its gather runs under the
+    // backend lock, start to finish (the reference's FixedCudaKvCache waits
+    // for its device work inside the lock).
+    std::unique_lock<std::mutex> fixed_lock(st->mutex, std::defer_lock);
+    if (!st->mgr) {
+        fixed_lock.lock();
+    }
     {
-        std::lock_guard<std::mutex> lock(st->mutex);
-        lease = st->mgr.acquireRequestReadLease(id);
-        if (!lease.ok()) {
-            return mapMetadata(lease.error);
+        std::unique_lock<std::mutex> lock(st->mutex, std::defer_lock);
+        if (st->mgr) {
+            lock.lock();
+            lease = st->mgr->acquireRequestReadLease(id);
+            if (!lease.ok()) {
+                return mapMetadata(lease.error);
+            }
         }
-        std::optional<BlockTable> const table = st->mgr.blockTable(id);
+        std::optional<BlockTable> const table = st->table(id);
+        if (!table && !st->mgr) {
+            return {EngineKvError::RequestNotFound};
+        }
         if (table) {
             tokens = table->tokenCount();
             for (MappingEntry const& e : table->entries()) {
@@ -913,8 +1034,10 @@ EngineKvStatus cudaBackendGather(EngineKvBackend& backend, RequestId id, void* d
             rc = static_cast<int>(cudaStreamSynchronize(s));
         }
     }
-    std::lock_guard<std::mutex> lock(st->mutex);
-    static_cast<void>(st->mgr.releasePageLease(lease.lease_id));
+    if (st->mgr) {
+        std::lock_guard<std::mutex> lock(st->mutex);
+        static_cast<void>(st->mgr->releasePageLease(lease.lease_id));
+    }
     if (descs.empty()) {
         return {EngineKvError::InvalidArgument};  // nothing committed to gather
     }
@@ -931,6 +1054,10 @@ std::uint32_t promoteWave(EngineKvBackend& backend,
 std::uint32_t cudaBackendPromoteMany(EngineKvBackend& backend,
     std::vector<std::pair<RequestId, std::uint32_t>> const& runs, CudaStream stream)
 {
+    auto* b = dynamic_cast<CudaBackend*>(&backend);
+    if (b == nullptr || !b->state()->mgr) {
+        return 0;  // only the two-pool runtime promotes
+    }
     // A request with a prepared promotion holds a reservation, so a second
     // run of the same request cannot be prepared until the first commits:
     // promote in waves holding at most one run per request, in run order.
@@ -970,13 +1097,13 @@ std::uint32_t promoteWave(EngineKvBackend& backend,
         std::lock_guard<std::mutex> lock(st->mutex);
         for (auto const& run : runs) {
             Pending p;
-            p.prepared = st->mgr.preparePromotion(run.first, run.second);
+            p.prepared = st->mgr->preparePromotion(run.first, run.second);
             if (!p.prepared.ok()) {
                 continue;
             }
-            p.lease = st->mgr.acquirePromotionIoLease(p.prepared.promotion_id);
+            p.lease = st->mgr->acquirePromotionIoLease(p.prepared.promotion_id);
             if (!p.lease.ok()) {
-                static_cast<void>(st->mgr.rollbackPromotion(p.prepared.promotion_id));
+                static_cast<void>(st->mgr->rollbackPromotion(p.prepared.promotion_id));
                 continue;
             }
             pending.push_back(p);
@@ -1002,10 +1129,10 @@ std::uint32_t promoteWave(EngineKvBackend& backend,
     std::uint32_t committed = 0;
     std::lock_guard<std::mutex> lock(st->mutex);
     for (Pending const& p : pending) {
-        static_cast<void>(st->mgr.releasePageLease(p.lease.lease_id));
+        static_cast<void>(st->mgr->releasePageLease(p.lease.lease_id));
         if (rc != 0) {
-            static_cast<void>(st->mgr.rollbackPromotion(p.prepared.promotion_id));
-        } else if (st->mgr.commitPromotion(p.prepared.promotion_id) == KvCacheError::None) {
+            static_cast<void>(st->mgr->rollbackPromotion(p.prepared.promotion_id));
+        } else if (st->mgr->commitPromotion(p.prepared.promotion_id) == KvCacheError::None) {
             ++committed;
         }
     }

@@ -52,6 +52,15 @@ enum class CudaFailurePoint : std::uint8_t { Submission, Completion };
 [[nodiscard]] std::unique_ptr<EngineKvBackend> createHeterogeneousCudaEngineKvBackend(
     EngineKvConfig config, std::uint32_t micro_page_capacity, std::uint32_t extent_page_capacity);
 
+// Fixed-page backend behind the same SPI (reference createFixedCudaEngineKvBackend,
+// include/kim-kv/cuda/cuda_engine_kv_backend.h:19-22, src/cuda/engine/backend.cpp:579-598):
+// FixedPageManager metadata, one device pool of page_capacity pages of
+// tokens_per_page tokens (8, 16, 32 or 64; the kernels read the page size from
+// kk_kv_pools::micro_page_tokens). Fork, partial-tail copy-on-write, rollback
+// and the fused decode step work as for the two-pool backend; there is no
+// promotion and there are no page leases.
+[[nodiscard]] std::unique_ptr<EngineKvBackend> createFixedCudaEngineKvBackend(
+    EngineKvConfig config, std::uint16_t tokens_per_page, std::uint32_t page_capacity);
 [[nodiscard]] bool injectCudaEngineFailureOnce(EngineKvBackend& backend, CudaFailurePoint point) noexcept;
 
 // ---- library-internal hooks used by the CUDA model runner ---------------------

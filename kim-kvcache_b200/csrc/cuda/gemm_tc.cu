@@ -92,6 +92,7 @@ struct EpiArgs {
     std::uint64_t extent_page;
     std::uint32_t micro_slots;
     std::uint32_t extent_slots;
+    std::uint32_t micro_cap;     // tokens per micro page
     std::uint32_t kv_row;        // kv_heads * head_dim
     std::uint32_t layer;
     std::uint32_t q_rows;
@@ -609,7 +610,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             } else {
                 kk_kv_slot const sl = slot_rec;
                 bool const micro = sl.kind == 0;
-                std::uint32_t const cap = micro ? 8u : 64u;
+                std::uint32_t const cap = micro ? e.micro_cap : 64u;
                 if (sl.active && sl.page_token < cap
                     && (micro ? sl.slot < e.micro_slots : sl.slot < e.extent_slots)) {
                     __half* page = micro ? e.micro + std::uint64_t(sl.slot) * e.micro_page
@@ -893,7 +894,7 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
     }
     if (d->epilogue == KK_EPI_QKV_ROPE) {
         kk_kv_pools const& p = d->pools;
-        if (d->head_dim != 64 || p.head_dim != 64 || d->positions == nullptr
+        if (d->head_dim != 64 || p.head_dim != 64 || d->positions == nullptr || !microPageTokensValid(p)
             || d->slots == nullptr || d->q_rows % 64 != 0 || d->kv_rows % 64 != 0
             || d->kv_rows != p.kv_heads * p.head_dim || d->layer >= p.layers
             || d->M != d->q_rows + 2 * d->kv_rows || !(d->rope_theta > 0.f)) {
@@ -904,7 +905,8 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
         e.micro = static_cast<__half*>(p.micro);
         e.extent = static_cast<__half*>(p.extent);
         e.kv_row = p.kv_heads * p.head_dim;
-        e.micro_page = std::uint64_t(p.layers) * 2u * 8u * e.kv_row;
+        e.micro_cap = microPageTokens(p);
+        e.micro_page = std::uint64_t(p.layers) * 2u * e.micro_cap * e.kv_row;
         e.extent_page = std::uint64_t(p.layers) * 2u * 64u * e.kv_row;
         e.micro_slots = p.micro == nullptr ? 0 : p.micro_capacity;
         e.extent_slots = p.extent == nullptr ? 0 : p.extent_capacity;

@@ -13,6 +13,18 @@
 
 namespace kk {
 
+// Tokens per page of a pool descriptor's micro pool (0 means 8), and whether
+// the descriptor names a supported size (8, or 16/32/64 for a fixed-page pool).
+inline std::uint32_t microPageTokens(kk_kv_pools const& p) noexcept
+{
+    return p.micro_page_tokens == 0 ? 8u : p.micro_page_tokens;
+}
+inline bool microPageTokensValid(kk_kv_pools const& p) noexcept
+{
+    std::uint32_t const t = microPageTokens(p);
+    return t == 8u || t == 16u || t == 32u || t == 64u;
+}
+
 // kk_paged_decode_attention with the item count in device memory; items
 // beyond *num_items (<= max_items) are ignored. The grid is sized for max_items.
 int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,

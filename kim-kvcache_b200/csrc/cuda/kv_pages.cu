@@ -27,6 +27,7 @@ struct PoolView {
     std::uint32_t extent_slots;
     std::uint32_t row;         // kv_heads * head_dim elements per token per K|V
     std::uint32_t layers;
+    std::uint32_t micro_cap;   // tokens per micro page
 };
 
 PoolView view(kk_kv_pools const& p)
@@ -35,7 +36,8 @@ PoolView view(kk_kv_pools const& p)
     v.micro = static_cast<__half*>(p.micro);
     v.extent = static_cast<__half*>(p.extent);
     v.row = p.kv_heads * p.head_dim;
-    v.micro_page = std::uint64_t(p.layers) * 2u * 8u * v.row;
+    v.micro_cap = microPageTokens(p);
+    v.micro_page = std::uint64_t(p.layers) * 2u * v.micro_cap * v.row;
     v.extent_page = std::uint64_t(p.layers) * 2u * 64u * v.row;
     v.micro_slots = p.micro == nullptr ? 0 : p.micro_capacity;
     v.extent_slots = p.extent == nullptr ? 0 : p.extent_capacity;
@@ -52,7 +54,7 @@ __device__ __forceinline__ __half* block_of(PoolView const& v, std::uint32_t kin
         atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
         return nullptr;
     }
-    std::uint32_t const cap = micro ? 8u : 64u;
+    std::uint32_t const cap = micro ? v.micro_cap : 64u;
     __half* page = micro ? v.micro + std::uint64_t(slot) * v.micro_page
                          : v.extent + std::uint64_t(slot) * v.extent_page;
     return page + (std::uint64_t(layer) * 2u + component) * cap * v.row;
@@ -70,7 +72,7 @@ __global__ void kv_write_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_slo
     if (!s.active) {
         return;
     }
-    std::uint32_t const cap = s.kind == 0 ? 8u : 64u;
+    std::uint32_t const cap = s.kind == 0 ? v.micro_cap : 64u;
     if (s.page_token >= cap) {
         atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
         return;
@@ -98,8 +100,8 @@ __global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy
     kk_kv_copy const c = copies[blockIdx.x];
     std::uint32_t const layer = layer_begin + blockIdx.y;
     std::uint32_t const component = blockIdx.z;
-    std::uint32_t const src_cap = c.src_kind == 0 ? 8u : 64u;
-    std::uint32_t const dst_cap = c.dst_kind == 0 ? 8u : 64u;
+    std::uint32_t const src_cap = c.src_kind == 0 ? v.micro_cap : 64u;
+    std::uint32_t const dst_cap = c.dst_kind == 0 ? v.micro_cap : 64u;
     if (c.tokens > src_cap || c.tokens > dst_cap) {
         atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
         return;
@@ -153,7 +155,7 @@ __global__ void kv_gather_kernel(PoolView v, kk_page_desc const* descs, std::uin
     std::uint32_t const layer = blockIdx.y / 2u;
     std::uint32_t const component = blockIdx.y % 2u;
     bool const micro = d.kind == 0;
-    std::uint32_t const cap = micro ? 8u : 64u;
+    std::uint32_t const cap = micro ? v.micro_cap : 64u;
     std::uint32_t const begin = d.logical_token_begin;
     std::uint32_t const end = begin + d.valid_tokens;
     __half* page = block_of(v, micro ? 0 : 1, d.slot, layer, component);
@@ -209,7 +211,7 @@ __global__ void fill_fp16_kernel(__half* data, std::uint64_t count, std::uint64_
 bool poolsOk(kk_kv_pools const* p)
 {
     return p != nullptr && p->layers != 0 && p->kv_heads != 0 && p->head_dim != 0
-        && (p->kv_heads * p->head_dim) % 8 == 0;
+        && (p->kv_heads * p->head_dim) % 8 == 0 && microPageTokensValid(*p);
 }
 
 } // namespace
@@ -257,7 +259,7 @@ int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots, uint32_
 {
     using namespace kk;
     if (!poolsOk(pools) || micro_slots == nullptr || pools->extent == nullptr
-        || extent_slot >= pools->extent_capacity) {
+        || extent_slot >= pools->extent_capacity || microPageTokens(*pools) != 8u) {
         return KK_EINVAL;
     }
     PromoteSlots src{};
