@@ -229,6 +229,8 @@ def run_ours(args, rank, world, local_rank):
     device_ms = []
     h2d, d2h = C.c_uint64(0), C.c_uint64(0)
     h2d_total = d2h_total = 0
+    host_us = (C.c_float * 5)()
+    host_phases = []
     ev0.record(stream)
     for _ in range(args.steps):
         step()
@@ -236,6 +238,8 @@ def run_ours(args, rank, world, local_rank):
         R["runner_last_transfer_bytes"](runner, C.byref(h2d), C.byref(d2h))
         h2d_total += h2d.value
         d2h_total += d2h.value
+        R["runner_last_host_us"](runner, host_us)
+        host_phases.append(list(host_us))
     ev1.record(stream)
     torch.cuda.synchronize(dev)
     e2e_ms = ev0.elapsed_time(ev1)
@@ -289,6 +293,9 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(tokens_total / (e2e_ms / 1e3), 1), "unit": "tok/s",
                 "h2d_bytes_per_step": round(h2d_total / args.steps), "d2h_bytes_per_step": round(d2h_total / args.steps)},
         "gpu_launches": launches * args.steps,
+        # Median host wall time per step inside the runner's decode call (µs).
+        "host_us_per_step": {name: round(statistics.median(p[i] for p in host_phases), 1)
+                             for i, name in enumerate(("reserve", "record", "launch", "wait", "commit"))},
         "roofline": roof,
         "clocks": clocks,
     }

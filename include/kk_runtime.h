@@ -296,6 +296,11 @@ KK_API uint32_t kkrt_runner_last_launches(void* runner);
  * token (and logits) readback. Returns 0 for a non-CUDA runner. No counterpart
  * in the reference (its per-lane uploads are not aggregated). */
 KK_API int kkrt_runner_last_transfer_bytes(void* runner, uint64_t* h2d, uint64_t* d2h);
+/* Host wall time of the last fused step in microseconds, by phase, into
+ * out[5]: lane reservations, step record (descriptors + work list), upload +
+ * graph launch, wait for the device, commits + auto-promotion. Returns 5, or
+ * 0 for a non-CUDA runner. No counterpart in the reference. */
+KK_API int kkrt_runner_last_host_us(void* runner, float* out);
 /* Detail text of the last failed fused step into out (NUL-terminated); returns its length. */
 KK_API uint32_t kkrt_runner_last_error(void* runner, char* out, uint32_t capacity);
 

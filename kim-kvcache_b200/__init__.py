@@ -486,6 +486,7 @@ RUNTIME_SIGNATURES = {
     "runner_last_step_ms": (_F, [_VP]),
     "runner_last_launches": (_U32, [_VP]),
     "runner_last_transfer_bytes": (_I, [_VP, C.POINTER(_U64), C.POINTER(_U64)]),
+    "runner_last_host_us": (_I, [_VP, C.POINTER(C.c_float)]),
     "runner_last_error": (_U32, [_VP, C.c_char_p, _U32]),
     "sched_create": (_VP, [_VP, _VP, _U32, _U32, _U64, _U32]),
     "sched_destroy": (None, [_VP]),

@@ -8,6 +8,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <new>
@@ -386,6 +387,17 @@ uint32_t kkrt_runner_last_launches(void* r)
 {
     auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
     return runner == nullptr ? 0 : runner->lastStepLaunches();
+}
+
+int kkrt_runner_last_host_us(void* r, float* out)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    if (runner == nullptr || out == nullptr) {
+        return 0;
+    }
+    std::array<float, 5> const us = runner->lastStepHostUs();
+    std::copy(us.begin(), us.end(), out);
+    return 5;
 }
 
 int kkrt_runner_last_transfer_bytes(void* r, uint64_t* h2d, uint64_t* d2h)

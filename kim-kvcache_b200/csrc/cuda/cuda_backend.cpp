@@ -710,7 +710,7 @@ public:
         // reference's FixedCudaKvCache).
         PageLeaseAcquireResult lease;
         if (st_->mgr) {
-            lease = st_->mgr->acquireTokenReservationLease(reservation.reservation_id);
+            lease = st_->mgr->acquireTokenReservationPin(reservation.reservation_id);
             if (!lease.ok()) {
                 static_cast<void>(st_->rollback(reservation.reservation_id));
                 result.status = mapMetadata(lease.error);
@@ -818,8 +818,36 @@ private:
             }
             return true;
         };
+        // `before` is `reserved` less the token just reserved: once `reserved`
+        // passed, every entry the two share is valid, and only the entry
+        // where they differ needs a look (the same verdict as checking
+        // `before` in full, which any other shape falls back to).
+        auto valid_before = [&](BlockTable const& b, BlockTable const& res) {
+            auto const& be = b.entries();
+            auto const& re = res.entries();
+            std::size_t const nb = be.size();
+            if (nb == 0 || (re.size() != nb && re.size() != nb + 1)
+                || !std::equal(be.begin(), be.end() - 1, re.begin())) {
+                return valid(b);
+            }
+            MappingEntry const& last = be.back();
+            if (re.size() == nb + 1 && last == re[nb - 1]) {
+                return true;  // a prefix of a valid table
+            }
+            std::uint16_t const cap = st_->fixed ? st_->fixed->tokensPerPage() : pageTokenCapacity(last.kind);
+            std::uint32_t const slots = last.kind == PageKind::Micro ? st_->storage.pools.micro_capacity
+                                                                     : st_->storage.pools.extent_capacity;
+            if (!last.handle.isStructurallyValid() || last.kind != last.handle.kind || cap == 0
+                || last.valid_tokens == 0 || last.valid_tokens > cap || last.handle.slot >= slots
+                || last.logical_token_begin != (nb > 1 ? be[nb - 2].logicalTokenEnd() : 0u)) {
+                return false;
+            }
+            return std::none_of(be.begin(), be.end() - 1,
+                [&](MappingEntry const& e) { return e.handle == last.handle; });
+        };
         std::uint32_t const kv = st_->config.kv_layout.kv_head_count;
-        if (!valid(r.before) || !valid(r.reserved) || r.reserved.tokenCount() != r.before.tokenCount() + 1
+        if (!valid(r.reserved) || !valid_before(r.before, r.reserved)
+            || r.reserved.tokenCount() != r.before.tokenCount() + 1
             || st_->config.query_head_count < kv || st_->config.query_head_count % kv != 0
             || r.reserved.entries().empty()) {
             return {CudaError::InvalidArgument, 0};

@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <array>
+#include <chrono>
 #include <cmath>
 #include <cstring>
 #include <fstream>
@@ -118,6 +120,9 @@ struct CudaTinyLlamaModelRunner::Impl {
     std::uint32_t last_launches{0};
     std::uint64_t last_h2d{0};
     std::uint64_t last_d2h{0};
+    // Host wall time of the last fused step's phases (microseconds): lane
+    // reservations, step record, upload + launch, wait, commits.
+    std::array<float, 5> last_host_us{};
 
     std::unordered_map<std::uint32_t, BatchPlans> plans;
     std::unordered_map<std::uint32_t, cudaGraphExec_t> graphs;
@@ -179,6 +184,7 @@ std::string CudaTinyLlamaModelRunner::lastError() const { return impl_->last_err
 std::uint32_t CudaTinyLlamaModelRunner::lastStepLaunches() const noexcept { return impl_->last_launches; }
 std::uint64_t CudaTinyLlamaModelRunner::lastStepH2dBytes() const noexcept { return impl_->last_h2d; }
 std::uint64_t CudaTinyLlamaModelRunner::lastStepD2hBytes() const noexcept { return impl_->last_d2h; }
+std::array<float, 5> CudaTinyLlamaModelRunner::lastStepHostUs() const noexcept { return impl_->last_host_us; }
 
 CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t batch, BatchPlans& out)
 {
@@ -410,6 +416,15 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         result.detail = "generation batch is empty or exceeds max batch size";
         return result;
     }
+    using Clock = std::chrono::steady_clock;
+    Clock::time_point const t_begin = Clock::now();
+    Clock::time_point t_mark = t_begin;
+    auto phase = [&](std::size_t i) {
+        Clock::time_point const now = Clock::now();
+        im.last_host_us[i] = std::chrono::duration<float, std::micro>(now - t_mark).count();
+        t_mark = now;
+    };
+    im.last_host_us = {};
     result.steps.resize(items.size());
     std::vector<std::size_t> lane_index;
     std::vector<TokenTransaction> txns;
@@ -442,6 +457,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         return result;
     }
 
+    phase(0);
     // Step inputs into the pinned mirror.
     auto* tokens = im.stepHost<std::uint32_t>(im.off_tokens);
     auto* positions = im.stepHost<std::uint32_t>(im.off_positions);
@@ -500,7 +516,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
     counts[0] = n_items;
     counts[1] = n_copies;
     std::size_t const bytes = im.off_descs + std::size_t(n_descs) * sizeof(kk_page_desc);
-    std::string fail_detail;
+    phase(1);
     cudaError_t e = cudaMemcpyAsync(im.step_dev, im.step_host, bytes, cudaMemcpyHostToDevice, im.stream);
     im.last_h2d = bytes;
     im.last_d2h = 0;
@@ -516,6 +532,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
                 cudaMemcpyDeviceToHost, im.stream);
             im.last_d2h += c.vocabulary_size * 4u;
         }
+        phase(2);
         if (e == cudaSuccess) {
             e = cudaStreamSynchronize(im.stream);
         }
@@ -531,6 +548,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         noteStreamCompleted(*im.kv, im.stream);
         cudaEventElapsedTime(&im.last_ms, im.ev_begin, im.ev_end);
     }
+    phase(3);
     std::vector<std::pair<RequestId, std::uint32_t>> promote;
     for (std::uint32_t b = 0; b < B; ++b) {
         std::size_t const i = lane_index[b];
@@ -552,6 +570,7 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
         // fold them into one extent page (skipped when they are shared).
         static_cast<void>(cudaBackendPromoteMany(*im.kv, promote, im.stream));
     }
+    phase(4);
     return result;
 }
 

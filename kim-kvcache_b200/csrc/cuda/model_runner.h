@@ -20,6 +20,7 @@
 #include "../host/generation.h"
 #include "cuda_backend.h"
 
+#include <array>
 #include <cstdint>
 #include <memory>
 #include <string>
@@ -128,6 +129,11 @@ public:
     // device -> host (greedy token ids, plus logits or captures when asked).
     [[nodiscard]] std::uint64_t lastStepH2dBytes() const noexcept;
     [[nodiscard]] std::uint64_t lastStepD2hBytes() const noexcept;
+    // Host wall time of the last fused step, in microseconds, by phase:
+    // [0] lane reservations, [1] step record (descriptors and work list),
+    // [2] upload + graph launch + readback enqueue, [3] wait for the device,
+    // [4] commits and auto-promotion.
+    [[nodiscard]] std::array<float, 5> lastStepHostUs() const noexcept;
     // Turns auto-promotion (CudaModelRunnerOptions::auto_promote) on or off.
     void setAutoPromote(bool enabled) noexcept;
 

@@ -136,6 +136,10 @@ public:
     [[nodiscard]] PageLeaseAcquireResult acquireRequestReadLease(RequestId request_id);
     [[nodiscard]] PageLeaseAcquireResult acquirePromotionIoLease(PromotionId id);
     [[nodiscard]] PageLeaseAcquireResult acquireTokenReservationLease(KvTokenReservationId id);
+    // The same lease, returning only its id (table and handles left empty):
+    // for a caller that already holds the reserved table, as the device
+    // backend does on every token reservation.
+    [[nodiscard]] PageLeaseAcquireResult acquireTokenReservationPin(KvTokenReservationId id);
     [[nodiscard]] KvCacheError releasePageLease(PageLeaseId lease_id);
 
     [[nodiscard]] std::optional<BlockTable> blockTable(RequestId request_id) const;
@@ -212,7 +216,8 @@ private:
         return 0;
     }
 
-    PageLeaseAcquireResult pinPages(std::vector<PageHandle> handles, BlockTable table);
+    PageLeaseAcquireResult pinPages(std::vector<PageHandle> handles, BlockTable const* table);
+    PageLeaseAcquireResult pinTokenReservation(KvTokenReservationId id, bool describe);
     KvCacheError rollbackReservationLocked(KvTokenReservationId id);
     KvCacheError rollbackPromotionLocked(PromotionId id);
     KvCacheError rollbackRequestPromotionsLocked(RequestId request_id);

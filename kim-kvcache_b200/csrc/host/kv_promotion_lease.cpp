@@ -273,7 +273,7 @@ std::optional<PromotionTransactionSnapshot> KvCacheManager::promotionTransaction
         p.logical_token_begin, p.sources, p.target};
 }
 
-PageLeaseAcquireResult KvCacheManager::pinPages(std::vector<PageHandle> handles, BlockTable table)
+PageLeaseAcquireResult KvCacheManager::pinPages(std::vector<PageHandle> handles, BlockTable const* table)
 {
     PageLeaseAcquireResult result;
     for (PageHandle const handle : handles) {
@@ -289,8 +289,10 @@ PageLeaseAcquireResult KvCacheManager::pinPages(std::vector<PageHandle> handles,
         result.error = KvCacheError::InternalInvariantViolation;
         return result;
     }
-    result.table = std::move(table);
-    result.handles = handles;
+    if (table != nullptr) {  // callers that keep only the id skip both copies
+        result.table = *table;
+        result.handles = handles;
+    }
     auto const inserted = leases_.emplace(id, Lease{id, std::move(handles)});
     if (!inserted.second) {
         result.error = KvCacheError::InternalInvariantViolation;
@@ -322,7 +324,7 @@ PageLeaseAcquireResult KvCacheManager::acquireRequestReadLease(RequestId request
     for (MappingEntry const& entry : found->second.entries_) {
         handles.push_back(entry.handle);
     }
-    return pinPages(std::move(handles), found->second);
+    return pinPages(std::move(handles), &found->second);
 }
 
 PageLeaseAcquireResult KvCacheManager::acquirePromotionIoLease(PromotionId id)
@@ -340,10 +342,21 @@ PageLeaseAcquireResult KvCacheManager::acquirePromotionIoLease(PromotionId id)
     }
     std::vector<PageHandle> handles(found->second.sources.begin(), found->second.sources.end());
     handles.push_back(found->second.target);
-    return pinPages(std::move(handles), BlockTable{});
+    BlockTable const none;
+    return pinPages(std::move(handles), &none);
 }
 
 PageLeaseAcquireResult KvCacheManager::acquireTokenReservationLease(KvTokenReservationId id)
+{
+    return pinTokenReservation(id, true);
+}
+
+PageLeaseAcquireResult KvCacheManager::acquireTokenReservationPin(KvTokenReservationId id)
+{
+    return pinTokenReservation(id, false);
+}
+
+PageLeaseAcquireResult KvCacheManager::pinTokenReservation(KvTokenReservationId id, bool describe)
 {
     PageLeaseAcquireResult result;
     if (id == kInvalidKvTokenReservationId) {
@@ -365,7 +378,7 @@ PageLeaseAcquireResult KvCacheManager::acquireTokenReservationLease(KvTokenReser
     if (r.replaced_sealed_tail.isStructurallyValid()) {
         handles.push_back(r.replaced_sealed_tail);  // COW source stays readable
     }
-    return pinPages(std::move(handles), r.candidate);
+    return pinPages(std::move(handles), describe ? &r.candidate : nullptr);
 }
 
 KvCacheError KvCacheManager::releasePageLease(PageLeaseId lease_id)
