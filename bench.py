@@ -34,6 +34,8 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 METRIC = "decode tok/s/GPU TinyLlama-shape c4/c32; paged-attn HBM GB/s vs 8 TB/s"
 SEED = 0x4B564341434845  # the reference benchmark seed (include/kim-kv/benchmark/benchmark.h:123)
@@ -121,7 +123,6 @@ def measured_peaks():
 
 
 def run_ours(args, rank, world, local_rank):
-    import numpy as np
     import torch
 
     kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
@@ -207,15 +208,21 @@ def run_ours(args, rank, world, local_rank):
     out_tok = (C.c_uint32 * B)()
     out_ok = (C.c_uint8 * B)()
 
+    # numpy views of the call's buffers: the caller's per-step bookkeeping
+    # (check every lane, feed the tokens back, advance the positions) is three
+    # vector operations instead of per-lane Python.
+    tokens_v, positions_v = np.ctypeslib.as_array(tokens), np.ctypeslib.as_array(positions)
+    out_tok_v, out_ok_v = np.ctypeslib.as_array(out_tok), np.ctypeslib.as_array(out_ok)
+    forward = R["runner_forward_batch"]
+
     def step():
-        ok = R["runner_forward_batch"](runner, B, ids, tokens, positions, out_tok, out_ok)
-        if not (ok and all(out_ok[i] for i in range(B))):
+        ok = forward(runner, B, ids, tokens, positions, out_tok, out_ok)
+        if not (ok and out_ok_v.all()):
             buf = C.create_string_buffer(512)
             R["runner_last_error"](runner, buf, 512)
             raise RuntimeError(f"decode step failed: {buf.value.decode()}")
-        for i in range(B):
-            tokens[i] = out_tok[i]
-            positions[i] += 1
+        tokens_v[:] = out_tok_v
+        positions_v += 1
 
     for _ in range(args.warmup):
         step()
@@ -399,7 +406,6 @@ def trace_step(kk, step, torch, dev, path):
     launch's first dependency-wait return (medians over CTAs, then over the
     inner layers), the launch's span to its last exit, and the hand-off from
     the previous launch's last exit."""
-    import numpy as np
     lib = kk.load_library()
     if not hasattr(lib, "kk_trace_read_gemm"):
         raise SystemExit("--trace needs the trace build: python kim-kvcache_b200/build.py --trace")

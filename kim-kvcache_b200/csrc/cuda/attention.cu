@@ -637,6 +637,9 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
     bool open = false;
     std::uint64_t pos = 0;
     std::uint32_t next_cut = 1;
+    // Position of the next cut, recomputed only when a cut is placed (the
+    // division stays out of the per-descriptor loop).
+    std::uint64_t next_target = num_parts > 1 ? target(1) : ~std::uint64_t{0};
     auto flush = [&]() {
         if (open && count - 1 < max_items) {
             items[count - 1] = cur;
@@ -660,14 +663,14 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
             std::uint64_t const c = descs[e].valid_tokens;
             bool cut_before = false;
             bool cut_after = false;
-            while (next_cut < num_parts && target(next_cut) < pos + c) {
-                std::uint64_t const t = target(next_cut);
-                if (2 * t < 2 * pos + c) {
+            while (next_cut < num_parts && next_target < pos + c) {
+                if (2 * next_target < 2 * pos + c) {
                     cut_before = true;
                 } else {
                     cut_after = true;
                 }
                 ++next_cut;
+                next_target = next_cut < num_parts ? target(next_cut) : ~std::uint64_t{0};
             }
             if (cut_before) {
                 flush();
