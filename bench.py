@@ -222,7 +222,7 @@ def run_ours(args, rank, world, local_rank):
             R["runner_last_error"](runner, buf, 512)
             raise RuntimeError(f"decode step failed: {buf.value.decode()}")
         tokens_v[:] = out_tok_v
-        positions_v += 1
+        positions_v[:] += 1
 
     for _ in range(args.warmup):
         step()

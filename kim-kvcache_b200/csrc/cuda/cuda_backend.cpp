@@ -174,6 +174,9 @@ struct State {
     std::mutex fault_mutex;
     bool fail_submission{false};
     bool fail_completion{false};
+    // Set while either injected failure is armed, so the per-lane checks of
+    // every transaction skip the mutex when none is.
+    std::atomic<bool> failure_armed{false};
 
     std::atomic<std::uint64_t> submit_seq{0};
     std::mutex sync_mutex;
@@ -231,10 +234,14 @@ struct State {
 
     bool consumeFailure(CudaFailurePoint point)
     {
+        if (!failure_armed.load(std::memory_order_acquire)) {
+            return false;
+        }
         std::lock_guard<std::mutex> lock(fault_mutex);
         bool& flag = point == CudaFailurePoint::Submission ? fail_submission : fail_completion;
         bool const was = flag;
         flag = false;
+        failure_armed.store(fail_submission || fail_completion, std::memory_order_release);
         return was;
     }
 
@@ -899,6 +906,7 @@ bool injectCudaEngineFailureOnce(EngineKvBackend& backend, CudaFailurePoint poin
     std::lock_guard<std::mutex> lock(b->state()->fault_mutex);
     (point == CudaFailurePoint::Submission ? b->state()->fail_submission
                                            : b->state()->fail_completion) = true;
+    b->state()->failure_armed.store(true, std::memory_order_release);
     return true;
 }
 
