@@ -49,18 +49,6 @@ def load_pkg(name, path):
     return mod
 
 
-def workload(config: str, rank: int):
-    rng = random.Random(SEED + 7919 * rank)
-    if config == "c2":
-        return dict(name="c2: TinyLlama-shape greedy decode, batch 1, prompt 6 (+32 new)",
-                    batch=1, contexts=[6])
-    if config == "c5":
-        return dict(name="c5: TinyLlama-shape decode replicas, 64 requests/GPU, ctx~U[64,1024]",
-                    batch=64, contexts=[rng.randint(64, 1024) for _ in range(64)])
-    return dict(name="c4: TinyLlama-shape decode, 32 lanes/GPU, ctx~U[1024,4096] extent+micro pages",
-                batch=32, contexts=[rng.randint(1024, 4096) for _ in range(32)])
-
-
 def gpu_id(torch, dev) -> str:
     """nvidia-smi --id of this process's GPU (UUID: immune to CUDA_VISIBLE_DEVICES)."""
     try:
@@ -135,7 +123,7 @@ def run_ours(args, rank, world, local_rank):
         dist = dist_mod
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
 
-    wl = workload(args.config, rank)
+    wl = synth.decode_workload(args.config)
     B = wl["batch"]
     contexts = wl["contexts"]
     cfg = dict(synth.TINYLLAMA)
@@ -171,26 +159,14 @@ def run_ours(args, rank, world, local_rank):
     else:
         # Room for every 64-token run that auto-promotion folds during the run:
         # with too few extents, promotion fails and the tails grow as micro pages.
-        extent_cap = sum((c + args.steps + args.warmup + 2) // 64 for c in contexts) + B
-        micro_cap = B * 16 + total_tokens // 8 + 64
+        micro_cap, extent_cap = synth.pool_capacities(contexts, args.steps + args.warmup + 3)
         backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
         assert backend, "backend allocation failed"
         pools = kk.KvPools()
         assert R["backend_pools"](backend, C.byref(pools))
-
-        # Prefix state: append ctx tokens, seal, promote every full 64-token run.
-        for i, ctx in enumerate(contexts):
-            rid = i + 1
-            assert R["backend_create_request"](backend, rid) == 0
-            assert R["backend_append"](backend, rid, ctx) == 0
-            R["backend_seal"](backend, rid)
-            for begin in range(0, (ctx // 64) * 64, 64):
-                assert R["backend_promote"](backend, rid, begin, sptr) == 0
-        # Synthetic KV contents for every page (the prefix K/V of a real prefill).
-        micro_elems = micro_cap * L * 2 * 8 * row
-        extent_elems = extent_cap * L * 2 * 64 * row
-        assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, SEED + rank, 0.35, sptr) == 0
-        assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, SEED + 1 + rank, 0.35, sptr) == 0
+        # Prefix state: append ctx tokens, seal, promote every full 64-token
+        # run, then seeded KV contents in every page.
+        synth.build_decode_prefixes(R, K, backend, pools, contexts, cfg, SEED + 2 * rank, sptr)
     torch.cuda.synchronize(dev)
 
     status = C.c_int(0)
@@ -262,20 +238,34 @@ def run_ours(args, rank, world, local_rank):
     roof = attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, stream, sptr)
 
     t = torch.tensor([dev_ms, e2e_ms], device=dev)
+    per_rank_ms = [dev_ms]
     if dist is not None:
+        gathered = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(gathered, t)
+        per_rank_ms = [round(float(g[0]) / args.steps, 4) for g in gathered]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dist.barrier()
+        dist.destroy_process_group()
     dev_ms, e2e_ms = float(t[0]), float(t[1])
+    if rank != 0:
+        R["runner_destroy"](runner)
+        R["backend_destroy"](backend)
+        return None
+    # After timing (untimed): one more decode step of every lane, checked lane
+    # by lane against the CPU oracle fed the GPU's own K/V; the oracle's pass
+    # over the same lanes is the CPU baseline at N = 1.
+    check = None
+    if not args.no_cpu_baseline and not fixed:
+        check = oracle_check(kk, R, runner, backend, cfg, B, ids, tokens_v, positions_v, synth,
+                             sptr, torch)
     R["runner_destroy"](runner)
     R["backend_destroy"](backend)
-    if dist is not None:
-        dist.destroy_process_group()
-    if rank != 0:
-        return None
     tokens_total = B * args.steps * world
     line = {
         "metric": METRIC,
         "value": round(tokens_total / (dev_ms / 1e3), 1),
+        "value_scope": f"whole job: decode tok/s summed over {world} GPU(s)",
+        "per_gpu_value": round(B * args.steps / (dev_ms / 1e3), 1),
         "unit": "tok/s",
         "n_gpus": world,
         "steps": args.steps,
@@ -306,8 +296,12 @@ def run_ours(args, rank, world, local_rank):
         "roofline": roof,
         "clocks": clocks,
     }
-    if not args.no_cpu_baseline and world == 1:
-        line["cpu_baseline"] = cpu_baseline(kk, synth, cfg, contexts, manifest, args)
+    if world > 1:
+        line["per_rank_ms_per_step"] = per_rank_ms
+    if check is not None:
+        line["parity"] = check["parity"]
+        if world == 1:
+            line["cpu_baseline"] = check["cpu_baseline"]
     return line
 
 
@@ -469,73 +463,87 @@ def cpu_model(synth, cfg, threads):
     import kk_oracle_py as ko
     archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
     _, _, weights = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31), keep_weights=True)
-    return ko, ko.Model(cfg, weights, threads=threads)
+    model = ko.Model(cfg, weights, threads=threads)
+    del weights
+    return ko, model
 
 
-def cpu_decode_sample(ko, model, cfg, contexts, lanes, steps):
-    import numpy as np
-    L, row = cfg["layers"], cfg["kv_heads"] * cfg["head_dim"]
-    rng = np.random.default_rng(5)
-    for b in range(lanes):
-        model.create(b + 1)
-        ctx = contexts[b]
-        k = (rng.uniform(-0.35, 0.35, (ctx, L, row))).astype(np.float16).view(np.uint16)
-        v = (rng.uniform(-0.35, 0.35, (ctx, L, row))).astype(np.float16).view(np.uint16)
-        model.append_kv(b + 1, k, v)
-    toks = [3 + b for b in range(lanes)]
-    pos = list(contexts[:lanes])
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        greedy, _, _ = model.forward(list(range(1, lanes + 1)), toks, pos, want_logits=False,
-                                     want_hidden=False)
-        toks = [int(x) for x in greedy]
-        pos = [p + 1 for p in pos]
-    dt = time.perf_counter() - t0
-    return lanes * steps / dt, dt
-
-
-def cpu_baseline(kk, synth, cfg, contexts, manifest, args):
+def oracle_check(kk, R, runner, backend, cfg, B, ids, tokens_v, positions_v, synth, sptr, torch):
+    """One decode step of all B lanes through the batched-logits call,
+    compared with the CPU oracle (the restatement of the reference decoder)
+    that attends over the K/V the GPU holds for every lane (read back with the
+    backend's gather). Returns the parity record (logits within 2e-2 on every
+    lane, greedy tokens identical wherever the top-2 gap exceeds 2e-2) and
+    the oracle's time for the same B-lane step as the CPU baseline."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import lane_parity as lp
     threads = os.cpu_count() or 1
-    ko, model = cpu_model(synth, cfg, threads)
-    lanes, steps = min(4, len(contexts)), 1
-    rate, dt = cpu_decode_sample(ko, model, cfg, contexts, lanes, steps)
+    _, model = cpu_model(synth, cfg, threads)
+    contexts_now = [int(x) for x in positions_v]
+    toks_in = [int(x) for x in tokens_v]
+    parity = lp.LaneParity(model, R, backend, list(ids), contexts_now, cfg, sptr, torch)
+    got, ok, logits = lp.forward_with_logits(R, runner, list(ids), toks_in, contexts_now, cfg["vocab"])
+    assert all(ok), "a lane of the checked step failed"
+    t0 = time.perf_counter()
+    parity.step(toks_in, contexts_now, got, logits)
+    dt = time.perf_counter() - t0
+    rec = parity.record()
+    rec["lanes"] = len(rec["lanes"])
+    parity.close()
     model.close()
-    return {"value": round(rate, 4), "unit": "tok/s", "cores": threads, "kind": "port",
-            "sample": f"{lanes} lanes x {steps} decode step(s) of the same workload "
-                      f"(contexts {contexts[:lanes]}), C oracle, {dt:.1f} s"}
+    return {"parity": rec,
+            "cpu_baseline": {"value": round(B / dt, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+                             "sample": f"one decode step of all {B} lanes (the GPU arm's lanes and "
+                                       f"contexts, on the K/V the GPU holds), C restatement of the "
+                                       f"reference FP16 decoder, {dt:.1f} s"}}
 
 
 def run_reference(args, rank, world):
+    """The reference arm: the CPU restatement of the reference's FP16 decoder
+    (kind "port"; the reference's own model arithmetic is test-local C++),
+    on all host cores, on the same config as our arm: the same B lanes and
+    per-lane contexts, one decode step of every lane per timed step."""
     if rank != 0:
         return None
     synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
-    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
-    wl = workload(args.config, 0)
+    wl = synth.decode_workload(args.config)
+    B, contexts = wl["batch"], wl["contexts"]
     cfg = dict(synth.TINYLLAMA)
-    cfg["max_positions"] = max(4608, max(wl["contexts"]) + args.steps + args.warmup + 8)
+    cfg["max_positions"] = max(4608, max(contexts) + args.steps + args.warmup + 8)
     threads = os.cpu_count() or 1
-    ko, model = cpu_model(synth, cfg, threads)
-    lanes = min(2, wl["batch"])
-    total_tok, total_t = 0, 0.0
-    for i in range(args.warmup + args.steps):
-        if i == args.warmup:
-            total_tok, total_t = 0, 0.0
-        rate, dt = cpu_decode_sample(ko, model, cfg, wl["contexts"][2 * (i % 2):], lanes, 1)
-        for b in range(lanes):
-            model.release(b + 1)
-        total_tok += lanes
-        total_t += dt
+    _, model = cpu_model(synth, cfg, threads)
+    L, row = cfg["layers"], cfg["kv_heads"] * cfg["head_dim"]
+    rng = np.random.default_rng(5)
+    longest = max(contexts)
+    k = rng.uniform(-0.35, 0.35, (longest, L, row)).astype(np.float16).view(np.uint16)
+    v = rng.uniform(-0.35, 0.35, (longest, L, row)).astype(np.float16).view(np.uint16)
+    for b, ctx in enumerate(contexts):
+        model.create(b + 1)
+        model.append_kv(b + 1, k[:ctx], v[:ctx])
+    del k, v
+    seqs = list(range(1, B + 1))
+    toks = [3 + (7919 * b) % 31997 for b in range(B)]
+    pos = list(contexts)
+    times = []
+    for _ in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        greedy, _, _ = model.forward(seqs, toks, pos, want_logits=False, want_hidden=False)
+        times.append(time.perf_counter() - t0)
+        toks = [int(x) for x in greedy]
+        pos = [p + 1 for p in pos]
     model.close()
-    value = total_tok / total_t
+    total_t = sum(times[args.warmup:])
+    value = B * args.steps / total_t
     return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(total_t / max(args.steps, 1) * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": wl["name"] + f" (bounded sample: {lanes} lanes per step)"},
+            "config": {"workload": wl["name"], "batch": B, "ctx_mean": round(sum(contexts) / B, 1)},
             "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads,
                              "kind": "port",
-                             "sample": f"{lanes} lanes x 1 decode step per timed step, "
-                                       "C restatement of the reference FP16 decoder"},
+                             "sample": f"{args.steps} timed decode steps of all {B} lanes (after "
+                                       f"{args.warmup} warm-up), C restatement of the reference FP16 "
+                                       "decoder on seeded K/V of the workload's contexts"},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -824,6 +832,8 @@ def main():
         args, rank, world, local_rank)
     if line is not None:
         print(json.dumps(line), flush=True)
+        if "parity" in line and not line["parity"]["ok"]:
+            sys.exit("parity gate failed: the checked step disagrees with the CPU oracle")
 
 
 if __name__ == "__main__":

@@ -34,6 +34,10 @@ extern "C" {
 #endif
 
 #define KK_EINVAL 1000
+/* Native error code of a transaction or step that failed because one of its
+ * kernels reported an error (a descriptor outside its pool, a bounded device
+ * wait that ran out) instead of the CUDA runtime. */
+#define KK_EDEVICE 1002
 
 typedef struct kk_kv_pools {
     void* micro;               /* micro_capacity pages of layers*2*T*kv_heads*head_dim fp16,
@@ -154,8 +158,9 @@ KK_KAPI int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer,
  * when a kernel starts. This entry point zeroes them on `stream` before every
  * launch. Nothing else needs initial values.
  *
- * The first call on each device looks up the scratch address; make it
- * before any stream capture. Calls that can overlap on one device (different
+ * The first call on each device (the device that owns `stream`) looks up the
+ * scratch address; make it before any stream capture. Arguments are checked
+ * before anything is queued: a rejected call writes nothing. Calls that can overlap on one device (different
  * streams, or several host threads) share the one scratch array and race:
  * serialize them on one stream, or use kk_paged_decode_attention with a
  * workspace per stream. Other arguments, results and errors are those of
@@ -315,8 +320,21 @@ KK_KAPI uint64_t kk_argmax_workspace_bytes(uint32_t M, uint32_t N);
 KK_KAPI int kk_gemm(const kk_gemm_desc* desc, void* stream);
 
 /* Reads and clears the device-side status words of all kernel modules
- * (synchronises the stream). 0 = no kernel recorded an error. */
+ * (synchronises the stream). 0 = no kernel recorded an error. These words
+ * collect the errors of the entry points above; the runtime's own launches
+ * (kk_runtime.h: the runner's fused step, the backend's per-layer
+ * transactions) report into per-step and per-stream words of their own and
+ * fail the affected transactions at commit. */
 KK_KAPI int kk_device_status(void* stream);
+
+/* Test hook for the bounded waits of K1 (no counterpart in the reference,
+ * whose failure injection is host-side only): from the next launch on, CTA 0
+ * of every TMA attention launch on the current device drops its stage number
+ * `stage` (issues no copy and no arrival for it), so that the consumers'
+ * bounded wait runs out after `wait_limit_ns` and the kernel reports
+ * kErrWaitTimeout and returns. stage 0xFFFFFFFF and wait_limit_ns 0 restore
+ * the defaults (no stage dropped, 2 s). Call it with no kernel in flight. */
+KK_KAPI int kk_debug_attention_fault(uint32_t stage, uint64_t wait_limit_ns);
 
 /* Programmatic dependent launch for subsequent launches on this thread (0/1). */
 KK_KAPI void kk_set_pdl(int enabled);

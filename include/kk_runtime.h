@@ -273,6 +273,13 @@ KK_API void kkrt_runner_destroy(void* runner);
  * Returns 1 when the batch result is well formed. */
 KK_API int kkrt_runner_forward_batch(void* runner, uint32_t n, const uint64_t* request_ids,
     const uint32_t* token_ids, const uint32_t* positions, uint32_t* out_tokens, uint8_t* out_ok);
+/* kkrt_runner_forward_batch that also fills logits [n][vocab] f32 (rows of
+ * failed lanes zero). No counterpart in the reference (its batched path
+ * returns tokens only): the same fused step run outside the captured graph,
+ * for checking every lane against the reference arithmetic. */
+KK_API int kkrt_runner_forward_batch_logits(void* runner, uint32_t n, const uint64_t* request_ids,
+    const uint32_t* token_ids, const uint32_t* positions, uint32_t* out_tokens, uint8_t* out_ok,
+    float* logits);
 /* Fused multi-token prefill (no counterpart in the reference, which feeds a
  * prompt one position per scheduler wave): appends n prompt tokens of one
  * request at positions first_position.. (KvCacheManager::append semantics,

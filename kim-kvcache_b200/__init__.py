@@ -407,6 +407,7 @@ KERNEL_SIGNATURES = {
     "kv_scatter": (_I, [C.POINTER(KvPools), _VP, _U32, _U32, _U32, _VP, _VP]),
     "fill_fp16": (_I, [_VP, _U64, _U64, C.c_float, _VP]),
     "device_status": (_I, [_VP]),
+    "debug_attention_fault": (_I, [_U32, _U64]),
     "set_pdl": (None, [_I]),
     "attention_set_variant": (_I, [_I]),
 }
@@ -480,6 +481,8 @@ RUNTIME_SIGNATURES = {
     "runner_set_auto_promote": (_I, [_VP, _I]),
     "runner_prefill": (_I, [_VP, C.c_uint64, _PU32, _U32, _U32, _PU32]),
     "runner_forward_batch": (_I, [_VP, _U32, _PU64, _PU32, _PU32, _PU32, C.POINTER(C.c_uint8)]),
+    "runner_forward_batch_logits": (_I, [_VP, _U32, _PU64, _PU32, _PU32, _PU32, C.POINTER(C.c_uint8),
+                                         C.POINTER(C.c_float)]),
     "runner_forward_token": (_I, [_VP, _U64, _U32, _U32, _PU32, C.POINTER(C.c_float),
                                   C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), _PU32, _U32,
                                   C.POINTER(C.c_uint16)]),

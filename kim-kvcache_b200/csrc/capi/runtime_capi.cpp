@@ -311,6 +311,31 @@ int kkrt_runner_forward_batch(void* r, uint32_t n, const uint64_t* ids, const ui
     return 1;
 }
 
+int kkrt_runner_forward_batch_logits(void* r, uint32_t n, const uint64_t* ids, const uint32_t* tokens,
+    const uint32_t* positions, uint32_t* out_tokens, uint8_t* out_ok, float* logits)
+{
+    auto* runner = dynamic_cast<CudaTinyLlamaModelRunner*>(RUN(r));
+    if (runner == nullptr || logits == nullptr) return 0;
+    std::vector<GenerationBatchItem> batch(n);
+    for (uint32_t i = 0; i < n; ++i) {
+        batch[i] = GenerationBatchItem{ids[i], tokens[i], positions[i]};
+    }
+    std::vector<float> rows;
+    GenerationBatchResult const res = runner->generationForwardBatchLogits(batch, rows);
+    if (!res.success || res.steps.size() != n) return 0;
+    std::size_t const V = runner->config().vocabulary_size;
+    for (uint32_t i = 0; i < n; ++i) {
+        out_tokens[i] = res.steps[i].greedy_token_id;
+        out_ok[i] = res.steps[i].success ? 1 : 0;
+        if (rows.size() >= (i + 1) * V) {
+            std::memcpy(logits + i * V, rows.data() + i * V, V * sizeof(float));
+        } else {
+            std::memset(logits + i * V, 0, V * sizeof(float));
+        }
+    }
+    return 1;
+}
+
 int kkrt_runner_forward_token(void* r, uint64_t id, uint32_t token, uint32_t position,
     uint32_t* out_token, float* logits, uint16_t* embedding, uint16_t* final_hidden,
     const uint32_t* layers, uint32_t n_layers, uint16_t* layer_hidden)

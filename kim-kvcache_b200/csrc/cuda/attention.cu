@@ -45,12 +45,17 @@ constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mutex;
 void* g_scratch_address[kMaxDevices] = {};
 
-// Device address of g_attn_scratch on the current device, looked up once per
-// device (the first call on a device does the lookup).
-int scratchAddress(void** out)
+// Device address of g_attn_scratch on the device that owns `stream`, looked
+// up once per device (the first call on a device does the lookup, with that
+// device made current for it).
+int scratchAddress(cudaStream_t stream, void** out)
 {
-    int device = 0;
-    cudaError_t e = cudaGetDevice(&device);
+    int current = 0;
+    cudaError_t e = cudaGetDevice(&current);
+    int device = current;
+    if (e == cudaSuccess && stream != nullptr) {
+        e = cudaStreamGetDevice(stream, &device);
+    }
     if (e != cudaSuccess) {
         return static_cast<int>(e);
     }
@@ -59,8 +64,14 @@ int scratchAddress(void** out)
     }
     std::lock_guard<std::mutex> lock(g_scratch_mutex);
     if (g_scratch_address[device] == nullptr) {
+        if (device != current && (e = cudaSetDevice(device)) != cudaSuccess) {
+            return static_cast<int>(e);
+        }
         void* address = nullptr;
         e = cudaGetSymbolAddress(&address, g_attn_scratch);
+        if (device != current) {
+            cudaSetDevice(current);
+        }
         if (e != cudaSuccess) {
             return static_cast<int>(e);
         }
@@ -105,6 +116,7 @@ struct AttnArgs {
     std::uint32_t* counters;         // [lanes] completion counters
     float* part_o;                   // [items][q_heads][64]
     float* part_ml;                  // [items][q_heads][2]
+    unsigned int* status;            // error word of this launch (never null in the kernel)
 };
 
 __device__ __forceinline__ void mma16816(float (&d)[4], std::uint32_t a0, std::uint32_t a1,
@@ -176,7 +188,7 @@ __device__ __forceinline__ void load_group(GroupRegs& g, AttnArgs const& a, Curs
     std::uint32_t const cap = micro ? a.micro_cap : kExtentTokens;
     if ((micro ? d.slot >= a.micro_slots : d.slot >= a.extent_slots)
         || d.valid_tokens > cap) {
-        atomicCAS(&g_attn_status, kErrNone, kErrBadDescriptor);
+        atomicCAS(a.status, kErrNone, kErrBadDescriptor);
         return;
     }
     std::uint32_t const first = c.group * 8u;
@@ -235,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_decode_attention_kernel(Att
         if (item.reserved & KK_ATTN_ITEM_MULTI_LANE) {
             // Items that may span lanes are served by the TMA kernel only.
             if (threadIdx.x == 0) {
-                atomicCAS(&g_attn_status, kErrNone, kErrBadArgument);
+                atomicCAS(a.status, kErrNone, kErrBadArgument);
             }
             continue;
         }
@@ -487,28 +499,55 @@ int numSms()
 } // namespace kk
 
 namespace {
-int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
-    const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
-    const kk_attn_item* items, uint32_t num_items, std::uint32_t const* num_items_dev,
-    const uint16_t* query, uint32_t query_stride,
-    uint16_t* output, uint32_t output_stride, float scale, void* workspace,
-    uint64_t workspace_bytes, int variant, cudaStream_t stream)
+// Argument checks of kk_paged_decode_attention other than the workspace:
+// nothing is launched (and nothing is written to the device) when they fail.
+bool attentionShapeValid(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
+    const kk_page_desc* descs, const kk_attn_lane* lanes, const kk_attn_item* items,
+    const uint16_t* query, uint32_t query_stride, const uint16_t* output, uint32_t output_stride,
+    float scale)
 {
     using namespace kk;
-    if (pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
+    return !(pools == nullptr || pools->head_dim != kHeadDim || layer >= pools->layers
         || (pools->kv_heads != 1 && pools->kv_heads != 2 && pools->kv_heads != 4
             && pools->kv_heads != 8)
         || q_heads % pools->kv_heads != 0 || q_heads / pools->kv_heads > 16
         || q_heads / pools->kv_heads == 0 || !(scale > 0.f) || query == nullptr
         || output == nullptr || descs == nullptr || lanes == nullptr || items == nullptr
-        || query_stride % 8 != 0 || output_stride % 8 != 0 || !microPageTokensValid(*pools)) {
-        return KK_EINVAL;
+        || query_stride % 8 != 0 || output_stride % 8 != 0 || !microPageTokensValid(*pools));
+}
+
+// attentionShapeValid plus the workspace: the completion counters and
+// partial states are only touched when some lane is split over several
+// items; partial states are read and written as float2/float4.
+bool attentionArgsValid(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
+    const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, const uint16_t* query, uint32_t query_stride,
+    const uint16_t* output, uint32_t output_stride, float scale, const void* workspace,
+    uint64_t workspace_bytes)
+{
+    using kk::kHeadDim;
+    if (!attentionShapeValid(pools, layer, q_heads, descs, lanes, items, query, query_stride, output,
+            output_stride, scale)) {
+        return false;
     }
-    // The workspace (completion counters + partial states) is only touched
-    // when some lane is split over several items.
     if (num_items > num_lanes
         && (workspace == nullptr
             || workspace_bytes < kk_attention_workspace_bytes(num_lanes, num_items, q_heads, kHeadDim))) {
+        return false;
+    }
+    return reinterpret_cast<std::uintptr_t>(workspace) % 16u == 0;
+}
+
+int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
+    const kk_page_desc* descs, const kk_attn_lane* lanes, uint32_t num_lanes,
+    const kk_attn_item* items, uint32_t num_items, std::uint32_t const* num_items_dev,
+    const uint16_t* query, uint32_t query_stride,
+    uint16_t* output, uint32_t output_stride, float scale, void* workspace,
+    uint64_t workspace_bytes, int variant, unsigned int* status, cudaStream_t stream)
+{
+    using namespace kk;
+    if (!attentionArgsValid(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items, query,
+            query_stride, output, output_stride, scale, workspace, workspace_bytes)) {
         return KK_EINVAL;
     }
     if (num_items == 0) {
@@ -537,9 +576,12 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     a.output = reinterpret_cast<__half*>(output);
     a.output_stride = output_stride;
     a.scale_log2 = scale * 1.4426950408889634f;
-    // Partial states are read and written as float2/float4.
-    if (reinterpret_cast<std::uintptr_t>(workspace) % 16u != 0) {
-        return KK_EINVAL;
+    a.status = status;
+    if (a.status == nullptr) {
+        cudaError_t const e = cudaGetSymbolAddress(reinterpret_cast<void**>(&a.status), g_attn_status);
+        if (e != cudaSuccess) {
+            return static_cast<int>(e);
+        }
     }
     // Without a workspace the kernels see null partial pointers: a lane that
     // turns out to be split is then reported (bad argument), never written.
@@ -560,7 +602,7 @@ int launchAttention(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
     if (tma_ok && variant != KK_ATTN_DIRECT) {
         return attentionTmaLaunch(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
             num_items_dev, query, query_stride, output, output_stride, scale, a.counters, a.part_o,
-            a.part_ml, stream);
+            a.part_ml, status, stream);
     }
     unsigned const grid = num_items < unsigned(numSms()) ? num_items : unsigned(numSms());
     return static_cast<int>(launch(paged_decode_attention_kernel, dim3(grid), dim3(kThreads), 0,
@@ -723,7 +765,8 @@ int kk_paged_decode_attention(const kk_kv_pools* pools, uint32_t layer, uint32_t
 {
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
         nullptr, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
-        kk::g_attention_variant.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
+        kk::g_attention_variant.load(std::memory_order_relaxed), nullptr,
+        static_cast<cudaStream_t>(stream));
 }
 
 int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t layer, uint32_t q_heads,
@@ -735,8 +778,16 @@ int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t layer, 
     if (need > KK_ATTN_SCRATCH_BYTES) {
         return KK_ENOSCRATCH;
     }
+    // Arguments first: a rejected call writes nothing to the device.
+    if (!attentionShapeValid(pools, layer, q_heads, descs, lanes, items, query, query_stride, output,
+            output_stride, scale)) {
+        return KK_EINVAL;
+    }
+    if (num_items == 0) {
+        return 0;
+    }
     void* scratch = nullptr;
-    int const rc = kk::scratchAddress(&scratch);
+    int const rc = kk::scratchAddress(static_cast<cudaStream_t>(stream), &scratch);
     if (rc != 0) {
         return rc;
     }
@@ -748,7 +799,8 @@ int kk_paged_decode_attention_noalloc(const kk_kv_pools* pools, uint32_t layer, 
     }
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items,
         nullptr, query, query_stride, output, output_stride, scale, scratch, KK_ATTN_SCRATCH_BYTES,
-        kk::g_attention_variant.load(std::memory_order_relaxed), static_cast<cudaStream_t>(stream));
+        kk::g_attention_variant.load(std::memory_order_relaxed), nullptr,
+        static_cast<cudaStream_t>(stream));
 }
 
 int kk_attention_set_variant(int variant)
@@ -770,9 +822,9 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
-    cudaStream_t stream)
+    unsigned int* status, cudaStream_t stream)
 {
-    if (num_items == nullptr) {
+    if (num_items == nullptr || status == nullptr) {
         return KK_EINVAL;
     }
     // The runner plans with kk_attention_plan_balanced wherever the TMA kernel
@@ -781,6 +833,17 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     int const variant = attentionTmaSupported(pools, q_heads) ? KK_ATTN_TMA : KK_ATTN_DIRECT;
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, max_items,
         num_items, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
-        variant, stream);
+        variant, status, stream);
+}
+
+int attentionLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint16_t const* query,
+    std::uint32_t query_stride, std::uint16_t* output, std::uint32_t output_stride, float scale,
+    void* workspace, std::uint64_t workspace_bytes, unsigned int* status, cudaStream_t stream)
+{
+    return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items, nullptr,
+        query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
+        g_attention_variant.load(std::memory_order_relaxed), status, stream);
 }
 } // namespace kk

@@ -43,6 +43,12 @@
 namespace kk {
 
 __device__ unsigned int g_attn_tma_status;
+// Test hook (kk_debug_attention_fault): CTA 0 of every launch drops stage
+// g_attn_fault_stage (no copy, no arrival), so its consumers' bounded wait
+// runs out; waits give up after g_attn_wait_limit_ns. Defaults: no stage
+// dropped, the production limit.
+__device__ std::uint32_t g_attn_fault_stage = 0xffffffffu;
+__device__ std::uint64_t g_attn_wait_limit_ns = kWaitLimitNs;
 #ifdef KK_TRACE
 __device__ TraceRec g_attn_trace[kTraceCap];
 __device__ unsigned int g_attn_trace_n;
@@ -121,6 +127,7 @@ struct TmaArgs {
     std::uint32_t* counters;
     float* part_o;
     float* part_ml;
+    unsigned int* status;  // error word of this launch (null: the module's word)
 };
 
 __device__ __forceinline__ void tma_load_5d_hint(void* dst, CUtensorMap const* map, std::uint64_t* bar,
@@ -195,12 +202,13 @@ __device__ __forceinline__ std::uint32_t pack_half2(float lo, float hi)
 // Bounded wait (suspending polls, wall-time limit) that also gives up as soon
 // as another warp raised the CTA's abort flag.
 __device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t phase,
-    int volatile* abort)
+    int volatile* abort, unsigned int* status)
 {
     if (mbar_try_wait_suspend(bar, phase)) {
         return true;
     }
     std::uint64_t const t0 = global_ns();
+    std::uint64_t const limit = *static_cast<std::uint64_t volatile*>(&g_attn_wait_limit_ns);
     for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
         if (mbar_try_wait_suspend(bar, phase)) {
             return true;
@@ -208,12 +216,28 @@ __device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t 
         if (*abort) {
             return false;
         }
-        if (global_ns() - t0 > kWaitLimitNs) {
+        if (global_ns() - t0 > limit) {
             break;
         }
     }
     *abort = 1;
-    atomicCAS(&g_attn_tma_status, kErrNone, kErrWaitTimeout);
+    atomicCAS(status, kErrNone, kErrWaitTimeout);
+    return false;
+}
+
+// Bounded wait that ignores the abort flag: used after an abort to let the
+// copies this CTA issued land before it exits.
+__device__ __forceinline__ bool wait_bounded(std::uint64_t* bar, std::uint32_t phase)
+{
+    std::uint64_t const t0 = global_ns();
+    for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+        if (mbar_try_wait_suspend(bar, phase)) {
+            return true;
+        }
+        if (global_ns() - t0 > kWaitLimitNs) {
+            break;
+        }
+    }
     return false;
 }
 
@@ -271,6 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
 
     std::uint32_t const warp = threadIdx.x / 32;
     std::uint32_t const lane = threadIdx.x % 32;
+    unsigned int* const st = a.status != nullptr ? a.status : &g_attn_tma_status;
 #ifdef KK_TRACE
     __shared__ TraceRec* s_tr;
     if (threadIdx.x == 0) {
@@ -328,13 +353,16 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         bool waited = false;
         std::uint32_t stage = 0;
         std::uint32_t qk = 0;  // lane segments started by this CTA
+        // Stage that the test hook drops in CTA 0 (none by default).
+        std::uint32_t const fault_stage =
+            blockIdx.x == 0 ? *static_cast<std::uint32_t volatile*>(&g_attn_fault_stage) : 0xffffffffu;
         // Publishes lane segment qk to the consumers: its bookkeeping in seg
         // and its query row (all heads) copied into qbuf by one bulk copy,
         // both covered by q_full, once the consumers took segment qk - 1's
         // query (q_empty). Consumers only read shared memory, so a new
         // segment costs them no global round trip.
         auto start_segment = [&](kk_attn_lane const& L, std::uint32_t lane_b, std::uint32_t part_slot) -> bool {
-            bool const ready = qk == 0u || wait_or_abort(q_empty, (qk - 1u) & 1u, s_abort);
+            bool const ready = qk == 0u || wait_or_abort(q_empty, (qk - 1u) & 1u, s_abort, st);
             if (!__all_sync(0xffffffffu, ready)) {
                 return false;
             }
@@ -349,13 +377,29 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             ++qk;
             return true;
         };
+        // Before the producer exits: lets the copies this CTA may still have
+        // in flight (the last kStages stages, the last query row) land, so
+        // that none outlives the CTA when the consumers gave up early.
+        auto drain = [&]() {
+            if (lane == 0) {
+                for (std::uint32_t j = stage > kStages ? stage - kStages : 0u; j < stage; ++j) {
+                    if (j != fault_stage) {
+                        wait_bounded(&full[j % kStages], (j / kStages) & 1u);
+                    }
+                }
+                if (qk != 0u) {
+                    wait_bounded(q_full, (qk - 1u) & 1u);
+                }
+            }
+            __syncwarp();
+        };
         for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
 
             kk_attn_item const item = a.items[it];
             std::uint32_t b = item.lane;
             if (b >= a.num_lanes) {
                 if (lane == 0) {
-                    atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+                    atomicCAS(st, kErrNone, kErrBadArgument);
                 }
                 b = 0;
             }
@@ -404,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         && valid <= (m ? a.micro_cap : 64u);
                     if (!ok) {
                         if (lane == 0) {
-                            atomicCAS(&g_attn_tma_status, kErrNone, kErrBadDescriptor);
+                            atomicCAS(st, kErrNone, kErrBadDescriptor);
                         }
                         continue;
                     }
@@ -427,15 +471,18 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 }
             }
             if (!start_segment(cur_lane, b, 2u * it)) {
+                drain();
                 return;
             }
             for (;;) {
                 std::uint32_t const s = stage % kStages;
                 bool const ready = stage < kStages
-                    || wait_or_abort(&empty[s], ((stage / kStages) - 1u) & 1u, s_abort);
+                    || wait_or_abort(&empty[s], ((stage / kStages) - 1u) & 1u, s_abort, st);
                 if (!__all_sync(0xffffffffu, ready)) {
+                    drain();
                     return;
                 }
+                bool const issue = lane == 0 && stage != fault_stage;
                 StageMeta m{};
                 m.lane = b;
                 std::uint8_t* base = ring + s * kStageBytes;
@@ -459,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                             std::uint32_t const left = j < groups_per_stage && first < vt ? vt - first : 0u;
                             m.valid |= std::uint64_t(left < 8u ? left : 8u) << (8u * j);
                         }
-                        if (lane == 0) {
+                        if (issue) {
                             mbar_expect_tx(&full[s], 2u * Hkv * bt * kRowBytes);
                             if (!per_head) {
                                 tma_load_5d_hint(base, map, &full[s], 0, static_cast<int>(tok), 0,
@@ -488,7 +535,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         std::uint32_t const lo = vt < 8u ? vt : 8u;
                         m.valid |= (std::uint64_t(lo) << (8u * n)) | (std::uint64_t(vt - lo) << (8u * (n + 1u)));
                         m.flags |= kMicroStage | kPage16;
-                        if (lane == 0) {
+                        if (issue) {
                             mbar_expect_tx(&full[s], 2u * Hkv * 16u * kRowBytes);
                             std::uint8_t* dst = base + n * Hkv * 8u * kRowBytes;
                             tma_load_5d_hint(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot, kv_policy);
@@ -502,14 +549,14 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         m.valid |= std::uint64_t(vt) << (8u * n);
                         if (a.micro_per_head == 0) {
                             m.flags |= kMicroStage;
-                            if (lane == 0) {
+                            if (issue) {
                                 mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
                                 std::uint8_t* dst = base + n * Hkv * 8u * kRowBytes;
                                 tma_load_5d_hint(dst, &tm_micro, &full[s], 0, 0, 0, static_cast<int>(kv), slot, kv_policy);
                                 tma_load_5d_hint(dst + v_offset, &tm_micro, &full[s], 0, 0, 0,
                                     static_cast<int>(kv + 1), slot, kv_policy);
                             }
-                        } else if (lane == 0) {
+                        } else if (issue) {
                             mbar_expect_tx(&full[s], 2u * Hkv * 8u * kRowBytes);
                             for (std::uint32_t h = 0; h < Hkv; ++h) {
                                 std::uint8_t* dst = base + (h * Ts + n * 8u) * kRowBytes;
@@ -545,7 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         }
                         if (nb >= a.num_lanes || cur_lane.desc_offset != e) {
                             if (lane == 0) {
-                                atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+                                atomicCAS(st, kErrNone, kErrBadArgument);
                             }
                             m.flags |= kItemEnd;
                             item_done = true;
@@ -559,7 +606,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         }
                     }
                 }
-                if (lane == 0) {
+                if (issue) {
                     meta[s] = m;
                     mbar_arrive(&full[s]);  // releases meta[s]; the phase ends when the bytes land
                 }
@@ -568,6 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     break;
                 }
                 if (next_segment && !start_segment(cur_lane, b, 2u * it + 1u)) {
+                    drain();
                     return;
                 }
                 if (!have) {
@@ -578,6 +626,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         if (lane == 0) {
             KK_ATTN_STAMP(2)
         }
+        // No CTA exits with its own copies in flight, also when the
+        // consumers gave up on an earlier stage.
+        drain();
         return;
     }
 
@@ -603,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     std::uint32_t cphase = 0;
     auto consumer_sync = [&]() {
         mbar_arrive(cbar);
-        wait_or_abort(cbar, cphase, s_abort);
+        wait_or_abort(cbar, cphase, s_abort, st);
         cphase ^= 1u;
     };
     // Takes lane segment ck from the producer: its bookkeeping and this
@@ -612,7 +663,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     std::uint32_t qf[NT][4][2];
     SegInfo si{};
     auto begin_segment = [&]() -> bool {
-        if (*s_abort || !wait_or_abort(q_full, ck & 1u, s_abort)) {
+        if (*s_abort || !wait_or_abort(q_full, ck & 1u, s_abort, st)) {
             return false;
         }
         si = *seg;
@@ -733,7 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         for (;;) {
 
             std::uint32_t const s = stage % kStages;
-            if (*s_abort || !wait_or_abort(&full[s], (stage / kStages) & 1u, s_abort)) {
+            if (*s_abort || !wait_or_abort(&full[s], (stage / kStages) & 1u, s_abort, st)) {
                 break;
             }
 #ifdef KK_TRACE
@@ -868,7 +919,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             // reported and its partial is dropped.
             bool const split = si.item_count > 1 && a.part_o != nullptr;
             if (si.item_count > 1 && a.part_o == nullptr && tid == 0) {
-                atomicCAS(&g_attn_tma_status, kErrNone, kErrBadArgument);
+                atomicCAS(st, kErrNone, kErrBadArgument);
             }
             bool const keep = si.item_count <= 1 || split;
             for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
@@ -1148,7 +1199,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream)
+    unsigned int* status, cudaStream_t stream)
 {
     PoolMaps maps{};
     if (!poolMaps(*pools, maps)) {
@@ -1188,6 +1239,7 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     a.counters = counters;
     a.part_o = part_o;
     a.part_ml = part_ml;
+    a.status = status;
     static int const sms = smCount();
     unsigned const grid = num_items < unsigned(sms) ? num_items : unsigned(sms);
     bool const narrow = a.group <= 8;
@@ -1198,6 +1250,20 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
 }
 
 int attentionTmaStatus(cudaStream_t stream) { return readStatus(&g_attn_tma_status, stream); }
+
+} // namespace kk
+
+extern "C" int kk_debug_attention_fault(uint32_t stage, uint64_t wait_limit_ns)
+{
+    cudaError_t e = cudaMemcpyToSymbol(kk::g_attn_fault_stage, &stage, sizeof(stage));
+    if (e == cudaSuccess) {
+        std::uint64_t const limit = wait_limit_ns == 0 ? kk::kWaitLimitNs : wait_limit_ns;
+        e = cudaMemcpyToSymbol(kk::g_attn_wait_limit_ns, &limit, sizeof(limit));
+    }
+    return static_cast<int>(e);
+}
+
+namespace kk {
 
 #ifdef KK_TRACE
 extern "C" KK_KAPI std::uint32_t kk_trace_read_attn(void* host, std::uint32_t cap, int reset)

@@ -4,6 +4,7 @@
 #include "cuda_backend.h"
 
 #include "../host/fixed_page_manager.h"
+#include "kernels_internal.h"
 
 #include <cuda_runtime.h>
 
@@ -125,10 +126,16 @@ struct Storage {
 struct Arena {
     static constexpr std::uint32_t kSlots = 64;
     static constexpr std::size_t kHeader = 96;  // kv_slot | copy | lane | item
+    // Device error words of the per-layer path, one per stream it launched on.
+    static constexpr std::uint32_t kStatusWords = 64;
     std::uint32_t max_desc{0};
     std::size_t slot_bytes{0};
     std::uint8_t* dev{nullptr};
     std::uint8_t* host{nullptr};
+    unsigned int* status{nullptr};
+    // Reads of the error words go through this stream, so that they never
+    // wait for work that callers queued after the point being checked.
+    cudaStream_t watch_stream{nullptr};
     std::vector<std::uint32_t> free_slots;
 
     bool init(std::uint32_t descriptors)
@@ -136,7 +143,10 @@ struct Arena {
         max_desc = descriptors;
         slot_bytes = (kHeader + std::size_t(descriptors) * sizeof(kk_page_desc) + 255) & ~std::size_t(255);
         if (cudaMalloc(reinterpret_cast<void**>(&dev), slot_bytes * kSlots) != cudaSuccess
-            || cudaMallocHost(reinterpret_cast<void**>(&host), slot_bytes * kSlots) != cudaSuccess) {
+            || cudaMallocHost(reinterpret_cast<void**>(&host), slot_bytes * kSlots) != cudaSuccess
+            || cudaMalloc(reinterpret_cast<void**>(&status), kStatusWords * sizeof(unsigned int)) != cudaSuccess
+            || cudaMemset(status, 0, kStatusWords * sizeof(unsigned int)) != cudaSuccess
+            || cudaStreamCreateWithFlags(&watch_stream, cudaStreamNonBlocking) != cudaSuccess) {
             return false;
         }
         for (std::uint32_t i = kSlots; i > 0; --i) {
@@ -149,6 +159,10 @@ struct Arena {
     {
         cudaFree(dev);
         cudaFreeHost(host);
+        cudaFree(status);
+        if (watch_stream != nullptr) {
+            cudaStreamDestroy(watch_stream);
+        }
     }
 
     // Offsets inside a slot.
@@ -181,6 +195,19 @@ struct State {
     std::atomic<std::uint64_t> submit_seq{0};
     std::mutex sync_mutex;
     std::unordered_map<void*, std::uint64_t> completed_seq;
+
+    // Device-detected errors of the per-layer path (a descriptor outside its
+    // pool, a bounded wait that ran out). The kernels that transactions
+    // launch on a stream report into that stream's error word; a commit reads
+    // it once the stream is synchronized. An error fails every transaction
+    // with work queued on the stream before the word is cleared again (the
+    // conservative reading: a word cannot tell which launch set it).
+    struct StreamWatch {
+        std::uint32_t word;
+        std::uint64_t checked;      // submissions up to here were checked
+        std::uint64_t failed_upto;  // submissions up to here are covered by a device error
+    };
+    std::unordered_map<void*, StreamWatch> watch;  // under sync_mutex
 
     State(EngineKvConfig c, std::uint32_t micro_cap, std::uint32_t extent_cap)
         : config(c), kind(EngineKvBackendKind::Heterogeneous)
@@ -245,11 +272,69 @@ struct State {
         return was;
     }
 
-    bool completed(void* stream, std::uint64_t seq)
+    // True when a synchronize of `stream` already covered submission `seq`;
+    // `covered` receives the submission it covered up to.
+    bool completed(void* stream, std::uint64_t seq, std::uint64_t& covered)
     {
         std::lock_guard<std::mutex> lock(sync_mutex);
         auto const f = completed_seq.find(stream);
-        return f != completed_seq.end() && f->second >= seq;
+        if (f == completed_seq.end() || f->second < seq) {
+            return false;
+        }
+        covered = f->second;
+        return true;
+    }
+
+    void noteCompleted(void* stream, std::uint64_t covered)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        std::uint64_t& c = completed_seq[stream];
+        c = c > covered ? c : covered;
+    }
+
+    // Error word of the per-layer kernels launched on `stream`.
+    unsigned int* statusWord(void* stream)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        auto f = watch.find(stream);
+        if (f == watch.end()) {
+            // More streams than words: the last word is shared (errors then
+            // fail the transactions of every stream that shares it).
+            std::uint32_t const n = static_cast<std::uint32_t>(watch.size());
+            std::uint32_t const w = n < Arena::kStatusWords ? n : Arena::kStatusWords - 1;
+            f = watch.emplace(stream, StreamWatch{w, 0, 0}).first;
+        }
+        return arena.status + f->second.word;
+    }
+
+    // Called once `stream` is synchronized up to submission `covered`: reads
+    // the stream's error word (once per such point) and, when it is set,
+    // clears it on the stream behind everything queued so far. Returns the
+    // last submission that a device error covers (0: none).
+    std::uint64_t checkStream(void* stream, std::uint64_t covered)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        auto const f = watch.find(stream);
+        if (f == watch.end()) {
+            return 0;  // no per-layer kernel ran on this stream
+        }
+        StreamWatch& w = f->second;
+        if (w.checked < covered) {
+            unsigned int code = 0;
+            cudaError_t e = cudaMemcpyAsync(&code, arena.status + w.word, sizeof(code), cudaMemcpyDeviceToHost,
+                arena.watch_stream);
+            if (e == cudaSuccess) {
+                e = cudaStreamSynchronize(arena.watch_stream);
+            }
+            if (e != cudaSuccess || code != 0) {
+                // Everything queued on the stream until the clear below is
+                // covered: the word may also hold an error of later work.
+                w.failed_upto = submit_seq.load();
+                cudaMemsetAsync(arena.status + w.word, 0, sizeof(unsigned int), static_cast<cudaStream_t>(stream));
+            }
+            w.checked = covered;
+        }
+        return w.failed_upto;
     }
 };
 
@@ -286,14 +371,16 @@ public:
         std::uint8_t* const dev = slotDev();
         cudaStream_t const s = static_cast<cudaStream_t>(stream_);
         int rc = 0;
+        unsigned int* const status = st_->statusWord(stream_);
         if (needs_copy_) {
-            rc = kk_kv_copy_tokens(&st_->storage.pools, write.layer, 1,
-                reinterpret_cast<kk_kv_copy const*>(dev + Arena::kCopyOff), 1, s);
+            rc = kk::kvCopy(&st_->storage.pools, write.layer, 1,
+                reinterpret_cast<kk_kv_copy const*>(dev + Arena::kCopyOff), 1, status, s);
         }
         if (rc == 0) {
-            rc = kk_kv_write(&st_->storage.pools, write.layer, 1,
-                reinterpret_cast<kk_kv_slot const*>(dev + Arena::kSlotOff), 1, write.device_key,
-                write.device_value, 0, 0, s);
+            rc = kk::kvWrite(&st_->storage.pools, write.layer, 1,
+                reinterpret_cast<kk_kv_slot const*>(dev + Arena::kSlotOff), 1,
+                static_cast<std::uint16_t const*>(write.device_key),
+                static_cast<std::uint16_t const*>(write.device_value), 0, 0, status, s);
         }
         if (rc != 0) {
             return fail(submitError(rc));
@@ -311,12 +398,13 @@ public:
         std::uint8_t* const dev = slotDev();
         std::uint32_t const hq = st_->config.query_head_count;
         std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
-        int const rc = kk_paged_decode_attention(&st_->storage.pools, r.layer, hq,
+        int const rc = kk::attentionLaunch(&st_->storage.pools, r.layer, hq,
             reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
             reinterpret_cast<kk_attn_lane const*>(dev + Arena::kLaneOff), 1,
-            reinterpret_cast<kk_attn_item const*>(dev + Arena::kItemOff), 1, r.device_query, row,
-            r.device_output, row, r.attention_scale, r.device_workspace, r.workspace_bytes,
-            static_cast<cudaStream_t>(stream_));
+            reinterpret_cast<kk_attn_item const*>(dev + Arena::kItemOff), 1,
+            static_cast<std::uint16_t const*>(r.device_query), row,
+            static_cast<std::uint16_t*>(r.device_output), row, r.attention_scale, r.device_workspace,
+            r.workspace_bytes, st_->statusWord(stream_), static_cast<cudaStream_t>(stream_));
         if (rc != 0) {
             return fail(submitError(rc));
         }
@@ -416,7 +504,13 @@ public:
         submission_ = final_ = s;
         return mapCuda(s);
     }
-    void markSubmitted() noexcept { last_submit_ = ++st_->submit_seq; }
+    void markSubmitted() noexcept
+    {
+        last_submit_ = ++st_->submit_seq;
+        if (first_submit_ == 0) {
+            first_submit_ = last_submit_;
+        }
+    }
 
 private:
     // Copies this transaction's write target, COW record, lane and descriptors
@@ -490,12 +584,22 @@ private:
             final_ = submission_;
             return final_;
         }
-        if (!st_->completed(stream_, last_submit_)) {
+        std::uint64_t covered = 0;
+        if (!st_->completed(stream_, last_submit_, covered)) {
+            covered = st_->submit_seq.load();
             cudaError_t const e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
             if (e != cudaSuccess) {
                 final_ = {CudaError::ExecutionFailed, static_cast<int>(e)};
                 return final_;
             }
+            st_->noteCompleted(stream_, covered);
+        }
+        // A device-detected error of work queued on this stream fails the
+        // transaction at commit (reference: a completion failure surfaces as
+        // ExecutionFailed, src/cuda/engine/transaction.cpp:84-120).
+        if (first_submit_ != 0 && st_->checkStream(stream_, covered) >= first_submit_) {
+            final_ = {CudaError::ExecutionFailed, KK_EDEVICE};
+            return final_;
         }
         if (st_->consumeFailure(CudaFailurePoint::Completion)) {
             final_ = {CudaError::ExecutionFailed, static_cast<int>(cudaErrorUnknown)};
@@ -541,6 +645,7 @@ private:
     bool finished_{false};
     bool resolved_{false};
     std::uint64_t last_submit_{0};
+    std::uint64_t first_submit_{0};
 
     friend void batchAttend(CudaTxn& self, PagedDecodeBatch& batch);
 };
@@ -625,13 +730,13 @@ void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
         auto* dev = reinterpret_cast<std::uint8_t*>(batch.device_items);
         PagedDecodeRequest const& r0 = batch.items[idx[ready[0]]].request;
         std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
-        rc = kk_paged_decode_attention(&st_->storage.pools, r0.layer, hq,
+        rc = kk::attentionLaunch(&st_->storage.pools, r0.layer, hq,
             reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
             reinterpret_cast<kk_attn_lane const*>(dev), static_cast<std::uint32_t>(ready.size()),
             reinterpret_cast<kk_attn_item const*>(dev + ready.size() * sizeof(kk_attn_lane)),
             static_cast<std::uint32_t>(ready.size()), reinterpret_cast<std::uint16_t const*>(qmin),
             row, reinterpret_cast<std::uint16_t*>(const_cast<std::uint8_t*>(omin)), row,
-            r0.attention_scale, r0.device_workspace, r0.workspace_bytes, s);
+            r0.attention_scale, r0.device_workspace, r0.workspace_bytes, st_->statusWord(stream_), s);
     }
     std::uint64_t ok_lanes = 0;
     for (std::size_t k : ready) {
@@ -1184,9 +1289,7 @@ void noteStreamCompleted(EngineKvBackend& backend, CudaStream stream) noexcept
         return;
     }
     State* st = b->state();
-    std::uint64_t const seq = st->submit_seq.load();
-    std::lock_guard<std::mutex> lock(st->sync_mutex);
-    st->completed_seq[stream] = seq;
+    st->noteCompleted(stream, st->submit_seq.load());
 }
 
 } // namespace kimkvcache

@@ -130,6 +130,7 @@ struct GemmArgs {
     // KK_EPI_RESIDUAL: sums of squares of the new FP16 rows over this tile,
     // sq_out[m_tile * kSqStride + n] (or null).
     float* sq_out;
+    unsigned int* status;           // error word of the launch (null: the module's word)
     EpiArgs epi;
 };
 
@@ -229,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint32_t const tid = threadIdx.x;
     std::uint32_t const warp = tid / 32;
     std::uint32_t const lane = tid % 32;
+    unsigned int* const st = args.status != nullptr ? args.status : &g_gemm_status;
 #ifdef KK_TRACE
     std::uint64_t tr[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
 #endif
@@ -306,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         }
         for (std::uint32_t i = pre; i < nk; ++i) {
             std::uint32_t const s = i % kStages;
-            if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, &g_gemm_status)) {
+            if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, st)) {
                 break;
             }
             mbar_arrive_expect_tx(&full[s], kStageBytes);
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         std::uint32_t const idesc = umma_idesc_f16_f32(kBM, BN);
         for (std::uint32_t i = 0; i < nk; ++i) {
             std::uint32_t const s = i % kStages;
-            if (!mbar_wait(&full[s], (i / kStages) & 1u, &g_gemm_status)) {
+            if (!mbar_wait(&full[s], (i / kStages) & 1u, st)) {
                 break;
             }
             tc_fence_after();
@@ -412,7 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         }
     }
-    bool const have_acc = mbar_wait(accum, 0, &g_gemm_status);
+    bool const have_acc = mbar_wait(accum, 0, st);
     tc_fence_after();
     KK_GEMM_STAMP(2)
 
@@ -461,7 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
             }
         }
-        bool const got = mbar_wait(rbar, 0, &g_gemm_status);
+        bool const got = mbar_wait(rbar, 0, st);
         KK_GEMM_STAMP(5)
         // Sum over the K slices in rank order (deterministic).
         for (std::uint32_t j = 0; j < cols; ++j) {
@@ -620,7 +622,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                         + sl.page_token) * e.kv_row + idx;
                     page[off] = hv;
                 } else if (sl.active) {
-                    atomicCAS(&g_gemm_status, kErrNone, kErrBadDescriptor);
+                    atomicCAS(st, kErrNone, kErrBadDescriptor);
                 }
             }
         }
@@ -1061,6 +1063,8 @@ bool gemmSetSumSquaresOut(GemmPlan& plan, float* sq_out)
     plan.args.sq_out = sq_out;
     return true;
 }
+
+void gemmSetStatus(GemmPlan& plan, unsigned int* status) { plan.args.status = status; }
 
 void gemmSetL2Prefetch(GemmPlan& plan, void const* ptr, std::uint64_t bytes)
 {

@@ -27,12 +27,22 @@ inline bool microPageTokensValid(kk_kv_pools const& p) noexcept
 
 // kk_paged_decode_attention with the item count in device memory; items
 // beyond *num_items (<= max_items) are ignored. The grid is sized for max_items.
+// Errors go to *status (a word of the caller's, zeroed by it) instead of the
+// module's word that kk_device_status reads.
 int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
     kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
     kk_attn_item const* items, std::uint32_t const* num_items, std::uint32_t max_items,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, void* workspace, std::uint64_t workspace_bytes,
-    cudaStream_t stream);
+    unsigned int* status, cudaStream_t stream);
+
+// kk_paged_decode_attention reporting errors to *status (null: the module's
+// word).
+int attentionLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint16_t const* query,
+    std::uint32_t query_stride, std::uint16_t* output, std::uint32_t output_stride, float scale,
+    void* workspace, std::uint64_t workspace_bytes, unsigned int* status, cudaStream_t stream);
 
 // TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
 // KV heads, up to 16 query heads per KV head; serves both plan kinds
@@ -44,12 +54,21 @@ int attentionTmaLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
     kk_attn_item const* items, std::uint32_t num_items, std::uint32_t const* num_items_dev,
     std::uint16_t const* query, std::uint32_t query_stride, std::uint16_t* output,
     std::uint32_t output_stride, float scale, std::uint32_t* counters, float* part_o, float* part_ml,
-    cudaStream_t stream);
+    unsigned int* status, cudaStream_t stream);
 
 // kk_kv_copy_tokens with the copy count in device memory (<= max_copies).
 int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
     kk_kv_copy const* copies, std::uint32_t const* num_copies, std::uint32_t max_copies,
-    cudaStream_t stream);
+    unsigned int* status, cudaStream_t stream);
+
+// kk_kv_write / kk_kv_copy_tokens reporting errors to *status (null: the
+// module's word).
+int kvWrite(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_slot const* slots, std::uint32_t num_lanes, std::uint16_t const* key,
+    std::uint16_t const* value, std::uint64_t lane_stride, std::uint64_t layer_stride,
+    unsigned int* status, cudaStream_t stream);
+int kvCopy(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_copy const* copies, std::uint32_t num_copies, unsigned int* status, cudaStream_t stream);
 
 struct GemmPlan;
 struct GemmPlanDeleter {
@@ -65,6 +84,8 @@ int gemmRun(GemmPlan const& plan, cudaStream_t stream);
 // [ptr, ptr + bytes) once its own inputs are requested: bytes that a later
 // kernel of the step streams (null or 0 clears it).
 void gemmSetL2Prefetch(GemmPlan& plan, void const* ptr, std::uint64_t bytes);
+// The plan's launches report errors to *status (null: the module's word).
+void gemmSetStatus(GemmPlan& plan, unsigned int* status);
 
 // Sums of squares for the fused RMSNorm, kept in arrays of rows of 64 floats
 // (one row per 128-row tile of the producing projection, one column per

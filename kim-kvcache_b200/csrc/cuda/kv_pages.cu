@@ -28,7 +28,13 @@ struct PoolView {
     std::uint32_t row;         // kv_heads * head_dim elements per token per K|V
     std::uint32_t layers;
     std::uint32_t micro_cap;   // tokens per micro page
+    unsigned int* status;      // error word of the launch (null: the module's word)
 };
+
+__device__ __forceinline__ void report(PoolView const& v, unsigned int code)
+{
+    atomicCAS(v.status != nullptr ? v.status : &g_pages_status, kErrNone, code);
+}
 
 PoolView view(kk_kv_pools const& p)
 {
@@ -51,7 +57,7 @@ __device__ __forceinline__ __half* block_of(PoolView const& v, std::uint32_t kin
 {
     bool const micro = kind == 0;
     if (micro ? slot >= v.micro_slots : slot >= v.extent_slots) {
-        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        report(v, kErrBadDescriptor);
         return nullptr;
     }
     std::uint32_t const cap = micro ? v.micro_cap : 64u;
@@ -74,7 +80,7 @@ __global__ void kv_write_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_slo
     }
     std::uint32_t const cap = s.kind == 0 ? v.micro_cap : 64u;
     if (s.page_token >= cap) {
-        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        report(v, kErrBadDescriptor);
         return;
     }
     __half* dst = block_of(v, s.kind, s.slot, layer_begin + layer_off, component);
@@ -103,7 +109,7 @@ __global__ void kv_copy_kernel(PoolView v, std::uint32_t layer_begin, kk_kv_copy
     std::uint32_t const src_cap = c.src_kind == 0 ? v.micro_cap : 64u;
     std::uint32_t const dst_cap = c.dst_kind == 0 ? v.micro_cap : 64u;
     if (c.tokens > src_cap || c.tokens > dst_cap) {
-        atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+        report(v, kErrBadDescriptor);
         return;
     }
     __half const* src = block_of(v, c.src_kind, c.src_slot, layer, component);
@@ -163,7 +169,7 @@ __global__ void kv_gather_kernel(PoolView v, kk_page_desc const* descs, std::uin
         || (in == nullptr ? end > total_tokens : false);
     if (bad) {
         if (threadIdx.x == 0) {
-            atomicCAS(&g_pages_status, kErrNone, kErrBadDescriptor);
+            report(v, kErrBadDescriptor);
         }
         return;
     }
@@ -223,35 +229,15 @@ int kk_kv_write(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t layer_c
     const kk_kv_slot* slots, uint32_t num_lanes, const uint16_t* key, const uint16_t* value,
     uint64_t lane_stride, uint64_t layer_stride, void* stream)
 {
-    using namespace kk;
-    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
-        || slots == nullptr || key == nullptr || value == nullptr || lane_stride % 8 != 0
-        || layer_stride % 8 != 0 || num_lanes > 65535u) {
-        return KK_EINVAL;
-    }
-    if (num_lanes == 0) {
-        return 0;
-    }
-    return static_cast<int>(launch(kv_write_kernel, dim3(num_lanes, layer_count, 2), dim3(64), 0,
-        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, slots,
-        reinterpret_cast<__half const*>(key), reinterpret_cast<__half const*>(value), lane_stride,
-        layer_stride));
+    return kk::kvWrite(pools, layer_begin, layer_count, slots, num_lanes, key, value, lane_stride,
+        layer_stride, nullptr, static_cast<cudaStream_t>(stream));
 }
 
 int kk_kv_copy_tokens(const kk_kv_pools* pools, uint32_t layer_begin, uint32_t layer_count,
     const kk_kv_copy* copies, uint32_t num_copies, void* stream)
 {
-    using namespace kk;
-    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
-        || copies == nullptr || num_copies > 65535u) {
-        return KK_EINVAL;
-    }
-    if (num_copies == 0) {
-        return 0;
-    }
-    return static_cast<int>(launch(kv_copy_kernel, dim3(num_copies, layer_count, 2), dim3(128), 0,
-        static_cast<cudaStream_t>(stream), 1, view(*pools), layer_begin, copies,
-        static_cast<std::uint32_t const*>(nullptr)));
+    return kk::kvCopy(pools, layer_begin, layer_count, copies, num_copies, nullptr,
+        static_cast<cudaStream_t>(stream));
 }
 
 int kk_kv_promote(const kk_kv_pools* pools, const uint32_t* micro_slots, uint32_t extent_slot,
@@ -327,13 +313,51 @@ int pagesStatus(cudaStream_t stream) { return readStatus(&g_pages_status, stream
 
 int kvCopyDevCount(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
     kk_kv_copy const* copies, std::uint32_t const* num_copies, std::uint32_t max_copies,
-    cudaStream_t stream)
+    unsigned int* status, cudaStream_t stream)
 {
     if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
         || copies == nullptr || num_copies == nullptr || max_copies == 0 || max_copies > 65535u) {
         return KK_EINVAL;
     }
+    PoolView v = view(*pools);
+    v.status = status;
     return static_cast<int>(launch(kv_copy_kernel, dim3(max_copies, layer_count, 2), dim3(128), 0,
-        stream, 1, view(*pools), layer_begin, copies, num_copies));
+        stream, 1, v, layer_begin, copies, num_copies));
+}
+
+int kvWrite(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_slot const* slots, std::uint32_t num_lanes, std::uint16_t const* key,
+    std::uint16_t const* value, std::uint64_t lane_stride, std::uint64_t layer_stride,
+    unsigned int* status, cudaStream_t stream)
+{
+    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
+        || slots == nullptr || key == nullptr || value == nullptr || lane_stride % 8 != 0
+        || layer_stride % 8 != 0 || num_lanes > 65535u) {
+        return KK_EINVAL;
+    }
+    if (num_lanes == 0) {
+        return 0;
+    }
+    PoolView v = view(*pools);
+    v.status = status;
+    return static_cast<int>(launch(kv_write_kernel, dim3(num_lanes, layer_count, 2), dim3(64), 0,
+        stream, 1, v, layer_begin, slots, reinterpret_cast<__half const*>(key),
+        reinterpret_cast<__half const*>(value), lane_stride, layer_stride));
+}
+
+int kvCopy(kk_kv_pools const* pools, std::uint32_t layer_begin, std::uint32_t layer_count,
+    kk_kv_copy const* copies, std::uint32_t num_copies, unsigned int* status, cudaStream_t stream)
+{
+    if (!poolsOk(pools) || layer_count == 0 || layer_begin + layer_count > pools->layers
+        || copies == nullptr || num_copies > 65535u) {
+        return KK_EINVAL;
+    }
+    if (num_copies == 0) {
+        return 0;
+    }
+    PoolView v = view(*pools);
+    v.status = status;
+    return static_cast<int>(launch(kv_copy_kernel, dim3(num_copies, layer_count, 2), dim3(128), 0,
+        stream, 1, v, layer_begin, copies, static_cast<std::uint32_t const*>(nullptr)));
 }
 } // namespace kk

@@ -86,7 +86,7 @@ struct CudaTinyLlamaModelRunner::Impl {
     std::uint16_t* attn{nullptr};
     std::uint16_t* act{nullptr};
     float* logits{nullptr};
-    std::uint32_t* out_tokens{nullptr};
+    std::uint32_t* out_tokens{nullptr};  // in the step's result block (below)
     void* attn_ws{nullptr};
     std::uint64_t attn_ws_bytes{0};
     void* argmax_ws{nullptr};
@@ -103,11 +103,19 @@ struct CudaTinyLlamaModelRunner::Impl {
     std::uint32_t max_items{0};
     std::uint32_t sm_count{148};
     std::uint32_t max_descs{0};
-    std::size_t off_counts{0}, off_tokens{0}, off_positions{0}, off_slots{0}, off_copies{0},
-        off_lanes{0}, off_items{0}, off_descs{0}, step_bytes{0};
+    std::size_t off_counts{0}, off_result{0}, off_tokens{0}, off_positions{0}, off_slots{0},
+        off_copies{0}, off_lanes{0}, off_items{0}, off_descs{0}, step_bytes{0};
     std::uint8_t* step_dev{nullptr};
     std::uint8_t* step_host{nullptr};
-    std::uint32_t* host_tokens{nullptr};
+    // Result block of a step: the step's error word (kResultHeader bytes, the
+    // word first), then the greedy token ids. It sits inside the uploaded
+    // part of the step record, so every upload clears the error word; the
+    // kernels of the step report errors there (first error wins), and one
+    // device-to-host copy brings back the word and the tokens together.
+    static constexpr std::size_t kResultHeader = 16;
+    unsigned int* status_dev{nullptr};
+    std::uint8_t* host_result{nullptr};
+    std::uint32_t const* host_tokens{nullptr};
 
     cudaEvent_t ev_begin{nullptr};
     cudaEvent_t ev_end{nullptr};
@@ -141,7 +149,7 @@ struct CudaTinyLlamaModelRunner::Impl {
         cudaFree(ws);
         cudaFree(step_dev);
         cudaFreeHost(step_host);
-        cudaFreeHost(host_tokens);
+        cudaFreeHost(host_result);
         if (capture_stream != nullptr) cudaStreamDestroy(capture_stream);
         if (ev_begin != nullptr) cudaEventDestroy(ev_begin);
         if (ev_end != nullptr) cudaEventDestroy(ev_end);
@@ -157,6 +165,7 @@ struct CudaTinyLlamaModelRunner::Impl {
         BatchPlans const& p, bool want_logits, ModelRunnerDebugCapture* debug);
     CudaModelRunnerStatus runStep(std::uint32_t batch, bool has_copies, bool want_logits,
         ModelRunnerDebugCapture* debug);
+    CudaModelRunnerStatus finishStep(std::uint32_t batch, std::vector<float>* logits_out, char const* what);
 };
 
 CudaTinyLlamaModelRunner::CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept
@@ -269,6 +278,9 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
     for (std::uint32_t l = 0; l < c.layer_count; ++l) {
         kk::gemmSetL2Prefetch(*out.o[l], layers[l].w_down,
             kk_gemm_packed_bytes(c.hidden_size, c.intermediate_size));
+        for (kk::GemmPlan* g : {out.qkv[l].get(), out.o[l].get(), out.gu[l].get(), out.down[l].get()}) {
+            kk::gemmSetStatus(*g, status_dev);
+        }
     }
     kk_gemm_desc lm = normedInput(base(lm_head, c.vocabulary_size, c.hidden_size, hidden, KK_EPI_ARGMAX,
         nullptr, 0));
@@ -282,6 +294,8 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         || !kk::gemmSetNormPartials(*out.lm_head_logits, sq_mlp_out, sq_tiles)) {
         return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "LM head plan rejected");
     }
+    kk::gemmSetStatus(*out.lm_head, status_dev);
+    kk::gemmSetStatus(*out.lm_head_logits, status_dev);
     return {};
 }
 
@@ -301,7 +315,7 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
     CudaModelRunnerStatus s;
     if (has_copies) {
         s = check(kk::kvCopyDevCount(&pools, 0, c.layer_count, stepDev<kk_kv_copy>(off_copies),
-                      stepDev<std::uint32_t>(off_counts) + 1, batch, stream), "copy-on-write");
+                      stepDev<std::uint32_t>(off_counts) + 1, batch, status_dev, stream), "copy-on-write");
         if (!s.ok()) return s;
     }
     // Embedding gather starts the residual stream; the first projection
@@ -317,12 +331,12 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::enqueueForward(cudaStream_
         }
     }
     for (std::uint32_t l = 0; l < c.layer_count; ++l) {
-        LayerWeights const& w = layers[l];
         if (!(s = check(kk::gemmRun(*p.qkv[l], stream), "qkv projection")).ok()
             || !(s = check(kk::attentionDevCount(&pools, l, c.attention_head_count,
                      stepDev<kk_page_desc>(off_descs), stepDev<kk_attn_lane>(off_lanes), batch,
                      stepDev<kk_attn_item>(off_items), stepDev<std::uint32_t>(off_counts), max_items,
-                     q, qrow, attn, qrow, scale, attn_ws, attn_ws_bytes, stream), "paged attention")).ok()
+                     q, qrow, attn, qrow, scale, attn_ws, attn_ws_bytes, status_dev, stream),
+                     "paged attention")).ok()
             || !(s = check(kk::gemmRun(*p.o[l], stream), "output projection")).ok()
             || !(s = check(kk::gemmRun(*p.gu[l], stream), "gate/up projection")).ok()
             || !(s = check(kk::gemmRun(*p.down[l], stream), "down projection")).ok()) {
@@ -403,6 +417,54 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::runStep(std::uint32_t batc
     kk_set_pdl(0);
     cudaEventRecord(ev_end, stream);
     return s;
+}
+
+char const* deviceErrorName(unsigned int code)
+{
+    switch (code) {
+    case 1: return "a bounded device wait ran out";
+    case 2: return "a page descriptor or KV slot outside its pool";
+    case 3: return "an inconsistent work list";
+    default: return "an unknown device error";
+    }
+}
+
+// Brings back the step's result block (error word + greedy ids) and the
+// optional logits, waits for the step, and turns a device-reported error into
+// ExecutionFailed. After such an error the split-attention completion
+// counters and the LM head's counter may be left mid-count by the CTAs that
+// gave up; both are cleared so that the next step starts clean.
+CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::finishStep(std::uint32_t batch,
+    std::vector<float>* logits_out, char const* what)
+{
+    std::size_t const bytes = kResultHeader + std::size_t(batch) * 4u;
+    cudaError_t e = cudaMemcpyAsync(host_result, status_dev, bytes, cudaMemcpyDeviceToHost, stream);
+    last_d2h += bytes;
+    if (e == cudaSuccess && logits_out != nullptr) {
+        std::size_t const n = std::size_t(batch) * cfg.vocabulary_size;
+        logits_out->resize(n);
+        e = cudaMemcpyAsync(logits_out->data(), logits, n * 4u, cudaMemcpyDeviceToHost, stream);
+        last_d2h += n * 4u;
+    }
+    if (e == cudaSuccess) {
+        e = cudaStreamSynchronize(stream);
+    }
+    if (e != cudaSuccess) {
+        return failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
+            std::string(what) + " failed: " + cudaGetErrorString(e));
+    }
+    unsigned int code = 0;
+    std::memcpy(&code, host_result, sizeof(code));
+    if (code == 0) {
+        return {};
+    }
+    cudaError_t const reset = cudaMemsetAsync(attn_ws, 0, align256(std::size_t(options.max_batch_size) * 4u),
+        stream);
+    if (reset == cudaSuccess && cudaMemsetAsync(argmax_ws, 0, 256, stream) == cudaSuccess) {
+        cudaStreamSynchronize(stream);
+    }
+    return failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(code),
+        std::string(what) + " failed: the device reported " + deviceErrorName(code));
 }
 
 // One fused step over every valid lane of `items`.
@@ -523,22 +585,18 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
     CudaModelRunnerStatus s = e == cudaSuccess
         ? im.runStep(B, n_copies != 0, want_logits, debug)
         : cudaFailure(static_cast<int>(e), "upload step inputs");
+    phase(2);
     if (s.ok()) {
-        e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, B * 4u, cudaMemcpyDeviceToHost, im.stream);
-        im.last_d2h += B * 4u;
-        if (e == cudaSuccess && logits_out != nullptr) {
-            logits_out->resize(c.vocabulary_size);
-            e = cudaMemcpyAsync(logits_out->data(), im.logits, c.vocabulary_size * 4u,
-                cudaMemcpyDeviceToHost, im.stream);
-            im.last_d2h += c.vocabulary_size * 4u;
-        }
-        phase(2);
-        if (e == cudaSuccess) {
-            e = cudaStreamSynchronize(im.stream);
-        }
-        if (e != cudaSuccess) {
-            s = failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
-                std::string("decode step failed: ") + cudaGetErrorString(e));
+        s = im.finishStep(B, logits_out, "decode step");
+    }
+    if (s.ok() && logits_out != nullptr) {
+        // Rows of the step are its lanes; hand them back in item order
+        // (rows of items that did not enter the step are zero).
+        std::size_t const V = c.vocabulary_size;
+        std::vector<float> rows = std::move(*logits_out);
+        logits_out->assign(items.size() * V, 0.0f);
+        for (std::uint32_t b = 0; b < B; ++b) {
+            std::copy(rows.begin() + b * V, rows.begin() + (b + 1) * V, logits_out->begin() + lane_index[b] * V);
         }
     }
     if (!s.ok()) {
@@ -688,15 +746,7 @@ GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId i
     CudaModelRunnerStatus s = e == cudaSuccess ? im.runStep(n, n_copies != 0, false, nullptr)
                                                : cudaFailure(static_cast<int>(e), "upload step inputs");
     if (s.ok()) {
-        e = cudaMemcpyAsync(im.host_tokens, im.out_tokens, n * 4u, cudaMemcpyDeviceToHost, im.stream);
-        im.last_d2h += n * 4u;
-        if (e == cudaSuccess) {
-            e = cudaStreamSynchronize(im.stream);
-        }
-        if (e != cudaSuccess) {
-            s = failure(CudaModelRunnerError::ExecutionFailed, static_cast<int>(e),
-                std::string("prefill step failed: ") + cudaGetErrorString(e));
-        }
+        s = im.finishStep(n, nullptr, "prefill step");
     }
     if (!s.ok()) {
         im.last_error = s.detail;
@@ -773,6 +823,12 @@ GenerationBatchResult CudaTinyLlamaModelRunner::generationForwardBatch(
     std::vector<GenerationBatchItem> const& batch)
 {
     return runBatch(*impl_, batch, false, nullptr, nullptr);
+}
+
+GenerationBatchResult CudaTinyLlamaModelRunner::generationForwardBatchLogits(
+    std::vector<GenerationBatchItem> const& batch, std::vector<float>& logits)
+{
+    return runBatch(*impl_, batch, true, nullptr, &logits);
 }
 
 GenerationStepResult CudaTinyLlamaModelRunner::generationForwardToken(RequestId request_id,
@@ -1032,7 +1088,6 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     std::size_t const o_attn = region(std::size_t(im->bpad) * H * 2);
     std::size_t const o_act = region(std::size_t(im->bpad) * I * 2);
     std::size_t const o_logits = region(std::size_t(bmax) * V * 4);
-    std::size_t const o_tok = region(std::size_t(bmax) * 4);
     im->attn_ws_bytes = kk_attention_workspace_bytes(bmax, im->max_items, c.attention_head_count,
         c.head_dimension);
     std::size_t const o_attn_ws = region(im->attn_ws_bytes);
@@ -1056,7 +1111,6 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     im->attn = reinterpret_cast<std::uint16_t*>(im->ws + o_attn);
     im->act = reinterpret_cast<std::uint16_t*>(im->ws + o_act);
     im->logits = reinterpret_cast<float*>(im->ws + o_logits);
-    im->out_tokens = reinterpret_cast<std::uint32_t*>(im->ws + o_tok);
     im->attn_ws = im->ws + o_attn_ws;
     im->argmax_ws = im->ws + o_argmax;
     im->sq_embed = reinterpret_cast<float*>(im->ws + o_sq_embed);
@@ -1065,6 +1119,7 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
 
     off = 0;
     im->off_counts = region(16);
+    im->off_result = region(CudaTinyLlamaModelRunner::Impl::kResultHeader + std::size_t(bmax) * 4);
     im->off_tokens = region(std::size_t(bmax) * 4);
     im->off_positions = region(std::size_t(bmax) * 4);
     im->off_slots = region(std::size_t(bmax) * sizeof(kk_kv_slot));
@@ -1078,7 +1133,13 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         e = cudaMallocHost(reinterpret_cast<void**>(&im->step_host), im->step_bytes);
     }
     if (e == cudaSuccess) {
-        e = cudaMallocHost(reinterpret_cast<void**>(&im->host_tokens), std::size_t(bmax) * 4);
+        e = cudaMallocHost(reinterpret_cast<void**>(&im->host_result),
+            CudaTinyLlamaModelRunner::Impl::kResultHeader + std::size_t(bmax) * 4);
+    }
+    if (e == cudaSuccess) {
+        im->status_dev = reinterpret_cast<unsigned int*>(im->step_dev + im->off_result);
+        im->out_tokens = reinterpret_cast<std::uint32_t*>(im->step_dev + im->off_result + CudaTinyLlamaModelRunner::Impl::kResultHeader);
+        im->host_tokens = reinterpret_cast<std::uint32_t const*>(im->host_result + CudaTinyLlamaModelRunner::Impl::kResultHeader);
     }
     if (e == cudaSuccess) {
         e = cudaStreamCreateWithFlags(&im->capture_stream, cudaStreamNonBlocking);

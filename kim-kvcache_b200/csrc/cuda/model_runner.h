@@ -105,6 +105,15 @@ public:
         std::vector<GenerationBatchItem> const& batch) override;
     [[nodiscard]] std::uint32_t generationMaxBatchSize() const noexcept override;
 
+    // generationForwardBatch that also returns every lane's FP32 logits
+    // (logits[i * vocab ...], row i = batch item i; rows of failed items are
+    // zero). The step runs the same kernels outside the captured graph (the
+    // LM head also stores its logits). No counterpart in the reference, whose
+    // batched path returns tokens only; used to check the fused step lane by
+    // lane against the reference arithmetic.
+    [[nodiscard]] GenerationBatchResult generationForwardBatchLogits(
+        std::vector<GenerationBatchItem> const& batch, std::vector<float>& logits);
+
     // Fused multi-token prefill (no counterpart in the reference, which feeds
     // prompts one position per wave): the prompt tokens at positions
     // first_position.. of one request run through the decode step as one

@@ -89,3 +89,59 @@ def write_archive(directory: str | os.PathLike, cfg: dict, seed: int, std: float
     manifest.write_text("\n".join(lines) + "\n")
     stamp.write_text(key)
     return str(manifest), str(data), (kept if keep_weights else None)
+
+
+# ---- decode workloads of the benchmark configs --------------------------------
+
+# The reference benchmark seed (include/kim-kv/benchmark/benchmark.h:123).
+BENCH_SEED = 0x4B564341434845
+
+
+def decode_workload(config: str) -> dict:
+    """Seeded decode workload of a BASELINE config: name, batch and per-lane
+    context lengths. Every replica (rank) gets the same contexts, so per-GPU
+    work is identical and the max-over-ranks time measures the GPUs, not the
+    draw."""
+    import random
+    rng = random.Random(BENCH_SEED)
+    if config == "c2":
+        return dict(name="c2: TinyLlama-shape greedy decode, batch 1, prompt 6 (+32 new)",
+                    batch=1, contexts=[6])
+    if config == "c5":
+        return dict(name="c5: TinyLlama-shape decode replicas, 64 requests/GPU, ctx~U[64,1024]",
+                    batch=64, contexts=[rng.randint(64, 1024) for _ in range(64)])
+    return dict(name="c4: TinyLlama-shape decode, 32 lanes/GPU, ctx~U[1024,4096] extent+micro pages",
+                batch=32, contexts=[rng.randint(1024, 4096) for _ in range(32)])
+
+
+def pool_capacities(contexts: list[int], extra_tokens: int) -> tuple[int, int]:
+    """(micro, extent) page capacities for lanes of these contexts that decode
+    `extra_tokens` more tokens each with auto-promotion on: room for every
+    64-token run that promotion folds, plus micro pages for the tails."""
+    B = len(contexts)
+    extent = sum((c + extra_tokens) // 64 for c in contexts) + B
+    micro = B * 16 + (sum(contexts) + B * extra_tokens) // 8 + 64
+    return micro, extent
+
+
+def build_decode_prefixes(R: dict, K: dict, backend, pools, contexts: list[int], cfg: dict,
+                          fill_seed: int, stream) -> None:
+    """Lane i (request i + 1) gets contexts[i] tokens of committed KV: the
+    runtime's own append -> seal -> promote path lays out the pages (64-token
+    extents for the body, 8-token micro pages for the tail), then every page
+    of both pools is filled with seeded FP16 values in [-0.35, 0.35) (the
+    prefix K/V a prefill would have written)."""
+    import ctypes as C
+    for i, ctx in enumerate(contexts):
+        rid = i + 1
+        assert R["backend_create_request"](backend, rid) == 0
+        assert R["backend_append"](backend, rid, ctx) == 0
+        R["backend_seal"](backend, rid)
+        for begin in range(0, (ctx // 64) * 64, 64):
+            assert R["backend_promote"](backend, rid, begin, stream) == 0
+    row = cfg["kv_heads"] * cfg["head_dim"]
+    L = cfg["layers"]
+    micro_elems = pools.micro_capacity * L * 2 * 8 * row
+    extent_elems = pools.extent_capacity * L * 2 * 64 * row
+    assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, fill_seed, 0.35, stream) == 0
+    assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, fill_seed + 1, 0.35, stream) == 0

@@ -16,6 +16,34 @@ LIB = HERE / "_build" / "libkk_oracle.so"
 REF_LIB = HERE / "_ref" / "libkimkv_ref.so"
 
 
+def reference_dir() -> Path | None:
+    """The reference source tree used to build oracle/_ref: the directory named
+    by KK_REFERENCE_DIR, else BASELINE.json's `reference_path`; None when
+    neither names an existing tree (as on a machine without the reference,
+    where the prebuilt oracle/_ref library or the committed golden fixtures
+    stand in)."""
+    import json
+    import os
+    cand = os.environ.get("KK_REFERENCE_DIR")
+    if not cand:
+        baseline = HERE.parent / "BASELINE.json"
+        if baseline.exists():
+            cand = json.loads(baseline.read_text()).get("reference_path")
+    if cand and (Path(cand) / "src").is_dir():
+        return Path(cand)
+    return None
+
+
+def build_ref() -> bool:
+    """Builds oracle/_ref from the reference tree when one is available."""
+    ref = reference_dir()
+    if ref is None:
+        return False
+    subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True,
+                   capture_output=True)
+    return REF_LIB.exists()
+
+
 class Config(C.Structure):
     _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("layers", C.c_uint32),
                 ("q_heads", C.c_uint32), ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32),

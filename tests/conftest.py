@@ -51,12 +51,13 @@ def kk_lib(kk):
 
 @pytest.fixture(scope="session")
 def ref_lib():
-    path = ROOT / "oracle" / "_ref" / "libkimkv_ref.so"
-    if not path.exists() and Path("/root/reference/src").exists():
-        subprocess.run(["make", "-C", str(ROOT / "oracle"), "ref"], check=True,
-                       capture_output=True)
+    import kk_oracle_py
+    path = kk_oracle_py.REF_LIB
     if not path.exists():
-        pytest.skip("reference oracle library not built (no reference tree here)")
+        kk_oracle_py.build_ref()
+    if not path.exists():
+        pytest.skip("reference oracle library not built: no reference tree here (set "
+                    "KK_REFERENCE_DIR, or BASELINE.json reference_path, to build it)")
     return C.CDLL(str(path))
 
 

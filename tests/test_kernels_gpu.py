@@ -377,6 +377,44 @@ def test_paged_attention_reports_bad_descriptor(kk, K, attn_variant, variant):
     # lane 1's output is unspecified (its table is corrupt); the other lanes are unaffected
 
 
+def test_paged_attention_wait_timeout_is_reported_not_hung(kk, K):
+    """A bounded wait that runs out: the test hook makes CTA 0 of the TMA
+    kernel drop its first stage (no copy, no arrival) and lowers the wait
+    limit to 1 ms. The launch ends on its own, reports kErrWaitTimeout (1),
+    and the next launch with the hook cleared is correct again."""
+    pools, micro, extent = make_pools(kk, 1, 4, 64, 64, 8, seed=21)
+    tables = build_tables([300, 17, 140], 64, 8, random.Random(4))
+    descs, lanes = descs_and_lanes(kk, tables)
+    items = (kk.AttnItem * 64)()
+    n_items = K["attention_plan_balanced"](descs, lanes, 3, 8, items, 64)
+    q = (torch.randn(3, 32 * 64) / 8).half().cuda()
+    out = torch.zeros(3, 32 * 64, dtype=torch.half, device="cuda")
+    ws = torch.zeros(K["attention_workspace_bytes"](3, n_items, 32, 64), dtype=torch.uint8,
+                     device="cuda")
+    d_descs, d_lanes, d_items = to_device_bytes(descs), to_device_bytes(lanes), to_device_bytes(items)
+
+    def run():
+        rc = K["paged_decode_attention"](C.byref(pools), 0, 32, p(d_descs), p(d_lanes), 3, p(d_items),
+                                         n_items, p(q), 32 * 64, p(out), 32 * 64, 0.125, p(ws),
+                                         ws.numel(), None)
+        assert rc == 0
+        torch.cuda.synchronize()
+
+    assert K["debug_attention_fault"](0, 1_000_000) == 0
+    try:
+        run()
+    finally:
+        assert K["debug_attention_fault"](0xFFFFFFFF, 0) == 0
+    assert K["device_status"](None) == 1  # kErrWaitTimeout, then cleared
+    ws.zero_()                            # completion counters left mid-count by the aborted CTA
+    run()
+    assert K["device_status"](None) == 0
+    for b, tbl in enumerate(tables):
+        k, v = gather_kv(micro, extent, tbl, 0)
+        ref = attention_ref(q[b].view(32, 64), k, v, 0.125)
+        torch.testing.assert_close(out[b].view(32, 64).float(), ref, atol=2e-3, rtol=2e-2)
+
+
 def test_attention_variant_switch_rejects_unknown(kk, K, attn_variant):
     assert K["attention_set_variant"](7) == kk.KK_EINVAL
     assert K["attention_set_variant"](-1) == kk.KK_EINVAL

@@ -202,6 +202,107 @@ def test_injected_failures_roll_back_one_lane(kk, tmp_path):
     s.close()
 
 
+EXECUTION_FAILED = 9  # EngineKvError::ExecutionFailed
+
+
+def _last_error(s):
+    buf = C.create_string_buffer(512)
+    s.R["runner_last_error"](s.runner, buf, 512)
+    return buf.value.decode()
+
+
+@pytest.mark.parametrize("graphs", [0, 1])
+def test_device_wait_timeout_fails_the_step_and_rolls_back(kk, tmp_path, graphs):
+    """A device-detected error fails the fused step at commit: the test hook
+    makes CTA 0 of every attention launch drop a stage with a 1 ms wait limit,
+    so a bounded wait runs out and the step's error word is set. Every lane
+    reports failure, every reservation rolls back (committed lengths,
+    tables and invariants unchanged, no transaction left open), and the same
+    positions decode correctly once the hook is cleared (reference: a
+    completion failure surfaces as ExecutionFailed and rolls the transaction
+    back, src/cuda/engine/transaction.cpp:84-120)."""
+    s = Stack(kk, tmp_path, SMALL, batch=4, graphs=graphs)
+    K = kk.kernels()
+    ids = [1, 2, 3]
+    for rid in ids:
+        s.create(rid)
+    toks, pos = [5, 6, 7], [0, 0, 0]
+    for _ in range(9):   # a few tokens of context, a micro page filled and sealed
+        got, ok = s.batch(ids, toks, pos)
+        want, logits, _ = s.oracle.forward(ids, toks, pos, want_hidden=False)
+        assert ok == [1, 1, 1]
+        assert_greedy(got, want, logits)
+        toks, pos = [int(w) for w in want], [p_ + 1 for p_ in pos]
+    snap0 = s.snapshot()
+    assert K["debug_attention_fault"](0, 1_000_000) == 0
+    try:
+        got, ok = s.batch(ids, toks, pos)
+    finally:
+        assert K["debug_attention_fault"](0xFFFFFFFF, 0) == 0
+    assert ok == [0, 0, 0]
+    assert "bounded device wait" in _last_error(s)
+    snap = s.snapshot()
+    assert snap.committed_token_count == snap0.committed_token_count == 27
+    assert snap.active_transaction_count == 0
+    assert snap.allocated_micro_pages == snap0.allocated_micro_pages
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    # the module-global words of the public entry points saw nothing
+    assert K["device_status"](s.stream) == 0
+    got, ok = s.batch(ids, toks, pos)
+    want, logits, _ = s.oracle.forward(ids, toks, pos, want_hidden=False)
+    assert ok == [1, 1, 1]
+    assert_greedy(got, want, logits)
+    assert s.snapshot().committed_token_count == 30
+    s.close()
+
+
+def test_per_layer_commit_fails_on_device_error(kk):
+    """The per-layer transaction SPI: a bounded wait that runs out inside
+    attendLayer fails the transaction at commit with ExecutionFailed and
+    rolls it back; a transaction on the same stream after the error commits."""
+    R, K = kk.runtime(), kk.kernels()
+    L, hkv, D, hq = 2, 4, 64, 32
+    backend = R["backend_create"](L, hkv, D, hq, hq * 512 * 4, 64, 4)
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert R["backend_create_request"](backend, 1) == 0
+    assert R["backend_append"](backend, 1, 70) == 0
+    g = torch.Generator().manual_seed(9)
+    q = (torch.randn(hq * D, generator=g) / 8).half().cuda()
+    out = torch.zeros_like(q)
+    ws = torch.zeros(hq * 512 * 4, dtype=torch.uint8, device="cuda")
+
+    def token(length, fault):
+        st = C.c_int(0)
+        t = R["txn_reserve"](backend, 1, length, stream, C.byref(st))
+        assert t and st.value == 0
+        for layer in range(L):
+            k = (torch.randn(hkv * D, generator=g) / 8).half().cuda()
+            v = (torch.randn(hkv * D, generator=g) / 8).half().cuda()
+            assert R["txn_write_layer"](t, layer, k.data_ptr(), v.data_ptr()) == 0
+            if fault:
+                assert K["debug_attention_fault"](0, 1_000_000) == 0
+            try:
+                assert R["txn_attend_layer"](t, layer, q.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                                             ws.numel(), 0.125) == 0
+                torch.cuda.synchronize()
+            finally:
+                assert K["debug_attention_fault"](0xFFFFFFFF, 0) == 0
+        rc = R["txn_commit"](t)
+        R["txn_destroy"](t)
+        return rc
+
+    assert token(70, fault=True) == EXECUTION_FAILED
+    snap = kk.BackendSnapshot()
+    R["backend_snapshot"](backend, C.byref(snap))
+    assert snap.committed_token_count == 70 and snap.active_transaction_count == 0
+    assert R["backend_check_invariants"](backend) == 1
+    assert token(70, fault=False) == 0
+    R["backend_snapshot"](backend, C.byref(snap))
+    assert snap.committed_token_count == 71 and snap.active_transaction_count == 0
+    assert R["backend_check_invariants"](backend) == 1
+    R["backend_destroy"](backend)
+
+
 class _DevArray:
     def __init__(self, ptr, n):
         self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<u2", "data": (ptr, False),
