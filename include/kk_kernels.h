@@ -291,13 +291,16 @@ typedef struct kk_gemm_desc {
     uint32_t weight_layout;    /* KK_W_ROW_MAJOR, or KK_W_PACKED: weight holds
                                   kk_gemm_pack_weight output for (M, K) */
     /* Fused RMSNorm of the input rows (replaces a separate rmsNormBatchKernel,
-     * src/cuda/model/kernels.cu:48-124): when norm_input is set, every output
-     * column n is scaled by rsqrt(mean_k norm_input[n][k]^2 + norm_eps) before
-     * the epilogue. With x = norm_input and W packed with the norm weights as
-     * column scale (kk_gemm_pack_weight_scaled), Y = RMSNorm(x) W^T. */
+     * src/cuda/model/kernels.cu:48-124, at the same FP16 rounding point): when
+     * norm_input is set, every X tile is normalised in shared memory before
+     * the tensor cores read it, X'[n][k] = half(x[n][k] * r[n] * g[k]) with
+     * r[n] = 1 / sqrt(mean_k norm_input[n][k]^2 + norm_eps) and g =
+     * norm_weight (1 when NULL); then Y = X' W^T. With x = norm_input this is
+     * the reference's half(RMSNorm(x)) followed by the projection. */
     const uint16_t* norm_input; /* [N][norm_stride] fp16, 16-byte aligned, or NULL */
     uint32_t norm_stride;
     float norm_eps;
+    const uint16_t* norm_weight; /* [K] fp16, 16-byte aligned, or NULL */
 } kk_gemm_desc;
 
 #define KK_W_ROW_MAJOR 0

@@ -831,7 +831,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                 // are never trusted (0 * NaN would be NaN).
                 std::uint32_t const mask0 = (2 * c4 < v0 ? 0x0000ffffu : 0u) | (2 * c4 + 1 < v0 ? 0xffff0000u : 0u);
                 std::uint32_t const mask1 = (2 * c4 < v1 ? 0x0000ffffu : 0u) | (2 * c4 + 1 < v1 ? 0xffff0000u : 0u);
-                std::uint32_t pb[NT][2];
+                // P is handed to the FP16 PV product as hi + lo halves
+                // (p = hi + lo to ~2^-22 relative), so the weights keep FP32
+                // precision as in the reference's softmax (which multiplies
+                // FP32 probabilities into V, paged_decode_kernels.cu:420-470).
+                std::uint32_t pb[NT][2], pl[NT][2];
 #pragma unroll
                 for (int nt = 0; nt < NT; ++nt) {
                     float p[4];
@@ -858,8 +862,12 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     }
                     // P^T fragments (token rows, head columns) transposed into
                     // the B layout of the PV product (k = token, n = head).
-                    pb[nt][0] = transpose8x8(pack_half2(p[0], p[1]));
-                    pb[nt][1] = transpose8x8(pack_half2(p[2], p[3]));
+                    __half2 const h01 = __floats2half2_rn(p[0], p[1]);
+                    __half2 const h23 = __floats2half2_rn(p[2], p[3]);
+                    pb[nt][0] = transpose8x8(*reinterpret_cast<std::uint32_t const*>(&h01));
+                    pb[nt][1] = transpose8x8(*reinterpret_cast<std::uint32_t const*>(&h23));
+                    pl[nt][0] = transpose8x8(pack_half2(p[0] - __low2float(h01), p[1] - __high2float(h01)));
+                    pl[nt][1] = transpose8x8(pack_half2(p[2] - __low2float(h23), p[3] - __high2float(h23)));
                 }
 #pragma unroll
                 for (std::uint32_t j = 0; j < 4; ++j) {
@@ -871,6 +879,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     for (int nt = 0; nt < NT; ++nt) {
                         mma16816(o[nt][j], va[0] & mask0, va[1] & mask0, va[2] & mask1, va[3] & mask1,
                             pb[nt][0], pb[nt][1]);
+                        mma16816(o[nt][j], va[0] & mask0, va[1] & mask0, va[2] & mask1, va[3] & mask1,
+                            pl[nt][0], pl[nt][1]);
                     }
                 }
             }

@@ -114,9 +114,10 @@ struct GemmArgs {
     std::uint32_t N;
     std::uint32_t split;
     std::uint32_t kb_total;
-    __half const* norm_x;           // RMS-normalise the output by the rows of norm_x (or null)
+    __half const* norm_x;           // RMS-normalise the X rows by the rows of norm_x (or null)
     std::uint32_t norm_stride;
     float norm_eps;
+    __half const* norm_w;           // RMSNorm weight [K] applied with the factor (null: 1)
     // L2 prefetch of bytes that a later kernel of the step reads (or null):
     // every CTA requests its share after the dependency wait, while this
     // kernel's own weights are already on chip.
@@ -151,6 +152,13 @@ __device__ __forceinline__ void bulk_copy_to_peer(std::uint32_t dst, void const*
         "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
         ::"r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(bar)
         : "memory");
+}
+
+// Barrier of `count` threads (multiple of 32) on hardware barrier `id` (id 0
+// is __syncthreads).
+__device__ __forceinline__ void named_barrier_sync(std::uint32_t id, std::uint32_t count)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ void cluster_arrive()
@@ -226,6 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(rbar + 1);
     int* flag = reinterpret_cast<int*>(tmem_slot + 4);
     float* rnorm = reinterpret_cast<float*>(flag + 4);  // [BN] per-column RMS factors
+    // With a fused RMSNorm the X tile of stage s lands on xfull[s] and full[s]
+    // completes only once warps 2-3 normalised it in place.
+    std::uint64_t* xfull = reinterpret_cast<std::uint64_t*>(rnorm + BN);
 
     std::uint32_t const tid = threadIdx.x;
     std::uint32_t const warp = tid / 32;
@@ -241,11 +252,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint32_t const kb_begin = rank * args.kb_total / S;
     std::uint32_t const nk = (rank + 1) * args.kb_total / S - kb_begin;
     constexpr std::uint32_t kStageBytes = kTileWBytes + BN * 128;
+    // Fused RMSNorm: X tiles are normalised in shared memory before the MMA
+    // reads them, X'[n][k] = half(x[n][k] * r[n] * g[k]), the rounding point
+    // of the reference's rmsNormBatchKernel (its output is FP16).
+    bool const xnorm = args.norm_x != nullptr;
+    std::uint32_t const w_expect = xnorm ? kTileWBytes : kStageBytes;
 
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 1);
+            mbar_init(&full[s], xnorm ? 2 : 1);  // producer (+ the normalising warps)
             mbar_init(&empty[s], 1);
+            mbar_init(&xfull[s], 1);
         }
         mbar_init(accum, 1);
         mbar_init(rbar, 1);
@@ -290,15 +307,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     static_cast<int>((kb_begin + i) * kBK), static_cast<int>(m_tile * kBM), policy);
             }
         };
+        // X tile i of the CTA: into full[] directly, or into xfull[] for the
+        // normalising warps.
+        auto load_x = [&](std::uint32_t s, std::uint32_t i) {
+            std::uint64_t* bar = &full[s];
+            if (xnorm) {
+                bar = &xfull[s];
+                mbar_arrive_expect_tx(bar, BN * 128u);
+            }
+            tma_load_2d(x_stage + s * BN * 128, &tm_x, bar, static_cast<int>((kb_begin + i) * kBK), 0);
+        };
         for (std::uint32_t i = 0; i < pre; ++i) {
-            mbar_arrive_expect_tx(&full[i], kStageBytes);
+            mbar_arrive_expect_tx(&full[i], w_expect);
             load_w(i, i);
         }
         pdl_wait();
         KK_GEMM_STAMP(1)
         for (std::uint32_t i = 0; i < pre; ++i) {
-            tma_load_2d(x_stage + i * BN * 128, &tm_x, &full[i],
-                static_cast<int>((kb_begin + i) * kBK), 0);
+            load_x(i, i);
         }
         if (args.l2_pf != nullptr) {
             L2PrefetchShare pf;
@@ -311,10 +337,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             if (!mbar_wait(&empty[s], ((i / kStages) - 1) & 1u, st)) {
                 break;
             }
-            mbar_arrive_expect_tx(&full[s], kStageBytes);
+            mbar_arrive_expect_tx(&full[s], w_expect);
             load_w(s, i);
-            tma_load_2d(x_stage + s * BN * 128, &tm_x, &full[s],
-                static_cast<int>((kb_begin + i) * kBK), 0);
+            load_x(s, i);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer.
@@ -367,50 +392,88 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         }
     }
-    if (args.norm_x != nullptr && args.sq_in != nullptr && warp >= 2) {
-        // While the tile streams: RMSNorm factors of this CTA's output columns
-        // from the producer's per-tile sums of squares, one thread per column,
-        // every partial requested at once and summed in tile order.
-        std::uint32_t const c0n = rank * args.N / S;
-        std::uint32_t const c1n = (rank + 1) * args.N / S;
-        for (std::uint32_t j = tid - 64u; c0n + j < c1n; j += 64u) {
-            float sum = 0.f;
-            for (std::uint32_t t0 = 0; t0 < args.sq_tiles; t0 += 16u) {
-                float v[16];
+    if (xnorm && warp >= 2) {
+        // Warps 2-3: the RMS factor of every batch row, then each X tile
+        // normalised in place as it lands.
+        std::uint32_t const t = tid - 64u;
+        if (args.sq_in != nullptr) {
+            // From the producing kernel's per-tile sums of squares, one thread
+            // per row, every partial requested at once and summed in tile order.
+            for (std::uint32_t n = t; n < static_cast<std::uint32_t>(BN); n += 64u) {
+                float sum = 0.f;
+                for (std::uint32_t t0 = 0; n < args.N && t0 < args.sq_tiles; t0 += 16u) {
+                    float v[16];
 #pragma unroll
-                for (std::uint32_t t = 0; t < 16u; ++t) {
-                    v[t] = t0 + t < args.sq_tiles ? args.sq_in[(t0 + t) * kSqStride + c0n + j] : 0.f;
+                    for (std::uint32_t q = 0; q < 16u; ++q) {
+                        v[q] = t0 + q < args.sq_tiles ? args.sq_in[(t0 + q) * kSqStride + n] : 0.f;
+                    }
+#pragma unroll
+                    for (std::uint32_t q = 0; q < 16u; ++q) {
+                        sum += v[q];
+                    }
+                }
+                rnorm[n] = n < args.N ? 1.0f / sqrtf(sum / static_cast<float>(args.K) + args.norm_eps) : 0.f;
+            }
+        } else {
+            // From the rows themselves, one warp per row.
+            for (std::uint32_t n = warp - 2u; n < static_cast<std::uint32_t>(BN); n += 2u) {
+                float sum = 0.f;
+                __half const* xr = args.norm_x + std::uint64_t(n) * args.norm_stride;
+                for (std::uint32_t k = lane * 8u; n < args.N && k < args.K; k += 256u) {
+                    uint4 const raw = *reinterpret_cast<uint4 const*>(xr + k);
+                    __half const* h = reinterpret_cast<__half const*>(&raw);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) {
+                        float const f = __half2float(h[e]);
+                        sum += f * f;
+                    }
                 }
 #pragma unroll
-                for (std::uint32_t t = 0; t < 16u; ++t) {
-                    sum += v[t];
+                for (int o = 16; o > 0; o >>= 1) {
+                    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                }
+                if (lane == 0) {
+                    rnorm[n] = n < args.N ? 1.0f / sqrtf(sum / static_cast<float>(args.K) + args.norm_eps) : 0.f;
                 }
             }
-            rnorm[j] = rsqrtf(sum / static_cast<float>(args.K) + args.norm_eps);
         }
-    } else if (args.norm_x != nullptr && warp >= 2) {
-        // While the tile streams: RMSNorm factors of this CTA's output columns,
-        // r[n] = rsqrt(mean_k x[n][k]^2 + eps), one warp per column.
-        std::uint32_t const c0n = rank * args.N / S;
-        std::uint32_t const c1n = (rank + 1) * args.N / S;
-        for (std::uint32_t n = c0n + (warp - 2u); n < c1n; n += 2u) {
-            __half const* xr = args.norm_x + std::uint64_t(n) * args.norm_stride;
-            float sum = 0.f;
-            for (std::uint32_t k = lane * 8u; k < args.K; k += 256u) {
-                uint4 const raw = *reinterpret_cast<uint4 const*>(xr + k);
-                __half const* h = reinterpret_cast<__half const*>(&raw);
+        named_barrier_sync(1, 64);
+        // Thread t owns 16-byte chunk t % 8 (dims 8c .. 8c+7 of the tile's 64)
+        // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
+        // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
+        std::uint32_t const c = t & 7u;
+        for (std::uint32_t i = 0; i < nk; ++i) {
+            std::uint32_t const s = i % kStages;
+            std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
+            float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+            if (args.norm_w != nullptr && k0 < args.K) {
+                uint4 const graw = *reinterpret_cast<uint4 const*>(args.norm_w + k0);
+                __half const* gh = reinterpret_cast<__half const*>(&graw);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
-                    float const f = __half2float(h[e]);
-                    sum += f * f;
+                    gv[e] = __half2float(gh[e]);
                 }
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (!mbar_wait(&xfull[s], (i / kStages) & 1u, st)) {
+                break;
             }
-            if (lane == 0) {
-                rnorm[n - c0n] = rsqrtf(sum / static_cast<float>(args.K) + args.norm_eps);
+            std::uint8_t* xs = x_stage + s * BN * 128;
+            for (std::uint32_t n = t >> 3; n < static_cast<std::uint32_t>(BN); n += 8u) {
+                uint4* chunk = reinterpret_cast<uint4*>(xs + n * 128u + ((c ^ (n & 7u)) << 4));
+                uint4 raw = *chunk;
+                __half* h = reinterpret_cast<__half*>(&raw);
+                float const r = rnorm[n];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    h[e] = __float2half_rn(__half2float(h[e]) * r * gv[e]);
+                }
+                *chunk = raw;
+            }
+            // Generic-proxy writes, read next by the tensor cores (async proxy).
+            fence_proxy_async_smem();
+            named_barrier_sync(1, 64);
+            if (t == 0) {
+                mbar_arrive(&full[s]);
             }
         }
     }
@@ -471,7 +534,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             for (std::uint32_t r = 0; r < S; ++r) {
                 acc += got ? recv[(r * cw + j) * kBM + row] : 0.f;
             }
-            red[j * kBM + row] = args.norm_x != nullptr ? acc * rnorm[j] : acc;
+            red[j * kBM + row] = acc;
         }
         // Cluster barrier phase 2, arrive: this CTA has received everything
         // (the receive mbarrier completed), so the senders' partials may go.
@@ -480,8 +543,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         cluster_arrive_relaxed();
     } else {
         for (std::uint32_t j = 0; j < cols; ++j) {
-            float const acc = part[(n0 + j) * kBM + row];
-            red[j * kBM + row] = args.norm_x != nullptr ? acc * rnorm[j] : acc;
+            red[j * kBM + row] = part[(n0 + j) * kBM + row];
         }
     }
     __syncthreads();
@@ -883,6 +945,10 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
         args.norm_x = reinterpret_cast<__half const*>(d->norm_input);
         args.norm_stride = d->norm_stride;
         args.norm_eps = d->norm_eps;
+        if ((reinterpret_cast<std::uintptr_t>(d->norm_weight) & 15u) != 0) {
+            return KK_EINVAL;
+        }
+        args.norm_w = reinterpret_cast<__half const*>(d->norm_weight);
     }
     EpiArgs& e = args.epi;
     e.kind = d->epilogue;

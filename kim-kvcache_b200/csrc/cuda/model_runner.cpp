@@ -220,18 +220,19 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         d.weight_layout = KK_W_PACKED;
         return d;
     };
-    // RMSNorm fused into the projection: rows of the residual stream are
-    // normalised inside the GEMM (the norm weight is folded into W).
-    auto normedInput = [&](kk_gemm_desc d) {
+    // RMSNorm fused into the projection: the GEMM normalises the residual
+    // rows in shared memory, half(x * r * g), before the tensor cores read them.
+    auto normedInput = [&](kk_gemm_desc d, std::uint16_t const* g) {
         d.norm_input = hidden;
         d.norm_stride = c.hidden_size;
         d.norm_eps = c.rms_norm_epsilon;
+        d.norm_weight = g;
         return d;
     };
     for (std::uint32_t l = 0; l < c.layer_count; ++l) {
         LayerWeights const& w = layers[l];
         kk_gemm_desc d = normedInput(base(w.w_qkv, qkv_rows, c.hidden_size, hidden, KK_EPI_QKV_ROPE, q,
-            c.hidden_size));
+            c.hidden_size), w.in_norm);
         d.positions = stepDev<std::uint32_t>(off_positions);
         d.slots = stepDev<kk_kv_slot>(off_slots);
         d.pools = pools;
@@ -252,7 +253,7 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
             || !make(atLayer(base(w.w_o, c.hidden_size, c.hidden_size, attn, KK_EPI_RESIDUAL, hidden,
                           c.hidden_size)), out.o.back())
             || !make(atLayer(normedInput(base(w.w_gu, 2 * c.intermediate_size, c.hidden_size, hidden,
-                          KK_EPI_SILU_PAIRS, act, c.intermediate_size))), out.gu.back())
+                          KK_EPI_SILU_PAIRS, act, c.intermediate_size), w.post_norm)), out.gu.back())
             || !make(atLayer(base(w.w_down, c.hidden_size, c.intermediate_size, act, KK_EPI_RESIDUAL, hidden,
                           c.hidden_size)), out.down.back())) {
             return failure(CudaModelRunnerError::InvalidArgument, KK_EINVAL, "projection plan rejected");
@@ -283,7 +284,7 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         }
     }
     kk_gemm_desc lm = normedInput(base(lm_head, c.vocabulary_size, c.hidden_size, hidden, KK_EPI_ARGMAX,
-        nullptr, 0));
+        nullptr, 0), final_norm);
     lm.tokens = out_tokens;
     lm.argmax_workspace = argmax_ws;
     kk_gemm_desc lm_logits = lm;
@@ -991,9 +992,10 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     // move the embedding table and norm weights into a compact row-major
     // allocation, and release the upload buffer.
     {
-        // The RMSNorm weight that precedes a projection is folded into its
-        // columns (qkv: input norm, gate/up: post-attention norm, LM head:
-        // final norm); the GEMM applies the per-row rsqrt factor itself.
+        // Projection matrices are packed as they are; the RMSNorm weight that
+        // precedes a projection is applied by the GEMM when it normalises its
+        // input rows (qkv: input norm, gate/up: post-attention norm, LM head:
+        // final norm).
         struct PackJob {
             std::uint16_t const* src;
             std::uint32_t M, K;
@@ -1002,13 +1004,13 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         };
         std::vector<PackJob> jobs;
         jobs.push_back({im->lm_head, static_cast<std::uint32_t>(V), static_cast<std::uint32_t>(H), &im->lm_head,
-            im->final_norm});
+            nullptr});
         for (LayerWeights& lw : im->layers) {
             jobs.push_back({lw.w_qkv, static_cast<std::uint32_t>(qkv_rows), static_cast<std::uint32_t>(H), &lw.w_qkv,
-                lw.in_norm});
+                nullptr});
             jobs.push_back({lw.w_o, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(H), &lw.w_o, nullptr});
             jobs.push_back({lw.w_gu, static_cast<std::uint32_t>(2 * I), static_cast<std::uint32_t>(H), &lw.w_gu,
-                lw.post_norm});
+                nullptr});
             jobs.push_back({lw.w_down, static_cast<std::uint32_t>(H), static_cast<std::uint32_t>(I), &lw.w_down,
                 nullptr});
         }

@@ -181,3 +181,77 @@ class Model:
             ptr(hidden, C.c_uint16) if hidden is not None else None, ptr(greedy, C.c_uint32))
         assert ok, "oracle forward rejected its inputs"
         return greedy, logits, hidden
+
+
+class RefModelConfig(C.Structure):
+    _fields_ = Config._fields_
+
+
+class RefModel:
+    """The reference's own model oracle (ReferenceModel of the reference's
+    runner contract test, compiled into oracle/_ref by ref_model_shim.cpp):
+    the contract archive with the reference test's weights (cfg None), or a
+    config whose weights are the given FP16 tensors (oracle order)."""
+
+    def __init__(self, cfg: dict | None = None, weights: list | None = None):
+        import tempfile
+        lib = C.CDLL(str(REF_LIB))
+        u16p = C.POINTER(C.c_uint16)
+        sig = {
+            "kref_model_create": (C.c_void_p, [C.POINTER(RefModelConfig), C.POINTER(u16p), C.c_char_p]),
+            "kref_model_destroy": (None, [C.c_void_p]),
+            "kref_model_config_of": (None, [C.c_void_p, C.POINTER(RefModelConfig)]),
+            "kref_model_tensor_count": (C.c_uint32, [C.c_void_p]),
+            "kref_model_tensor": (C.c_uint64, [C.c_void_p, C.c_uint32, u16p]),
+            "kref_model_forward": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, C.POINTER(C.c_float),
+                                             u16p]),
+            "kref_model_generate": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_uint32, C.c_uint32,
+                                              C.POINTER(C.c_uint32)]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(lib, name)
+            fn.restype, fn.argtypes = res, args
+        self.lib = lib
+        scratch = tempfile.gettempdir().encode()
+        if cfg is None:
+            self.h = lib.kref_model_create(None, None, scratch)
+        else:
+            c = RefModelConfig(cfg["hidden"], cfg["intermediate"], cfg["layers"], cfg["q_heads"],
+                               cfg["kv_heads"], cfg["head_dim"], cfg["vocab"], cfg["max_positions"],
+                               cfg["eps"], cfg["theta"])
+            keep = [np.ascontiguousarray(w, dtype=np.uint16).ravel() for w in weights]
+            arr = (u16p * len(keep))(*[ptr(w, C.c_uint16) for w in keep])
+            self.h = lib.kref_model_create(C.byref(c), arr, scratch)
+        assert self.h
+        out = RefModelConfig()
+        lib.kref_model_config_of(self.h, C.byref(out))
+        self.cfg = {name: getattr(out, name) for name, _ in RefModelConfig._fields_}
+
+    def tensors(self) -> list:
+        out = []
+        for i in range(self.lib.kref_model_tensor_count(self.h)):
+            n = self.lib.kref_model_tensor(self.h, i, None)
+            t = np.zeros(n, dtype=np.uint16)
+            self.lib.kref_model_tensor(self.h, i, ptr(t, C.c_uint16))
+            out.append(t)
+        return out
+
+    def forward(self, token: int, position: int):
+        logits = np.zeros(self.cfg["vocab"], dtype=np.float32)
+        hidden = np.zeros(self.cfg["hidden"], dtype=np.uint16)
+        assert self.lib.kref_model_forward(self.h, token, position, ptr(logits, C.c_float),
+                                           ptr(hidden, C.c_uint16))
+        return logits, hidden
+
+    def generate(self, prompt: list, max_new: int) -> list:
+        out = (C.c_uint32 * max_new)()
+        n = self.lib.kref_model_generate(self.h, (C.c_uint32 * len(prompt))(*prompt), len(prompt),
+                                         max_new, out)
+        return [out[i] for i in range(n)]
+
+    def close(self):
+        if self.h:
+            self.lib.kref_model_destroy(self.h)
+            self.h = None
+
+    __del__ = close

@@ -180,22 +180,23 @@ def test_gemm_argmax_matches_numpy(kk, K, V, N, wlayout):
 @pytest.mark.parametrize("M,Kd,N,epi", [(2560, 2048, 32, "f32"), (11264, 2048, 7, "silu"),
                                          (32000, 2048, 4, "argmax"), (300, 512, 33, "f32")])
 def test_gemm_fused_rmsnorm_matches_torch(kk, K, M, Kd, N, epi):
-    """norm_input + column-scaled packing = RMSNorm(x) (weight g) followed by
-    the projection, in one kernel."""
+    """norm_input + norm_weight = the reference's FP16 RMSNorm of x (weight g,
+    rounded to FP16 as rmsNormBatchKernel stores it) followed by the
+    projection, in one kernel: the kernel normalises its X tiles in shared
+    memory before the tensor cores read them."""
     g = torch.Generator().manual_seed(M + N)
     w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
     gw = (1.0 + 0.1 * torch.randn(Kd, generator=g)).half().cuda()
     x = (torch.randn(64, Kd, generator=g) * 3).half().cuda()
-    packed = torch.empty(K["gemm_packed_bytes"](M, Kd) // 2, dtype=torch.half, device="cuda")
-    assert K["gemm_pack_weight_scaled"](p(w), M, Kd, p(gw), p(packed), None) == 0
+    packed = packed_weight(kk, K, w)
     eps = 1e-5
     xf = x[:N].float()
-    normed = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * gw.float()).half().float()
+    normed = (xf * (1.0 / torch.sqrt(xf.pow(2).mean(-1, keepdim=True) + eps)) * gw.float()).half().float()
     ref = normed @ w.float().T
     d = kk.GemmDesc()
     d.weight, d.weight_layout, d.M, d.K = p(packed), kk.W_PACKED, M, Kd
     d.x, d.N, d.x_stride, d.x_rows = p(x), N, Kd, 64
-    d.norm_input, d.norm_stride, d.norm_eps = p(x), Kd, eps
+    d.norm_input, d.norm_stride, d.norm_eps, d.norm_weight = p(x), Kd, eps, p(gw)
     if epi == "f32":
         out = torch.zeros(N, M, device="cuda")
         d.epilogue, d.out, d.out_stride = kk.EPI_STORE_F32, p(out), M

@@ -194,3 +194,99 @@ def test_manifest_loader_matches_reference_errors(kk, kk_lib, ref_lib, tmp_path)
         ours = buf.value.decode()
         assert ref_lib.kref_sha256_range(data.encode(), C.c_uint64(off), C.c_uint64(n), buf) == 0
         assert ours == buf.value.decode() == hashlib.sha256(raw[off:off + n]).hexdigest()
+
+
+# ---- the model oracle against the reference's own ReferenceModel ------------------
+#
+# ReferenceModel (tests/cuda/cuda_model_runner_test.cpp:213-420 of the
+# reference) is test-local C++; oracle/ref_model_shim.cpp compiles that test
+# file in place into oracle/_ref and exposes it. kk_oracle.c must reproduce
+# it bit for bit: same rounding points, same summation order, same libm calls.
+
+MODEL_SMALL = dict(hidden=512, intermediate=1024, layers=3, q_heads=8, kv_heads=2, head_dim=64,
+                   vocab=1000, max_positions=512, eps=1e-5, theta=10000.0)
+
+
+def _synth():
+    import importlib.util
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    spec = importlib.util.spec_from_file_location("kk_synth", root / "kim-kvcache_b200" / "synthetic.py")
+    m = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(m)
+    return m
+
+
+def _synthetic_weights(cfg, seed, std):
+    synth = _synth()
+    rng = np.random.default_rng(seed)
+    return [synth.make_tensor(n, s, rng, std) for n, s in synth.tensor_list(cfg)]
+
+
+def _run_both(ref, oracle, tokens):
+    """Feeds the same positions to the reference model and the oracle; both
+    logits (FP32 bit patterns) and the final normalised hidden states (FP16
+    bits) must be identical."""
+    for pos, tok in enumerate(tokens):
+        rl, rh = ref.forward(tok, pos)
+        _, ol, oh = oracle.forward([7], [tok], [pos])
+        assert np.array_equal(rl.view(np.uint32), ol[0].view(np.uint32)), \
+            f"position {pos}: max |diff| {np.max(np.abs(rl - ol[0]))}"
+        assert np.array_equal(rh, oh[0]), f"position {pos}: final hidden differs"
+
+
+def test_model_oracle_equals_reference_model_on_the_contract_archive(ref_lib):
+    """The reference test's own contract archive and weights (TestArchive,
+    :55-211): every logit and final hidden value bit-exact over a prompt, and
+    the greedy generation equal to the reference's referenceGeneration."""
+    ref = ko.RefModel()
+    cfg = dict(ref.cfg)
+    oracle = ko.Model(cfg, ref.tensors(), threads=2)
+    oracle.create(7)
+    prompt = [1, 3, 7, 11, 2, 15, 4, 9, 0, 13]
+    _run_both(ref, oracle, prompt)
+    gen = ko.RefModel()
+    want = gen.generate(prompt[:4], 12)
+    oracle.create(8)
+    tok = None
+    for pos, t in enumerate(prompt[:4]):
+        g, _, _ = oracle.forward([8], [t], [pos], want_hidden=False)
+        tok = int(g[0])
+    got = []
+    for i in range(12):
+        got.append(tok)
+        if i < 11:
+            g, _, _ = oracle.forward([8], [tok], [4 + i], want_hidden=False)
+            tok = int(g[0])
+    assert got == want
+    gen.close()
+    ref.close()
+    oracle.close()
+
+
+def test_model_oracle_equals_reference_model_small_config(ref_lib):
+    """A 3-layer GQA config (hidden 512, 8 query / 2 KV heads, head_dim 64,
+    vocab 1000) with seeded N(0, 0.05) FP16 weights, 9 positions."""
+    w = _synthetic_weights(MODEL_SMALL, 31, 0.05)
+    ref = ko.RefModel(MODEL_SMALL, w)
+    oracle = ko.Model(MODEL_SMALL, w, threads=4)
+    oracle.create(7)
+    _run_both(ref, oracle, [1, 999, 5, 17, 400, 3, 3, 250, 77])
+    ref.close()
+    oracle.close()
+
+
+@pytest.mark.slow
+def test_model_oracle_equals_reference_model_tinyllama_shape(ref_lib):
+    """BASELINE config 2's shape (TinyLlama-1.1B: 22 layers, hidden 2048, 32
+    query / 4 KV heads, vocab 32000, N(0, 0.02) weights), batch 1, 3 positions."""
+    synth = _synth()
+    cfg = {k: v for k, v in synth.TINYLLAMA.items() if k not in ("bos", "eos")}
+    w = _synthetic_weights(cfg, 5, 0.02)
+    ref = ko.RefModel(cfg, w)
+    oracle = ko.Model(cfg, w, threads=8)
+    del w
+    oracle.create(7)
+    _run_both(ref, oracle, [2207, 31999, 3])
+    ref.close()
+    oracle.close()
