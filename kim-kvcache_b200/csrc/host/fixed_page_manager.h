@@ -4,11 +4,12 @@
 // (include/kim-kv/fixed/fixed_page_manager.h:30-166,
 // src/fixed/fixed_page_manager.cpp, src/fixed/fixed_token_reservation.cpp).
 //
-// Create / append / reserve-commit-rollback / seal / fork / partial-tail COW /
-// release follow the two-pool manager's semantics with every page of size
-// tokens_per_page; there is no promotion and there are no leases. Pages carry
-// PageKind::Micro in block tables (the kind only names the pool), and table
-// invariants are checked against tokens_per_page.
+// It is the single-pool configuration of the page-table engine that also
+// runs KvCacheManager (paged_tables.h): create / append / reserve-commit-
+// rollback / seal / fork / partial-tail COW / release with every page of
+// size tokens_per_page; there is no promotion and there are no leases. Pages
+// carry PageKind::Micro in block tables (the kind only names the pool), and
+// table invariants are checked against tokens_per_page.
 #pragma once
 
 #include "kv_cache_manager.h"
@@ -54,49 +55,8 @@ public:
     [[nodiscard]] bool checkInvariants() const;
 
 private:
-    // Per physical page: lifecycle state and sharing. The handle generation
-    // is kept when a page is freed, so stale handles stay detectable.
-    struct Page {
-        PageState state{PageState::Free};
-        std::uint32_t generation{0};
-        std::uint16_t valid_tokens{0};
-        std::uint32_t ref_count{0};
-        RequestId owner{kInvalidRequestId};  // the one request that may write a Mutable page
-    };
-
-    // A reserved next token: exactly one of `target` (a new page, or the copy
-    // of a sealed partial tail) and `in_place` (the request's own Mutable
-    // tail) is set.
-    struct Reservation {
-        RequestId request{kInvalidRequestId};
-        std::uint64_t table_version{0};
-        BlockTable candidate{};
-        PageHandle target{PageHandle::invalid()};
-        PageHandle in_place{PageHandle::invalid()};
-        PageHandle replaced_tail{PageHandle::invalid()};
-    };
-
-    [[nodiscard]] Page* page(PageHandle h) noexcept;
-    [[nodiscard]] Page const* page(PageHandle h) const noexcept;
-    [[nodiscard]] KvCacheError stage(std::uint16_t initial_valid, PageHandle& out);
-    void unstage(std::vector<PageHandle> const& staged) noexcept;
-    void markFree(Page& p) noexcept;
-    [[nodiscard]] KvCacheError freePage(PageHandle h);
-    [[nodiscard]] KvCacheError dropReference(PageHandle h);
-    // A page that now backs `entry` of `owner`'s committed table.
-    void publish(Page& p, std::uint16_t valid_tokens, RequestId owner) noexcept;
-    [[nodiscard]] bool reserved(RequestId r) const noexcept { return by_request_.count(r) != 0; }
-    [[nodiscard]] KvTokenReservationId nextReservationId();
-    [[nodiscard]] bool consistent() const;
-
     std::uint16_t page_tokens_;
-    PagePool pool_;
-    std::vector<Page> pages_;
-    std::unordered_map<RequestId, BlockTable> requests_;
-    std::unordered_map<KvTokenReservationId, Reservation> reservations_;
-    std::unordered_map<RequestId, KvTokenReservationId> by_request_;
-    KvTokenReservationId next_reservation_{1};
-    std::uint64_t peak_allocated_{0};
+    TableEngine core_;
     mutable std::mutex mutex_;
 };
 

@@ -1,7 +1,10 @@
-// KvCacheManager: request lifecycle, append, token reservations.
-// Reference semantics: src/runtime/kv_cache_manager.cpp:12-249,
-// kv_cache_append.cpp:12-258, token_reservation.cpp:10-326,
-// kv_cache_lifecycle.cpp:12-195, kv_cache_inspection.cpp:12-78.
+// KvCacheManager: the two-pool configuration of the page-table engine
+// (paged_tables.h) plus what only this runtime has: promotion of 8 sealed
+// micro pages into one extent page, and page leases.
+//
+// Reference semantics: src/runtime/kv_cache_manager.cpp, kv_cache_append.cpp,
+// token_reservation.cpp, kv_cache_lifecycle.cpp, promotion.cpp:80-457,
+// page_lease.cpp:31-189, kv_cache_invariants.cpp.
 #include "kv_cache_manager.h"
 
 #include <algorithm>
@@ -11,535 +14,62 @@
 namespace kimkvcache {
 
 KvCacheManager::KvCacheManager(std::uint32_t micro_capacity, std::uint32_t extent_capacity)
-    : micro_pool_(PageKind::Micro, micro_capacity)
-    , extent_pool_(PageKind::Extent, extent_capacity)
-    , micro_pages_(micro_capacity)
-    , extent_pages_(extent_capacity)
+    : core_(kMicroPageTokenCapacity, micro_capacity, extent_capacity)
 {
 }
 
-// Takes a fresh micro page for a staged copy-on-write or growth target. The
-// page stays CopyTarget (unreferenced) until the owning operation commits.
-KvCacheError KvCacheManager::stageMicro(std::uint16_t initial_valid_tokens, PageHandle& out)
+bool KvCacheManager::promoting(RequestId request_id) const
 {
-    if (initial_valid_tokens >= kMicroPageTokenCapacity) {
-        return KvCacheError::InvalidArgument;
-    }
-    PageAllocationResult const got = micro_pool_.allocate();
-    if (!got.ok()) {
-        return got.error == PagePoolError::Exhausted ? KvCacheError::ResourceExhausted
-                                                     : KvCacheError::InternalInvariantViolation;
-    }
-    out = got.handle;
-    if (out.slot >= micro_pages_.size()) {
-        static_cast<void>(micro_pool_.release(out));
-        out = PageHandle::invalid();
-        return KvCacheError::InternalInvariantViolation;
-    }
-    Page& p = micro_pages_[out.slot];
-    if (p.state != PageState::Free || p.ref_count != 0 || p.promotion_pins != 0
-        || p.inflight_readers != 0) {
-        static_cast<void>(micro_pool_.release(out));
-        out = PageHandle::invalid();
-        return KvCacheError::InternalInvariantViolation;
-    }
-    p = Page{PageState::CopyTarget, out.generation, initial_valid_tokens, 0, 0, 0,
-        kInvalidRequestId};
-    return KvCacheError::None;
+    return std::any_of(promotions_.begin(), promotions_.end(),
+        [request_id](auto const& p) { return p.second.request_id == request_id; });
 }
 
-void KvCacheManager::clearFreed(Page& p) noexcept
-{
-    // The generation is kept: it identifies the last handle issued for the slot.
-    p.state = PageState::Free;
-    p.valid_tokens = 0;
-    p.ref_count = 0;
-    p.promotion_pins = 0;
-    p.inflight_readers = 0;
-    p.mutable_owner = kInvalidRequestId;
-}
-
-void KvCacheManager::unstage(std::vector<Staged> const& staged) noexcept
-{
-    for (auto it = staged.rbegin(); it != staged.rend(); ++it) {
-        Page* p = page(it->handle);
-        if (p == nullptr || p->state != PageState::CopyTarget || p->ref_count != 0) {
-            continue;
-        }
-        if (micro_pool_.release(it->handle) == PagePoolError::None) {
-            clearFreed(*p);
-        }
-    }
-}
-
-// Drops an unreferenced page: back to its pool, or Retiring while a lease or
-// a promotion still pins it.
-KvCacheError KvCacheManager::retireOrFree(PageHandle handle)
-{
-    Page* p = page(handle);
-    if (p == nullptr || p->state == PageState::Free) {
-        return KvCacheError::InternalInvariantViolation;
-    }
-    if (p->ref_count != 0) {
-        return KvCacheError::InvalidState;
-    }
-    p->mutable_owner = kInvalidRequestId;
-    if (p->promotion_pins != 0 || p->inflight_readers != 0) {
-        p->state = PageState::Retiring;
-        return KvCacheError::None;
-    }
-    PagePool& pool = poolFor(handle.kind);
-    if (pool.validate(handle) != PagePoolError::None
-        || pool.release(handle) != PagePoolError::None) {
-        return KvCacheError::InternalInvariantViolation;
-    }
-    clearFreed(*p);
-    return KvCacheError::None;
-}
-
-KvCacheError KvCacheManager::dropReference(PageHandle handle)
-{
-    Page* p = page(handle);
-    if (p == nullptr || p->state == PageState::Free || p->state == PageState::CopyTarget
-        || p->ref_count == 0) {
-        return KvCacheError::InternalInvariantViolation;
-    }
-    if (--p->ref_count != 0) {
-        return KvCacheError::None;
-    }
-    return retireOrFree(handle);
-}
-
-bool KvCacheManager::hasReservation(RequestId request_id) const noexcept
-{
-    return request_reservation_.find(request_id) != request_reservation_.end();
-}
+// ---- delegated table operations ----------------------------------------------------------
 
 KvCacheError KvCacheManager::createRequest(RequestId request_id)
 {
-    if (request_id == kInvalidRequestId) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    return requests_.emplace(request_id, BlockTable{}).second
-        ? KvCacheError::None : KvCacheError::RequestAlreadyExists;
+    return core_.create(request_id);
 }
 
 KvCacheError KvCacheManager::append(RequestId request_id, std::uint32_t token_count)
 {
-    if (request_id == kInvalidRequestId || token_count == 0) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(request_id);
-    if (found == requests_.end()) {
-        return KvCacheError::RequestNotFound;
-    }
-    if (hasReservation(request_id)) {
-        return KvCacheError::RequestConflict;
-    }
-    BlockTable& table = found->second;
-    std::uint32_t const old_tokens = table.tokenCount();
-    if (token_count > std::numeric_limits<std::uint32_t>::max() - old_tokens) {
-        return KvCacheError::InvalidArgument;
-    }
-
-    constexpr std::size_t kNone = std::numeric_limits<std::size_t>::max();
-    std::size_t const max_new_pages =
-        (static_cast<std::size_t>(token_count) + kMicroPageTokenCapacity - 1)
-            / kMicroPageTokenCapacity + 1;
-    BlockTable candidate = table;
-    candidate.entries_.reserve(candidate.entries_.size() + max_new_pages);
-    std::vector<Staged> staged;
-    staged.reserve(max_new_pages);
-    std::size_t active = kNone;
-    PageHandle existing_mutable = PageHandle::invalid();
-    PageHandle replaced_sealed_tail = PageHandle::invalid();
-
-    if (!candidate.entries_.empty()) {
-        std::size_t const tail_index = candidate.entries_.size() - 1;
-        MappingEntry& tail = candidate.entries_[tail_index];
-        Page* tail_page = page(tail.handle);
-        if (tail_page == nullptr || tail_page->valid_tokens != tail.valid_tokens) {
-            return KvCacheError::InternalInvariantViolation;
-        }
-        if (tail.kind == PageKind::Micro && tail.valid_tokens < kMicroPageTokenCapacity) {
-            if (tail_page->state == PageState::Mutable) {
-                if (tail_page->ref_count != 1 || tail_page->mutable_owner != request_id) {
-                    return KvCacheError::InternalInvariantViolation;
-                }
-                existing_mutable = tail.handle;
-                active = tail_index;
-            } else if (tail_page->state == PageState::Sealed) {
-                // Shared or sealed partial tail: copy-on-write into a new page.
-                PageHandle copy = PageHandle::invalid();
-                KvCacheError const error = stageMicro(tail.valid_tokens, copy);
-                if (error != KvCacheError::None) {
-                    return error;
-                }
-                staged.push_back(Staged{copy, tail_index});
-                replaced_sealed_tail = tail.handle;
-                tail.kind = PageKind::Micro;
-                tail.handle = copy;
-                active = tail_index;
-            } else {
-                return KvCacheError::InvalidState;
-            }
-        } else if (tail_page->state != PageState::Sealed) {
-            return KvCacheError::InternalInvariantViolation;
-        }
-    }
-
-    std::uint32_t remaining = token_count;
-    std::uint32_t logical_end = old_tokens;
-    while (remaining != 0) {
-        if (active == kNone) {
-            PageHandle fresh = PageHandle::invalid();
-            KvCacheError const error = stageMicro(0, fresh);
-            if (error != KvCacheError::None) {
-                unstage(staged);
-                return error;
-            }
-            active = candidate.entries_.size();
-            candidate.entries_.push_back(MappingEntry{logical_end, 0, PageKind::Micro, fresh});
-            staged.push_back(Staged{fresh, active});
-        }
-        MappingEntry& entry = candidate.entries_[active];
-        std::uint32_t const take = std::min<std::uint32_t>(
-            remaining, kMicroPageTokenCapacity - entry.valid_tokens);
-        entry.valid_tokens = static_cast<std::uint16_t>(entry.valid_tokens + take);
-        logical_end += take;
-        remaining -= take;
-        if (entry.valid_tokens == kMicroPageTokenCapacity) {
-            active = kNone;
-        }
-    }
-    candidate.version_ = table.version_ + 1;
-
-    // Re-validate everything before entering the no-fail commit section.
-    bool consistent = candidate.checkInvariants();
-    if (consistent && existing_mutable.isStructurallyValid()) {
-        Page const* p = page(existing_mutable);
-        consistent = p != nullptr && p->state == PageState::Mutable && p->ref_count == 1
-            && p->mutable_owner == request_id;
-    }
-    if (consistent && replaced_sealed_tail.isStructurallyValid()) {
-        Page const* p = page(replaced_sealed_tail);
-        consistent = p != nullptr && p->state == PageState::Sealed && p->ref_count != 0;
-    }
-    for (std::size_t i = 0; consistent && i < staged.size(); ++i) {
-        Page const* p = page(staged[i].handle);
-        consistent = p != nullptr && p->state == PageState::CopyTarget && p->ref_count == 0
-            && staged[i].entry_index < candidate.entries_.size()
-            && candidate.entries_[staged[i].entry_index].handle == staged[i].handle;
-    }
-    if (!consistent) {
-        unstage(staged);
-        return KvCacheError::InternalInvariantViolation;
-    }
-
-    if (replaced_sealed_tail.isStructurallyValid()) {
-        KvCacheError const error = dropReference(replaced_sealed_tail);
-        if (error != KvCacheError::None) {
-            unstage(staged);
-            return error;
-        }
-    }
-    if (existing_mutable.isStructurallyValid()) {
-        Page* p = page(existing_mutable);
-        for (MappingEntry const& entry : candidate.entries_) {
-            if (entry.handle == existing_mutable) {
-                p->valid_tokens = entry.valid_tokens;
-                if (entry.valid_tokens == kMicroPageTokenCapacity) {
-                    p->state = PageState::Sealed;
-                    p->mutable_owner = kInvalidRequestId;
-                }
-                break;
-            }
-        }
-    }
-    for (Staged const& s : staged) {
-        Page* p = page(s.handle);
-        MappingEntry const& entry = candidate.entries_[s.entry_index];
-        p->valid_tokens = entry.valid_tokens;
-        p->ref_count = 1;
-        bool const full = entry.valid_tokens == kMicroPageTokenCapacity;
-        p->state = full ? PageState::Sealed : PageState::Mutable;
-        p->mutable_owner = full ? kInvalidRequestId : request_id;
-    }
-    table = std::move(candidate);
-    return KvCacheError::None;
+    return core_.append(request_id, token_count);
 }
 
-TokenReservationResult KvCacheManager::reserveToken(
-    RequestId request_id, std::uint32_t expected_committed_tokens)
+TokenReservationResult KvCacheManager::reserveToken(RequestId request_id, std::uint32_t expected)
 {
-    TokenReservationResult result;
-    result.request_id = request_id;
-    result.logical_token_position = expected_committed_tokens;
-    if (request_id == kInvalidRequestId) {
-        result.error = KvCacheError::InvalidArgument;
-        return result;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(request_id);
-    if (found == requests_.end()) {
-        result.error = KvCacheError::RequestNotFound;
-        return result;
-    }
-    bool const promoting = std::any_of(promotions_.begin(), promotions_.end(),
-        [request_id](auto const& p) { return p.second.request_id == request_id; });
-    if (hasReservation(request_id) || promoting) {
-        result.error = KvCacheError::RequestConflict;
-        return result;
-    }
-    BlockTable const& before = found->second;
-    if (before.tokenCount() != expected_committed_tokens
-        || before.version_ == std::numeric_limits<std::uint64_t>::max()
-        || expected_committed_tokens == std::numeric_limits<std::uint32_t>::max()) {
-        result.error = KvCacheError::InvalidState;
-        return result;
-    }
-
-    BlockTable candidate = before;
-    candidate.entries_.reserve(candidate.entries_.size() + 1);
-    PageHandle staged = PageHandle::invalid();
-    PageHandle existing_mutable = PageHandle::invalid();
-    PageHandle replaced_sealed_tail = PageHandle::invalid();
-
-    bool const needs_new_page = candidate.entries_.empty()
-        || candidate.entries_.back().kind == PageKind::Extent
-        || candidate.entries_.back().valid_tokens == kMicroPageTokenCapacity;
-    if (needs_new_page) {
-        KvCacheError const error = stageMicro(0, staged);
-        if (error != KvCacheError::None) {
-            result.error = error;
-            return result;
-        }
-        candidate.entries_.push_back(
-            MappingEntry{expected_committed_tokens, 1, PageKind::Micro, staged});
-    } else {
-        MappingEntry& tail = candidate.entries_.back();
-        Page const* tail_page = page(tail.handle);
-        if (tail_page == nullptr || tail.kind != PageKind::Micro
-            || tail_page->valid_tokens != tail.valid_tokens) {
-            result.error = KvCacheError::InternalInvariantViolation;
-            return result;
-        }
-        if (tail_page->state == PageState::Mutable) {
-            if (tail_page->ref_count != 1 || tail_page->mutable_owner != request_id) {
-                result.error = KvCacheError::InternalInvariantViolation;
-                return result;
-            }
-            existing_mutable = tail.handle;
-        } else if (tail_page->state == PageState::Sealed) {
-            KvCacheError const error = stageMicro(tail.valid_tokens, staged);
-            if (error != KvCacheError::None) {
-                result.error = error;
-                return result;
-            }
-            replaced_sealed_tail = tail.handle;
-            tail.handle = staged;
-        } else {
-            result.error = KvCacheError::InvalidState;
-            return result;
-        }
-        ++tail.valid_tokens;
-    }
-    candidate.version_ = before.version_ + 1;
-
-    auto abandon = [&](KvCacheError error) {
-        if (staged.isStructurallyValid()) {
-            static_cast<void>(retireOrFree(staged));
-        }
-        result.error = error;
-        return result;
-    };
-    if (!candidate.checkInvariants()) {
-        return abandon(KvCacheError::InternalInvariantViolation);
-    }
-    KvTokenReservationId const id = nextFreeId(next_reservation_id_, reservations_);
-    if (id == kInvalidKvTokenReservationId) {
-        return abandon(KvCacheError::InternalInvariantViolation);
-    }
-    auto const inserted = reservations_.emplace(id, Reservation{id, request_id,
-        before.version_, candidate, staged, existing_mutable, replaced_sealed_tail});
-    if (!inserted.second) {
-        return abandon(KvCacheError::InternalInvariantViolation);
-    }
-    if (!request_reservation_.emplace(request_id, id).second) {
-        reservations_.erase(inserted.first);
-        return abandon(KvCacheError::InternalInvariantViolation);
-    }
-    result.error = KvCacheError::None;
-    result.reservation_id = id;
-    result.before = before;
-    result.reserved = std::move(candidate);
-    return result;
+    // A prepared promotion holds the request's table version: no token may
+    // be reserved until it is committed or rolled back.
+    bool const busy = request_id != kInvalidRequestId && core_.table(request_id) != nullptr
+        && promoting(request_id);
+    return core_.reserve(request_id, expected, busy);
 }
 
 KvCacheError KvCacheManager::commitTokenReservation(KvTokenReservationId id)
 {
-    if (id == kInvalidKvTokenReservationId) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = reservations_.find(id);
-    if (found == reservations_.end()) {
-        return KvCacheError::TokenReservationNotFound;
-    }
-    Reservation& r = found->second;
-    auto request = requests_.find(r.request_id);
-    if (request == requests_.end() || request->second.version_ != r.prepared_version) {
-        return KvCacheError::RequestConflict;
-    }
-    MappingEntry const tail = r.candidate.entries_.back();
-    Page* staged = r.staged_target.isStructurallyValid() ? page(r.staged_target) : nullptr;
-    Page* existing = r.existing_mutable.isStructurallyValid() ? page(r.existing_mutable) : nullptr;
-    Page* replaced = r.replaced_sealed_tail.isStructurallyValid()
-        ? page(r.replaced_sealed_tail) : nullptr;
-    if ((staged != nullptr && (staged->state != PageState::CopyTarget || staged->ref_count != 0))
-        || (existing != nullptr
-            && (existing->state != PageState::Mutable || existing->ref_count != 1
-                || existing->mutable_owner != r.request_id))
-        || (replaced != nullptr
-            && (replaced->state != PageState::Sealed || replaced->ref_count == 0))) {
-        return KvCacheError::InternalInvariantViolation;
-    }
-    if (r.replaced_sealed_tail.isStructurallyValid()) {
-        KvCacheError const error = dropReference(r.replaced_sealed_tail);
-        if (error != KvCacheError::None) {
-            return error;
-        }
-    }
-    bool const full = tail.valid_tokens == kMicroPageTokenCapacity;
-    if (existing != nullptr) {
-        existing->valid_tokens = tail.valid_tokens;
-        if (full) {
-            existing->state = PageState::Sealed;
-            existing->mutable_owner = kInvalidRequestId;
-        }
-    }
-    if (staged != nullptr) {
-        staged->valid_tokens = tail.valid_tokens;
-        staged->ref_count = 1;
-        staged->state = full ? PageState::Sealed : PageState::Mutable;
-        staged->mutable_owner = full ? kInvalidRequestId : r.request_id;
-    }
-    request->second = std::move(r.candidate);
-    request_reservation_.erase(r.request_id);
-    reservations_.erase(found);
-    return KvCacheError::None;
-}
-
-KvCacheError KvCacheManager::rollbackReservationLocked(KvTokenReservationId id)
-{
-    auto found = reservations_.find(id);
-    if (found == reservations_.end()) {
-        return KvCacheError::TokenReservationNotFound;
-    }
-    if (found->second.staged_target.isStructurallyValid()) {
-        KvCacheError const error = retireOrFree(found->second.staged_target);
-        if (error != KvCacheError::None) {
-            return error;
-        }
-    }
-    request_reservation_.erase(found->second.request_id);
-    reservations_.erase(found);
-    return KvCacheError::None;
+    return core_.commit(id);
 }
 
 KvCacheError KvCacheManager::rollbackTokenReservation(KvTokenReservationId id)
 {
-    if (id == kInvalidKvTokenReservationId) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    return rollbackReservationLocked(id);
+    return core_.rollback(id);
 }
 
 KvCacheError KvCacheManager::sealTail(RequestId request_id)
 {
-    if (request_id == kInvalidRequestId) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(request_id);
-    if (found == requests_.end()) {
-        return KvCacheError::RequestNotFound;
-    }
-    if (hasReservation(request_id)) {
-        return KvCacheError::RequestConflict;
-    }
-    BlockTable const& table = found->second;
-    if (table.entries_.empty()) {
-        return KvCacheError::InvalidState;
-    }
-    MappingEntry const& tail = table.entries_.back();
-    Page* p = page(tail.handle);
-    if (p == nullptr || p->valid_tokens != tail.valid_tokens) {
-        return KvCacheError::InternalInvariantViolation;
-    }
-    if (p->state == PageState::Sealed) {
-        return KvCacheError::None;
-    }
-    if (p->state != PageState::Mutable || p->ref_count != 1 || p->mutable_owner != request_id) {
-        return KvCacheError::InvalidState;
-    }
-    p->state = PageState::Sealed;  // mapping unchanged: the version stays
-    p->mutable_owner = kInvalidRequestId;
-    return KvCacheError::None;
+    return core_.seal(request_id);
 }
 
 KvCacheError KvCacheManager::forkRequest(RequestId source, RequestId child)
 {
-    if (source == kInvalidRequestId || child == kInvalidRequestId || source == child) {
-        return KvCacheError::InvalidArgument;
-    }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(source);
-    if (found == requests_.end()) {
-        return KvCacheError::RequestNotFound;
-    }
-    if (hasReservation(source)) {
-        return KvCacheError::RequestConflict;
-    }
-    if (requests_.find(child) != requests_.end()) {
-        return KvCacheError::RequestAlreadyExists;
-    }
-    BlockTable const& table = found->second;
-    for (std::size_t i = 0; i < table.entries_.size(); ++i) {
-        MappingEntry const& entry = table.entries_[i];
-        Page const* p = page(entry.handle);
-        if (p == nullptr || p->valid_tokens != entry.valid_tokens || p->ref_count == 0
-            || p->ref_count == std::numeric_limits<std::uint32_t>::max()) {
-            return KvCacheError::InternalInvariantViolation;
-        }
-        if (p->state == PageState::Mutable) {
-            if (i + 1 != table.entries_.size() || p->ref_count != 1
-                || p->mutable_owner != source) {
-                return KvCacheError::InternalInvariantViolation;
-            }
-        } else if (p->state != PageState::Sealed) {
-            return KvCacheError::InvalidState;
-        }
-    }
-    BlockTable child_table = table;
-    child_table.version_ = child_table.entries_.empty() ? 0 : 1;
-    if (!requests_.emplace(child, std::move(child_table)).second) {
-        return KvCacheError::RequestAlreadyExists;
-    }
-    // Both requests now share every page; the source's mutable tail becomes
-    // sealed so that the next write by either side copies it.
-    for (MappingEntry const& entry : table.entries_) {
-        Page* p = page(entry.handle);
-        if (p->state == PageState::Mutable) {
-            p->state = PageState::Sealed;
-            p->mutable_owner = kInvalidRequestId;
-        }
-        ++p->ref_count;
-    }
-    return KvCacheError::None;
+    return core_.fork(source, child);
 }
 
 KvCacheError KvCacheManager::releaseRequest(RequestId request_id)
@@ -548,61 +78,439 @@ KvCacheError KvCacheManager::releaseRequest(RequestId request_id)
         return KvCacheError::InvalidArgument;
     }
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(request_id);
-    if (found == requests_.end()) {
+    if (core_.table(request_id) == nullptr) {
         return KvCacheError::RequestNotFound;
     }
-    if (hasReservation(request_id)) {
+    if (core_.pending(request_id)) {
         return KvCacheError::RequestConflict;
     }
-    KvCacheError const rolled = rollbackRequestPromotionsLocked(request_id);
-    if (rolled != KvCacheError::None) {
-        return rolled;
-    }
-    BlockTable const& table = found->second;
-    for (MappingEntry const& entry : table.entries_) {
-        Page const* p = page(entry.handle);
-        if (p == nullptr || p->state == PageState::Free || p->state == PageState::CopyTarget
-            || p->ref_count == 0) {
-            return KvCacheError::InternalInvariantViolation;
+    // Pending promotions of the request are undone first, in the map's order.
+    for (;;) {
+        auto const p = std::find_if(promotions_.begin(), promotions_.end(),
+            [request_id](auto const& e) { return e.second.request_id == request_id; });
+        if (p == promotions_.end()) {
+            break;
+        }
+        KvCacheError const err = undoPromotion(p->first);
+        if (err != KvCacheError::None) {
+            return err;
         }
     }
-    for (MappingEntry const& entry : table.entries_) {
-        KvCacheError const error = dropReference(entry.handle);
-        if (error != KvCacheError::None) {
-            return error;
-        }
-    }
-    requests_.erase(found);
-    return KvCacheError::None;
+    return core_.release(request_id);
 }
 
 std::optional<BlockTable> KvCacheManager::blockTable(RequestId request_id) const
 {
     std::lock_guard<std::mutex> lock(mutex_);
-    auto found = requests_.find(request_id);
-    if (found == requests_.end()) {
-        return std::nullopt;
-    }
-    return found->second;
+    BlockTable const* t = core_.table(request_id);
+    return t == nullptr ? std::nullopt : std::optional<BlockTable>(*t);
 }
 
 std::optional<PageMetadataSnapshot> KvCacheManager::pageMetadata(PageHandle handle) const
 {
     std::lock_guard<std::mutex> lock(mutex_);
-    Page const* p = page(handle);
-    if (p == nullptr) {
+    auto const [s, i] = core_.find(handle);
+    if (s == nullptr) {
         return std::nullopt;
     }
-    return PageMetadataSnapshot{handle, p->state, p->valid_tokens, p->ref_count,
-        p->promotion_pins, p->inflight_readers, p->mutable_owner};
+    return PageMetadataSnapshot{handle, s->state[i], s->valid[i], s->refs[i], s->pins[i], s->readers[i],
+        s->owner[i]};
 }
 
 KvCacheManagerSnapshot KvCacheManager::snapshot() const
 {
     std::lock_guard<std::mutex> lock(mutex_);
-    return KvCacheManagerSnapshot{requests_.size(), promotions_.size(), leases_.size(),
-        reservations_.size(), micro_pool_.snapshot(), extent_pool_.snapshot()};
+    return KvCacheManagerSnapshot{core_.requestCount(), promotions_.size(), leases_.size(),
+        core_.reservationCount(), core_.slots(PageKind::Micro).pool.snapshot(),
+        core_.slots(PageKind::Extent).pool.snapshot()};
+}
+
+// ---- promotion -------------------------------------------------------------------------------
+
+// Entries [first, first + 8) of `table` form a promotable run starting at
+// logical token `begin`: full, sealed, unshared micro pages in order, each
+// pinned exactly `pins` times (0 before prepare, 1 by the prepared
+// promotion) and, when `expect` is given, exactly the prepared pages.
+bool KvCacheManager::runEligible(BlockTable const& table, std::size_t first, std::uint32_t begin,
+    std::array<PageHandle, kPromotionSourcePageCount> const* expect, std::uint32_t pins) const
+{
+    if (first > table.entries_.size() || table.entries_.size() - first < kPromotionSourcePageCount) {
+        return false;
+    }
+    PageSlots const& micro = core_.slots(PageKind::Micro);
+    for (std::size_t k = 0; k < kPromotionSourcePageCount; ++k) {
+        MappingEntry const& m = table.entries_[first + k];
+        std::uint64_t const at = std::uint64_t(begin) + k * kMicroPageTokenCapacity;
+        if (at > std::numeric_limits<std::uint32_t>::max() || m.logical_token_begin != at
+            || m.kind != PageKind::Micro || m.valid_tokens != kMicroPageTokenCapacity
+            || (expect != nullptr && m.handle != (*expect)[k])) {
+            return false;
+        }
+        std::int64_t const i = micro.slotOf(m.handle);
+        if (i < 0 || micro.state[i] != PageState::Sealed || micro.valid[i] != kMicroPageTokenCapacity
+            || micro.refs[i] != 1 || micro.pins[i] != pins || micro.owner[i] != kInvalidRequestId
+            || micro.pool.validate(m.handle) != PagePoolError::None) {
+            return false;
+        }
+    }
+    return true;
+}
+
+PromotionPrepareResult KvCacheManager::preparePromotion(RequestId request_id, std::uint32_t begin)
+{
+    PromotionPrepareResult r;
+    r.request_id = request_id;
+    r.logical_token_begin = begin;
+    if (request_id == kInvalidRequestId) {
+        r.error = KvCacheError::InvalidArgument;
+        return r;
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    BlockTable const* t = core_.table(request_id);
+    if (t == nullptr) {
+        r.error = KvCacheError::RequestNotFound;
+        return r;
+    }
+    if (core_.pending(request_id)) {
+        r.error = KvCacheError::RequestConflict;
+        return r;
+    }
+    if (t->version_ == std::numeric_limits<std::uint64_t>::max()) {
+        r.error = KvCacheError::PromotionConflict;
+        return r;
+    }
+    auto const at = std::find_if(t->entries_.begin(), t->entries_.end(),
+        [begin](MappingEntry const& m) { return m.logical_token_begin == begin; });
+    std::size_t const first = static_cast<std::size_t>(at - t->entries_.begin());
+    if (at == t->entries_.end() || !runEligible(*t, first, begin, nullptr, 0)) {
+        r.error = KvCacheError::PromotionNotEligible;
+        return r;
+    }
+    Promotion p{request_id, t->version_, begin, first, {}, PageHandle::invalid()};
+    for (std::size_t k = 0; k < kPromotionSourcePageCount; ++k) {
+        p.sources[k] = t->entries_[first + k].handle;
+    }
+    if ((r.error = core_.stage(PageKind::Extent, kExtentPageTokenCapacity, p.target)) != KvCacheError::None) {
+        return r;
+    }
+    PromotionId const id = promotion_ids_.next(promotions_);
+    if (id == kInvalidPromotionId) {
+        static_cast<void>(core_.retire(p.target));
+        r.error = KvCacheError::InternalInvariantViolation;
+        return r;
+    }
+    PageSlots& micro = core_.slots(PageKind::Micro);
+    for (PageHandle const h : p.sources) {
+        ++micro.pins[h.slot];
+    }
+    r.promotion_id = id;
+    r.source_handles = p.sources;
+    r.target_handle = p.target;
+    promotions_.emplace(id, p);
+    return r;
+}
+
+// Returns the staged target and unpins the sources; a source whose last
+// table reference went while it was pinned leaves now.
+KvCacheError KvCacheManager::undoPromotion(PromotionId id)
+{
+    auto const f = promotions_.find(id);
+    if (f == promotions_.end()) {
+        return KvCacheError::PromotionNotFound;
+    }
+    Promotion const& p = f->second;
+    PageSlots& micro = core_.slots(PageKind::Micro);
+    PageSlots const& extent = core_.slots(PageKind::Extent);
+    std::int64_t const ti = extent.slotOf(p.target);
+    bool intact = ti >= 0 && extent.state[ti] == PageState::CopyTarget
+        && extent.valid[ti] == kExtentPageTokenCapacity && extent.refs[ti] == 0 && extent.pins[ti] == 0
+        && extent.owner[ti] == kInvalidRequestId && extent.pool.validate(p.target) == PagePoolError::None;
+    for (PageHandle const h : p.sources) {
+        std::int64_t const i = micro.slotOf(h);
+        intact = intact && i >= 0
+            && (micro.state[i] == PageState::Sealed || micro.state[i] == PageState::Retiring)
+            && micro.valid[i] == kMicroPageTokenCapacity && micro.pins[i] == 1
+            && micro.owner[i] == kInvalidRequestId && micro.pool.validate(h) == PagePoolError::None;
+    }
+    if (!intact) {
+        return KvCacheError::InternalInvariantViolation;
+    }
+    KvCacheError err = core_.retire(p.target);
+    for (std::size_t k = 0; err == KvCacheError::None && k < kPromotionSourcePageCount; ++k) {
+        std::uint32_t const i = p.sources[k].slot;
+        --micro.pins[i];
+        if (micro.refs[i] == 0) {
+            err = core_.retire(p.sources[k]);
+        }
+    }
+    if (err == KvCacheError::None) {
+        promotions_.erase(f);
+    }
+    return err;
+}
+
+KvCacheError KvCacheManager::rollbackPromotion(PromotionId id)
+{
+    if (id == kInvalidPromotionId) {
+        return KvCacheError::InvalidArgument;
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    return undoPromotion(id);
+}
+
+KvCacheError KvCacheManager::commitPromotion(PromotionId id)
+{
+    if (id == kInvalidPromotionId) {
+        return KvCacheError::InvalidArgument;
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    auto const f = promotions_.find(id);
+    if (f == promotions_.end()) {
+        return KvCacheError::PromotionNotFound;
+    }
+    Promotion const p = f->second;
+    BlockTable* t = core_.table(p.request_id);
+    PageSlots& extent = core_.slots(PageKind::Extent);
+    std::int64_t const ti = extent.slotOf(p.target);
+    // The table must still be the prepared version, with the run in place,
+    // and the target untouched; otherwise the promotion is abandoned (its
+    // own undo error wins over the conflict).
+    bool ok = t != nullptr && t->version_ == p.prepared_version
+        && t->version_ != std::numeric_limits<std::uint64_t>::max() && ti >= 0
+        && extent.state[ti] == PageState::CopyTarget && extent.valid[ti] == kExtentPageTokenCapacity
+        && extent.refs[ti] == 0 && extent.pins[ti] == 0 && extent.readers[ti] == 0
+        && extent.owner[ti] == kInvalidRequestId && extent.pool.validate(p.target) == PagePoolError::None
+        && runEligible(*t, p.first_entry, p.logical_token_begin, &p.sources, 1);
+    BlockTable next;
+    if (ok) {
+        next = *t;
+        auto const run = next.entries_.begin() + static_cast<std::ptrdiff_t>(p.first_entry);
+        *run = MappingEntry{p.logical_token_begin, kExtentPageTokenCapacity, PageKind::Extent, p.target};
+        next.entries_.erase(run + 1, run + static_cast<std::ptrdiff_t>(kPromotionSourcePageCount));
+        next.version_ = t->version_ + 1;
+        if (!next.checkInvariants()) {
+            KvCacheError const undone = undoPromotion(id);
+            return undone == KvCacheError::None ? KvCacheError::InternalInvariantViolation : undone;
+        }
+    } else {
+        KvCacheError const undone = undoPromotion(id);
+        return undone == KvCacheError::None ? KvCacheError::PromotionConflict : undone;
+    }
+    // No-fail from here: the extent replaces the run, the sources drop out.
+    *t = std::move(next);
+    extent.state[ti] = PageState::Sealed;
+    extent.refs[ti] = 1;
+    PageSlots& micro = core_.slots(PageKind::Micro);
+    for (PageHandle const h : p.sources) {
+        --micro.refs[h.slot];
+        --micro.pins[h.slot];
+        KvCacheError const err = core_.retire(h);
+        if (err != KvCacheError::None) {
+            return err;
+        }
+    }
+    promotions_.erase(id);
+    return KvCacheError::None;
+}
+
+std::optional<PromotionTransactionSnapshot> KvCacheManager::promotionTransaction(PromotionId id) const
+{
+    std::lock_guard<std::mutex> lock(mutex_);
+    auto const f = promotions_.find(id);
+    if (f == promotions_.end()) {
+        return std::nullopt;
+    }
+    Promotion const& p = f->second;
+    return PromotionTransactionSnapshot{id, p.request_id, p.prepared_version, p.logical_token_begin,
+        p.sources, p.target};
+}
+
+// ---- leases ------------------------------------------------------------------------------------
+
+// Pins every page of `handles` as read by device work in flight. `table`
+// (when given) and the handles are echoed in the result.
+PageLeaseAcquireResult KvCacheManager::lease(std::vector<PageHandle> handles, BlockTable const* table)
+{
+    PageLeaseAcquireResult r;
+    for (PageHandle const h : handles) {
+        auto const [s, i] = core_.find(h);
+        if (s == nullptr || s->state[i] == PageState::Free || s->state[i] == PageState::Retiring
+            || s->readers[i] == std::numeric_limits<std::uint32_t>::max()) {
+            r.error = KvCacheError::InvalidState;
+            return r;
+        }
+    }
+    PageLeaseId const id = lease_ids_.next(leases_);
+    if (id == kInvalidPageLeaseId) {
+        r.error = KvCacheError::InternalInvariantViolation;
+        return r;
+    }
+    for (PageHandle const h : handles) {
+        auto const [s, i] = core_.find(h);
+        ++s->readers[i];
+    }
+    if (table != nullptr) {
+        r.table = *table;
+        r.handles = handles;
+    }
+    leases_.emplace(id, std::move(handles));
+    r.lease_id = id;
+    return r;
+}
+
+PageLeaseAcquireResult KvCacheManager::acquireRequestReadLease(RequestId request_id)
+{
+    if (request_id == kInvalidRequestId) {
+        return PageLeaseAcquireResult{KvCacheError::InvalidArgument, kInvalidPageLeaseId, {}, {}};
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    BlockTable const* t = core_.table(request_id);
+    if (t == nullptr) {
+        return PageLeaseAcquireResult{KvCacheError::RequestNotFound, kInvalidPageLeaseId, {}, {}};
+    }
+    std::vector<PageHandle> pages;
+    pages.reserve(t->entries_.size());
+    for (MappingEntry const& m : t->entries_) {
+        pages.push_back(m.handle);
+    }
+    return lease(std::move(pages), t);
+}
+
+PageLeaseAcquireResult KvCacheManager::acquirePromotionIoLease(PromotionId id)
+{
+    if (id == kInvalidPromotionId) {
+        return PageLeaseAcquireResult{KvCacheError::InvalidArgument, kInvalidPageLeaseId, {}, {}};
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    auto const f = promotions_.find(id);
+    if (f == promotions_.end()) {
+        return PageLeaseAcquireResult{KvCacheError::PromotionNotFound, kInvalidPageLeaseId, {}, {}};
+    }
+    std::vector<PageHandle> pages(f->second.sources.begin(), f->second.sources.end());
+    pages.push_back(f->second.target);
+    BlockTable const no_table;
+    return lease(std::move(pages), &no_table);
+}
+
+PageLeaseAcquireResult KvCacheManager::acquireTokenReservationLease(KvTokenReservationId id)
+{
+    return leaseReservation(id, true);
+}
+
+PageLeaseAcquireResult KvCacheManager::acquireTokenReservationPin(KvTokenReservationId id)
+{
+    return leaseReservation(id, false);
+}
+
+// The reserved table's pages, plus the sealed tail a copy-on-write reads from.
+PageLeaseAcquireResult KvCacheManager::leaseReservation(KvTokenReservationId id, bool describe)
+{
+    if (id == kInvalidKvTokenReservationId) {
+        return PageLeaseAcquireResult{KvCacheError::InvalidArgument, kInvalidPageLeaseId, {}, {}};
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    PendingToken const* p = core_.reservation(id);
+    if (p == nullptr) {
+        return PageLeaseAcquireResult{KvCacheError::TokenReservationNotFound, kInvalidPageLeaseId, {}, {}};
+    }
+    std::vector<PageHandle> pages;
+    pages.reserve(p->edit.table.entries_.size() + 1);
+    for (MappingEntry const& m : p->edit.table.entries_) {
+        pages.push_back(m.handle);
+    }
+    if (p->edit.replaced.isStructurallyValid()) {
+        pages.push_back(p->edit.replaced);
+    }
+    return lease(std::move(pages), describe ? &p->edit.table : nullptr);
+}
+
+KvCacheError KvCacheManager::releasePageLease(PageLeaseId lease_id)
+{
+    if (lease_id == kInvalidPageLeaseId) {
+        return KvCacheError::InvalidArgument;
+    }
+    std::lock_guard<std::mutex> lock(mutex_);
+    auto const f = leases_.find(lease_id);
+    if (f == leases_.end()) {
+        return KvCacheError::InvalidState;
+    }
+    for (PageHandle const h : f->second) {
+        auto const [s, i] = core_.find(h);
+        if (s == nullptr || s->state[i] == PageState::Free || s->readers[i] == 0) {
+            return KvCacheError::InternalInvariantViolation;
+        }
+    }
+    std::vector<PageHandle> const pages = std::move(f->second);
+    leases_.erase(f);
+    for (PageHandle const h : pages) {
+        auto const [s, i] = core_.find(h);
+        --s->readers[i];
+        // A page that only the lease kept alive leaves with it.
+        if (s->state[i] == PageState::Retiring && s->refs[i] == 0 && s->pins[i] == 0 && s->readers[i] == 0) {
+            KvCacheError const err = core_.retire(h);
+            if (err != KvCacheError::None) {
+                return err;
+            }
+        }
+    }
+    return KvCacheError::None;
+}
+
+// ---- invariants --------------------------------------------------------------------------------
+
+bool KvCacheManager::checkInvariants() const
+{
+    std::lock_guard<std::mutex> lock(mutex_);
+    PageSlots const& micro = core_.slots(PageKind::Micro);
+    PageSlots const& extent = core_.slots(PageKind::Extent);
+    ExpectedCounts xm(micro.size());
+    ExpectedCounts xe(extent.size());
+    if (!core_.auditTables(xm, &xe)) {
+        return false;
+    }
+    // Promotions: a staged extent target each, and one pin on each source of
+    // a run that is still in place in the request's table.
+    for (auto const& [id, p] : promotions_) {
+        BlockTable const* t = core_.table(p.request_id);
+        std::int64_t const ti = extent.slotOf(p.target);
+        if (id == kInvalidPromotionId || t == nullptr || p.prepared_version > t->version_ || ti < 0
+            || xe.staged[ti] != 0 || extent.state[ti] != PageState::CopyTarget) {
+            return false;
+        }
+        xe.staged[ti] = 1;
+        auto const at = std::find_if(t->entries_.begin(), t->entries_.end(),
+            [&p](MappingEntry const& m) { return m.handle == p.sources[0]; });
+        std::size_t const first = static_cast<std::size_t>(at - t->entries_.begin());
+        if (at == t->entries_.end() || first + kPromotionSourcePageCount > t->entries_.size()) {
+            return false;
+        }
+        for (std::size_t k = 0; k < kPromotionSourcePageCount; ++k) {
+            MappingEntry const& m = t->entries_[first + k];
+            std::int64_t const i = micro.slotOf(p.sources[k]);
+            if (i < 0 || m.handle != p.sources[k] || m.kind != PageKind::Micro
+                || m.valid_tokens != kMicroPageTokenCapacity
+                || m.logical_token_begin != std::uint64_t(p.logical_token_begin) + k * kMicroPageTokenCapacity
+                || micro.state[i] != PageState::Sealed || xm.pins[i] != 0) {
+                return false;
+            }
+            xm.pins[i] = 1;
+        }
+    }
+    for (auto const& [id, pages] : leases_) {
+        if (id == kInvalidPageLeaseId) {
+            return false;
+        }
+        for (PageHandle const h : pages) {
+            auto const [s, i] = core_.find(h);
+            ExpectedCounts& x = h.kind == PageKind::Extent ? xe : xm;
+            if (s == nullptr || s->state[i] == PageState::Free
+                || x.readers[i] == std::numeric_limits<std::uint32_t>::max()) {
+                return false;
+            }
+            ++x.readers[i];
+        }
+    }
+    return core_.auditSlots(micro, xm) && core_.auditSlots(extent, xe);
 }
 
 } // namespace kimkvcache

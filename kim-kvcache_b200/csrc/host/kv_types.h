@@ -224,6 +224,7 @@ public:
 private:
     friend class KvCacheManager;
     friend class FixedPageManager;
+    friend class TableEngine;
     std::vector<MappingEntry> entries_;
     std::uint64_t version_{0};
 };
