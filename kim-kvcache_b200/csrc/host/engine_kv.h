@@ -208,6 +208,16 @@ public:
     [[nodiscard]] TokenTransactionBackend* backend() const noexcept { return backend_.get(); }
 
 private:
+    // The three ways of advancing through the layers.
+    enum class Step : std::uint8_t { Write, Attend, AllLayers };
+    // None when `step` on `layer` is the transaction's next move;
+    // InvalidState when it is not live, LayerOutOfOrder otherwise.
+    [[nodiscard]] EngineKvError admit(Step step, std::uint32_t layer) const noexcept;
+    // The phase after an admitted step: the next one, or Failed.
+    void settle(Step step, EngineKvStatus const& outcome) noexcept;
+    // Ends a live transaction in `end` (Committed or RolledBack).
+    void finish(TokenTransactionPhase end) noexcept;
+    void adopt(TokenTransaction& other) noexcept;
     [[nodiscard]] bool active() const noexcept;
     void rollbackNoexcept() noexcept;
     void resetMovedFrom() noexcept;

@@ -212,6 +212,8 @@ typedef struct {
 typedef struct {
     kko_config c;
     uint32_t threads;
+    /* 1: the summation-order twin (kko_model_set_wide_sums) */
+    int wide;
     float *embed, *lm_head, *final_norm;
     layer_w* layer;
     sequence* seqs;
@@ -395,7 +397,7 @@ int kko_seq_fork(void* mp, uint64_t source, uint64_t child)
         return 0;
     }
     size_t const KV = (size_t)m->c.kv_heads * m->c.head_dim;
-    for (uint32_t l = 0; l < m->c.layers; ++l) {
+    for (uint32_t l = 0; src->length != 0 && l < m->c.layers; ++l) {
         memcpy(dst->keys[l], src->keys[l], sizeof(float) * KV * src->length);
         memcpy(dst->values[l], src->values[l], sizeof(float) * KV * src->length);
     }
@@ -479,7 +481,7 @@ typedef struct {
     const float* w;
     const float* x;
     float* y;
-    uint32_t rows, cols, batch, round;
+    uint32_t rows, cols, batch, round, wide;
 } matvec_ctx;
 
 static void matvec_row(void* p, uint32_t row)
@@ -489,8 +491,16 @@ static void matvec_row(void* p, uint32_t row)
     for (uint32_t b = 0; b < c->batch; ++b) {
         const float* x = c->x + (size_t)b * c->cols;
         float sum = 0.0f;
-        for (uint32_t i = 0; i < c->cols; ++i) {
-            sum += w[i] * x[i];
+        if (c->wide) {
+            double d = 0.0;
+            for (uint32_t i = 0; i < c->cols; ++i) {
+                d += (double)w[i] * (double)x[i];
+            }
+            sum = (float)d;
+        } else {
+            for (uint32_t i = 0; i < c->cols; ++i) {
+                sum += w[i] * x[i];
+            }
         }
         c->y[(size_t)b * c->rows + row] = c->round ? round16(sum) : sum;
     }
@@ -499,8 +509,18 @@ static void matvec_row(void* p, uint32_t row)
 static void matvec(model* m, const float* w, const float* x, float* y, uint32_t rows, uint32_t cols,
     uint32_t batch, int round)
 {
-    matvec_ctx c = {w, x, y, rows, cols, batch, (uint32_t)round};
+    matvec_ctx c = {w, x, y, rows, cols, batch, (uint32_t)round, (uint32_t)m->wide};
     parallel_for(m->threads, rows, matvec_row, &c);
+}
+
+/* The summation-order twin: the same arithmetic and FP16 rounding points,
+ * with the projection dot products summed in double precision and rounded
+ * to float once. Comparing the two measures how far a different (equally
+ * valid) summation order alone moves the outputs of this model: the noise
+ * floor any other implementation of the reference arithmetic meets. */
+void kko_model_set_wide_sums(void* mp, int wide)
+{
+    ((model*)mp)->wide = wide != 0;
 }
 
 static void rms_norm(const float* x, const float* w, float* y, uint32_t n, float eps)

@@ -63,6 +63,11 @@ int kko_seq_append_kv(void* model, uint64_t seq, uint32_t n, const uint16_t* k, 
 int kko_forward_batch(void* model, uint32_t n, const uint64_t* seqs, const uint32_t* token_ids,
     const uint32_t* positions, float* logits, uint16_t* final_hidden, uint32_t* tokens);
 
+/* 1: projections sum in double precision and round once (a second,
+ * equally valid summation order of the same arithmetic), to measure the
+ * model's sensitivity to summation order; 0: the reference's order. */
+void kko_model_set_wide_sums(void* model, int wide);
+
 /* First maximum (ties -> lowest index). */
 uint32_t kko_argmax(const float* values, uint32_t count);
 

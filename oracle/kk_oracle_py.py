@@ -84,6 +84,7 @@ def load() -> C.CDLL:
             "kko_forward_batch": (C.c_int, [C.c_void_p, C.c_uint32, u64p, u32p, u32p, f32p, u16p,
                                             u32p]),
             "kko_argmax": (C.c_uint32, [f32p, C.c_uint32]),
+            "kko_model_set_wide_sums": (None, [C.c_void_p, C.c_int]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
@@ -166,6 +167,9 @@ class Model:
         v = np.ascontiguousarray(v, dtype=np.uint16)
         n = k.shape[0]
         assert self.lib.kko_seq_append_kv(self.h, seq, n, ptr(k, C.c_uint16), ptr(v, C.c_uint16))
+
+    def set_wide_sums(self, wide: bool):
+        self.lib.kko_model_set_wide_sums(self.h, 1 if wide else 0)
 
     def forward(self, seqs, tokens, positions, want_logits=True, want_hidden=True):
         n = len(seqs)

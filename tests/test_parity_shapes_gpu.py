@@ -7,10 +7,13 @@ with ctx ~ U[64, 1024].
 Lanes are checked against the CPU oracle (the restatement of the
 reference's FP16-rounding decoder, tests/cuda/cuda_model_runner_test.cpp
 :213-420) fed the K/V the GPU holds for them (read back with the backend's
-gather). Gates as in the reference's runner contract (:536-553) and the
-logits within 2e-2 absolute on the steps that return
-logits, greedy tokens identical wherever the oracle's top-2 gap exceeds 2e-2
-on every step (the captured-graph steps included), every lane committed.
+gather). Gates (oracle/lane_parity.py): greedy tokens identical wherever the
+oracle's top-2 gap exceeds 2e-2 on every step (the captured-graph steps
+included); logits within 2e-2 absolute on the steps that return logits, or
+within 1.5 x the deviation of the oracle's own summation-order twin on the
+same rows where that floor is higher (never above the 0.035 the reference
+allows its own CUDA runner, cuda_model_runner_test.cpp:536); every lane
+committed.
 """
 import ctypes as C
 import importlib.util
@@ -97,7 +100,7 @@ def test_fused_step_matches_oracle_at_bench_shape(kk, tinyllama, config):
     rec = parity.record()
     print(config, rec)
     assert rec["logit_rows_compared"] == 2 * len(sel)
-    assert rec["max_abs_logit_err"] <= lp.TOL, rec
+    assert rec["max_abs_logit_err"] <= parity.logit_bound(), rec
     assert not parity.mismatches, parity.mismatches
     snap = kk.BackendSnapshot()
     R["backend_snapshot"](backend, C.byref(snap))
