@@ -1,63 +1,110 @@
-// Single-request greedy generation loop (reference semantics:
-// src/engine/generation.cpp:27-343): validate, create the KV request, prefill
-// one position per model call, then decode until EOS / max_new_tokens /
-// cancellation / stop; the KV request is always released at the end.
+// Single-request greedy generation and the default model SPI behaviour.
+// Reference semantics: src/engine/generation.cpp (validation, terminal
+// reasons and errors, release of the KV request on every exit, TTFT/TPOT).
+//
+// generate() walks the request's positions once: positions below the prompt
+// length feed prompt tokens, the ones after feed back the previous greedy
+// token, which is emitted first. Before every position the run may end
+// (stop, cancellation, EOS, max_new_tokens); close() turns any ending into
+// the terminal and releases the KV request.
 #include "generation.h"
 
 #include <chrono>
 #include <limits>
 #include <new>
+#include <optional>
 
 namespace kimkvcache {
 namespace {
 
 using Clock = std::chrono::steady_clock;
 
-std::uint64_t nanosBetween(Clock::time_point a, Clock::time_point b) noexcept
+std::uint64_t elapsedNs(Clock::time_point from, Clock::time_point to) noexcept
 {
-    auto const d = std::chrono::duration_cast<std::chrono::nanoseconds>(b - a).count();
-    return d > 0 ? static_cast<std::uint64_t>(d) : 0;
+    auto const ns = std::chrono::duration_cast<std::chrono::nanoseconds>(to - from).count();
+    return ns > 0 ? static_cast<std::uint64_t>(ns) : 0;
+}
+
+struct Ending {
+    GenerationTerminalReason reason;
+    GenerationError error;
+    std::string detail;
+};
+
+Ending failure(GenerationError e, std::string detail)
+{
+    return Ending{GenerationTerminalReason::Failed, e, std::move(detail)};
+}
+
+// Why a request cannot run on this model, if it cannot.
+std::optional<std::string> rejectReason(GenerationRequest const& r, TinyLlamaConfig const& m)
+{
+    std::size_t const prompt = r.prompt_token_ids.size();
+    std::uint32_t const max_new = r.sampling.max_new_tokens;
+    if (!m.valid() || r.request_id == kInvalidRequestId || prompt == 0 || max_new == 0) {
+        return std::string("a request needs an id, a prompt, max_new_tokens and a valid model");
+    }
+    if (prompt > m.max_position_embeddings || max_new > m.max_position_embeddings - prompt + 1) {
+        return std::string("prompt plus completion is longer than the model's positions");
+    }
+    if (r.sampling.eos_token_id.value_or(m.eos_token_id) >= m.vocabulary_size) {
+        return std::string("EOS token id is outside the vocabulary");
+    }
+    for (std::uint32_t t : r.prompt_token_ids) {
+        if (t >= m.vocabulary_size) {
+            return std::string("a prompt token id is outside the vocabulary");
+        }
+    }
+    return std::nullopt;
 }
 
 } // namespace
 
 std::string_view toString(GenerationError e) noexcept
 {
-    static constexpr std::string_view n[] = {"none", "invalid_argument", "runtime_stopped",
-        "model_failed", "kv_backend_failed", "internal_error"};
-    auto const i = static_cast<std::size_t>(e);
-    return i < 6 ? n[i] : "unknown";
+    switch (e) {
+    case GenerationError::None: return "none";
+    case GenerationError::InvalidArgument: return "invalid_argument";
+    case GenerationError::RuntimeStopped: return "runtime_stopped";
+    case GenerationError::ModelFailed: return "model_failed";
+    case GenerationError::KvBackendFailed: return "kv_backend_failed";
+    case GenerationError::InternalError: return "internal_error";
+    }
+    return "unknown";
 }
 
 std::string_view toString(GenerationTerminalReason r) noexcept
 {
-    static constexpr std::string_view n[] = {"eos_token", "max_new_tokens", "cancelled",
-        "runtime_stopped", "failed"};
-    auto const i = static_cast<std::size_t>(r);
-    return i < 5 ? n[i] : "unknown";
+    switch (r) {
+    case GenerationTerminalReason::EosToken: return "eos_token";
+    case GenerationTerminalReason::MaxNewTokens: return "max_new_tokens";
+    case GenerationTerminalReason::Cancelled: return "cancelled";
+    case GenerationTerminalReason::RuntimeStopped: return "runtime_stopped";
+    case GenerationTerminalReason::Failed: return "failed";
+    }
+    return "unknown";
 }
 
-GenerationBatchResult GenerationModelRunner::generationForwardBatch(
-    std::vector<GenerationBatchItem> const& batch)
+// ---- default model SPI -------------------------------------------------------------------------
+
+GenerationBatchResult GenerationModelRunner::generationForwardBatch(std::vector<GenerationBatchItem> const& batch)
 {
-    GenerationBatchResult result;
+    GenerationBatchResult out;
     if (batch.empty()) {
-        result.detail = "generation batch must not be empty";
-        return result;
+        out.detail = "an empty generation batch";
+        return out;
     }
     try {
-        result.steps.reserve(batch.size());
-        for (GenerationBatchItem const& item : batch) {
-            result.steps.push_back(
-                generationForwardToken(item.request_id, item.token_id, item.expected_position));
-        }
+        out.steps.resize(batch.size());
     } catch (std::bad_alloc const&) {
-        result.steps.clear();
-        result.detail = "generation batch result allocation failed";
-        return result;
+        out.detail = "no memory for the batch result";
+        return out;
     }
-    result.success = true;
-    return result;
+    for (std::size_t i = 0; i < batch.size(); ++i) {
+        out.steps[i] = generationForwardToken(batch[i].request_id, batch[i].token_id, batch[i].expected_position);
+    }
+    out.success = true;
+    return out;
 }
 
 std::uint32_t GenerationModelRunner::generationMaxBatchSize() const noexcept
@@ -65,157 +112,130 @@ std::uint32_t GenerationModelRunner::generationMaxBatchSize() const noexcept
     return std::numeric_limits<std::uint32_t>::max();
 }
 
+GenerationStepResult GenerationModelRunner::generationPrefill(RequestId, std::uint32_t const*, std::uint32_t,
+    std::uint32_t)
+{
+    return GenerationStepResult{false, 0, "this model runner has no fused prefill"};
+}
+
+// ---- single-request runtime ---------------------------------------------------------------------
+
 GenerationTerminal SingleRequestGenerationRuntime::generate(GenerationRequest const& request)
 {
-    Clock::time_point const started = Clock::now();
-    GenerationTerminal terminal;
-    terminal.request_id = request.request_id;
-    bool idle = false;
-    if (!generating_.compare_exchange_strong(idle, true, std::memory_order_acq_rel)) {
-        terminal.error = GenerationError::InvalidArgument;
-        terminal.detail = "single-request runtime is already generating";
-        terminal.metrics.e2e_ns = nanosBetween(started, Clock::now());
-        return terminal;
+    Clock::time_point const t0 = Clock::now();
+    GenerationTerminal out;
+    out.request_id = request.request_id;
+    bool expected_idle = false;
+    if (!generating_.compare_exchange_strong(expected_idle, true, std::memory_order_acq_rel)) {
+        out.error = GenerationError::InvalidArgument;
+        out.detail = "another generation is running on this runtime";
+        out.metrics.e2e_ns = elapsedNs(t0, Clock::now());
+        return out;
     }
-    struct Guard {
-        std::atomic<bool>& flag;
-        ~Guard() { flag.store(false, std::memory_order_release); }
-    } guard{generating_};
+    struct Idle {
+        std::atomic<bool>& busy;
+        ~Idle() { busy.store(false, std::memory_order_release); }
+    } const idle_on_exit{generating_};
 
-    TinyLlamaConfig const config = runner_->generationConfig();
-    bool created = false;
-    bool emitted = false;
-    Clock::time_point first_token{};
-    Clock::time_point last_token{};
-    auto cancelled = [&] { return request.cancellation && request.cancellation->cancelled(); };
-    auto finish = [&](GenerationTerminalReason reason, GenerationError error, std::string detail) {
-        terminal.reason = reason;
-        terminal.error = error;
-        terminal.detail = std::move(detail);
-        terminal.usage.completion_tokens = static_cast<std::uint32_t>(terminal.output_token_ids.size());
-        terminal.usage.total_tokens = terminal.usage.prompt_tokens + terminal.usage.completion_tokens;
-        if (created) {
+    TinyLlamaConfig const model = runner_->generationConfig();
+    bool kv_open = false;
+    std::optional<Clock::time_point> first_emit;
+    Clock::time_point last_emit{};
+    auto close = [&](Ending e) -> GenerationTerminal {
+        out.reason = e.reason;
+        out.error = e.error;
+        out.detail = std::move(e.detail);
+        out.usage.completion_tokens = static_cast<std::uint32_t>(out.output_token_ids.size());
+        out.usage.total_tokens = out.usage.prompt_tokens + out.usage.completion_tokens;
+        if (kv_open) {
+            kv_open = false;
             EngineKvStatus const released = kv_->releaseRequest(request.request_id);
-            created = false;
             if (!released.ok()) {
-                terminal.reason = GenerationTerminalReason::Failed;
-                terminal.error = GenerationError::KvBackendFailed;
-                terminal.detail = "release request failed: ";
-                terminal.detail += toString(released.error);
+                out.reason = GenerationTerminalReason::Failed;
+                out.error = GenerationError::KvBackendFailed;
+                out.detail = std::string("the KV request could not be released: ") + std::string(toString(released.error));
             }
         }
-        Clock::time_point const done = Clock::now();
-        terminal.metrics.e2e_ns = nanosBetween(started, done);
-        if (emitted) {
-            terminal.metrics.ttft_ns = nanosBetween(started, first_token);
-            if (terminal.output_token_ids.size() > 1) {
-                terminal.metrics.tpot_ns = nanosBetween(first_token, last_token)
-                    / (terminal.output_token_ids.size() - 1);
-            }
+        out.metrics.e2e_ns = elapsedNs(t0, Clock::now());
+        if (first_emit) {
+            out.metrics.ttft_ns = elapsedNs(t0, *first_emit);
+            std::size_t const n = out.output_token_ids.size();
+            out.metrics.tpot_ns = n > 1 ? elapsedNs(*first_emit, last_emit) / (n - 1) : 0;
         }
-        return terminal;
+        return out;
+    };
+    auto cancelled = [&] { return request.cancellation != nullptr && request.cancellation->cancelled(); };
+    // Stop wins over cancellation at every boundary.
+    auto interruption = [&](char const* where) -> std::optional<Ending> {
+        if (stopped()) {
+            return Ending{GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
+                std::string("runtime stopped ") + where};
+        }
+        if (cancelled()) {
+            return Ending{GenerationTerminalReason::Cancelled, GenerationError::None,
+                std::string("request cancelled ") + where};
+        }
+        return std::nullopt;
     };
 
     if (stopped()) {
-        return finish(GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
-            "runtime is stopped");
+        return close(Ending{GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
+            "runtime is stopped"});
     }
-    if (!config.valid() || request.request_id == kInvalidRequestId
-        || request.prompt_token_ids.empty() || request.sampling.max_new_tokens == 0) {
-        return finish(GenerationTerminalReason::Failed, GenerationError::InvalidArgument,
-            "request id, prompt, model config, and max_new_tokens are required");
+    std::size_t const prompt = request.prompt_token_ids.size();
+    bool const shaped = model.valid() && request.request_id != kInvalidRequestId && prompt != 0
+        && request.sampling.max_new_tokens != 0;
+    if (shaped) {
+        out.usage.prompt_tokens = static_cast<std::uint32_t>(prompt);
     }
-    terminal.usage.prompt_tokens = static_cast<std::uint32_t>(request.prompt_token_ids.size());
-    if (request.prompt_token_ids.size() > config.max_position_embeddings
-        || request.sampling.max_new_tokens
-            > config.max_position_embeddings - request.prompt_token_ids.size() + 1) {
-        return finish(GenerationTerminalReason::Failed, GenerationError::InvalidArgument,
-            "prompt and completion exceed the model position limit");
-    }
-    std::uint32_t const eos = request.sampling.eos_token_id.value_or(config.eos_token_id);
-    if (eos >= config.vocabulary_size) {
-        return finish(GenerationTerminalReason::Failed, GenerationError::InvalidArgument,
-            "EOS token is outside the model vocabulary");
-    }
-    for (std::uint32_t t : request.prompt_token_ids) {
-        if (t >= config.vocabulary_size) {
-            return finish(GenerationTerminalReason::Failed, GenerationError::InvalidArgument,
-                "prompt token is outside the model vocabulary");
-        }
+    if (std::optional<std::string> why = rejectReason(request, model)) {
+        return close(failure(GenerationError::InvalidArgument, std::move(*why)));
     }
     if (cancelled()) {
-        return finish(GenerationTerminalReason::Cancelled, GenerationError::None,
-            "request cancelled before prefill");
+        return close(Ending{GenerationTerminalReason::Cancelled, GenerationError::None,
+            "request cancelled before its prompt"});
     }
-    EngineKvStatus const made = kv_->createRequest(request.request_id);
-    if (!made.ok()) {
-        return finish(GenerationTerminalReason::Failed, GenerationError::KvBackendFailed,
-            std::string("create request failed: ") + std::string(toString(made.error)));
+    EngineKvStatus const created = kv_->createRequest(request.request_id);
+    if (!created.ok()) {
+        return close(failure(GenerationError::KvBackendFailed,
+            std::string("the KV request could not be created: ") + std::string(toString(created.error))));
     }
-    created = true;
+    kv_open = true;
 
-    auto step = [&](std::uint32_t token, std::uint32_t position, std::uint32_t& next) -> bool {
-        GenerationStepResult s = runner_->generationForwardToken(request.request_id, token, position);
-        if (!s.success) {
-            finish(GenerationTerminalReason::Failed, GenerationError::ModelFailed, std::move(s.detail));
-            return false;
-        }
-        if (s.greedy_token_id >= config.vocabulary_size) {
-            finish(GenerationTerminalReason::Failed, GenerationError::ModelFailed,
-                "model returned a token outside the vocabulary");
-            return false;
-        }
-        next = s.greedy_token_id;
-        return true;
-    };
-
+    std::uint32_t const eos = request.sampling.eos_token_id.value_or(model.eos_token_id);
     std::uint32_t next = 0;
-    for (std::size_t pos = 0; pos < request.prompt_token_ids.size(); ++pos) {
-        if (stopped()) {
-            return finish(GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
-                "runtime stopped during prefill");
+    for (std::size_t pos = 0;; ++pos) {
+        bool const decoding = pos >= prompt;
+        if (std::optional<Ending> e = interruption(decoding ? "during decode" : "during the prompt")) {
+            return close(std::move(*e));
         }
-        if (cancelled()) {
-            return finish(GenerationTerminalReason::Cancelled, GenerationError::None,
-                "request cancelled during prefill");
+        if (decoding) {
+            try {
+                out.output_token_ids.push_back(next);
+            } catch (std::bad_alloc const&) {
+                return close(failure(GenerationError::InternalError, "no memory for the completion"));
+            }
+            last_emit = Clock::now();
+            first_emit = first_emit.value_or(last_emit);
+            if (next == eos) {
+                return close(Ending{GenerationTerminalReason::EosToken, GenerationError::None, "EOS generated"});
+            }
+            if (out.output_token_ids.size() == request.sampling.max_new_tokens) {
+                return close(Ending{GenerationTerminalReason::MaxNewTokens, GenerationError::None,
+                    "max_new_tokens generated"});
+            }
         }
-        if (!step(request.prompt_token_ids[pos], static_cast<std::uint32_t>(pos), next)) {
-            return terminal;
+        std::uint32_t const token = decoding ? next : request.prompt_token_ids[pos];
+        GenerationStepResult step = runner_->generationForwardToken(request.request_id, token,
+            static_cast<std::uint32_t>(pos));
+        if (!step.success) {
+            return close(failure(GenerationError::ModelFailed, std::move(step.detail)));
         }
+        if (step.greedy_token_id >= model.vocabulary_size) {
+            return close(failure(GenerationError::ModelFailed, "the model returned a token outside the vocabulary"));
+        }
+        next = step.greedy_token_id;
     }
-    for (std::uint32_t generated = 0; generated < request.sampling.max_new_tokens; ++generated) {
-        if (stopped()) {
-            return finish(GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
-                "runtime stopped during decode");
-        }
-        if (cancelled()) {
-            return finish(GenerationTerminalReason::Cancelled, GenerationError::None,
-                "request cancelled during decode");
-        }
-        try {
-            terminal.output_token_ids.push_back(next);
-        } catch (std::bad_alloc const&) {
-            return finish(GenerationTerminalReason::Failed, GenerationError::InternalError,
-                "completion token allocation failed");
-        }
-        last_token = Clock::now();
-        if (!emitted) {
-            first_token = last_token;
-            emitted = true;
-        }
-        if (next == eos) {
-            return finish(GenerationTerminalReason::EosToken, GenerationError::None, "EOS token generated");
-        }
-        if (generated + 1 == request.sampling.max_new_tokens) {
-            return finish(GenerationTerminalReason::MaxNewTokens, GenerationError::None,
-                "max_new_tokens reached");
-        }
-        if (!step(next, terminal.usage.prompt_tokens + generated, next)) {
-            return terminal;
-        }
-    }
-    return finish(GenerationTerminalReason::Failed, GenerationError::InternalError,
-        "generation loop exited without a terminal reason");
 }
 
 } // namespace kimkvcache

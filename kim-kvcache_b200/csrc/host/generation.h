@@ -52,6 +52,12 @@ struct GenerationRequest final {
     std::vector<std::uint32_t> prompt_token_ids{};
     SamplingConfig sampling{};
     std::shared_ptr<GenerationCancellationToken> cancellation{};
+    // Extension (no counterpart in the reference): the first
+    // kv_prefix_tokens prompt positions are already committed under
+    // request_id in the KV backend, e.g. a prefix shared by forking another
+    // request. The scheduler then neither creates the KV request nor feeds
+    // those positions; it must be below the prompt length. 0: none.
+    std::uint32_t kv_prefix_tokens{0};
 };
 
 struct GenerationUsage final {
@@ -115,6 +121,15 @@ public:
     [[nodiscard]] virtual GenerationBatchResult generationForwardBatch(
         std::vector<GenerationBatchItem> const& batch);
     [[nodiscard]] virtual std::uint32_t generationMaxBatchSize() const noexcept;
+    // Extension (no counterpart in the reference, which feeds a prompt one
+    // position per model batch): consecutive prompt positions
+    // [first_position, first_position + count) of one request in one call,
+    // each attending causally; returns the greedy token after the last one.
+    // The committed KV length must equal first_position. Runners without a
+    // fused prefill keep the default, which reports it unsupported.
+    [[nodiscard]] virtual bool generationSupportsPrefill() const noexcept { return false; }
+    [[nodiscard]] virtual GenerationStepResult generationPrefill(RequestId request_id,
+        std::uint32_t const* tokens, std::uint32_t count, std::uint32_t first_position);
 
 protected:
     GenerationModelRunner() = default;

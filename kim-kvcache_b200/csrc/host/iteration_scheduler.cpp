@@ -1,7 +1,14 @@
-// FIFO iteration scheduler (reference semantics:
-// src/engine/iteration_scheduler.cpp:27-772). Batch composition, terminal
-// order and metrics bookkeeping follow the reference step by step, so the
-// same submissions produce the same sequence of model batches.
+// Iteration-level FIFO scheduler. Reference semantics:
+// src/engine/iteration_scheduler.cpp (admission gates, quotas, waves, batch
+// splitting, terminal handling); the parity tests replay the same
+// submissions on both and compare every model batch, counter and terminal.
+//
+// An iteration takes up to max_batched_tokens requests off the FIFO as
+// Lanes, each with its quota of positions. Lanes are then advanced in waves:
+// a wave asks every lane with quota left for its next position (in FIFO
+// order, while the token budget lasts), and runs the wave as model batches
+// of at most the runner's batch size. A Slot is one admitted request: what
+// it feeds next, how it takes a model step, how it ends.
 #include "iteration_scheduler.h"
 
 #include <algorithm>
@@ -15,477 +22,533 @@ namespace {
 
 using Clock = std::chrono::steady_clock;
 
-std::uint64_t nanosBetween(Clock::time_point a, Clock::time_point b) noexcept
+std::uint64_t elapsedNs(Clock::time_point from, Clock::time_point to) noexcept
 {
-    auto const d = std::chrono::duration_cast<std::chrono::nanoseconds>(b - a).count();
-    return d > 0 ? static_cast<std::uint64_t>(d) : 0;
+    auto const ns = std::chrono::duration_cast<std::chrono::nanoseconds>(to - from).count();
+    return ns > 0 ? static_cast<std::uint64_t>(ns) : 0;
 }
 
-// Worst-case committed KV tokens of a request: the last generated token is
-// never fed back through the model.
-std::uint64_t kvBudget(GenerationRequest const& r) noexcept
+// Committed KV tokens a request can reach: prompt + completion minus the
+// last generated token, which never goes back through the model.
+std::uint64_t kvTokensNeeded(GenerationRequest const& r) noexcept
 {
-    return static_cast<std::uint64_t>(r.prompt_token_ids.size()) + r.sampling.max_new_tokens - 1;
+    return r.prompt_token_ids.size() + std::uint64_t(r.sampling.max_new_tokens) - 1;
 }
+
+struct Slot {
+    GenerationRequest req;
+    GenerationTerminal out;
+    SchedulerRequestState state{SchedulerRequestState::Waiting};
+    std::uint64_t kv_tokens{0};
+    std::uint32_t fed{0};          // prompt positions that went through the model (or came as a prefix)
+    bool kv_open{false};
+    bool cancel{false};
+    Clock::time_point admitted{};
+    bool emitted{false};
+    Clock::time_point first_emit{};
+    Clock::time_point last_emit{};
+
+    [[nodiscard]] std::uint32_t promptLen() const noexcept
+    {
+        return static_cast<std::uint32_t>(req.prompt_token_ids.size());
+    }
+    [[nodiscard]] bool prefilling() const noexcept { return fed < promptLen(); }
+    [[nodiscard]] bool closed() const noexcept { return state == SchedulerRequestState::Terminal; }
+    [[nodiscard]] bool cancelSeen() const noexcept
+    {
+        return cancel || (req.cancellation != nullptr && req.cancellation->cancelled());
+    }
+    // The position this request feeds next: a prompt token, or its last
+    // output fed back.
+    [[nodiscard]] GenerationBatchItem nextItem() const
+    {
+        if (prefilling()) {
+            return GenerationBatchItem{req.request_id, req.prompt_token_ids[fed], fed};
+        }
+        std::uint32_t const pos = out.usage.prompt_tokens + static_cast<std::uint32_t>(out.output_token_ids.size()) - 1;
+        return GenerationBatchItem{req.request_id, out.output_token_ids.back(), pos};
+    }
+};
+
+struct Lane {
+    Slot* slot;
+    std::uint32_t quota;
+};
+
+// A planned model position of a wave.
+struct Cell {
+    Slot* slot;
+    GenerationBatchItem item;
+    bool prompt;
+};
 
 } // namespace
 
 class IterationSchedulerRuntime::Impl final {
 public:
-    struct Record final {
-        GenerationRequest request{};
-        SchedulerRequestState state{SchedulerRequestState::Created};
-        GenerationTerminal terminal{};
-        std::uint64_t kv_budget{0};
-        std::uint32_t prompt_position{0};
-        bool kv_created{false};
-        bool cancel_requested{false};
-        bool emitted{false};
-        Clock::time_point started{};
-        Clock::time_point first_token{};
-        Clock::time_point last_token{};
-    };
-
     Impl(EngineKvBackend& k, GenerationModelRunner& r, IterationSchedulerConfig c) noexcept
         : kv(&k), runner(&r), config(c)
     {
     }
 
-    void setState(RequestId id, SchedulerRequestState s)
+    EngineKvBackend* kv;
+    GenerationModelRunner* runner;
+    IterationSchedulerConfig config;
+    std::atomic<bool> halted{false};
+    std::unordered_map<RequestId, Slot> slots;
+    std::unordered_map<RequestId, SchedulerRequestState> status;  // every id ever submitted
+    std::deque<RequestId> fifo;
+    std::vector<GenerationTerminal> done;
+    std::uint64_t iterations{0};
+    std::uint64_t kv_reserved{0};
+    SchedulerIterationResult totals{};
+
+    [[nodiscard]] bool stopped() const noexcept { return halted.load(std::memory_order_acquire); }
+
+    void mark(Slot& s, SchedulerRequestState st)
     {
-        auto const f = states.find(id);
-        if (f != states.end()) {
-            f->second = s;
+        s.state = st;
+        auto const f = status.find(s.req.request_id);
+        if (f != status.end()) {
+            f->second = st;
         }
     }
 
-    SchedulerAdmissionResult reject(RequestId id, SchedulerAdmissionError e, std::string detail,
-        bool remember)
+    // ---- admission ----
+
+    SchedulerAdmissionResult refuse(RequestId id, SchedulerAdmissionError e, std::string why, bool record)
     {
-        if (remember && id != kInvalidRequestId) {
+        if (record && id != kInvalidRequestId) {
             try {
-                states.emplace(id, SchedulerRequestState::Rejected);
+                status.emplace(id, SchedulerRequestState::Rejected);
             } catch (std::bad_alloc const&) {
-                return {false, SchedulerAdmissionError::InternalError, "failed to record rejected request"};
+                return {false, SchedulerAdmissionError::InternalError, "no memory to record the rejection"};
             }
         }
-        return {false, e, std::move(detail)};
+        return {false, e, std::move(why)};
     }
 
-    std::optional<std::string> invalidReason(GenerationRequest const& r) const
+    std::optional<std::string> invalid(GenerationRequest const& r) const
     {
-        TinyLlamaConfig const m = runner->generationConfig();
         if (!config.valid()) {
-            return "scheduler configuration is invalid";
+            return std::string("the scheduler configuration is invalid");
         }
-        if (!m.valid() || r.request_id == kInvalidRequestId || r.prompt_token_ids.empty()
-            || r.sampling.max_new_tokens == 0) {
-            return "request id, prompt, model config, and max_new_tokens are required";
+        TinyLlamaConfig const m = runner->generationConfig();
+        std::size_t const prompt = r.prompt_token_ids.size();
+        if (!m.valid() || r.request_id == kInvalidRequestId || prompt == 0 || r.sampling.max_new_tokens == 0) {
+            return std::string("a request needs an id, a prompt, max_new_tokens and a valid model");
         }
-        if (r.prompt_token_ids.size() > m.max_position_embeddings
-            || r.sampling.max_new_tokens > m.max_position_embeddings - r.prompt_token_ids.size() + 1) {
-            return "prompt and completion exceed the model position limit";
+        if (prompt > m.max_position_embeddings || r.sampling.max_new_tokens > m.max_position_embeddings - prompt + 1) {
+            return std::string("prompt plus completion is longer than the model's positions");
         }
         if (r.sampling.eos_token_id.value_or(m.eos_token_id) >= m.vocabulary_size) {
-            return "EOS token is outside the model vocabulary";
+            return std::string("EOS token id is outside the vocabulary");
         }
-        for (std::uint32_t t : r.prompt_token_ids) {
-            if (t >= m.vocabulary_size) {
-                return "prompt token is outside the model vocabulary";
-            }
+        if (std::any_of(r.prompt_token_ids.begin(), r.prompt_token_ids.end(),
+                [&](std::uint32_t t) { return t >= m.vocabulary_size; })) {
+            return std::string("a prompt token id is outside the vocabulary");
+        }
+        if (r.kv_prefix_tokens >= prompt) {
+            return std::string("the KV prefix must leave at least one prompt position to feed");
         }
         return std::nullopt;
     }
 
-    void finish(Record& rec, GenerationTerminalReason reason, GenerationError error, std::string detail)
+    // ---- endings ----
+
+    void close(Slot& s, GenerationTerminalReason reason, GenerationError error, std::string detail)
     {
-        if (rec.state == SchedulerRequestState::Terminal) {
+        if (s.closed()) {
             return;
         }
-        GenerationTerminal& t = rec.terminal;
+        GenerationTerminal& t = s.out;
         t.reason = reason;
         t.error = error;
         t.detail = std::move(detail);
         t.usage.completion_tokens = static_cast<std::uint32_t>(t.output_token_ids.size());
         t.usage.total_tokens = t.usage.prompt_tokens + t.usage.completion_tokens;
-        if (rec.kv_created) {
-            EngineKvStatus const released = kv->releaseRequest(rec.request.request_id);
-            rec.kv_created = false;
+        if (s.kv_open) {
+            s.kv_open = false;
+            EngineKvStatus const released = kv->releaseRequest(s.req.request_id);
             if (!released.ok()) {
                 t.reason = GenerationTerminalReason::Failed;
                 t.error = GenerationError::KvBackendFailed;
-                t.detail = "release request failed: ";
-                t.detail += toString(released.error);
+                t.detail = std::string("the KV request could not be released: ") + std::string(toString(released.error));
             }
         }
-        Clock::time_point const now = Clock::now();
-        t.metrics.e2e_ns = nanosBetween(rec.started, now);
-        if (rec.emitted) {
-            t.metrics.ttft_ns = nanosBetween(rec.started, rec.first_token);
-            if (t.output_token_ids.size() > 1) {
-                t.metrics.tpot_ns = nanosBetween(rec.first_token, rec.last_token)
-                    / (t.output_token_ids.size() - 1);
-            }
+        t.metrics.e2e_ns = elapsedNs(s.admitted, Clock::now());
+        if (s.emitted) {
+            t.metrics.ttft_ns = elapsedNs(s.admitted, s.first_emit);
+            std::size_t const n = t.output_token_ids.size();
+            t.metrics.tpot_ns = n > 1 ? elapsedNs(s.first_emit, s.last_emit) / (n - 1) : 0;
         }
-        rec.state = SchedulerRequestState::Terminal;
-        setState(rec.request.request_id, SchedulerRequestState::Terminal);
-        reserved_kv_tokens -= rec.kv_budget;
+        mark(s, SchedulerRequestState::Terminal);
+        kv_reserved -= s.kv_tokens;
         try {
-            terminals.push_back(t);
+            done.push_back(t);
         } catch (std::bad_alloc const&) {
         }
     }
 
-    void stopRecord(Record& rec)
+    void closeStopped(Slot& s)
     {
-        finish(rec, GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
-            "runtime stopped at iteration boundary");
+        close(s, GenerationTerminalReason::RuntimeStopped, GenerationError::RuntimeStopped,
+            "runtime stopped between iterations");
     }
 
-    void stopAll()
+    void closeCancelled(Slot& s)
     {
-        while (!queue.empty()) {
-            RequestId const id = queue.front();
-            queue.pop_front();
-            auto const f = records.find(id);
-            if (f != records.end() && f->second.state != SchedulerRequestState::Terminal) {
-                stopRecord(f->second);
+        close(s, GenerationTerminalReason::Cancelled, GenerationError::None, "request cancelled between iterations");
+    }
+
+    void closeFailed(Slot& s, GenerationError e, std::string why)
+    {
+        close(s, GenerationTerminalReason::Failed, e, std::move(why));
+    }
+
+    void stopQueued()
+    {
+        while (!fifo.empty()) {
+            auto const f = slots.find(fifo.front());
+            fifo.pop_front();
+            if (f != slots.end() && !f->second.closed()) {
+                closeStopped(f->second);
             }
         }
     }
 
-    bool cancelledOrStopped(Record& rec)
-    {
-        if (rec.cancel_requested || (rec.request.cancellation && rec.request.cancellation->cancelled())) {
-            finish(rec, GenerationTerminalReason::Cancelled, GenerationError::None,
-                "request cancelled at iteration boundary");
-            return true;
-        }
-        if (stopped.load(std::memory_order_acquire)) {
-            stopRecord(rec);
-            return true;
-        }
-        return false;
-    }
+    // ---- one model position of a slot ----
 
-    // Next position of a request; creates its KV request on first touch.
-    bool prepare(Record& rec, GenerationBatchItem& item, bool& prefill)
+    // True when the slot may feed a position now: not cancelled or stopped,
+    // and its KV request open (created on first use unless it came with a
+    // committed prefix).
+    bool ready(Slot& s)
     {
-        if (cancelledOrStopped(rec)) {
+        if (s.cancelSeen()) {
+            closeCancelled(s);
             return false;
         }
-        if (!rec.kv_created) {
-            EngineKvStatus const created = kv->createRequest(rec.request.request_id);
-            if (!created.ok()) {
-                finish(rec, GenerationTerminalReason::Failed, GenerationError::KvBackendFailed,
-                    std::string("create request failed: ") + std::string(toString(created.error)));
-                return false;
-            }
-            rec.kv_created = true;
-            rec.state = SchedulerRequestState::Running;
-            setState(rec.request.request_id, SchedulerRequestState::Running);
+        if (stopped()) {
+            closeStopped(s);
+            return false;
         }
-        prefill = rec.prompt_position < rec.request.prompt_token_ids.size();
-        if (prefill) {
-            item = {rec.request.request_id, rec.request.prompt_token_ids[rec.prompt_position],
-                rec.prompt_position};
-        } else {
-            std::uint32_t const pos = rec.terminal.usage.prompt_tokens
-                + static_cast<std::uint32_t>(rec.terminal.output_token_ids.size()) - 1;
-            item = {rec.request.request_id, rec.terminal.output_token_ids.back(), pos};
+        if (!s.kv_open) {
+            if (s.req.kv_prefix_tokens == 0) {
+                EngineKvStatus const made = kv->createRequest(s.req.request_id);
+                if (!made.ok()) {
+                    closeFailed(s, GenerationError::KvBackendFailed,
+                        std::string("the KV request could not be created: ") + std::string(toString(made.error)));
+                    return false;
+                }
+            }
+            s.kv_open = true;
+            mark(s, SchedulerRequestState::Running);
         }
         return true;
     }
 
-    void apply(Record& rec, GenerationStepResult step, bool prefill)
+    // Takes the model's answer for `positions` positions of the slot (one
+    // unless a fused prompt chunk).
+    void take(Slot& s, GenerationStepResult step, std::uint32_t prompt_positions)
     {
-        if (!step.success) {
-            finish(rec, GenerationTerminalReason::Failed, GenerationError::ModelFailed, std::move(step.detail));
-            return;
-        }
         TinyLlamaConfig const m = runner->generationConfig();
+        if (!step.success) {
+            closeFailed(s, GenerationError::ModelFailed, std::move(step.detail));
+            return;
+        }
         if (step.greedy_token_id >= m.vocabulary_size) {
-            finish(rec, GenerationTerminalReason::Failed, GenerationError::ModelFailed,
-                "model returned a token outside the vocabulary");
+            closeFailed(s, GenerationError::ModelFailed, "the model returned a token outside the vocabulary");
             return;
         }
-        if (prefill) {
-            ++rec.prompt_position;
-        }
-        if (stopped.load(std::memory_order_acquire)) {
-            stopRecord(rec);
+        s.fed += prompt_positions;
+        // After a model step, stop wins over cancellation.
+        if (stopped()) {
+            closeStopped(s);
             return;
         }
-        if (rec.cancel_requested || (rec.request.cancellation && rec.request.cancellation->cancelled())) {
-            finish(rec, GenerationTerminalReason::Cancelled, GenerationError::None,
-                "request cancelled at iteration boundary");
+        if (s.cancelSeen()) {
+            closeCancelled(s);
             return;
         }
-        if (rec.prompt_position != rec.request.prompt_token_ids.size()) {
-            return;  // still prefilling: the step's token is not an output
+        if (s.prefilling()) {
+            return;  // a prompt position's prediction is not an output
         }
         try {
-            rec.terminal.output_token_ids.push_back(step.greedy_token_id);
+            s.out.output_token_ids.push_back(step.greedy_token_id);
         } catch (std::bad_alloc const&) {
-            finish(rec, GenerationTerminalReason::Failed, GenerationError::InternalError,
-                "completion token allocation failed");
+            closeFailed(s, GenerationError::InternalError, "no memory for the completion");
             return;
         }
-        rec.last_token = Clock::now();
-        if (!rec.emitted) {
-            rec.first_token = rec.last_token;
-            rec.emitted = true;
+        s.last_emit = Clock::now();
+        if (!s.emitted) {
+            s.emitted = true;
+            s.first_emit = s.last_emit;
         }
-        std::uint32_t const eos = rec.request.sampling.eos_token_id.value_or(m.eos_token_id);
-        if (step.greedy_token_id == eos) {
-            finish(rec, GenerationTerminalReason::EosToken, GenerationError::None, "EOS token generated");
-        } else if (rec.terminal.output_token_ids.size() == rec.request.sampling.max_new_tokens) {
-            finish(rec, GenerationTerminalReason::MaxNewTokens, GenerationError::None,
-                "max_new_tokens reached");
+        if (step.greedy_token_id == s.req.sampling.eos_token_id.value_or(m.eos_token_id)) {
+            close(s, GenerationTerminalReason::EosToken, GenerationError::None, "EOS generated");
+        } else if (s.out.output_token_ids.size() == s.req.sampling.max_new_tokens) {
+            close(s, GenerationTerminalReason::MaxNewTokens, GenerationError::None, "max_new_tokens generated");
         }
     }
 
-    EngineKvBackend* kv;
-    GenerationModelRunner* runner;
-    IterationSchedulerConfig config;
-    std::atomic<bool> stopped{false};
-    std::unordered_map<RequestId, Record> records;
-    std::unordered_map<RequestId, SchedulerRequestState> states;
-    std::deque<RequestId> queue;
-    std::vector<GenerationTerminal> terminals;
-    std::uint64_t iterations{0};
-    std::uint64_t reserved_kv_tokens{0};
-    std::uint64_t forward_tokens{0};
-    std::uint64_t forward_batches{0};
-    std::uint64_t prefill_tokens{0};
-    std::uint64_t decode_tokens{0};
+    // ---- an iteration ----
+
+    std::vector<Lane> pickLanes(SchedulerIterationResult&)
+    {
+        std::vector<Lane> lanes;
+        std::size_t n = std::min<std::size_t>(fifo.size(), config.max_batched_tokens);
+        try {
+            lanes.reserve(n);
+            for (; n != 0; --n) {
+                auto const f = slots.find(fifo.front());
+                fifo.pop_front();
+                if (f == slots.end() || f->second.closed()) {
+                    continue;
+                }
+                Slot& s = f->second;
+                std::uint32_t const left = s.promptLen() - s.fed;
+                lanes.push_back(Lane{&s, left == 0 ? 1u : std::min(left, config.prefill_chunk_size)});
+            }
+        } catch (std::bad_alloc const&) {
+            failLanes(lanes, GenerationError::InternalError, "no memory to plan the iteration");
+        }
+        return lanes;
+    }
+
+    void failLanes(std::vector<Lane> const& lanes, GenerationError e, char const* why)
+    {
+        for (Lane const& l : lanes) {
+            closeFailed(*l.slot, e, why);
+        }
+    }
+
+    // Fused prompt chunks: one model call per prompt lane for its quota
+    // (bounded by the token budget); decode lanes are left for the waves.
+    void fusedPrompts(std::vector<Lane>& lanes, std::uint32_t& budget, SchedulerIterationResult& r)
+    {
+        for (Lane& l : lanes) {
+            Slot& s = *l.slot;
+            if (budget == 0 || l.quota == 0 || s.closed() || !s.prefilling()) {
+                continue;
+            }
+            if (!ready(s)) {
+                l.quota = 0;
+                continue;
+            }
+            std::uint32_t const n = std::min(l.quota, budget);
+            GenerationStepResult step = runner->generationPrefill(s.req.request_id, s.req.prompt_token_ids.data() + s.fed,
+                n, s.fed);
+            l.quota = 0;
+            budget -= n;
+            ++r.model_forward_batches;
+            r.model_forward_tokens += n;
+            r.prefill_tokens += n;
+            take(s, std::move(step), n);
+            if (stopped()) {
+                return;
+            }
+        }
+    }
+
+    // The next wave: one position of every lane with quota left, in FIFO
+    // order, while the budget lasts.
+    std::vector<Cell> nextWave(std::vector<Lane>& lanes, std::uint32_t& budget)
+    {
+        std::vector<Cell> wave;
+        wave.reserve(std::min<std::size_t>(lanes.size(), budget));
+        for (Lane& l : lanes) {
+            if (budget == 0) {
+                break;
+            }
+            if (l.quota == 0 || l.slot->closed()) {
+                continue;
+            }
+            if (!ready(*l.slot)) {
+                l.quota = 0;
+                continue;
+            }
+            wave.push_back(Cell{l.slot, l.slot->nextItem(), l.slot->prefilling()});
+            --l.quota;
+            --budget;
+        }
+        return wave;
+    }
+
+    // Runs a wave as model batches of at most `cap` positions.
+    void runWave(std::vector<Cell> const& wave, std::uint32_t cap, SchedulerIterationResult& r)
+    {
+        for (std::size_t lo = 0; lo < wave.size(); lo += cap) {
+            std::size_t const hi = std::min<std::size_t>(wave.size(), lo + cap);
+            std::vector<GenerationBatchItem> batch;
+            try {
+                batch.reserve(hi - lo);
+                for (std::size_t i = lo; i < hi; ++i) {
+                    batch.push_back(wave[i].item);
+                }
+            } catch (std::bad_alloc const&) {
+                for (std::size_t i = lo; i < hi; ++i) {
+                    closeFailed(*wave[i].slot, GenerationError::InternalError, "no memory for the model batch");
+                }
+                continue;
+            }
+            GenerationBatchResult res = runner->generationForwardBatch(batch);
+            ++r.model_forward_batches;
+            r.model_forward_tokens += static_cast<std::uint32_t>(batch.size());
+            for (std::size_t i = lo; i < hi; ++i) {
+                ++(wave[i].prompt ? r.prefill_tokens : r.decode_tokens);
+            }
+            bool const well_formed = res.success && res.steps.size() == batch.size();
+            std::string const why = well_formed ? std::string()
+                : (res.detail.empty() ? std::string("the model returned a malformed batch result") : res.detail);
+            for (std::size_t i = lo; i < hi; ++i) {
+                if (well_formed) {
+                    take(*wave[i].slot, std::move(res.steps[i - lo]), wave[i].prompt ? 1u : 0u);
+                } else {
+                    closeFailed(*wave[i].slot, GenerationError::ModelFailed, why);
+                }
+            }
+            if (stopped()) {
+                return;
+            }
+        }
+    }
+
+    SchedulerIterationResult iterate()
+    {
+        SchedulerIterationResult r;
+        r.iteration = ++iterations;
+        std::size_t const ended_before = done.size();
+        if (stopped()) {
+            stopQueued();
+            r.terminals_produced = static_cast<std::uint32_t>(done.size() - ended_before);
+            return r;
+        }
+        std::vector<Lane> lanes = pickLanes(r);
+        std::uint32_t budget = config.max_batched_tokens;
+        std::uint32_t const cap = runner->generationMaxBatchSize();
+        if (cap == 0) {
+            failLanes(lanes, GenerationError::ModelFailed, "the model runner reports a zero batch size");
+        } else {
+            if (config.fused_prefill && runner->generationSupportsPrefill()) {
+                fusedPrompts(lanes, budget, r);
+            }
+            while (budget != 0) {
+                std::vector<Cell> wave;
+                try {
+                    wave = nextWave(lanes, budget);
+                } catch (std::bad_alloc const&) {
+                    failLanes(lanes, GenerationError::InternalError, "no memory for the model batch");
+                    break;
+                }
+                if (wave.empty()) {
+                    break;
+                }
+                runWave(wave, cap, r);
+                if (stopped()) {
+                    break;
+                }
+            }
+        }
+        totals.model_forward_tokens += r.model_forward_tokens;
+        totals.model_forward_batches += r.model_forward_batches;
+        totals.prefill_tokens += r.prefill_tokens;
+        totals.decode_tokens += r.decode_tokens;
+        // Live lanes go back to the end of the FIFO (or end, on a stop).
+        for (Lane const& l : lanes) {
+            if (l.slot->closed()) {
+                continue;
+            }
+            if (stopped()) {
+                closeStopped(*l.slot);
+            } else {
+                fifo.push_back(l.slot->req.request_id);
+            }
+        }
+        if (stopped()) {
+            stopQueued();
+        }
+        r.terminals_produced = static_cast<std::uint32_t>(done.size() - ended_before);
+        return r;
+    }
 };
 
-IterationSchedulerRuntime::IterationSchedulerRuntime(EngineKvBackend& kv,
-    GenerationModelRunner& runner, IterationSchedulerConfig config)
+IterationSchedulerRuntime::IterationSchedulerRuntime(EngineKvBackend& kv, GenerationModelRunner& runner,
+    IterationSchedulerConfig config)
     : impl_(std::make_unique<Impl>(kv, runner, config))
 {
 }
 
 IterationSchedulerRuntime::~IterationSchedulerRuntime()
 {
-    if (impl_) {
-        impl_->stopped.store(true, std::memory_order_release);
-        impl_->stopAll();
+    if (impl_ != nullptr) {
+        impl_->halted.store(true, std::memory_order_release);
+        impl_->stopQueued();
     }
 }
 
 SchedulerAdmissionResult IterationSchedulerRuntime::submit(GenerationRequest request)
 {
     Impl& im = *impl_;
+    RequestId const id = request.request_id;
     if (stopped()) {
-        return im.reject(request.request_id, SchedulerAdmissionError::RuntimeStopped,
-            "runtime is stopped", true);
+        return im.refuse(id, SchedulerAdmissionError::RuntimeStopped, "runtime is stopped", true);
     }
-    if (im.states.find(request.request_id) != im.states.end()) {
-        return im.reject(request.request_id, SchedulerAdmissionError::DuplicateRequest,
-            "request id has already been submitted", false);
+    if (im.status.count(id) != 0) {
+        return im.refuse(id, SchedulerAdmissionError::DuplicateRequest, "this request id was submitted before", false);
     }
-    if (std::optional<std::string> why = im.invalidReason(request)) {
-        return im.reject(request.request_id, SchedulerAdmissionError::InvalidArgument,
-            std::move(*why), true);
+    if (std::optional<std::string> why = im.invalid(request)) {
+        return im.refuse(id, SchedulerAdmissionError::InvalidArgument, std::move(*why), true);
     }
     if (snapshot().activeCount() >= im.config.max_active_requests) {
-        return im.reject(request.request_id, SchedulerAdmissionError::MaxActiveRequests,
-            "max_active_requests admission gate rejected request", true);
+        return im.refuse(id, SchedulerAdmissionError::MaxActiveRequests, "max_active_requests reached", true);
     }
-    std::uint64_t const budget = kvBudget(request);
-    if (budget > im.config.max_kv_tokens
-        || im.reserved_kv_tokens > im.config.max_kv_tokens - budget) {
-        return im.reject(request.request_id, SchedulerAdmissionError::KvTokenBudget,
-            "KV token budget admission gate rejected request", true);
+    std::uint64_t const need = kvTokensNeeded(request);
+    if (need > im.config.max_kv_tokens || im.kv_reserved > im.config.max_kv_tokens - need) {
+        return im.refuse(id, SchedulerAdmissionError::KvTokenBudget, "max_kv_tokens would be exceeded", true);
     }
     try {
-        Impl::Record rec;
-        rec.request = std::move(request);
-        rec.state = SchedulerRequestState::Waiting;
-        rec.terminal.request_id = rec.request.request_id;
-        rec.terminal.usage.prompt_tokens = static_cast<std::uint32_t>(rec.request.prompt_token_ids.size());
-        rec.kv_budget = budget;
-        rec.started = Clock::now();
-        RequestId const id = rec.request.request_id;
-        im.records.emplace(id, std::move(rec));
+        Slot s;
+        s.kv_tokens = need;
+        s.fed = request.kv_prefix_tokens;
+        s.out.request_id = id;
+        s.out.usage.prompt_tokens = static_cast<std::uint32_t>(request.prompt_token_ids.size());
+        s.req = std::move(request);
+        s.admitted = Clock::now();
+        im.slots.emplace(id, std::move(s));
         try {
-            im.states.emplace(id, SchedulerRequestState::Waiting);
-            im.queue.push_back(id);
+            im.status.emplace(id, SchedulerRequestState::Waiting);
+            im.fifo.push_back(id);
         } catch (...) {
-            im.states.erase(id);
-            im.records.erase(id);
+            im.status.erase(id);
+            im.slots.erase(id);
             throw;
         }
-        im.reserved_kv_tokens += budget;
     } catch (std::bad_alloc const&) {
-        return {false, SchedulerAdmissionError::InternalError, "scheduler admission allocation failed"};
+        return {false, SchedulerAdmissionError::InternalError, "no memory to admit the request"};
     }
+    im.kv_reserved += need;
     return {true, SchedulerAdmissionError::None, {}};
 }
 
 bool IterationSchedulerRuntime::cancel(RequestId id) noexcept
 {
-    auto const f = impl_->records.find(id);
-    if (f == impl_->records.end() || f->second.state == SchedulerRequestState::Terminal) {
+    auto const f = impl_->slots.find(id);
+    if (f == impl_->slots.end() || f->second.closed()) {
         return false;
     }
-    f->second.cancel_requested = true;
-    f->second.state = SchedulerRequestState::Cancelling;
-    impl_->setState(id, SchedulerRequestState::Cancelling);
+    f->second.cancel = true;
+    impl_->mark(f->second, SchedulerRequestState::Cancelling);
     return true;
 }
 
-SchedulerIterationResult IterationSchedulerRuntime::runIteration()
-{
-    Impl& im = *impl_;
-    SchedulerIterationResult result;
-    result.iteration = ++im.iterations;
-    std::size_t const terminals_before = im.terminals.size();
-    if (stopped()) {
-        im.stopAll();
-        result.terminals_produced = static_cast<std::uint32_t>(im.terminals.size() - terminals_before);
-        return result;
-    }
-
-    struct Selected {
-        Impl::Record* rec;
-        std::uint32_t steps_left;
-    };
-    struct Planned {
-        Impl::Record* rec;
-        GenerationBatchItem item;
-        bool prefill;
-    };
-    auto failAll = [&](std::vector<Selected> const& sel, GenerationError e, char const* why) {
-        for (Selected const& s : sel) {
-            if (s.rec->state != SchedulerRequestState::Terminal) {
-                im.finish(*s.rec, GenerationTerminalReason::Failed, e, why);
-            }
-        }
-    };
-
-    // FIFO selection: at most max_batched_tokens requests, each with its quota.
-    std::size_t const take = std::min<std::size_t>(im.queue.size(), im.config.max_batched_tokens);
-    std::vector<Selected> selected;
-    try {
-        selected.reserve(take);
-        for (std::size_t i = 0; i < take; ++i) {
-            RequestId const id = im.queue.front();
-            im.queue.pop_front();
-            auto const f = im.records.find(id);
-            if (f == im.records.end() || f->second.state == SchedulerRequestState::Terminal) {
-                continue;
-            }
-            Impl::Record& rec = f->second;
-            std::uint32_t const prompt_left =
-                static_cast<std::uint32_t>(rec.request.prompt_token_ids.size()) - rec.prompt_position;
-            std::uint32_t const quota = prompt_left == 0 ? 1 : std::min(prompt_left, im.config.prefill_chunk_size);
-            selected.push_back(Selected{&rec, quota});
-        }
-    } catch (std::bad_alloc const&) {
-        failAll(selected, GenerationError::InternalError, "scheduler batch planning allocation failed");
-    }
-
-    std::uint32_t budget = im.config.max_batched_tokens;
-    std::uint32_t const batch_cap = im.runner->generationMaxBatchSize();
-    if (batch_cap == 0) {
-        failAll(selected, GenerationError::ModelFailed, "model runner reported a zero maximum batch size");
-    }
-    // Waves: every selected request with quota left contributes one position.
-    while (budget != 0 && batch_cap != 0) {
-        std::vector<Planned> plan;
-        try {
-            plan.reserve(std::min<std::size_t>(selected.size(), budget));
-            for (Selected& s : selected) {
-                if (s.steps_left == 0 || budget == 0 || s.rec->state == SchedulerRequestState::Terminal) {
-                    continue;
-                }
-                GenerationBatchItem item;
-                bool prefill = false;
-                if (im.prepare(*s.rec, item, prefill)) {
-                    plan.push_back(Planned{s.rec, item, prefill});
-                    --s.steps_left;
-                    --budget;
-                } else {
-                    s.steps_left = 0;
-                }
-            }
-        } catch (std::bad_alloc const&) {
-            failAll(selected, GenerationError::InternalError, "scheduler model batch allocation failed");
-            break;
-        }
-        if (plan.empty()) {
-            break;
-        }
-        for (std::size_t begin = 0; begin < plan.size(); begin += batch_cap) {
-            std::size_t const end = std::min<std::size_t>(plan.size(), begin + batch_cap);
-            std::vector<GenerationBatchItem> batch;
-            try {
-                batch.reserve(end - begin);
-                for (std::size_t i = begin; i < end; ++i) {
-                    batch.push_back(plan[i].item);
-                }
-            } catch (std::bad_alloc const&) {
-                for (std::size_t i = begin; i < end; ++i) {
-                    im.finish(*plan[i].rec, GenerationTerminalReason::Failed,
-                        GenerationError::InternalError, "scheduler model batch allocation failed");
-                }
-                continue;
-            }
-            GenerationBatchResult out = im.runner->generationForwardBatch(batch);
-            ++result.model_forward_batches;
-            result.model_forward_tokens += static_cast<std::uint32_t>(batch.size());
-            for (std::size_t i = begin; i < end; ++i) {
-                ++(plan[i].prefill ? result.prefill_tokens : result.decode_tokens);
-            }
-            if (!out.success || out.steps.size() != batch.size()) {
-                std::string const detail = out.detail.empty()
-                    ? "model returned an invalid batch result" : std::move(out.detail);
-                for (std::size_t i = begin; i < end; ++i) {
-                    im.finish(*plan[i].rec, GenerationTerminalReason::Failed,
-                        GenerationError::ModelFailed, detail);
-                }
-            } else {
-                for (std::size_t i = begin; i < end; ++i) {
-                    im.apply(*plan[i].rec, std::move(out.steps[i - begin]), plan[i].prefill);
-                }
-            }
-            if (stopped()) {
-                break;
-            }
-        }
-        if (stopped()) {
-            break;
-        }
-    }
-
-    im.forward_tokens += result.model_forward_tokens;
-    im.forward_batches += result.model_forward_batches;
-    im.prefill_tokens += result.prefill_tokens;
-    im.decode_tokens += result.decode_tokens;
-    for (Selected const& s : selected) {
-        if (s.rec->state != SchedulerRequestState::Terminal) {
-            if (stopped()) {
-                im.stopRecord(*s.rec);
-            } else {
-                im.queue.push_back(s.rec->request.request_id);
-            }
-        }
-    }
-    if (stopped()) {
-        im.stopAll();
-    }
-    result.terminals_produced = static_cast<std::uint32_t>(im.terminals.size() - terminals_before);
-    return result;
-}
+SchedulerIterationResult IterationSchedulerRuntime::runIteration() { return impl_->iterate(); }
 
 std::vector<GenerationTerminal> IterationSchedulerRuntime::drain()
 {
     while (!idle()) {
-        SchedulerIterationResult const it = runIteration();
-        if (it.model_forward_tokens == 0 && it.terminals_produced == 0 && !stopped()) {
+        SchedulerIterationResult const r = runIteration();
+        bool const progressed = r.model_forward_tokens != 0 || r.terminals_produced != 0;
+        if (!progressed && !stopped()) {
             break;
         }
     }
@@ -495,17 +558,14 @@ std::vector<GenerationTerminal> IterationSchedulerRuntime::drain()
 std::vector<GenerationTerminal> IterationSchedulerRuntime::takeTerminals()
 {
     std::vector<GenerationTerminal> out;
-    out.swap(impl_->terminals);
+    out.swap(impl_->done);
     return out;
 }
 
 std::optional<SchedulerRequestState> IterationSchedulerRuntime::requestState(RequestId id) const
 {
-    auto const f = impl_->states.find(id);
-    if (f == impl_->states.end()) {
-        return std::nullopt;
-    }
-    return f->second;
+    auto const f = impl_->status.find(id);
+    return f == impl_->status.end() ? std::nullopt : std::optional<SchedulerRequestState>(f->second);
 }
 
 IterationSchedulerSnapshot IterationSchedulerRuntime::snapshot() const
@@ -513,15 +573,16 @@ IterationSchedulerSnapshot IterationSchedulerRuntime::snapshot() const
     Impl const& im = *impl_;
     IterationSchedulerSnapshot s;
     s.iteration_count = im.iterations;
-    s.accepted_count = im.records.size();
-    s.reserved_kv_tokens = im.reserved_kv_tokens;
-    s.model_forward_tokens = im.forward_tokens;
-    s.model_forward_batches = im.forward_batches;
-    s.prefill_tokens = im.prefill_tokens;
-    s.decode_tokens = im.decode_tokens;
+    s.accepted_count = im.slots.size();
+    s.reserved_kv_tokens = im.kv_reserved;
+    s.model_forward_tokens = im.totals.model_forward_tokens;
+    s.model_forward_batches = im.totals.model_forward_batches;
+    s.prefill_tokens = im.totals.prefill_tokens;
+    s.decode_tokens = im.totals.decode_tokens;
     s.stopped = stopped();
-    for (auto const& e : im.states) {
-        switch (e.second) {
+    for (auto const& [id, st] : im.status) {
+        static_cast<void>(id);
+        switch (st) {
         case SchedulerRequestState::Waiting: ++s.waiting_count; break;
         case SchedulerRequestState::Running: ++s.running_count; break;
         case SchedulerRequestState::Cancelling: ++s.cancelling_count; break;
@@ -533,11 +594,8 @@ IterationSchedulerSnapshot IterationSchedulerRuntime::snapshot() const
     return s;
 }
 
-bool IterationSchedulerRuntime::idle() const noexcept { return impl_->queue.empty(); }
-void IterationSchedulerRuntime::stop() noexcept { impl_->stopped.store(true, std::memory_order_release); }
-bool IterationSchedulerRuntime::stopped() const noexcept
-{
-    return impl_->stopped.load(std::memory_order_acquire);
-}
+bool IterationSchedulerRuntime::idle() const noexcept { return impl_->fifo.empty(); }
+void IterationSchedulerRuntime::stop() noexcept { impl_->halted.store(true, std::memory_order_release); }
+bool IterationSchedulerRuntime::stopped() const noexcept { return impl_->stopped(); }
 
 } // namespace kimkvcache

@@ -4,7 +4,10 @@
 // admission gates (max active requests, worst-case KV-token budget), per
 // iteration quota min(prompt remaining, prefill_chunk_size) or 1 for decode,
 // "waves" in which every selected request advances by one position, waves
-// split into model batches of at most the runner's batch size.
+// split into model batches of at most the runner's batch size. Two
+// extensions are off by default: fused prefill chunks
+// (IterationSchedulerConfig::fused_prefill) and requests whose prompt prefix
+// is already in the KV backend (GenerationRequest::kv_prefix_tokens).
 #pragma once
 
 #include "generation.h"
@@ -42,6 +45,11 @@ struct IterationSchedulerConfig final {
     std::uint32_t max_batched_tokens{0};
     std::uint64_t max_kv_tokens{0};
     std::uint32_t prefill_chunk_size{16};
+    // Extension (no counterpart in the reference): when the runner has a
+    // fused prefill (GenerationModelRunner::generationPrefill), a request's
+    // prompt quota of an iteration goes to the model as one multi-position
+    // call instead of one position per wave. Off: the reference's waves.
+    bool fused_prefill{false};
 
     [[nodiscard]] constexpr bool valid() const noexcept
     {
