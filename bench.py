@@ -548,6 +548,101 @@ def run_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_c3(args):
+    """TinyLlama shape, 4 concurrent requests through the
+    iteration scheduler, prompts seeded uniform in [128, 512], chunked
+    prefill in 64-token chunks mixed with decode, 128 new tokens each. Two
+    requests share a prompt prefix of 256 + k tokens (k seeded in [1, 7], so
+    the shared tail page is partial): it is prefilled once under request 1,
+    forked to request 2 in the KV backend, and both are submitted with that
+    prefix already in the cache, so each one's first write copies the shared
+    partial tail. The scheduler hands every prompt chunk to the runner's
+    fused prefill. Timed with CUDA events around the whole workload (prefix
+    prefill, fork, submissions, drain), host calls included: value = output
+    tokens per second; prompt and total token rates are reported beside it."""
+    import torch
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cfg = dict(synth.TINYLLAMA)
+    cfg["max_positions"] = 4608
+    archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
+    manifest, data, _ = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31))
+    R = kk.runtime()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    hq, hkv, D, L = cfg["q_heads"], cfg["kv_heads"], cfg["head_dim"], cfg["layers"]
+    rng = random.Random(SEED)
+    k = rng.randint(1, 7)
+    P = 256 + k
+    lengths = [rng.randint(128, 512) for _ in range(4)]
+    lengths[0], lengths[1] = max(lengths[0], P + 1), max(lengths[1], P + 1)
+    prefix = [rng.randrange(3, 32000) for _ in range(P)]
+    prompts = [prefix + [rng.randrange(3, 32000) for _ in range(n - P)] if i < 2
+               else [rng.randrange(3, 32000) for _ in range(n)] for i, n in enumerate(lengths)]
+    new_tokens, chunk = 128, 64
+    runs = args.steps if args.steps <= 8 else 3
+    backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, 4 * (512 + 128) // 8 + 64,
+                                  4 * (512 + 128) // 64 + 8)
+    status, detail = C.c_int(0), C.create_string_buffer(512)
+    runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr, chunk, 1, 1,
+                                C.byref(status), detail, 512)
+    assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
+    assert R["runner_set_auto_promote"](runner, 1) == 1
+    out = C.c_uint32(0)
+
+    def workload(base):
+        ids = [base + i for i in range(4)]
+        assert R["backend_create_request"](backend, ids[0]) == 0
+        pre = (C.c_uint32 * P)(*prefix)
+        if not R["runner_prefill"](runner, ids[0], pre, P, 0, C.byref(out)):
+            raise RuntimeError("prefix prefill failed")
+        assert R["backend_fork"](backend, ids[0], ids[1]) == 0
+        sched = kk.Scheduler(R, backend, runner, 4, 4 * chunk, 10 ** 6, chunk, fused_prefill=True)
+        for i, rid in enumerate(ids):
+            assert sched.submit(rid, prompts[i], new_tokens, -1, kv_prefix=P if i < 2 else 0) == 0
+        terms = sched.drain()
+        sched.close()
+        return terms
+
+    for w in range(max(1, args.warmup // 3)):
+        workload(1000 * (w + 1))
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(gpu_id(torch, dev))
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    produced = 0
+    ev0.record(stream)
+    for r in range(runs):
+        terms = workload(100000 * (r + 1))
+        assert all(t["error"] == 0 for t in terms), terms
+        produced += sum(len(t["tokens"]) for t in terms)
+    ev1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    clocks = sampler.stop()
+    snap = kk.BackendSnapshot()
+    R["backend_snapshot"](backend, C.byref(snap))
+    assert snap.request_count == 0 and R["backend_check_invariants"](backend) == 1
+    R["runner_destroy"](runner)
+    R["backend_destroy"](backend)
+    prompt_tok = runs * sum(lengths)
+    print(json.dumps({
+        "metric": "scheduler output tok/s TinyLlama-shape c3 (4 requests, chunked fused prefill + decode)",
+        "value": round(produced / (ms / 1e3), 1), "unit": "tok/s", "n_gpus": 1, "steps": runs,
+        "warmup": max(1, args.warmup // 3), "ms_per_step": round(ms / runs, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": "c3: 4 requests, prompts ~U[128,512] (two share a forked 256+k prefix), "
+                               "chunk 64, 128 new tokens each", "prompt_lengths": lengths, "shared_prefix": P,
+                   "k": k, "fused_prefill": True, "auto_promote": True},
+        "prompt_tok_per_s": round(prompt_tok / (ms / 1e3), 1),
+        "total_tok_per_s": round((prompt_tok + produced) / (ms / 1e3), 1),
+        "e2e": {"value": round(produced / (ms / 1e3), 1), "unit": "tok/s",
+                "note": "host scheduler calls inside the CUDA-event-timed region"},
+        "clocks": clocks}), flush=True)
+
+
 def run_prefill(args):
     """Prompt throughput of the fused multi-token prefill (kkrt_runner_prefill):
     --prefill-requests prompts of --prompt tokens each, every prompt fed in
@@ -789,7 +884,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5"])
+    ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5", "c3"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", choices=["attention", "gemm", "gather"], default=None,
                     help="time one hot kernel on a standalone case (profiling)")
@@ -827,6 +922,9 @@ def main():
         return
     if args.prefill:
         run_prefill(args)
+        return
+    if args.config == "c3" and args.impl == "ours":
+        run_c3(args)
         return
     line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
         args, rank, world, local_rank)

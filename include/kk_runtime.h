@@ -342,6 +342,19 @@ KK_API void kkrt_sched_destroy(void* sched);
 /* submit: returns SchedulerAdmissionError (0 accepted). eos < 0: model default. */
 KK_API int kkrt_sched_submit(void* sched, uint64_t request_id, const uint32_t* prompt,
     uint32_t prompt_len, uint32_t max_new_tokens, int64_t eos);
+/* Extensions (no counterpart in the reference):
+ * kkrt_sched_create_ex: flags bit 0 (KKRT_SCHED_FUSED_PREFILL) hands each
+ * request's prompt quota of an iteration to the runner's fused prefill as one
+ * multi-position call (IterationSchedulerConfig::fused_prefill).
+ * kkrt_sched_submit_prefixed: the first kv_prefix_tokens prompt positions
+ * are already committed under request_id in the KV backend (e.g. a prefix
+ * shared by forking another request); the scheduler neither creates the KV
+ * request nor feeds those positions (GenerationRequest::kv_prefix_tokens). */
+#define KKRT_SCHED_FUSED_PREFILL 1u
+KK_API void* kkrt_sched_create_ex(void* backend, void* model_runner, uint32_t max_active,
+    uint32_t max_batched_tokens, uint64_t max_kv_tokens, uint32_t prefill_chunk, uint32_t flags);
+KK_API int kkrt_sched_submit_prefixed(void* sched, uint64_t request_id, const uint32_t* prompt,
+    uint32_t prompt_len, uint32_t max_new_tokens, int64_t eos, uint32_t kv_prefix_tokens);
 KK_API int kkrt_sched_cancel(void* sched, uint64_t request_id);
 KK_API void kkrt_sched_run_iteration(void* sched, kk_iteration* out);
 KK_API void kkrt_sched_stop(void* sched);

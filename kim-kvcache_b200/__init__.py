@@ -492,7 +492,9 @@ RUNTIME_SIGNATURES = {
     "runner_last_host_us": (_I, [_VP, C.POINTER(C.c_float)]),
     "runner_last_error": (_U32, [_VP, C.c_char_p, _U32]),
     "sched_create": (_VP, [_VP, _VP, _U32, _U32, _U64, _U32]),
+    "sched_create_ex": (_VP, [_VP, _VP, _U32, _U32, _U64, _U32, _U32]),
     "sched_destroy": (None, [_VP]),
+    "sched_submit_prefixed": (_I, [_VP, _U64, _PU32, _U32, _U32, _I64, _U32]),
     "sched_submit": (_I, [_VP, _U64, _PU32, _U32, _U32, _I64]),
     "sched_cancel": (_I, [_VP, _U64]),
     "sched_run_iteration": (None, [_VP, C.POINTER(Iteration)]),
@@ -540,12 +542,19 @@ class Scheduler:
     reference shim exposes the same calls with the kref_ prefix)."""
 
     def __init__(self, fns: dict, backend, runner, max_active, max_batched_tokens, max_kv_tokens,
-                 prefill_chunk):
+                 prefill_chunk, fused_prefill=False):
         self.f = fns
-        self.h = fns["sched_create"](backend, runner, max_active, max_batched_tokens,
-                                     max_kv_tokens, prefill_chunk)
+        if fused_prefill:
+            self.h = fns["sched_create_ex"](backend, runner, max_active, max_batched_tokens,
+                                            max_kv_tokens, prefill_chunk, 1)
+        else:
+            self.h = fns["sched_create"](backend, runner, max_active, max_batched_tokens,
+                                         max_kv_tokens, prefill_chunk)
 
-    def submit(self, rid, prompt, max_new, eos=-1):
+    def submit(self, rid, prompt, max_new, eos=-1, kv_prefix=0):
+        if kv_prefix:
+            return self.f["sched_submit_prefixed"](self.h, rid, _u32(prompt), len(prompt), max_new, eos,
+                                                   kv_prefix)
         return self.f["sched_submit"](self.h, rid, _u32(prompt), len(prompt), max_new, eos)
 
     def cancel(self, rid):

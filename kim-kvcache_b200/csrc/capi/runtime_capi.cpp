@@ -450,17 +450,35 @@ void* kkrt_sched_create(void* b, void* r, uint32_t max_active, uint32_t max_toke
     return s;
 }
 
+void* kkrt_sched_create_ex(void* b, void* r, uint32_t max_active, uint32_t max_tokens, uint64_t max_kv,
+    uint32_t chunk, uint32_t flags)
+{
+    auto* s = new (std::nothrow) Sched;
+    if (s == nullptr) return nullptr;
+    IterationSchedulerConfig cfg{max_active, max_tokens, max_kv, chunk};
+    cfg.fused_prefill = (flags & KKRT_SCHED_FUSED_PREFILL) != 0;
+    s->rt = std::make_unique<IterationSchedulerRuntime>(*KV(b), *RUN(r), cfg);
+    return s;
+}
+
 void kkrt_sched_destroy(void* s) { delete static_cast<Sched*>(s); }
+
+int kkrt_sched_submit_prefixed(void* s, uint64_t id, const uint32_t* prompt, uint32_t len, uint32_t max_new,
+    int64_t eos, uint32_t kv_prefix_tokens)
+{
+    GenerationRequest req;
+    req.request_id = id;
+    if (len != 0) req.prompt_token_ids.assign(prompt, prompt + len);
+    req.sampling.max_new_tokens = max_new;
+    if (eos >= 0) req.sampling.eos_token_id = static_cast<std::uint32_t>(eos);
+    req.kv_prefix_tokens = kv_prefix_tokens;
+    return static_cast<int>(static_cast<Sched*>(s)->rt->submit(std::move(req)).error);
+}
 
 int kkrt_sched_submit(void* s, uint64_t id, const uint32_t* prompt, uint32_t len, uint32_t max_new,
     int64_t eos)
 {
-    GenerationRequest req;
-    req.request_id = id;
-    req.prompt_token_ids.assign(prompt, prompt + len);
-    req.sampling.max_new_tokens = max_new;
-    if (eos >= 0) req.sampling.eos_token_id = static_cast<std::uint32_t>(eos);
-    return static_cast<int>(static_cast<Sched*>(s)->rt->submit(std::move(req)).error);
+    return kkrt_sched_submit_prefixed(s, id, prompt, len, max_new, eos, 0);
 }
 
 int kkrt_sched_cancel(void* s, uint64_t id) { return static_cast<Sched*>(s)->rt->cancel(id) ? 1 : 0; }

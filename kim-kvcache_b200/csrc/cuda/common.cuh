@@ -150,6 +150,30 @@ __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, std::uint32_t phas
     return false;
 }
 
+// The same bounded wait polling without suspending the thread, for a wait
+// that is expected to end within a few hundred nanoseconds and sits on the
+// critical path (a suspended thread wakes up late).
+__device__ __forceinline__ bool mbar_wait_spin(std::uint64_t* bar, std::uint32_t phase,
+    unsigned int* status)
+{
+    if (mbar_try_wait(bar, phase)) {
+        return true;
+    }
+    std::uint64_t const t0 = global_ns();
+    for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
+        if (mbar_try_wait(bar, phase)) {
+            return true;
+        }
+        if ((i & 255u) == 255u && global_ns() - t0 > kWaitLimitNs) {
+            break;
+        }
+    }
+    if (status != nullptr) {
+        atomicCAS(status, kErrNone, kErrWaitTimeout);
+    }
+    return false;
+}
+
 // ---- TMA (no multicast anywhere) -------------------------------------------
 
 __device__ __forceinline__ void tma_load_2d(void* dst, CUtensorMap const* map,

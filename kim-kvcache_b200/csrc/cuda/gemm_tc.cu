@@ -442,19 +442,30 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
         std::uint32_t const c = t & 7u;
+        // This thread's 8 norm weights of stage i (ones without a weight);
+        // requested one stage ahead, so the load never waits on L2.
+        auto norm_chunk = [&](std::uint32_t i) {
+            std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
+            uint4 g = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);  // FP16 1.0 x 8
+            if (args.norm_w != nullptr && i < nk && k0 < args.K) {
+                g = __ldg(reinterpret_cast<uint4 const*>(args.norm_w + k0));
+            }
+            return g;
+        };
+        uint4 g_next = norm_chunk(0);
         for (std::uint32_t i = 0; i < nk; ++i) {
             std::uint32_t const s = i % kStages;
-            std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
-            float gv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
-            if (args.norm_w != nullptr && k0 < args.K) {
-                uint4 const graw = *reinterpret_cast<uint4 const*>(args.norm_w + k0);
+            float gv[8];
+            {
+                uint4 const graw = g_next;
                 __half const* gh = reinterpret_cast<__half const*>(&graw);
 #pragma unroll
                 for (int e = 0; e < 8; ++e) {
                     gv[e] = __half2float(gh[e]);
                 }
             }
-            if (!mbar_wait(&xfull[s], (i / kStages) & 1u, st)) {
+            g_next = norm_chunk(i + 1);
+            if (!mbar_wait_spin(&xfull[s], (i / kStages) & 1u, st)) {
                 break;
             }
             std::uint8_t* xs = x_stage + s * BN * 128;

@@ -762,7 +762,18 @@ GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId i
 GenerationStepResult CudaTinyLlamaModelRunner::prefill(RequestId request_id,
     std::vector<std::uint32_t> const& prompt, std::uint32_t first_position)
 {
-    GenerationStepResult r = prefillChunks(request_id, prompt, first_position);
+    GenerationStepResult r = prefillChunks(request_id, prompt.data(), static_cast<std::uint32_t>(prompt.size()),
+        first_position, true);
+    if (!r.success) {
+        impl_->last_error = r.detail;
+    }
+    return r;
+}
+
+GenerationStepResult CudaTinyLlamaModelRunner::generationPrefill(RequestId request_id, std::uint32_t const* tokens,
+    std::uint32_t count, std::uint32_t first_position)
+{
+    GenerationStepResult r = prefillChunks(request_id, tokens, count, first_position, false);
     if (!r.success) {
         impl_->last_error = r.detail;
     }
@@ -770,25 +781,25 @@ GenerationStepResult CudaTinyLlamaModelRunner::prefill(RequestId request_id,
 }
 
 GenerationStepResult CudaTinyLlamaModelRunner::prefillChunks(RequestId request_id,
-    std::vector<std::uint32_t> const& prompt, std::uint32_t first_position)
+    std::uint32_t const* prompt, std::uint32_t count, std::uint32_t first_position, bool release_on_failure)
 {
     Impl& im = *impl_;
     TinyLlamaConfig const& c = im.cfg;
-    if (request_id == kInvalidRequestId || prompt.empty()
-        || first_position + prompt.size() > c.max_position_embeddings) {
+    if (request_id == kInvalidRequestId || prompt == nullptr || count == 0
+        || std::uint64_t(first_position) + count > c.max_position_embeddings) {
         return {false, 0, "request, prompt, or position is out of range"};
     }
-    for (std::uint32_t t : prompt) {
-        if (t >= c.vocabulary_size) {
+    for (std::uint32_t i = 0; i < count; ++i) {
+        if (prompt[i] >= c.vocabulary_size) {
             return {false, 0, "token id is out of range"};
         }
     }
     GenerationStepResult last{false, 0, "empty prompt"};
     std::uint32_t const chunk = im.options.max_batch_size;
     std::vector<std::pair<RequestId, std::uint32_t>> promote;
-    for (std::size_t done = 0; done < prompt.size(); done += chunk) {
-        std::uint32_t const n = static_cast<std::uint32_t>(std::min<std::size_t>(chunk, prompt.size() - done));
-        std::uint32_t const first = first_position + static_cast<std::uint32_t>(done);
+    for (std::uint32_t done = 0; done < count; done += chunk) {
+        std::uint32_t const n = std::min<std::uint32_t>(chunk, count - done);
+        std::uint32_t const first = first_position + done;
         BlockTable before;
         if (!cudaBackendTable(*im.kv, request_id, before) || before.tokenCount() != first) {
             return {false, 0, "request not found or its committed length differs from the prompt position"};
@@ -801,11 +812,15 @@ GenerationStepResult CudaTinyLlamaModelRunner::prefillChunks(RequestId request_i
         if (!cudaBackendTable(*im.kv, request_id, after)) {
             return {false, 0, "request vanished during prefill"};
         }
-        last = prefillStep(im, request_id, prompt.data() + done, n, first, before, after);
+        last = prefillStep(im, request_id, prompt + done, n, first, before, after);
         if (!last.success) {
             // As the reference's append data path does after a device failure:
-            // the request's pages cannot be trusted any more, release it.
-            static_cast<void>(im.kv->releaseRequest(request_id));
+            // the request's pages cannot be trusted any more, release it (or
+            // leave that to the owner, the scheduler, which releases it when
+            // it ends the request).
+            if (release_on_failure) {
+                static_cast<void>(im.kv->releaseRequest(request_id));
+            }
             return last;
         }
         if (im.auto_promote) {

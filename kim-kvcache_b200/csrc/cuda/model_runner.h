@@ -128,6 +128,12 @@ public:
     [[nodiscard]] GenerationStepResult prefill(RequestId request_id,
         std::vector<std::uint32_t> const& prompt, std::uint32_t first_position);
 
+    // The scheduler's view of prefill() (GenerationModelRunner extension):
+    // on a device failure the request stays for its owner to release.
+    [[nodiscard]] bool generationSupportsPrefill() const noexcept override { return true; }
+    [[nodiscard]] GenerationStepResult generationPrefill(RequestId request_id, std::uint32_t const* tokens,
+        std::uint32_t count, std::uint32_t first_position) override;
+
     // Device time of the last fused step (ms, from CUDA events), 0 if unknown.
     [[nodiscard]] float lastStepDeviceMs() const noexcept;
     // Detail of the last failed fused step (empty if none).
@@ -150,7 +156,8 @@ private:
     explicit CudaTinyLlamaModelRunner(std::unique_ptr<Impl> impl) noexcept;
     std::unique_ptr<Impl> impl_;
     [[nodiscard]] GenerationStepResult prefillChunks(RequestId request_id,
-        std::vector<std::uint32_t> const& prompt, std::uint32_t first_position);
+        std::uint32_t const* prompt, std::uint32_t count, std::uint32_t first_position,
+        bool release_on_failure);
     friend GenerationStepResult prefillStep(Impl&, RequestId, std::uint32_t const*, std::uint32_t,
         std::uint32_t, BlockTable const&, BlockTable const&);
     friend CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const&,

@@ -183,6 +183,65 @@ def test_scheduler_end_to_end_matches_oracle_generation(kk, tmp_path):
     s.close()
 
 
+def _oracle_generation(s, seq, prompt, max_new, eos):
+    """The oracle fed one position at a time (the reference's scheduler
+    path): greedy outputs, and whether every top-2 gap exceeded the
+    tolerance (only then must the tokens match exactly)."""
+    s.oracle.create(seq)
+    for p_, t in enumerate(prompt):
+        g, lg, _ = s.oracle.forward([seq], [t], [p_], want_hidden=False)
+    tok, out, gaps_ok = int(g[0]), [], True
+    top = np.sort(lg[0])[-2:]
+    gaps_ok = top[1] - top[0] > TOL
+    for i in range(max_new):
+        out.append(tok)
+        if tok == eos or i == max_new - 1:
+            break
+        g, lg, _ = s.oracle.forward([seq], [tok], [len(prompt) + i], want_hidden=False)
+        top = np.sort(lg[0])[-2:]
+        gaps_ok = gaps_ok and top[1] - top[0] > TOL
+        tok = int(g[0])
+    return out, gaps_ok
+
+
+@pytest.mark.parametrize("fused", [True, False], ids=["fused_prefill", "waves"])
+def test_scheduler_forked_prefix_requests_match_oracle(kk, tmp_path, fused):
+    """BASELINE config 3's structure at a small shape: two requests share a
+    prompt prefix of 40 + k tokens (k = 3: the shared tail page is partial),
+    built once and forked in the backend, then submitted with that prefix
+    already in the KV cache (kv_prefix_tokens); two more requests are fresh.
+    The scheduler runs chunked prefill (chunk 16) mixed with decode, as fused
+    multi-position prefill calls or as the reference's one-position waves.
+    Each request's greedy output must equal the oracle fed its whole prompt
+    one position at a time, the forked pair's first writes copying the shared
+    partial tail."""
+    s = Stack(kk, tmp_path, SMALL, batch=16)
+    rng = random.Random(33)
+    P = 40 + 3
+    prefix = [rng.randrange(3, 1000) for _ in range(P)]
+    assert s.R["backend_create_request"](s.backend, 1) == 0
+    got, err = _prefill(s, 1, prefix, 0)
+    assert got is not None, err
+    assert s.R["backend_fork"](s.backend, 1, 2) == 0
+    prompts = {1: prefix + [rng.randrange(3, 1000) for _ in range(21)],
+               2: prefix + [rng.randrange(3, 1000) for _ in range(5)],
+               3: [rng.randrange(3, 1000) for _ in range(19)],
+               4: [rng.randrange(3, 1000) for _ in range(70)]}
+    sched = kk.Scheduler(s.R, s.backend, s.runner, 8, 64, 10 ** 6, 16, fused_prefill=fused)
+    for rid, prompt in prompts.items():
+        assert sched.submit(rid, prompt, 10, kv_prefix=P if rid in (1, 2) else 0) == 0
+    terms = {t["request_id"]: t for t in sched.drain()}
+    sched.close()
+    for rid, prompt in prompts.items():
+        want, gaps_ok = _oracle_generation(s, 100 + rid, prompt, 10, SMALL["eos"])
+        assert terms[rid]["error"] == 0, terms[rid]
+        if gaps_ok:
+            assert terms[rid]["tokens"] == want, (rid, terms[rid]["tokens"], want)
+    assert s.snapshot().request_count == 0
+    assert s.R["backend_check_invariants"](s.backend) == 1
+    s.close()
+
+
 def test_injected_failures_roll_back_one_lane(kk, tmp_path):
     s = Stack(kk, tmp_path, SMALL)
     for rid in (1, 2):

@@ -13,8 +13,11 @@ import pytest
 
 
 def bind_scheduler(kk, lib, prefix):
+    # The reference exposes the common entry points; this library's
+    # extensions (fused prefill, KV-prefix requests) are bound where present.
     return kk.bind(lib, prefix, {k: v for k, v in kk.RUNTIME_SIGNATURES.items()
-                                 if k.startswith(("sched_", "fake_", "generate"))})
+                                 if k.startswith(("sched_", "fake_", "generate"))
+                                 and hasattr(lib, prefix + k)})
 
 
 def both(kk, kk_lib, ref_lib):
