@@ -301,6 +301,13 @@ typedef struct kk_gemm_desc {
     uint32_t norm_stride;
     float norm_eps;
     const uint16_t* norm_weight; /* [K] fp16, 16-byte aligned, or NULL */
+    /* KK_EPI_QKV_ROPE: optional table of the rotation factors, [rope_positions]
+     * [head_dim / 2] pairs (cos, sin) of position * theta^(-2d / head_dim),
+     * 8-byte aligned; NULL computes them in the kernel (sincosf). The runner
+     * fills it once on the host, with the host math library the reference's
+     * model uses, for every position up to max_position_embeddings. */
+    const float* rope_cos_sin;
+    uint32_t rope_positions;
 } kk_gemm_desc;
 
 #define KK_W_ROW_MAJOR 0

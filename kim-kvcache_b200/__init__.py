@@ -375,7 +375,8 @@ class GemmDesc(C.Structure):
                 ("kv_rows", C.c_uint32), ("head_dim", C.c_uint32), ("rope_theta", C.c_float),
                 ("tokens", C.c_void_p), ("argmax_workspace", C.c_void_p),
                 ("weight_layout", C.c_uint32), ("norm_input", C.c_void_p),
-                ("norm_stride", C.c_uint32), ("norm_eps", C.c_float), ("norm_weight", C.c_void_p)]
+                ("norm_stride", C.c_uint32), ("norm_eps", C.c_float), ("norm_weight", C.c_void_p),
+                ("rope_cos_sin", C.c_void_p), ("rope_positions", C.c_uint32)]
 
 
 _VP = C.c_void_p

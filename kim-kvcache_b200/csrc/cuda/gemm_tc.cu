@@ -99,6 +99,8 @@ struct EpiArgs {
     std::uint32_t q_rows;
     std::uint32_t kv_rows;
     float theta;
+    float2 const* rope_cs;       // [positions][32] (cos, sin), or null: computed here
+    std::uint32_t rope_positions;
     // KK_EPI_ARGMAX
     std::uint32_t* tokens;
     float* part_val;
@@ -291,6 +293,36 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     // griddepcontrol.wait, which returns once this grid has completed.
     pdl_launch_dependents();
 
+    // QKV epilogue inputs that come from the host (positions, KV slots, RoPE
+    // factors): requested now, before the dependency wait, by every thread
+    // for its row and the CTA's columns.
+    constexpr std::uint32_t kPre = 8;
+    std::uint32_t const pn0 = rank * args.N / S;
+    std::uint32_t const pcols = (rank + 1) * args.N / S - pn0;
+    bool const prefetched = pcols <= kPre;
+    kk_kv_slot kvs[kPre];
+    float2 rope[kPre];
+    std::uint32_t pos[kPre];
+#pragma unroll
+    for (std::uint32_t j = 0; j < kPre; ++j) {
+        kvs[j] = kk_kv_slot{0, 0, 0, 0};
+        rope[j] = make_float2(1.f, 0.f);
+        pos[j] = 0;
+        if (EPI == KK_EPI_QKV_ROPE && prefetched && j < pcols) {
+            pos[j] = args.epi.positions[pn0 + j];
+            kvs[j] = args.epi.slots[pn0 + j];
+        }
+    }
+    if (EPI == KK_EPI_QKV_ROPE && args.epi.rope_cs != nullptr) {
+        std::uint32_t const d32 = (m_tile * kBM + tid) & 31u;
+#pragma unroll
+        for (std::uint32_t j = 0; j < kPre; ++j) {
+            if (prefetched && j < pcols && pos[j] < args.epi.rope_positions) {
+                rope[j] = args.epi.rope_cs[std::uint64_t(pos[j]) * 32u + d32];
+            }
+        }
+    }
+
     if (warp == 0 && lane == 0) {
         // Producer. Weights never depend on the previous kernel: request them
         // before waiting for it; activations only after.
@@ -367,29 +399,15 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     pdl_wait();
     // Epilogue inputs of this CTA's columns, requested now so that they are
     // in registers when the reduced tile is ready: the residual rows (written
-    // by the previous kernel, hence after the wait) and the RoPE positions
-    // and KV slots of the QKV epilogue.
-    constexpr std::uint32_t kPre = 8;
-    std::uint32_t const pn0 = rank * args.N / S;
-    std::uint32_t const pcols = (rank + 1) * args.N / S - pn0;
+    // by the previous kernel, hence after the wait); the QKV epilogue's
+    // positions, KV slots and RoPE factors were requested at kernel start.
     std::uint32_t const pm = m_tile * kBM + tid;
-    bool const prefetched = pcols <= kPre;
     __half resid[kPre];
-    std::uint32_t pos[kPre];
-    kk_kv_slot kvs[kPre];
 #pragma unroll
     for (std::uint32_t j = 0; j < kPre; ++j) {
         resid[j] = __float2half_rn(0.f);
-        pos[j] = 0;
-        kvs[j] = kk_kv_slot{0, 0, 0, 0};
-        if (prefetched && j < pcols) {
-            std::uint32_t const n = pn0 + j;
-            if (EPI == KK_EPI_RESIDUAL && pm < args.M) {
-                resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(n) * args.epi.out_stride + pm];
-            } else if (EPI == KK_EPI_QKV_ROPE) {
-                pos[j] = args.epi.positions[n];
-                kvs[j] = args.epi.slots[n];
-            }
+        if (EPI == KK_EPI_RESIDUAL && prefetched && j < pcols && pm < args.M) {
+            resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(pn0 + j) * args.epi.out_stride + pm];
         }
     }
     if (xnorm && warp >= 2) {
@@ -653,32 +671,42 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         bool const is_v = m >= e.q_rows + e.kv_rows;
         std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
         std::uint32_t const d = idx & 63u;
-        float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+        // The rotation's first product minus (or plus) the second, each
+        // rounded on its own (no fused multiply-add), as the reference's
+        // host model computes it.
 #pragma unroll 1
         for (std::uint32_t j = 0; j < cols; ++j) {
             std::uint32_t const n = n0 + j;
             // Prefetched values when the CTA owns at most kPre columns.
             std::uint32_t position = 0;
             kk_kv_slot slot_rec{0, 0, 0, 0};
+            float2 cs = make_float2(1.f, 0.f);
 #pragma unroll
             for (std::uint32_t q = 0; q < kPre; ++q) {
                 if (prefetched && q == j) {
                     position = pos[q];
                     slot_rec = kvs[q];
+                    cs = rope[q];
                 }
             }
             if (!prefetched) {
                 position = e.positions[n];
                 slot_rec = e.slots[n];
+                if (e.rope_cs != nullptr && position < e.rope_positions) {
+                    cs = e.rope_cs[std::uint64_t(position) * 32u + (d & 31u)];
+                }
             }
             float const mine = __half2float(__float2half_rn(red[j * kBM + row]));
             float out = mine;
             if (!is_v) {
                 float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
-                float const angle = static_cast<float>(position) * inv_freq;
-                float s, c;
-                sincosf(angle, &s, &c);
-                out = d < 32u ? mine * c - other * s : mine * c + other * s;
+                if (e.rope_cs == nullptr) {
+                    float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+                    sincosf(static_cast<float>(position) * inv_freq, &cs.y, &cs.x);
+                }
+                float const a = __fmul_rn(mine, cs.x);
+                float const b = __fmul_rn(other, cs.y);
+                out = d < 32u ? __fsub_rn(a, b) : __fadd_rn(a, b);
             }
             __half const hv = __float2half_rn(out);
             if (m < e.q_rows) {
@@ -994,6 +1022,13 @@ int buildArgs(kk_gemm_desc const* d, GemmArgs& args)
         e.q_rows = d->q_rows;
         e.kv_rows = d->kv_rows;
         e.theta = d->rope_theta;
+        if (d->rope_cos_sin != nullptr) {
+            if ((reinterpret_cast<std::uintptr_t>(d->rope_cos_sin) & 7u) != 0 || d->rope_positions == 0) {
+                return KK_EINVAL;
+            }
+            e.rope_cs = reinterpret_cast<float2 const*>(d->rope_cos_sin);
+            e.rope_positions = d->rope_positions;
+        }
     }
     if (d->epilogue == KK_EPI_ARGMAX) {
         if (d->tokens == nullptr || d->argmax_workspace == nullptr) {

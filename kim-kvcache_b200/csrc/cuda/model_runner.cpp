@@ -6,6 +6,7 @@
 #include "kernels_internal.h"
 
 #include <cuda_runtime.h>
+#include <math.h>
 
 #include <algorithm>
 #include <array>
@@ -98,6 +99,9 @@ struct CudaTinyLlamaModelRunner::Impl {
     float* sq_embed{nullptr};
     float* sq_attn_out{nullptr};
     float* sq_mlp_out{nullptr};
+    // RoPE factors (cos, sin) of every position and rotation pair, computed
+    // once on the host with the math library the reference's model uses.
+    float* rope_cs{nullptr};
 
     // Step inputs: one region on the device, a pinned mirror on the host.
     std::uint32_t max_items{0};
@@ -241,6 +245,8 @@ CudaModelRunnerStatus CudaTinyLlamaModelRunner::Impl::buildPlans(std::uint32_t b
         d.kv_rows = c.kv_head_count * c.head_dimension;
         d.head_dim = c.head_dimension;
         d.rope_theta = c.rope_theta;
+        d.rope_cos_sin = rope_cs;
+        d.rope_positions = c.max_position_embeddings;
         out.qkv.emplace_back();
         out.o.emplace_back();
         out.gu.emplace_back();
@@ -1109,6 +1115,7 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
         c.head_dimension);
     std::size_t const o_attn_ws = region(im->attn_ws_bytes);
     std::size_t const o_argmax = region(kk_argmax_workspace_bytes(c.vocabulary_size, bmax));
+    std::size_t const o_rope = region(std::size_t(c.max_position_embeddings) * (c.head_dimension / 2) * 8);
     std::size_t const sq_bytes = std::size_t((H + 127) / 128) * 64 * 4;
     std::size_t const o_sq_embed = region(sq_bytes);
     std::size_t const o_sq_attn = region(sq_bytes);
@@ -1133,6 +1140,26 @@ CudaModelRunnerCreateResult createCudaTinyLlamaModelRunner(std::string const& ma
     im->sq_embed = reinterpret_cast<float*>(im->ws + o_sq_embed);
     im->sq_attn_out = reinterpret_cast<float*>(im->ws + o_sq_attn);
     im->sq_mlp_out = reinterpret_cast<float*>(im->ws + o_sq_mlp);
+    im->rope_cs = reinterpret_cast<float*>(im->ws + o_rope);
+    {
+        // angle = position * theta^(-2d / head_dim), as the reference's model
+        // computes it (float arithmetic, host libm), pairs (cos, sin).
+        std::uint32_t const half = c.head_dimension / 2;
+        std::vector<float> table(std::size_t(c.max_position_embeddings) * half * 2);
+        for (std::uint32_t d = 0; d < half; ++d) {
+            float const inv = ::powf(c.rope_theta, -2.0f * static_cast<float>(d) / static_cast<float>(c.head_dimension));
+            for (std::uint32_t p = 0; p < c.max_position_embeddings; ++p) {
+                float const angle = static_cast<float>(p) * inv;
+                table[(std::size_t(p) * half + d) * 2] = ::cosf(angle);
+                table[(std::size_t(p) * half + d) * 2 + 1] = ::sinf(angle);
+            }
+        }
+        e = cudaMemcpy(im->rope_cs, table.data(), table.size() * sizeof(float), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            out.status = failure(CudaModelRunnerError::AllocationFailed, static_cast<int>(e), "RoPE table");
+            return out;
+        }
+    }
 
     off = 0;
     im->off_counts = region(16);
