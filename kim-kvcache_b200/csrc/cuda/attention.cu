@@ -660,13 +660,16 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
 #else
     constexpr std::uint64_t kSegmentCost = 144;
 #endif
+    // A page occupies whole 8-token groups of a stage whatever its valid
+    // count, so it costs its valid tokens rounded up to a group.
+    auto cost = [](kk_page_desc const& d) -> std::uint64_t { return (d.valid_tokens + 7u) & ~7u; };
     std::uint64_t total = 0;
     for (std::uint32_t b = 0; b < num_lanes; ++b) {
         if (lanes[b].desc_count != 0) {
             total += kSegmentCost;
         }
         for (std::uint32_t e = lanes[b].desc_offset; e < lanes[b].desc_offset + lanes[b].desc_count; ++e) {
-            total += descs[e].valid_tokens;
+            total += cost(descs[e]);
         }
     }
     // Cut k of num_parts - 1 lands on the page boundary nearest to
@@ -702,7 +705,7 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
             pos += kSegmentCost;
         }
         for (std::uint32_t e = ln.desc_offset; e < end; ++e) {
-            std::uint64_t const c = descs[e].valid_tokens;
+            std::uint64_t const c = cost(descs[e]);
             bool cut_before = false;
             bool cut_after = false;
             while (next_cut < num_parts && next_target < pos + c) {

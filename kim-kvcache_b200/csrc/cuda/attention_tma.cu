@@ -67,6 +67,9 @@ constexpr int kStages = 3;
 constexpr std::uint32_t kStageBytes = 32768;           // K 16 KB + V 16 KB
 constexpr std::uint32_t kRowBytes = kHeadDim * 2;      // one head x one token
 constexpr std::uint32_t kORow = kHeadDim + 4;          // padded merge row (floats)
+// Partials a combining thread requests at once: a lane of the balanced plan
+// spans about 5-6 items, so all of them arrive in one L2 round trip.
+constexpr std::uint32_t kCombineBatch = 8;
 
 constexpr std::uint32_t kSegEnd = 1u;    // last stage of a lane segment
 constexpr std::uint32_t kItemEnd = 2u;   // last stage of the item
@@ -239,6 +242,13 @@ __device__ __forceinline__ bool wait_bounded(std::uint64_t* bar, std::uint32_t p
         }
     }
     return false;
+}
+
+__device__ __forceinline__ std::uint32_t atom_add_acq_rel_gpu(std::uint32_t* p, std::uint32_t v)
+{
+    std::uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
 }
 
 __device__ __forceinline__ void store_row8(__half* out, float const (&acc)[8], float inv)
@@ -699,9 +709,9 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     auto combine = [&](SegInfo const& sg) {
         // Every partial of lane sg.lane: item j = item_offset + i wrote slot
         // 2j, except the lane's first item, which wrote slot 2j + 1 when it
-        // started with an earlier lane. Loads of four items are issued
-        // together and folded with an online rescale, so the combine costs a
-        // few L2 round trips whatever the lane's item count.
+        // started with an earlier lane. Loads of kCombineBatch items are
+        // issued together and folded with an online rescale, so a combine
+        // costs one L2 round trip for the lanes of the balanced plan.
         std::uint32_t const first = sg.item_offset;
         std::uint32_t const count = sg.item_count;
         for (std::uint32_t idx = tid; idx < a.q_heads * 8u; idx += kConsumerWarps * 32) {
@@ -710,11 +720,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
             float M = kNegInf;
             float L = 0.f;
             float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            for (std::uint32_t i0 = 0; i0 < count; i0 += 4u) {
-                float2 ml[4];
-                float4 lo[4], hi[4];
+            for (std::uint32_t i0 = 0; i0 < count; i0 += kCombineBatch) {
+                float2 ml[kCombineBatch];
+                float4 lo[kCombineBatch], hi[kCombineBatch];
 #pragma unroll
-                for (std::uint32_t k = 0; k < 4; ++k) {
+                for (std::uint32_t k = 0; k < kCombineBatch; ++k) {
                     std::uint32_t const i = i0 + k;
                     if (i < count) {
                         std::uint64_t const sl = 2ull * (first + i) + (i == 0 ? sg.first_sub : 0u);
@@ -729,7 +739,7 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     }
                 }
 #pragma unroll
-                for (std::uint32_t k = 0; k < 4; ++k) {
+                for (std::uint32_t k = 0; k < kCombineBatch; ++k) {
                     float const m_new = fmaxf(M, ml[k].x);
                     float const m_use = m_new == kNegInf ? 0.f : m_new;
                     float const fo = exp2f(M - m_use);       // rescale of what is folded so far
@@ -756,9 +766,8 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
     // Reads the pending lane's answer (thread 0 wrote s_last before calling)
     // and combines it if this CTA was the lane's last.
     auto resolve_pending = [&]() {
-        consumer_sync();
+        consumer_sync();  // thread 0's acquire reaches the other consumers through this barrier
         if (*s_last) {
-            __threadfence();
             combine(pend);
         }
         pending = false;
@@ -977,8 +986,11 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                     *s_last = pend_done + 1 == pend.item_count;
                 }
                 if (split) {
-                    __threadfence();  // cumulative: publishes every thread's partial
-                    pend_done = atomicAdd(&a.counters[si.lane], 1u);
+                    // Release (cumulative over the partial stores of every
+                    // consumer thread, ordered before this one by the
+                    // consumer barrier) and acquire in one atomic: the CTA
+                    // that counts last also sees every other partial.
+                    pend_done = atom_add_acq_rel_gpu(&a.counters[si.lane], 1u);
                 }
             }
             if (pending) {

@@ -163,6 +163,22 @@ __device__ __forceinline__ void named_barrier_sync(std::uint32_t id, std::uint32
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over the participating threads,
+// so that all of them take the same branch afterwards.
+__device__ __forceinline__ bool named_barrier_and(std::uint32_t id, std::uint32_t count, bool pred)
+{
+    std::uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<std::uint32_t>(pred)), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 __device__ __forceinline__ void cluster_arrive()
 {
     asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
@@ -460,8 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
         std::uint32_t const c = t & 7u;
-        // This thread's 8 norm weights of stage i (ones without a weight);
-        // requested one stage ahead, so the load never waits on L2.
+        // This thread's 8 norm weights of stage i (FP16 ones without a weight).
         auto norm_chunk = [&](std::uint32_t i) {
             std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
             uint4 g = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);  // FP16 1.0 x 8
@@ -470,21 +485,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
             return g;
         };
-        uint4 g_next = norm_chunk(0);
-        for (std::uint32_t i = 0; i < nk; ++i) {
-            std::uint32_t const s = i % kStages;
+        auto transform = [&](std::uint32_t s, uint4 graw) {
             float gv[8];
-            {
-                uint4 const graw = g_next;
-                __half const* gh = reinterpret_cast<__half const*>(&graw);
+            __half const* gh = reinterpret_cast<__half const*>(&graw);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    gv[e] = __half2float(gh[e]);
-                }
-            }
-            g_next = norm_chunk(i + 1);
-            if (!mbar_wait_spin(&xfull[s], (i / kStages) & 1u, st)) {
-                break;
+            for (int e = 0; e < 8; ++e) {
+                gv[e] = __half2float(gh[e]);
             }
             std::uint8_t* xs = x_stage + s * BN * 128;
             for (std::uint32_t n = t >> 3; n < static_cast<std::uint32_t>(BN); n += 8u) {
@@ -498,10 +504,51 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 }
                 *chunk = raw;
             }
-            // Generic-proxy writes, read next by the tensor cores (async proxy).
+        };
+        // The stages requested right after the dependency wait land together:
+        // they are normalised as one batch behind one proxy fence and one
+        // barrier, so the MMA of the prefetched weights starts after one
+        // hand-over instead of one per stage. Later stages go one by one
+        // (their weights stream from HBM meanwhile). Norm weights are
+        // requested one step ahead, so those loads never wait on L2.
+        std::uint32_t const first = nk < static_cast<std::uint32_t>(kStages) ? nk : kStages;
+        uint4 gfirst[kStages];
+#pragma unroll
+        for (int j = 0; j < kStages; ++j) {
+            gfirst[j] = norm_chunk(j);
+        }
+        uint4 g_next = norm_chunk(first);
+        bool got = true;
+#pragma unroll
+        for (int j = 0; j < kStages; ++j) {
+            if (got && static_cast<std::uint32_t>(j) < first) {
+                got = mbar_wait_spin(&xfull[j], 0u, st);
+                if (got) {
+                    transform(j, gfirst[j]);
+                }
+            }
+        }
+        // Generic-proxy writes, read next by the tensor cores (async proxy).
+        // A wait that gave up stops every normalising thread at the same
+        // point (the MMA warp's own bounded wait then ends the tile).
+        fence_proxy_async_smem();
+        bool ok = named_barrier_and(1, 64, got);
+        if (t == 0 && ok) {
+            for (std::uint32_t j = 0; j < first; ++j) {
+                mbar_arrive(&full[j]);
+            }
+        }
+        for (std::uint32_t i = first; ok && i < nk; ++i) {
+            std::uint32_t const s = i % kStages;
+            uint4 const graw = g_next;
+            g_next = norm_chunk(i + 1);
+            got = mbar_wait_spin(&xfull[s], (i / kStages) & 1u, st);
+            if (got) {
+                transform(s, graw);
+            }
             fence_proxy_async_smem();
-            named_barrier_sync(1, 64);
-            if (t == 0) {
+            ok = named_barrier_and(1, 64, got);
+            if (t == 0 && ok) {
                 mbar_arrive(&full[s]);
             }
         }

@@ -211,11 +211,19 @@ class RefModel:
                                              u16p]),
             "kref_model_generate": (C.c_int, [C.c_void_p, C.POINTER(C.c_uint32), C.c_uint32, C.c_uint32,
                                               C.POINTER(C.c_uint32)]),
+            "kref_model_lane_create": (C.c_void_p, [C.c_void_p]),
+            "kref_model_lane_destroy": (None, [C.c_void_p]),
+            "kref_model_lane_length": (C.c_uint32, [C.c_void_p]),
+            "kref_model_lane_append_kv": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint32, u16p, u16p]),
+            "kref_model_forward_lanes": (C.c_int, [C.c_void_p, C.c_uint32, C.POINTER(C.c_void_p),
+                                                   C.POINTER(C.c_uint32), C.POINTER(C.c_uint32),
+                                                   C.POINTER(C.c_uint32), C.c_uint32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(lib, name)
             fn.restype, fn.argtypes = res, args
         self.lib = lib
+        self.lanes = []
         scratch = tempfile.gettempdir().encode()
         if cfg is None:
             self.h = lib.kref_model_create(None, None, scratch)
@@ -253,8 +261,38 @@ class RefModel:
                                          max_new, out)
         return [out[i] for i in range(n)]
 
+    # Lanes: more ReferenceModel instances over this archive (own K/V each).
+    def lane_create(self) -> int:
+        lane = self.lib.kref_model_lane_create(self.h)
+        assert lane
+        self.lanes.append(lane)
+        return lane
+
+    def lane_append_kv(self, lane: int, k: np.ndarray, v: np.ndarray):
+        """k, v: FP16 bits [n][layers][kv_heads * head_dim]."""
+        k = np.ascontiguousarray(k, np.uint16)
+        v = np.ascontiguousarray(v, np.uint16)
+        assert self.lib.kref_model_lane_append_kv(self.h, lane, k.shape[0], ptr(k, C.c_uint16),
+                                                  ptr(v, C.c_uint16))
+
+    def lane_length(self, lane: int) -> int:
+        return self.lib.kref_model_lane_length(lane)
+
+    def forward_lanes(self, lanes: list, tokens: list, positions: list, threads: int) -> list:
+        """ReferenceModel::forward once per lane, over `threads` host threads;
+        the greedy token of each lane."""
+        n = len(lanes)
+        out = (C.c_uint32 * n)()
+        assert self.lib.kref_model_forward_lanes(self.h, n, (C.c_void_p * n)(*lanes),
+                                                 (C.c_uint32 * n)(*tokens), (C.c_uint32 * n)(*positions),
+                                                 out, threads), "reference forward rejected its inputs"
+        return list(out)
+
     def close(self):
-        if self.h:
+        for lane in getattr(self, "lanes", []):
+            self.lib.kref_model_lane_destroy(lane)
+        self.lanes = []
+        if getattr(self, "h", None):
             self.lib.kref_model_destroy(self.h)
             self.h = None
 

@@ -35,6 +35,7 @@
 #include <limits>
 #include <memory>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <utility>
 #include <vector>
@@ -184,6 +185,79 @@ KREF_API int kref_model_forward(void* p, uint32_t token, uint32_t position, floa
         for (std::size_t i = 0; i < h->model->final_hidden.size(); ++i) {
             final_hidden[i] = fp16(h->model->final_hidden[i]);
         }
+    }
+    return 1;
+}
+
+// ---- lanes: further ReferenceModel instances over the same archive --------
+// A lane is one ReferenceModel (its own keys / values) reading the shared,
+// immutable archive; lanes may run forward concurrently.
+
+KREF_API void* kref_model_lane_create(void* p)
+{
+    try {
+        return new ReferenceModel(*static_cast<RefModel*>(p)->archive);
+    } catch (...) {
+        return nullptr;
+    }
+}
+
+KREF_API void kref_model_lane_destroy(void* lane) { delete static_cast<ReferenceModel*>(lane); }
+
+KREF_API uint32_t kref_model_lane_length(void* lane)
+{
+    return static_cast<uint32_t>(static_cast<ReferenceModel*>(lane)->keys[0].size());
+}
+
+// Appends n past tokens of given K / V (FP16 bits, [n][layers][kv_heads *
+// head_dim] each) to the lane's cache, as forward would have stored them.
+KREF_API int kref_model_lane_append_kv(void* p, void* lane, uint32_t n, const uint16_t* k,
+    const uint16_t* v)
+{
+    TinyLlamaConfig const& c = static_cast<RefModel*>(p)->archive->config;
+    auto* m = static_cast<ReferenceModel*>(lane);
+    std::size_t const row = std::size_t(c.kv_head_count) * c.head_dimension;
+    for (uint32_t t = 0; t < n; ++t) {
+        for (uint32_t l = 0; l < c.layer_count; ++l) {
+            std::size_t const base = (std::size_t(t) * c.layer_count + l) * row;
+            std::vector<float> kr(row), vr(row);
+            for (std::size_t e = 0; e < row; ++e) {
+                kr[e] = fp32(k[base + e]);
+                vr[e] = fp32(v[base + e]);
+            }
+            m->keys[l].push_back(std::move(kr));
+            m->values[l].push_back(std::move(vr));
+        }
+    }
+    return 1;
+}
+
+// One ReferenceModel::forward per lane, lanes spread over `threads` host
+// threads; next[i] is the lane's greedy token (first maximum, as
+// referenceGeneration takes it). Returns 1 when every lane ran.
+KREF_API int kref_model_forward_lanes(void* p, uint32_t n, void* const* lanes, const uint32_t* tokens,
+    const uint32_t* positions, uint32_t* next, uint32_t threads)
+{
+    TinyLlamaConfig const& c = static_cast<RefModel*>(p)->archive->config;
+    for (uint32_t i = 0; i < n; ++i) {
+        auto* m = static_cast<ReferenceModel*>(lanes[i]);
+        if (tokens[i] >= c.vocabulary_size || positions[i] != m->keys[0].size()) return 0;
+    }
+    std::atomic<uint32_t> cursor{0};
+    auto work = [&]() {
+        for (uint32_t i = cursor.fetch_add(1); i < n; i = cursor.fetch_add(1)) {
+            std::vector<float> const logits = static_cast<ReferenceModel*>(lanes[i])->forward(
+                tokens[i], positions[i]);
+            next[i] = static_cast<uint32_t>(std::max_element(logits.begin(), logits.end()) - logits.begin());
+        }
+    };
+    std::vector<std::thread> pool;
+    for (uint32_t t = 1; t < std::max<uint32_t>(1u, std::min(threads, n)); ++t) {
+        pool.emplace_back(work);
+    }
+    work();
+    for (std::thread& t : pool) {
+        t.join();
     }
     return 1;
 }

@@ -13,7 +13,10 @@
 #include "kim-kv/reference/kv_reference.h"
 #include "kim-kv/runtime/kv_cache_manager.h"
 
+#include <algorithm>
+#include <atomic>
 #include <cstring>
+#include <thread>
 #include <vector>
 
 using namespace kimkvcache;
@@ -181,6 +184,115 @@ KK_API int kref_reference_attention(uint32_t layers, uint32_t heads, uint32_t di
     if (!referenceAttention(layout, contiguous, token_count, q, out)) return 0;
     std::memcpy(output, out.data(), out.size() * sizeof(float));
     return 1;
+}
+
+// One step of the config-1 workload on the host, with the reference's own
+// parts: per lane KvCacheManager::reserveToken(expected) for the next token,
+// the new token's K / V (FP16, [lanes][kv_heads][dim]) stored into the host
+// pools at the reserved page, the lane's reserved table gathered per KV head
+// into a contiguous [K|V][token][dim] buffer (the CPU form of gatherKernel,
+// src/cuda/kv/page_kernels.cu:184-242), referenceAttention per query head on
+// its KV head (KvLayout{1, 1, dim}) rounded to FP16 as the paged kernel
+// stores it, then commit (commit != 0) or rollback of every reservation.
+// Pools: micro [slot][layers][K|V][8][kv_heads][dim], extent the same with
+// 64 tokens. (lane, KV head) pairs run on `threads` std::threads.
+// Returns 1 on success, 0 when a reservation or an attention call fails.
+KK_API int kref_c1_step(void* mgr, uint32_t lanes, uint64_t const* ids, uint32_t const* expected,
+    uint16_t* micro, uint16_t* extent, uint32_t layers, uint32_t layer, uint32_t kv_heads, uint32_t dim,
+    uint32_t q_heads, uint16_t const* k_new, uint16_t const* v_new, uint16_t const* q, uint16_t* out,
+    int commit, uint32_t threads)
+{
+    if (kv_heads == 0 || q_heads % kv_heads != 0 || layer >= layers) return 0;
+    std::vector<TokenReservationResult> res;
+    res.reserve(lanes);
+    bool ok = true;
+    for (uint32_t i = 0; i < lanes && ok; ++i) {
+        res.push_back(M(mgr)->reserveToken(ids[i], expected[i]));
+        ok = res.back().ok();
+    }
+    auto element = [&](MappingEntry const& m, uint32_t within, uint32_t kv, uint32_t h) -> uint16_t* {
+        std::size_t const page_tokens = m.kind == PageKind::Micro ? 8 : 64;
+        uint16_t* pool = m.kind == PageKind::Micro ? micro : extent;
+        std::size_t const off = ((((std::size_t(m.handle.slot) * layers + layer) * 2 + kv) * page_tokens
+                                     + within) * kv_heads + h) * dim;
+        return pool + off;
+    };
+    auto locate = [](BlockTable const& t, uint32_t token, uint32_t& within) -> MappingEntry const* {
+        for (MappingEntry const& m : t.entries()) {
+            if (token >= m.logical_token_begin && token < m.logical_token_begin + m.valid_tokens) {
+                within = token - m.logical_token_begin;
+                return &m;
+            }
+        }
+        return nullptr;
+    };
+    for (uint32_t i = 0; i < lanes && ok; ++i) {
+        uint32_t within = 0;
+        MappingEntry const* m = locate(res[i].reserved, expected[i], within);
+        if (m == nullptr) {
+            ok = false;
+            break;
+        }
+        for (uint32_t h = 0; h < kv_heads; ++h) {
+            std::memcpy(element(*m, within, 0, h), k_new + (std::size_t(i) * kv_heads + h) * dim, dim * 2);
+            std::memcpy(element(*m, within, 1, h), v_new + (std::size_t(i) * kv_heads + h) * dim, dim * 2);
+        }
+    }
+    std::atomic<uint32_t> next{0};
+    std::atomic<bool> failed{false};
+    uint32_t const group = q_heads / kv_heads;
+    auto work = [&]() {
+        std::vector<KvScalar> kv;
+        std::vector<float> query(dim), o;
+        for (uint32_t w = next.fetch_add(1); w < lanes * kv_heads; w = next.fetch_add(1)) {
+            uint32_t const i = w / kv_heads;
+            uint32_t const h = w % kv_heads;
+            uint32_t const tokens = expected[i] + 1;
+            kv.assign(std::size_t(2) * tokens * dim, 0);
+            for (MappingEntry const& m : res[i].reserved.entries()) {
+                for (uint32_t t = 0; t < m.valid_tokens; ++t) {
+                    uint32_t const token = m.logical_token_begin + t;
+                    if (token >= tokens) continue;
+                    std::memcpy(&kv[std::size_t(token) * dim], element(m, t, 0, h), dim * 2);
+                    std::memcpy(&kv[(std::size_t(tokens) + token) * dim], element(m, t, 1, h), dim * 2);
+                }
+            }
+            for (uint32_t g = 0; g < group; ++g) {
+                uint32_t const qh = h * group + g;
+                uint16_t const* qs = q + (std::size_t(i) * q_heads + qh) * dim;
+                for (uint32_t d = 0; d < dim; ++d) {
+                    query[d] = kvScalarToFloat(qs[d]);
+                }
+                if (!referenceAttention(KvLayout{1, 1, dim}, kv, tokens, query, o)) {
+                    failed = true;
+                    return;
+                }
+                uint16_t* os = out + (std::size_t(i) * q_heads + qh) * dim;
+                for (uint32_t d = 0; d < dim; ++d) {
+                    os[d] = floatToKvScalar(o[d]);
+                }
+            }
+        }
+    };
+    if (ok) {
+        std::vector<std::thread> pool;
+        for (uint32_t t = 1; t < std::max<uint32_t>(1u, std::min(threads, lanes * kv_heads)); ++t) {
+            pool.emplace_back(work);
+        }
+        work();
+        for (std::thread& t : pool) {
+            t.join();
+        }
+    }
+    for (TokenReservationResult const& r : res) {
+        if (r.ok()) {
+            KvCacheError const e = commit != 0 && ok && !failed
+                ? M(mgr)->commitTokenReservation(r.reservation_id)
+                : M(mgr)->rollbackTokenReservation(r.reservation_id);
+            ok = ok && e == KvCacheError::None;
+        }
+    }
+    return ok && !failed ? 1 : 0;
 }
 
 // loadWeightManifest + validateWeightDataFile (src/model/weight_manifest.cpp:461-684).

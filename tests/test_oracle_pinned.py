@@ -276,6 +276,45 @@ def test_model_oracle_equals_reference_model_small_config(ref_lib):
     oracle.close()
 
 
+def test_reference_lanes_on_given_kv_match_the_oracle(ref_lib):
+    """The reference arm's form of the reference model: several
+    ReferenceModel lanes over one archive, each fed a seeded past K/V and run
+    concurrently; every greedy token equals the oracle's on the same K/V and
+    a lone lane's run on one thread."""
+    w = _synthetic_weights(MODEL_SMALL, 44, 0.05)
+    ref = ko.RefModel(MODEL_SMALL, w)
+    oracle = ko.Model(MODEL_SMALL, w, threads=4)
+    L, row = MODEL_SMALL["layers"], MODEL_SMALL["kv_heads"] * MODEL_SMALL["head_dim"]
+    rng = np.random.default_rng(9)
+    contexts = [1, 9, 40, 77]
+    lanes = []
+    for i, ctx in enumerate(contexts):
+        k = (rng.standard_normal((ctx, L, row)) / 8).astype(np.float16).view(np.uint16)
+        v = (rng.standard_normal((ctx, L, row)) / 8).astype(np.float16).view(np.uint16)
+        lane = ref.lane_create()
+        ref.lane_append_kv(lane, k, v)
+        assert ref.lane_length(lane) == ctx
+        lanes.append(lane)
+        oracle.create(100 + i)
+        oracle.append_kv(100 + i, k, v)
+        if i == len(contexts) - 1:
+            single = ko.RefModel(MODEL_SMALL, w)
+            single_lane = single.lane_create()
+            single.lane_append_kv(single_lane, k, v)
+    toks, pos = [5, 17, 999, 3], list(contexts)
+    for _ in range(3):
+        got = ref.forward_lanes(lanes, toks, pos, threads=3)
+        want, _, _ = oracle.forward([100 + i for i in range(len(contexts))], toks, pos, want_logits=False,
+                                    want_hidden=False)
+        assert got == [int(x) for x in want]
+        one = single.forward_lanes([single_lane], [toks[-1]], [pos[-1]], threads=1)
+        assert one == [got[-1]]
+        toks, pos = got, [p + 1 for p in pos]
+    single.close()
+    ref.close()
+    oracle.close()
+
+
 @pytest.mark.slow
 def test_model_oracle_equals_reference_model_tinyllama_shape(ref_lib):
     """BASELINE config 2's shape (TinyLlama-1.1B: 22 layers, hidden 2048, 32
