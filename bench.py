@@ -39,6 +39,11 @@ import numpy as np
 ROOT = Path(__file__).resolve().parent
 METRIC = "decode tok/s/GPU TinyLlama-shape c4/c32; paged-attn HBM GB/s vs 8 TB/s"
 SEED = 0x4B564341434845  # the reference benchmark seed (include/kim-kv/benchmark/benchmark.h:123)
+# Wall-time bound of the reference arm's timed steps (the whole arm then ends
+# within a few minutes on the box's host cores).
+REFERENCE_BUDGET_S = 90.0
+# Positions per fused prefill call in the prompted decode workload (c5).
+PREFILL_CHUNK = 128
 
 
 def load_pkg(name, path):
@@ -126,6 +131,9 @@ def run_ours(args, rank, world, local_rank):
     wl = synth.decode_workload(args.config)
     B = wl["batch"]
     contexts = wl["contexts"]
+    # c5 as BASELINE states it: the lanes' contexts are their prompts, run
+    # through the fused prefill before decoding (c4/c2: synthetic prefixes).
+    prompted = args.config == "c5" and args.pages == "hetero"
     cfg = dict(synth.TINYLLAMA)
     cfg["max_positions"] = max(4608, max(contexts) + args.steps + args.warmup + 8)
     archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
@@ -160,19 +168,22 @@ def run_ours(args, rank, world, local_rank):
         # Room for every 64-token run that auto-promotion folds during the run:
         # with too few extents, promotion fails and the tails grow as micro pages.
         micro_cap, extent_cap = synth.pool_capacities(contexts, args.steps + args.warmup + 3)
+        if prompted:
+            micro_cap += PREFILL_CHUNK // 8 + 8  # a chunk's pages before promotion folds them
         backend = R["backend_create"](L, hkv, D, hq, hq * cfg["max_positions"] * 4, micro_cap, extent_cap)
         assert backend, "backend allocation failed"
         pools = kk.KvPools()
         assert R["backend_pools"](backend, C.byref(pools))
-        # Prefix state: append ctx tokens, seal, promote every full 64-token
-        # run, then seeded KV contents in every page.
-        synth.build_decode_prefixes(R, K, backend, pools, contexts, cfg, SEED + 2 * rank, sptr)
+        if not prompted:
+            # Prefix state: append ctx tokens, seal, promote every full
+            # 64-token run, then seeded KV contents in every page.
+            synth.build_decode_prefixes(R, K, backend, pools, contexts, cfg, SEED + 2 * rank, sptr)
     torch.cuda.synchronize(dev)
 
     status = C.c_int(0)
     detail = C.create_string_buffer(512)
-    runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr, max(B, 1),
-                                1, 1, C.byref(status), detail, 512)
+    runner = R["runner_create"](manifest.encode(), data.encode(), backend, sptr,
+                                max(B, PREFILL_CHUNK if prompted else 1), 1, 1, C.byref(status), detail, 512)
     assert runner, f"runner creation failed: {status.value} {detail.value.decode()}"
     # Fold each lane's 8 sealed micro pages into an extent whenever decode
     # completes a 64-token run, so tails stay short (8 micro -> 1 extent).
@@ -181,6 +192,30 @@ def run_ours(args, rank, world, local_rank):
     ids = (C.c_uint64 * B)(*range(1, B + 1))
     tokens = (C.c_uint32 * B)(*[random.Random(SEED + b).randrange(3, 32000) for b in range(B)])
     positions = (C.c_uint32 * B)(*contexts)
+    prefill = None
+    if prompted:
+        # The prompts go through the fused chunked prefill (the runner's
+        # multi-position step, PREFILL_CHUNK positions per call), timed with
+        # CUDA events around the API calls (prompt upload included); each
+        # call returns the lane's first generated token.
+        rng = random.Random(SEED)
+        prompts = [(C.c_uint32 * n)(*[rng.randrange(3, 32000) for _ in range(n)]) for n in contexts]
+        out1 = C.c_uint32(0)
+        pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pe0.record(stream)
+        for i, n in enumerate(contexts):
+            assert R["backend_create_request"](backend, i + 1) == 0
+            if not R["runner_prefill"](runner, i + 1, prompts[i], n, 0, C.byref(out1)):
+                buf = C.create_string_buffer(512)
+                R["runner_last_error"](runner, buf, 512)
+                raise RuntimeError(f"prefill of lane {i} failed: {buf.value.decode()}")
+            tokens[i] = out1.value
+        pe1.record(stream)
+        torch.cuda.synchronize(dev)
+        pms = pe0.elapsed_time(pe1)
+        prefill = {"prompt_tokens": sum(contexts), "ms": round(pms, 3),
+                   "tok_per_s": round(sum(contexts) / (pms / 1e3), 1), "chunk": PREFILL_CHUNK,
+                   "calls": len(contexts)}
     out_tok = (C.c_uint32 * B)()
     out_ok = (C.c_uint8 * B)()
 
@@ -200,8 +235,10 @@ def run_ours(args, rank, world, local_rank):
         tokens_v[:] = out_tok_v
         positions_v[:] += 1
 
+    warm_ms = 0.0
     for _ in range(args.warmup):
         step()
+        warm_ms += R["runner_last_step_ms"](runner)
     torch.cuda.synchronize(dev)
     if dist is not None:
         dist.barrier()
@@ -298,6 +335,17 @@ def run_ours(args, rank, world, local_rank):
     }
     if world > 1:
         line["per_rank_ms_per_step"] = per_rank_ms
+    if prefill is not None:
+        # The whole c5 job of this GPU: prompts through prefill, then every
+        # decode step (warm-up included), device time; new tokens = the one
+        # each prefill returns + one per decode step.
+        job_ms = prefill["ms"] + warm_ms + dev_ms
+        new_tok = B * (1 + args.warmup + args.steps)
+        line["config"]["workload"] = wl["name"].replace("ctx~", "prompts~") + ", fused prefill then decode"
+        line["prefill"] = prefill
+        line["job"] = {"prompt_tokens": prefill["prompt_tokens"], "new_tokens": new_tok,
+                       "device_ms": round(job_ms, 3), "new_tok_per_s": round(new_tok / (job_ms / 1e3), 1),
+                       "scope": "one GPU (each replica runs the same job)"}
     if check is not None:
         line["parity"] = check["parity"]
         if world == 1:
@@ -499,51 +547,84 @@ def oracle_check(kk, R, runner, backend, cfg, B, ids, tokens_v, positions_v, syn
 
 
 def run_reference(args, rank, world):
-    """The reference arm: the CPU restatement of the reference's FP16 decoder
-    (kind "port"; the reference's own model arithmetic is test-local C++),
-    on all host cores, on the same config as our arm: the same B lanes and
-    per-lane contexts, one decode step of every lane per timed step."""
+    """The reference arm: the reference's own model arithmetic, ReferenceModel
+    of its runner contract test (tests/cuda/cuda_model_runner_test.cpp:
+    213-420), compiled from the reference tree into oracle/_ref (kind
+    "reference"); where that library is absent, the C restatement of it
+    (kind "port"). The same B lanes and contexts as our arm, one
+    ReferenceModel per lane holding that lane's K/V (seeded), lanes spread
+    over every host core; a step decodes one token of every lane. The timed
+    steps stop at --steps or when the next step would pass REFERENCE_BUDGET_S
+    (stated in the sample). Rank 0 only."""
     if rank != 0:
         return None
     synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import kk_oracle_py as ko
     wl = synth.decode_workload(args.config)
     B, contexts = wl["batch"], wl["contexts"]
     cfg = dict(synth.TINYLLAMA)
     cfg["max_positions"] = max(4608, max(contexts) + args.steps + args.warmup + 8)
     threads = os.cpu_count() or 1
-    _, model = cpu_model(synth, cfg, threads)
+    archive_dir = Path(tempfile.gettempdir()) / f"kk_bench_archive_{cfg['max_positions']}"
+    _, _, weights = synth.write_archive(archive_dir, cfg, seed=SEED % (2 ** 31), keep_weights=True)
+    kind = "reference" if ko.REF_LIB.exists() else "port"
+    model = ko.RefModel(cfg, weights) if kind == "reference" else ko.Model(cfg, weights, threads=threads)
+    del weights
     L, row = cfg["layers"], cfg["kv_heads"] * cfg["head_dim"]
     rng = np.random.default_rng(5)
     longest = max(contexts)
     k = rng.uniform(-0.35, 0.35, (longest, L, row)).astype(np.float16).view(np.uint16)
     v = rng.uniform(-0.35, 0.35, (longest, L, row)).astype(np.float16).view(np.uint16)
+    lanes = []
     for b, ctx in enumerate(contexts):
-        model.create(b + 1)
-        model.append_kv(b + 1, k[:ctx], v[:ctx])
+        if kind == "reference":
+            lane = model.lane_create()
+            model.lane_append_kv(lane, k[:ctx], v[:ctx])
+        else:
+            lane = b + 1
+            model.create(lane)
+            model.append_kv(lane, k[:ctx], v[:ctx])
+        lanes.append(lane)
     del k, v
-    seqs = list(range(1, B + 1))
+
+    def forward(toks, pos):
+        if kind == "reference":
+            return model.forward_lanes(lanes, toks, pos, threads)
+        greedy, _, _ = model.forward(lanes, toks, pos, want_logits=False, want_hidden=False)
+        return [int(x) for x in greedy]
+
     toks = [3 + (7919 * b) % 31997 for b in range(B)]
     pos = list(contexts)
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        toks = forward(toks, pos)
+        pos = [p + 1 for p in pos]
     times = []
-    for _ in range(args.warmup + args.steps):
+    begin = time.perf_counter()
+    while len(times) < args.steps:
+        if times and time.perf_counter() - begin + statistics.fmean(times) > REFERENCE_BUDGET_S:
+            break
         t0 = time.perf_counter()
-        greedy, _, _ = model.forward(seqs, toks, pos, want_logits=False, want_hidden=False)
+        toks = forward(toks, pos)
         times.append(time.perf_counter() - t0)
-        toks = [int(x) for x in greedy]
         pos = [p + 1 for p in pos]
     model.close()
-    total_t = sum(times[args.warmup:])
-    value = B * args.steps / total_t
+    total_t = sum(times)
+    value = B * len(times) / total_t
+    what = ("ReferenceModel (the reference's test-local FP16 decoder, compiled from its source), one per lane"
+            if kind == "reference" else "C restatement of the reference FP16 decoder")
+    sample = (f"{len(times)} timed decode steps of all {B} lanes (after {warm} warm-up; bounded by "
+              f"{REFERENCE_BUDGET_S:.0f} s of the requested {args.steps}), {what}, {threads} host threads, "
+              "seeded K/V of the workload's contexts")
     return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_t / max(args.steps, 1) * 1e3, 2), "higher_is_better": True,
+            "n_gpus": world, "steps": len(times), "steps_requested": args.steps, "warmup": warm,
+            "ms_per_step": round(total_t / max(len(times), 1) * 1e3, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": wl["name"], "batch": B, "ctx_mean": round(sum(contexts) / B, 1)},
-            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads,
-                             "kind": "port",
-                             "sample": f"{args.steps} timed decode steps of all {B} lanes (after "
-                                       f"{args.warmup} warm-up), C restatement of the reference FP16 "
-                                       "decoder on seeded K/V of the workload's contexts"},
+            "config": {"workload": wl["name"], "batch": B, "ctx_mean": round(sum(contexts) / B, 1),
+                       "same_config": True},
+            "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": kind,
+                             "sample": sample},
             "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -641,6 +722,224 @@ def run_c3(args):
         "e2e": {"value": round(produced / (ms / 1e3), 1), "unit": "tok/s",
                 "note": "host scheduler calls inside the CUDA-event-timed region"},
         "clocks": clocks}), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# config 1: single-layer GQA paged decode attention + one-token KV append
+
+C1_METRIC = "c1 attention+append step latency (1 layer, 4 lanes, ctx 17/100/513/2000)"
+
+
+class _DevArray:
+    def __init__(self, ptr, n):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<u2", "data": (ptr, False), "version": 3}
+
+
+def c1_reference(kk, synth, seed: int, data: dict):
+    """The reference's config-1 CPU path (oracle/_ref): its KvCacheManager
+    laid out like the GPU arm's backend, host pools holding the same seeded
+    K/V, and kref_c1_step (reserveToken, K/V store, gather, referenceAttention
+    per query head, rollback). Returns (step(threads) -> output, manager)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import kk_oracle_py as ko
+    lib = C.CDLL(str(ko.REF_LIB))
+    mgr = kk.Manager(lib, "kref_", synth.C1_POOL_PAGES, synth.C1_POOL_PAGES)
+
+    def promote(rid, begin):
+        err, pid, _, _ = mgr.prepare_promotion(rid, begin)
+        return err if err else mgr.commit_promotion(pid)
+
+    synth.c1_layout(mgr.create, mgr.append, mgr.seal, promote, mgr.release, seed)
+    f = lib.kref_c1_step
+    u16p = C.POINTER(C.c_uint16)
+    f.restype = C.c_int
+    f.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(C.c_uint64), C.POINTER(C.c_uint32), u16p, u16p,
+                  C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, u16p, u16p, u16p, u16p,
+                  C.c_int, C.c_uint32]
+    B = len(synth.C1_CONTEXTS)
+    micro, extent = data["micro"].copy(), data["extent"].copy()
+    out = np.zeros((B, synth.C1_SHAPE["q_heads"] * synth.C1_SHAPE["head_dim"]), np.uint16)
+    ids = (C.c_uint64 * B)(*range(1, B + 1))
+    expected = (C.c_uint32 * B)(*synth.C1_CONTEXTS)
+    p = lambda a: a.ctypes.data_as(u16p)
+
+    def step(threads):
+        assert f(mgr.h, B, ids, expected, p(micro), p(extent), synth.C1_SHAPE["layers"], 0, synth.C1_SHAPE["kv_heads"],
+                 synth.C1_SHAPE["head_dim"], synth.C1_SHAPE["q_heads"], p(data["k"]), p(data["v"]), p(data["q"]), p(out),
+                 0, threads) == 1, "reference config-1 step failed"
+        return out
+
+    return step, mgr
+
+
+def run_c1(args):
+    """BASELINE config 1 on one GPU: a 1-layer backend (4 KV heads, head_dim
+    64, 32 query heads) over a 4096-page micro and a 4096-page extent pool
+    laid out by synthetic.c1_layout, 4 lanes of context 17 / 100 / 513 / 2000, seeded
+    N(0,1)/8 contents. A step is the reference-facing per-layer token
+    transaction of every lane: reserveToken, writeLayer of the new token's K/V,
+    one attendLayerBatch over the 4 lanes (the paged decode-attention
+    kernel), then rollback, so every step sees the same tables. value = mean
+    device-timed latency of a step with the inputs resident (CUDA events on
+    the stream, host calls inside); e2e = the same with the queries and the
+    new K/V uploaded from pinned host memory and the outputs read back every
+    step. After timing: the page tables equal the reference KvCacheManager's
+    entry for entry, and the outputs are within 2e-2 of the reference's own
+    CPU path on the same contents (its timing is the CPU baseline)."""
+    import torch
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    R = kk.runtime()
+    stream = torch.cuda.current_stream(dev)
+    sptr = C.c_void_p(stream.cuda_stream)
+    L, H, D, Q = synth.C1_SHAPE["layers"], synth.C1_SHAPE["kv_heads"], synth.C1_SHAPE["head_dim"], synth.C1_SHAPE["q_heads"]
+    B = len(synth.C1_CONTEXTS)
+    ws_bytes = Q * 4096 * 4
+    backend = R["backend_create"](L, H, D, Q, ws_bytes, synth.C1_POOL_PAGES, synth.C1_POOL_PAGES)
+    assert backend, "backend allocation failed"
+    synth.c1_layout(lambda r: R["backend_create_request"](backend, r), lambda r, n: R["backend_append"](backend, r, n),
+              lambda r: R["backend_seal"](backend, r), lambda r, b: R["backend_promote"](backend, r, b, sptr),
+              lambda r: R["backend_release"](backend, r), SEED)
+    data = synth.c1_data(SEED)
+    pools = kk.KvPools()
+    assert R["backend_pools"](backend, C.byref(pools))
+    for name, ptr in (("micro", pools.micro), ("extent", pools.extent)):
+        host = torch.from_numpy(data[name].reshape(-1).view(np.int16))
+        torch.as_tensor(_DevArray(ptr, host.numel()), device=dev).view(torch.int16).copy_(host)
+    q_h, k_h, v_h = (torch.from_numpy(data[n].view(np.int16)).pin_memory() for n in ("q", "k", "v"))
+    q_d, k_d, v_d = q_h.to(dev), k_h.to(dev), v_h.to(dev)
+    out_d = torch.zeros_like(q_d)
+    out_h = torch.zeros_like(q_h).pin_memory()
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize(dev)
+    st = C.c_int(0)
+    statuses = (C.c_int * B)()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def step(upload: bool, tables: list | None = None):
+        if upload:
+            q_d.copy_(q_h, non_blocking=True)
+            k_d.copy_(k_h, non_blocking=True)
+            v_d.copy_(v_h, non_blocking=True)
+        txns = []
+        for i in range(B):
+            t = R["txn_reserve"](backend, i + 1, synth.C1_CONTEXTS[i], sptr, C.byref(st))
+            assert t and st.value == 0, f"reserve failed: {st.value}"
+            txns.append(t)
+        for i, t in enumerate(txns):
+            assert R["txn_write_layer"](t, 0, k_d[i].data_ptr(), v_d[i].data_ptr()) == 0
+        ev[2].record(stream)
+        R["txn_attend_batch"]((C.c_void_p * B)(*txns), B, 0, q_d.data_ptr(), out_d.data_ptr(), Q * D * 2,
+                              ws.data_ptr(), ws_bytes, 1.0 / math.sqrt(D), statuses)
+        ev[3].record(stream)
+        assert list(statuses) == [0] * B, list(statuses)
+        if upload:
+            out_h.copy_(out_d, non_blocking=True)
+        if tables is not None:
+            for t in txns:
+                buf = (kk.KkEntry * 64)()
+                tt = kk.KkTableOut(C.cast(buf, C.POINTER(kk.KkEntry)), 64, 0, 0)
+                assert R["txn_reserved_table"](t, C.byref(tt)) == 1
+                tables.append(kk.Manager._entries(tt, buf)[1])
+        for t in txns:
+            assert R["txn_rollback"](t) == 0
+            R["txn_destroy"](t)
+
+    def timed(upload: bool, n: int):
+        lat, attend = [], []
+        for _ in range(n):
+            ev[0].record(stream)
+            step(upload)
+            ev[1].record(stream)
+            ev[1].synchronize()
+            lat.append(ev[0].elapsed_time(ev[1]) * 1e3)
+            attend.append(ev[2].elapsed_time(ev[3]) * 1e3)
+        return lat, attend
+
+    timed(False, args.warmup)
+    timed(True, args.warmup)
+    sampler = ClockSampler(gpu_id(torch, dev))
+    sampler.start()
+    lat, attend = timed(False, args.steps)
+    lat_e2e, _ = timed(True, args.steps)
+    clocks = sampler.stop()
+
+    # Checks (untimed): one more step, its reserved tables and outputs.
+    tables = []
+    step(True, tables)
+    torch.cuda.synchronize(dev)
+    got = out_h.numpy().view(np.uint16).view(np.float16).astype(np.float32)
+    ref_step, mgr = c1_reference(kk, synth, SEED, data)
+    ref_tables = []
+    for i in range(B):
+        err, rid, _, reserved = mgr.reserve(i + 1, synth.C1_CONTEXTS[i])
+        assert err == 0
+        ref_tables.append(reserved[1])
+        assert mgr.rollback(rid) == 0
+    threads = os.cpu_count() or 1
+    want = ref_step(threads).view(np.float16).astype(np.float32)
+    err = float(np.max(np.abs(got - want)))
+    t0, n_ref = time.perf_counter(), 0
+    while n_ref < 3 or (time.perf_counter() - t0 < 10.0 and n_ref < args.steps):
+        ref_step(threads)
+        n_ref += 1
+    ref_us = (time.perf_counter() - t0) / n_ref * 1e6
+    mgr.close()
+    R["backend_destroy"](backend)
+    parity = {"lanes": B, "max_abs_err": round(err, 6), "tolerance": 2e-2,
+              "tables_equal_reference": tables == ref_tables, "ok": err <= 2e-2 and tables == ref_tables}
+    kv_bytes = sum((c + 1) * H * D * 2 * 2 for c in synth.C1_CONTEXTS) * L
+    mean = statistics.fmean(lat)
+    return {
+        "metric": C1_METRIC, "value": round(mean, 2), "unit": "us", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(mean / 1e3, 5), "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic (seeded N(0,1)/8)",
+        "config": {"workload": "c1: 1 layer, 4 KV heads x 64, 32 query heads, 4 lanes ctx "
+                               "17/100/513/2000, 4096-page micro + 4096-page extent pools, seeded "
+                               "permutation; reserve + writeLayer + attendLayerBatch + rollback per step",
+                   "l2": "working set (2.7 MB) stays in L2: a latency figure, not a bandwidth one"},
+        "latency_us": {"p50": round(statistics.median(lat), 2), "p90": round(float(np.percentile(lat, 90)), 2),
+                       "attend_call_p50": round(statistics.median(attend), 2)},
+        "e2e": {"value": round(statistics.fmean(lat_e2e), 2), "unit": "us",
+                "p50": round(statistics.median(lat_e2e), 2),
+                "h2d_bytes_per_step": int(q_h.numel() * 2 + k_h.numel() * 2 + v_h.numel() * 2),
+                "d2h_bytes_per_step": int(out_h.numel() * 2)},
+        "algorithmic_kv_bytes_per_step": kv_bytes,
+        "gpu_launches": None,
+        "parity": parity,
+        "cpu_baseline": {"value": round(ref_us, 2), "unit": "us", "cores": threads, "kind": "reference",
+                         "sample": f"{n_ref} steps of the reference's CPU path on the same layout and "
+                                   "contents (KvCacheManager reserve/rollback + gather + "
+                                   "referenceAttention per query head, std::thread over lanes x KV heads)"},
+        "clocks": clocks,
+    }
+
+
+def run_reference_c1(args):
+    """Reference arm of config 1: the reference's own CPU path (kref_c1_step,
+    oracle/_ref) on the same layout and contents as run_c1, all host cores."""
+    kk = load_pkg("kim_kvcache_b200", ROOT / "kim-kvcache_b200" / "__init__.py")
+    synth = load_pkg("kk_synthetic", ROOT / "kim-kvcache_b200" / "synthetic.py")
+    data = synth.c1_data(SEED)
+    step, mgr = c1_reference(kk, synth, SEED, data)
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        step(threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step(threads)
+    us = (time.perf_counter() - t0) / max(args.steps, 1) * 1e6
+    mgr.close()
+    return {"impl": "reference", "metric": C1_METRIC, "value": round(us, 2), "unit": "us", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(us / 1e3, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic (seeded N(0,1)/8)", "config": {"workload": "c1 (as the GPU arm)"},
+            "cpu_baseline": {"value": round(us, 2), "unit": "us", "cores": threads, "kind": "reference",
+                             "sample": f"{args.steps} steps after {args.warmup} warm-up: KvCacheManager "
+                                       "reserve/rollback + gather + referenceAttention per query head"},
+            "e2e": {"value": round(us, 2), "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def run_prefill(args):
@@ -884,7 +1183,7 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5", "c3"])
+    ap.add_argument("--config", default="c4", choices=["c4", "c2", "c5", "c3", "c1"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", choices=["attention", "gemm", "gather"], default=None,
                     help="time one hot kernel on a standalone case (profiling)")
@@ -926,12 +1225,17 @@ def main():
     if args.config == "c3" and args.impl == "ours":
         run_c3(args)
         return
-    line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
-        args, rank, world, local_rank)
+    if args.config == "c1":
+        line = None
+        if rank == 0:
+            line = run_reference_c1(args) if args.impl == "reference" else run_c1(args)
+    else:
+        line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(
+            args, rank, world, local_rank)
     if line is not None:
         print(json.dumps(line), flush=True)
         if "parity" in line and not line["parity"]["ok"]:
-            sys.exit("parity gate failed: the checked step disagrees with the CPU oracle")
+            sys.exit("parity gate failed: the checked step disagrees with the CPU reference")
 
 
 if __name__ == "__main__":

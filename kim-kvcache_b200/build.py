@@ -8,6 +8,11 @@ objects in _build_trace/): every CTA of the projection and attention kernels
 records %globaltimer stamps of its phases, read back by
 `python bench.py --trace OUT`. Rebuild without --trace for measurements.
 
+--define NAME[=VALUE] (repeatable) compiles the CUDA sources with an extra
+preprocessor definition, objects in their own _build_<defines>/ folder:
+the tuning variants the kernels expose (KK_GEMM_STAGES, KK_PLAN_SEGMENT_COST,
+KK_MBAR_SPIN, ...), for A/B timing against the default build.
+
 Objects go to kim-kvcache_b200/_build/, the library to
 kim-kvcache_b200/lib/libkk_b200.so (both git-ignored; the .so travels to the
 GPU box with the working tree). Recompiles a source when it or any header
@@ -70,14 +75,18 @@ def compile_one(src: Path, force: bool, hdr_time: float, extra: list[str],
 
 
 def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
-          ptxas_info: bool = False, trace: bool = False) -> Path:
+          ptxas_info: bool = False, trace: bool = False, defines: list[str] | None = None) -> Path:
+    defines = sorted(defines or [])
     obj_dir = PKG / "_build_trace" if trace else OBJ
+    if defines:
+        obj_dir = obj_dir.parent / (obj_dir.name + "_" + "_".join(d.replace("=", "-") for d in defines))
     obj_dir.mkdir(parents=True, exist_ok=True)
     LIB.parent.mkdir(parents=True, exist_ok=True)
     hdr_time = newest_header()
     extra = ["-Xptxas", "-v"] if ptxas_info else []
     if trace:
         extra.append("-DKK_TRACE")
+    extra += [f"-D{d}" for d in defines]
     srcs = sources()
     jobs = jobs or min(8, os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(jobs) as pool:
@@ -90,7 +99,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
     # The library is relinked whenever it was last linked from the other
     # object set (plain vs trace), recorded beside it.
     stamp = LIB.parent / ".variant"
-    variant = "trace" if trace else "plain"
+    variant = ("trace" if trace else "plain") + "".join(f" -D{d}" for d in defines)
     switched = not stamp.exists() or stamp.read_text() != variant
     if force or switched or not LIB.exists() or any(o.stat().st_mtime > lib_time for o in objs):
         cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
@@ -108,9 +117,11 @@ if __name__ == "__main__":
     ap.add_argument("-v", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
     ap.add_argument("--trace", action="store_true")
+    ap.add_argument("--define", action="append", default=[], metavar="NAME[=VALUE]",
+                    help="extra preprocessor definition for the CUDA sources (tuning variants)")
     a = ap.parse_args()
     try:
-        print(build(a.force, a.j, a.v, a.ptxas_info, a.trace))
+        print(build(a.force, a.j, a.v, a.ptxas_info, a.trace, a.define))
     except RuntimeError as e:
         print(e, file=sys.stderr)
         sys.exit(1)

@@ -207,13 +207,13 @@ __device__ __forceinline__ std::uint32_t pack_half2(float lo, float hi)
 __device__ __forceinline__ bool wait_or_abort(std::uint64_t* bar, std::uint32_t phase,
     int volatile* abort, unsigned int* status)
 {
-    if (mbar_try_wait_suspend(bar, phase)) {
+    if (mbar_poll(bar, phase)) {
         return true;
     }
     std::uint64_t const t0 = global_ns();
     std::uint64_t const limit = *static_cast<std::uint64_t volatile*>(&g_attn_wait_limit_ns);
     for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
-        if (mbar_try_wait_suspend(bar, phase)) {
+        if (mbar_poll(bar, phase)) {
             return true;
         }
         if (*abort) {

@@ -127,17 +127,28 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(std::uint64_t* bar, std::u
     return done != 0;
 }
 
-// Bounded wait on an mbarrier phase (suspending polls, limited by wall time
-// and poll count). Returns false, and records the error, when it gives up.
+// The poll of the bounded pipeline waits: suspending by default; the
+// KK_MBAR_SPIN tuning variant polls without suspending.
+__device__ __forceinline__ bool mbar_poll(std::uint64_t* bar, std::uint32_t phase)
+{
+#ifdef KK_MBAR_SPIN
+    return mbar_try_wait(bar, phase);
+#else
+    return mbar_try_wait_suspend(bar, phase);
+#endif
+}
+
+// Bounded wait on an mbarrier phase (polls limited by wall time and poll
+// count). Returns false, and records the error, when it gives up.
 __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, std::uint32_t phase,
     unsigned int* status)
 {
-    if (mbar_try_wait_suspend(bar, phase)) {
+    if (mbar_poll(bar, phase)) {
         return true;
     }
     std::uint64_t const t0 = global_ns();
     for (std::uint32_t i = 0; i < kMaxWaitPolls; ++i) {
-        if (mbar_try_wait_suspend(bar, phase)) {
+        if (mbar_poll(bar, phase)) {
             return true;
         }
         if (global_ns() - t0 > kWaitLimitNs) {

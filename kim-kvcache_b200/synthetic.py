@@ -145,3 +145,67 @@ def build_decode_prefixes(R: dict, K: dict, backend, pools, contexts: list[int],
     extent_elems = pools.extent_capacity * L * 2 * 64 * row
     assert K["fill_fp16"](C.c_void_p(pools.micro), micro_elems, fill_seed, 0.35, stream) == 0
     assert K["fill_fp16"](C.c_void_p(pools.extent), extent_elems, fill_seed + 1, 0.35, stream) == 0
+
+
+# ---- single-layer paged attention + one-token append ----
+
+C1_CONTEXTS = [17, 100, 513, 2000]
+C1_POOL_PAGES = 4096
+C1_SHAPE = dict(layers=1, kv_heads=4, head_dim=64, q_heads=32)
+
+
+def c1_layout(create, append, seal, promote, release, seed: int, pool_pages: int = C1_POOL_PAGES,
+              contexts: list[int] = C1_CONTEXTS) -> None:
+    """The config-1 page layout through a page-table API (the product backend
+    or a KvCacheManager, same calls; each returns 0 on success): every extent
+    slot and then every micro slot is allocated once and released in a seeded
+    order, so the pools' LIFO free lists hand out slots in a seeded
+    permutation; then lane i (request i + 1) appends its context, seals, and
+    promotes every full 64-token run (body = extents, tail = 8-token micro
+    pages). Both pools hold pool_pages pages."""
+    import random
+    rng = random.Random(seed)
+    base = 1 << 20
+    ids = []
+    for i in range(pool_pages):
+        rid = base + i
+        assert create(rid) == 0 and append(rid, 64) == 0
+        seal(rid)
+        assert promote(rid, 0) == 0
+        ids.append(rid)
+    rng.shuffle(ids)
+    for rid in ids:
+        assert release(rid) == 0
+    ids = []
+    for i in range(pool_pages):
+        rid = 2 * base + i
+        assert create(rid) == 0 and append(rid, 8) == 0
+        ids.append(rid)
+    rng.shuffle(ids)
+    for rid in ids:
+        assert release(rid) == 0
+    for i, ctx in enumerate(contexts):
+        rid = i + 1
+        assert create(rid) == 0 and append(rid, ctx) == 0
+        seal(rid)
+        for begin in range(0, (ctx // 64) * 64, 64):
+            assert promote(rid, begin) == 0
+
+
+def c1_data(seed: int, pool_pages: int = C1_POOL_PAGES, lanes: int = len(C1_CONTEXTS)) -> dict:
+    """Seeded FP16 contents (uint16 bits), all N(0, 1) / 8: both pools
+    ([slot][layer][K|V][tokens][kv_head][dim]), the step's queries
+    [lane][q_head * dim] and the appended token's K and V [lane][kv_head * dim]."""
+    rng = np.random.default_rng(seed)
+    L, H, D, Q = C1_SHAPE["layers"], C1_SHAPE["kv_heads"], C1_SHAPE["head_dim"], C1_SHAPE["q_heads"]
+
+    def normal(shape):
+        out = np.empty(shape, np.float16)
+        flat = out.reshape(-1)
+        for i in range(0, flat.size, 1 << 24):
+            n = min(1 << 24, flat.size - i)
+            flat[i:i + n] = (rng.standard_normal(n, dtype=np.float32) / 8).astype(np.float16)
+        return out.view(np.uint16)
+
+    return {"micro": normal((pool_pages, L, 2, 8, H, D)), "extent": normal((pool_pages, L, 2, 64, H, D)),
+            "q": normal((lanes, Q * D)), "k": normal((lanes, H * D)), "v": normal((lanes, H * D))}

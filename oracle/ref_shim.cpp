@@ -227,6 +227,27 @@ KK_API int kref_c1_step(void* mgr, uint32_t lanes, uint64_t const* ids, uint32_t
         return nullptr;
     };
     for (uint32_t i = 0; i < lanes && ok; ++i) {
+        // Partial-tail copy-on-write, as the reference backend performs it
+        // (src/cuda/kv/append.cpp:45-98): an entry of `before` whose handle
+        // changed in `reserved` is the shared partial tail, and its valid
+        // tokens are copied into the new page (every layer, K and V).
+        for (MappingEntry const& old_entry : res[i].before.entries()) {
+            for (MappingEntry const& now : res[i].reserved.entries()) {
+                if (now.logical_token_begin != old_entry.logical_token_begin || now.handle == old_entry.handle) {
+                    continue;
+                }
+                for (uint32_t l = 0; l < layers; ++l) {
+                    for (uint32_t kv = 0; kv < 2; ++kv) {
+                        for (uint32_t t = 0; t < old_entry.valid_tokens; ++t) {
+                            std::size_t const row = std::size_t(kv_heads) * dim;
+                            std::size_t const src = (((std::size_t(old_entry.handle.slot) * layers + l) * 2 + kv) * 8 + t) * row;
+                            std::size_t const dst = (((std::size_t(now.handle.slot) * layers + l) * 2 + kv) * 8 + t) * row;
+                            std::memcpy(micro + dst, micro + src, row * 2);
+                        }
+                    }
+                }
+            }
+        }
         uint32_t within = 0;
         MappingEntry const* m = locate(res[i].reserved, expected[i], within);
         if (m == nullptr) {

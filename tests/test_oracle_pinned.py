@@ -329,3 +329,60 @@ def test_model_oracle_equals_reference_model_tinyllama_shape(ref_lib):
     _run_both(ref, oracle, [2207, 31999, 3])
     ref.close()
     oracle.close()
+
+
+def test_config1_step_tables_and_attention_match_the_reference(kk, kk_lib, ref_lib):
+    """BASELINE config 1 on the CPU side, at a 512-page pool: the seeded
+    permutation layout built through the product KvCacheManager and through
+    the reference's gives identical reserved tables (partial-tail COW pages
+    included), and the oracle's paged GQA attention over the reserved tables
+    equals the reference's own config-1 host step (reserveToken, K/V store,
+    COW copy, gather, referenceAttention per query head) bit for bit.
+    (512 pages: a lane's context is appended as micro pages before its full
+    runs are promoted.)"""
+    synth = _synth()
+    pages = 512
+    data = synth.c1_data(11, pool_pages=pages)
+    mgrs = [kk.Manager(kk_lib, "kkrt_", pages, pages), kk.Manager(ref_lib, "kref_", pages, pages)]
+    for m in mgrs:
+        def promote(rid, begin, m=m):
+            err, pid, _, _ = m.prepare_promotion(rid, begin)
+            return err if err else m.commit_promotion(pid)
+        synth.c1_layout(m.create, m.append, m.seal, promote, m.release, 11, pool_pages=pages)
+    B = len(synth.C1_CONTEXTS)
+    micro, extent = data["micro"].copy(), data["extent"].copy()
+    for i, ctx in enumerate(synth.C1_CONTEXTS):
+        got = [m.reserve(i + 1, ctx) for m in mgrs]
+        assert got[0][0] == 0 and got[0][2:] == got[1][2:], f"lane {i}: tables differ"
+        _, rid, before, reserved = got[1]
+        for old in before[1]:
+            for new in reserved[1]:
+                if new[0] == old[0] and (new[3], new[4]) != (old[3], old[4]):
+                    micro[new[3], :, :, :old[1]] = micro[old[3], :, :, :old[1]]
+        for e in reserved[1]:
+            if e[0] <= ctx < e[0] + e[1]:
+                pool = micro if e[2] == 0 else extent
+                pool[e[3], 0, 0, ctx - e[0]] = data["k"][i].reshape(4, 64)
+                pool[e[3], 0, 1, ctx - e[0]] = data["v"][i].reshape(4, 64)
+        table = [(e[3], e[0], e[1], e[2]) for e in reserved[1]]
+        data.setdefault("oracle", []).append(ko.paged_attention(micro, extent, 1, 4, 64, 0, 32, table,
+                                                                data["q"][i]))
+        for m, g in zip(mgrs, got):
+            assert m.rollback(g[1]) == 0
+    assert mgrs[0].snapshot() == mgrs[1].snapshot()
+    f = ref_lib.kref_c1_step
+    u16p = C.POINTER(C.c_uint16)
+    f.restype = C.c_int
+    f.argtypes = [C.c_void_p, C.c_uint32, C.POINTER(C.c_uint64), C.POINTER(C.c_uint32), u16p, u16p,
+                  C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, u16p, u16p, u16p, u16p,
+                  C.c_int, C.c_uint32]
+    out = np.zeros((B, 32 * 64), np.uint16)
+    rm, rx = data["micro"].copy(), data["extent"].copy()
+    p = lambda a: a.ctypes.data_as(u16p)
+    assert f(mgrs[1].h, B, (C.c_uint64 * B)(*range(1, B + 1)), (C.c_uint32 * B)(*synth.C1_CONTEXTS), p(rm),
+             p(rx), 1, 0, 4, 64, 32, p(data["k"]), p(data["v"]), p(data["q"]), p(out), 0, 3) == 1
+    for i in range(B):
+        assert np.array_equal(out[i], data["oracle"][i]), f"lane {i}"
+    for m in mgrs:
+        assert m.invariants()
+        m.close()
