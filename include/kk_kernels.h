@@ -101,8 +101,15 @@ typedef struct kk_attn_lane {
 /* A split-KV work item: a run [desc_begin, desc_end) of the descriptor array.
  * Items of kk_attention_plan lie inside one lane (flags 0); items of
  * kk_attention_plan_balanced may continue from `lane` into the following
- * lanes when their descriptors are contiguous (flags KK_ATTN_ITEM_MULTI_LANE). */
+ * lanes when their descriptors are contiguous (flags KK_ATTN_ITEM_MULTI_LANE),
+ * and may cut a full 64-token extent page in half: the item's first
+ * descriptor then starts at token KK_ATTN_ITEM_SKIP(flags) and its last one
+ * ends at token KK_ATTN_ITEM_LIMIT(flags) (0: at its valid count), so two
+ * consecutive items share that descriptor. Only extent descriptors may be cut. */
 #define KK_ATTN_ITEM_MULTI_LANE 1u
+#define KK_ATTN_ITEM_SKIP(flags) (((flags) >> 8) & 0xffu)
+#define KK_ATTN_ITEM_LIMIT(flags) (((flags) >> 16) & 0xffu)
+#define KK_ATTN_EXTENT_HALF 32u
 typedef struct kk_attn_item {
     uint32_t lane;             /* first lane of the item */
     uint32_t desc_begin;

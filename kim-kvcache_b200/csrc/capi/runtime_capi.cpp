@@ -240,13 +240,41 @@ int kkrt_txn_attend_layer(void* t, uint32_t layer, const void* q, void* o, void*
         static_cast<KvScalar*>(o), ws, static_cast<std::size_t>(ws_bytes), scale}).error);
 }
 
+namespace {
+
+// Device batch item buffer of kkrt_txn_attend_batch: grown on demand, never
+// shrunk (a replaced buffer is kept: a launch queued earlier may still read it).
+DevicePagedDecodeBatchItem* batchItemScratch(uint32_t n)
+{
+    static std::mutex mutex;
+    static std::vector<DevicePagedDecodeBatchItem*> buffers;
+    static uint32_t capacity = 0;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (n > capacity || buffers.empty()) {
+        uint32_t const want = std::max<uint32_t>(n, 64u);
+        DevicePagedDecodeBatchItem* p = nullptr;
+        if (cudaMalloc(reinterpret_cast<void**>(&p), sizeof(DevicePagedDecodeBatchItem) * want) != cudaSuccess) {
+            return nullptr;
+        }
+        buffers.push_back(p);
+        capacity = want;
+    }
+    return buffers.back();
+}
+
+} // namespace
+
 void kkrt_txn_attend_batch(void* const* txns, uint32_t n, uint32_t layer, const void* q, void* o,
     uint64_t row_bytes, void* ws, uint64_t ws_bytes, float scale, int* statuses)
 {
+    // The batch item buffers the engine API asks for. This library's backend
+    // keeps its work lists in per-stream device scratch of its own and reads
+    // them only when that scratch could not be allocated; the device buffer
+    // is therefore one process-wide allocation, grown on demand, instead of
+    // a cudaMalloc / synchronize / cudaFree per call.
     std::vector<PagedDecodeBatchItem> items(n);
     std::vector<DevicePagedDecodeBatchItem> host(n);
-    DevicePagedDecodeBatchItem* dev = nullptr;
-    cudaMalloc(reinterpret_cast<void**>(&dev), sizeof(DevicePagedDecodeBatchItem) * (n == 0 ? 1 : n));
+    DevicePagedDecodeBatchItem* dev = batchItemScratch(n);
     for (uint32_t i = 0; i < n; ++i) {
         items[i].transaction = T(txns[i]);
         items[i].request = PagedDecodeRequest{layer,
@@ -254,10 +282,8 @@ void kkrt_txn_attend_batch(void* const* txns, uint32_t n, uint32_t layer, const 
             reinterpret_cast<KvScalar*>(static_cast<std::uint8_t*>(o) + i * row_bytes), ws,
             static_cast<std::size_t>(ws_bytes), scale};
     }
-    PagedDecodeBatch batch{items.data(), n, host.data(), dev, n};
+    PagedDecodeBatch batch{items.data(), n, host.data(), dev, dev != nullptr ? n : 0u};
     attendLayerBatch(batch);
-    cudaDeviceSynchronize();  // the scratch must outlive the upload
-    cudaFree(dev);
     for (uint32_t i = 0; i < n; ++i) {
         statuses[i] = static_cast<int>(items[i].status.error);
     }

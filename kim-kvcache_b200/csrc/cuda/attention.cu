@@ -31,6 +31,16 @@ namespace kk {
 
 __device__ unsigned int g_attn_status;
 
+// Cost model of the balanced plan, in tokens: every token, plus a fixed
+// charge per lane for what a CTA spends at the end of each lane segment
+// (merge, partial write, completion count and combine), measured at about
+// four and a half 32-token stages on B200.
+#ifdef KK_PLAN_SEGMENT_COST
+constexpr std::uint64_t kPlanSegmentCost = KK_PLAN_SEGMENT_COST;
+#else
+constexpr std::uint64_t kPlanSegmentCost = 144;
+#endif
+
 // Kernel choice for kk_paged_decode_attention (KK_ATTN_*), process-wide.
 std::atomic<int> g_attention_variant{KK_ATTN_AUTO};
 
@@ -651,15 +661,7 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
     if (num_parts == 0) {
         num_parts = 1;
     }
-    // Cost model of the token stream, in tokens: every token, plus a fixed
-    // charge per lane for what a CTA spends at the end of each lane segment
-    // (merge, partial write, completion count and combine), measured at
-    // about four and a half 32-token stages on B200.
-#ifdef KK_PLAN_SEGMENT_COST
-    constexpr std::uint64_t kSegmentCost = KK_PLAN_SEGMENT_COST;
-#else
-    constexpr std::uint64_t kSegmentCost = 144;
-#endif
+    constexpr std::uint64_t kSegmentCost = kk::kPlanSegmentCost;
     // A page occupies whole 8-token groups of a stage whatever its valid
     // count, so it costs its valid tokens rounded up to a group.
     auto cost = [](kk_page_desc const& d) -> std::uint64_t { return (d.valid_tokens + 7u) & ~7u; };
@@ -672,8 +674,10 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
             total += cost(descs[e]);
         }
     }
-    // Cut k of num_parts - 1 lands on the page boundary nearest to
-    // k * total / num_parts, so the runs are equal to within half a page.
+    // Cut k of num_parts - 1 lands on the unit boundary nearest to
+    // k * total / num_parts, where a unit is a page, or half of a full
+    // 64-token extent page (a stage's worth: the two halves stream as two
+    // stages), so the runs are equal to within a quarter of an extent.
     std::uint64_t const whole = total / num_parts;
     std::uint64_t const rest = total % num_parts;
     auto target = [&](std::uint64_t k) { return whole * k + rest * k / num_parts; };
@@ -705,37 +709,47 @@ uint32_t kk_attention_plan_balanced(const kk_page_desc* descs, kk_attn_lane* lan
             pos += kSegmentCost;
         }
         for (std::uint32_t e = ln.desc_offset; e < end; ++e) {
-            std::uint64_t const c = cost(descs[e]);
-            bool cut_before = false;
-            bool cut_after = false;
-            while (next_cut < num_parts && next_target < pos + c) {
-                if (2 * next_target < 2 * pos + c) {
-                    cut_before = true;
-                } else {
-                    cut_after = true;
+            bool const halves = descs[e].kind == 1u && descs[e].valid_tokens == 64u;  // a full extent
+            std::uint32_t const units = halves ? 2u : 1u;
+            std::uint64_t const c = halves ? KK_ATTN_EXTENT_HALF : cost(descs[e]);
+            for (std::uint32_t h = 0; h < units; ++h) {
+                bool cut_before = false;
+                bool cut_after = false;
+                while (next_cut < num_parts && next_target < pos + c) {
+                    if (2 * next_target < 2 * pos + c) {
+                        cut_before = true;
+                    } else {
+                        cut_after = true;
+                    }
+                    ++next_cut;
+                    next_target = next_cut < num_parts ? target(next_cut) : ~std::uint64_t{0};
                 }
-                ++next_cut;
-                next_target = next_cut < num_parts ? target(next_cut) : ~std::uint64_t{0};
-            }
-            if (cut_before) {
-                flush();
-            }
-            if (!open) {
-                cur = kk_attn_item{b, e, e, KK_ATTN_ITEM_MULTI_LANE};
-                open = true;
-                ++count;
-            }
-            if (ln.item_count == 0 || ln.item_offset + ln.item_count != count) {
-                if (ln.item_count == 0) {
-                    ln.item_offset = count - 1;
-                    ln.first_item_shared = cur.lane != b ? 1u : 0u;
+                if (cut_before && open) {
+                    if (h == 1u) {
+                        cur.reserved |= KK_ATTN_EXTENT_HALF << 16;  // ends after the first half
+                    }
+                    flush();
                 }
-                ++ln.item_count;
-            }
-            cur.desc_end = e + 1;
-            pos += c;
-            if (cut_after) {
-                flush();
+                if (!open) {
+                    cur = kk_attn_item{b, e, e, KK_ATTN_ITEM_MULTI_LANE | (h == 1u ? KK_ATTN_EXTENT_HALF << 8 : 0u)};
+                    open = true;
+                    ++count;
+                }
+                if (ln.item_count == 0 || ln.item_offset + ln.item_count != count) {
+                    if (ln.item_count == 0) {
+                        ln.item_offset = count - 1;
+                        ln.first_item_shared = cur.lane != b ? 1u : 0u;
+                    }
+                    ++ln.item_count;
+                }
+                cur.desc_end = e + 1;
+                pos += c;
+                if (cut_after) {
+                    if (h + 1u < units) {
+                        cur.reserved |= KK_ATTN_EXTENT_HALF << 16;
+                    }
+                    flush();
+                }
             }
         }
     }
@@ -837,6 +851,29 @@ int attentionDevCount(kk_kv_pools const* pools, std::uint32_t layer, std::uint32
     return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, max_items,
         num_items, query, query_stride, output, output_stride, scale, workspace, workspace_bytes,
         variant, status, stream);
+}
+
+int attentionLaunchTma(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint16_t const* query,
+    std::uint32_t query_stride, std::uint16_t* output, std::uint32_t output_stride, float scale,
+    void* workspace, std::uint64_t workspace_bytes, unsigned int* status, cudaStream_t stream)
+{
+    return launchAttention(pools, layer, q_heads, descs, lanes, num_lanes, items, num_items, nullptr,
+        query, query_stride, output, output_stride, scale, workspace, workspace_bytes, KK_ATTN_TMA, status,
+        stream);
+}
+
+std::uint32_t attentionPlanParts(kk_attn_lane const* lanes, std::uint32_t num_lanes, std::uint32_t sm_count)
+{
+    std::uint64_t cost = 0;
+    for (std::uint32_t b = 0; b < num_lanes; ++b) {
+        if (lanes[b].desc_count != 0) {
+            cost += lanes[b].token_count + kPlanSegmentCost;
+        }
+    }
+    std::uint64_t const parts = cost / kAttnMinPartCost;
+    return parts < 1 ? 1u : parts > sm_count ? sm_count : static_cast<std::uint32_t>(parts);
 }
 
 int attentionLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,

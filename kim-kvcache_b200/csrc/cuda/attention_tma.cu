@@ -406,6 +406,10 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
         for (std::uint32_t it = blockIdx.x; it < num_items; it += gridDim.x) {
 
             kk_attn_item const item = a.items[it];
+            // A half-extent cut: the item's first descriptor starts at token
+            // skip0, its last one ends at token limit_last (0: valid count).
+            std::uint32_t const skip0 = KK_ATTN_ITEM_SKIP(item.reserved);
+            std::uint32_t const limit_last = KK_ATTN_ITEM_LIMIT(item.reserved);
             std::uint32_t b = item.lane;
             if (b >= a.num_lanes) {
                 if (lane == 0) {
@@ -462,9 +466,19 @@ __global__ void __launch_bounds__(kThreads, 1) paged_attention_tma_kernel(
                         }
                         continue;
                     }
-                    if (valid != 0) {
-                        vt = valid;
-                        tok = 0;
+                    std::uint32_t const first = e == item.desc_begin ? skip0 : 0u;
+                    std::uint32_t const last = e + 1u == item.desc_end && limit_last != 0u && limit_last < valid
+                        ? limit_last : valid;
+                    if (m && (first != 0u || last != valid)) {
+                        // Only extent pages are cut (a micro page is one box).
+                        if (lane == 0) {
+                            atomicCAS(st, kErrNone, kErrBadDescriptor);
+                        }
+                        continue;
+                    }
+                    if (first < last) {
+                        vt = last;
+                        tok = first;
                         slot = static_cast<int>(d_slot);
                         micro = m;
                         have = true;

@@ -133,8 +133,12 @@ struct Arena {
     std::uint8_t* dev{nullptr};
     std::uint8_t* host{nullptr};
     unsigned int* status{nullptr};
-    // Reads of the error words go through this stream, so that they never
-    // wait for work that callers queued after the point being checked.
+    // Pinned mirror of the error words: a commit that synchronizes a stream
+    // queues the copy of the stream's word in front of the synchronize, so
+    // the word is on the host when the synchronize returns.
+    unsigned int* status_host{nullptr};
+    // Other reads of the error words go through this stream, so that they
+    // never wait for work that callers queued after the point being checked.
     cudaStream_t watch_stream{nullptr};
     std::vector<std::uint32_t> free_slots;
 
@@ -146,6 +150,8 @@ struct Arena {
             || cudaMallocHost(reinterpret_cast<void**>(&host), slot_bytes * kSlots) != cudaSuccess
             || cudaMalloc(reinterpret_cast<void**>(&status), kStatusWords * sizeof(unsigned int)) != cudaSuccess
             || cudaMemset(status, 0, kStatusWords * sizeof(unsigned int)) != cudaSuccess
+            || cudaMallocHost(reinterpret_cast<void**>(&status_host), kStatusWords * sizeof(unsigned int))
+                != cudaSuccess
             || cudaStreamCreateWithFlags(&watch_stream, cudaStreamNonBlocking) != cudaSuccess) {
             return false;
         }
@@ -160,6 +166,7 @@ struct Arena {
         cudaFree(dev);
         cudaFreeHost(host);
         cudaFree(status);
+        cudaFreeHost(status_host);
         if (watch_stream != nullptr) {
             cudaStreamDestroy(watch_stream);
         }
@@ -206,8 +213,22 @@ struct State {
         std::uint32_t word;
         std::uint64_t checked;      // submissions up to here were checked
         std::uint64_t failed_upto;  // submissions up to here are covered by a device error
+        std::uint64_t mirrored;     // the pinned mirror holds the word as of this submission
     };
     std::unordered_map<void*, StreamWatch> watch;  // under sync_mutex
+
+    // Per-stream device scratch of the per-layer attention launches: the
+    // lane records and balanced work list, and the split-lane workspace
+    // (completion counters zeroed when created; the kernel leaves them
+    // zero). Work on one stream is ordered, so one set per stream suffices.
+    static constexpr std::uint32_t kMaxPlanItems = 1024;
+    struct AttendScratch {
+        std::uint8_t* plan{nullptr};
+        void* workspace{nullptr};
+        std::uint64_t workspace_bytes{0};
+    };
+    std::unordered_map<void*, AttendScratch> attend_scratch;  // under sync_mutex
+    std::uint32_t sm_count{1};
 
     State(EngineKvConfig c, std::uint32_t micro_cap, std::uint32_t extent_cap)
         : config(c), kind(EngineKvBackendKind::Heterogeneous)
@@ -217,6 +238,7 @@ struct State {
         if (storage.status.ok() && !arena.init(micro_cap + extent_cap)) {
             storage.status = {CudaError::AllocationFailed, 0};
         }
+        initSmCount();
     }
 
     State(EngineKvConfig c, std::uint16_t tokens_per_page, std::uint32_t page_capacity, bool)
@@ -226,6 +248,16 @@ struct State {
     {
         if (storage.status.ok() && !arena.init(page_capacity)) {
             storage.status = {CudaError::AllocationFailed, 0};
+        }
+        initSmCount();
+    }
+
+    void initSmCount()
+    {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess
+            && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0) {
+            sm_count = static_cast<std::uint32_t>(sms);
         }
     }
 
@@ -292,6 +324,97 @@ struct State {
         c = c > covered ? c : covered;
     }
 
+    // The stream's attention scratch (created on first use; nullptr when the
+    // allocation fails, and the caller then plans one item per lane).
+    AttendScratch const* attendScratch(void* stream)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        auto f = attend_scratch.find(stream);
+        if (f != attend_scratch.end()) {
+            return &f->second;
+        }
+        AttendScratch sc;
+        std::uint32_t const hq = config.query_head_count;
+        sc.workspace_bytes = kk_attention_workspace_bytes(Arena::kSlots, kMaxPlanItems, hq,
+            config.kv_layout.head_dimension);
+        std::size_t const plan_bytes = Arena::kSlots * sizeof(kk_attn_lane) + kMaxPlanItems * sizeof(kk_attn_item);
+        if (cudaMalloc(reinterpret_cast<void**>(&sc.plan), plan_bytes) != cudaSuccess
+            || cudaMalloc(&sc.workspace, sc.workspace_bytes) != cudaSuccess
+            || kk_attention_workspace_init(sc.workspace, Arena::kSlots, stream) != 0) {
+            cudaFree(sc.plan);
+            cudaFree(sc.workspace);
+            return nullptr;
+        }
+        return &attend_scratch.emplace(stream, sc).first->second;
+    }
+
+    ~State()
+    {
+        for (auto& [stream, sc] : attend_scratch) {
+            cudaFree(sc.plan);
+            cudaFree(sc.workspace);
+        }
+    }
+
+    // One layer of attention over host lane records whose descriptors are in
+    // the arena, with the work list in the stream's scratch. Where the TMA
+    // kernel serves the shape: a token-balanced work list
+    // (kk_attention_plan_balanced, no part shorter than
+    // kk::kAttnMinPartCost) with the scratch's split-lane workspace, so a
+    // long lane is spread over many SMs. Otherwise one item per lane for the
+    // process-wide kernel choice, with the caller's workspace. Returns 0, a
+    // CUDA error or KK_EINVAL; -1 when the scratch is unavailable.
+    int attendPlanned(kk_attn_lane const* lanes, std::uint32_t n, std::uint32_t layer, void const* query,
+        void* output, float scale, void* workspace, std::uint64_t workspace_bytes, void* stream)
+    {
+        std::uint32_t const hq = config.query_head_count;
+        if (n == 0 || n > Arena::kSlots) {
+            return -1;
+        }
+        AttendScratch const* sc = attendScratch(stream);
+        if (sc == nullptr) {
+            return -1;
+        }
+        bool const tma = kk::attentionTmaSupported(&storage.pools, hq);
+        std::size_t const lane_bytes = n * sizeof(kk_attn_lane);
+        std::vector<std::uint8_t> host(lane_bytes + kMaxPlanItems * sizeof(kk_attn_item));
+        auto* planned = reinterpret_cast<kk_attn_lane*>(host.data());
+        std::memcpy(planned, lanes, lane_bytes);
+        auto* items = reinterpret_cast<kk_attn_item*>(host.data() + lane_bytes);
+        std::uint32_t count = n;
+        if (tma) {
+            count = kk_attention_plan_balanced(reinterpret_cast<kk_page_desc const*>(arena.host), planned, n,
+                kk::attentionPlanParts(planned, n, sm_count), items, kMaxPlanItems);
+            if (count == 0 || count > kMaxPlanItems) {
+                return KK_EINVAL;
+            }
+        } else {
+            for (std::uint32_t j = 0; j < n; ++j) {
+                planned[j].item_offset = j;
+                planned[j].item_count = 1;
+                planned[j].first_item_shared = 0;
+                items[j] = kk_attn_item{j, planned[j].desc_offset, planned[j].desc_offset + planned[j].desc_count, 0};
+            }
+        }
+        auto const s = static_cast<cudaStream_t>(stream);
+        // From pageable memory: the bytes are staged when the call returns.
+        cudaError_t const e = cudaMemcpyAsync(sc->plan, host.data(), lane_bytes + count * sizeof(kk_attn_item),
+            cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) {
+            return static_cast<int>(e);
+        }
+        std::uint32_t const row = hq * config.kv_layout.head_dimension;
+        auto const* descs = reinterpret_cast<kk_page_desc const*>(arena.dev);
+        auto const* dl = reinterpret_cast<kk_attn_lane const*>(sc->plan);
+        auto const* di = reinterpret_cast<kk_attn_item const*>(sc->plan + lane_bytes);
+        auto const* q = static_cast<std::uint16_t const*>(query);
+        auto* o = static_cast<std::uint16_t*>(output);
+        return tma ? kk::attentionLaunchTma(&storage.pools, layer, hq, descs, dl, n, di, count, q, row, o, row, scale,
+                         sc->workspace, sc->workspace_bytes, statusWord(stream), s)
+                   : kk::attentionLaunch(&storage.pools, layer, hq, descs, dl, n, di, count, q, row, o, row, scale,
+                         workspace, workspace_bytes, statusWord(stream), s);
+    }
+
     // Error word of the per-layer kernels launched on `stream`.
     unsigned int* statusWord(void* stream)
     {
@@ -302,15 +425,31 @@ struct State {
             // fail the transactions of every stream that shares it).
             std::uint32_t const n = static_cast<std::uint32_t>(watch.size());
             std::uint32_t const w = n < Arena::kStatusWords ? n : Arena::kStatusWords - 1;
-            f = watch.emplace(stream, StreamWatch{w, 0, 0}).first;
+            f = watch.emplace(stream, StreamWatch{w, 0, 0, 0}).first;
         }
         return arena.status + f->second.word;
     }
 
+    // Queues, on `stream`, the copy of its error word into the pinned mirror
+    // (to be followed by a synchronize of the stream that covers `seq`).
+    void queueStatusRead(void* stream, std::uint64_t seq)
+    {
+        std::lock_guard<std::mutex> lock(sync_mutex);
+        auto const f = watch.find(stream);
+        if (f == watch.end()) {
+            return;
+        }
+        if (cudaMemcpyAsync(arena.status_host + f->second.word, arena.status + f->second.word, sizeof(unsigned int),
+                cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream)) == cudaSuccess) {
+            f->second.mirrored = seq;
+        }
+    }
+
     // Called once `stream` is synchronized up to submission `covered`: reads
-    // the stream's error word (once per such point) and, when it is set,
-    // clears it on the stream behind everything queued so far. Returns the
-    // last submission that a device error covers (0: none).
+    // the stream's error word (once per such point; from the pinned mirror
+    // when the synchronize brought it along) and, when it is set, clears it
+    // on the stream behind everything queued so far. Returns the last
+    // submission that a device error covers (0: none).
     std::uint64_t checkStream(void* stream, std::uint64_t covered)
     {
         std::lock_guard<std::mutex> lock(sync_mutex);
@@ -321,10 +460,15 @@ struct State {
         StreamWatch& w = f->second;
         if (w.checked < covered) {
             unsigned int code = 0;
-            cudaError_t e = cudaMemcpyAsync(&code, arena.status + w.word, sizeof(code), cudaMemcpyDeviceToHost,
-                arena.watch_stream);
-            if (e == cudaSuccess) {
-                e = cudaStreamSynchronize(arena.watch_stream);
+            cudaError_t e = cudaSuccess;
+            if (w.mirrored >= covered) {
+                code = *static_cast<unsigned int volatile*>(arena.status_host + w.word);
+            } else {
+                e = cudaMemcpyAsync(&code, arena.status + w.word, sizeof(code), cudaMemcpyDeviceToHost,
+                    arena.watch_stream);
+                if (e == cudaSuccess) {
+                    e = cudaStreamSynchronize(arena.watch_stream);
+                }
             }
             if (e != cudaSuccess || code != 0) {
                 // Everything queued on the stream until the clear below is
@@ -394,6 +538,17 @@ public:
         CudaStatus const checked = prepareAttention(r);
         if (!checked.ok()) {
             return mapCuda(checked);
+        }
+        kk_attn_lane lane{descOffset() + static_cast<std::uint32_t>(Arena::kDescOff / sizeof(kk_page_desc)),
+            static_cast<std::uint32_t>(reserved_.entries().size()), reserved_.tokenCount(), 0, 1, 0, 0, 0};
+        int const planned = st_->attendPlanned(&lane, 1, r.layer, r.device_query, r.device_output,
+            r.attention_scale, r.device_workspace, r.workspace_bytes, stream_);
+        if (planned >= 0) {
+            if (planned != 0) {
+                return fail(submitError(planned));
+            }
+            markSubmitted();
+            return {};
         }
         std::uint8_t* const dev = slotDev();
         std::uint32_t const hq = st_->config.query_head_count;
@@ -587,6 +742,7 @@ private:
         std::uint64_t covered = 0;
         if (!st_->completed(stream_, last_submit_, covered)) {
             covered = st_->submit_seq.load();
+            st_->queueStatusRead(stream_, covered);
             cudaError_t const e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream_));
             if (e != cudaSuccess) {
                 final_ = {CudaError::ExecutionFailed, static_cast<int>(e)};
@@ -684,8 +840,7 @@ void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
         qmin = std::min(qmin, reinterpret_cast<std::uint8_t const*>(batch.items[i].request.device_query));
         omin = std::min(omin, reinterpret_cast<std::uint8_t const*>(batch.items[i].request.device_output));
     }
-    std::size_t const lanes_bytes = txns.size() * (sizeof(kk_attn_lane) + sizeof(kk_attn_item));
-    bool strided = batch.item_capacity * sizeof(DevicePagedDecodeBatchItem) >= lanes_bytes;
+    bool strided = true;
     for (std::size_t i : idx) {
         PagedDecodeRequest const& r = batch.items[i].request;
         std::ptrdiff_t const dq = reinterpret_cast<std::uint8_t const*>(r.device_query) - qmin;
@@ -709,9 +864,8 @@ void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
     if (ready.empty()) {
         return;
     }
-    auto* host = reinterpret_cast<std::uint8_t*>(batch.host_items);
-    auto* lanes = reinterpret_cast<kk_attn_lane*>(host);
-    auto* items = reinterpret_cast<kk_attn_item*>(host + ready.size() * sizeof(kk_attn_lane));
+    std::vector<kk_attn_lane> lanes(ready.size());
+    std::vector<kk_attn_item> items(ready.size());
     for (std::size_t j = 0; j < ready.size(); ++j) {
         CudaTxn* t = txns[ready[j]];
         PagedDecodeRequest const& r = batch.items[idx[ready[j]]].request;
@@ -723,20 +877,35 @@ void CudaTxn::attendLayerBatch(PagedDecodeBatch& batch)
         items[j] = kk_attn_item{static_cast<std::uint32_t>(j), off, off + count, 0};
     }
     cudaStream_t const s = static_cast<cudaStream_t>(stream_);
-    std::size_t const bytes = ready.size() * (sizeof(kk_attn_lane) + sizeof(kk_attn_item));
-    int rc = static_cast<int>(cudaMemcpyAsync(batch.device_items, batch.host_items, bytes,
-        cudaMemcpyHostToDevice, s));
-    if (rc == 0) {
-        auto* dev = reinterpret_cast<std::uint8_t*>(batch.device_items);
-        PagedDecodeRequest const& r0 = batch.items[idx[ready[0]]].request;
-        std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
-        rc = kk::attentionLaunch(&st_->storage.pools, r0.layer, hq,
-            reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
-            reinterpret_cast<kk_attn_lane const*>(dev), static_cast<std::uint32_t>(ready.size()),
-            reinterpret_cast<kk_attn_item const*>(dev + ready.size() * sizeof(kk_attn_lane)),
-            static_cast<std::uint32_t>(ready.size()), reinterpret_cast<std::uint16_t const*>(qmin),
-            row, reinterpret_cast<std::uint16_t*>(const_cast<std::uint8_t*>(omin)), row,
-            r0.attention_scale, r0.device_workspace, r0.workspace_bytes, st_->statusWord(stream_), s);
+    PagedDecodeRequest const& rq = batch.items[idx[ready[0]]].request;
+    int rc = st_->attendPlanned(lanes.data(), static_cast<std::uint32_t>(lanes.size()), rq.layer, qmin,
+        const_cast<std::uint8_t*>(omin), rq.attention_scale, rq.device_workspace, rq.workspace_bytes, stream_);
+    if (rc < 0) {
+        // Without the stream's scratch: one item per lane, through the
+        // caller's batch buffers (as the reference's batched launch uses them).
+        std::size_t const lane_bytes = ready.size() * sizeof(kk_attn_lane);
+        std::size_t const bytes = lane_bytes + ready.size() * sizeof(kk_attn_item);
+        if (batch.host_items == nullptr || batch.device_items == nullptr
+            || batch.item_capacity * sizeof(DevicePagedDecodeBatchItem) < bytes) {
+            rc = KK_EINVAL;
+        } else {
+            auto* host = reinterpret_cast<std::uint8_t*>(batch.host_items);
+            std::memcpy(host, lanes.data(), lane_bytes);
+            std::memcpy(host + lane_bytes, items.data(), bytes - lane_bytes);
+            rc = static_cast<int>(cudaMemcpyAsync(batch.device_items, batch.host_items, bytes,
+                cudaMemcpyHostToDevice, s));
+        }
+        if (rc == 0) {
+            auto* dev = reinterpret_cast<std::uint8_t*>(batch.device_items);
+            std::uint32_t const row = hq * st_->config.kv_layout.head_dimension;
+            rc = kk::attentionLaunch(&st_->storage.pools, rq.layer, hq,
+                reinterpret_cast<kk_page_desc const*>(st_->arena.dev),
+                reinterpret_cast<kk_attn_lane const*>(dev), static_cast<std::uint32_t>(ready.size()),
+                reinterpret_cast<kk_attn_item const*>(dev + lane_bytes), static_cast<std::uint32_t>(ready.size()),
+                reinterpret_cast<std::uint16_t const*>(qmin), row,
+                reinterpret_cast<std::uint16_t*>(const_cast<std::uint8_t*>(omin)), row, rq.attention_scale,
+                rq.device_workspace, rq.workspace_bytes, st_->statusWord(stream_), s);
+        }
     }
     std::uint64_t ok_lanes = 0;
     for (std::size_t k : ready) {

@@ -44,6 +44,21 @@ int attentionLaunch(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t
     std::uint32_t query_stride, std::uint16_t* output, std::uint32_t output_stride, float scale,
     void* workspace, std::uint64_t workspace_bytes, unsigned int* status, cudaStream_t stream);
 
+// attentionLaunch with the TMA kernel whatever the process-wide variant
+// switch: the balanced work lists (kk_attention_plan_balanced) are served by
+// it only. The caller checks attentionTmaSupported first.
+int attentionLaunchTma(kk_kv_pools const* pools, std::uint32_t layer, std::uint32_t q_heads,
+    kk_page_desc const* descs, kk_attn_lane const* lanes, std::uint32_t num_lanes,
+    kk_attn_item const* items, std::uint32_t num_items, std::uint16_t const* query,
+    std::uint32_t query_stride, std::uint16_t* output, std::uint32_t output_stride, float scale,
+    void* workspace, std::uint64_t workspace_bytes, unsigned int* status, cudaStream_t stream);
+
+// Parts for kk_attention_plan_balanced: one per SM, but none smaller than
+// kAttnMinPartCost tokens of plan cost, so that a small batch is not cut
+// into items shorter than what a first stage and a combine cost.
+constexpr std::uint32_t kAttnMinPartCost = 256;
+std::uint32_t attentionPlanParts(kk_attn_lane const* lanes, std::uint32_t num_lanes, std::uint32_t sm_count);
+
 // TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
 // KV heads, up to 16 query heads per KV head; serves both plan kinds
 // (kk_attention_plan and kk_attention_plan_balanced). Arguments are validated

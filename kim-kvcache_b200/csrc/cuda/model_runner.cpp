@@ -572,10 +572,11 @@ GenerationBatchResult runBatch(CudaTinyLlamaModelRunner::Impl& im,
                 static_cast<std::uint8_t>(e.kind), 0, 0};
         }
     }
-    // One token-balanced run per SM (the TMA attention kernel serves every
-    // shape this runner accepts).
-    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, B, im.sm_count,
-        im.stepHost<kk_attn_item>(im.off_items), im.max_items);
+    // One token-balanced run per SM, none shorter than the cost of a first
+    // stage and a combine (the TMA attention kernel serves every shape this
+    // runner accepts).
+    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, B,
+        kk::attentionPlanParts(lanes, B, im.sm_count), im.stepHost<kk_attn_item>(im.off_items), im.max_items);
     if (n_items > im.max_items) {
         result.success = false;
         result.detail = "attention work list capacity exceeded";
@@ -738,8 +739,8 @@ GenerationStepResult prefillStep(CudaTinyLlamaModelRunner::Impl& im, RequestId i
         }
         lanes[i] = kk_attn_lane{lane_first, n_descs - lane_first, p + 1, 0, 0, i, 0, 0};
     }
-    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, n, im.sm_count,
-        im.stepHost<kk_attn_item>(im.off_items), im.max_items);
+    std::uint32_t const n_items = kk_attention_plan_balanced(descs, lanes, n,
+        kk::attentionPlanParts(lanes, n, im.sm_count), im.stepHost<kk_attn_item>(im.off_items), im.max_items);
     if (n_items > im.max_items) {
         return {false, 0, "attention work list capacity exceeded"};
     }

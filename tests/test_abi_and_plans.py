@@ -56,27 +56,48 @@ def make_tables(kk, contexts, seed):
     return arr, lanes, len(descs)
 
 
+def item_span(it, e, descs):
+    """Tokens [first, last) of descriptor e that item `it` covers."""
+    valid = descs[e].valid_tokens
+    first = (it.reserved >> 8) & 0xFF if e == it.desc_begin else 0
+    limit = (it.reserved >> 16) & 0xFF
+    last = limit if e == it.desc_end - 1 and limit else valid
+    return first, last
+
+
 def check_cover(kk, descs, lanes, items, n_items, multi_lane):
-    """Items tile the descriptor array in order; lane ranges match the items."""
+    """Items tile the descriptor array in order, token for token: an item
+    starts where the previous one ended, on the same descriptor only when
+    that descriptor (a full extent) is cut at its half. Lane ranges match."""
     nl = len(lanes)
-    pos = 0
+    pos = (0, 0)   # (descriptor, token) where the next item must start
     touched = {b: [] for b in range(nl)}
     for i in range(n_items):
         it = items[i]
-        assert it.desc_begin == pos and it.desc_end > it.desc_begin
-        assert (it.reserved == kk.ATTN_ITEM_MULTI_LANE) == multi_lane
+        flags = it.reserved & 0xFF
+        assert flags == (kk.ATTN_ITEM_MULTI_LANE if multi_lane else 0)
+        assert it.desc_end > it.desc_begin
+        first, _ = item_span(it, it.desc_begin, descs)
+        if first:
+            assert pos == (it.desc_begin, first) and descs[it.desc_begin].kind == 1, (i, pos)
+        else:
+            assert pos == (it.desc_begin, 0), (i, pos)
         b = it.lane
-        e = it.desc_begin
-        while e < it.desc_end:
+        for e in range(it.desc_begin, it.desc_end):
             while lanes[b].desc_offset + lanes[b].desc_count <= e:
                 b += 1
                 assert multi_lane, "per-lane items never cross a lane"
             assert lanes[b].desc_offset <= e
+            f, l = item_span(it, e, descs)
+            assert f < l or descs[e].valid_tokens == 0
+            if l != descs[e].valid_tokens:
+                assert e == it.desc_end - 1 and descs[e].kind == 1 and descs[e].valid_tokens == 64 and l == 32
             if not touched[b] or touched[b][-1] != i:
                 touched[b].append(i)
-            e += 1
-        pos = it.desc_end
-    assert pos == sum(lanes[b].desc_count for b in range(nl))
+        last_e = it.desc_end - 1
+        _, l = item_span(it, last_e, descs)
+        pos = (last_e, l) if l != descs[last_e].valid_tokens else (it.desc_end, 0)
+    assert pos == (sum(lanes[b].desc_count for b in range(nl)), 0)
     for b in range(nl):
         got = list(range(lanes[b].item_offset, lanes[b].item_offset + lanes[b].item_count))
         assert got == touched[b], (b, got, touched[b])
@@ -106,13 +127,18 @@ def test_balanced_plan_covers_and_balances(kk, seed, parts):
     starts = {lanes[b].desc_offset for b in range(len(contexts)) if lanes[b].desc_count}
     total_cost = total + SEG * len(starts)
     per = total_cost / parts
-    costs = [sum(descs[e].valid_tokens + (SEG if e in starts else 0)
-                 for e in range(items[i].desc_begin, items[i].desc_end)) for i in range(n)]
+    def span_cost(i, e):
+        f, l = item_span(items[i], e, descs)
+        seg = SEG if e in starts and f == 0 else 0
+        return (l - f) + seg
+    costs = [sum(span_cost(i, e) for e in range(items[i].desc_begin, items[i].desc_end)) for i in range(n)]
     assert n <= parts
-    assert max(costs) <= per + 2 * (32 + SEG) + 1
+    # A cut lands within half a unit (a micro page, or half of a full extent)
+    # of its target, plus a segment charge.
+    assert max(costs) <= per + 2 * (16 + SEG) + 8
     if per >= 128:
         assert n == parts
-        assert min(costs) >= per - 2 * (32 + SEG) - 1
+        assert min(costs) >= per - 2 * (16 + SEG) - 8
 
 
 def test_balanced_plan_counts_items_beyond_capacity(kk):
