@@ -876,11 +876,14 @@ def run_c1(args):
     torch.cuda.synchronize(dev)
     got = out_h.numpy().view(np.uint16).view(np.float16).astype(np.float32)
     ref_step, mgr = c1_reference(kk, synth, SEED, data)
-    ref_tables = []
+    # As the GPU step does: every lane reserved, then every lane rolled back.
+    ref_tables, ref_ids = [], []
     for i in range(B):
         err, rid, _, reserved = mgr.reserve(i + 1, synth.C1_CONTEXTS[i])
         assert err == 0
         ref_tables.append(reserved[1])
+        ref_ids.append(rid)
+    for rid in ref_ids:
         assert mgr.rollback(rid) == 0
     threads = os.cpu_count() or 1
     want = ref_step(threads).view(np.float16).astype(np.float32)
