@@ -43,7 +43,7 @@ SEED = 0x4B564341434845  # the reference benchmark seed (include/kim-kv/benchmar
 # within a few minutes on the box's host cores).
 REFERENCE_BUDGET_S = 90.0
 # Positions per fused prefill call in the prompted decode workload (c5).
-PREFILL_CHUNK = 128
+PREFILL_CHUNK = 64
 
 
 def load_pkg(name, path):
@@ -1216,7 +1216,7 @@ def main():
                     help="time the fused multi-token prefill instead of decode (one GPU)")
     ap.add_argument("--prompt", type=int, default=1024, help="--prefill: tokens per prompt")
     ap.add_argument("--prefill-requests", type=int, default=8, help="--prefill: prompts timed")
-    ap.add_argument("--prefill-chunk", type=int, default=128,
+    ap.add_argument("--prefill-chunk", type=int, default=64,
                     help="--prefill: positions per fused step (the runner batch size)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)

@@ -602,7 +602,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
             }
         }
+#ifdef KK_GEMM_SPIN_RBAR
+        bool const got = mbar_wait_spin(rbar, 0, st);
+#else
         bool const got = mbar_wait(rbar, 0, st);
+#endif
         KK_GEMM_STAMP(5)
         // Sum over the K slices in rank order (deterministic).
         for (std::uint32_t j = 0; j < cols; ++j) {
