@@ -438,7 +438,7 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
 # partials received, reduced, epilogue stored, exit. Attention CTA: entry,
 # producer's wait returned, producer done, first stage taken, consumers done,
 # exit (aux = stages | split-combine flag << 31).
-GEMM_PHASES = ["wait", "acc", "part", "cl_wait", "recv", "reduced", "epi", "exit"]
+GEMM_PHASES = ["wait", "acc", "part", "cl_wait", "recv", "reduced", "epi", "exit", "xnorm"]
 ATTN_PHASES = ["wait", "prod_done", "first_stage", "cons_done", "exit"]
 
 
@@ -483,7 +483,8 @@ def trace_step(kk, step, torch, dev, path):
         t = r["t"].astype(np.int64)
         waits = t[:, 1][t[:, 1] > 0]
         w0 = int(waits.min()) if len(waits) else int(t[:, 0].min())
-        cols = [1, 2, 3, 4, 5, 6, 7, 8] if phases is GEMM_PHASES else [1, 2, 3, 4, 5]
+        # GEMM stamp 9: the stages requested before the wait normalised (fused RMSNorm only).
+        cols = [1, 2, 3, 4, 5, 6, 7, 8, 9] if phases is GEMM_PHASES else [1, 2, 3, 4, 5]
         med = [float(np.median(t[:, c][t[:, c] > 0] - w0)) / 1e3 if (t[:, c] > 0).any() else float("nan")
                for c in cols]
         end = int(t[:, 8 if phases is GEMM_PHASES else 5].max())

@@ -262,6 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     unsigned int* const st = args.status != nullptr ? args.status : &g_gemm_status;
 #ifdef KK_TRACE
     std::uint64_t tr[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    __shared__ std::uint64_t s_xnorm_ready;  // stamp 9: the first stages normalised (or 0)
+    if (tid == 0) {
+        s_xnorm_ready = 0;
+    }
 #endif
     KK_GEMM_STAMP(0)
     std::uint32_t const S = args.split;
@@ -537,6 +541,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             for (std::uint32_t j = 0; j < first; ++j) {
                 mbar_arrive(&full[j]);
             }
+#ifdef KK_TRACE
+            s_xnorm_ready = global_ns();
+#endif
         }
         for (std::uint32_t i = first; ok && i < nk; ++i) {
             std::uint32_t const s = i % kStages;
@@ -602,11 +609,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
             }
         }
-#ifdef KK_GEMM_SPIN_RBAR
-        bool const got = mbar_wait_spin(rbar, 0, st);
-#else
         bool const got = mbar_wait(rbar, 0, st);
-#endif
         KK_GEMM_STAMP(5)
         // Sum over the K slices in rank order (deterministic).
         for (std::uint32_t j = 0; j < cols; ++j) {
@@ -867,6 +870,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
 #ifdef KK_TRACE
     if (tid == 0) {
         tr[8] = global_ns();
+        tr[9] = s_xnorm_ready;
         std::uint32_t const slot = atomicAdd(&g_gemm_trace_n, 1u);
         if (slot < kTraceCap) {
             TraceRec& r = g_gemm_trace[slot];
