@@ -438,7 +438,8 @@ def attention_roofline(kk, K, R, backend, pools, B, contexts, positions, cfg, st
 # partials received, reduced, epilogue stored, exit. Attention CTA: entry,
 # producer's wait returned, producer done, first stage taken, consumers done,
 # exit (aux = stages | split-combine flag << 31).
-GEMM_PHASES = ["wait", "acc", "part", "cl_wait", "recv", "reduced", "epi", "exit", "xnorm"]
+GEMM_PHASES = ["wait", "acc", "part", "cl_wait", "recv", "reduced", "epi", "exit", "xnorm", "rnorm", "x_land",
+               "x_done", "mma0", "x_first_done", "x_last_land"]
 ATTN_PHASES = ["wait", "prod_done", "first_stage", "cons_done", "exit"]
 
 
@@ -451,7 +452,7 @@ def trace_step(kk, step, torch, dev, path):
     lib = kk.load_library()
     if not hasattr(lib, "kk_trace_read_gemm"):
         raise SystemExit("--trace needs the trace build: python kim-kvcache_b200/build.py --trace")
-    rec = np.dtype([("tag", "<u4"), ("block", "<u4"), ("smid", "<u4"), ("aux", "<u4"), ("t", "<u8", 10)])
+    rec = np.dtype([("tag", "<u4"), ("block", "<u4"), ("smid", "<u4"), ("aux", "<u4"), ("t", "<u8", 16)])
     readers = {"gemm": lib.kk_trace_read_gemm, "attn": lib.kk_trace_read_attn}
     for fn in readers.values():
         fn.restype = C.c_uint32
@@ -483,8 +484,9 @@ def trace_step(kk, step, torch, dev, path):
         t = r["t"].astype(np.int64)
         waits = t[:, 1][t[:, 1] > 0]
         w0 = int(waits.min()) if len(waits) else int(t[:, 0].min())
-        # GEMM stamp 9: the stages requested before the wait normalised (fused RMSNorm only).
-        cols = [1, 2, 3, 4, 5, 6, 7, 8, 9] if phases is GEMM_PHASES else [1, 2, 3, 4, 5]
+        # GEMM stamps 9-12: the fused RMSNorm's release, RMS factors, first X
+        # tile landed, transforms done; 13: the first MMA issued.
+        cols = list(range(1, 16)) if phases is GEMM_PHASES else [1, 2, 3, 4, 5]
         med = [float(np.median(t[:, c][t[:, c] > 0] - w0)) / 1e3 if (t[:, c] > 0).any() else float("nan")
                for c in cols]
         end = int(t[:, 8 if phases is GEMM_PHASES else 5].max())

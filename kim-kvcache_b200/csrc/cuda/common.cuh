@@ -99,7 +99,7 @@ struct TraceRec {
     std::uint32_t block;  // blockIdx.y << 16 | blockIdx.x
     std::uint32_t smid;
     std::uint32_t aux;
-    std::uint64_t t[10];
+    std::uint64_t t[16];
 };
 constexpr std::uint32_t kTraceCap = 1u << 16;
 

@@ -261,10 +261,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
     std::uint32_t const lane = tid % 32;
     unsigned int* const st = args.status != nullptr ? args.status : &g_gemm_status;
 #ifdef KK_TRACE
-    std::uint64_t tr[10] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
-    __shared__ std::uint64_t s_xnorm_ready;  // stamp 9: the first stages normalised (or 0)
-    if (tid == 0) {
-        s_xnorm_ready = 0;
+    std::uint64_t tr[16] = {0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0, 0};
+    // Stamps of other threads (0: not reached): 9 the first stages normalised
+    // and released, 10 the RMS factors ready, 11 the first X tile seen landed,
+    // 12 the first stages' transforms done, 13 the first MMA issued, 14 the
+    // first stage's transform done, 15 the last prefetched X tile seen landed.
+    __shared__ std::uint64_t s_xstamp[7];
+    if (tid < 7) {
+        s_xstamp[tid] = 0;
     }
 #endif
     KK_GEMM_STAMP(0)
@@ -402,6 +406,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 break;
             }
             tc_fence_after();
+#ifdef KK_TRACE
+            if (i == 0) {
+                s_xstamp[4] = global_ns();
+            }
+#endif
             std::uint64_t const a = umma_desc_k_sw128(w_stage + s * kTileWBytes);
             std::uint64_t const b = umma_desc_k_sw128(x_stage + s * BN * 128);
 #pragma unroll
@@ -476,6 +485,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         }
         named_barrier_sync(1, 64);
+#ifdef KK_TRACE
+        if (t == 0) {
+            s_xstamp[1] = global_ns();
+        }
+#endif
         // Thread t owns 16-byte chunk t % 8 (dims 8c .. 8c+7 of the tile's 64)
         // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
@@ -489,24 +503,37 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
             return g;
         };
+        // One stage in place: x' = half((x * r) * g) per element, FP32
+        // products rounded once (packed conversions, two elements each).
         auto transform = [&](std::uint32_t s, uint4 graw) {
-            float gv[8];
-            __half const* gh = reinterpret_cast<__half const*>(&graw);
+            float2 gv[4];
+            __half2 const* gh = reinterpret_cast<__half2 const*>(&graw);
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                gv[e] = __half2float(gh[e]);
+            for (int e = 0; e < 4; ++e) {
+                gv[e] = __half22float2(gh[e]);
             }
             std::uint8_t* xs = x_stage + s * BN * 128;
-            for (std::uint32_t n = t >> 3; n < static_cast<std::uint32_t>(BN); n += 8u) {
-                uint4* chunk = reinterpret_cast<uint4*>(xs + n * 128u + ((c ^ (n & 7u)) << 4));
-                uint4 raw = *chunk;
-                __half* h = reinterpret_cast<__half*>(&raw);
-                float const r = rnorm[n];
+            // The thread's BN / 8 rows (t / 8, t / 8 + 8, ...): every load
+            // first, then the math and the stores, so the loads overlap.
+            constexpr std::uint32_t kRows = BN / 8;
+            uint4 raw[kRows];
+            float rr[kRows];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    h[e] = __float2half_rn(__half2float(h[e]) * r * gv[e]);
+            for (std::uint32_t q = 0; q < kRows; ++q) {
+                std::uint32_t const n = (t >> 3) + 8u * q;
+                raw[q] = *reinterpret_cast<uint4 const*>(xs + n * 128u + ((c ^ (n & 7u)) << 4));
+                rr[q] = rnorm[n];
+            }
+#pragma unroll
+            for (std::uint32_t q = 0; q < kRows; ++q) {
+                std::uint32_t const n = (t >> 3) + 8u * q;
+                __half2* h = reinterpret_cast<__half2*>(&raw[q]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    float2 const f = __half22float2(h[e]);
+                    h[e] = __floats2half2_rn(f.x * rr[q] * gv[e].x, f.y * rr[q] * gv[e].y);
                 }
-                *chunk = raw;
+                *reinterpret_cast<uint4*>(xs + n * 128u + ((c ^ (n & 7u)) << 4)) = raw[q];
             }
         };
         // The stages requested right after the dependency wait land together:
@@ -514,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // barrier, so the MMA of the prefetched weights starts after one
         // hand-over instead of one per stage. Later stages go one by one
         // (their weights stream from HBM meanwhile). Norm weights are
-        // requested one step ahead, so those loads never wait on L2.
+        // requested one step ahead.
         std::uint32_t const first = nk < static_cast<std::uint32_t>(kStages) ? nk : kStages;
         uint4 gfirst[kStages];
 #pragma unroll
@@ -527,11 +554,29 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         for (int j = 0; j < kStages; ++j) {
             if (got && static_cast<std::uint32_t>(j) < first) {
                 got = mbar_wait_spin(&xfull[j], 0u, st);
+#ifdef KK_TRACE
+                if (j == 0 && t == 0) {
+                    s_xstamp[2] = global_ns();
+                }
+                if (static_cast<std::uint32_t>(j) + 1u == first && t == 0) {
+                    s_xstamp[6] = global_ns();
+                }
+#endif
                 if (got) {
                     transform(j, gfirst[j]);
                 }
+#ifdef KK_TRACE
+                if (j == 0 && t == 0) {
+                    s_xstamp[5] = global_ns();
+                }
+#endif
             }
         }
+#ifdef KK_TRACE
+        if (t == 0) {
+            s_xstamp[3] = global_ns();
+        }
+#endif
         // Generic-proxy writes, read next by the tensor cores (async proxy).
         // A wait that gave up stops every normalising thread at the same
         // point (the MMA warp's own bounded wait then ends the tile).
@@ -542,7 +587,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 mbar_arrive(&full[j]);
             }
 #ifdef KK_TRACE
-            s_xnorm_ready = global_ns();
+            s_xstamp[0] = global_ns();
 #endif
         }
         for (std::uint32_t i = first; ok && i < nk; ++i) {
@@ -870,7 +915,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
 #ifdef KK_TRACE
     if (tid == 0) {
         tr[8] = global_ns();
-        tr[9] = s_xnorm_ready;
+        for (int i = 0; i < 7; ++i) {
+            tr[9 + i] = s_xstamp[i];
+        }
         std::uint32_t const slot = atomicAdd(&g_gemm_trace_n, 1u);
         if (slot < kTraceCap) {
             TraceRec& r = g_gemm_trace[slot];
@@ -878,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             r.block = (blockIdx.y << 16) | blockIdx.x;
             r.smid = sm_id();
             r.aux = args.K;
-            for (int i = 0; i < 10; ++i) {
+            for (int i = 0; i < 16; ++i) {
                 r.t[i] = tr[i];
             }
         }
