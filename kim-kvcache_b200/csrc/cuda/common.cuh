@@ -89,6 +89,18 @@ __device__ __forceinline__ std::uint64_t global_ns()
     return t;
 }
 
+// 16-byte read-only global load issued where it stands in the program (a
+// plain __ldg of constant data may be sunk by the compiler to its first
+// use, which puts its latency after any wait in between).
+__device__ __forceinline__ uint4 ldg_u4_now(void const* p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
 #ifdef KK_TRACE
 // Phase trace, compiled only into instrumented builds (-DKK_TRACE): each CTA
 // of an instrumented kernel fills one record with %globaltimer stamps of its

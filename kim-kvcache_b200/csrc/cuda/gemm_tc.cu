@@ -443,6 +443,25 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // Warps 2-3: the RMS factor of every batch row, then each X tile
         // normalised in place as it lands.
         std::uint32_t const t = tid - 64u;
+        std::uint32_t const c = t & 7u;
+        // This thread's 8 norm weights of stage i (FP16 ones without a
+        // weight), issued in program order: those of the first stages go out
+        // together with the sums of squares below.
+        auto norm_chunk = [&](std::uint32_t i) {
+            std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
+            uint4 g = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);  // FP16 1.0 x 8
+            if (args.norm_w != nullptr && i < nk && k0 < args.K) {
+                g = ldg_u4_now(args.norm_w + k0);
+            }
+            return g;
+        };
+        std::uint32_t const first = nk < static_cast<std::uint32_t>(kStages) ? nk : kStages;
+        uint4 gfirst[kStages];
+#pragma unroll
+        for (int j = 0; j < kStages; ++j) {
+            gfirst[j] = norm_chunk(j);
+        }
+        uint4 g_next = norm_chunk(first);
         if (args.sq_in != nullptr) {
             // From the producing kernel's per-tile sums of squares, one thread
             // per row, every partial requested at once and summed in tile order.
@@ -493,16 +512,6 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // Thread t owns 16-byte chunk t % 8 (dims 8c .. 8c+7 of the tile's 64)
         // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
-        std::uint32_t const c = t & 7u;
-        // This thread's 8 norm weights of stage i (FP16 ones without a weight).
-        auto norm_chunk = [&](std::uint32_t i) {
-            std::uint32_t const k0 = (kb_begin + i) * kBK + c * 8u;
-            uint4 g = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);  // FP16 1.0 x 8
-            if (args.norm_w != nullptr && i < nk && k0 < args.K) {
-                g = __ldg(reinterpret_cast<uint4 const*>(args.norm_w + k0));
-            }
-            return g;
-        };
         // One stage in place: x' = half((x * r) * g) per element, FP32
         // products rounded once (packed conversions, two elements each).
         auto transform = [&](std::uint32_t s, uint4 graw) {
@@ -540,15 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // they are normalised as one batch behind one proxy fence and one
         // barrier, so the MMA of the prefetched weights starts after one
         // hand-over instead of one per stage. Later stages go one by one
-        // (their weights stream from HBM meanwhile). Norm weights are
-        // requested one step ahead.
-        std::uint32_t const first = nk < static_cast<std::uint32_t>(kStages) ? nk : kStages;
-        uint4 gfirst[kStages];
-#pragma unroll
-        for (int j = 0; j < kStages; ++j) {
-            gfirst[j] = norm_chunk(j);
-        }
-        uint4 g_next = norm_chunk(first);
+        // (their weights stream from HBM meanwhile). Later norm weights are
+        // requested one stage ahead.
         bool got = true;
 #pragma unroll
         for (int j = 0; j < kStages; ++j) {
