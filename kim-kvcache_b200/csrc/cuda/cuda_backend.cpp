@@ -475,6 +475,13 @@ struct State {
                 // covered: the word may also hold an error of later work.
                 w.failed_upto = submit_seq.load();
                 cudaMemsetAsync(arena.status + w.word, 0, sizeof(unsigned int), static_cast<cudaStream_t>(stream));
+                // An attention launch that gave up may have left split-lane
+                // completion counts behind: the stream's next launch starts
+                // from zero again.
+                auto const sc = attend_scratch.find(stream);
+                if (sc != attend_scratch.end()) {
+                    static_cast<void>(kk_attention_workspace_init(sc->second.workspace, Arena::kSlots, stream));
+                }
             }
             w.checked = covered;
         }
