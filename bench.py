@@ -84,6 +84,15 @@ class ClockSampler:
                 stdout=self.file, stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return
+        # nvidia-smi takes a moment to start: wait (up to 3 s) for its first
+        # sample, so that a short timed region is still sampled.
+        deadline = time.time() + 3.0
+        while time.time() < deadline and self.proc.poll() is None:
+            self.file.flush()
+            if os.path.getsize(self.file.name) > 0:
+                break
+            time.sleep(0.02)
 
     def stop(self) -> dict:
         if self.proc is None:
