@@ -61,6 +61,11 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
+// With a fused RMSNorm the CTA has two more warps (4 and 5): warps 2-5
+// normalise the activation tiles (one warp per SM sub-partition), and only
+// warps 0-3 run the epilogue (one TMEM lane quarter and 32 rows each).
+constexpr int kThreadsXnorm = 192;
+constexpr std::uint32_t kXnThreads = 128;  // normalising threads (warps 2-5)
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
 constexpr std::uint32_t kSqStride = 64;  // columns per row of a sums-of-squares array
 // Four W+X stages: with the split-K receive buffer about 99 KB at N <= 32,
@@ -234,7 +239,7 @@ constexpr std::size_t smemBytes()
 // own epilogue, which keeps the code that runs after the main loop small
 // (instruction fetches after the main loop are on the critical path).
 template <int BN, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
+__global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
     const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
     GemmArgs args)
 {
@@ -435,12 +440,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
 #pragma unroll
     for (std::uint32_t j = 0; j < kPre; ++j) {
         resid[j] = __float2half_rn(0.f);
-        if (EPI == KK_EPI_RESIDUAL && prefetched && j < pcols && pm < args.M) {
+        if (EPI == KK_EPI_RESIDUAL && prefetched && j < pcols && tid < kBM && pm < args.M) {
             resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(pn0 + j) * args.epi.out_stride + pm];
         }
     }
     if (xnorm && warp >= 2) {
-        // Warps 2-3: the RMS factor of every batch row, then each X tile
+        // Warps 2-5: the RMS factor of every batch row, then each X tile
         // normalised in place as it lands.
         std::uint32_t const t = tid - 64u;
         std::uint32_t const c = t & 7u;
@@ -465,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         if (args.sq_in != nullptr) {
             // From the producing kernel's per-tile sums of squares, one thread
             // per row, every partial requested at once and summed in tile order.
-            for (std::uint32_t n = t; n < static_cast<std::uint32_t>(BN); n += 64u) {
+            for (std::uint32_t n = t; n < static_cast<std::uint32_t>(BN); n += kXnThreads) {
                 float sum = 0.f;
                 for (std::uint32_t t0 = 0; n < args.N && t0 < args.sq_tiles; t0 += 16u) {
                     float v[16];
@@ -482,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
             }
         } else {
             // From the rows themselves, one warp per row.
-            for (std::uint32_t n = warp - 2u; n < static_cast<std::uint32_t>(BN); n += 2u) {
+            for (std::uint32_t n = warp - 2u; n < static_cast<std::uint32_t>(BN); n += kXnThreads / 32u) {
                 float sum = 0.f;
                 __half const* xr = args.norm_x + std::uint64_t(n) * args.norm_stride;
                 for (std::uint32_t k = lane * 8u; n < args.N && k < args.K; k += 256u) {
@@ -503,14 +508,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 }
             }
         }
-        named_barrier_sync(1, 64);
+        named_barrier_sync(1, kXnThreads);
 #ifdef KK_TRACE
         if (t == 0) {
             s_xstamp[1] = global_ns();
         }
 #endif
         // Thread t owns 16-byte chunk t % 8 (dims 8c .. 8c+7 of the tile's 64)
-        // of rows t / 8, t / 8 + 8, ...; the tile is [BN rows][128 bytes] with
+        // of rows t / 8, t / 8 + 16, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
         // One stage in place: x' = half((x * r) * g) per element, FP32
         // products rounded once (packed conversions, two elements each).
@@ -522,20 +527,20 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 gv[e] = __half22float2(gh[e]);
             }
             std::uint8_t* xs = x_stage + s * BN * 128;
-            // The thread's BN / 8 rows (t / 8, t / 8 + 8, ...): every load
+            // The thread's BN / 16 rows (t / 8, t / 8 + 16, ...): every load
             // first, then the math and the stores, so the loads overlap.
-            constexpr std::uint32_t kRows = BN / 8;
+            constexpr std::uint32_t kRows = BN / 16;
             uint4 raw[kRows];
             float rr[kRows];
 #pragma unroll
             for (std::uint32_t q = 0; q < kRows; ++q) {
-                std::uint32_t const n = (t >> 3) + 8u * q;
+                std::uint32_t const n = (t >> 3) + 16u * q;
                 raw[q] = *reinterpret_cast<uint4 const*>(xs + n * 128u + ((c ^ (n & 7u)) << 4));
                 rr[q] = rnorm[n];
             }
 #pragma unroll
             for (std::uint32_t q = 0; q < kRows; ++q) {
-                std::uint32_t const n = (t >> 3) + 8u * q;
+                std::uint32_t const n = (t >> 3) + 16u * q;
                 __half2* h = reinterpret_cast<__half2*>(&raw[q]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -583,7 +588,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         // A wait that gave up stops every normalising thread at the same
         // point (the MMA warp's own bounded wait then ends the tile).
         fence_proxy_async_smem();
-        bool ok = named_barrier_and(1, 64, got);
+        bool ok = named_barrier_and(1, kXnThreads, got);
         if (t == 0 && ok) {
             for (std::uint32_t j = 0; j < first; ++j) {
                 mbar_arrive(&full[j]);
@@ -601,116 +606,141 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                 transform(s, graw);
             }
             fence_proxy_async_smem();
-            ok = named_barrier_and(1, 64, got);
+            ok = named_barrier_and(1, kXnThreads, got);
             if (t == 0 && ok) {
                 mbar_arrive(&full[s]);
             }
         }
     }
-    bool const have_acc = mbar_wait(accum, 0, st);
-    tc_fence_after();
-    KK_GEMM_STAMP(2)
+    // The epilogue: warps 0-3, one TMEM lane quarter and 32 rows each (their
+    // barriers count 128 threads). Warps 4-5 of a fused-RMSNorm CTA only
+    // take part in the cluster barrier's phases.
+    if (tid < kBM) {
+        bool const have_acc = mbar_wait(accum, 0, st);
+        tc_fence_after();
+        KK_GEMM_STAMP(2)
 
-    // TMEM -> this CTA's FP32 partial tile, column-major [BN][128] (aliases the
-    // W stages: every MMA that read them has completed).
-    float* part = reinterpret_cast<float*>(smem);
-    std::uint32_t const row = tid;
+        // TMEM -> this CTA's FP32 partial tile, column-major [BN][128] (aliases the
+        // W stages: every MMA that read them has completed).
+        float* part = reinterpret_cast<float*>(smem);
+        std::uint32_t const row = tid;
 #pragma unroll
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        tmem_ld16(tmem + ((warp * 32u) << 16) + static_cast<std::uint32_t>(c0), v);
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(tmem + ((warp * 32u) << 16) + static_cast<std::uint32_t>(c0), v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            part[(c0 + j) * kBM + row] = have_acc && nk != 0 ? v[j] : 0.f;
-        }
-    }
-    std::uint32_t const n0 = rank * args.N / S;
-    std::uint32_t const n1 = (rank + 1) * args.N / S;
-    std::uint32_t const cols = n1 - n0;
-    std::uint32_t const m = m_tile * kBM + row;
-    EpiArgs const& e = args.epi;
-    // The receive buffer holds one slot of up to cw columns per source rank;
-    // the reduced columns and the argmax scratch follow the partial in the
-    // (now idle) ring.
-    std::uint32_t const cw = (args.N + S - 1) / S;
-    float* red = part + BN * kBM;
-    float* amax_v = red + (S > 1 ? cw : static_cast<std::uint32_t>(BN)) * kBM;  // [4][BN]
-    std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4 * BN);  // [4][BN]
-    if (S > 1) {
-        fence_proxy_async_smem();
-    }
-    tc_fence_before();
-    __syncthreads();
-    KK_GEMM_STAMP(3)
-    if (S > 1) {
-        // The partial is written; every peer's receive buffer is armed (phase
-        // 1 of the cluster barrier, long complete by now). Thread r pushes
-        // owner r's columns.
-        cluster_wait();
-        KK_GEMM_STAMP(4)
-        if (tid < S) {
-            std::uint32_t const r0 = tid * args.N / S;
-            std::uint32_t const r1 = (tid + 1) * args.N / S;
-            if (r1 > r0) {
-                bulk_copy_to_peer(cluster_map(recv + rank * cw * kBM, tid), part + r0 * kBM,
-                    (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
+            for (int j = 0; j < 16; ++j) {
+                part[(c0 + j) * kBM + row] = have_acc && nk != 0 ? v[j] : 0.f;
             }
         }
-        bool const got = mbar_wait(rbar, 0, st);
-        KK_GEMM_STAMP(5)
-        // Sum over the K slices in rank order (deterministic).
-        for (std::uint32_t j = 0; j < cols; ++j) {
-            float acc = 0.f;
-            for (std::uint32_t r = 0; r < S; ++r) {
-                acc += got ? recv[(r * cw + j) * kBM + row] : 0.f;
+        std::uint32_t const n0 = rank * args.N / S;
+        std::uint32_t const n1 = (rank + 1) * args.N / S;
+        std::uint32_t const cols = n1 - n0;
+        std::uint32_t const m = m_tile * kBM + row;
+        EpiArgs const& e = args.epi;
+        // The receive buffer holds one slot of up to cw columns per source rank;
+        // the reduced columns and the argmax scratch follow the partial in the
+        // (now idle) ring.
+        std::uint32_t const cw = (args.N + S - 1) / S;
+        float* red = part + BN * kBM;
+        float* amax_v = red + (S > 1 ? cw : static_cast<std::uint32_t>(BN)) * kBM;  // [4][BN]
+        std::uint32_t* amax_i = reinterpret_cast<std::uint32_t*>(amax_v + 4 * BN);  // [4][BN]
+        if (S > 1) {
+            fence_proxy_async_smem();
+        }
+        tc_fence_before();
+        named_barrier_sync(2, kBM);
+        KK_GEMM_STAMP(3)
+        if (S > 1) {
+            // The partial is written; every peer's receive buffer is armed (phase
+            // 1 of the cluster barrier, long complete by now). Thread r pushes
+            // owner r's columns.
+            cluster_wait();
+            KK_GEMM_STAMP(4)
+            if (tid < S) {
+                std::uint32_t const r0 = tid * args.N / S;
+                std::uint32_t const r1 = (tid + 1) * args.N / S;
+                if (r1 > r0) {
+                    bulk_copy_to_peer(cluster_map(recv + rank * cw * kBM, tid), part + r0 * kBM,
+                        (r1 - r0) * kBM * 4u, cluster_map(rbar, tid));
+                }
             }
-            red[j * kBM + row] = acc;
+            bool const got = mbar_wait(rbar, 0, st);
+            KK_GEMM_STAMP(5)
+            // Sum over the K slices in rank order (deterministic).
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                float acc = 0.f;
+                for (std::uint32_t r = 0; r < S; ++r) {
+                    acc += got ? recv[(r * cw + j) * kBM + row] : 0.f;
+                }
+                red[j * kBM + row] = acc;
+            }
+            // Cluster barrier phase 2, arrive: this CTA has received everything
+            // (the receive mbarrier completed), so the senders' partials may go.
+            // Relaxed: no memory needs ordering here, and a release arrive waits
+            // for this CTA's outstanding memory operations.
+            cluster_arrive_relaxed();
+        } else {
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                red[j * kBM + row] = part[(n0 + j) * kBM + row];
+            }
         }
-        // Cluster barrier phase 2, arrive: this CTA has received everything
-        // (the receive mbarrier completed), so the senders' partials may go.
-        // Relaxed: no memory needs ordering here, and a release arrive waits
-        // for this CTA's outstanding memory operations.
-        cluster_arrive_relaxed();
-    } else {
-        for (std::uint32_t j = 0; j < cols; ++j) {
-            red[j * kBM + row] = part[(n0 + j) * kBM + row];
-        }
-    }
-    __syncthreads();
-    KK_GEMM_STAMP(6)
+        named_barrier_sync(2, kBM);
+        KK_GEMM_STAMP(6)
 
-    switch (EPI) {
-    case KK_EPI_STORE_F16:
-        if (m < args.M) {
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] =
-                    __float2half_rn(red[j * kBM + row]);
+        switch (EPI) {
+        case KK_EPI_STORE_F16:
+            if (m < args.M) {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] =
+                        __float2half_rn(red[j * kBM + row]);
+                }
             }
-        }
-        break;
-    case KK_EPI_STORE_F32:
-        if (m < args.M) {
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
+            break;
+        case KK_EPI_STORE_F32:
+            if (m < args.M) {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
+                }
             }
-        }
-        break;
-    case KK_EPI_RESIDUAL: {
-        // New rows h = half(resid + half(acc)); with sq_out, also the tile's
-        // sum of h^2 per column (the next RMSNorm's statistics), reduced in a
-        // fixed order: lanes by shuffles, then the four warps in turn.
-        float* wsq = amax_v;  // [4][BN], idle in this epilogue
-        bool const want_sq = args.sq_out != nullptr;
-        if (prefetched) {
+            break;
+        case KK_EPI_RESIDUAL: {
+            // New rows h = half(resid + half(acc)); with sq_out, also the tile's
+            // sum of h^2 per column (the next RMSNorm's statistics), reduced in a
+            // fixed order: lanes by shuffles, then the four warps in turn.
+            float* wsq = amax_v;  // [4][BN], idle in this epilogue
+            bool const want_sq = args.sq_out != nullptr;
+            if (prefetched) {
 #pragma unroll
-            for (std::uint32_t j = 0; j < kPre; ++j) {
-                if (j < cols) {
-                    __half const h = __hadd(resid[j], __float2half_rn(red[j * kBM + row]));
+                for (std::uint32_t j = 0; j < kPre; ++j) {
+                    if (j < cols) {
+                        __half const h = __hadd(resid[j], __float2half_rn(red[j * kBM + row]));
+                        if (m < args.M) {
+                            static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = h;
+                        }
+                        if (want_sq) {
+                            float const f = m < args.M ? __half2float(h) : 0.f;
+                            float q = f * f;
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                q += __shfl_xor_sync(0xffffffffu, q, o);
+                            }
+                            if (lane == 0) {
+                                wsq[warp * BN + j] = q;
+                            }
+                        }
+                    }
+                }
+            } else {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    float f = 0.f;
                     if (m < args.M) {
-                        static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = h;
+                        __half* hp = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
+                        __half const h = __hadd(*hp, __float2half_rn(red[j * kBM + row]));
+                        *hp = h;
+                        f = __half2float(h);
                     }
                     if (want_sq) {
-                        float const f = m < args.M ? __half2float(h) : 0.f;
                         float q = f * f;
 #pragma unroll
                         for (int o = 16; o > 0; o >>= 1) {
@@ -722,192 +752,176 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
                     }
                 }
             }
-        } else {
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                float f = 0.f;
-                if (m < args.M) {
-                    __half* hp = static_cast<__half*>(e.out) + std::uint64_t(n0 + j) * e.out_stride + m;
-                    __half const h = __hadd(*hp, __float2half_rn(red[j * kBM + row]));
-                    *hp = h;
-                    f = __half2float(h);
-                }
-                if (want_sq) {
-                    float q = f * f;
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) {
-                        q += __shfl_xor_sync(0xffffffffu, q, o);
-                    }
-                    if (lane == 0) {
-                        wsq[warp * BN + j] = q;
-                    }
+            if (want_sq) {
+                named_barrier_sync(2, kBM);
+                if (tid < cols) {
+                    args.sq_out[m_tile * kSqStride + n0 + tid] =
+                        ((wsq[tid] + wsq[BN + tid]) + wsq[2 * BN + tid]) + wsq[3 * BN + tid];
                 }
             }
-        }
-        if (want_sq) {
-            __syncthreads();
-            if (tid < cols) {
-                args.sq_out[m_tile * kSqStride + n0 + tid] =
-                    ((wsq[tid] + wsq[BN + tid]) + wsq[2 * BN + tid]) + wsq[3 * BN + tid];
-            }
-        }
-        break;
-    }
-    case KK_EPI_SILU_PAIRS:
-        // Rows 2i / 2i+1 hold gate_i / up_i.
-        if ((m & 1u) == 0 && m < args.M) {
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                float const g = __half2float(__float2half_rn(red[j * kBM + row]));
-                float const u = __half2float(__float2half_rn(red[j * kBM + (row ^ 1u)]));
-                static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m / 2] =
-                    __float2half_rn(g / (1.0f + expf(-g)) * u);
-            }
-        }
-        break;
-    case KK_EPI_QKV_ROPE: {
-        std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
-        if (m >= args.M || m >= kv_end) {
             break;
         }
-        // RoPE pairs dims d and d+32 of a head: rows row and row^32 of the tile.
-        bool const is_v = m >= e.q_rows + e.kv_rows;
-        std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
-        std::uint32_t const d = idx & 63u;
-        // The rotation's first product minus (or plus) the second, each
-        // rounded on its own (no fused multiply-add), as the reference's
-        // host model computes it.
+        case KK_EPI_SILU_PAIRS:
+            // Rows 2i / 2i+1 hold gate_i / up_i.
+            if ((m & 1u) == 0 && m < args.M) {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    float const g = __half2float(__float2half_rn(red[j * kBM + row]));
+                    float const u = __half2float(__float2half_rn(red[j * kBM + (row ^ 1u)]));
+                    static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m / 2] =
+                        __float2half_rn(g / (1.0f + expf(-g)) * u);
+                }
+            }
+            break;
+        case KK_EPI_QKV_ROPE: {
+            std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
+            if (m >= args.M || m >= kv_end) {
+                break;
+            }
+            // RoPE pairs dims d and d+32 of a head: rows row and row^32 of the tile.
+            bool const is_v = m >= e.q_rows + e.kv_rows;
+            std::uint32_t const idx = m < e.q_rows ? m : (is_v ? m - e.q_rows - e.kv_rows : m - e.q_rows);
+            std::uint32_t const d = idx & 63u;
+            // The rotation's first product minus (or plus) the second, each
+            // rounded on its own (no fused multiply-add), as the reference's
+            // host model computes it.
 #pragma unroll 1
-        for (std::uint32_t j = 0; j < cols; ++j) {
-            std::uint32_t const n = n0 + j;
-            // Prefetched values when the CTA owns at most kPre columns.
-            std::uint32_t position = 0;
-            kk_kv_slot slot_rec{0, 0, 0, 0};
-            float2 cs = make_float2(1.f, 0.f);
-#pragma unroll
-            for (std::uint32_t q = 0; q < kPre; ++q) {
-                if (prefetched && q == j) {
-                    position = pos[q];
-                    slot_rec = kvs[q];
-                    cs = rope[q];
-                }
-            }
-            if (!prefetched) {
-                position = e.positions[n];
-                slot_rec = e.slots[n];
-                if (e.rope_cs != nullptr && position < e.rope_positions) {
-                    cs = e.rope_cs[std::uint64_t(position) * 32u + (d & 31u)];
-                }
-            }
-            float const mine = __half2float(__float2half_rn(red[j * kBM + row]));
-            float out = mine;
-            if (!is_v) {
-                float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
-                if (e.rope_cs == nullptr) {
-                    float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
-                    sincosf(static_cast<float>(position) * inv_freq, &cs.y, &cs.x);
-                }
-                float const a = __fmul_rn(mine, cs.x);
-                float const b = __fmul_rn(other, cs.y);
-                out = d < 32u ? __fsub_rn(a, b) : __fadd_rn(a, b);
-            }
-            __half const hv = __float2half_rn(out);
-            if (m < e.q_rows) {
-                static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + idx] = hv;
-            } else {
-                kk_kv_slot const sl = slot_rec;
-                bool const micro = sl.kind == 0;
-                std::uint32_t const cap = micro ? e.micro_cap : 64u;
-                if (sl.active && sl.page_token < cap
-                    && (micro ? sl.slot < e.micro_slots : sl.slot < e.extent_slots)) {
-                    __half* page = micro ? e.micro + std::uint64_t(sl.slot) * e.micro_page
-                                         : e.extent + std::uint64_t(sl.slot) * e.extent_page;
-                    std::uint64_t const off = ((std::uint64_t(e.layer) * 2u + (is_v ? 1u : 0u)) * cap
-                        + sl.page_token) * e.kv_row + idx;
-                    page[off] = hv;
-                } else if (sl.active) {
-                    atomicCAS(st, kErrNone, kErrBadDescriptor);
-                }
-            }
-        }
-        break;
-    }
-    case KK_EPI_ARGMAX: {
-        bool const valid = m < args.M;
-        if (valid && e.out != nullptr) {
             for (std::uint32_t j = 0; j < cols; ++j) {
-                static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
-            }
-        }
-        // Per warp, every column's winner over its 32 rows; then per column
-        // over the 4 warps. Ties keep the lowest index.
-        for (std::uint32_t j = 0; j < cols; ++j) {
-            float bv = valid ? red[j * kBM + row] : -INFINITY;
-            std::uint32_t bi = valid ? m : 0xffffffffu;
+                std::uint32_t const n = n0 + j;
+                // Prefetched values when the CTA owns at most kPre columns.
+                std::uint32_t position = 0;
+                kk_kv_slot slot_rec{0, 0, 0, 0};
+                float2 cs = make_float2(1.f, 0.f);
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                float const ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                std::uint32_t const oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (better(ov, oi, bv, bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
-            if (lane == 0) {
-                amax_v[warp * BN + j] = bv;
-                amax_i[warp * BN + j] = bi;
-            }
-        }
-        __syncthreads();
-        if (tid < cols) {
-            float bv = amax_v[tid];
-            std::uint32_t bi = amax_i[tid];
-            for (int w = 1; w < 4; ++w) {
-                if (better(amax_v[w * BN + tid], amax_i[w * BN + tid], bv, bi)) {
-                    bv = amax_v[w * BN + tid];
-                    bi = amax_i[w * BN + tid];
-                }
-            }
-            e.part_val[std::uint64_t(m_tile) * args.N + n0 + tid] = bv;
-            e.part_idx[std::uint64_t(m_tile) * args.N + n0 + tid] = bi;
-        }
-        break;
-    }
-    default:
-        break;
-    }
-
-    if (EPI == KK_EPI_ARGMAX) {
-        // The last CTA of the launch folds the per-tile winners of every column.
-        __threadfence();
-        __syncthreads();
-        if (tid == 0) {
-            std::uint32_t const done = atomicAdd(e.counter, 1u);
-            *flag = done + 1 == e.num_m_tiles * S;
-        }
-        __syncthreads();
-        if (*flag) {
-            __threadfence();
-            for (std::uint32_t n = tid; n < args.N; n += kThreads) {
-                float bv = -FLT_MAX;     // same starting point as the reference reduction
-                std::uint32_t bi = 0;
-                for (std::uint32_t t = 0; t < e.num_m_tiles; ++t) {
-                    float const v = __ldcg(e.part_val + std::uint64_t(t) * args.N + n);
-                    std::uint32_t const i = __ldcg(e.part_idx + std::uint64_t(t) * args.N + n);
-                    if (better(v, i, bv, bi)) {
-                        bv = v;
-                        bi = i;
+                for (std::uint32_t q = 0; q < kPre; ++q) {
+                    if (prefetched && q == j) {
+                        position = pos[q];
+                        slot_rec = kvs[q];
+                        cs = rope[q];
                     }
                 }
-                e.tokens[n] = bi;
+                if (!prefetched) {
+                    position = e.positions[n];
+                    slot_rec = e.slots[n];
+                    if (e.rope_cs != nullptr && position < e.rope_positions) {
+                        cs = e.rope_cs[std::uint64_t(position) * 32u + (d & 31u)];
+                    }
+                }
+                float const mine = __half2float(__float2half_rn(red[j * kBM + row]));
+                float out = mine;
+                if (!is_v) {
+                    float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
+                    if (e.rope_cs == nullptr) {
+                        float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
+                        sincosf(static_cast<float>(position) * inv_freq, &cs.y, &cs.x);
+                    }
+                    float const a = __fmul_rn(mine, cs.x);
+                    float const b = __fmul_rn(other, cs.y);
+                    out = d < 32u ? __fsub_rn(a, b) : __fadd_rn(a, b);
+                }
+                __half const hv = __float2half_rn(out);
+                if (m < e.q_rows) {
+                    static_cast<__half*>(e.out)[std::uint64_t(n) * e.out_stride + idx] = hv;
+                } else {
+                    kk_kv_slot const sl = slot_rec;
+                    bool const micro = sl.kind == 0;
+                    std::uint32_t const cap = micro ? e.micro_cap : 64u;
+                    if (sl.active && sl.page_token < cap
+                        && (micro ? sl.slot < e.micro_slots : sl.slot < e.extent_slots)) {
+                        __half* page = micro ? e.micro + std::uint64_t(sl.slot) * e.micro_page
+                                             : e.extent + std::uint64_t(sl.slot) * e.extent_page;
+                        std::uint64_t const off = ((std::uint64_t(e.layer) * 2u + (is_v ? 1u : 0u)) * cap
+                            + sl.page_token) * e.kv_row + idx;
+                        page[off] = hv;
+                    } else if (sl.active) {
+                        atomicCAS(st, kErrNone, kErrBadDescriptor);
+                    }
+                }
             }
+            break;
+        }
+        case KK_EPI_ARGMAX: {
+            bool const valid = m < args.M;
+            if (valid && e.out != nullptr) {
+                for (std::uint32_t j = 0; j < cols; ++j) {
+                    static_cast<float*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m] = red[j * kBM + row];
+                }
+            }
+            // Per warp, every column's winner over its 32 rows; then per column
+            // over the 4 warps. Ties keep the lowest index.
+            for (std::uint32_t j = 0; j < cols; ++j) {
+                float bv = valid ? red[j * kBM + row] : -INFINITY;
+                std::uint32_t bi = valid ? m : 0xffffffffu;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    float const ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    std::uint32_t const oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (better(ov, oi, bv, bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) {
+                    amax_v[warp * BN + j] = bv;
+                    amax_i[warp * BN + j] = bi;
+                }
+            }
+            named_barrier_sync(2, kBM);
+            if (tid < cols) {
+                float bv = amax_v[tid];
+                std::uint32_t bi = amax_i[tid];
+                for (int w = 1; w < 4; ++w) {
+                    if (better(amax_v[w * BN + tid], amax_i[w * BN + tid], bv, bi)) {
+                        bv = amax_v[w * BN + tid];
+                        bi = amax_i[w * BN + tid];
+                    }
+                }
+                e.part_val[std::uint64_t(m_tile) * args.N + n0 + tid] = bv;
+                e.part_idx[std::uint64_t(m_tile) * args.N + n0 + tid] = bi;
+            }
+            break;
+        }
+        default:
+            break;
+        }
+
+        if (EPI == KK_EPI_ARGMAX) {
+            // The last CTA of the launch folds the per-tile winners of every column.
+            __threadfence();
+            named_barrier_sync(2, kBM);
             if (tid == 0) {
-                *e.counter = 0;
+                std::uint32_t const done = atomicAdd(e.counter, 1u);
+                *flag = done + 1 == e.num_m_tiles * S;
+            }
+            named_barrier_sync(2, kBM);
+            if (*flag) {
+                __threadfence();
+                for (std::uint32_t n = tid; n < args.N; n += kThreads) {
+                    float bv = -FLT_MAX;     // same starting point as the reference reduction
+                    std::uint32_t bi = 0;
+                    for (std::uint32_t t = 0; t < e.num_m_tiles; ++t) {
+                        float const v = __ldcg(e.part_val + std::uint64_t(t) * args.N + n);
+                        std::uint32_t const i = __ldcg(e.part_idx + std::uint64_t(t) * args.N + n);
+                        if (better(v, i, bv, bi)) {
+                            bv = v;
+                            bi = i;
+                        }
+                    }
+                    e.tokens[n] = bi;
+                }
+                if (tid == 0) {
+                    *e.counter = 0;
+                }
             }
         }
-    }
 
-    KK_GEMM_STAMP(7)
-    if (S > 1) {
-        cluster_wait();  // this CTA's partial stays alive until every owner has received it
+        KK_GEMM_STAMP(7)
+        if (S > 1) {
+            cluster_wait();  // this CTA's partial stays alive until every owner has received it
+        }
+    } else if (S > 1) {
+        cluster_wait();
+        cluster_arrive_relaxed();
+        cluster_wait();
     }
     __syncthreads();
     if (warp == 2) {
@@ -923,7 +937,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(
         std::uint32_t const slot = atomicAdd(&g_gemm_trace_n, 1u);
         if (slot < kTraceCap) {
             TraceRec& r = g_gemm_trace[slot];
-            r.tag = (static_cast<std::uint32_t>(EPI) << 16) | e.layer;
+            r.tag = (static_cast<std::uint32_t>(EPI) << 16) | args.epi.layer;
             r.block = (blockIdx.y << 16) | blockIdx.x;
             r.smid = sm_id();
             r.aux = args.K;
@@ -1156,7 +1170,8 @@ int runGemmOne(GemmPlan const& plan, cudaStream_t stream)
         return static_cast<int>(c);
     }
     return static_cast<int>(launch(gemm_tc_kernel<BN, EPI>, dim3(plan.args.split, plan.tiles),
-        dim3(kThreads), smemBytes<BN>(), stream, plan.args.split, plan.tm_w, plan.tm_x, plan.args));
+        dim3(plan.args.norm_x != nullptr ? kThreadsXnorm : kThreads), smemBytes<BN>(), stream, plan.args.split,
+        plan.tm_w, plan.tm_x, plan.args));
 }
 
 template <int BN>
