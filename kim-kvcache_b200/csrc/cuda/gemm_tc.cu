@@ -761,17 +761,21 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
             }
             break;
         }
-        case KK_EPI_SILU_PAIRS:
-            // Rows 2i / 2i+1 hold gate_i / up_i.
-            if ((m & 1u) == 0 && m < args.M) {
-                for (std::uint32_t j = 0; j < cols; ++j) {
-                    float const g = __half2float(__float2half_rn(red[j * kBM + row]));
-                    float const u = __half2float(__float2half_rn(red[j * kBM + (row ^ 1u)]));
-                    static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + m / 2] =
+        case KK_EPI_SILU_PAIRS: {
+            // Rows 2i / 2i+1 hold gate_i / up_i; the pair's two threads take
+            // alternate columns (thread 2i the even ones, 2i+1 the odd ones).
+            std::uint32_t const pr = row & ~1u;
+            std::uint32_t const mp = m_tile * kBM + pr;
+            if (mp < args.M) {
+                for (std::uint32_t j = row & 1u; j < cols; j += 2u) {
+                    float const g = __half2float(__float2half_rn(red[j * kBM + pr]));
+                    float const u = __half2float(__float2half_rn(red[j * kBM + pr + 1u]));
+                    static_cast<__half*>(e.out)[std::uint64_t(n0 + j) * e.out_stride + mp / 2] =
                         __float2half_rn(g / (1.0f + expf(-g)) * u);
                 }
             }
             break;
+        }
         case KK_EPI_QKV_ROPE: {
             std::uint32_t const kv_end = e.q_rows + 2 * e.kv_rows;
             if (m >= args.M || m >= kv_end) {
