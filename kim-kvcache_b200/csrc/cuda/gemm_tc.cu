@@ -85,6 +85,14 @@ constexpr int stagesFor()
 #endif
 }
 
+// The QKV epilogue's host inputs for the CTA's (at most 8) columns, staged
+// in shared memory at kernel start.
+struct QkvStage {
+    std::uint32_t pos[8];
+    kk_kv_slot slot[8];
+    float2 cs[8][32];
+};
+
 struct EpiArgs {
     std::uint32_t kind;
     void* out;
@@ -323,32 +331,27 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
     pdl_launch_dependents();
 
     // QKV epilogue inputs that come from the host (positions, KV slots, RoPE
-    // factors): requested now, before the dependency wait, by every thread
-    // for its row and the CTA's columns.
+    // factors of the CTA's columns): staged in shared memory now, before the
+    // dependency wait, so the epilogue reads them there (they are not held
+    // in registers across the main loop).
     constexpr std::uint32_t kPre = 8;
     std::uint32_t const pn0 = rank * args.N / S;
     std::uint32_t const pcols = (rank + 1) * args.N / S - pn0;
     bool const prefetched = pcols <= kPre;
-    kk_kv_slot kvs[kPre];
-    float2 rope[kPre];
-    std::uint32_t pos[kPre];
-#pragma unroll
-    for (std::uint32_t j = 0; j < kPre; ++j) {
-        kvs[j] = kk_kv_slot{0, 0, 0, 0};
-        rope[j] = make_float2(1.f, 0.f);
-        pos[j] = 0;
-        if (EPI == KK_EPI_QKV_ROPE && prefetched && j < pcols) {
-            pos[j] = args.epi.positions[pn0 + j];
-            kvs[j] = args.epi.slots[pn0 + j];
-        }
-    }
-    if (EPI == KK_EPI_QKV_ROPE && args.epi.rope_cs != nullptr) {
-        std::uint32_t const d32 = (m_tile * kBM + tid) & 31u;
-#pragma unroll
-        for (std::uint32_t j = 0; j < kPre; ++j) {
-            if (prefetched && j < pcols && pos[j] < args.epi.rope_positions) {
-                rope[j] = args.epi.rope_cs[std::uint64_t(pos[j]) * 32u + d32];
+    [[maybe_unused]] QkvStage* qs = nullptr;
+    if constexpr (EPI == KK_EPI_QKV_ROPE) {
+        __shared__ QkvStage s_qkv;
+        qs = &s_qkv;
+        for (std::uint32_t idx = tid; prefetched && idx < pcols * 32u && tid < kBM; idx += kBM) {
+            std::uint32_t const j = idx / 32u;
+            std::uint32_t const d = idx % 32u;
+            std::uint32_t const p = args.epi.positions[pn0 + j];
+            if (d == 0) {
+                s_qkv.pos[j] = p;
+                s_qkv.slot[j] = args.epi.slots[pn0 + j];
             }
+            s_qkv.cs[j][d] = args.epi.rope_cs != nullptr && p < args.epi.rope_positions
+                ? args.epi.rope_cs[std::uint64_t(p) * 32u + d] : make_float2(1.f, 0.f);
         }
     }
 
@@ -791,19 +794,15 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
 #pragma unroll 1
             for (std::uint32_t j = 0; j < cols; ++j) {
                 std::uint32_t const n = n0 + j;
-                // Prefetched values when the CTA owns at most kPre columns.
+                // Staged values when the CTA owns at most kPre columns.
                 std::uint32_t position = 0;
                 kk_kv_slot slot_rec{0, 0, 0, 0};
                 float2 cs = make_float2(1.f, 0.f);
-#pragma unroll
-                for (std::uint32_t q = 0; q < kPre; ++q) {
-                    if (prefetched && q == j) {
-                        position = pos[q];
-                        slot_rec = kvs[q];
-                        cs = rope[q];
-                    }
-                }
-                if (!prefetched) {
+                if (prefetched) {
+                    position = qs->pos[j];
+                    slot_rec = qs->slot[j];
+                    cs = qs->cs[j][d & 31u];
+                } else {
                     position = e.positions[n];
                     slot_rec = e.slots[n];
                     if (e.rope_cs != nullptr && position < e.rope_positions) {
