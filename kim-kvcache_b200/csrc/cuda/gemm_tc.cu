@@ -670,13 +670,20 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
             }
             bool const got = mbar_wait(rbar, 0, st);
             KK_GEMM_STAMP(5)
-            // Sum over the K slices in rank order (deterministic).
-            for (std::uint32_t j = 0; j < cols; ++j) {
-                float acc = 0.f;
+            // Sum over the K slices in rank order (deterministic), two
+            // columns at a time so that their shared-memory loads overlap.
+            for (std::uint32_t j = 0; j < cols; j += 2u) {
+                bool const two = j + 1u < cols;
+                float acc0 = 0.f;
+                float acc1 = 0.f;
                 for (std::uint32_t r = 0; r < S; ++r) {
-                    acc += got ? recv[(r * cw + j) * kBM + row] : 0.f;
+                    acc0 += got ? recv[(r * cw + j) * kBM + row] : 0.f;
+                    acc1 += got && two ? recv[(r * cw + j + 1u) * kBM + row] : 0.f;
                 }
-                red[j * kBM + row] = acc;
+                red[j * kBM + row] = acc0;
+                if (two) {
+                    red[(j + 1u) * kBM + row] = acc1;
+                }
             }
             // Cluster barrier phase 2, arrive: this CTA has received everything
             // (the receive mbarrier completed), so the senders' partials may go.
