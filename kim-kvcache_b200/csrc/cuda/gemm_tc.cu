@@ -670,19 +670,29 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
             }
             bool const got = mbar_wait(rbar, 0, st);
             KK_GEMM_STAMP(5)
-            // Sum over the K slices in rank order (deterministic), two
+            // Sum over the K slices in rank order (deterministic), four
             // columns at a time so that their shared-memory loads overlap.
-            for (std::uint32_t j = 0; j < cols; j += 2u) {
-                bool const two = j + 1u < cols;
+            for (std::uint32_t j = 0; j < cols; j += 4u) {
                 float acc0 = 0.f;
                 float acc1 = 0.f;
+                float acc2 = 0.f;
+                float acc3 = 0.f;
                 for (std::uint32_t r = 0; r < S; ++r) {
-                    acc0 += got ? recv[(r * cw + j) * kBM + row] : 0.f;
-                    acc1 += got && two ? recv[(r * cw + j + 1u) * kBM + row] : 0.f;
+                    float const* src = recv + (r * cw + j) * kBM + row;
+                    acc0 += got ? src[0] : 0.f;
+                    acc1 += got && j + 1u < cols ? src[kBM] : 0.f;
+                    acc2 += got && j + 2u < cols ? src[2u * kBM] : 0.f;
+                    acc3 += got && j + 3u < cols ? src[3u * kBM] : 0.f;
                 }
                 red[j * kBM + row] = acc0;
-                if (two) {
+                if (j + 1u < cols) {
                     red[(j + 1u) * kBM + row] = acc1;
+                }
+                if (j + 2u < cols) {
+                    red[(j + 2u) * kBM + row] = acc2;
+                }
+                if (j + 3u < cols) {
+                    red[(j + 3u) * kBM + row] = acc3;
                 }
             }
             // Cluster barrier phase 2, arrive: this CTA has received everything
