@@ -209,6 +209,17 @@ __device__ __forceinline__ void cluster_wait()
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
+// RoPE cos / sin of a position and pair index when the caller gives no
+// factor table: kept out of line so that the QKV epilogue's own code (run
+// once per launch, its instruction fetches on the critical path) stays small.
+__device__ __noinline__ float2 ropeFactors(float theta, std::uint32_t position, std::uint32_t pair)
+{
+    float const inv_freq = powf(theta, -2.0f * static_cast<float>(pair) / 64.0f);
+    float2 cs;
+    sincosf(static_cast<float>(position) * inv_freq, &cs.y, &cs.x);
+    return cs;
+}
+
 __device__ __forceinline__ bool better(float v, std::uint32_t i, float bv, std::uint32_t bi)
 {
     return v > bv || (v == bv && i < bi);
@@ -831,8 +842,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
                 if (!is_v) {
                     float const other = __half2float(__float2half_rn(red[j * kBM + (row ^ 32u)]));
                     if (e.rope_cs == nullptr) {
-                        float const inv_freq = powf(e.theta, -2.0f * static_cast<float>(d & 31u) / 64.0f);
-                        sincosf(static_cast<float>(position) * inv_freq, &cs.y, &cs.x);
+                        cs = ropeFactors(e.theta, position, d & 31u);
                     }
                     float const a = __fmul_rn(mine, cs.x);
                     float const b = __fmul_rn(other, cs.y);
