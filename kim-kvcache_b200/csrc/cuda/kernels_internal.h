@@ -56,7 +56,11 @@ int attentionLaunchTma(kk_kv_pools const* pools, std::uint32_t layer, std::uint3
 // Parts for kk_attention_plan_balanced: one per SM, but none smaller than
 // kAttnMinPartCost tokens of plan cost, so that a small batch is not cut
 // into items shorter than what a first stage and a combine cost.
+#ifdef KK_ATTN_MIN_PART_COST
+constexpr std::uint32_t kAttnMinPartCost = KK_ATTN_MIN_PART_COST;
+#else
 constexpr std::uint32_t kAttnMinPartCost = 256;
+#endif
 std::uint32_t attentionPlanParts(kk_attn_lane const* lanes, std::uint32_t num_lanes, std::uint32_t sm_count);
 
 // TMA-fed persistent attention kernel (attention_tma.cu): head_dim 64, 1/2/4/8
