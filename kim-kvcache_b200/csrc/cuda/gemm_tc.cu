@@ -16,7 +16,7 @@
 //    one 16 KB untiled bulk copy and a CTA's K range one sequential stream,
 //    which keeps DRAM pages open instead of touching 128 rows per tile.
 //
-// Structure of one CTA (128 threads):
+// Structure of one CTA (128 threads; more with a fused RMSNorm, below):
 //  * warp 0 / lane 0 issues the W tile loads and TMA loads of BNx64 X tiles
 //    (128-byte swizzle) into an NS-stage mbarrier ring; W tiles for the first
 //    stages are requested before griddepcontrol.wait, and every CTA triggers
@@ -61,11 +61,19 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kBK = 64;                  // FP16 elements in one 128-byte swizzle row
 constexpr int kThreads = 128;
-// With a fused RMSNorm the CTA has two more warps (4 and 5): warps 2-5
-// normalise the activation tiles (one warp per SM sub-partition), and only
-// warps 0-3 run the epilogue (one TMEM lane quarter and 32 rows each).
-constexpr int kThreadsXnorm = 192;
-constexpr std::uint32_t kXnThreads = 128;  // normalising threads (warps 2-5)
+// With a fused RMSNorm, KK_XNORM_WARPS warps starting at warp 2 normalise the
+// activation tiles (8 by default: warps 2-9, two per SM sub-partition, so the
+// CTA has 320 threads), and only warps 0-3 run the epilogue (one TMEM lane
+// quarter and 32 rows each). Measured on the decode step: 8 normalising warps
+// beat 4 (c4 -0.8 %, c5 -3.2 %), 4 beat 2 (-2.5 %); 16 (576 threads) made
+// the step 30 % slower.
+#ifndef KK_XNORM_WARPS
+#define KK_XNORM_WARPS 8
+#endif
+static_assert(KK_XNORM_WARPS == 2 || KK_XNORM_WARPS == 4 || KK_XNORM_WARPS == 8,
+    "the normalising warps cover 8, 16 or 32 tile rows per pass");
+constexpr std::uint32_t kXnThreads = KK_XNORM_WARPS * 32;  // normalising threads
+constexpr int kThreadsXnorm = 64 + static_cast<int>(kXnThreads);
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
 constexpr std::uint32_t kSqStride = 64;  // columns per row of a sums-of-squares array
 // Four W+X stages: with the split-K receive buffer about 99 KB at N <= 32,
@@ -459,7 +467,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
         }
     }
     if (xnorm && warp >= 2) {
-        // Warps 2-5: the RMS factor of every batch row, then each X tile
+        // The normalising warps: the RMS factor of every batch row, then each X tile
         // normalised in place as it lands.
         std::uint32_t const t = tid - 64u;
         std::uint32_t const c = t & 7u;
@@ -529,7 +537,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
         }
 #endif
         // Thread t owns 16-byte chunk t % 8 (dims 8c .. 8c+7 of the tile's 64)
-        // of rows t / 8, t / 8 + 16, ...; the tile is [BN rows][128 bytes] with
+        // of rows t / 8, t / 8 + kXnThreads / 8, ...; the tile is [BN rows][128 bytes] with
         // the 128-byte swizzle, chunk c of row n at n*128 + ((c ^ n%8) * 16).
         // One stage in place: x' = half((x * r) * g) per element, FP32
         // products rounded once (packed conversions, two elements each).
@@ -541,20 +549,26 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
                 gv[e] = __half22float2(gh[e]);
             }
             std::uint8_t* xs = x_stage + s * BN * 128;
-            // The thread's BN / 16 rows (t / 8, t / 8 + 16, ...): every load
-            // first, then the math and the stores, so the loads overlap.
-            constexpr std::uint32_t kRows = BN / 16;
+            // The thread's rows (t / 8, t / 8 + kRowStep, ...): every load
+            // first, then the math and the stores, so the loads overlap. With
+            // more threads than the tile has row chunks (BN < kRowStep) the
+            // threads past the last row have none.
+            constexpr std::uint32_t kRowStep = kXnThreads / 8u;
+            constexpr std::uint32_t kRows = (static_cast<std::uint32_t>(BN) + kRowStep - 1u) / kRowStep;
+            if (static_cast<std::uint32_t>(BN) < kRowStep && (t >> 3) >= static_cast<std::uint32_t>(BN)) {
+                return;
+            }
             uint4 raw[kRows];
             float rr[kRows];
 #pragma unroll
             for (std::uint32_t q = 0; q < kRows; ++q) {
-                std::uint32_t const n = (t >> 3) + 16u * q;
+                std::uint32_t const n = (t >> 3) + kRowStep * q;
                 raw[q] = *reinterpret_cast<uint4 const*>(xs + n * 128u + ((c ^ (n & 7u)) << 4));
                 rr[q] = rnorm[n];
             }
 #pragma unroll
             for (std::uint32_t q = 0; q < kRows; ++q) {
-                std::uint32_t const n = (t >> 3) + 16u * q;
+                std::uint32_t const n = (t >> 3) + kRowStep * q;
                 __half2* h = reinterpret_cast<__half2*>(&raw[q]);
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
@@ -627,7 +641,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
         }
     }
     // The epilogue: warps 0-3, one TMEM lane quarter and 32 rows each (their
-    // barriers count 128 threads). Warps 4-5 of a fused-RMSNorm CTA only
+    // barriers count 128 threads). Warps 4 and up of a fused-RMSNorm CTA only
     // take part in the cluster barrier's phases.
     if (tid < kBM) {
         bool const have_acc = mbar_wait(accum, 0, st);
