@@ -11,7 +11,7 @@ records %globaltimer stamps of its phases, read back by
 --define NAME[=VALUE] (repeatable) compiles the CUDA sources with an extra
 preprocessor definition, objects in their own _build_<defines>/ folder:
 the tuning variants the kernels expose (KK_GEMM_STAGES, KK_PLAN_SEGMENT_COST,
-KK_ATTN_MIN_PART_COST, KK_XNORM_WARPS, KK_MBAR_SPIN, ...), for A/B timing against
+KK_ATTN_MIN_PART_COST, KK_XNORM_WARPS[_QKV], KK_MBAR_SPIN, ...), for A/B timing against
 the default build.
 
 Objects go to kim-kvcache_b200/_build/, the library to

@@ -72,8 +72,18 @@ constexpr int kThreads = 128;
 #endif
 static_assert(KK_XNORM_WARPS == 2 || KK_XNORM_WARPS == 4 || KK_XNORM_WARPS == 8,
     "the normalising warps cover 8, 16 or 32 tile rows per pass");
-constexpr std::uint32_t kXnThreads = KK_XNORM_WARPS * 32;  // normalising threads
-constexpr int kThreadsXnorm = 64 + static_cast<int>(kXnThreads);
+#ifndef KK_XNORM_WARPS_QKV
+#define KK_XNORM_WARPS_QKV KK_XNORM_WARPS
+#endif
+static_assert(KK_XNORM_WARPS_QKV == 2 || KK_XNORM_WARPS_QKV == 4 || KK_XNORM_WARPS_QKV == 8,
+    "the normalising warps cover 8, 16 or 32 tile rows per pass");
+// Normalising threads of a projection with epilogue `epi` (the QKV one may
+// use fewer, KK_XNORM_WARPS_QKV).
+constexpr std::uint32_t xnThreadsFor(int epi)
+{
+    return (epi == KK_EPI_QKV_ROPE ? KK_XNORM_WARPS_QKV : KK_XNORM_WARPS) * 32u;
+}
+constexpr int kThreadsXnorm = 64 + (KK_XNORM_WARPS > KK_XNORM_WARPS_QKV ? KK_XNORM_WARPS : KK_XNORM_WARPS_QKV) * 32;
 constexpr std::uint32_t kTileWBytes = kBM * kBK * 2;
 constexpr std::uint32_t kSqStride = 64;  // columns per row of a sums-of-squares array
 // Four W+X stages: with the split-K receive buffer about 99 KB at N <= 32,
@@ -271,6 +281,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
     GemmArgs args)
 {
     constexpr int kStages = stagesFor<BN>();
+    constexpr std::uint32_t kXnThreads = xnThreadsFor(EPI);  // normalising threads (fused RMSNorm)
     extern __shared__ std::uint8_t smem_raw[];
     std::uint32_t const pad = (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     std::uint8_t* smem = smem_raw + pad;
@@ -466,7 +477,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
             resid[j] = static_cast<__half const*>(args.epi.out)[std::uint64_t(pn0 + j) * args.epi.out_stride + pm];
         }
     }
-    if (xnorm && warp >= 2) {
+    if (xnorm && warp >= 2 && warp < 2u + kXnThreads / 32u) {
         // The normalising warps: the RMS factor of every batch row, then each X tile
         // normalised in place as it lands.
         std::uint32_t const t = tid - 64u;
@@ -1214,7 +1225,8 @@ int runGemmOne(GemmPlan const& plan, cudaStream_t stream)
         return static_cast<int>(c);
     }
     return static_cast<int>(launch(gemm_tc_kernel<BN, EPI>, dim3(plan.args.split, plan.tiles),
-        dim3(plan.args.norm_x != nullptr ? kThreadsXnorm : kThreads), smemBytes<BN>(), stream, plan.args.split,
+        dim3(plan.args.norm_x != nullptr ? 64u + xnThreadsFor(EPI) : static_cast<unsigned>(kThreads)),
+        smemBytes<BN>(), stream, plan.args.split,
         plan.tm_w, plan.tm_x, plan.args));
 }
 
