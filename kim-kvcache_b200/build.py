@@ -10,7 +10,7 @@ records %globaltimer stamps of its phases, read back by
 
 --define NAME[=VALUE] (repeatable) compiles the CUDA sources with an extra
 preprocessor definition, objects in their own _build_<defines>/ folder:
-the tuning variants the kernels expose (KK_GEMM_STAGES, KK_PLAN_SEGMENT_COST,
+the tuning variants the kernels expose (KK_GEMM_STAGES[_N64], KK_PLAN_SEGMENT_COST,
 KK_ATTN_MIN_PART_COST, KK_XNORM_WARPS[_QKV], KK_MBAR_SPIN, ...), for A/B timing against
 the default build.
 

@@ -90,14 +90,18 @@ constexpr std::uint32_t kSqStride = 64;  // columns per row of a sums-of-squares
 // so an attention CTA or a second projection CTA fits beside this one on an
 // SM and can start (and prefetch its weights under programmatic dependent
 // launch) while this kernel drains. Measured on the decode step, 4 beats 3
-// and 5. At BN = 64 (prefill chunks) three stages keep a CTA at ~107 KB, two
-// per SM (four made it ~131 KB, one per SM). The epilogue's partial and
+// and 5. At BN = 64 (64-lane decode, prefill chunks) three stages keep a CTA
+// at ~107 KB, two per SM; four (~131 KB, one per SM; build variant
+// KK_GEMM_STAGES_N64=4) made the 64-lane decode step 39 % slower and c3 5 %
+// slower. The epilogue's partial and
 // reduced tiles reuse the ring (at most 66 KB, BN = 64).
 template <int BN>
 constexpr int stagesFor()
 {
 #ifdef KK_GEMM_STAGES
     return KK_GEMM_STAGES;
+#elif defined(KK_GEMM_STAGES_N64)
+    return BN >= 64 ? KK_GEMM_STAGES_N64 : 4;
 #else
     return BN >= 64 ? 3 : 4;
 #endif
