@@ -255,12 +255,15 @@ constexpr std::uint32_t tmemCols()
 
 // Receive buffer of the split-K reduction, outside the ring so that peers
 // can push into it while this CTA's MMAs still read the ring: one slot of
-// ceil(N/S) FP32 columns per source rank, S * ceil(N/S) <= BN + 1 columns in
-// all (the planner lowers S until that holds). Sized so that a CTA (98.5 KB
-// at BN = 32) and an attention CTA share an SM.
+// ceil(N/S) FP32 columns per source rank, S * ceil(N/S) <= recvCols columns
+// in all (the planner lowers S until that holds). BN + 1 at BN <= 32, so
+// that a CTA (98.5 KB at BN = 32) and an attention CTA share an SM, which
+// admits S = 3 at N = 32; BN + 2 above, which admits S = 3 at N = 64 (the
+// gate/up projection's 88 row tiles then run 264 CTAs instead of 176) and
+// keeps two 107 KB CTAs per SM.
 constexpr std::uint32_t recvCols(std::uint32_t bn)
 {
-    return bn + 1u;
+    return bn <= 32u ? bn + 1u : bn + 2u;
 }
 
 template <int BN>
@@ -300,7 +303,7 @@ __global__ void __launch_bounds__(kThreadsXnorm, 1) gemm_tc_kernel(
     int* flag = reinterpret_cast<int*>(tmem_slot + 4);
     float* rnorm = reinterpret_cast<float*>(flag + 4);  // [BN] per-column RMS factors
     // With a fused RMSNorm the X tile of stage s lands on xfull[s] and full[s]
-    // completes only once warps 2-3 normalised it in place.
+    // completes only once the normalising warps rewrote it in place.
     std::uint64_t* xfull = reinterpret_cast<std::uint64_t*>(rnorm + BN);
 
     std::uint32_t const tid = threadIdx.x;

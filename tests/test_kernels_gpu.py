@@ -68,7 +68,8 @@ def gemm(kk, K, w, x, epi, out=None, out_stride=0, split=0, layout=0, **extra):
 
 @pytest.mark.parametrize("M,Kd,N,split", [
     (128, 64, 16, 1), (256, 2048, 32, 0), (300, 1000, 7, 3), (2560, 2048, 32, 0),
-    (2048, 5632, 64, 0), (640, 512, 1, 2), (11264, 2048, 33, 0), (100, 256, 64, 4)])
+    (2048, 5632, 64, 0), (640, 512, 1, 2), (11264, 2048, 33, 0), (100, 256, 64, 4),
+    (11264, 2048, 64, 0), (384, 640, 62, 3)])
 def test_gemm_store_f32_matches_torch(kk, K, M, Kd, N, split, wlayout):
     g = torch.Generator().manual_seed(M * 7 + Kd + N)
     w = (torch.randn(M, Kd, generator=g) * 0.05).half().cuda()
